@@ -1,0 +1,222 @@
+"""Static flat-slab slot schedule (host side, integer, install time).
+
+For one layer this decides, once, where every retained (source scale, head) K/V segment lives in
+the layer's flat slab ``[B, capacity, D]``, and derives everything the per-scale hot path needs.
+It reproduces ``_segmented_flat_build_static_slot_schedule`` (enable_real_pruning_fast.py:260-558)
+bit for bit:
+
+1. Live interval of each (source ``s``, head ``h``): ``[s+1, end)`` where ``end`` is the first
+   target whose removed set holds ``h`` for ``s`` (or ``num_scales``); empty intervals are
+   dropped (:276-310).
+2. Intervals are placed in ``(start, end, -length, source, head)`` order (:313-322). Before each
+   placement the intervals that ended by its start are freed and the free list is coalesced
+   (:324-337, merge rule :1033-1047); the segment takes the best-fitting free block - least
+   leftover, then lowest offset - from its front, else the high-water mark grows (:338-370).
+3. Per target ``t``: ``[H, S]`` starts/ends and ``[H]`` counts of the live segments, each head's
+   segments in source-scale order (:383-412).
+4. Copy descriptors, sorted by destination slot (:414-482): the activation pack of target ``t``
+   reads the dense ``[B, H, T_t, D]`` cache of the ``T_t`` tokens before ``t`` (:484-510); the
+   append after scale ``s`` reads that scale's ``[B, H, n_s, D]`` K/V (:512-545). Source rows use
+   the flat ``head * seq_len + token`` index (:469).
+
+The capacity bound of :206-234 (max over targets of retained tokens) is reported beside the
+allocated high-water mark; like the reference default (``..._ALLOW_OVERALLOC=1``) the high-water
+mark is used even when it exceeds the bound.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def capacity_bound_for_layer(controller, *, layer_idx: int, num_heads: int) -> int:
+    """``_segmented_flat_cache_capacity_for_layer``: max over targets of sum over earlier
+    sources of (heads kept) x tokens."""
+    mask = controller.removed_mask_for_layer(layer_idx)  # [t, s, h]
+    ranges = controller.scale_ranges
+    num_scales = len(controller.scale_schedule)
+    tokens = np.array([ranges[s][1] - ranges[s][0] for s in range(num_scales)], dtype=np.int64)
+    best = 0
+    for t in range(1, num_scales):
+        kept = num_heads - mask[t, :t, :].sum(axis=1).astype(np.int64)
+        best = max(best, int((kept * np.maximum(tokens[:t], 0)).sum()))
+    return best
+
+
+def merge_free_blocks(blocks):
+    """Sort by offset and coalesce overlapping or touching blocks; zero-length blocks vanish."""
+    out = []
+    for off, length in sorted((int(o), int(n)) for o, n in blocks if int(n) > 0):
+        if out and off <= out[-1][0] + out[-1][1]:
+            last_off, last_len = out[-1]
+            out[-1] = (last_off, max(last_off + last_len, off + length) - last_off)
+        else:
+            out.append((off, length))
+    return out
+
+
+def _copy_runs(items, sequence_len: int):
+    """Group copy items (sorted by destination) into destination-contiguous runs."""
+    runs = []
+    for item in sorted(items, key=lambda it: it["dst_offset"]):
+        if item["length"] <= 0:
+            continue
+        src = item["head"] * sequence_len + item["src_start"]
+        if runs and runs[-1]["dst_end"] == item["dst_offset"]:
+            run = runs[-1]
+        else:
+            run = {"dst_start": item["dst_offset"], "dst_end": item["dst_offset"],
+                   "sequence_len": int(sequence_len), "copy_items": []}
+            runs.append(run)
+        run["copy_items"].append(
+            {"dst_start": item["dst_offset"], "src_start": src, "length": item["length"]})
+        run["dst_end"] += item["length"]
+    for run in runs:
+        ci = run["copy_items"]
+        contiguous = all(ci[i + 1]["src_start"] == ci[i]["src_start"] + ci[i]["length"]
+                         for i in range(len(ci) - 1))
+        run["contiguous_src_start"] = ci[0]["src_start"] if contiguous else None
+        run["contiguous_src_end"] = (ci[0]["src_start"] + run["dst_end"] - run["dst_start"]
+                                     if contiguous else None)
+    return runs
+
+
+def copy_descriptors(runs):
+    """Flatten runs into the int64 ``(dst_starts, src_starts, lengths)`` arrays the pack kernel
+    takes, plus the longest item and total slots
+    (``_segmented_flat_static_copy_metadata_for_runs``, enable_real_pruning_fast.py:610-671)."""
+    items = [it for run in runs for it in run["copy_items"]]
+    if not items:
+        return None
+    dst = np.array([it["dst_start"] for it in items], dtype=np.int64)
+    src = np.array([it["src_start"] for it in items], dtype=np.int64)
+    lengths = np.array([it["length"] for it in items], dtype=np.int64)
+    return {"dst_starts": dst, "src_starts": src, "lengths": lengths,
+            "max_length": int(lengths.max()), "slots": int(lengths.sum()),
+            "item_count": len(items)}
+
+
+def build_static_slot_schedule(controller, *, layer_idx: int, num_heads: int,
+                               allow_overalloc: bool = True):
+    """Return the reference's schedule dict (keys ``enabled``, ``capacity``, ``capacity_bound``,
+    ``allocated_capacity``, ``overalloc_slots``, ``segments``, ``segments_by_key``,
+    ``segments_by_target``, ``metadata_cpu_by_target``, ``old_pack_runs_by_target``,
+    ``old_pack_cache_lens_by_target``, ``append_runs_by_key``); metadata values are numpy int32."""
+    num_heads = int(num_heads)
+    bound = capacity_bound_for_layer(controller, layer_idx=layer_idx, num_heads=num_heads)
+    ranges = controller.scale_ranges
+    num_scales = len(controller.scale_schedule)
+    mask = controller.removed_mask_for_layer(layer_idx)  # [t, s, h]
+
+    intervals = []
+    for s in sorted(ranges):
+        start_t = s + 1
+        if start_t >= num_scales:
+            continue
+        lo, hi = ranges[s]
+        length = int(hi) - int(lo)
+        if length <= 0:
+            continue
+        removed_later = mask[start_t:, s, :]  # [t - start_t, h]
+        for h in range(num_heads):
+            hits = np.flatnonzero(removed_later[:, h])
+            end_t = start_t + int(hits[0]) if hits.size else num_scales
+            if end_t <= start_t:
+                continue
+            intervals.append({"source_scale": s, "head": h, "start_target": start_t,
+                              "end_target": end_t, "length": length,
+                              "scale_start": int(lo), "scale_end": int(hi)})
+
+    free, active, assigned, high_water = [], [], [], 0
+    for seg in sorted(intervals, key=lambda it: (it["start_target"], it["end_target"],
+                                                 -it["length"], it["source_scale"], it["head"])):
+        still = []
+        for a in active:
+            if a["end_target"] <= seg["start_target"]:
+                free.append((a["offset"], a["length"]))
+            else:
+                still.append(a)
+        active = still
+        free = merge_free_blocks(free)
+        need = seg["length"]
+        best = None
+        for i, (off, length) in enumerate(free):
+            if length >= need and (best is None or (length - need, off) < (best[0], best[2])):
+                best = (length - need, i, off, length)
+        if best is not None:
+            _, i, off, length = best
+            if length == need:
+                del free[i]
+            else:
+                free[i] = (off + need, length - need)
+            offset = off
+        else:
+            offset = high_water
+            high_water += need
+        placed = dict(seg)
+        placed["offset"] = int(offset)
+        assigned.append(placed)
+        active.append(placed)
+
+    if high_water > bound and not allow_overalloc:
+        return {"enabled": False, "capacity": bound, "capacity_bound": bound,
+                "allocated_capacity": high_water}
+
+    by_key = {(seg["source_scale"], seg["head"]): seg for seg in assigned}
+    by_target, metadata = {}, {}
+    for t in range(1, num_scales):
+        live = [seg for seg in assigned if seg["start_target"] <= t < seg["end_target"]]
+        by_target[t] = live
+        per_head = [[] for _ in range(num_heads)]
+        for seg in live:
+            per_head[seg["head"]].append(seg)
+        width = max((len(x) for x in per_head), default=0)
+        starts = np.zeros((num_heads, width), dtype=np.int32)
+        ends = np.zeros((num_heads, width), dtype=np.int32)
+        counts = np.zeros((num_heads,), dtype=np.int32)
+        for h, segs in enumerate(per_head):
+            segs.sort(key=lambda x: x["source_scale"])
+            counts[h] = len(segs)
+            for i, seg in enumerate(segs):
+                starts[h, i] = seg["offset"]
+                ends[h, i] = seg["offset"] + seg["length"]
+        metadata[t] = (starts, ends, counts)
+
+    old_runs, old_lens = {}, {}
+    for t, live in by_target.items():
+        if t not in ranges:
+            continue
+        old_len = int(ranges[t][0])
+        old_lens[t] = old_len
+        items = []
+        for seg in live:
+            hi = min(seg["scale_end"], old_len)
+            if seg["scale_start"] < hi:
+                items.append({"dst_offset": seg["offset"], "head": seg["head"],
+                              "src_start": seg["scale_start"], "length": hi - seg["scale_start"]})
+        old_runs[t] = _copy_runs(items, old_len)
+
+    append_runs = {}
+    for s, (lo, hi) in ranges.items():
+        nxt = s + 1
+        if nxt >= num_scales or int(hi) - int(lo) <= 0:
+            continue
+        cur_len = int(hi) - int(lo)
+        items = []
+        for h in range(num_heads):
+            seg = by_key.get((s, h))
+            if seg is None or not (seg["start_target"] <= nxt < seg["end_target"]):
+                continue
+            items.append({"dst_offset": seg["offset"], "head": h, "src_start": 0,
+                          "length": cur_len})
+        append_runs[(s, nxt)] = _copy_runs(items, cur_len)
+
+    return {
+        "enabled": True, "capacity": int(high_water), "capacity_bound": int(bound),
+        "allocated_capacity": int(high_water),
+        "overalloc_slots": max(0, int(high_water) - int(bound)),
+        "segments": assigned, "segments_by_key": by_key, "segments_by_target": by_target,
+        "metadata_cpu_by_target": metadata, "metadata_device_cache": {},
+        "old_pack_runs_by_target": old_runs, "old_pack_cache_lens_by_target": old_lens,
+        "append_runs_by_key": append_runs,
+    }
