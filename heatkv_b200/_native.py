@@ -1,0 +1,99 @@
+"""ctypes binding of libheatkv.so (the C ABI declared in include/heatkv.h).
+
+The library is loaded from the package directory (it is built in-tree by ``heatkv_b200.build``).
+There is no fallback: when the library is missing or cannot be loaded every entry point raises
+``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libheatkv.so")
+
+HEATKV_OK = 0
+HEATKV_ERR_INVALID_ARGUMENT = -1
+HEATKV_ERR_UNSUPPORTED = -2
+HEATKV_ERR_CUDA = -3
+
+DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+ATTN_AUTO, ATTN_EXACT, ATTN_TCGEN05 = 0, 1, 2
+
+DEVICE_PACK_OUT_OF_RANGE = 0x1
+DEVICE_WAIT_TIMEOUT = 0x2
+DEVICE_BAD_SEGMENT = 0x4
+
+# every symbol include/heatkv.h declares, with its ctypes signature
+_i64 = ctypes.c_int64
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+SIGNATURES = {
+    "heatkv_last_error_string": (ctypes.c_char_p, []),
+    "heatkv_version": (ctypes.c_char_p, []),
+    "heatkv_pack_kv": (_i, [_p, _p, _p, _p, _i, _i, _i64, _i64, _i64, _i64, _p, _p, _p, _i64,
+                            _i64, _p]),
+    "heatkv_segmented_attention": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i64, _i64,
+                                        _i64, _i64, _i64, _i64, ctypes.c_float, _i, _i, _p]),
+    "heatkv_device_status": (_i, [ctypes.POINTER(ctypes.c_uint32), _i, _p]),
+}
+
+_lock = threading.Lock()
+_lib = None
+_load_error = None
+
+
+def library_path() -> str:
+    return _LIB_PATH
+
+
+def load():
+    """Load (once) and return the ctypes library; RuntimeError if it is not available."""
+    global _lib, _load_error
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(_LIB_PATH):
+                _load_error = (f"libheatkv.so not found at {_LIB_PATH}; build it with "
+                               "`python -m heatkv_b200.build`")
+                raise RuntimeError(_load_error)
+            lib = ctypes.CDLL(_LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    """Map a heatkv_status to the reference's exception types."""
+    if status == HEATKV_OK:
+        return
+    msg = load().heatkv_last_error_string().decode(errors="replace") or what
+    if status == HEATKV_ERR_INVALID_ARGUMENT:
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def stream_handle(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def device_status(device=None, clear: bool = True) -> int:
+    """Sticky HEATKV_DEVICE_* flags of ``device`` (synchronises its current stream)."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    flags = ctypes.c_uint32(0)
+    with torch.cuda.device(device):
+        check(load().heatkv_device_status(ctypes.byref(flags), int(clear), stream_handle(device)),
+              "heatkv_device_status")
+    return int(flags.value)

@@ -1,0 +1,40 @@
+// Launch interface shared by the attention kernels and the C entry points.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace heatkv {
+
+struct AttnArgs {
+  const void* q;          // [B, H, Lq, D]
+  const void* slab_k;     // [B, capacity, D] (may be null when capacity == 0)
+  const void* slab_v;
+  const int32_t* seg_starts;  // [H, max_segments]
+  const int32_t* seg_ends;
+  const int32_t* seg_counts;  // [H]
+  const void* cur_k;      // [B, H, Lq, D]
+  const void* cur_v;
+  void* out;              // [B, Lq, H*D]
+  int64_t batch;
+  int64_t heads;
+  int64_t q_len;
+  int64_t capacity;
+  int64_t max_segments;
+  float scale;
+};
+
+constexpr int kMaxSegments = 256;
+
+cudaError_t launch_attention_simt(const AttnArgs& a, int q_dtype, int k_dtype, int v_dtype,
+                                  cudaStream_t st);
+// Returns cudaErrorNotSupported when the tensor-core kernel cannot take these arguments.
+cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st);
+
+cudaError_t launch_pack_kv(void* dst_k, void* dst_v, const void* src_k, const void* src_v,
+                           int64_t row_bytes_k, int64_t row_bytes_v, int64_t batch,
+                           int64_t src_rows, int64_t dst_rows, const int64_t* dst_starts,
+                           const int64_t* src_starts, const int64_t* lengths, int64_t n_items,
+                           int64_t max_length, cudaStream_t stream);
+
+}  // namespace heatkv

@@ -1,0 +1,143 @@
+// C entry points of libheatkv.so (declared in include/heatkv.h): argument validation, kernel
+// selection, error strings and the sticky device status word.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "attn.h"
+#include "common.cuh"
+
+namespace heatkv {
+__device__ unsigned int g_device_status = 0;
+}  // namespace heatkv
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(HEATKV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool valid_dtype(int d) {
+  return d == HEATKV_DTYPE_F32 || d == HEATKV_DTYPE_F16 || d == HEATKV_DTYPE_BF16;
+}
+
+int64_t dtype_size(int d) { return d == HEATKV_DTYPE_F32 ? 4 : 2; }
+
+}  // namespace
+
+extern "C" {
+
+const char* heatkv_last_error_string(void) { return g_last_error.c_str(); }
+
+const char* heatkv_version(void) { return "heatkv-b200 0.1 (sm_100a)"; }
+
+int heatkv_pack_kv(void* dst_k, void* dst_v, const void* src_k, const void* src_v, int k_dtype,
+                   int v_dtype, int64_t batch, int64_t src_rows, int64_t dst_rows,
+                   int64_t head_dim, const int64_t* dst_starts, const int64_t* src_starts,
+                   const int64_t* lengths, int64_t n_items, int64_t max_length, void* stream) {
+  g_last_error.clear();
+  if (!valid_dtype(k_dtype) || !valid_dtype(v_dtype))
+    return fail(HEATKV_ERR_UNSUPPORTED, "pack_flat_segments_kv: unsupported dtype code");
+  if (batch < 0 || src_rows < 0 || dst_rows < 0 || head_dim <= 0 || n_items < 0)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "pack_flat_segments_kv: negative size");
+  if (n_items == 0 || batch == 0 || max_length <= 0) return HEATKV_OK;
+  if (!dst_k || !dst_v || !src_k || !src_v || !dst_starts || !src_starts || !lengths)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "pack_flat_segments_kv: null pointer");
+  if (n_items > 65535 || batch > 65535)
+    return fail(HEATKV_ERR_UNSUPPORTED,
+                "pack_flat_segments_kv supports at most 65535 items and 65535 batch rows per call");
+  if ((max_length + 31) / 32 > 0x7fffffffLL)
+    return fail(HEATKV_ERR_UNSUPPORTED, "pack_flat_segments_kv: max_length too large");
+  cudaError_t e = heatkv::launch_pack_kv(
+      dst_k, dst_v, src_k, src_v, head_dim * dtype_size(k_dtype), head_dim * dtype_size(v_dtype),
+      batch, src_rows, dst_rows, dst_starts, src_starts, lengths, n_items, max_length,
+      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "pack_flat_segments_kv launch");
+  return HEATKV_OK;
+}
+
+int heatkv_segmented_attention(const void* q, const void* slab_k, const void* slab_v,
+                               const int32_t* seg_starts, const int32_t* seg_ends,
+                               const int32_t* seg_counts, const void* cur_k, const void* cur_v,
+                               void* out, int q_dtype, int k_dtype, int v_dtype, int64_t batch,
+                               int64_t heads, int64_t q_len, int64_t capacity, int64_t head_dim,
+                               int64_t max_segments, float softmax_scale, int use_exp2,
+                               int kernel, void* stream) {
+  (void)use_exp2;  // exp and exp2 modes compute the same softmax
+  g_last_error.clear();
+  if (!valid_dtype(q_dtype) || !valid_dtype(k_dtype) || !valid_dtype(v_dtype))
+    return fail(HEATKV_ERR_UNSUPPORTED,
+                "real_scale_fused_segmented supports only float16, bfloat16, or float32 tensors");
+  if (head_dim != 128)
+    return fail(HEATKV_ERR_UNSUPPORTED, "real_scale_fused_segmented v1 only supports head_dim=128");
+  if (q_len <= 0)
+    return fail(HEATKV_ERR_UNSUPPORTED, "real_scale_fused_segmented requires current_len > 0");
+  if (batch < 0 || heads <= 0 || capacity < 0 || max_segments < 0)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: invalid sizes");
+  if (batch == 0) return HEATKV_OK;
+  if (!q || !cur_k || !cur_v || !out || !seg_counts || (max_segments > 0 && (!seg_starts || !seg_ends)))
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: null pointer");
+  if (capacity > 0 && (!slab_k || !slab_v))
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: null slab with capacity > 0");
+  if (max_segments > heatkv::kMaxSegments)
+    return fail(HEATKV_ERR_UNSUPPORTED, "real_scale_fused_segmented supports at most %d segments per head",
+                heatkv::kMaxSegments);
+  if (heads > 65535 || batch > 65535 || (q_len + 63) / 64 > 0x7fffffffLL)
+    return fail(HEATKV_ERR_UNSUPPORTED, "real_scale_fused_segmented: grid too large");
+  if (kernel != HEATKV_ATTN_AUTO && kernel != HEATKV_ATTN_EXACT && kernel != HEATKV_ATTN_TCGEN05)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: unknown kernel selector");
+
+  heatkv::AttnArgs a{q,     slab_k,        slab_v, seg_starts, seg_ends, seg_counts, cur_k,
+                     cur_v, out,           batch,  heads,      q_len,    capacity,   max_segments,
+                     softmax_scale};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool same16 = (q_dtype == k_dtype && k_dtype == v_dtype && q_dtype != HEATKV_DTYPE_F32);
+  if (kernel == HEATKV_ATTN_TCGEN05 && !same16)
+    return fail(HEATKV_ERR_UNSUPPORTED,
+                "tcgen05 segmented attention needs q, k and v all bfloat16 or all float16");
+  if (kernel != HEATKV_ATTN_EXACT && same16) {
+    cudaError_t e = heatkv::launch_attention_sm100(a, q_dtype == HEATKV_DTYPE_BF16, st);
+    if (e == cudaSuccess) return HEATKV_OK;
+    if (e != cudaErrorNotSupported || kernel == HEATKV_ATTN_TCGEN05)
+      return cuda_fail(e, "tcgen05 segmented attention launch");
+  }
+  cudaError_t e = heatkv::launch_attention_simt(a, q_dtype, k_dtype, v_dtype, st);
+  if (e != cudaSuccess) return cuda_fail(e, "segmented attention launch");
+  return HEATKV_OK;
+}
+
+int heatkv_device_status(uint32_t* flags, int clear, void* stream) {
+  g_last_error.clear();
+  if (!flags) return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_device_status: null flags");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, heatkv::g_device_status, sizeof(v), 0,
+                                            cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "heatkv_device_status read");
+  if (clear) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbolAsync(heatkv::g_device_status, &zero, sizeof(zero), 0,
+                                cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "heatkv_device_status clear");
+  }
+  *flags = v;
+  return HEATKV_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,126 @@
+// Slab compaction: copy (src_start, dst_start, length) token runs of K and V into the flat slab.
+//
+// Same copy as the reference's _pack_flat_segments_kv_kernel (real_pruning_fused_attention.py:33-73):
+//   dst[b, dst_start + t, :] = src[b, src_start + t, :]   for every item, t < length, K and V.
+// The reference launches a (batch, item, 32-token chunk) grid of masked scalar element copies.
+// Here the copy is pure bytes: each block moves a chunk of rows of one item for one batch row,
+// K then V, with 16-byte vector loads/stores when the rows allow it (256-byte bf16 rows, 512-byte
+// fp32 rows), all loads of a thread issued before its stores. The kernel is HBM-bound: every byte
+// is read once and written once. Descriptors are bounds-checked on the device; an item reaching
+// outside its tensor is skipped and flagged instead of corrupting memory.
+#include "common.cuh"
+
+namespace heatkv {
+
+constexpr int kPackThreads = 256;
+constexpr int kPackRowsPerBlock = 32;   // rows of K (and of V) per block
+constexpr int kPackUnroll = 4;          // vectors in flight per thread
+
+template <typename V>
+__device__ __forceinline__ void copy_rows(char* __restrict__ dst, const char* __restrict__ src,
+                                          int64_t nbytes) {
+  // nbytes and both pointers are multiples of sizeof(V)
+  const int64_t nvec = nbytes / static_cast<int64_t>(sizeof(V));
+  const V* s = reinterpret_cast<const V*>(src);
+  V* d = reinterpret_cast<V*>(dst);
+  for (int64_t base = threadIdx.x; base < nvec; base += int64_t(kPackThreads) * kPackUnroll) {
+    V regs[kPackUnroll];
+#pragma unroll
+    for (int u = 0; u < kPackUnroll; ++u) {
+      const int64_t i = base + int64_t(u) * kPackThreads;
+      if (i < nvec) regs[u] = __ldg(s + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kPackUnroll; ++u) {
+      const int64_t i = base + int64_t(u) * kPackThreads;
+      if (i < nvec) d[i] = regs[u];
+    }
+  }
+}
+
+struct PackArgs {
+  char* dst_k;
+  char* dst_v;
+  const char* src_k;
+  const char* src_v;
+  int64_t row_bytes_k;
+  int64_t row_bytes_v;
+  int64_t src_rows;
+  int64_t dst_rows;
+  const int64_t* dst_starts;
+  const int64_t* src_starts;
+  const int64_t* lengths;
+};
+
+// grid = (row chunks, items, batch rows)
+template <typename VK, typename VV>
+__global__ void __launch_bounds__(kPackThreads) pack_kv_kernel(PackArgs a) {
+  const int64_t item = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int64_t len = a.lengths[item];
+  const int64_t row0 = int64_t(blockIdx.x) * kPackRowsPerBlock;
+  if (row0 >= len) return;
+  const int64_t d0 = a.dst_starts[item];
+  const int64_t s0 = a.src_starts[item];
+  if (len < 0 || d0 < 0 || s0 < 0 || d0 + len > a.dst_rows || s0 + len > a.src_rows) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) raise_status(HEATKV_DEVICE_PACK_OUT_OF_RANGE);
+    return;
+  }
+  const int64_t rows = min(int64_t(kPackRowsPerBlock), len - row0);
+  {
+    const int64_t rb = a.row_bytes_k;
+    copy_rows<VK>(a.dst_k + ((b * a.dst_rows) + d0 + row0) * rb,
+                  a.src_k + ((b * a.src_rows) + s0 + row0) * rb, rows * rb);
+  }
+  {
+    const int64_t rb = a.row_bytes_v;
+    copy_rows<VV>(a.dst_v + ((b * a.dst_rows) + d0 + row0) * rb,
+                  a.src_v + ((b * a.src_rows) + s0 + row0) * rb, rows * rb);
+  }
+}
+
+static int vec_width(const void* p0, const void* p1, int64_t row_bytes) {
+  const uintptr_t bits = reinterpret_cast<uintptr_t>(p0) | reinterpret_cast<uintptr_t>(p1) |
+                         static_cast<uintptr_t>(row_bytes);
+  if ((bits & 15u) == 0) return 16;
+  if ((bits & 7u) == 0) return 8;
+  if ((bits & 3u) == 0) return 4;
+  if ((bits & 1u) == 0) return 2;
+  return 1;
+}
+
+template <typename VK>
+static cudaError_t launch_v(int wv, dim3 grid, cudaStream_t st, const PackArgs& a) {
+  switch (wv) {
+    case 16: pack_kv_kernel<VK, uint4><<<grid, kPackThreads, 0, st>>>(a); break;
+    case 8: pack_kv_kernel<VK, uint2><<<grid, kPackThreads, 0, st>>>(a); break;
+    case 4: pack_kv_kernel<VK, uint32_t><<<grid, kPackThreads, 0, st>>>(a); break;
+    case 2: pack_kv_kernel<VK, uint16_t><<<grid, kPackThreads, 0, st>>>(a); break;
+    default: pack_kv_kernel<VK, uint8_t><<<grid, kPackThreads, 0, st>>>(a); break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pack_kv(void* dst_k, void* dst_v, const void* src_k, const void* src_v,
+                           int64_t row_bytes_k, int64_t row_bytes_v, int64_t batch,
+                           int64_t src_rows, int64_t dst_rows, const int64_t* dst_starts,
+                           const int64_t* src_starts, const int64_t* lengths, int64_t n_items,
+                           int64_t max_length, cudaStream_t stream) {
+  PackArgs a{static_cast<char*>(dst_k), static_cast<char*>(dst_v),
+             static_cast<const char*>(src_k), static_cast<const char*>(src_v),
+             row_bytes_k, row_bytes_v, src_rows, dst_rows, dst_starts, src_starts, lengths};
+  const int64_t chunks = (max_length + kPackRowsPerBlock - 1) / kPackRowsPerBlock;
+  dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(n_items),
+            static_cast<unsigned>(batch));
+  const int wk = vec_width(dst_k, src_k, row_bytes_k);
+  const int wv = vec_width(dst_v, src_v, row_bytes_v);
+  switch (wk) {
+    case 16: return launch_v<uint4>(wv, grid, stream, a);
+    case 8: return launch_v<uint2>(wv, grid, stream, a);
+    case 4: return launch_v<uint32_t>(wv, grid, stream, a);
+    case 2: return launch_v<uint16_t>(wv, grid, stream, a);
+    default: return launch_v<uint8_t>(wv, grid, stream, a);
+  }
+}
+
+}  // namespace heatkv

@@ -1,0 +1,123 @@
+/*
+ * heatkv.h - C ABI of libheatkv.so, the B200 (sm_100a) kernels of the HeatKV hot path.
+ *
+ * The library replaces the two device operations of the reference's kernel module
+ * (real_pruning_fused_attention.py):
+ *   - heatkv_pack_kv            <- pack_flat_segments_kv (:365-441) and its Triton kernel
+ *                                  _pack_flat_segments_kv_kernel (:33-73)
+ *   - heatkv_segmented_attention <- fused_real_pruning_flat_segmented_attention (:445-591) and its
+ *                                  Triton kernel _fused_real_pruning_segmented_attention_kernel
+ *                                  (:76-267)
+ *
+ * Conventions
+ *   - Every pointer argument is a device pointer unless stated otherwise; tensors are dense,
+ *     row-major (C-contiguous) and the caller owns them.
+ *   - Every call is asynchronous on `stream` (a cudaStream_t passed as void*; NULL = legacy
+ *     default stream) and performs no host<->device synchronisation and no allocation.
+ *   - Every call returns a heatkv_status; on failure heatkv_last_error_string() holds a message
+ *     for the calling thread. No C++ exception crosses this interface.
+ *   - Errors that can only be seen on the device (a copy descriptor outside its tensor, a bounded
+ *     wait that expired) never fault: the offending work is skipped and a sticky flag is raised,
+ *     read with heatkv_device_status().
+ */
+#ifndef HEATKV_H_
+#define HEATKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. The Python layer maps INVALID_ARGUMENT to ValueError and the others to
+ * RuntimeError, matching the exception types of the reference wrappers. */
+typedef enum {
+  HEATKV_OK = 0,
+  HEATKV_ERR_INVALID_ARGUMENT = -1, /* shape / pointer / size mismatch */
+  HEATKV_ERR_UNSUPPORTED = -2,      /* dtype, head_dim or sequence length not supported */
+  HEATKV_ERR_CUDA = -3,             /* CUDA runtime or driver error while launching */
+} heatkv_status;
+
+/* Element types of tensors crossing the interface. */
+typedef enum {
+  HEATKV_DTYPE_F32 = 0,
+  HEATKV_DTYPE_F16 = 1,
+  HEATKV_DTYPE_BF16 = 2,
+} heatkv_dtype;
+
+/* Bits of the sticky device status word (heatkv_device_status). */
+#define HEATKV_DEVICE_PACK_OUT_OF_RANGE 0x1u  /* a pack descriptor left its tensor; item skipped */
+#define HEATKV_DEVICE_WAIT_TIMEOUT 0x2u       /* a bounded pipeline wait expired; tile skipped */
+#define HEATKV_DEVICE_BAD_SEGMENT 0x4u        /* a segment lay outside the slab; it was clipped */
+
+/* Attention kernel selection for heatkv_segmented_attention. */
+typedef enum {
+  HEATKV_ATTN_AUTO = 0,   /* tensor-core kernel when q/k/v are all bf16 or all f16, else exact */
+  HEATKV_ATTN_EXACT = 1,  /* CUDA-core kernel: fp32 products and accumulation for every dtype */
+  HEATKV_ATTN_TCGEN05 = 2 /* tcgen05/TMEM kernel; requires q/k/v all bf16 or all f16 */
+} heatkv_attn_kernel;
+
+/* Message describing the last failing call made by this thread ("" if none). */
+const char* heatkv_last_error_string(void);
+
+/* Library version string. */
+const char* heatkv_version(void);
+
+/*
+ * heatkv_pack_kv - copy token runs of K and V into the flat slab.
+ * Replaces pack_flat_segments_kv (real_pruning_fused_attention.py:365-441).
+ *
+ * For item i in [0, n_items) and batch row b in [0, batch):
+ *     dst_k[b, dst_starts[i] + t, :] = src_k[b, src_starts[i] + t, :]   for t < lengths[i]
+ * and the same for V. src_* are [batch, src_rows, head_dim] (the flat [B, H*S, D] view of a
+ * [B, H, S, D] tensor), dst_* are [batch, dst_rows, head_dim]. K and V may have different dtypes
+ * (k_dtype for src_k/dst_k, v_dtype for src_v/dst_v); bytes are copied unchanged.
+ * dst_starts / src_starts / lengths are int64 device arrays of n_items entries.
+ * max_length must be >= every lengths[i] (rows beyond max_length are not copied).
+ * Items with a negative start or length, or reaching past src_rows / dst_rows, are skipped and
+ * raise HEATKV_DEVICE_PACK_OUT_OF_RANGE.
+ */
+int heatkv_pack_kv(void* dst_k, void* dst_v, const void* src_k, const void* src_v,
+                   int k_dtype, int v_dtype, int64_t batch, int64_t src_rows, int64_t dst_rows,
+                   int64_t head_dim, const int64_t* dst_starts, const int64_t* src_starts,
+                   const int64_t* lengths, int64_t n_items, int64_t max_length, void* stream);
+
+/*
+ * heatkv_segmented_attention - block-causal attention of the current scale's queries over the
+ * head's slab segments plus the current scale's K/V.
+ * Replaces fused_real_pruning_flat_segmented_attention (real_pruning_fused_attention.py:445-591).
+ *
+ *   q, cur_k, cur_v : [batch, heads, q_len, head_dim], dtypes q_dtype / k_dtype / v_dtype
+ *   slab_k, slab_v  : [batch, capacity, head_dim], dtypes k_dtype / v_dtype; may be NULL when
+ *                     capacity == 0 (the reference's persisted_k=None)
+ *   seg_starts, seg_ends : int32 [heads, max_segments]; seg_counts : int32 [heads]
+ *                     head h attends slab rows [seg_starts[h,i], seg_ends[h,i]) for
+ *                     i < seg_counts[h]; entries with start >= end are skipped; ranges are
+ *                     clipped to [0, capacity) (HEATKV_DEVICE_BAD_SEGMENT when clipping occurs)
+ *   out             : [batch, q_len, heads * head_dim] in q_dtype
+ *   softmax_scale   : multiplies q.k before the softmax; use_exp2 selects the reference's
+ *                     "exp2" mode, which computes the same softmax (it only rescales the
+ *                     exponent base), so it is accepted and has no numerical effect here.
+ * head_dim must be 128 and q_len > 0. max_segments <= 256.
+ */
+int heatkv_segmented_attention(const void* q, const void* slab_k, const void* slab_v,
+                               const int32_t* seg_starts, const int32_t* seg_ends,
+                               const int32_t* seg_counts, const void* cur_k, const void* cur_v,
+                               void* out, int q_dtype, int k_dtype, int v_dtype, int64_t batch,
+                               int64_t heads, int64_t q_len, int64_t capacity, int64_t head_dim,
+                               int64_t max_segments, float softmax_scale, int use_exp2,
+                               int kernel, void* stream);
+
+/*
+ * heatkv_device_status - read (and with clear != 0, reset) the sticky HEATKV_DEVICE_* flags of
+ * the current CUDA device. This call synchronises `stream`. Not part of the reference interface:
+ * the reference's Triton kernels do not check descriptors on the device.
+ */
+int heatkv_device_status(uint32_t* flags, int clear, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HEATKV_H_ */

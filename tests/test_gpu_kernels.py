@@ -1,0 +1,265 @@
+"""GPU parity of the libheatkv kernels (run with ``pytest -m gpu`` on a B200).
+
+Attention: tcgen05 (bf16/fp16) and exact (every dtype) kernels against the float64 CPU oracle on
+the seeded edge cases, against the outputs recorded from the reference itself, and on larger
+random segment layouts against a plain PyTorch fp32 reference on the GPU. Tolerances: bf16/fp16
+max |err| <= 2e-2 and max |err| / max |ref| <= 1e-2; fp32 (exact kernel) 1e-5.
+Pack: bit-exact against the oracle for random descriptors and mixed K/V dtypes; out-of-range
+descriptors are skipped and flagged.
+"""
+
+import hashlib
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from heatkv_b200 import _native, synthetic
+from heatkv_b200.real_pruning_fused_attention import (
+    fused_real_pruning_flat_segmented_attention as attn,
+    pack_flat_segments_kv as pack,
+)
+from heatkv_b200.scheduler import build_static_slot_schedule, copy_descriptors
+from oracle.attention import segmented_attention as oracle_attention
+from oracle.pack import pack_flat_segments as oracle_pack
+
+pytestmark = pytest.mark.gpu
+
+BF16_ATOL, BF16_REL = 2e-2, 1e-2
+FP32_ATOL = 1e-5
+
+
+@pytest.fixture(scope="module", autouse=True)
+def cuda_device():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    _native.load()
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    return torch.device("cuda", 0)
+
+
+@pytest.fixture
+def kernel(monkeypatch):
+    def set_kernel(name):
+        monkeypatch.setenv("HEATKV_ATTENTION_KERNEL", name)
+    return set_kernel
+
+
+def _to(inputs, dev):
+    out = {}
+    for k, v in inputs.items():
+        out[k] = v.to(dev) if isinstance(v, torch.Tensor) else v
+    return out
+
+
+def _check_lowp(out, ref):
+    out = np.asarray(out, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    err = np.abs(out - ref).max()
+    scale = max(np.abs(ref).max(), 1e-30)
+    assert err <= BF16_ATOL, f"max abs err {err}"
+    assert err / scale <= BF16_REL, f"relative err {err / scale}"
+
+
+@pytest.mark.parametrize("case", synthetic.ATTENTION_CASES, ids=lambda c: c.name)
+@pytest.mark.parametrize("which", ["auto", "exact"])
+def test_attention_cases(case, which, cuda_device, kernel, golden_dir):
+    kernel(which)
+    inputs = synthetic.attention_case_inputs(case)
+    ref = oracle_attention(**inputs)
+    out = attn(**_to(inputs, cuda_device)).float().cpu().numpy()
+    golden = np.load(os.path.join(golden_dir, "attention_cases.npz"))[case.name]
+    if case.dtype == "bf16":
+        golden = torch.from_numpy(golden).view(torch.bfloat16).float().numpy()
+    if case.dtype == "f32":
+        np.testing.assert_allclose(out, ref, atol=FP32_ATOL, rtol=FP32_ATOL)
+        np.testing.assert_allclose(out, golden, atol=FP32_ATOL, rtol=FP32_ATOL)
+    else:
+        _check_lowp(out, ref)
+        _check_lowp(out, golden)
+    assert _native.device_status(cuda_device) == 0
+
+
+def _torch_reference(q, pk, pv, starts, ends, counts, ck, cv, scale):
+    """Plain PyTorch fp32 reference on the GPU (gather the head's slab rows, then softmax)."""
+    B, H, L, D = q.shape
+    out = torch.empty(B, L, H, D, dtype=torch.float32, device=q.device)
+    st, en, ct = starts.cpu(), ends.cpu(), counts.cpu()
+    for h in range(H):
+        idx = [torch.arange(int(st[h, i]), int(en[h, i])) for i in range(int(ct[h]))
+               if int(st[h, i]) < int(en[h, i])]
+        idx = torch.cat(idx).to(q.device) if idx else torch.zeros(0, dtype=torch.long, device=q.device)
+        keys = torch.cat([pk[:, idx].float(), ck[:, h].float()], dim=1)  # [B, S+L, D]
+        vals = torch.cat([pv[:, idx].float(), cv[:, h].float()], dim=1)
+        s = torch.einsum("bld,bsd->bls", q[:, h].float(), keys) * scale
+        out[:, :, h] = torch.softmax(s, dim=-1) @ vals
+    return out.reshape(B, L, H * D)
+
+
+def _random_layout(rng, heads, max_segments, capacity, lengths=(1, 4, 16, 36, 64, 127, 128, 129, 300, 576)):
+    starts = np.zeros((heads, max_segments), np.int32)
+    ends = np.zeros((heads, max_segments), np.int32)
+    counts = np.zeros((heads,), np.int32)
+    for h in range(heads):
+        c = int(rng.integers(0, max_segments + 1))
+        counts[h] = c
+        for i in range(c):
+            n = min(int(rng.choice(lengths)), capacity)
+            s = int(rng.integers(0, capacity - n + 1))
+            starts[h, i], ends[h, i] = s, s + n
+    return [torch.from_numpy(x) for x in (starts, ends, counts)]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,H,L,cap,S", [
+    (1, 1, 1, 700, 3), (2, 3, 4, 400, 4), (1, 2, 127, 900, 5), (2, 2, 128, 900, 5),
+    (1, 3, 129, 1200, 6), (2, 2, 255, 800, 4), (1, 2, 256, 900, 6), (2, 1, 257, 1500, 8),
+    (2, 16, 576, 4000, 12), (1, 4, 1024, 3000, 12),
+])
+def test_tcgen05_random_layouts(dtype, B, H, L, cap, S, cuda_device, kernel):
+    kernel("tcgen05")
+    rng = np.random.default_rng(B * 1000 + H * 100 + L)
+    gen = torch.Generator().manual_seed(L)
+    q, ck, cv = (torch.randn(B, H, L, 128, generator=gen).to(dtype).to(cuda_device) for _ in range(3))
+    pk, pv = (torch.randn(B, cap, 128, generator=gen).to(dtype).to(cuda_device) for _ in range(2))
+    st, en, ct = _random_layout(rng, H, S, cap)
+    scale = 1.0 / math.sqrt(128)
+    out = attn(q=q, persisted_k=pk, persisted_v=pv, segment_starts=st.to(cuda_device),
+               segment_ends=en.to(cuda_device), segment_counts=ct.to(cuda_device),
+               current_k=ck, current_v=cv, softmax_scale=scale)
+    ref = _torch_reference(q, pk, pv, st, en, ct, ck, cv, scale)
+    _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
+    assert _native.device_status(cuda_device) == 0
+
+
+@pytest.mark.parametrize("L,cap,S", [(1, 300, 3), (64, 700, 6), (130, 900, 5), (300, 1500, 8)])
+def test_exact_fp32_random_layouts(L, cap, S, cuda_device, kernel):
+    kernel("auto")  # fp32 inputs always take the exact kernel
+    rng = np.random.default_rng(L)
+    gen = torch.Generator().manual_seed(L + 1)
+    B, H = 2, 3
+    q, ck, cv = (torch.randn(B, H, L, 128, generator=gen) for _ in range(3))
+    pk, pv = (torch.randn(B, cap, 128, generator=gen) for _ in range(2))
+    st, en, ct = _random_layout(rng, H, S, cap)
+    scale = 1.0 / math.sqrt(128)
+    ref = oracle_attention(q=q, persisted_k=pk, persisted_v=pv, segment_starts=st, segment_ends=en,
+                           segment_counts=ct, current_k=ck, current_v=cv, softmax_scale=scale)
+    d = cuda_device
+    out = attn(q=q.to(d), persisted_k=pk.to(d), persisted_v=pv.to(d), segment_starts=st.to(d),
+               segment_ends=en.to(d), segment_counts=ct.to(d), current_k=ck.to(d),
+               current_v=cv.to(d), softmax_scale=scale)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, atol=FP32_ATOL, rtol=FP32_ATOL)
+
+
+def test_exact_mixed_dtypes_real_model_layout(cuda_device):
+    """q, k fp32 and v bf16: the dtypes of the real model (cos-attn under bf16 autocast)."""
+    rng = np.random.default_rng(7)
+    gen = torch.Generator().manual_seed(7)
+    B, H, L, cap = 2, 4, 100, 600
+    q, ck = (torch.randn(B, H, L, 128, generator=gen) for _ in range(2))
+    cv = torch.randn(B, H, L, 128, generator=gen).bfloat16()
+    pk = torch.randn(B, cap, 128, generator=gen)
+    pv = torch.randn(B, cap, 128, generator=gen).bfloat16()
+    st, en, ct = _random_layout(rng, H, 5, cap)
+    ref = oracle_attention(q=q, persisted_k=pk, persisted_v=pv, segment_starts=st, segment_ends=en,
+                           segment_counts=ct, current_k=ck, current_v=cv, softmax_scale=0.09)
+    d = cuda_device
+    out = attn(q=q.to(d), persisted_k=pk.to(d), persisted_v=pv.to(d), segment_starts=st.to(d),
+               segment_ends=en.to(d), segment_counts=ct.to(d), current_k=ck.to(d),
+               current_v=cv.to(d), softmax_scale=0.09)
+    assert out.dtype == torch.float32
+    np.testing.assert_allclose(out.cpu().numpy(), ref, atol=FP32_ATOL, rtol=FP32_ATOL)
+
+
+@pytest.mark.parametrize("kd,vd", [(torch.bfloat16, torch.bfloat16), (torch.float32, torch.bfloat16),
+                                   (torch.float16, torch.float32)])
+def test_pack_random_descriptors(kd, vd, cuda_device):
+    rng = np.random.default_rng(3)
+    B, H, S, cap, D = 3, 5, 150, 2000, 128
+    gen = torch.Generator().manual_seed(3)
+    src_k = torch.randn(B, H * S, D, generator=gen).to(kd)
+    src_v = torch.randn(B, H * S, D, generator=gen).to(vd)
+    dst_k = torch.randn(B, cap, D, generator=gen).to(kd)
+    dst_v = torch.randn(B, cap, D, generator=gen).to(vd)
+    # non-overlapping destination runs of assorted lengths (1 .. S)
+    lengths = rng.integers(1, S + 1, size=9)
+    dst = np.cumsum(np.concatenate([[0], lengths[:-1] + rng.integers(0, 7, size=8)]))
+    src = np.array([int(rng.integers(0, H)) * S + int(rng.integers(0, S - n + 1)) for n in lengths])
+    exp_k, exp_v = dst_k.clone(), dst_v.clone()
+    oracle_pack(exp_k.view(torch.int16 if kd != torch.float32 else torch.int32).numpy(),
+                exp_v.view(torch.int16 if vd != torch.float32 else torch.int32).numpy(),
+                src_k.view(torch.int16 if kd != torch.float32 else torch.int32).numpy(),
+                src_v.view(torch.int16 if vd != torch.float32 else torch.int32).numpy(),
+                dst, src, lengths)
+    d = cuda_device
+    gk, gv = dst_k.to(d), dst_v.to(d)
+    pack(dst_k=gk, dst_v=gv, src_k=src_k.to(d), src_v=src_v.to(d),
+         dst_starts=torch.from_numpy(dst).to(d), src_starts=torch.from_numpy(src).to(d),
+         lengths=torch.from_numpy(lengths).to(d))
+    assert torch.equal(gk.cpu(), exp_k) and torch.equal(gv.cpu(), exp_v)
+    assert _native.device_status(d) == 0
+
+
+def test_pack_out_of_range_item_is_skipped_and_flagged(cuda_device):
+    d = cuda_device
+    src = torch.arange(2 * 10 * 128, dtype=torch.float32, device=d).reshape(2, 10, 128)
+    dst_k = torch.zeros(2, 20, 128, device=d)
+    dst_v = torch.zeros(2, 20, 128, device=d)
+    pack(dst_k=dst_k, dst_v=dst_v, src_k=src, src_v=src,
+         dst_starts=torch.tensor([0, 18], device=d), src_starts=torch.tensor([2, 0], device=d),
+         lengths=torch.tensor([3, 5], device=d))  # second item would end at row 23 > 20
+    assert torch.equal(dst_k[:, :3], src[:, 2:5])
+    assert torch.count_nonzero(dst_k[:, 3:]) == 0
+    assert _native.device_status(d) & _native.DEVICE_PACK_OUT_OF_RANGE
+    assert _native.device_status(d) == 0  # cleared by the previous read
+
+
+def _sha(t):
+    return list(hashlib.sha256(t.contiguous().cpu().numpy().tobytes()).digest())
+
+
+def test_config1_pipeline_against_reference(cuda_device, golden_dir):
+    """Activation pack, per-scale appends and fused attention of config 1 on the GPU reproduce the
+    reference's slab bytes (SHA-256) and attention outputs (fp32, 1e-5)."""
+    from test_host_golden import config1_controller
+
+    cfg, ctrl = config1_controller()
+    sched = build_static_slot_schedule(ctrl, layer_idx=0, num_heads=cfg.num_heads)
+    pk_golden = np.load(os.path.join(golden_dir, "pack_c1.npz"))["digests"].tolist()
+    ga = np.load(os.path.join(golden_dir, "attention_c1.npz"))
+    d = cuda_device
+    qkv = [tuple(x.to(d) for x in s) for s in synthetic.config1_qkv(cfg)]
+    first = synthetic.first_pruned_target(ctrl.removed_heads_by_source_for, len(qkv))
+    cap = sched["capacity"]
+    slab_k = torch.zeros(cfg.batch, cap, 128, device=d)
+    slab_v = torch.zeros_like(slab_k)
+
+    def run_pack(runs, k, v):
+        desc = copy_descriptors(runs)
+        B, H, T, D = k.shape
+        pack(dst_k=slab_k, dst_v=slab_v, src_k=k.reshape(B, H * T, D), src_v=v.reshape(B, H * T, D),
+             dst_starts=torch.from_numpy(desc["dst_starts"]).to(d),
+             src_starts=torch.from_numpy(desc["src_starts"]).to(d),
+             lengths=torch.from_numpy(desc["lengths"]).to(d), max_length=desc["max_length"])
+
+    dense_k = torch.cat([qkv[s][1] for s in range(first)], dim=2)
+    dense_v = torch.cat([qkv[s][2] for s in range(first)], dim=2)
+    run_pack(sched["old_pack_runs_by_target"][first], dense_k, dense_v)
+    assert [first, -1] + _sha(slab_k) + _sha(slab_v) == pk_golden[0]
+    step = 1
+    for t in range(first, len(qkv)):
+        q, k, v = qkv[t]
+        st, en, ct = (torch.from_numpy(x).to(d) for x in sched["metadata_cpu_by_target"][t])
+        out = attn(q=q, persisted_k=slab_k, persisted_v=slab_v, segment_starts=st, segment_ends=en,
+                   segment_counts=ct, current_k=k, current_v=v, softmax_scale=cfg.softmax_scale)
+        o = out.cpu().numpy()
+        np.testing.assert_allclose(o[:, :4, :], ga[f"t{t}_head_rows"], atol=FP32_ATOL, rtol=FP32_ATOL)
+        np.testing.assert_allclose(synthetic.output_checksums(o), ga[f"t{t}_checksums"],
+                                   rtol=1e-5, atol=1e-3)
+        if t + 1 < len(qkv):
+            run_pack(sched["append_runs_by_key"][(t, t + 1)], k, v)
+            assert [t, t + 1] + _sha(slab_k) + _sha(slab_v) == pk_golden[step]
+            step += 1
+    assert _native.device_status(d) == 0
