@@ -10,6 +10,8 @@
 // Block = 256 threads computes 64 query rows of one (b, h). Per 32-key tile: S = Q K^T with each
 // thread owning 4 rows x 2 keys (K staged transposed in shared memory), row statistics reduced over
 // the 16 threads of a half-warp, then O += P V with each thread owning 4 rows x 8 columns.
+#include <atomic>
+
 #include "attn.h"
 #include "common.cuh"
 
@@ -233,8 +235,17 @@ template <typename TQ, typename TK, typename TV>
 static cudaError_t launch_simt_t(const AttnArgs& a, cudaStream_t st) {
   auto kern = attn_simt_kernel<TQ, TK, TV>;
   const int smem = static_cast<int>(sizeof(SimtSmem));
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  // opt in to >48 KiB dynamic shared memory once per device (never inside a graph capture)
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  const uint64_t bit = uint64_t(1) << (dev & 63);
+  if (!(configured.load() & bit)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(bit);
+  }
   dim3 grid(static_cast<unsigned>((a.q_len + kSimtM - 1) / kSimtM), static_cast<unsigned>(a.heads),
             static_cast<unsigned>(a.batch));
   kern<<<grid, kSimtThreads, smem, st>>>(a);

@@ -30,6 +30,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 namespace heatkv {
@@ -548,8 +549,17 @@ cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st
   if (blocks >= (int64_t(1) << 31)) return cudaErrorNotSupported;
   const int smem = static_cast<int>(sizeof(Smem)) + 1024;
   auto kern = bf16 ? attn_sm100_kernel<true> : attn_sm100_kernel<false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  // opt in to >48 KiB dynamic shared memory once per device (never inside a graph capture)
+  static std::atomic<uint64_t> configured[2] = {{0}, {0}};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  const uint64_t bit = uint64_t(1) << (dev & 63);
+  if (!(configured[bf16].load() & bit)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured[bf16].fetch_or(bit);
+  }
   kern<<<static_cast<unsigned>(blocks), kThreads, smem, st>>>(tq, tck, tcv, tsk, tsv, p);
   return cudaGetLastError();
 }

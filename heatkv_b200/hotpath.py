@@ -1,0 +1,272 @@
+"""Device-resident execution plan of the HeatKV hot path for a whole model.
+
+For every layer this turns the static slab schedule (``scheduler.build_static_slot_schedule``) into
+device tensors once, and emits the per-image launch sequence of the reference orchestrator
+(enable_real_pruning_fast.py:1951-2254 with its defaults: static schedule, Triton static copy,
+baseline-prefix activation) as prepared C-ABI calls:
+
+* target ``t`` before the layer's first pruned target ``t0``: attention over the layer's dense
+  cache (the reference's SDPA + ``torch.cat`` path, :2073-2121), here run by the same kernel with
+  the dense cache ``[B, H, Ld, D]`` viewed as a flat slab and one segment per head, then the
+  current scale's K/V appended into the preallocated dense cache (no concatenation copy);
+* end of scale ``t0 - 1``: activation pack of the retained (source, head) segments from the dense
+  cache into the slab (``old_pack_runs_by_target[t0]``, :1999-2037 -> :871-967);
+* targets ``t >= t0``: fused segmented attention over the slab (:2123-2155), then the append of the
+  current scale into its slab segments (``append_runs_by_key[(t, t+1)]``, :2218-2225 -> :969-1024).
+
+Calls go straight to libheatkv.so with pre-bound pointers (the validated Python wrappers are the
+public per-call API; this engine is the pre-planned path used by the model installer, the benchmark
+and CUDA-graph capture). Layers are visited scale by scale, like the model's forward.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+from typing import Callable, Optional
+
+import numpy as np
+import torch
+
+from . import _native
+from .scheduler import build_static_slot_schedule, copy_descriptors
+
+
+@dataclasses.dataclass
+class Launch:
+    kind: str            # "attention" | "pack"
+    layer: int
+    target: int
+    fn: Callable
+    args: tuple          # ctypes arguments without the trailing stream
+    work: float          # algorithmic FLOPs (attention) or HBM bytes (pack)
+
+    def __call__(self, stream: ctypes.c_void_p) -> None:
+        status = self.fn(*self.args, stream)
+        if status != _native.HEATKV_OK:
+            _native.check(status, f"{self.kind} launch (layer {self.layer}, target {self.target})")
+
+
+def _dev(x: np.ndarray, device, dtype=None) -> torch.Tensor:
+    t = torch.from_numpy(np.ascontiguousarray(x))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.to(device)
+
+
+class LayerPlan:
+    """Slab schedule of one layer, resident on ``device``."""
+
+    def __init__(self, controller, layer_idx: int, num_heads: int, device, schedule=None):
+        self.layer = int(layer_idx)
+        self.num_heads = int(num_heads)
+        self.ranges = controller.scale_ranges
+        self.num_scales = len(controller.scale_schedule)
+        self.tokens = [self.ranges[s][1] - self.ranges[s][0] for s in range(self.num_scales)]
+        sched = schedule if schedule is not None else build_static_slot_schedule(
+            controller, layer_idx=layer_idx, num_heads=num_heads)
+        self.schedule = sched
+        self.capacity = int(sched["capacity"])
+        self.first_target = next(
+            (t for t in range(1, self.num_scales) if controller.any_removed(layer_idx, t)),
+            self.num_scales)
+        t0 = self.first_target
+        # dense cache length per head: tokens before t0 (or before the last scale)
+        self.dense_len = int(self.ranges[min(t0, self.num_scales - 1)][0])
+        H, Ld = self.num_heads, self.dense_len
+        # dense-prefix attention metadata: head h reads flat rows [h*Ld, h*Ld + T_t)
+        self.dense_meta = {}
+        for t in range(min(t0, self.num_scales)):
+            old = int(self.ranges[t][0])
+            st = (np.arange(H, dtype=np.int32) * Ld).reshape(H, 1)
+            meta = (st, st + old, np.ones(H, dtype=np.int32) * (1 if old > 0 else 0))
+            self.dense_meta[t] = tuple(_dev(m, device) for m in meta) + (meta,)
+        # dense appends: scale t's tokens of head h -> flat row h*Ld + start_t
+        self.dense_append = {}
+        for t in range(min(t0, self.num_scales - 1)):
+            n = self.tokens[t]
+            dst = np.arange(H, dtype=np.int64) * Ld + int(self.ranges[t][0])
+            src = np.arange(H, dtype=np.int64) * n
+            ln = np.full(H, n, dtype=np.int64)
+            self.dense_append[t] = (_dev(dst, device), _dev(src, device), _dev(ln, device), H, n,
+                                    H * n)
+        # activation: retained segments live at t0, read from the dense cache layout
+        self.activation = None
+        if t0 < self.num_scales:
+            items = [(seg["offset"], seg["head"] * Ld + seg["scale_start"], seg["length"])
+                     for seg in sched["segments_by_target"][t0]]
+            if items:
+                items.sort()
+                arr = np.array(items, dtype=np.int64)
+                self.activation = (_dev(arr[:, 0], device), _dev(arr[:, 1], device),
+                                   _dev(arr[:, 2], device), len(items), int(arr[:, 2].max()),
+                                   int(arr[:, 2].sum()))
+        # fused targets: slab metadata and appends
+        self.slab_meta = {}
+        for t in range(t0, self.num_scales):
+            st, en, ct = sched["metadata_cpu_by_target"][t]
+            self.slab_meta[t] = (_dev(st, device), _dev(en, device), _dev(ct, device), (st, en, ct))
+        self.slab_append = {}
+        for t in range(t0, self.num_scales - 1):
+            d = copy_descriptors(sched["append_runs_by_key"].get((t, t + 1), []))
+            if d is None:
+                continue
+            self.slab_append[t] = (_dev(d["dst_starts"], device), _dev(d["src_starts"], device),
+                                   _dev(d["lengths"], device), d["item_count"], d["max_length"],
+                                   d["slots"])
+
+    def attention_slots(self, t: int) -> np.ndarray:
+        """Attended slab slots per head at target t (for FLOP accounting)."""
+        meta = self.dense_meta[t][3] if t < self.first_target else self.slab_meta[t][3]
+        st, en, ct = meta
+        slots = np.zeros(self.num_heads, dtype=np.int64)
+        for h in range(self.num_heads):
+            for i in range(int(ct[h])):
+                slots[h] += max(0, int(en[h, i]) - int(st[h, i]))
+        return slots
+
+
+class HotPath:
+    """All layers of one model for a fixed batch: slabs, dense caches and launch plans."""
+
+    def __init__(self, controller, num_layers: int, num_heads: int, batch: int, device,
+                 k_dtype=torch.bfloat16, v_dtype=torch.bfloat16, head_dim: int = 128,
+                 layers: Optional[list] = None):
+        self.device = torch.device(device)
+        self.num_layers = int(num_layers)
+        self.num_heads = int(num_heads)
+        self.batch = int(batch)
+        self.head_dim = int(head_dim)
+        self.k_dtype, self.v_dtype = k_dtype, v_dtype
+        self.plans = [LayerPlan(controller, l, num_heads, self.device) for l in
+                      (layers if layers is not None else range(num_layers))]
+        self.num_scales = self.plans[0].num_scales
+        self.tokens = self.plans[0].tokens
+        B, H, D = self.batch, self.num_heads, self.head_dim
+        self.slab_k, self.slab_v, self.dense_k, self.dense_v = [], [], [], []
+        for p in self.plans:
+            cap = max(p.capacity, 1)
+            self.slab_k.append(torch.zeros(B, cap, D, dtype=k_dtype, device=self.device))
+            self.slab_v.append(torch.zeros(B, cap, D, dtype=v_dtype, device=self.device))
+            ld = max(p.dense_len, 1)
+            self.dense_k.append(torch.zeros(B, H * ld, D, dtype=k_dtype, device=self.device))
+            self.dense_v.append(torch.zeros(B, H * ld, D, dtype=v_dtype, device=self.device))
+        self.lib = _native.load()
+
+    def slab_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.slab_k + self.slab_v)
+
+    # ------------------------------------------------------------------ launch plans
+    def launches(self, inputs, outputs, *, kernel: int = _native.ATTN_AUTO,
+                 softmax_scale: Optional[float] = None) -> list:
+        """Launch list of one image. ``inputs[i][t] = (q, k, v)`` ([B, H, n_t, D]) and
+        ``outputs[i][t]`` ([B, n_t, H*D]) for plan index i; the tensors must stay alive."""
+        B, H, D = self.batch, self.num_heads, self.head_dim
+        scale = float(softmax_scale) if softmax_scale is not None else D ** -0.5
+        lib = self.lib
+        dt = _native.DTYPE_CODES
+        out = []
+        for t in range(self.num_scales):
+            n = self.tokens[t]
+            for i, p in enumerate(self.plans):
+                q, k, v = inputs[i][t]
+                o = outputs[i][t]
+                dense = t < p.first_target
+                if dense:
+                    st, en, ct, _ = p.dense_meta[t]
+                    sk, sv = self.dense_k[i], self.dense_v[i]
+                    cap = H * max(p.dense_len, 1)
+                else:
+                    st, en, ct, _ = p.slab_meta[t]
+                    sk, sv = self.slab_k[i], self.slab_v[i]
+                    cap = max(p.capacity, 1)
+                flops = float(4 * n * (p.attention_slots(t) + n).sum() * D * B)
+                out.append(Launch(
+                    "attention", p.layer, t, lib.heatkv_segmented_attention,
+                    (_native.ptr(q), _native.ptr(sk), _native.ptr(sv), _native.ptr(st),
+                     _native.ptr(en), _native.ptr(ct), _native.ptr(k), _native.ptr(v),
+                     _native.ptr(o), dt[q.dtype], dt[k.dtype], dt[v.dtype], B, H, n, cap, D,
+                     int(st.shape[1]), ctypes.c_float(scale), 0, kernel), flops))
+                row_k = D * k.element_size()
+                row_v = D * v.element_size()
+                if dense and t in p.dense_append:
+                    dst, src, ln, items, mx, slots = p.dense_append[t]
+                    out.append(self._pack(p.layer, t, self.dense_k[i], self.dense_v[i], k, v,
+                                          H * n, H * max(p.dense_len, 1), dst, src, ln, items, mx,
+                                          slots, row_k, row_v))
+                if dense and t + 1 == p.first_target and p.activation is not None:
+                    dst, src, ln, items, mx, slots = p.activation
+                    out.append(self._pack(p.layer, t, self.slab_k[i], self.slab_v[i],
+                                          self.dense_k[i], self.dense_v[i],
+                                          H * max(p.dense_len, 1), max(p.capacity, 1), dst, src,
+                                          ln, items, mx, slots, row_k, row_v, flat_src=True))
+                if not dense and t in p.slab_append:
+                    dst, src, ln, items, mx, slots = p.slab_append[t]
+                    out.append(self._pack(p.layer, t, self.slab_k[i], self.slab_v[i], k, v,
+                                          H * n, max(p.capacity, 1), dst, src, ln, items, mx,
+                                          slots, row_k, row_v))
+        return out
+
+    def _pack(self, layer, t, dk, dv, sk, sv, src_rows, dst_rows, dst, src, ln, items, mx, slots,
+              row_k, row_v, flat_src=False):
+        dt = _native.DTYPE_CODES
+        B, D = self.batch, self.head_dim
+        nbytes = 2.0 * slots * B * (row_k + row_v)
+        return Launch("pack", layer, t, self.lib.heatkv_pack_kv,
+                      (_native.ptr(dk), _native.ptr(dv), _native.ptr(sk), _native.ptr(sv),
+                       dt[dk.dtype], dt[dv.dtype], B, src_rows, dst_rows, D, _native.ptr(dst),
+                       _native.ptr(src), _native.ptr(ln), items, mx), nbytes)
+
+    @staticmethod
+    def run(launches, stream=None, events=None) -> None:
+        """Issue the launches on ``stream`` (default: current). ``events[j] = (start, end)``
+        brackets launch j when given (timing events may be external graph nodes)."""
+        s = stream if stream is not None else torch.cuda.current_stream()
+        handle = ctypes.c_void_p(s.cuda_stream)
+        if events is None:
+            for launch in launches:
+                launch(handle)
+        else:
+            for launch, ev in zip(launches, events):
+                if ev is None:
+                    launch(handle)
+                else:
+                    ev[0].record(s)
+                    launch(handle)
+                    ev[1].record(s)
+
+
+def allocate_io(hot: HotPath, *, dtype=torch.bfloat16, seed: int = 0, device=None,
+                pin_host: bool = False, fill: bool = True):
+    """Seeded N(0, 1) inputs ``[plan][t] = (q, k, v)`` and outputs ``[plan][t]`` for one image of
+    ``hot``. Each kind lives in one flat buffer (the views stay contiguous). With ``pin_host`` the
+    buffers are pinned host memory instead."""
+    device = hot.device if device is None else torch.device(device)
+    B, H, D = hot.batch, hot.num_heads, hot.head_dim
+    per_layer = sum(hot.tokens)
+    nl = len(hot.plans)
+    total = nl * B * H * per_layer * D
+    kw = dict(dtype=dtype)
+    if pin_host:
+        bufs = [torch.empty(total, **kw).pin_memory() for _ in range(3)]
+        obuf = torch.empty(total, **kw).pin_memory()
+    else:
+        bufs = [torch.empty(total, device=device, **kw) for _ in range(3)]
+        obuf = torch.empty(total, device=device, **kw)
+    if fill:
+        gen = torch.Generator(device=bufs[0].device).manual_seed(seed)
+        for b in bufs:
+            b.normal_(generator=gen)
+    inputs, outputs = [], []
+    off = 0
+    for _ in range(nl):
+        li, lo = [], []
+        for t in range(hot.num_scales):
+            n = hot.tokens[t]
+            sz = B * H * n * D
+            li.append(tuple(b[off:off + sz].view(B, H, n, D) for b in bufs))
+            lo.append(obuf[off:off + sz].view(B, n, H * D))
+            off += sz
+        inputs.append(li)
+        outputs.append(lo)
+    return inputs, outputs, bufs, obuf

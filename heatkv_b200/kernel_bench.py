@@ -1,0 +1,98 @@
+"""Micro-benchmark of one libheatkv kernel shape (used for tuning sweeps and ncu captures).
+
+    python -m heatkv_b200.kernel_bench attention --rows 2 --heads 16 --q-len 4096 --slots 650
+    python -m heatkv_b200.kernel_bench pack --rows 2 --heads 16 --q-len 4096
+
+``attention``: one call shaped like a fused target of the 2B model - per head six slab segments
+(1, 4, 16, 36, 64 and the rest of ``--slots`` slots) plus ``--q-len`` current tokens.
+``pack``: the append of one scale (every head's ``--q-len`` tokens) into a slab.
+Prints per-call device time (CUDA events, warm, back to back) and the achieved TFLOP/s or GB/s.
+"""
+
+from __future__ import annotations
+
+import argparse
+import math
+
+import torch
+
+from . import _native
+from .real_pruning_fused_attention import (fused_real_pruning_flat_segmented_attention,
+                                           pack_flat_segments_kv)
+
+
+def attention_case(rows, heads, q_len, slots, dtype=torch.bfloat16, device="cuda", seed=0):
+    g = torch.Generator(device=device).manual_seed(seed)
+    q, k, v = (torch.randn(rows, heads, q_len, 128, device=device, generator=g).to(dtype)
+               for _ in range(3))
+    cap = heads * slots
+    pk, pv = (torch.randn(rows, cap, 128, device=device, generator=g).to(dtype) for _ in range(2))
+    lens = [1, 4, 16, 36, 64]
+    lens.append(max(0, slots - sum(lens)))
+    st = torch.zeros(heads, len(lens), dtype=torch.int32)
+    en = torch.zeros_like(st)
+    for h in range(heads):
+        off = h * slots
+        for i, n in enumerate(lens):
+            st[h, i], en[h, i] = off, off + n
+            off += n
+    ct = torch.full((heads,), len(lens), dtype=torch.int32)
+    kw = dict(q=q, persisted_k=pk, persisted_v=pv, segment_starts=st.to(device),
+              segment_ends=en.to(device), segment_counts=ct.to(device), current_k=k, current_v=v,
+              softmax_scale=1.0 / math.sqrt(128))
+    flops = 4.0 * q_len * (slots + q_len) * 128 * rows * heads
+    return kw, flops
+
+
+def time_call(fn, iters, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("kernel", choices=["attention", "pack"])
+    ap.add_argument("--rows", type=int, default=2)
+    ap.add_argument("--heads", type=int, default=16)
+    ap.add_argument("--q-len", type=int, default=4096)
+    ap.add_argument("--slots", type=int, default=650)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--dtype", choices=["bf16", "f16", "f32"], default="bf16")
+    args = ap.parse_args(argv)
+    dtype = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[args.dtype]
+    if args.kernel == "attention":
+        kw, flops = attention_case(args.rows, args.heads, args.q_len, args.slots, dtype)
+        ms = time_call(lambda: fused_real_pruning_flat_segmented_attention(**kw), args.iters,
+                       args.warmup)
+        print(f"attention rows={args.rows} heads={args.heads} q_len={args.q_len} "
+              f"slots={args.slots} {args.dtype}: {ms * 1e3:.1f} us/call, "
+              f"{flops / ms / 1e9:.1f} TFLOP/s", flush=True)
+    else:
+        H, n, B = args.heads, args.q_len, args.rows
+        src_k = torch.randn(B, H * n, 128, device="cuda").to(dtype)
+        src_v = torch.randn(B, H * n, 128, device="cuda").to(dtype)
+        dst_k = torch.zeros(B, H * n + 1000, 128, device="cuda", dtype=dtype)
+        dst_v = torch.zeros_like(dst_k)
+        dst = torch.arange(H, device="cuda", dtype=torch.int64) * n + 7
+        src = torch.arange(H, device="cuda", dtype=torch.int64) * n
+        ln = torch.full((H,), n, device="cuda", dtype=torch.int64)
+        fn = lambda: pack_flat_segments_kv(dst_k=dst_k, dst_v=dst_v, src_k=src_k, src_v=src_v,  # noqa: E731
+                                           dst_starts=dst, src_starts=src, lengths=ln, max_length=n)
+        ms = time_call(fn, args.iters, args.warmup)
+        nbytes = 2.0 * B * H * n * 128 * dst_k.element_size() * 2
+        print(f"pack rows={B} heads={H} tokens={n} {args.dtype}: {ms * 1e3:.1f} us/call, "
+              f"{nbytes / ms / 1e6:.1f} GB/s", flush=True)
+    assert _native.device_status() == 0
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,68 @@
+"""The whole per-image hot path on the GPU (dense-prefix scales, slab activation, per-scale appends,
+fused segmented attention) against an independent formulation: for every (layer, target, head)
+attention over exactly the tokens the keep-mask retains - scales 0..2 always, scale s >= 3 unless
+the controller removes (s, head) at that target - computed with plain PyTorch fp32 on the GPU.
+This checks the slab schedule, the pack descriptors and the kernel together at full 13-scale size.
+"""
+
+import math
+
+import pytest
+import torch
+
+from heatkv_b200 import _native
+from heatkv_b200.hotpath import HotPath, allocate_io
+
+pytestmark = pytest.mark.gpu
+
+BF16_ATOL, BF16_REL = 2e-2, 1e-2
+
+
+def _controller(model, budget):
+    import bench
+    return bench.build_controller(model, budget)
+
+
+def _retained_tokens(ctrl, layer, target, head):
+    ranges = ctrl.scale_ranges
+    mask = ctrl.removed_mask_for_layer(layer)
+    idx = []
+    for s in range(target):
+        if mask[target, s, head]:
+            continue
+        idx.append(torch.arange(ranges[s][0], ranges[s][1]))
+    return torch.cat(idx) if idx else torch.zeros(0, dtype=torch.long)
+
+
+def _reference(ctrl, layer, t, inputs_layer, head_dim=128):
+    q, k, v = inputs_layer[t]
+    B, H, n, D = q.shape
+    full_k = torch.cat([inputs_layer[s][1] for s in range(t + 1)], dim=2).float()
+    full_v = torch.cat([inputs_layer[s][2] for s in range(t + 1)], dim=2).float()
+    start = ctrl.scale_ranges[t][0]
+    out = torch.empty(B, n, H, D, device=q.device)
+    for h in range(H):
+        idx = torch.cat([_retained_tokens(ctrl, layer, t, h),
+                         torch.arange(start, start + n)]).to(q.device)
+        s = torch.einsum("bnd,bsd->bns", q[:, h].float(), full_k[:, h, idx]) / math.sqrt(D)
+        out[:, :, h] = torch.softmax(s, -1) @ full_v[:, h, idx]
+    return out.reshape(B, n, H * D)
+
+
+@pytest.mark.parametrize("model,budget,layers", [("2b", 0.10, [0, 21]), ("2b", 0.05, [3]),
+                                                 ("2b", 1.00, [7]), ("8b", 0.10, [39])])
+def test_hot_path_matches_keep_mask_attention(model, budget, layers):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device("cuda", 0)
+    ctrl, L, H = _controller(model, budget)
+    hot = HotPath(ctrl, L, H, 2, dev, torch.bfloat16, torch.bfloat16, layers=layers)
+    inputs, outputs, _, _ = allocate_io(hot, seed=3)
+    hot.run(hot.launches(inputs, outputs))
+    torch.cuda.synchronize()
+    assert _native.device_status(dev) == 0
+    for i, layer in enumerate(layers):
+        for t in range(hot.num_scales):
+            ref = _reference(ctrl, layer, t, inputs[i])
+            err = (outputs[i][t].float() - ref).abs().max().item()
+            scale = ref.abs().max().item()
+            assert err <= BF16_ATOL and err / scale <= BF16_REL, (layer, t, err, scale)
