@@ -285,11 +285,13 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.synchronize(dev)
     step_ms = start.elapsed_time(end) / args.steps
     att_ms, pack_ms = 0.0, 0.0
+    by_target = [0.0] * hot.num_scales
     for i in range(args.steps):
         for launch, (e0, e1) in zip(launches, ev_sets[args.warmup + i]):
             d = e0.elapsed_time(e1)
             if launch.kind == "attention":
                 att_ms += d
+                by_target[launch.target] += d / args.steps
             else:
                 pack_ms += d
     att_ms /= args.steps
@@ -371,7 +373,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
                      "peak_kind": f"bf16_tflops_sustained ({peak_src})",
                      "frac_of_burst": round(att_achieved / burst, 4),
                      "kernel": "attn_sm100_kernel", "launches_per_step": n_att,
-                     "ms_per_step": round(att_ms, 3)},
+                     "ms_per_step": round(att_ms, 3),
+                     "ms_by_target": [round(x, 3) for x in by_target]},
         "roofline_pack": {"bound": "hbm", "achieved": round(pack_achieved, 1) if pack_achieved else None,
                           "peak": hbm, "unit": "GB/s",
                           "frac": round(pack_achieved / hbm, 4) if pack_achieved else None,

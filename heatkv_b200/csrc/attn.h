@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <stddef.h>
 #include <stdint.h>
 
 namespace heatkv {
@@ -22,6 +23,10 @@ struct AttnArgs {
   int64_t capacity;
   int64_t max_segments;
   float scale;
+  const int32_t* head_order = nullptr;  // [heads] permutation, longest first; null = natural
+  int kv_splits = 1;                    // key-range splits per query block; 0 = automatic
+  void* workspace = nullptr;            // split partials and counters (zeroed before first use)
+  size_t workspace_bytes = 0;
 };
 
 constexpr int kMaxSegments = 256;
@@ -30,6 +35,9 @@ cudaError_t launch_attention_simt(const AttnArgs& a, int q_dtype, int k_dtype, i
                                   cudaStream_t st);
 // Returns cudaErrorNotSupported when the tensor-core kernel cannot take these arguments.
 cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st);
+// Splits chosen by kv_splits = 0 and the workspace bytes a launch with `splits` needs.
+int attention_auto_splits(int64_t batch, int64_t heads, int64_t q_len);
+size_t attention_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int splits);
 
 cudaError_t launch_pack_kv(void* dst_k, void* dst_v, const void* src_k, const void* src_v,
                            int64_t row_bytes_k, int64_t row_bytes_v, int64_t batch,

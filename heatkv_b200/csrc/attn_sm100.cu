@@ -1,4 +1,5 @@
-// Segmented flat-slab attention on Blackwell tensor cores (sm_100a): TMA + tcgen05 + TMEM.
+// Segmented flat-slab attention on Blackwell tensor cores (sm_100a): TMA + tcgen05 + TMEM, with a
+// persistent length-aware scheduler and split-KV.
 //
 // Computes what _fused_real_pruning_segmented_attention_kernel (real_pruning_fused_attention.py:76-267)
 // computes with its default bf16 dot modes: for batch row b and head h, the keys are the head's
@@ -6,22 +7,31 @@
 // scale) with fp32 scores and fp32 row sums, P rounded to the value dtype for the PV product, fp32
 // accumulation, output [B, Lq, H*D] in q's dtype.
 //
-// Design (one CTA per (b, h, 256 query rows), 1 CTA per SM):
-//   * warp 8      : TMA producer. Q (two 128-row tiles) once, then K and V tiles of 128 keys into
-//                   a 2-stage ring. A tile is 128 rows of one segment (or of the current scale);
-//                   pruned scales have no segment and cost nothing. Rows past a segment's end are
-//                   loaded but masked; rows past the tensor end are zero-filled by TMA.
-//   * warp 9      : TMEM allocator and single-thread tcgen05.mma issuer.
-//                   S_t = Q_t K^T (M=128, N=128, K=128, SS operands, K-major SW128) into TMEM,
-//                   O_t += P_t V (A = P_t read from TMEM, B = V as an MN-major SW128 operand).
-//                   Issue order per key tile j: PV_0(j-1), QK_0(j), PV_1(j-1), QK_1(j), so one Q
-//                   tile's MMAs run while the other tile's softmax runs.
+// Work decomposition. A query block is 256 rows (two 128-row Q tiles) of one (b, h). Its key
+// tiles are the head's segments in 128-row steps followed by the current scale's tiles; pruned
+// scales have no segment and cost nothing. An item is (head, b, query block, split): with
+// kv_splits = S > 1 the block's key tiles are divided into S contiguous ranges whose partial
+// results (unnormalised O, running max m, row sum l) go to the workspace; the CTA that finishes a
+// block's last split (an atomic counter per block) merges the S partials into the output. Items
+// are ordered longest head first (head_order, computed by the host from the segment lengths) and
+// CTA c of a persistent grid of at most one CTA per SM runs items c, c + grid, c + 2*grid, ...
+// which balances the uneven slab lengths across the SMs. No CTA ever waits on another.
+//
+// CTA roles (384 threads, 1 CTA per SM, 201 KB shared memory):
+//   * warp 8       : TMA producer. Per item the two Q tiles (after the previous item's last QK),
+//                    then K and V tiles into a 2-stage ring. Rows past a segment's end are loaded
+//                    and masked; rows past the tensor end are zero-filled by TMA.
+//   * warp 9       : TMEM allocator and single-thread tcgen05.mma issuer.
+//                    S_t = Q_t K^T (M=128, N=128, K=128, both operands K-major SW128 in smem),
+//                    O_t += P_t V (A = P_t read from TMEM, B = V as an MN-major SW128 operand).
+//                    Issue order per key tile j: PV_0(j-1), QK_0(j), PV_1(j-1), QK_1(j), so one Q
+//                    tile's MMAs run while the other tile's softmax runs.
 //   * warps 0-3, 4-7 : softmax warpgroups of Q tiles 0 and 1, one TMEM lane (query row) per
-//                   thread. Scores are read from TMEM, masked past the tile's valid keys, and
-//                   turned into P = exp2(s*scale*log2e - m) which is written back into TMEM over
-//                   the scores (bf16/f16 pairs). The running max m is only raised when a tile's
-//                   max exceeds it by more than 8 (factor 256); O in TMEM is then rescaled in
-//                   place. The final O / l is written straight to global memory.
+//                    thread. Scores come from TMEM in one 128-column load, P = exp2(s*scale*log2e
+//                    - m) is written back over them as bf16/f16 pairs. The running max is only
+//                    raised when a tile exceeds it by more than 8 (factor 256); O in TMEM is then
+//                    rescaled in place. The epilogue writes O / l (or a partial) from TMEM.
+//   * warps 10-11  : idle (they complete the third warpgroup for the register split).
 //   TMEM columns: S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512).
 // Every wait is bounded (common.cuh); on expiry the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains
 // its in-flight copies and MMAs, frees TMEM and returns.
@@ -31,6 +41,8 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <algorithm>
 #include <mutex>
 
 namespace heatkv {
@@ -38,22 +50,26 @@ namespace heatkv {
 namespace sm100 {
 
 constexpr int kBM = 128;        // query rows per Q tile
-constexpr int kNQ = 2;          // Q tiles per CTA
+constexpr int kNQ = 2;          // Q tiles per query block
 constexpr int kBN = 128;        // keys per K/V tile
 constexpr int kD = 128;         // head dim
 constexpr int kStages = 2;      // K/V ring depth
-constexpr int kThreads = 320;   // 10 warps
+constexpr int kThreads = 384;   // 12 warps = 3 warpgroups
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr uint32_t kHalfBytes = kBM * 64 * 2;    // one 128-row x 64-column 16-bit box: 16 KiB
 constexpr uint32_t kTileBytes = 2 * kHalfBytes;  // 128 x 128 x 2 bytes
 constexpr uint32_t kTmemCols = 512;
+constexpr int kMaxHeads = 128;
+constexpr int kMaxSegTable = 2048;               // heads x segments kept in shared memory
+constexpr int kNumSms = 148;
+constexpr int kMaxSplits = 4;             // key-range splits per query block
 
 struct __align__(1024) Smem {
   uint8_t q[kNQ][kTileBytes];
   uint8_t k[kStages][kTileBytes];
   uint8_t v[kStages][kTileBytes];
-  uint64_t q_full;
+  uint64_t q_full, q_empty;
   uint64_t k_full[kStages];
   uint64_t k_empty[kStages];
   uint64_t v_full[kStages];
@@ -61,13 +77,16 @@ struct __align__(1024) Smem {
   uint64_t s_full[kNQ];
   uint64_t p_full[kNQ];
   uint64_t o_final[kNQ];
+  uint64_t o_free[kNQ];
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
-  int nseg;
-  int ntiles;
-  int seg_start[kMaxSegments];
-  int seg_end[kMaxSegments];
+  int last_flag;
+  int head_order[kMaxHeads];
+  int head_nseg[kMaxHeads];     // compacted segments of each head
+  int head_tiles[kMaxHeads];    // key tiles of each head (segments + current scale)
+  int seg_start[kMaxSegTable];  // [head * seg_stride + i]
+  int seg_end[kMaxSegTable];
 };
 
 struct Params {
@@ -75,30 +94,76 @@ struct Params {
   const int32_t* seg_starts;
   const int32_t* seg_ends;
   const int32_t* seg_counts;
+  const int32_t* head_order;  // [heads] or null (natural order)
   void* out;
-  float scale_log2;  // softmax_scale * log2(e)
-  int qpairs;        // ceil(Lq / 256)
+  uint32_t* ws_counter;       // [blocks] (zero between calls) when splits > 1
+  float2* ws_ml;              // [blocks * splits * 256]
+  float* ws_o;                // [blocks * splits * 256 * 128]
+  float scale_log2;           // softmax_scale * log2(e)
+  int qpairs;                 // query blocks per (b, h): ceil(Lq / 256)
+  int splits;                 // key-range splits per query block
+  int n_items;                // heads * batch * qpairs * splits
+  int seg_stride;             // segment-table row length (max_segments)
 };
+
+struct Item {
+  int h, b, qp, split, block;  // block = (rank * batch + b) * qpairs + qp
+  int q0, nq;                  // first query row, Q tiles (1 or 2)
+  int j0, n;                   // first key tile of the split, number of key tiles
+};
+
+__device__ __forceinline__ Item decode_item(const Smem& sm, const Params& p, int item) {
+  Item it;
+  it.split = item % p.splits;
+  it.block = item / p.splits;
+  it.qp = it.block % p.qpairs;
+  const int rb = it.block / p.qpairs;
+  it.b = rb % static_cast<int>(p.batch);
+  const int rank = rb / static_cast<int>(p.batch);
+  it.h = sm.head_order[rank];
+  it.q0 = it.qp * (kNQ * kBM);
+  it.nq = (static_cast<int>(p.q_len) - it.q0) > kBM ? 2 : 1;
+  const int tiles = sm.head_tiles[it.h];
+  it.j0 = static_cast<int>((int64_t(tiles) * it.split) / p.splits);
+  it.n = static_cast<int>((int64_t(tiles) * (it.split + 1)) / p.splits) - it.j0;
+  return it;
+}
 
 // Walks the key tiles of one head: each segment in 128-row steps, then the current scale.
 struct TileCursor {
-  int seg;
-  int pos;
+  const int* st;
+  const int* en;
+  int nseg, seg, pos;
   bool current;
-  __device__ void begin(const Smem& sm) {
+  // position on tile j0 of head h
+  __device__ void begin(const Smem& sm, int h, int stride, int j0) {
+    st = sm.seg_start + h * stride;
+    en = sm.seg_end + h * stride;
+    nseg = sm.head_nseg[h];
     seg = 0;
-    current = sm.nseg == 0;
-    pos = current ? 0 : sm.seg_start[0];
-  }
-  __device__ int valid(const Smem& sm, int q_len) const {
-    return current ? min(kBN, q_len - pos) : min(kBN, sm.seg_end[seg] - pos);
-  }
-  __device__ void next(const Smem& sm, int q_len) {
-    pos += kBN;
-    if (!current && pos >= sm.seg_end[seg]) {
+    current = false;
+    while (seg < nseg) {
+      const int t = (en[seg] - st[seg] + kBN - 1) / kBN;
+      if (j0 < t) break;
+      j0 -= t;
       ++seg;
-      if (seg < sm.nseg) {
-        pos = sm.seg_start[seg];
+    }
+    if (seg < nseg) {
+      pos = st[seg] + j0 * kBN;
+    } else {
+      current = true;
+      pos = j0 * kBN;
+    }
+  }
+  __device__ int valid(int q_len) const {
+    return current ? min(kBN, q_len - pos) : min(kBN, en[seg] - pos);
+  }
+  __device__ void next() {
+    pos += kBN;
+    if (!current && pos >= en[seg]) {
+      ++seg;
+      if (seg < nseg) {
+        pos = st[seg];
       } else {
         current = true;
         pos = 0;
@@ -124,26 +189,19 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
-// 128 consecutive TMEM columns of this warp's 32 lanes, waited on inside the same asm so no use
-// of the registers can be scheduled before the data has arrived.
-__device__ __forceinline__ void tmem_ld128_sync(uint32_t taddr, float (&x)[128]) {
-  uint32_t r[32];
+__device__ __forceinline__ void tmem_ld16_sync(uint32_t taddr, float (&x)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr + c * 32)
-        : "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[i]);
-  }
+  for (int i = 0; i < 16; ++i) x[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ void tmem_ld32_sync(uint32_t taddr, float (&x)[32]) {
@@ -163,6 +221,75 @@ __device__ __forceinline__ void tmem_ld32_sync(uint32_t taddr, float (&x)[32]) {
   for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r[i]);
 }
 
+
+// All 128 TMEM columns of this thread's lane in one load, waited on inside the same asm so no use
+// of the registers can be scheduled before the data has arrived.
+__device__ __forceinline__ void tmem_ld_row128(uint32_t taddr, float (&x)[128]) {
+  uint32_t r[128];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]), "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]), "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]), "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 128; ++i) x[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// packed pairs of fp32 (sm_100 f32x2 arithmetic)
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^y for a pair on the FMA pipe (offloads MUFU). y is rounded to the nearest integer n with the
+// 1.5*2^23 shift, 2^(y-n) on [-0.5, 0.5] comes from a cubic fitted here by weighted least squares
+// (max relative error 7.5e-5, far below the bf16 rounding P receives), and n is added to the
+// exponent field. Inputs below -125 are clamped (2^-125 is negligible next to the row sum >= 1).
+__device__ __forceinline__ void exp2_poly_x2(uint64_t y, float& r0, float& r1) {
+  float y0, y1;
+  f2unpack(y, y0, y1);
+  y = f2pack(fmaxf(y0, -125.f), fmaxf(y1, -125.f));
+  const uint64_t magic = f2pack(12582912.f, 12582912.f);
+  const uint64_t neg_magic = f2pack(-12582912.f, -12582912.f);
+  const uint64_t t = add2(y, magic);
+  const uint64_t n = add2(t, neg_magic);
+  const uint64_t f = fma2(n, f2pack(-1.f, -1.f), y);
+  uint64_t p = fma2(f, f2pack(0.055186375975608826f, 0.055186375975608826f),
+                    f2pack(0.24261236190795898f, 0.24261236190795898f));
+  p = fma2(p, f, f2pack(0.6932582855224609f, 0.6932582855224609f));
+  p = fma2(p, f, f2pack(0.9999279379844666f, 0.9999279379844666f));
+  float p0, p1, t0, t1;
+  f2unpack(p, p0, p1);
+  f2unpack(t, t0, t1);
+  r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
+// Pairs of P columns whose exp2 runs on the FMA pipe: pair i with (i % kPolyMod) >= kPolyMod -
+// kPolyCount, kPolyCount being a template parameter of the kernel (0..kPolyMod).
+constexpr int kPolyMod = 4;
+
 // A drain wait for the error path: bounded, ignores the abort flag.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   const long long t0 = clock64();
@@ -174,7 +301,12 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   }
 }
 
-template <bool kBF16>
+
+__device__ __forceinline__ void named_bar_softmax() {
+  asm volatile("bar.sync 1, 256;" ::: "memory");
+}
+
+template <bool kBF16, int kPolyCount>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_ck,
@@ -185,22 +317,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem& sm = *reinterpret_cast<Smem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   volatile int* abort_flag = &sm.abort_flag;
-
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  // work item: blockIdx.x = (h * batch + b) * qpairs + qp
-  const int qp = blockIdx.x % p.qpairs;
-  const int bh_lin = blockIdx.x / p.qpairs;
-  const int b = bh_lin % p.batch;
-  const int h = bh_lin / p.batch;
   const int Lq = static_cast<int>(p.q_len);
-  const int q0 = qp * (kNQ * kBM);
-  const int nq = (Lq - q0) > kBM ? 2 : 1;
+  const int H = static_cast<int>(p.heads);
+  const int stride = p.seg_stride;
 
   // ---------------------------------------------------------------- setup
   if (threadIdx.x == 0) {
     sm.abort_flag = 0;
     mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.q_empty, 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.k_full[s], 1);
       mbar_init(&sm.k_empty[s], 1);
@@ -209,45 +336,54 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < kNQ; ++t) {
       mbar_init(&sm.s_full[t], 1);
-      mbar_init(&sm.p_full[t], kBM);
+      mbar_init(&sm.p_full[t], 4);   // one arrive per softmax warp
       mbar_init(&sm.o_final[t], 1);
+      mbar_init(&sm.o_free[t], 4);
     }
     mbar_init(&sm.drain, 1);
     fence_mbar_init();
   }
   if (warp == kProducerWarp) {
-    // this head's non-empty segments, clipped to the slab, compacted in order
-    const int cnt = max(0, min(p.seg_counts[h], static_cast<int>(p.max_segments)));
-    int total = 0;
-    bool clipped = false;
-    for (int base = 0; base < cnt; base += 32) {
-      const int i = base + lane;
-      int s = 0, e = 0;
-      if (i < cnt) {
-        s = p.seg_starts[int64_t(h) * p.max_segments + i];
-        e = p.seg_ends[int64_t(h) * p.max_segments + i];
-        if (s < e && (s < 0 || e > p.capacity)) clipped = true;
-        s = max(s, 0);
-        e = static_cast<int>(min64(e, p.capacity));
-      }
-      const bool keep = (i < cnt) && (s < e);
-      const unsigned m = __ballot_sync(0xffffffffu, keep);
-      if (keep) {
-        const int slot = total + __popc(m & ((1u << lane) - 1u));
-        sm.seg_start[slot] = s;
-        sm.seg_end[slot] = e;
-      }
-      total += __popc(m);
+    // stage the [H, S] metadata, then compact every head's non-empty segments in place, clipped
+    // to the slab, and count its key tiles
+    const int S = static_cast<int>(p.max_segments);
+    for (int i = lane; i < H * S; i += 32) {
+      sm.seg_start[i] = p.seg_starts[i];
+      sm.seg_end[i] = p.seg_ends[i];
     }
-    if (__any_sync(0xffffffffu, clipped) && lane == 0 && b == 0 && qp == 0)
-      raise_status(HEATKV_DEVICE_BAD_SEGMENT);
+    bool bad = false;
+    for (int r = lane; r < H; r += 32) {
+      int h = p.head_order ? p.head_order[r] : r;
+      if (h < 0 || h >= H) {
+        bad = true;
+        h = r;
+      }
+      sm.head_order[r] = h;
+      sm.head_nseg[r] = p.seg_counts[r];
+    }
     __syncwarp();
+    for (int h = lane; h < H; h += 32) {
+      const int cnt = max(0, min(sm.head_nseg[h], S));
+      int n = 0, tiles = 0;
+      for (int i = 0; i < cnt; ++i) {
+        int s0 = sm.seg_start[h * S + i];
+        int e0 = sm.seg_end[h * S + i];
+        if (s0 >= e0) continue;
+        if (s0 < 0 || e0 > p.capacity) bad = true;
+        s0 = max(s0, 0);
+        e0 = static_cast<int>(min64(e0, p.capacity));
+        if (s0 >= e0) continue;
+        sm.seg_start[h * S + n] = s0;  // n <= i: compaction in place
+        sm.seg_end[h * S + n] = e0;
+        ++n;
+        tiles += (e0 - s0 + kBN - 1) / kBN;
+      }
+      sm.head_nseg[h] = n;
+      sm.head_tiles[h] = tiles + (Lq + kBN - 1) / kBN;
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0 && blockIdx.x == 0)
+      raise_status(HEATKV_DEVICE_BAD_SEGMENT);
     if (lane == 0) {
-      int nt = 0;
-      for (int i = 0; i < total; ++i) nt += (sm.seg_end[i] - sm.seg_start[i] + kBN - 1) / kBN;
-      nt += (Lq + kBN - 1) / kBN;
-      sm.nseg = total;
-      sm.ntiles = nt;
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_ck);
       tma_prefetch_desc(&tm_cv);
@@ -263,48 +399,65 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const int ntiles = sm.ntiles;
+
+  // Register split. The launch holds kThreads x 168 = 64,512 registers (ptxas cap for 384
+  // threads); the producer/MMA warpgroup gives back to 56 and the two softmax warpgroups grow to
+  // 224: 128 x 56 + 2 x 128 x 224 = 64,512, exactly the launch total.
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+  }
 
   if (warp == kProducerWarp) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
-      const int qrow = static_cast<int>((int64_t(b) * p.heads + h) * p.q_len) + q0;
-      mbar_arrive_expect_tx(&sm.q_full, nq * kTileBytes);
-      for (int t = 0; t < nq; ++t) {
-        tma_load_2d(sm.q[t], &tm_q, 0, qrow + t * kBM, &sm.q_full);
-        tma_load_2d(sm.q[t] + kHalfBytes, &tm_q, 64, qrow + t * kBM, &sm.q_full);
-      }
-      const int cur_row0 = static_cast<int>((int64_t(b) * p.heads + h) * p.q_len);
-      const int slab_row0 = static_cast<int>(int64_t(b) * p.capacity);
-      TileCursor cur;
-      cur.begin(sm);
-      int j = 0;
-      for (; j < ntiles; ++j) {
-        const int s = j % kStages;
-        const uint32_t use = j / kStages;
-        const CUtensorMap* mk = cur.current ? &tm_ck : &tm_sk;
-        const CUtensorMap* mv = cur.current ? &tm_cv : &tm_sv;
-        const int row = cur.current ? cur_row0 + cur.pos : slab_row0 + cur.pos;
-        if (j >= kStages && !mbar_wait(&sm.k_empty[s], (use - 1) & 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&sm.k_full[s], kTileBytes);
-        tma_load_2d(sm.k[s], mk, 0, row, &sm.k_full[s]);
-        tma_load_2d(sm.k[s] + kHalfBytes, mk, 64, row, &sm.k_full[s]);
-        if (j >= kStages && !mbar_wait(&sm.v_empty[s], (use - 1) & 1, abort_flag)) {
-          ++j;  // the K half of this tile is in flight
-          break;
+      uint32_t gk = 0, gv = 0, qcnt = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+        const Item it = decode_item(sm, p, item);
+        if (it.n == 0) continue;
+        if (qcnt > 0 && !(ok = mbar_wait(&sm.q_empty, (qcnt - 1) & 1, abort_flag))) break;
+        const int bh = it.b * H + it.h;
+        const int qrow = bh * Lq + it.q0;
+        mbar_arrive_expect_tx(&sm.q_full, it.nq * kTileBytes);
+        for (int t = 0; t < it.nq; ++t) {
+          tma_load_2d(sm.q[t], &tm_q, 0, qrow + t * kBM, &sm.q_full);
+          tma_load_2d(sm.q[t] + kHalfBytes, &tm_q, 64, qrow + t * kBM, &sm.q_full);
         }
-        mbar_arrive_expect_tx(&sm.v_full[s], kTileBytes);
-        tma_load_2d(sm.v[s], mv, 0, row, &sm.v_full[s]);
-        tma_load_2d(sm.v[s] + kHalfBytes, mv, 64, row, &sm.v_full[s]);
-        cur.next(sm, Lq);
+        ++qcnt;
+        const int cur_row0 = bh * Lq;
+        const int slab_row0 = static_cast<int>(int64_t(it.b) * p.capacity);
+        TileCursor cur;
+        cur.begin(sm, it.h, stride, it.j0);
+        for (int j = 0; j < it.n; ++j) {
+          const CUtensorMap* mk = cur.current ? &tm_ck : &tm_sk;
+          const CUtensorMap* mv = cur.current ? &tm_cv : &tm_sv;
+          const int row = cur.current ? cur_row0 + cur.pos : slab_row0 + cur.pos;
+          int s = gk % kStages;
+          if (gk >= kStages && !(ok = mbar_wait(&sm.k_empty[s], ((gk / kStages) - 1) & 1, abort_flag)))
+            break;
+          mbar_arrive_expect_tx(&sm.k_full[s], kTileBytes);
+          tma_load_2d(sm.k[s], mk, 0, row, &sm.k_full[s]);
+          tma_load_2d(sm.k[s] + kHalfBytes, mk, 64, row, &sm.k_full[s]);
+          ++gk;
+          s = gv % kStages;
+          if (gv >= kStages && !(ok = mbar_wait(&sm.v_empty[s], ((gv / kStages) - 1) & 1, abort_flag)))
+            break;
+          mbar_arrive_expect_tx(&sm.v_full[s], kTileBytes);
+          tma_load_2d(sm.v[s], mv, 0, row, &sm.v_full[s]);
+          tma_load_2d(sm.v[s] + kHalfBytes, mv, 64, row, &sm.v_full[s]);
+          ++gv;
+          cur.next();
+        }
       }
-      if (*abort_flag) {
+      if (!ok || *abort_flag) {
         // let every copy already issued land before the CTA's shared memory goes away
-        mbar_drain(&sm.q_full, 0);
-        for (int jj = max(0, j - kStages); jj < j; ++jj) {
-          mbar_drain(&sm.k_full[jj % kStages], (jj / kStages) & 1);
-          mbar_drain(&sm.v_full[jj % kStages], (jj / kStages) & 1);
-        }
+        if (qcnt > 0) mbar_drain(&sm.q_full, (qcnt - 1) & 1);
+        for (uint32_t g = gk > kStages ? gk - kStages : 0; g < gk; ++g)
+          mbar_drain(&sm.k_full[g % kStages], (g / kStages) & 1);
+        for (uint32_t g = gv > kStages ? gv - kStages : 0; g < gv; ++g)
+          mbar_drain(&sm.v_full[g % kStages], (g / kStages) & 1);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -312,160 +465,320 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_f16(kBF16, kBM, kBN, false, false);
       constexpr uint32_t idesc_pv = idesc_f16(kBF16, kBM, kD, false, true);
-      const uint32_t tm_s[2] = {tmem + 0, tmem + 128};
-      const uint32_t tm_o[2] = {tmem + 256, tmem + 384};
-      bool ok = mbar_wait(&sm.q_full, 0, abort_flag);
-      if (ok) tc_fence_after();
-      auto issue_pv = [&](int t, int jj) {
-        const uint32_t vbase = smem_u32(sm.v[jj % kStages]);
+      auto issue_pv = [&](int t, uint32_t g, bool accumulate) {
+        const uint32_t vbase = smem_u32(sm.v[g % kStages]);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           // B = V rows [16kk, 16kk+16): 16 keys x 128 columns, MN-major; 8-key groups 1 KiB
           // apart (SBO), the two 64-column halves 16 KiB apart (LBO)
           const uint64_t bdesc = smem_desc_sw128(vbase + kk * 2048, kHalfBytes, 1024);
-          umma_ts(tm_o[t], tm_s[t] + kk * 8, bdesc, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+          umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, bdesc, idesc_pv,
+                  (accumulate || kk > 0) ? 1u : 0u);
         }
       };
-      auto issue_qk = [&](int t, int jj) {
+      auto issue_qk = [&](int t, uint32_t g) {
         const uint32_t qbase = smem_u32(sm.q[t]);
-        const uint32_t kbase = smem_u32(sm.k[jj % kStages]);
+        const uint32_t kbase = smem_u32(sm.k[g % kStages]);
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk / 4) * kHalfBytes + (kk % 4) * 32;
           const uint64_t adesc = smem_desc_sw128(qbase + off, 16, 1024);
           const uint64_t bdesc = smem_desc_sw128(kbase + off, 16, 1024);
-          umma_ss(tm_s[t], adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+          umma_ss(tmem + t * 128, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
-      for (int j = 0; ok && j < ntiles; ++j) {
-        const int s = j % kStages;
-        if (!(ok = mbar_wait(&sm.k_full[s], (j / kStages) & 1, abort_flag))) break;
+      uint32_t g = 0, qcnt = 0;
+      uint32_t pcnt[kNQ] = {0, 0}, ocnt[kNQ] = {0, 0};
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+        const Item it = decode_item(sm, p, item);
+        if (it.n == 0) continue;
+        if (!(ok = mbar_wait(&sm.q_full, qcnt & 1, abort_flag))) break;
+        ++qcnt;
         tc_fence_after();
-        for (int t = 0; t < nq && ok; ++t) {
-          if (j > 0) {
-            if (t == 0) {
-              if (!(ok = mbar_wait(&sm.v_full[(j - 1) % kStages], ((j - 1) / kStages) & 1,
-                                   abort_flag)))
+        for (int j = 0; ok && j < it.n; ++j) {
+          const uint32_t gj = g + j;
+          for (int t = 0; t < it.nq; ++t) {
+            if (j > 0) {
+              if (t == 0 && !(ok = mbar_wait(&sm.v_full[(gj - 1) % kStages], ((gj - 1) / kStages) & 1,
+                                              abort_flag)))
                 break;
+              if (!(ok = mbar_wait(&sm.p_full[t], (pcnt[t] + j - 1) & 1, abort_flag))) break;
+              if (j == 1 && ocnt[t] > 0 &&
+                  !(ok = mbar_wait(&sm.o_free[t], (ocnt[t] - 1) & 1, abort_flag)))
+                break;
+              tc_fence_after();
+              issue_pv(t, gj - 1, j > 1);
+              if (t == it.nq - 1) tc_commit(&sm.v_empty[(gj - 1) % kStages]);
             }
-            if (!(ok = mbar_wait(&sm.p_full[t], (j - 1) & 1, abort_flag))) break;
-            tc_fence_after();
-            issue_pv(t, j - 1);
-            if (t == nq - 1) tc_commit(&sm.v_empty[(j - 1) % kStages]);
+            if (t == 0) {
+              if (!(ok = mbar_wait(&sm.k_full[gj % kStages], (gj / kStages) & 1, abort_flag))) break;
+              tc_fence_after();
+            }
+            issue_qk(t, gj);
+            tc_commit(&sm.s_full[t]);
           }
-          issue_qk(t, j);
-          tc_commit(&sm.s_full[t]);
+          if (!ok) break;
+          tc_commit(&sm.k_empty[gj % kStages]);
+          if (j == it.n - 1) tc_commit(&sm.q_empty);
         }
-        if (ok) tc_commit(&sm.k_empty[s]);
-      }
-      if (ok) {
-        const int j = ntiles - 1;
-        ok = mbar_wait(&sm.v_full[j % kStages], (j / kStages) & 1, abort_flag);
-        for (int t = 0; t < nq && ok; ++t) {
-          if (!(ok = mbar_wait(&sm.p_full[t], j & 1, abort_flag))) break;
+        if (!ok) break;
+        const uint32_t gl = g + it.n - 1;
+        if (!(ok = mbar_wait(&sm.v_full[gl % kStages], (gl / kStages) & 1, abort_flag))) break;
+        for (int t = 0; t < it.nq; ++t) {
+          if (!(ok = mbar_wait(&sm.p_full[t], (pcnt[t] + it.n - 1) & 1, abort_flag))) break;
+          if (it.n == 1 && ocnt[t] > 0 &&
+              !(ok = mbar_wait(&sm.o_free[t], (ocnt[t] - 1) & 1, abort_flag)))
+            break;
           tc_fence_after();
-          issue_pv(t, j);
+          issue_pv(t, gl, it.n > 1);
           tc_commit(&sm.o_final[t]);
+        }
+        if (!ok) break;
+        tc_commit(&sm.v_empty[gl % kStages]);
+        g += it.n;
+        for (int t = 0; t < it.nq; ++t) {
+          pcnt[t] += it.n;
+          ocnt[t] += 1;
         }
       }
       // every MMA issued by this thread has completed once `drain` fires
       tc_commit(&sm.drain);
       mbar_drain(&sm.drain, 0);
     }
-  } else {
+  } else if (warp < 8) {
     // ---------------------------------------------------------------- softmax warpgroups
     const int t = warp / 4;
     const int quad = warp % 4;
-    if (t < nq) {
-      const int row = quad * 32 + lane;  // TMEM lane == query row within the tile
-      const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-      const uint32_t tS = tmem + lane_off + t * 128;
-      const uint32_t tO = tmem + lane_off + 256 + t * 128;
-      const float c = p.scale_log2;
+    const int row = quad * 32 + lane;  // TMEM lane == query row within the tile
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t tS = tmem + lane_off + t * 128;
+    const uint32_t tO = tmem + lane_off + 256 + t * 128;
+    const float c = p.scale_log2;
+    using OutT = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
+    uint32_t cnt = 0, ocnt = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+      const Item it = decode_item(sm, p, item);
+      const bool active = ok && (t < it.nq) && (it.n > 0);
       float m_run = -INFINITY;
       float l_run = 0.f;
-      bool ok = true;
-      TileCursor cur;
-      cur.begin(sm);
-      for (int j = 0; j < ntiles; ++j) {
-        const int valid = cur.valid(sm, Lq);
-        ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], j & 1, abort_flag));
-        if (!ok) break;
-        tc_fence_after();
-        float x[128];
-        tmem_ld128_sync(tS, x);
-        float mx = -INFINITY;
-        if (valid >= kBN) {
+      if (active) {
+        TileCursor cur;
+        cur.begin(sm, it.h, stride, it.j0);
+        for (int j = 0; j < it.n; ++j) {
+          const int valid = cur.valid(Lq);
+          ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], (cnt + j) & 1, abort_flag));
+          if (!ok) break;
+          tc_fence_after();
+          float x[128];
+          tmem_ld_row128(tS, x);
+          if (valid < kBN) {
 #pragma unroll
-          for (int i = 0; i < 128; ++i) mx = fmaxf(mx, x[i]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 128; ++i) {
-            x[i] = (i < valid) ? x[i] : -INFINITY;
-            mx = fmaxf(mx, x[i]);
+            for (int i = 0; i < 128; ++i) x[i] = (i < valid) ? x[i] : -INFINITY;
           }
-        }
-        const float mx2 = mx * c;
-        if (j == 0) {
-          m_run = mx2;
-        } else if (__any_sync(0xffffffffu, mx2 > m_run + 8.0f)) {
-          // raise the running max; rescale this row of O (PV(j-1) has completed: the commit
-          // that signalled S(j) covers every earlier MMA)
-          const float m_new = fmaxf(m_run, mx2);
-          const float alpha = ex2(m_run - m_new);
-          l_run *= alpha;
-          m_run = m_new;
+          // row max: 8 independent chains of 3-input max
+          float a[8];
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            float o[32];
-            tmem_ld32_sync(tO + cc * 32, o);
-            uint32_t w[32];
+          for (int k = 0; k < 8; ++k) a[k] = fmaxf(x[k], x[k + 8]);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[i] * alpha);
-            tmem_st32(tO + cc * 32, w);
+          for (int i = 2; i < 16; i += 2) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) a[k] = max3f(a[k], x[k + 8 * i], x[k + 8 * i + 8]);
           }
-        }
-        const float neg_m = -m_run;
-        float sum = 0.f;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pk[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float p0 = ex2(fmaf(x[64 * half + 2 * i], c, neg_m));
-            const float p1 = ex2(fmaf(x[64 * half + 2 * i + 1], c, neg_m));
-            sum += p0 + p1;
-            pk[i] = pack2<kBF16>(p0, p1);
+          const float mx =
+              max3f(max3f(a[0], a[1], a[2]), max3f(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+          const float mx2 = mx * c;
+          // Lazy max: keep the running max unless this tile exceeds it by more than 8 (a factor
+          // of 256 in P); raising it requires rescaling this row of O, done below once the scores
+          // are dead (PV(j-1) has completed: the commit that signalled S(j) covers it).
+          float alpha = 1.f;
+          bool rescale = false;
+          if (j == 0) {
+            m_run = mx2;
+          } else if (__any_sync(0xffffffffu, mx2 > m_run + 8.0f)) {
+            const float m_new = fmaxf(m_run, mx2);
+            alpha = ex2(m_run - m_new);
+            l_run *= alpha;
+            m_run = m_new;
+            rescale = true;
           }
-          tmem_st32(tS + 32 * half, pk);
+          // P = exp2(s * c - m) in pairs; 4 partial row sums
+          const uint64_t c2 = f2pack(c, c);
+          const uint64_t nm2 = f2pack(-m_run, -m_run);
+          uint64_t acc[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) acc[k] = f2pack(0.f, 0.f);
+#pragma unroll
+          for (int quarter = 0; quarter < 4; ++quarter) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int pi = quarter * 16 + i;  // pair index: columns 2pi, 2pi+1
+              const uint64_t y = fma2(f2pack(x[2 * pi], x[2 * pi + 1]), c2, nm2);
+              float p0, p1;
+              if ((pi % kPolyMod) >= kPolyMod - kPolyCount) {
+                exp2_poly_x2(y, p0, p1);
+                if (valid < kBN) {
+                  p0 = (2 * pi < valid) ? p0 : 0.f;
+                  p1 = (2 * pi + 1 < valid) ? p1 : 0.f;
+                }
+              } else {
+                float y0, y1;
+                f2unpack(y, y0, y1);
+                p0 = ex2(y0);
+                p1 = ex2(y1);
+              }
+              acc[pi & 3] = add2(acc[pi & 3], f2pack(p0, p1));
+              pk[i] = pack2<kBF16>(p0, p1);
+            }
+            tmem_st16(tS + 16 * quarter, pk);
+          }
+          {
+            const uint64_t s01 = add2(acc[0], acc[1]);
+            const uint64_t s23 = add2(acc[2], acc[3]);
+            float u0, u1;
+            f2unpack(add2(s01, s23), u0, u1);
+            l_run += u0 + u1;
+          }
+          if (rescale) {  // warp-uniform
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+              float o[16];
+              tmem_ld16_sync(tO + cc * 16, o);
+              uint32_t w[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(o[i] * alpha);
+              tmem_st16(tO + cc * 16, w);
+            }
+          }
+          // every lane's TMEM stores are complete and ordered before the warp's single arrive
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.p_full[t]);
+          cur.next();
         }
-        l_run += sum;
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&sm.p_full[t]);
-        cur.next(sm, Lq);
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.o_final[t], ocnt & 1, abort_flag));
+        cnt += it.n;
       }
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.o_final[t], 0, abort_flag));
-      if (ok) {
-        tc_fence_after();
-        const int qrow = q0 + t * kBM + row;
-        const float inv = 1.f / l_run;
-        using OutT = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
-        OutT* orow = static_cast<OutT*>(p.out) +
-                     ((int64_t(b) * p.q_len + qrow) * p.heads + h) * kD;
+      const bool have_o = active && ok;
+      if (have_o) tc_fence_after();
+      const int qrow = it.q0 + t * kBM + row;
+      if (p.splits == 1) {
+        if (have_o) {
+          const float inv = 1.f / l_run;
+          OutT* orow = static_cast<OutT*>(p.out) + ((int64_t(it.b) * p.q_len + qrow) * p.heads + it.h) * kD;
+#pragma unroll 1
+          for (int cc = 0; cc < 8; ++cc) {
+            float o[16];
+            tmem_ld16_sync(tO + cc * 16, o);
+            if (qrow < Lq) {
+              uint32_t w[8];
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          float o[32];
-          tmem_ld32_sync(tO + cc * 32, o);
-          if (qrow < Lq) {
-            uint32_t w[16];
+              for (int i = 0; i < 8; ++i) w[i] = pack2<kBF16>(o[2 * i] * inv, o[2 * i + 1] * inv);
+              uint4* dst = reinterpret_cast<uint4*>(orow + cc * 16);
+              dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+              dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            }
+          }
+        }
+      } else {
+        // partial result of this split: (m, l) and the unnormalised O row
+        const int64_t slot = (int64_t(it.block) * p.splits + it.split) * (kNQ * kBM) + t * kBM + row;
+        if (have_o) {
+          float4* dst = reinterpret_cast<float4*>(p.ws_o + slot * kD);
+#pragma unroll 1
+          for (int cc = 0; cc < 8; ++cc) {
+            float o[16];
+            tmem_ld16_sync(tO + cc * 16, o);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) w[i] = pack2<kBF16>(o[2 * i] * inv, o[2 * i + 1] * inv);
+            for (int i = 0; i < 4; ++i)
+              __stcg(dst + cc * 4 + i, make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]));
+          }
+          __stcg(p.ws_ml + slot, make_float2(m_run, l_run));
+        } else {
+          __stcg(p.ws_ml + slot, make_float2(-INFINITY, 0.f));
+        }
+        if (have_o) {
+          // O_t has been read: the MMA may start the next item's first PV into it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.o_free[t]);
+          ++ocnt;
+        }
+        // grid-sync pattern: CTA barrier, then one thread publishes with a gpu-scope fence
+        named_bar_softmax();
+        if (threadIdx.x == 0) {
+          __threadfence();
+          const unsigned old = atomicAdd(p.ws_counter + it.block, 1u);
+          const int last = (old == static_cast<unsigned>(p.splits - 1)) ? 1 : 0;
+          if (last) {
+            p.ws_counter[it.block] = 0;  // every split has arrived: reset for the next call
+            __threadfence();
+          }
+          sm.last_flag = last;
+        }
+        named_bar_softmax();
+        if (sm.last_flag && t < it.nq && qrow < Lq) {
+          // merge the splits of this row: O = sum_k 2^(m_k - M) O_k / sum_k 2^(m_k - M) l_k
+          const int64_t base = int64_t(it.block) * p.splits * (kNQ * kBM) + t * kBM + row;
+          float2 ml[kMaxSplits];
+          float M = -INFINITY;
+#pragma unroll
+          for (int k = 0; k < kMaxSplits; ++k) {
+            ml[k] = k < p.splits ? __ldcg(p.ws_ml + base + int64_t(k) * (kNQ * kBM))
+                                 : make_float2(-INFINITY, 0.f);
+            if (ml[k].y > 0.f) M = fmaxf(M, ml[k].x);
+          }
+          float w[kMaxSplits];
+          float L = 0.f;
+#pragma unroll
+          for (int k = 0; k < kMaxSplits; ++k) {
+            w[k] = ml[k].y > 0.f ? ex2(ml[k].x - M) : 0.f;
+            L = fmaf(w[k], ml[k].y, L);
+          }
+          const float inv = 1.f / L;
+#pragma unroll
+          for (int k = 0; k < kMaxSplits; ++k) w[k] *= inv;
+          OutT* orow = static_cast<OutT*>(p.out) + ((int64_t(it.b) * p.q_len + qrow) * p.heads + it.h) * kD;
+#pragma unroll 1
+          for (int cc = 0; cc < 4; ++cc) {  // 32 columns per step, every split's loads in flight
+            float4 v[kMaxSplits][8];
+#pragma unroll
+            for (int k = 0; k < kMaxSplits; ++k) {
+              const float4* src = reinterpret_cast<const float4*>(
+                                      p.ws_o + (base + int64_t(k) * (kNQ * kBM)) * kD) + cc * 8;
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                v[k][i] = (w[k] != 0.f) ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+              for (int k = 0; k < kMaxSplits; ++k) {
+                a.x = fmaf(w[k], v[k][i].x, a.x);
+                a.y = fmaf(w[k], v[k][i].y, a.y);
+                a.z = fmaf(w[k], v[k][i].z, a.z);
+                a.w = fmaf(w[k], v[k][i].w, a.w);
+              }
+              pk[2 * i] = pack2<kBF16>(a.x, a.y);
+              pk[2 * i + 1] = pack2<kBF16>(a.z, a.w);
+            }
             uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
           }
         }
+      }
+      if (p.splits == 1 && have_o) {
+        // O_t has been read: the MMA may start the next item's first PV into it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.o_free[t]);
+        ++ocnt;
       }
     }
   }
@@ -511,20 +824,84 @@ static bool encode_rows(CUtensorMap* map, const void* base, int64_t rows, bool b
   return r == CUDA_SUCCESS;
 }
 
+static int sm_count() {
+  static std::atomic<int> cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kNumSms;
+  int v = cached[dev & 63].load();
+  if (v == 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = kNumSms;
+    cached[dev & 63].store(v);
+  }
+  return v;
+}
+
+struct WsLayout {
+  size_t counter_off, ml_off, o_off, total;
+};
+
+// The per-block counters live in a fixed region at the start of the workspace that nothing else
+// ever writes: calls of different shapes share one workspace, and a counter must find zero
+// where an earlier call may have left partial results had the regions moved with the shape.
+constexpr int64_t kMaxCounterBlocks = 16384;
+
+static WsLayout ws_layout(int64_t blocks, int splits) {
+  WsLayout w{};
+  if (splits <= 1) return w;
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+  w.counter_off = 0;
+  w.ml_off = size_t(kMaxCounterBlocks) * sizeof(uint32_t);
+  const size_t rows = size_t(blocks) * size_t(splits) * (kNQ * kBM);
+  w.o_off = w.ml_off + up(rows * sizeof(float2));
+  w.total = w.o_off + up(rows * kD * sizeof(float));
+  return w;
+}
+
 }  // namespace sm100
+
+int attention_auto_splits(int64_t batch, int64_t heads, int64_t q_len) {
+  using namespace sm100;
+  const int64_t blocks = batch * heads * ((q_len + kNQ * kBM - 1) / (kNQ * kBM));
+  const int64_t target = 2 * int64_t(sm_count());
+  if (blocks >= target) return 1;
+  return static_cast<int>(std::min<int64_t>(kMaxSplits, (target + blocks - 1) / blocks));
+}
+
+size_t attention_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int splits) {
+  using namespace sm100;
+  if (splits <= 0) splits = attention_auto_splits(batch, heads, q_len);
+  const int64_t blocks = batch * heads * ((q_len + kNQ * kBM - 1) / (kNQ * kBM));
+  if (blocks > kMaxCounterBlocks) return 0;
+  return ws_layout(blocks, std::min(splits, kMaxSplits)).total;
+}
 
 cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st) {
   using namespace sm100;
   const int64_t cur_rows = a.batch * a.heads * a.q_len;
   const int64_t slab_rows = a.batch * a.capacity;
   if (cur_rows >= (int64_t(1) << 31) || slab_rows >= (int64_t(1) << 31) ||
-      a.max_segments > kMaxSegments || !(a.scale > 0.f))
+      a.heads > kMaxHeads || a.heads * std::max<int64_t>(a.max_segments, 1) > kMaxSegTable ||
+      !(a.scale > 0.f))
     return cudaErrorNotSupported;
   const uintptr_t align = reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.cur_k) |
                           reinterpret_cast<uintptr_t>(a.cur_v) |
                           reinterpret_cast<uintptr_t>(a.slab_k) |
                           reinterpret_cast<uintptr_t>(a.slab_v) | reinterpret_cast<uintptr_t>(a.out);
   if (align & 15u) return cudaErrorNotSupported;
+  const int qpairs = static_cast<int>((a.q_len + kNQ * kBM - 1) / (kNQ * kBM));
+  const int64_t blocks = a.batch * a.heads * qpairs;
+  int splits = a.kv_splits <= 0 ? attention_auto_splits(a.batch, a.heads, a.q_len) : a.kv_splits;
+  if (splits > kMaxSplits) splits = kMaxSplits;
+  if (blocks > kMaxCounterBlocks) splits = 1;
+  WsLayout wl = ws_layout(blocks, splits);
+  if (splits > 1 && (a.workspace == nullptr || a.workspace_bytes < wl.total ||
+                     (reinterpret_cast<uintptr_t>(a.workspace) & 255u))) {
+    splits = 1;  // no (or too small) workspace: run unsplit
+    wl = ws_layout(blocks, 1);
+  }
+  const int64_t n_items = blocks * splits;
+  if (n_items >= (int64_t(1) << 31)) return cudaErrorNotSupported;
   CUtensorMap tq, tck, tcv, tsk, tsv;
   const void* sk = a.capacity > 0 ? a.slab_k : a.cur_k;
   const void* sv = a.capacity > 0 ? a.slab_v : a.cur_v;
@@ -542,13 +919,29 @@ cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st
   p.seg_starts = a.seg_starts;
   p.seg_ends = a.seg_ends;
   p.seg_counts = a.seg_counts;
+  p.head_order = a.head_order;
   p.out = a.out;
+  uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+  p.ws_counter = splits > 1 ? reinterpret_cast<uint32_t*>(ws + wl.counter_off) : nullptr;
+  p.ws_ml = splits > 1 ? reinterpret_cast<float2*>(ws + wl.ml_off) : nullptr;
+  p.ws_o = splits > 1 ? reinterpret_cast<float*>(ws + wl.o_off) : nullptr;
   p.scale_log2 = a.scale * 1.4426950408889634f;
-  p.qpairs = static_cast<int>((a.q_len + kNQ * kBM - 1) / (kNQ * kBM));
-  const int64_t blocks = a.batch * a.heads * p.qpairs;
-  if (blocks >= (int64_t(1) << 31)) return cudaErrorNotSupported;
+  p.qpairs = qpairs;
+  p.splits = splits;
+  p.n_items = static_cast<int>(n_items);
+  p.seg_stride = static_cast<int>(std::max<int64_t>(a.max_segments, 1));
   const int smem = static_cast<int>(sizeof(Smem)) + 1024;
-  auto kern = bf16 ? attn_sm100_kernel<true> : attn_sm100_kernel<false>;
+  // share of exp2 evaluated on the FMA pipe: HEATKV_EXP2_POLY = 0..2 quarters (default 0)
+  static const int poly = [] {
+    const char* e = getenv("HEATKV_EXP2_POLY");
+    const int v = e ? atoi(e) : 0;
+    return (v >= 0 && v <= 2) ? v : 0;
+  }();
+  using Kern = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, Params);
+  static const Kern table[2][3] = {
+      {attn_sm100_kernel<false, 0>, attn_sm100_kernel<false, 1>, attn_sm100_kernel<false, 2>},
+      {attn_sm100_kernel<true, 0>, attn_sm100_kernel<true, 1>, attn_sm100_kernel<true, 2>}};
+  const Kern kern = table[bf16 ? 1 : 0][poly];
   // opt in to >48 KiB dynamic shared memory once per device (never inside a graph capture)
   static std::atomic<uint64_t> configured[2] = {{0}, {0}};
   int dev = 0;
@@ -560,7 +953,8 @@ cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st
     if (e != cudaSuccess) return e;
     configured[bf16].fetch_or(bit);
   }
-  kern<<<static_cast<unsigned>(blocks), kThreads, smem, st>>>(tq, tck, tcv, tsk, tsv, p);
+  const int grid = static_cast<int>(std::min<int64_t>(n_items, sm_count()));
+  kern<<<grid, kThreads, smem, st>>>(tq, tck, tcv, tsk, tsv, p);
   return cudaGetLastError();
 }
 

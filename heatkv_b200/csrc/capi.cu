@@ -70,14 +70,13 @@ int heatkv_pack_kv(void* dst_k, void* dst_v, const void* src_k, const void* src_
   return HEATKV_OK;
 }
 
-int heatkv_segmented_attention(const void* q, const void* slab_k, const void* slab_v,
-                               const int32_t* seg_starts, const int32_t* seg_ends,
-                               const int32_t* seg_counts, const void* cur_k, const void* cur_v,
-                               void* out, int q_dtype, int k_dtype, int v_dtype, int64_t batch,
-                               int64_t heads, int64_t q_len, int64_t capacity, int64_t head_dim,
-                               int64_t max_segments, float softmax_scale, int use_exp2,
-                               int kernel, void* stream) {
-  (void)use_exp2;  // exp and exp2 modes compute the same softmax
+static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
+                          const int32_t* seg_starts, const int32_t* seg_ends,
+                          const int32_t* seg_counts, const void* cur_k, const void* cur_v, void* out,
+                          int q_dtype, int k_dtype, int v_dtype, int64_t batch, int64_t heads,
+                          int64_t q_len, int64_t capacity, int64_t head_dim, int64_t max_segments,
+                          float softmax_scale, int kernel, const int32_t* head_order,
+                          int kv_splits, void* workspace, size_t workspace_bytes, void* stream) {
   g_last_error.clear();
   if (!valid_dtype(q_dtype) || !valid_dtype(k_dtype) || !valid_dtype(v_dtype))
     return fail(HEATKV_ERR_UNSUPPORTED,
@@ -86,7 +85,7 @@ int heatkv_segmented_attention(const void* q, const void* slab_k, const void* sl
     return fail(HEATKV_ERR_UNSUPPORTED, "real_scale_fused_segmented v1 only supports head_dim=128");
   if (q_len <= 0)
     return fail(HEATKV_ERR_UNSUPPORTED, "real_scale_fused_segmented requires current_len > 0");
-  if (batch < 0 || heads <= 0 || capacity < 0 || max_segments < 0)
+  if (batch < 0 || heads <= 0 || capacity < 0 || max_segments < 0 || kv_splits < 0)
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: invalid sizes");
   if (batch == 0) return HEATKV_OK;
   if (!q || !cur_k || !cur_v || !out || !seg_counts || (max_segments > 0 && (!seg_starts || !seg_ends)))
@@ -104,6 +103,10 @@ int heatkv_segmented_attention(const void* q, const void* slab_k, const void* sl
   heatkv::AttnArgs a{q,     slab_k,        slab_v, seg_starts, seg_ends, seg_counts, cur_k,
                      cur_v, out,           batch,  heads,      q_len,    capacity,   max_segments,
                      softmax_scale};
+  a.head_order = head_order;
+  a.kv_splits = kv_splits;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool same16 = (q_dtype == k_dtype && k_dtype == v_dtype && q_dtype != HEATKV_DTYPE_F32);
   if (kernel == HEATKV_ATTN_TCGEN05 && !same16)
@@ -118,6 +121,47 @@ int heatkv_segmented_attention(const void* q, const void* slab_k, const void* sl
   cudaError_t e = heatkv::launch_attention_simt(a, q_dtype, k_dtype, v_dtype, st);
   if (e != cudaSuccess) return cuda_fail(e, "segmented attention launch");
   return HEATKV_OK;
+}
+
+int heatkv_segmented_attention(const void* q, const void* slab_k, const void* slab_v,
+                               const int32_t* seg_starts, const int32_t* seg_ends,
+                               const int32_t* seg_counts, const void* cur_k, const void* cur_v,
+                               void* out, int q_dtype, int k_dtype, int v_dtype, int64_t batch,
+                               int64_t heads, int64_t q_len, int64_t capacity, int64_t head_dim,
+                               int64_t max_segments, float softmax_scale, int use_exp2,
+                               int kernel, void* stream) {
+  (void)use_exp2;  // exp and exp2 modes compute the same softmax
+  return attention_impl(q, slab_k, slab_v, seg_starts, seg_ends, seg_counts, cur_k, cur_v, out,
+                        q_dtype, k_dtype, v_dtype, batch, heads, q_len, capacity, head_dim,
+                        max_segments, softmax_scale, kernel, nullptr, 1, nullptr, 0, stream);
+}
+
+int heatkv_segmented_attention_ws(const void* q, const void* slab_k, const void* slab_v,
+                                  const int32_t* seg_starts, const int32_t* seg_ends,
+                                  const int32_t* seg_counts, const void* cur_k, const void* cur_v,
+                                  void* out, int q_dtype, int k_dtype, int v_dtype, int64_t batch,
+                                  int64_t heads, int64_t q_len, int64_t capacity, int64_t head_dim,
+                                  int64_t max_segments, float softmax_scale, int use_exp2,
+                                  int kernel, const int32_t* head_order, int kv_splits,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  (void)use_exp2;
+  if (kv_splits != 1 && workspace != nullptr) {
+    const size_t need = heatkv::attention_workspace_bytes(batch, heads, q_len, kv_splits);
+    if (workspace_bytes < need)
+      return fail(HEATKV_ERR_INVALID_ARGUMENT,
+                  "heatkv_segmented_attention_ws: workspace of %zu bytes, %zu needed",
+                  workspace_bytes, need);
+  }
+  return attention_impl(q, slab_k, slab_v, seg_starts, seg_ends, seg_counts, cur_k, cur_v, out,
+                        q_dtype, k_dtype, v_dtype, batch, heads, q_len, capacity, head_dim,
+                        max_segments, softmax_scale, kernel, head_order, kv_splits, workspace,
+                        workspace_bytes, stream);
+}
+
+size_t heatkv_attention_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len,
+                                        int kv_splits) {
+  if (batch <= 0 || heads <= 0 || q_len <= 0 || kv_splits < 0) return 0;
+  return heatkv::attention_workspace_bytes(batch, heads, q_len, kv_splits);
 }
 
 int heatkv_device_status(uint32_t* flags, int clear, void* stream) {

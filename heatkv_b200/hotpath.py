@@ -32,6 +32,46 @@ from . import _native
 from .scheduler import build_static_slot_schedule, copy_descriptors
 
 
+NUM_SMS = 148
+BLOCK_ROWS = 256   # query rows per block of the tcgen05 kernel (two 128-row tiles)
+KEY_TILE = 128
+
+
+def plan_attention(slots_per_segment, q_len: int, batch: int, *, sms: int = NUM_SMS,
+                   max_splits: int = 4):
+    """Length-aware schedule of one attention launch: heads longest first and the number of
+    key-range splits per query block that minimises the makespan of the kernel's round-robin
+    assignment of items to at most ``sms`` persistent CTAs.
+
+    ``slots_per_segment[h]`` lists the head's segment lengths. Cost model, in units of one
+    128 x 128 query-tile x key-tile step: key tiles x query tiles of the item, plus 2 units per
+    item (Q load, pipeline fill, epilogue) and 1 more per split item (partial write and merge).
+    Returns ``(head_order, splits)``."""
+    tiles = np.array([sum((int(n) + KEY_TILE - 1) // KEY_TILE for n in segs if n > 0)
+                      + (q_len + KEY_TILE - 1) // KEY_TILE for segs in slots_per_segment],
+                     dtype=np.int64)
+    order = np.argsort(-tiles, kind="stable").astype(np.int32)
+    qpairs = (q_len + BLOCK_ROWS - 1) // BLOCK_ROWS
+    nq = np.full(qpairs, 2, dtype=np.int64)
+    if q_len - (qpairs - 1) * BLOCK_ROWS <= BLOCK_ROWS // 2:
+        nq[-1] = 1
+    best = None
+    for splits in range(1, max_splits + 1):
+        s = np.arange(splits)
+        n = tiles[order][:, None]                                     # [H, 1]
+        per_split = (n * (s + 1)) // splits - (n * s) // splits       # [H, S]
+        cost = per_split[:, None, None, :] * nq[None, None, :, None]  # [H, 1, Q, S]
+        cost = np.broadcast_to(cost, (len(order), batch, qpairs, splits)).astype(np.float64)
+        cost = cost + 2.0 + (1.0 if splits > 1 else 0.0)
+        flat = cost.reshape(-1)
+        grid = min(len(flat), sms)
+        pad = (-len(flat)) % grid
+        makespan = np.pad(flat, (0, pad)).reshape(-1, grid).sum(axis=0).max()
+        if best is None or makespan < best[0] * 0.97:
+            best = (makespan, splits)
+    return order, best[1]
+
+
 @dataclasses.dataclass
 class Launch:
     kind: str            # "attention" | "pack"
@@ -115,6 +155,13 @@ class LayerPlan:
                                    _dev(d["lengths"], device), d["item_count"], d["max_length"],
                                    d["slots"])
 
+    def segment_lengths(self, t: int):
+        """Per head, the lengths of the slab segments attended at target t."""
+        meta = self.dense_meta[t][3] if t < self.first_target else self.slab_meta[t][3]
+        st, en, ct = meta
+        return [[max(0, int(en[h, i]) - int(st[h, i])) for i in range(int(ct[h]))]
+                for h in range(self.num_heads)]
+
     def attention_slots(self, t: int) -> np.ndarray:
         """Attended slab slots per head at target t (for FLOP accounting)."""
         meta = self.dense_meta[t][3] if t < self.first_target else self.slab_meta[t][3]
@@ -152,6 +199,23 @@ class HotPath:
             self.dense_k.append(torch.zeros(B, H * ld, D, dtype=k_dtype, device=self.device))
             self.dense_v.append(torch.zeros(B, H * ld, D, dtype=v_dtype, device=self.device))
         self.lib = _native.load()
+        # length-aware schedule of every attention launch (host planner, device head orders)
+        self.schedule = {}
+        ws_bytes = 0
+        import os
+        forced = int(os.environ.get("HEATKV_PLAN_SPLITS", "1"))
+        natural = os.environ.get("HEATKV_PLAN_ORDER", "lpt") == "natural"
+        for i, p in enumerate(self.plans):
+            for t in range(self.num_scales):
+                order, splits = plan_attention(p.segment_lengths(t), self.tokens[t], self.batch)
+                if forced > 0:
+                    splits = forced
+                if natural:
+                    order = np.arange(self.num_heads, dtype=np.int32)
+                self.schedule[(i, t)] = (torch.from_numpy(order).to(self.device), splits)
+                ws_bytes = max(ws_bytes, int(self.lib.heatkv_attention_workspace_bytes(
+                    self.batch, self.num_heads, self.tokens[t], splits)))
+        self.workspace = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=self.device)
 
     def slab_bytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in self.slab_k + self.slab_v)
@@ -181,12 +245,14 @@ class HotPath:
                     sk, sv = self.slab_k[i], self.slab_v[i]
                     cap = max(p.capacity, 1)
                 flops = float(4 * n * (p.attention_slots(t) + n).sum() * D * B)
+                order, splits = self.schedule[(i, t)]
                 out.append(Launch(
-                    "attention", p.layer, t, lib.heatkv_segmented_attention,
+                    "attention", p.layer, t, lib.heatkv_segmented_attention_ws,
                     (_native.ptr(q), _native.ptr(sk), _native.ptr(sv), _native.ptr(st),
                      _native.ptr(en), _native.ptr(ct), _native.ptr(k), _native.ptr(v),
                      _native.ptr(o), dt[q.dtype], dt[k.dtype], dt[v.dtype], B, H, n, cap, D,
-                     int(st.shape[1]), ctypes.c_float(scale), 0, kernel), flops))
+                     int(st.shape[1]), ctypes.c_float(scale), 0, kernel, _native.ptr(order),
+                     int(splits), _native.ptr(self.workspace), self.workspace.numel()), flops))
                 row_k = D * k.element_size()
                 row_v = D * v.element_size()
                 if dense and t in p.dense_append:

@@ -27,8 +27,10 @@ def attention_case(rows, heads, q_len, slots, dtype=torch.bfloat16, device="cuda
                for _ in range(3))
     cap = heads * slots
     pk, pv = (torch.randn(rows, cap, 128, device=device, generator=g).to(dtype) for _ in range(2))
-    lens = [1, 4, 16, 36, 64]
-    lens.append(max(0, slots - sum(lens)))
+    lens = [n for n in (1, 4, 16, 36, 64) if n <= slots]
+    while sum(lens) > slots:
+        lens.pop()
+    lens.append(slots - sum(lens))
     st = torch.zeros(heads, len(lens), dtype=torch.int32)
     en = torch.zeros_like(st)
     for h in range(heads):
@@ -91,7 +93,8 @@ def main(argv=None):
         nbytes = 2.0 * B * H * n * 128 * dst_k.element_size() * 2
         print(f"pack rows={B} heads={H} tokens={n} {args.dtype}: {ms * 1e3:.1f} us/call, "
               f"{nbytes / ms / 1e6:.1f} GB/s", flush=True)
-    assert _native.device_status() == 0
+    flags = _native.device_status()
+    assert flags == 0, f"device status flags {flags:#x}"
 
 
 if __name__ == "__main__":

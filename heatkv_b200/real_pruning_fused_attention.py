@@ -143,6 +143,17 @@ def pack_flat_segments_kv(
 
 
 _SUPPORTED = (torch.float16, torch.bfloat16, torch.float32)
+_WORKSPACES: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-device scratch of the split-KV scheduler, zero-filled when (re)allocated; every call
+    leaves it zeroed again, so it is reused across calls on the device's streams in order."""
+    ws = _WORKSPACES.get(device)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _WORKSPACES[device] = ws
+    return ws
 
 
 def fused_real_pruning_flat_segmented_attention(
@@ -237,7 +248,10 @@ def fused_real_pruning_flat_segmented_attention(
     current_v = current_v.contiguous()
     capacity = int(persisted_k.shape[1])
     output = q.new_empty((batch_size, current_len, num_heads * head_dim))
-    status = lib.heatkv_segmented_attention(
+    splits = int(os.environ.get("HEATKV_KV_SPLITS", "1"))
+    need = int(lib.heatkv_attention_workspace_bytes(batch_size, num_heads, current_len, splits))
+    ws = _workspace(q.device, need) if need > 0 else None
+    status = lib.heatkv_segmented_attention_ws(
         _native.ptr(q), _native.ptr(persisted_k) if capacity else None,
         _native.ptr(persisted_v) if capacity else None, _native.ptr(segment_starts),
         _native.ptr(segment_ends), _native.ptr(segment_counts), _native.ptr(current_k),
@@ -245,6 +259,7 @@ def fused_real_pruning_flat_segmented_attention(
         _native.DTYPE_CODES[current_k.dtype], _native.DTYPE_CODES[current_v.dtype],
         int(batch_size), int(num_heads), int(current_len), capacity, int(head_dim),
         int(segment_starts.shape[1]), float(softmax_scale), int(softmax_mode == "exp2"), kernel,
+        None, splits, _native.ptr(ws), 0 if ws is None else ws.numel(),
         _native.stream_handle(q.device))
     _native.check(status, "fused_real_pruning_flat_segmented_attention")
     return output

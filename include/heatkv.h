@@ -110,6 +110,38 @@ int heatkv_segmented_attention(const void* q, const void* slab_k, const void* sl
                                int kernel, void* stream);
 
 /*
+ * heatkv_segmented_attention_ws - heatkv_segmented_attention with the length-aware scheduler's
+ * options. Same computation and arguments, plus:
+ *   head_order      : int32 [heads] device array, a permutation of the heads, longest key range
+ *                     first (NULL = natural order). Work is issued in this order over a persistent
+ *                     grid of at most one CTA per SM, which balances uneven slab lengths.
+ *   kv_splits       : split every 256-row query block's key tiles into this many ranges processed
+ *                     by different CTAs and merged by the last one (0 = choose from the shapes,
+ *                     1 = no split). Applies to the tcgen05 kernel.
+ *   workspace       : device scratch of workspace_bytes >= heatkv_attention_workspace_bytes(...)
+ *                     for kv_splits > 1, 256-byte aligned, zero-filled once before its first use
+ *                     (every call leaves it zeroed again). Concurrent calls need separate
+ *                     workspaces. NULL runs unsplit.
+ * Extends fused_real_pruning_flat_segmented_attention (real_pruning_fused_attention.py:445-591);
+ * the reference's Triton grid has no scheduler options.
+ */
+int heatkv_segmented_attention_ws(const void* q, const void* slab_k, const void* slab_v,
+                                  const int32_t* seg_starts, const int32_t* seg_ends,
+                                  const int32_t* seg_counts, const void* cur_k, const void* cur_v,
+                                  void* out, int q_dtype, int k_dtype, int v_dtype, int64_t batch,
+                                  int64_t heads, int64_t q_len, int64_t capacity, int64_t head_dim,
+                                  int64_t max_segments, float softmax_scale, int use_exp2,
+                                  int kernel, const int32_t* head_order, int kv_splits,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * heatkv_attention_workspace_bytes - scratch bytes heatkv_segmented_attention_ws needs for these
+ * sizes and kv_splits (0 = the automatic choice); 0 when no scratch is needed.
+ */
+size_t heatkv_attention_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len,
+                                        int kv_splits);
+
+/*
  * heatkv_device_status - read (and with clear != 0, reset) the sticky HEATKV_DEVICE_* flags of
  * the current CUDA device. This call synchronises `stream`. Not part of the reference interface:
  * the reference's Triton kernels do not check descriptors on the device.

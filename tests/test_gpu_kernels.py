@@ -263,3 +263,72 @@ def test_config1_pipeline_against_reference(cuda_device, golden_dir):
             assert [t, t + 1] + _sha(slab_k) + _sha(slab_v) == pk_golden[step]
             step += 1
     assert _native.device_status(d) == 0
+
+
+def _attention_ws(q, pk, pv, st, en, ct, ck, cv, scale, *, head_order, splits, workspace):
+    import ctypes
+    lib = _native.load()
+    B, H, L, D = q.shape
+    out = torch.empty(B, L, H * D, dtype=q.dtype, device=q.device)
+    dt = _native.DTYPE_CODES
+    status = lib.heatkv_segmented_attention_ws(
+        _native.ptr(q), _native.ptr(pk), _native.ptr(pv), _native.ptr(st), _native.ptr(en),
+        _native.ptr(ct), _native.ptr(ck), _native.ptr(cv), _native.ptr(out), dt[q.dtype],
+        dt[ck.dtype], dt[cv.dtype], B, H, L, pk.shape[1], D, st.shape[1], ctypes.c_float(scale), 0,
+        _native.ATTN_TCGEN05, _native.ptr(head_order), splits, _native.ptr(workspace),
+        0 if workspace is None else workspace.numel(), _native.stream_handle(q.device))
+    _native.check(status, "heatkv_segmented_attention_ws")
+    return out
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 4])
+@pytest.mark.parametrize("B,H,L,cap,S", [(1, 3, 129, 1500, 6), (2, 4, 576, 3000, 10),
+                                         (2, 16, 1600, 5000, 12), (1, 2, 20, 900, 4)])
+def test_tcgen05_split_kv_and_head_order(splits, B, H, L, cap, S, cuda_device):
+    """Split-KV partials merged by the last CTA and a shuffled head order give the same result as
+    the reference; the workspace counters are back to zero after every call."""
+    rng = np.random.default_rng(splits * 7 + L)
+    gen = torch.Generator().manual_seed(L + splits)
+    d = cuda_device
+    q, ck, cv = (torch.randn(B, H, L, 128, generator=gen).bfloat16().to(d) for _ in range(3))
+    pk, pv = (torch.randn(B, cap, 128, generator=gen).bfloat16().to(d) for _ in range(2))
+    st, en, ct = _random_layout(rng, H, S, cap)
+    order = torch.from_numpy(rng.permutation(H).astype(np.int32)).to(d)
+    lib = _native.load()
+    nbytes = int(lib.heatkv_attention_workspace_bytes(B, H, L, splits))
+    ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=d)
+    scale = 1.0 / math.sqrt(128)
+    ref = _torch_reference(q, pk, pv, st, en, ct, ck, cv, scale)
+    for _ in range(2):  # second call reuses the workspace the first one left zeroed
+        out = _attention_ws(q, pk, pv, st.to(d), en.to(d), ct.to(d), ck, cv, scale,
+                            head_order=order, splits=splits, workspace=ws)
+        _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
+    if splits > 1:
+        blocks = B * H * ((L + 255) // 256)
+        assert int(ws[: 4 * blocks].count_nonzero()) == 0, "split counters not reset"
+    assert _native.device_status(d) == 0
+
+
+def test_workspace_shared_across_shapes(cuda_device):
+    """One workspace serves calls of different shapes in any order (the split counters sit in a
+    region no partial result ever overwrites)."""
+    d = cuda_device
+    lib = _native.load()
+    shapes = [(2, 4, 576, 3000, 10, 3), (2, 16, 1600, 5000, 12, 2), (1, 3, 129, 1500, 6, 5),
+              (2, 16, 1024, 4000, 12, 4)]
+    need = max(int(lib.heatkv_attention_workspace_bytes(B, H, L, sp)) for B, H, L, _, _, sp in shapes)
+    ws = torch.zeros(need, dtype=torch.uint8, device=d)
+    scale = 1.0 / math.sqrt(128)
+    for rep in range(2):
+        for k, (B, H, L, cap, S, sp) in enumerate(shapes):
+            rng = np.random.default_rng(100 * rep + k)
+            gen = torch.Generator().manual_seed(100 * rep + k)
+            q, ck, cv = (torch.randn(B, H, L, 128, generator=gen).bfloat16().to(d) for _ in range(3))
+            pk, pv = (torch.randn(B, cap, 128, generator=gen).bfloat16().to(d) for _ in range(2))
+            st, en, ct = _random_layout(rng, H, S, cap)
+            order = torch.from_numpy(rng.permutation(H).astype(np.int32)).to(d)
+            out = _attention_ws(q, pk, pv, st.to(d), en.to(d), ct.to(d), ck, cv, scale,
+                                head_order=order, splits=sp, workspace=ws)
+            ref = _torch_reference(q, pk, pv, st, en, ct, ck, cv, scale)
+            _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
+    assert _native.device_status(d) == 0
