@@ -1,7 +1,8 @@
 """Build libheatkv.so in-tree with nvcc for sm_100a.
 
-``python -m heatkv_b200.build`` compiles every ``csrc/*.cu`` (relocatable device code, so the
-files share the device status word) and links ``heatkv_b200/libheatkv.so``. Objects go to
+``python -m heatkv_b200.build`` compiles every ``csrc/*.cu`` (whole-program device code: kernels
+receive the device status word's address as a parameter, and ``setmaxnreg`` register splits are
+only honoured without relocatable device code) and links ``heatkv_b200/libheatkv.so``. Objects go to
 ``heatkv_b200/_build/``; a file is recompiled only when it or a header changed. The build needs no
 GPU: nvcc cross-compiles for ``-gencode arch=compute_100a,code=sm_100a``.
 """
@@ -22,7 +23,7 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libheatkv.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC",
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
               "--expt-relaxed-constexpr", "-I", os.path.join(REPO, "include"), "-I", CSRC]
 
 
@@ -70,7 +71,7 @@ def build(force: bool = False, verbose: bool = False, extra=()) -> str:
     if todo or force or not os.path.exists(LIB) or \
             any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
         tmp = LIB + ".tmp"
-        cmd = [nvcc()] + ARCH + ["-shared", "-rdc=true", "-Xcompiler", "-fPIC", "-cudart", "static",
+        cmd = [nvcc()] + ARCH + ["-shared", "-Xcompiler", "-fPIC", "-cudart", "static",
                                  "-o", tmp] + objs
         if verbose:
             print(" ".join(cmd), flush=True)

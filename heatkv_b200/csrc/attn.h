@@ -27,7 +27,12 @@ struct AttnArgs {
   int kv_splits = 1;                    // key-range splits per query block; 0 = automatic
   void* workspace = nullptr;            // split partials and counters (zeroed before first use)
   size_t workspace_bytes = 0;
+  unsigned int* status = nullptr;       // device status word (device_status_ptr())
 };
+
+// Device address of the sticky status word on the current device (resolved once per device);
+// null when it cannot be resolved.
+unsigned int* device_status_ptr();
 
 constexpr int kMaxSegments = 256;
 
@@ -43,6 +48,6 @@ cudaError_t launch_pack_kv(void* dst_k, void* dst_v, const void* src_k, const vo
                            int64_t row_bytes_k, int64_t row_bytes_v, int64_t batch,
                            int64_t src_rows, int64_t dst_rows, const int64_t* dst_starts,
                            const int64_t* src_starts, const int64_t* lengths, int64_t n_items,
-                           int64_t max_length, cudaStream_t stream);
+                           int64_t max_length, unsigned int* status, cudaStream_t stream);
 
 }  // namespace heatkv

@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(kSimtThreads) attn_simt_kernel(AttnArgs a) {
       ++n;
     }
     sm.nseg = n;
-    if (clipped && mblk == 0 && b == 0) raise_status(HEATKV_DEVICE_BAD_SEGMENT);
+    if (clipped && mblk == 0 && b == 0) raise_status(a.status, HEATKV_DEVICE_BAD_SEGMENT);
   }
   // Q rows (zero past Lq)
   const TQ* qp = static_cast<const TQ*>(a.q) + (bh * Lq + m0) * kSimtD;

@@ -17,7 +17,7 @@
 // CTA c of a persistent grid of at most one CTA per SM runs items c, c + grid, c + 2*grid, ...
 // which balances the uneven slab lengths across the SMs. No CTA ever waits on another.
 //
-// CTA roles (384 threads, 1 CTA per SM, 201 KB shared memory):
+// CTA roles (384 threads, 168 registers each, 1 CTA per SM, 211 KB shared memory):
 //   * warp 8       : TMA producer. Per item the two Q tiles (after the previous item's last QK),
 //                    then K and V tiles into a 2-stage ring. Rows past a segment's end are loaded
 //                    and masked; rows past the tensor end are zero-filled by TMA.
@@ -31,7 +31,7 @@
 //                    - m) is written back over them as bf16/f16 pairs. The running max is only
 //                    raised when a tile exceeds it by more than 8 (factor 256); O in TMEM is then
 //                    rescaled in place. The epilogue writes O / l (or a partial) from TMEM.
-//   * warps 10-11  : idle (they complete the third warpgroup for the register split).
+//   * warps 10-11  : idle.
 //   TMEM columns: S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512).
 // Every wait is bounded (common.cuh); on expiry the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains
 // its in-flight copies and MMAs, frees TMEM and returns.
@@ -99,6 +99,7 @@ struct Params {
   uint32_t* ws_counter;       // [blocks] (zero between calls) when splits > 1
   float2* ws_ml;              // [blocks * splits * 256]
   float* ws_o;                // [blocks * splits * 256 * 128]
+  unsigned int* status;       // device status word
   float scale_log2;           // softmax_scale * log2(e)
   int qpairs;                 // query blocks per (b, h): ceil(Lq / 256)
   int splits;                 // key-range splits per query block
@@ -286,16 +287,49 @@ __device__ __forceinline__ void exp2_poly_x2(uint64_t y, float& r0, float& r1) {
   r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
+// 2^y for a pair with one MUFU operation: the arguments are rounded to fp16 and the packed
+// half-precision exp2 returns both results. With the lazy running max the argument is at most 8,
+// so rounding it to fp16 changes any p > 2^-8 by at most 0.14 %, below the bf16 rounding that P
+// receives before the PV product (0.39 %); smaller p are below 2^-8 of the row maximum.
+__device__ __forceinline__ void exp2_half_x2(float y0, float y1, float& r0, float& r1) {
+  uint32_t h, e;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(y1), "f"(y0));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(h));
+  __half2 v = *reinterpret_cast<__half2*>(&e);
+  r0 = __low2float(v);
+  r1 = __high2float(v);
+}
+
 // Pairs of P columns whose exp2 runs on the FMA pipe: pair i with (i % kPolyMod) >= kPolyMod -
 // kPolyCount, kPolyCount being a template parameter of the kernel (0..kPolyMod).
 constexpr int kPolyMod = 4;
 
+// Row max of 128 scores: 8 independent chains of 3-input max.
+__device__ __forceinline__ float row_max128(const float (&x)[128]) {
+  float a[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) a[k] = fmaxf(x[k], x[k + 8]);
+#pragma unroll
+  for (int i = 2; i < 16; i += 2) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = max3f(a[k], x[k + 8 * i], x[k + 8 * i + 8]);
+  }
+  return max3f(max3f(a[0], a[1], a[2]), max3f(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+}
+
+__device__ __forceinline__ void mask_tail(float (&x)[128], int valid) {
+  if (valid < 128) {
+#pragma unroll
+    for (int i = 0; i < 128; ++i) x[i] = (i < valid) ? x[i] : -INFINITY;
+  }
+}
+
 // A drain wait for the error path: bounded, ignores the abort flag.
-__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, unsigned int* status) {
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (clock64() - t0 > kWaitBudgetCycles / 4) {
-      raise_status(HEATKV_DEVICE_WAIT_TIMEOUT);
+      raise_status(status, HEATKV_DEVICE_WAIT_TIMEOUT);
       return;
     }
   }
@@ -382,7 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm.head_tiles[h] = tiles + (Lq + kBN - 1) / kBN;
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0 && blockIdx.x == 0)
-      raise_status(HEATKV_DEVICE_BAD_SEGMENT);
+      raise_status(p.status, HEATKV_DEVICE_BAD_SEGMENT);
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_ck);
@@ -400,14 +434,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  // Register split. The launch holds kThreads x 168 = 64,512 registers (ptxas cap for 384
-  // threads); the producer/MMA warpgroup gives back to 56 and the two softmax warpgroups grow to
-  // 224: 128 x 56 + 2 x 128 x 224 = 64,512, exactly the launch total.
-  if (warp >= 8) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
-  } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
-  }
 
   if (warp == kProducerWarp) {
     // ---------------------------------------------------------------- TMA producer
@@ -417,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
         const Item it = decode_item(sm, p, item);
         if (it.n == 0) continue;
-        if (qcnt > 0 && !(ok = mbar_wait(&sm.q_empty, (qcnt - 1) & 1, abort_flag))) break;
+        if (qcnt > 0 && !(ok = mbar_wait(&sm.q_empty, (qcnt - 1) & 1, abort_flag, p.status))) break;
         const int bh = it.b * H + it.h;
         const int qrow = bh * Lq + it.q0;
         mbar_arrive_expect_tx(&sm.q_full, it.nq * kTileBytes);
@@ -435,14 +461,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const CUtensorMap* mv = cur.current ? &tm_cv : &tm_sv;
           const int row = cur.current ? cur_row0 + cur.pos : slab_row0 + cur.pos;
           int s = gk % kStages;
-          if (gk >= kStages && !(ok = mbar_wait(&sm.k_empty[s], ((gk / kStages) - 1) & 1, abort_flag)))
+          if (gk >= kStages && !(ok = mbar_wait(&sm.k_empty[s], ((gk / kStages) - 1) & 1, abort_flag, p.status)))
             break;
           mbar_arrive_expect_tx(&sm.k_full[s], kTileBytes);
           tma_load_2d(sm.k[s], mk, 0, row, &sm.k_full[s]);
           tma_load_2d(sm.k[s] + kHalfBytes, mk, 64, row, &sm.k_full[s]);
           ++gk;
           s = gv % kStages;
-          if (gv >= kStages && !(ok = mbar_wait(&sm.v_empty[s], ((gv / kStages) - 1) & 1, abort_flag)))
+          if (gv >= kStages && !(ok = mbar_wait(&sm.v_empty[s], ((gv / kStages) - 1) & 1, abort_flag, p.status)))
             break;
           mbar_arrive_expect_tx(&sm.v_full[s], kTileBytes);
           tma_load_2d(sm.v[s], mv, 0, row, &sm.v_full[s]);
@@ -451,13 +477,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           cur.next();
         }
       }
-      if (!ok || *abort_flag) {
+      if (!ok || *abort_flag, p.status) {
         // let every copy already issued land before the CTA's shared memory goes away
-        if (qcnt > 0) mbar_drain(&sm.q_full, (qcnt - 1) & 1);
+        if (qcnt > 0) mbar_drain(&sm.q_full, (qcnt - 1) & 1, p.status);
         for (uint32_t g = gk > kStages ? gk - kStages : 0; g < gk; ++g)
-          mbar_drain(&sm.k_full[g % kStages], (g / kStages) & 1);
+          mbar_drain(&sm.k_full[g % kStages], (g / kStages) & 1, p.status);
         for (uint32_t g = gv > kStages ? gv - kStages : 0; g < gv; ++g)
-          mbar_drain(&sm.v_full[g % kStages], (g / kStages) & 1);
+          mbar_drain(&sm.v_full[g % kStages], (g / kStages) & 1, p.status);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -493,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
         const Item it = decode_item(sm, p, item);
         if (it.n == 0) continue;
-        if (!(ok = mbar_wait(&sm.q_full, qcnt & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(&sm.q_full, qcnt & 1, abort_flag, p.status))) break;
         ++qcnt;
         tc_fence_after();
         for (int j = 0; ok && j < it.n; ++j) {
@@ -501,18 +527,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int t = 0; t < it.nq; ++t) {
             if (j > 0) {
               if (t == 0 && !(ok = mbar_wait(&sm.v_full[(gj - 1) % kStages], ((gj - 1) / kStages) & 1,
-                                              abort_flag)))
+                                              abort_flag, p.status)))
                 break;
-              if (!(ok = mbar_wait(&sm.p_full[t], (pcnt[t] + j - 1) & 1, abort_flag))) break;
+              if (!(ok = mbar_wait(&sm.p_full[t], (pcnt[t] + j - 1) & 1, abort_flag, p.status))) break;
               if (j == 1 && ocnt[t] > 0 &&
-                  !(ok = mbar_wait(&sm.o_free[t], (ocnt[t] - 1) & 1, abort_flag)))
+                  !(ok = mbar_wait(&sm.o_free[t], (ocnt[t] - 1) & 1, abort_flag, p.status)))
                 break;
               tc_fence_after();
               issue_pv(t, gj - 1, j > 1);
               if (t == it.nq - 1) tc_commit(&sm.v_empty[(gj - 1) % kStages]);
             }
             if (t == 0) {
-              if (!(ok = mbar_wait(&sm.k_full[gj % kStages], (gj / kStages) & 1, abort_flag))) break;
+              if (!(ok = mbar_wait(&sm.k_full[gj % kStages], (gj / kStages) & 1, abort_flag, p.status))) break;
               tc_fence_after();
             }
             issue_qk(t, gj);
@@ -524,11 +550,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         const uint32_t gl = g + it.n - 1;
-        if (!(ok = mbar_wait(&sm.v_full[gl % kStages], (gl / kStages) & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(&sm.v_full[gl % kStages], (gl / kStages) & 1, abort_flag, p.status))) break;
         for (int t = 0; t < it.nq; ++t) {
-          if (!(ok = mbar_wait(&sm.p_full[t], (pcnt[t] + it.n - 1) & 1, abort_flag))) break;
+          if (!(ok = mbar_wait(&sm.p_full[t], (pcnt[t] + it.n - 1) & 1, abort_flag, p.status))) break;
           if (it.n == 1 && ocnt[t] > 0 &&
-              !(ok = mbar_wait(&sm.o_free[t], (ocnt[t] - 1) & 1, abort_flag)))
+              !(ok = mbar_wait(&sm.o_free[t], (ocnt[t] - 1) & 1, abort_flag, p.status)))
             break;
           tc_fence_after();
           issue_pv(t, gl, it.n > 1);
@@ -544,7 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // every MMA issued by this thread has completed once `drain` fires
       tc_commit(&sm.drain);
-      mbar_drain(&sm.drain, 0);
+      mbar_drain(&sm.drain, 0, p.status);
     }
   } else if (warp < 8) {
     // ---------------------------------------------------------------- softmax warpgroups
@@ -568,27 +594,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         cur.begin(sm, it.h, stride, it.j0);
         for (int j = 0; j < it.n; ++j) {
           const int valid = cur.valid(Lq);
-          ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], (cnt + j) & 1, abort_flag));
+          ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], (cnt + j) & 1, abort_flag, p.status));
           if (!ok) break;
           tc_fence_after();
           float x[128];
           tmem_ld_row128(tS, x);
-          if (valid < kBN) {
-#pragma unroll
-            for (int i = 0; i < 128; ++i) x[i] = (i < valid) ? x[i] : -INFINITY;
-          }
-          // row max: 8 independent chains of 3-input max
-          float a[8];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) a[k] = fmaxf(x[k], x[k + 8]);
-#pragma unroll
-          for (int i = 2; i < 16; i += 2) {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) a[k] = max3f(a[k], x[k + 8 * i], x[k + 8 * i + 8]);
-          }
-          const float mx =
-              max3f(max3f(a[0], a[1], a[2]), max3f(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
-          const float mx2 = mx * c;
+          mask_tail(x, valid);
+          const float mx2 = row_max128(x) * c;
           // Lazy max: keep the running max unless this tile exceeds it by more than 8 (a factor
           // of 256 in P); raising it requires rescaling this row of O, done below once the scores
           // are dead (PV(j-1) has completed: the commit that signalled S(j) covers it).
@@ -603,38 +615,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             m_run = m_new;
             rescale = true;
           }
-          // P = exp2(s * c - m) in pairs; 4 partial row sums
-          const uint64_t c2 = f2pack(c, c);
-          const uint64_t nm2 = f2pack(-m_run, -m_run);
-          uint64_t acc[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) acc[k] = f2pack(0.f, 0.f);
-#pragma unroll
-          for (int quarter = 0; quarter < 4; ++quarter) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int pi = quarter * 16 + i;  // pair index: columns 2pi, 2pi+1
-              const uint64_t y = fma2(f2pack(x[2 * pi], x[2 * pi + 1]), c2, nm2);
-              float p0, p1;
-              if ((pi % kPolyMod) >= kPolyMod - kPolyCount) {
-                exp2_poly_x2(y, p0, p1);
-                if (valid < kBN) {
-                  p0 = (2 * pi < valid) ? p0 : 0.f;
-                  p1 = (2 * pi + 1 < valid) ? p1 : 0.f;
-                }
-              } else {
-                float y0, y1;
-                f2unpack(y, y0, y1);
-                p0 = ex2(y0);
-                p1 = ex2(y1);
-              }
-              acc[pi & 3] = add2(acc[pi & 3], f2pack(p0, p1));
-              pk[i] = pack2<kBF16>(p0, p1);
-            }
-            tmem_st16(tS + 16 * quarter, pk);
-          }
           {
+            // P = exp2(s * c - m) in pairs, stored over the scores in 16-column steps
+            const uint64_t c2 = f2pack(c, c);
+            const uint64_t nm2 = f2pack(-m_run, -m_run);
+            uint64_t acc[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) acc[k] = f2pack(0.f, 0.f);
+#pragma unroll
+            for (int quarter = 0; quarter < 4; ++quarter) {
+              uint32_t pk[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int pi = quarter * 16 + i;  // pair index: columns 2pi, 2pi+1
+                const uint64_t y = fma2(f2pack(x[2 * pi], x[2 * pi + 1]), c2, nm2);
+                float p0, p1;
+                if (kPolyCount == 3) {  // packed half-precision exp2 for every pair
+                  float y0, y1;
+                  f2unpack(y, y0, y1);
+                  exp2_half_x2(y0, y1, p0, p1);
+                } else if ((pi % kPolyMod) >= kPolyMod - kPolyCount) {
+                  exp2_poly_x2(y, p0, p1);
+                  if (valid < kBN) {
+                    p0 = (2 * pi < valid) ? p0 : 0.f;
+                    p1 = (2 * pi + 1 < valid) ? p1 : 0.f;
+                  }
+                } else {
+                  float y0, y1;
+                  f2unpack(y, y0, y1);
+                  p0 = ex2(y0);
+                  p1 = ex2(y1);
+                }
+                acc[pi & 3] = add2(acc[pi & 3], f2pack(p0, p1));
+                pk[i] = pack2<kBF16>(p0, p1);
+              }
+              tmem_st16(tS + 16 * quarter, pk);
+            }
             const uint64_t s01 = add2(acc[0], acc[1]);
             const uint64_t s23 = add2(acc[2], acc[3]);
             float u0, u1;
@@ -659,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(&sm.p_full[t]);
           cur.next();
         }
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.o_final[t], ocnt & 1, abort_flag));
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.o_final[t], ocnt & 1, abort_flag, p.status));
         cnt += it.n;
       }
       const bool have_o = active && ok;
@@ -743,19 +759,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < kMaxSplits; ++k) w[k] *= inv;
           OutT* orow = static_cast<OutT*>(p.out) + ((int64_t(it.b) * p.q_len + qrow) * p.heads + it.h) * kD;
 #pragma unroll 1
-          for (int cc = 0; cc < 4; ++cc) {  // 32 columns per step, every split's loads in flight
-            float4 v[kMaxSplits][8];
+          for (int cc = 0; cc < 8; ++cc) {  // 16 columns per step, every split's loads in flight
+            float4 v[kMaxSplits][4];
 #pragma unroll
             for (int k = 0; k < kMaxSplits; ++k) {
               const float4* src = reinterpret_cast<const float4*>(
-                                      p.ws_o + (base + int64_t(k) * (kNQ * kBM)) * kD) + cc * 8;
+                                      p.ws_o + (base + int64_t(k) * (kNQ * kBM)) * kD) + cc * 4;
 #pragma unroll
-              for (int i = 0; i < 8; ++i)
+              for (int i = 0; i < 4; ++i)
                 v[k][i] = (w[k] != 0.f) ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            uint32_t pk[16];
+            uint32_t pk[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < 4; ++i) {
               float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
               for (int k = 0; k < kMaxSplits; ++k) {
@@ -767,9 +783,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               pk[2 * i] = pack2<kBF16>(a.x, a.y);
               pk[2 * i + 1] = pack2<kBF16>(a.z, a.w);
             }
-            uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+            uint4* dst = reinterpret_cast<uint4*>(orow + cc * 16);
+            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
           }
         }
       }
@@ -921,6 +937,7 @@ cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st
   p.seg_counts = a.seg_counts;
   p.head_order = a.head_order;
   p.out = a.out;
+  p.status = a.status;
   uint8_t* ws = static_cast<uint8_t*>(a.workspace);
   p.ws_counter = splits > 1 ? reinterpret_cast<uint32_t*>(ws + wl.counter_off) : nullptr;
   p.ws_ml = splits > 1 ? reinterpret_cast<float2*>(ws + wl.ml_off) : nullptr;
@@ -931,16 +948,19 @@ cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st
   p.n_items = static_cast<int>(n_items);
   p.seg_stride = static_cast<int>(std::max<int64_t>(a.max_segments, 1));
   const int smem = static_cast<int>(sizeof(Smem)) + 1024;
-  // share of exp2 evaluated on the FMA pipe: HEATKV_EXP2_POLY = 0..2 quarters (default 0)
+  // exp2 variant: HEATKV_EXP2_POLY = 0 (fp32 MUFU), 1-2 (quarters of the pairs on the FMA
+  // pipe), 3 (packed half-precision MUFU for every pair); default 0
   static const int poly = [] {
     const char* e = getenv("HEATKV_EXP2_POLY");
     const int v = e ? atoi(e) : 0;
-    return (v >= 0 && v <= 2) ? v : 0;
+    return (v >= 0 && v <= 3) ? v : 0;
   }();
   using Kern = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, Params);
-  static const Kern table[2][3] = {
-      {attn_sm100_kernel<false, 0>, attn_sm100_kernel<false, 1>, attn_sm100_kernel<false, 2>},
-      {attn_sm100_kernel<true, 0>, attn_sm100_kernel<true, 1>, attn_sm100_kernel<true, 2>}};
+  static const Kern table[2][4] = {
+      {attn_sm100_kernel<false, 0>, attn_sm100_kernel<false, 1>, attn_sm100_kernel<false, 2>,
+       attn_sm100_kernel<false, 3>},
+      {attn_sm100_kernel<true, 0>, attn_sm100_kernel<true, 1>, attn_sm100_kernel<true, 2>,
+       attn_sm100_kernel<true, 3>}};
   const Kern kern = table[bf16 ? 1 : 0][poly];
   // opt in to >48 KiB dynamic shared memory once per device (never inside a graph capture)
   static std::atomic<uint64_t> configured[2] = {{0}, {0}};

@@ -8,8 +8,29 @@
 #include "attn.h"
 #include "common.cuh"
 
+#include <atomic>
+#include <mutex>
+
 namespace heatkv {
 __device__ unsigned int g_device_status = 0;
+
+unsigned int* device_status_ptr() {
+  static std::atomic<unsigned int*> cache[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  unsigned int* p = cache[dev].load();
+  if (p) return p;
+  std::lock_guard<std::mutex> lock(mu);
+  p = cache[dev].load();
+  if (!p) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_device_status) != cudaSuccess) return nullptr;
+    p = static_cast<unsigned int*>(addr);
+    cache[dev].store(p);
+  }
+  return p;
+}
 }  // namespace heatkv
 
 namespace {
@@ -65,7 +86,7 @@ int heatkv_pack_kv(void* dst_k, void* dst_v, const void* src_k, const void* src_
   cudaError_t e = heatkv::launch_pack_kv(
       dst_k, dst_v, src_k, src_v, head_dim * dtype_size(k_dtype), head_dim * dtype_size(v_dtype),
       batch, src_rows, dst_rows, dst_starts, src_starts, lengths, n_items, max_length,
-      static_cast<cudaStream_t>(stream));
+      heatkv::device_status_ptr(), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "pack_flat_segments_kv launch");
   return HEATKV_OK;
 }
@@ -107,6 +128,7 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
   a.kv_splits = kv_splits;
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;
+  a.status = heatkv::device_status_ptr();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool same16 = (q_dtype == k_dtype && k_dtype == v_dtype && q_dtype != HEATKV_DTYPE_F32);
   if (kernel == HEATKV_ATTN_TCGEN05 && !same16)

@@ -12,10 +12,11 @@
 
 namespace heatkv {
 
-// Sticky per-device status word (HEATKV_DEVICE_* bits), defined in capi.cu.
-extern __device__ unsigned int g_device_status;
-
-__device__ __forceinline__ void raise_status(unsigned int bits) { atomicOr(&g_device_status, bits); }
+// Kernels receive the address of the sticky per-device status word (HEATKV_DEVICE_* bits, defined
+// in capi.cu) as a parameter; null disables reporting.
+__device__ __forceinline__ void raise_status(unsigned int* status, unsigned int bits) {
+  if (status) atomicOr(status, bits);
+}
 
 __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 
@@ -73,7 +74,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // does not complete within `budget_cycles` or when another thread of the CTA already aborted.
 // No wait in this library can spin forever.
 constexpr long long kWaitBudgetCycles = 2000000000LL;  // ~1 s at B200 clocks
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          unsigned int* status) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t it = 0;; ++it) {
@@ -82,7 +84,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       if (*abort) return false;
       if (clock64() - t0 > kWaitBudgetCycles) {
         *abort = 1;
-        raise_status(HEATKV_DEVICE_WAIT_TIMEOUT);
+        raise_status(status, HEATKV_DEVICE_WAIT_TIMEOUT);
         return false;
       }
     }

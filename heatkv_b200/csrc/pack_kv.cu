@@ -50,6 +50,7 @@ struct PackArgs {
   const int64_t* dst_starts;
   const int64_t* src_starts;
   const int64_t* lengths;
+  unsigned int* status;
 };
 
 // grid = (row chunks, items, batch rows)
@@ -63,7 +64,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kv_kernel(PackArgs a) {
   const int64_t d0 = a.dst_starts[item];
   const int64_t s0 = a.src_starts[item];
   if (len < 0 || d0 < 0 || s0 < 0 || d0 + len > a.dst_rows || s0 + len > a.src_rows) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) raise_status(HEATKV_DEVICE_PACK_OUT_OF_RANGE);
+    if (blockIdx.x == 0 && threadIdx.x == 0) raise_status(a.status, HEATKV_DEVICE_PACK_OUT_OF_RANGE);
     return;
   }
   const int64_t rows = min(int64_t(kPackRowsPerBlock), len - row0);
@@ -105,10 +106,10 @@ cudaError_t launch_pack_kv(void* dst_k, void* dst_v, const void* src_k, const vo
                            int64_t row_bytes_k, int64_t row_bytes_v, int64_t batch,
                            int64_t src_rows, int64_t dst_rows, const int64_t* dst_starts,
                            const int64_t* src_starts, const int64_t* lengths, int64_t n_items,
-                           int64_t max_length, cudaStream_t stream) {
+                           int64_t max_length, unsigned int* status, cudaStream_t stream) {
   PackArgs a{static_cast<char*>(dst_k), static_cast<char*>(dst_v),
              static_cast<const char*>(src_k), static_cast<const char*>(src_v),
-             row_bytes_k, row_bytes_v, src_rows, dst_rows, dst_starts, src_starts, lengths};
+             row_bytes_k, row_bytes_v, src_rows, dst_rows, dst_starts, src_starts, lengths, status};
   const int64_t chunks = (max_length + kPackRowsPerBlock - 1) / kPackRowsPerBlock;
   dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(n_items),
             static_cast<unsigned>(batch));
