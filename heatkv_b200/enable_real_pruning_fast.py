@@ -1,0 +1,508 @@
+"""Drop-in for the reference's ``enable_real_pruning_fast.py``: HeatKV scale-specific pruning of
+an Infinity-style model, with the flat-slab KV cache run on the B200 kernels of libheatkv.
+
+Entry points (same names, arguments and errors as the reference):
+
+* ``enable_real_pruning_scale_specific_fused_segmented(model, budget, orders, *, ...)`` (:2381) and
+  ``enable_real_pruning_scale_specific_fast`` (:2279) - install: validate the orders, derive the
+  strict budget view (``budget.strict_removed_heads_by_scale_specific_for_budget``), build the
+  controller and, per layer, the static slab schedule (``scheduler.build_static_slot_schedule``),
+  then patch every self-attention module's ``forward`` and ``kv_caching``.
+* the patched ``forward`` (:1951-2254): dense scales run the module's own forward until a layer's
+  first target with removed heads; the end of the scale before it packs the retained segments of
+  the dense cache into the slab (activation, :2020-2037); every later scale runs the fused
+  segmented attention over the slab and appends its own K/V into its slab segments (:2218-2225);
+  the final scale frees the slab (:2176-2185).
+* ``reset_/set_/snapshot_real_pruning_fast_phase_profile`` (:40-62) - CUDA-event phase timers for
+  ``materialize``, ``attention`` and ``compact`` and the slab byte counters (:102-163).
+
+Attention modules are found by type name ``SelfAttention`` (the reference's ``isinstance`` check,
+:2294) or passed explicitly with ``attention_modules=``; they must expose ``num_heads``,
+``head_dim``, ``mat_qkv``, ``q_bias``, ``v_bias``, ``zero_k_bias``, ``proj``, ``proj_drop``,
+``scale``, ``cos_attn`` and ``kv_caching`` like ``infinity.models.basic.SelfAttention``. The 2-D
+RoPE function is taken from the module's defining Python module (``apply_rotary_emb``).
+
+Precision note: with cos-attn under bf16 autocast the model produces fp32 q/k and bf16 v; those
+mixed calls run the exact CUDA-core kernel. All-bf16/all-fp16 calls run the tcgen05 kernel.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+import time
+import types
+from typing import Optional
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+from torch.nn.functional import scaled_dot_product_attention as slow_attn
+
+from . import budget as _budget
+from .enable_pruning import (
+    ScaleSpecificPruningController,
+    _assign_layer_indices,
+    _validate_and_normalize_removed_heads_by_scale_specific,
+    _validate_and_normalize_scale_specific_removal_orders,
+)
+from .real_pruning_fused_attention import (
+    fused_real_pruning_flat_segmented_attention,
+    pack_flat_segments_kv,
+)
+from .scheduler import build_static_slot_schedule, copy_descriptors
+
+# ------------------------------------------------------------------------------------------------
+# phase profiler and slab counters (enable_real_pruning_fast.py:32-163)
+# ------------------------------------------------------------------------------------------------
+_PHASE_PROFILE_ENABLED = False
+_PHASE_CPU_NS: dict = {}
+_PHASE_CUDA_MS: dict = {}
+_PHASE_CALLS: dict = {}
+_SEGMENTED_FLAT_STATS: dict = {}
+_PROFILE_PHASES = {"materialize", "attention", "compact"}
+
+
+def reset_real_pruning_fast_phase_profile() -> None:
+    _PHASE_CPU_NS.clear()
+    _PHASE_CUDA_MS.clear()
+    _PHASE_CALLS.clear()
+    _SEGMENTED_FLAT_STATS.clear()
+
+
+def set_real_pruning_fast_phase_profile_enabled(enabled: bool = True) -> None:
+    global _PHASE_PROFILE_ENABLED
+    _PHASE_PROFILE_ENABLED = bool(enabled)
+    reset_real_pruning_fast_phase_profile()
+
+
+def snapshot_real_pruning_fast_phase_profile(*, reset: bool = False) -> dict:
+    result = {
+        "cpu_ms": {k: v / 1e6 for k, v in _PHASE_CPU_NS.items()},
+        "cuda_ms": dict(_PHASE_CUDA_MS),
+        "calls": dict(_PHASE_CALLS),
+        "segmented_flat_stats": dict(_SEGMENTED_FLAT_STATS),
+    }
+    if reset:
+        reset_real_pruning_fast_phase_profile()
+    return result
+
+
+class _Phase:
+    """Times one phase with CUDA events; the events are resolved lazily (no synchronisation on
+    the hot path, unlike the reference's per-phase ``synchronize``)."""
+
+    _pending: list = []
+
+    def __init__(self, name: str):
+        self.name = name
+        self.active = _PHASE_PROFILE_ENABLED and name in _PROFILE_PHASES
+
+    def __enter__(self):
+        if self.active:
+            self.t0 = time.perf_counter_ns()
+            self.e0 = torch.cuda.Event(enable_timing=True) if torch.cuda.is_available() else None
+            if self.e0 is not None:
+                self.e0.record()
+        return self
+
+    def __exit__(self, *exc):
+        if not self.active:
+            return
+        _PHASE_CPU_NS[self.name] = _PHASE_CPU_NS.get(self.name, 0) + time.perf_counter_ns() - self.t0
+        _PHASE_CALLS[self.name] = _PHASE_CALLS.get(self.name, 0) + 1
+        if self.e0 is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            _Phase._pending.append((self.name, self.e0, e1))
+            if len(_Phase._pending) > 4096:
+                _resolve_phase_events()
+
+
+def _resolve_phase_events() -> None:
+    for name, e0, e1 in _Phase._pending:
+        e1.synchronize()
+        _PHASE_CUDA_MS[name] = _PHASE_CUDA_MS.get(name, 0.0) + e0.elapsed_time(e1)
+    _Phase._pending.clear()
+
+
+_orig_snapshot = snapshot_real_pruning_fast_phase_profile
+
+
+def snapshot_real_pruning_fast_phase_profile(*, reset: bool = False) -> dict:  # noqa: F811
+    _resolve_phase_events()
+    return _orig_snapshot(reset=reset)
+
+
+def _stat_add(name: str, value=1) -> None:
+    if _PHASE_PROFILE_ENABLED:
+        _SEGMENTED_FLAT_STATS[name] = _SEGMENTED_FLAT_STATS.get(name, 0) + value
+
+
+def _record_kv_copy(prefix: str, slots: int, k: torch.Tensor, v: torch.Tensor) -> None:
+    if not _PHASE_PROFILE_ENABLED or slots <= 0:
+        return
+    _stat_add(f"{prefix}_slots", int(slots))
+    _stat_add(f"{prefix}_bytes", int(slots) * int(k.shape[0]) * int(k.shape[-1])
+              * (k.element_size() + v.element_size()))
+
+
+def _fused_softmax_mode() -> str:
+    mode = os.environ.get("REAL_PRUNING_FUSED_SOFTMAX_MODE", "exp")
+    return mode if mode in {"exp", "exp2"} else "exp"
+
+
+def _validate_merge_mode(merge_mode: str) -> str:
+    if merge_mode != "exact":
+        raise ValueError("real pruning fast v1 only supports merge_mode='exact'")
+    return merge_mode
+
+
+# ------------------------------------------------------------------------------------------------
+# per-layer device state
+# ------------------------------------------------------------------------------------------------
+
+
+class _LayerState:
+    """Static schedule of one layer and its device-resident metadata / copy descriptors."""
+
+    def __init__(self, controller, layer_idx: int, num_heads: int):
+        self.schedule = build_static_slot_schedule(controller, layer_idx=layer_idx,
+                                                   num_heads=num_heads)
+        self.capacity = int(self.schedule["capacity"])
+        self.device = None
+        self.meta = {}
+        self.old_pack = {}
+        self.append = {}
+
+    def to(self, device: torch.device) -> None:
+        if self.device == device:
+            return
+        sched = self.schedule
+        self.meta = {t: tuple(torch.from_numpy(np.ascontiguousarray(a)).to(device) for a in m)
+                     for t, m in sched["metadata_cpu_by_target"].items()}
+
+        def desc(runs):
+            d = copy_descriptors(runs)
+            if d is None:
+                return None
+            return (torch.from_numpy(d["dst_starts"]).to(device),
+                    torch.from_numpy(d["src_starts"]).to(device),
+                    torch.from_numpy(d["lengths"]).to(device), d["max_length"], d["slots"])
+
+        self.old_pack = {t: desc(r) for t, r in sched["old_pack_runs_by_target"].items()}
+        self.append = {k: desc(r) for k, r in sched["append_runs_by_key"].items()}
+        self.device = device
+
+
+def _pack(desc, dst_k, dst_v, src_k, src_v, prefix: str) -> None:
+    """Copy descriptor items from a ``[B, H, S, D]`` source into the slab ``[B, cap, D]``."""
+    if desc is None:
+        return
+    dst, src, ln, max_len, slots = desc
+    B, H, S, D = src_k.shape
+    pack_flat_segments_kv(dst_k=dst_k, dst_v=dst_v,
+                          src_k=src_k.reshape(B, H * S, D), src_v=src_v.reshape(B, H * S, D),
+                          dst_starts=dst, src_starts=src, lengths=ln, max_length=max_len)
+    _stat_add(f"{prefix}_calls")
+    _record_kv_copy(prefix, slots, dst_k, dst_v)
+
+
+def _items_desc(items, seq_len: int, device):
+    """Copy descriptors for ad-hoc ``(dst_offset, head, src_start, length)`` items."""
+    items = [it for it in items if it[3] > 0]
+    if not items:
+        return None
+    items.sort()
+    dst = torch.tensor([it[0] for it in items], dtype=torch.int64, device=device)
+    src = torch.tensor([it[1] * seq_len + it[2] for it in items], dtype=torch.int64, device=device)
+    ln = torch.tensor([it[3] for it in items], dtype=torch.int64, device=device)
+    return dst, src, ln, max(it[3] for it in items), sum(it[3] for it in items)
+
+
+def _rope_fn(module):
+    mod = sys.modules.get(type(module).__module__)
+    fn = getattr(mod, "apply_rotary_emb", None) if mod is not None else None
+    if fn is None:
+        raise RuntimeError("rope2d_freqs_grid given but apply_rotary_emb was not found beside "
+                           f"{type(module).__name__}")
+    return fn
+
+
+def _ensure_slab(self, batch: int, head_dim: int, device, k_dtype, v_dtype) -> None:
+    cap = max(int(self._heatkv_layer.capacity), 0)
+    shape = (batch, cap, head_dim)
+    ck, cv = getattr(self, "_heatkv_slab_k", None), getattr(self, "_heatkv_slab_v", None)
+    if (ck is None or tuple(ck.shape) != shape or ck.device != device or ck.dtype != k_dtype
+            or cv.dtype != v_dtype):
+        self._heatkv_slab_k = torch.empty(shape, device=device, dtype=k_dtype)
+        self._heatkv_slab_v = torch.empty(shape, device=device, dtype=v_dtype)
+        _stat_add("storage_allocations")
+        _stat_add("storage_capacity_slots", cap)
+    self._heatkv_layer.to(device)
+
+
+def _reset_state(self) -> None:
+    self._real_pruning_segmented_cache_active = False
+    self._real_pruning_logical_len = 0
+    self._heatkv_slab_k = None
+    self._heatkv_slab_v = None
+
+
+def _activate_from_dense(self, dense_k, dense_v, target: int) -> None:
+    """Pack the retained segments of the dense ``[B, H, T, D]`` cache (T = tokens before
+    ``target``) into the slab (enable_real_pruning_fast.py:1639-1671 with the static runs)."""
+    B, H, T, D = dense_k.shape
+    _ensure_slab(self, B, D, dense_k.device, dense_k.dtype, dense_v.dtype)
+    layer = self._heatkv_layer
+    if layer.schedule["old_pack_cache_lens_by_target"].get(target) == T:
+        desc = layer.old_pack.get(target)
+    else:
+        items = []
+        for seg in layer.schedule["segments_by_target"].get(target, []):
+            hi = min(seg["scale_end"], T)
+            if seg["scale_start"] < hi:
+                items.append((seg["offset"], seg["head"], seg["scale_start"], hi - seg["scale_start"]))
+        desc = _items_desc(items, T, dense_k.device)
+    _pack(desc, self._heatkv_slab_k, self._heatkv_slab_v, dense_k.contiguous(),
+          dense_v.contiguous(), "activation_copy")
+    self._real_pruning_segmented_cache_active = True
+
+
+def _activate_from_dense_and_current(self, dense_k, dense_v, cur_k, cur_v, current_scale: int,
+                                     old_len: int, target: int) -> None:
+    """Activation that also packs the current scale (enable_real_pruning_fast.py:1673-1789)."""
+    B, H, L, D = cur_k.shape
+    _ensure_slab(self, B, D, cur_k.device, cur_k.dtype, cur_v.dtype)
+    old_items, cur_items = [], []
+    for seg in self._heatkv_layer.schedule["segments_by_target"].get(target, []):
+        if seg["source_scale"] == current_scale:
+            s0 = max(seg["scale_start"], old_len) - old_len
+            s1 = min(seg["scale_end"], old_len + L) - old_len
+            if s0 < s1:
+                cur_items.append((seg["offset"], seg["head"], s0, s1 - s0))
+        elif dense_k is not None:
+            hi = min(seg["scale_end"], old_len)
+            if seg["scale_start"] < hi:
+                old_items.append((seg["offset"], seg["head"], seg["scale_start"], hi - seg["scale_start"]))
+    if old_items and dense_k is not None:
+        _pack(_items_desc(old_items, old_len, cur_k.device), self._heatkv_slab_k,
+              self._heatkv_slab_v, dense_k.contiguous(), dense_v.contiguous(), "activation_copy")
+    _pack(_items_desc(cur_items, L, cur_k.device), self._heatkv_slab_k, self._heatkv_slab_v,
+          cur_k, cur_v, "activation_copy")
+    self._real_pruning_segmented_cache_active = True
+
+
+# ------------------------------------------------------------------------------------------------
+# patched forward / kv_caching
+# ------------------------------------------------------------------------------------------------
+
+
+def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=None, attn_fn=None,
+                                               scale_schedule=None, rope2d_freqs_grid=None,
+                                               scale_ind=0):
+    if not self.caching:
+        raise NotImplementedError("real pruning fused segmented only supports kv-cached inference")
+    if attn_bias_or_two_vector is not None:
+        raise NotImplementedError("real pruning fused segmented does not support training attention masks")
+    if attn_fn is not None:
+        raise NotImplementedError("real pruning fused segmented does not support custom attention functions")
+    ctrl = self._real_pruning_scale_specific_controller
+    layer = self.layer_idx
+    batch_size, seq_len, channels = x.shape
+    final_scale = self._num_scales == scale_ind + 1
+    old_len = int(getattr(self, "_real_pruning_logical_len", 0))
+    logical_len = old_len + seq_len
+    active = bool(getattr(self, "_real_pruning_segmented_cache_active", False))
+
+    if not active and not ctrl.any_removed(layer, scale_ind) and _baseline_prefix_enabled():
+        # dense scale: the module's own forward (SDPA over its cat cache)
+        output = self._pre_real_prune_scale_specific_fast_forward(
+            x, attn_bias_or_two_vector, attn_fn=attn_fn, scale_schedule=scale_schedule,
+            rope2d_freqs_grid=rope2d_freqs_grid, scale_ind=scale_ind)
+        self._real_pruning_logical_len = logical_len
+        if final_scale:
+            _reset_state(self)
+            self.cached_k = self.cached_v = None
+            return output
+        if ctrl.any_removed(layer, scale_ind + 1):
+            with _Phase("compact"):
+                _activate_from_dense(self, self.cached_k, self.cached_v, scale_ind + 1)
+            self.cached_k = self.cached_v = None
+        return output
+
+    qkv = F.linear(input=x, weight=self.mat_qkv.weight,
+                   bias=torch.cat((self.q_bias, self.zero_k_bias, self.v_bias))).view(
+        batch_size, seq_len, 3, self.num_heads, self.head_dim)
+    q, k, v = qkv.unbind(dim=2)
+    q = q.permute(0, 2, 1, 3).contiguous()
+    k = k.permute(0, 2, 1, 3).contiguous()
+    v = v.permute(0, 2, 1, 3).contiguous()
+    del qkv
+    if self.cos_attn:
+        scale_mul = self.scale_mul_1H11.reshape(1, self.num_heads, 1, 1).clamp_max(
+            self.max_scale_mul).exp()
+        q = F.normalize(q, dim=-1, eps=1e-12).mul(scale_mul).contiguous()
+        k = F.normalize(k, dim=-1, eps=1e-12).contiguous()
+        v = v.contiguous()
+    if rope2d_freqs_grid is not None:
+        if scale_schedule is None:
+            raise ValueError("scale_schedule is required when rope2d_freqs_grid is provided")
+        q, k = _rope_fn(self)(q, k, scale_schedule, rope2d_freqs_grid, self.pad_to_multiplier,
+                              self.rope2d_normalized_by_hw, scale_ind)
+
+    removed_now = ctrl.any_removed(layer, scale_ind)
+    dense_candidate = None
+    if old_len == 0:
+        with _Phase("attention"):
+            output = slow_attn(query=q, key=k, value=v, scale=self.scale, dropout_p=0.0).transpose(
+                1, 2).reshape(batch_size, seq_len, channels)
+    elif not active and not removed_now:
+        with _Phase("materialize"):
+            attn_k = torch.cat((self.cached_k, k), dim=2)
+            attn_v = torch.cat((self.cached_v, v), dim=2)
+            dense_candidate = (attn_k, attn_v)
+        with _Phase("attention"):
+            output = slow_attn(query=q, key=attn_k, value=attn_v, scale=self.scale,
+                               dropout_p=0.0).transpose(1, 2).reshape(batch_size, seq_len, channels)
+    else:
+        with _Phase("materialize"):
+            if not active:
+                _activate_from_dense(self, self.cached_k, self.cached_v, scale_ind)
+                self.cached_k = self.cached_v = None
+                active = True
+            self._heatkv_layer.to(k.device)
+            starts, ends, counts = self._heatkv_layer.meta[scale_ind]
+        with _Phase("attention"):
+            output = fused_real_pruning_flat_segmented_attention(
+                q=q, persisted_k=self._heatkv_slab_k, persisted_v=self._heatkv_slab_v,
+                segment_starts=starts, segment_ends=ends, segment_counts=counts, current_k=k,
+                current_v=v, softmax_scale=self.scale, softmax_mode=_fused_softmax_mode())
+    del q
+    output = self.proj_drop(self.proj(output))
+
+    with _Phase("compact"):
+        if final_scale:
+            _reset_state(self)
+            self.cached_k = self.cached_v = None
+        else:
+            removed_next = ctrl.any_removed(layer, scale_ind + 1)
+            if not active and not removed_next:
+                if dense_candidate is not None:
+                    self.cached_k, self.cached_v = dense_candidate
+                elif self.cached_k is None:
+                    self.cached_k, self.cached_v = k, v
+                else:
+                    self.cached_k = torch.cat((self.cached_k, k), dim=2)
+                    self.cached_v = torch.cat((self.cached_v, v), dim=2)
+            elif active:
+                _pack(self._heatkv_layer.append.get((scale_ind, scale_ind + 1)),
+                      self._heatkv_slab_k, self._heatkv_slab_v, k, v, "append_copy")
+            else:
+                _activate_from_dense_and_current(self, self.cached_k, self.cached_v, k, v,
+                                                 scale_ind, old_len, scale_ind + 1)
+                self.cached_k = self.cached_v = None
+            self._real_pruning_logical_len = logical_len
+    return output
+
+
+def _baseline_prefix_enabled() -> bool:
+    return os.environ.get("REAL_PRUNING_FUSED_SEGMENTED_BASELINE_PREFIX", "1") not in {
+        "0", "false", "False", "no", "NO"}
+
+
+def _real_pruning_scale_specific_fast_kv_caching(self, enable: bool):
+    self._pre_real_prune_scale_specific_fast_kv_caching(enable)
+    self._real_pruning_scale_specific_controller.reset()
+    _reset_state(self)
+    if enable:
+        try:
+            device = next(self.parameters()).device
+        except StopIteration:
+            device = torch.device("cpu")
+        if device.type == "cuda":
+            self._heatkv_layer.to(device)
+
+
+def _attention_modules(model):
+    return [m for m in model.modules() if type(m).__name__ == "SelfAttention"]
+
+
+def enable_real_pruning_scale_specific_fast(model, budget, scale_specific_removal_orders, *,
+                                            protected_prefix_scales=4, source_scale_start=None,
+                                            skip_last_scale=True, merge_mode="exact",
+                                            attention_impl="fused_segmented",
+                                            requested_generation_batch_size=None,
+                                            attention_modules=None, scale_schedule=None):
+    """Install HeatKV scale-specific pruning (enable_real_pruning_fast.py:2279-2378)."""
+    merge_mode = _validate_merge_mode(merge_mode)
+    if attention_impl != "fused_segmented":
+        raise ValueError(f"unsupported real pruning fast attention_impl: {attention_impl!r}")
+    modules = list(attention_modules) if attention_modules is not None else _attention_modules(model)
+    if not modules:
+        return model
+    _assign_layer_indices(modules)
+    num_heads = modules[0].num_heads
+    if any(m.num_heads != num_heads for m in modules):
+        raise ValueError("real pruning fast requires all SelfAttention modules to use the same num_heads")
+    protected_prefix_scales = int(protected_prefix_scales)
+    if protected_prefix_scales < 0:
+        raise ValueError("protected_prefix_scales must be non-negative")
+    if source_scale_start is None:
+        source_scale_start = protected_prefix_scales
+    source_scale_start = int(source_scale_start)
+    schedule = _budget.get_scale_schedule() if scale_schedule is None else list(scale_schedule)
+    if len(schedule) <= protected_prefix_scales:
+        raise ValueError("scale-specific real pruning fast requires at least one scale after the protected prefix")
+    normalized_orders = _validate_and_normalize_scale_specific_removal_orders(
+        scale_specific_removal_orders, modules, source_scale_start=source_scale_start)
+    view = _budget.strict_removed_heads_by_scale_specific_for_budget(
+        budget, normalized_orders, num_layers=len(modules), num_heads=num_heads,
+        source_scale_start=source_scale_start, protected_prefix_scales=protected_prefix_scales,
+        skip_last_scale=skip_last_scale, scale_schedule=schedule)
+    normalized_removed = _validate_and_normalize_removed_heads_by_scale_specific(
+        view["removed_heads_by_scale"], modules, source_scale_start=source_scale_start)
+    controller = ScaleSpecificPruningController(
+        num_layers=len(modules), num_heads=num_heads,
+        static_removed_heads_by_scale=normalized_removed, source_scale_start=source_scale_start,
+        scale_schedule=schedule)
+    for module in modules:
+        module._num_scales = len(schedule)
+        module._real_pruning_scale_specific_controller = controller
+        module._real_prune_scale_specific_budget = float(budget)
+        module._real_prune_merge_mode = merge_mode
+        module._real_pruning_requested_generation_batch_size = (
+            None if requested_generation_batch_size is None else int(requested_generation_batch_size))
+        module._heatkv_layer = _LayerState(controller, module.layer_idx, num_heads)
+        module._real_pruning_segmented_static_schedule = module._heatkv_layer.schedule
+        try:
+            device = next(module.parameters()).device
+        except StopIteration:
+            device = torch.device("cpu")
+        if device.type == "cuda":
+            module._heatkv_layer.to(device)
+        _reset_state(module)
+        module._real_pruning_fast_attention_impl = attention_impl
+        if not hasattr(module, "_pre_real_prune_scale_specific_fast_forward"):
+            module._pre_real_prune_scale_specific_fast_forward = module.forward
+        module.forward = types.MethodType(_real_pruning_scale_specific_fast_forward, module)
+        if not hasattr(module, "_pre_real_prune_scale_specific_fast_kv_caching"):
+            module._pre_real_prune_scale_specific_fast_kv_caching = module.kv_caching
+        module.kv_caching = types.MethodType(_real_pruning_scale_specific_fast_kv_caching, module)
+    return model
+
+
+def enable_real_pruning_scale_specific_fused_segmented(model, budget, scale_specific_removal_orders,
+                                                       *, protected_prefix_scales=4,
+                                                       source_scale_start=None,
+                                                       skip_last_scale=True, merge_mode="exact",
+                                                       requested_generation_batch_size=None,
+                                                       attention_modules=None,
+                                                       scale_schedule=None):
+    """Alias of the installer with ``attention_impl='fused_segmented'`` (:2381-2402)."""
+    return enable_real_pruning_scale_specific_fast(
+        model, budget, scale_specific_removal_orders,
+        protected_prefix_scales=protected_prefix_scales, source_scale_start=source_scale_start,
+        skip_last_scale=skip_last_scale, merge_mode=merge_mode, attention_impl="fused_segmented",
+        requested_generation_batch_size=requested_generation_batch_size,
+        attention_modules=attention_modules, scale_schedule=scale_schedule)

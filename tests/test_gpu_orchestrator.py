@@ -1,0 +1,126 @@
+"""The drop-in installer end to end on a small Infinity-shaped model (GPU): after
+``enable_real_pruning_scale_specific_fused_segmented`` every layer's output at every one of the 13
+scales equals attention over exactly the tokens the keep-mask retains (plain PyTorch fp32 on the
+GPU), through the model's own projections. bf16 model (tcgen05 kernel, 2e-2 / 1e-2) and fp32
+cos-attn model (exact kernel, 1e-4)."""
+
+import math
+
+import pytest
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from heatkv_b200 import _native, synthetic
+from heatkv_b200.enable_real_pruning_fast import (
+    enable_real_pruning_scale_specific_fused_segmented,
+    set_real_pruning_fast_phase_profile_enabled,
+    snapshot_real_pruning_fast_phase_profile,
+)
+
+pytestmark = pytest.mark.gpu
+
+
+class SelfAttention(nn.Module):
+    """Infinity's self-attention (infinity/models/basic.py:196-316, customized_flash_attn=False)
+    reduced to what the installer touches."""
+
+    def __init__(self, embed_dim, num_heads, cos_attn):
+        super().__init__()
+        self.num_heads, self.head_dim = num_heads, embed_dim // num_heads
+        self.cos_attn = cos_attn
+        if cos_attn:
+            self.scale = 1
+            self.scale_mul_1H11 = nn.Parameter(torch.full((1, num_heads, 1, 1), 4.0).log())
+            self.max_scale_mul = math.log(100)
+        else:
+            self.scale = 1 / math.sqrt(self.head_dim)
+        self.mat_qkv = nn.Linear(embed_dim, embed_dim * 3, bias=False)
+        self.q_bias = nn.Parameter(torch.randn(embed_dim) * 0.02)
+        self.v_bias = nn.Parameter(torch.randn(embed_dim) * 0.02)
+        self.register_buffer("zero_k_bias", torch.zeros(embed_dim))
+        self.proj = nn.Linear(embed_dim, embed_dim)
+        self.proj_drop = nn.Identity()
+        self.caching, self.cached_k, self.cached_v = False, None, None
+        self.pad_to_multiplier, self.rope2d_normalized_by_hw = 1, 0
+
+    def kv_caching(self, enable):
+        self.caching, self.cached_k, self.cached_v = enable, None, None
+
+    def qkv(self, x):
+        B, L, C = x.shape
+        qkv = F.linear(x, self.mat_qkv.weight, torch.cat((self.q_bias, self.zero_k_bias, self.v_bias)))
+        q, k, v = qkv.view(B, L, 3, self.num_heads, self.head_dim).permute(2, 0, 3, 1, 4).unbind(0)
+        if self.cos_attn:
+            mul = self.scale_mul_1H11.clamp_max(self.max_scale_mul).exp()
+            q = F.normalize(q, dim=-1, eps=1e-12).mul(mul)
+            k = F.normalize(k, dim=-1, eps=1e-12)
+        return q.contiguous(), k.contiguous(), v.contiguous()
+
+    def forward(self, x, attn_bias_or_two_vector, attn_fn=None, scale_schedule=None,
+                rope2d_freqs_grid=None, scale_ind=0):
+        B, L, C = x.shape
+        q, k, v = self.qkv(x)
+        if self.caching:
+            if self.cached_k is None:
+                self.cached_k, self.cached_v = k, v
+            else:
+                k = self.cached_k = torch.cat((self.cached_k, k), dim=2)
+                v = self.cached_v = torch.cat((self.cached_v, v), dim=2)
+        out = F.scaled_dot_product_attention(q, k, v, scale=self.scale)
+        return self.proj_drop(self.proj(out.transpose(1, 2).reshape(B, L, C)))
+
+
+def _masked_reference(module, ctrl, layer, xs, t):
+    """Attention of scale t's queries over the retained earlier tokens + scale t, fp32."""
+    with torch.no_grad():
+        qkv = [module.qkv(x) for x in xs[: t + 1]]
+        q = qkv[t][0].float()
+        k = torch.cat([z[1] for z in qkv], dim=2).float()
+        v = torch.cat([z[2] for z in qkv], dim=2).float()
+        mask = ctrl.removed_mask_for_layer(layer)
+        ranges = ctrl.scale_ranges
+        B, H, n, D = q.shape
+        out = torch.empty(B, n, H, D, device=q.device)
+        for h in range(H):
+            idx = [torch.arange(*ranges[s]) for s in range(t) if not mask[t, s, h]]
+            idx.append(torch.arange(*ranges[t]))
+            idx = torch.cat(idx).to(q.device)
+            att = torch.softmax((q[:, h] @ k[:, h, idx].transpose(-1, -2)) * module.scale, -1)
+            out[:, :, h] = att @ v[:, h, idx]
+        return module.proj(out.reshape(B, n, H * D).to(module.proj.weight.dtype)).float()
+
+
+@pytest.mark.parametrize("dtype,cos_attn,atol,rel", [(torch.bfloat16, False, 2e-2, 1e-2),
+                                                    (torch.float32, True, 1e-4, 1e-4)])
+def test_installed_model_matches_keep_mask_attention(dtype, cos_attn, atol, rel):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    L, H, C = 3, 16, 2048
+    model = nn.ModuleList([SelfAttention(C, H, cos_attn) for _ in range(L)]).to(dev, dtype)
+    orders = synthetic.random_removal_orders(L, H, seed=7)
+    enable_real_pruning_scale_specific_fused_segmented(
+        model, 0.10, orders, protected_prefix_scales=3, source_scale_start=3)
+    ctrl = model[0]._real_pruning_scale_specific_controller
+    for m in model:
+        m.kv_caching(True)
+    set_real_pruning_fast_phase_profile_enabled(True)
+    schedule = synthetic.SCALE_SCHEDULE_1M
+    xs = {l: [torch.randn(2, h * w, C, device=dev, dtype=dtype) for _, h, w in schedule]
+          for l in range(L)}
+    outs = {l: [] for l in range(L)}
+    with torch.no_grad():
+        for t in range(len(schedule)):
+            for l, m in enumerate(model):
+                outs[l].append(m(xs[l][t], None, scale_ind=t))
+    prof = snapshot_real_pruning_fast_phase_profile(reset=True)
+    set_real_pruning_fast_phase_profile_enabled(False)
+    assert prof["calls"].get("attention", 0) > 0 and prof["calls"].get("compact", 0) > 0
+    assert any(m._real_pruning_segmented_cache_active is False for m in model)  # freed at the end
+    assert _native.device_status(dev) == 0
+    for l, m in enumerate(model):
+        for t in range(len(schedule)):
+            ref = _masked_reference(m, ctrl, l, xs[l], t)
+            err = (outs[l][t].float() - ref).abs().max().item()
+            assert err <= atol and err / ref.abs().max().item() <= rel, (l, t, err)
