@@ -31,7 +31,8 @@
 //                    - m) is written back over them as bf16/f16 pairs. The running max is only
 //                    raised when a tile exceeds it by more than 8 (factor 256); O in TMEM is then
 //                    rescaled in place. The epilogue writes O / l (or a partial) from TMEM.
-//   * warps 10-11  : idle.
+//   * warp 10      : clears the rows past the valid keys of partial V tiles (see below).
+//   * warp 11      : idle.
 //   TMEM columns: S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512).
 // Every wait is bounded (common.cuh); on expiry the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains
 // its in-flight copies and MMAs, frees TMEM and returns.
@@ -57,6 +58,7 @@ constexpr int kStages = 2;      // K/V ring depth
 constexpr int kThreads = 384;   // 12 warps = 3 warpgroups
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
+constexpr int kVFixWarp = 10;
 constexpr uint32_t kHalfBytes = kBM * 64 * 2;    // one 128-row x 64-column 16-bit box: 16 KiB
 constexpr uint32_t kTileBytes = 2 * kHalfBytes;  // 128 x 128 x 2 bytes
 constexpr uint32_t kTmemCols = 512;
@@ -73,6 +75,7 @@ struct __align__(1024) Smem {
   uint64_t k_full[kStages];
   uint64_t k_empty[kStages];
   uint64_t v_full[kStages];
+  uint64_t v_ready[kStages];   // V tile landed and, if partial, its tail rows cleared
   uint64_t v_empty[kStages];
   uint64_t s_full[kNQ];
   uint64_t p_full[kNQ];
@@ -366,6 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.k_full[s], 1);
       mbar_init(&sm.k_empty[s], 1);
       mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_ready[s], 1);
       mbar_init(&sm.v_empty[s], 1);
     }
     for (int t = 0; t < kNQ; ++t) {
@@ -526,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t gj = g + j;
           for (int t = 0; t < it.nq; ++t) {
             if (j > 0) {
-              if (t == 0 && !(ok = mbar_wait(&sm.v_full[(gj - 1) % kStages], ((gj - 1) / kStages) & 1,
+              if (t == 0 && !(ok = mbar_wait(&sm.v_ready[(gj - 1) % kStages], ((gj - 1) / kStages) & 1,
                                               abort_flag, p.status)))
                 break;
               if (!(ok = mbar_wait(&sm.p_full[t], (pcnt[t] + j - 1) & 1, abort_flag, p.status))) break;
@@ -550,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         const uint32_t gl = g + it.n - 1;
-        if (!(ok = mbar_wait(&sm.v_full[gl % kStages], (gl / kStages) & 1, abort_flag, p.status))) break;
+        if (!(ok = mbar_wait(&sm.v_ready[gl % kStages], (gl / kStages) & 1, abort_flag, p.status))) break;
         for (int t = 0; t < it.nq; ++t) {
           if (!(ok = mbar_wait(&sm.p_full[t], (pcnt[t] + it.n - 1) & 1, abort_flag, p.status))) break;
           if (it.n == 1 && ocnt[t] > 0 &&
@@ -571,6 +575,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       // every MMA issued by this thread has completed once `drain` fires
       tc_commit(&sm.drain);
       mbar_drain(&sm.drain, 0, p.status);
+    }
+  } else if (warp == kVFixWarp) {
+    // ---------------------------------------------------------------- V tail clearing
+    // A V tile is 128 slab rows; past the end of a segment (or of the current scale) they hold
+    // whatever the slab holds there. P is exactly 0 for those keys, but 0 x NaN (uninitialised
+    // slab slots) would still poison O, so this warp clears the tail rows of every partial tile
+    // after it lands and before the MMA issuer may read it (v_ready). A 128-byte swizzled row keeps
+    // all of its bytes inside its own 128-byte line, so whole lines are cleared.
+    uint32_t g = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+      const Item it = decode_item(sm, p, item);
+      if (it.n == 0) continue;
+      TileCursor cur;
+      cur.begin(sm, it.h, stride, it.j0);
+      for (int j = 0; j < it.n; ++j, ++g) {
+        const int s = g % kStages;
+        ok = __all_sync(0xffffffffu, mbar_wait(&sm.v_full[s], (g / kStages) & 1, abort_flag, p.status));
+        if (!ok) break;
+        const int valid = cur.valid(Lq);
+        if (valid < kBN) {
+          uint8_t* base = sm.v[s];
+          const int chunks = (kBN - valid) * 2 * 8;  // rows x halves x 16-byte chunks
+          for (int i = lane; i < chunks; i += 32) {
+            const int line = i / 8;
+            const int row = valid + line / 2, half = line % 2;
+            *reinterpret_cast<uint4*>(base + half * kHalfBytes + row * 128 + (i % 8) * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.v_ready[s]);
+        cur.next();
+      }
     }
   } else if (warp < 8) {
     // ---------------------------------------------------------------- softmax warpgroups

@@ -332,3 +332,34 @@ def test_workspace_shared_across_shapes(cuda_device):
             ref = _torch_reference(q, pk, pv, st, en, ct, ck, cv, scale)
             _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
     assert _native.device_status(d) == 0
+
+
+@pytest.mark.parametrize("which,dtype", [("tcgen05", torch.bfloat16), ("exact", torch.bfloat16),
+                                         ("exact", torch.float32)])
+def test_slab_rows_outside_segments_are_never_used(which, dtype, cuda_device, kernel):
+    """Slab slots no segment covers may hold anything (the slab is uninitialised memory); rows a
+    128-key tile loads past a segment's end must not reach the output even when they are NaN."""
+    kernel(which)
+    rng = np.random.default_rng(5)
+    gen = torch.Generator().manual_seed(5)
+    B, H, L, cap, S = 2, 4, 200, 1500, 6
+    d = cuda_device
+    q, ck, cv = (torch.randn(B, H, L, 128, generator=gen).to(dtype).to(d) for _ in range(3))
+    st, en, ct = _random_layout(rng, H, S, cap, lengths=(1, 5, 36, 100, 129, 250))
+    pk = torch.full((B, cap, 128), float("nan"), dtype=dtype)
+    pv = torch.full((B, cap, 128), float("nan"), dtype=dtype)
+    for h in range(H):
+        for i in range(int(ct[h])):
+            s0, e0 = int(st[h, i]), int(en[h, i])
+            pk[:, s0:e0] = torch.randn(B, e0 - s0, 128, generator=gen).to(dtype)
+            pv[:, s0:e0] = torch.randn(B, e0 - s0, 128, generator=gen).to(dtype)
+    pk, pv = pk.to(d), pv.to(d)
+    scale = 1.0 / math.sqrt(128)
+    out = attn(q=q, persisted_k=pk, persisted_v=pv, segment_starts=st.to(d), segment_ends=en.to(d),
+               segment_counts=ct.to(d), current_k=ck, current_v=cv, softmax_scale=scale)
+    assert torch.isfinite(out).all()
+    ref = _torch_reference(q, pk, pv, st, en, ct, ck, cv, scale)
+    if dtype == torch.float32:
+        np.testing.assert_allclose(out.cpu().numpy(), ref.cpu().numpy(), atol=FP32_ATOL, rtol=FP32_ATOL)
+    else:
+        _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
