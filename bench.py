@@ -58,7 +58,7 @@ def build_controller(model: str, budget: float):
         num_heads = heads
 
     view = bud.strict_removed_heads_by_scale_specific_for_budget(
-        budget, bud.orders(int(model[0])), num_layers=layers, num_heads=heads,
+        budget, bud.orders(model_type=int(model[0])), num_layers=layers, num_heads=heads,
         source_scale_start=3, protected_prefix_scales=3)
     norm = _validate_and_normalize_removed_heads_by_scale_specific(
         view["removed_heads_by_scale"], [_M()] * layers, source_scale_start=3)

@@ -32,10 +32,20 @@ def get_scale_schedule():
     return [tuple(x) for x in SCALE_SCHEDULE_1M]
 
 
-def orders(model_type: int = 2):
-    """The shipped S-CAS removal orders (``orders/{2,8}b.json``) as ``9 x [[head, layer], ...]``."""
+def orders(start_order=3, prompts=10, model_type=2):
+    """The shipped S-CAS removal orders (``orders/{2,8}b.json``) as ``9 x [[head, layer], ...]``.
+
+    Same signature as tools/utils.py:604 so its call sites (``orders(initial_scales,
+    model_type=2)``) work unchanged. The shipped orders were ranked from source scale 3 over 10
+    prompts; other values are rejected as in the reference. The reference first looks for a
+    locally regenerated ``outputs/scas_2b/scas_orders.json``; pass such orders to the installer
+    directly instead.
+    """
     import json
     import os
+
+    if start_order != 3 or prompts != 10:
+        raise AssertionError("the shipped orders were computed with start_order=3 and prompts=10")
 
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "orders", f"{int(model_type)}b.json")
     with open(path) as fh:

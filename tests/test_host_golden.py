@@ -41,7 +41,7 @@ class _Mod:
 def _orders(kind, layers, heads):
     if kind == "rand":
         return synthetic.random_removal_orders(layers, heads, seed=1234)
-    return budget.orders(int(kind[0]))
+    return budget.orders(model_type=int(kind[0]))
 
 
 def _controller(name):
@@ -175,8 +175,8 @@ def test_budget_errors_match_reference_messages():
         budget.pruned_heads_for_budget(1.5)
     with pytest.raises(ValueError, match="below the minimum feasible ratio"):
         budget.strict_pruning_schedule_for_budget_scale_specific(
-            0.001, budget.orders(2), source_scale_start=3, protected_prefix_scales=3)
-    bad = [list(o) for o in budget.orders(2)]
+            0.001, budget.orders(model_type=2), source_scale_start=3, protected_prefix_scales=3)
+    bad = [list(o) for o in budget.orders(model_type=2)]
     bad[0][1] = list(bad[0][0])
     with pytest.raises(ValueError, match="duplicate"):
         budget.strict_removed_heads_by_scale_specific_for_budget(0.1, bad, source_scale_start=3)
@@ -185,7 +185,7 @@ def test_budget_errors_match_reference_messages():
 
 
 def test_controller_from_prune_counts_matches_static_view():
-    orders = budget.orders(2)
+    orders = budget.orders(model_type=2)
     counts = {t: (0 if t < 8 else 100 * (t - 7)) for t in range(13)}
     ctrl = ScaleSpecificPruningController(num_layers=32, num_heads=16, prune_counts=counts,
                                           scale_specific_removal_orders=orders,
