@@ -207,3 +207,80 @@ int heatkv_device_status(uint32_t* flags, int clear, void* stream) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// Attention without any allocation (see heatkv_segmented_attention_noalloc in include/heatkv.h).
+//
+// Some callers cannot allocate device memory at the moment they call the attention: code running
+// under an allocator that is frozen or owned by someone else (a memory pool that must not grow
+// while a serving step is in flight), and library hosts with no CUDA allocator of their own. For
+// them the split-KV scratch lives in this fixed array, which every GPU that loads the library
+// keeps until the process exits. Its device address is looked up once per device.
+// ------------------------------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(32) << 20;      // 32 MiB per device
+constexpr size_t kStaticCounterBytes = size_t(16384) * sizeof(uint32_t);  // split counters
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on the current device, resolved on the first call made
+// with each device current (host code cannot use the symbol itself as a device pointer).
+int static_scratch_ptr(void** out) {
+  static std::atomic<void*> cache[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "heatkv_segmented_attention_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= 64)
+    return fail(HEATKV_ERR_UNSUPPORTED, "heatkv_segmented_attention_noalloc: device index %d", dev);
+  void* p = cache[dev].load();
+  if (!p) {
+    std::lock_guard<std::mutex> lock(mu);
+    p = cache[dev].load();
+    if (!p) {
+      e = cudaGetSymbolAddress(&p, g_static_scratch);
+      if (e != cudaSuccess || p == nullptr)
+        return cuda_fail(e, "heatkv_segmented_attention_noalloc: cudaGetSymbolAddress");
+      cache[dev].store(p);
+    }
+  }
+  *out = p;
+  return HEATKV_OK;
+}
+
+}  // namespace
+
+extern "C" int heatkv_segmented_attention_noalloc(
+    const void* q, const void* slab_k, const void* slab_v, const int32_t* seg_starts,
+    const int32_t* seg_ends, const int32_t* seg_counts, const void* cur_k, const void* cur_v,
+    void* out, int q_dtype, int k_dtype, int v_dtype, int64_t batch, int64_t heads, int64_t q_len,
+    int64_t capacity, int64_t head_dim, int64_t max_segments, float softmax_scale, int use_exp2,
+    int kernel, const int32_t* head_order, int kv_splits, void* stream) {
+  (void)use_exp2;
+  g_last_error.clear();
+  if (kv_splits < 0)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_segmented_attention_noalloc: kv_splits < 0");
+  if (batch <= 0 || heads <= 0 || q_len <= 0)
+    return attention_impl(q, slab_k, slab_v, seg_starts, seg_ends, seg_counts, cur_k, cur_v, out,
+                          q_dtype, k_dtype, v_dtype, batch, heads, q_len, capacity, head_dim,
+                          max_segments, softmax_scale, kernel, head_order, 1, nullptr, 0, stream);
+  const size_t need = heatkv::attention_workspace_bytes(batch, heads, q_len, kv_splits);
+  if (need > kStaticScratchBytes)
+    return fail(HEATKV_ERR_UNSUPPORTED,
+                "heatkv_segmented_attention_noalloc: these sizes need %zu bytes of scratch, more "
+                "than the fixed %zu; use kv_splits=1 or heatkv_segmented_attention_ws",
+                need, kStaticScratchBytes);
+  void* scratch = nullptr;
+  if (need > 0) {
+    int rc = static_scratch_ptr(&scratch);
+    if (rc != HEATKV_OK) return rc;
+    // the split counters must read zero when the kernel starts
+    cudaError_t e = cudaMemsetAsync(scratch, 0, kStaticCounterBytes,
+                                    static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "heatkv_segmented_attention_noalloc: clear counters");
+  }
+  return attention_impl(q, slab_k, slab_v, seg_starts, seg_ends, seg_counts, cur_k, cur_v, out,
+                        q_dtype, k_dtype, v_dtype, batch, heads, q_len, capacity, head_dim,
+                        max_segments, softmax_scale, kernel, head_order, need > 0 ? kv_splits : 1,
+                        scratch, need > 0 ? kStaticScratchBytes : 0, stream);
+}

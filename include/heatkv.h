@@ -142,6 +142,32 @@ size_t heatkv_attention_workspace_bytes(int64_t batch, int64_t heads, int64_t q_
                                         int kv_splits);
 
 /*
+ * heatkv_segmented_attention_noalloc - heatkv_segmented_attention_ws for callers that cannot
+ * allocate device memory: code running under a memory pool that must not grow while a serving
+ * step is in flight, or a host without a CUDA allocator of its own. It takes no workspace; the
+ * split-KV scratch is a fixed 32 MiB array inside the library that every GPU which loads the
+ * library keeps until the process exits. No counterpart exists in the reference (its Triton
+ * kernel needs no scratch).
+ *   - Allocates nothing: no cudaMalloc/cudaFree and no allocating library routine. The first call
+ *     made with a device current looks up that device's scratch address (cudaGetSymbolAddress);
+ *     make that first call before any stream capture.
+ *   - kv_splits whose scratch would exceed 32 MiB (heatkv_attention_workspace_bytes(...) >
+ *     33554432) are rejected with HEATKV_ERR_UNSUPPORTED; kv_splits = 1 needs no scratch.
+ *   - Every call shares the one array and leaves its last contents there; the split counters are
+ *     cleared on `stream` before each launch. Calls that overlap on the GPU (different streams
+ *     without ordering) race on the array.
+ * Other arguments as heatkv_segmented_attention_ws.
+ */
+int heatkv_segmented_attention_noalloc(const void* q, const void* slab_k, const void* slab_v,
+                                       const int32_t* seg_starts, const int32_t* seg_ends,
+                                       const int32_t* seg_counts, const void* cur_k,
+                                       const void* cur_v, void* out, int q_dtype, int k_dtype,
+                                       int v_dtype, int64_t batch, int64_t heads, int64_t q_len,
+                                       int64_t capacity, int64_t head_dim, int64_t max_segments,
+                                       float softmax_scale, int use_exp2, int kernel,
+                                       const int32_t* head_order, int kv_splits, void* stream);
+
+/*
  * heatkv_device_status - read (and with clear != 0, reset) the sticky HEATKV_DEVICE_* flags of
  * the current CUDA device. This call synchronises `stream`. Not part of the reference interface:
  * the reference's Triton kernels do not check descriptors on the device.
