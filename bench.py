@@ -37,6 +37,8 @@ sys.path.insert(0, REPO)
 METRIC = "segmented-attn TFLOP/s & ms/image (2B shape, 1024^2, 10% budget)"
 WORKLOAD = ("configs[1]: Infinity-2B attention stack at 1024^2 - 32 layers x 16 heads x 128, "
             "13 scales, batch 1 (+CFG = 2 rows) per GPU, 10% budget from orders/2b.json")
+WORKLOAD_SHARDED = ("Infinity-2B attention stack at 1024^2, 10% budget from orders/2b.json: one "
+                    "fixed batch sharded by (row, head) units over the GPUs, outputs all-gathered")
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -234,23 +236,86 @@ def image_flops(ctrl, layers, heads, rows) -> float:
 # GPU arm
 # ------------------------------------------------------------------------------------------------
 
+class _Workload:
+    """What one rank runs per step: its launch list, the buffers copied in the e2e leg, and the
+    work counted for the JSON line."""
+
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+
+
+def _image_workload(args, ctrl, layers, heads, rank, world, dev):
+    """Default: every rank runs its own image (``--rows`` rows) - weak scaling, no collective."""
+    import torch
+
+    from heatkv_b200.hotpath import HotPath, allocate_io
+    hot = HotPath(ctrl, layers, heads, args.rows, dev, torch.bfloat16, torch.bfloat16)
+    inputs, outputs, in_bufs, out_buf = allocate_io(hot, seed=1000 + rank)
+    launches = hot.launches(inputs, outputs)
+    att = sum(l.work for l in launches if l.kind == "attention")
+    return _Workload(
+        engine=hot, launches=launches, keep=(inputs, outputs), in_bufs=in_bufs, out_buf=out_buf,
+        att_flops=att, job_flops=att * world, images=args.rows / 2 * world, scaling="weak",
+        rows_label={"rows_per_gpu": args.rows}, slab_bytes=hot.slab_bytes(), plan=None)
+
+
+def _sharded_workload(args, ctrl, layers, heads, rank, world, dev):
+    """``--shard``: one fixed batch of ``--global-rows`` rows split over the ranks by (row, head)
+    units (``heatkv_b200.sharding``); after every attention the rank blocks are all-gathered
+    over NCCL and reassembled, so each rank holds the full output - strong scaling."""
+    import torch
+
+    from heatkv_b200 import sharding
+    from heatkv_b200.hotpath import allocate_io
+    costs = sharding.head_costs(ctrl, layers, heads)
+    plan = sharding.plan_shards(costs, args.global_rows, world, split=args.shard)
+    sh = sharding.ShardedHotPath(ctrl, layers, heads, plan, rank, dev, torch.bfloat16,
+                                 torch.bfloat16, gather=True)
+    inputs, outputs, in_bufs, _ = allocate_io(sh.local, seed=1000 + rank)
+    # the full [B, n_t, H * D] outputs every rank receives
+    per_layer = sum(sh.tokens)
+    full_buf = torch.empty(layers * args.global_rows * per_layer * heads * 128,
+                           dtype=torch.bfloat16, device=dev)
+    full, off = [], 0
+    for _ in range(layers):
+        row = []
+        for n in sh.tokens:
+            sz = args.global_rows * n * heads * 128
+            row.append(full_buf[off:off + sz].view(args.global_rows, n, heads * 128))
+            off += sz
+        full.append(row)
+    gbuf = sh.allocate_gather_buffer()
+    launches = sh.launches(inputs, outputs, full, gbuf)
+    att = sum(l.work for l in launches if l.kind == "attention")
+    job = image_flops(ctrl, layers, heads, args.global_rows)
+    return _Workload(
+        engine=sh.local, launches=launches, keep=(inputs, outputs, full, gbuf), in_bufs=in_bufs,
+        out_buf=full_buf if rank == 0 else None, att_flops=att, job_flops=job,
+        images=args.global_rows / 2, scaling="strong",
+        rows_label={"global_rows": args.global_rows, "shard": args.shard,
+                    "row_groups": plan.row_groups, "head_groups": plan.head_groups,
+                    "head_imbalance": round(plan.imbalance(costs), 4)},
+        slab_bytes=sh.local.slab_bytes(), plan=plan)
+
+
 def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     import torch
     import torch.distributed as dist
 
     from heatkv_b200 import _native
-    from heatkv_b200.hotpath import HotPath, allocate_io
+    from heatkv_b200.hotpath import HotPath
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     peaks, peak_src = load_peaks()
     ctrl, layers, heads = build_controller(args.model, args.budget)
-    hot = HotPath(ctrl, layers, heads, args.rows, dev, torch.bfloat16, torch.bfloat16)
-    inputs, outputs, in_bufs, out_buf = allocate_io(hot, seed=1000 + rank)
-    launches = hot.launches(inputs, outputs)
+    make = _image_workload if args.shard == "image" else _sharded_workload
+    wl = make(args, ctrl, layers, heads, rank, world, dev)
+    hot, launches = wl.engine, wl.launches
     n_att = sum(1 for l in launches if l.kind == "attention")
-    att_flops = sum(l.work for l in launches if l.kind == "attention")
+    att_flops = wl.att_flops
     pack_bytes = sum(l.work for l in launches if l.kind == "pack")
+    n_own = sum(1 for l in launches if l.kind in ("attention", "pack", "gather"))
 
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
@@ -258,18 +323,24 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
             hot.run(launches, stream)
     stream.synchronize()
 
-    # one graph per timed step, each with its own external timing events around every launch
+    # The timed steps replay one CUDA graph of the step's launches. A second set of graphs, with
+    # external timing events around every launch, is replayed after the timed region for the
+    # per-kernel figures (the events cost ~1 us per launch, so they stay out of `value`).
+    step_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(step_graph, stream=stream):
+        hot.run(launches, stream)
     graphs, ev_sets = [], []
     mk = lambda: torch.cuda.Event(enable_timing=True, external=True)  # noqa: E731
-    for _ in range(args.steps + args.warmup):
-        evs = [(mk(), mk()) for _ in launches]
+    timed_kinds = ("attention", "pack")
+    for _ in range(args.steps):
+        evs = [(mk(), mk()) if l.kind in timed_kinds else None for l in launches]
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             hot.run(launches, stream, evs)
         graphs.append(g)
         ev_sets.append(evs)
     for i in range(args.warmup):
-        graphs[i].replay()
+        step_graph.replay()
     torch.cuda.synchronize(dev)
 
     if world > 1:
@@ -279,16 +350,29 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     with ClockSampler(local_rank) as clk, torch.cuda.stream(stream):
         start.record(stream)
         for i in range(args.steps):
-            graphs[args.warmup + i].replay()
+            step_graph.replay()
         end.record(stream)
         end.synchronize()
     torch.cuda.synchronize(dev)
     step_ms = start.elapsed_time(end) / args.steps
+    # attribution pass: the same steps with per-launch events
+    if world > 1:
+        dist.barrier()
+    with torch.cuda.stream(stream):
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for g in graphs:
+            g.replay()
+        a1.record(stream)
+        a1.synchronize()
+    step_ms_events = a0.elapsed_time(a1) / args.steps
     att_ms, pack_ms = 0.0, 0.0
     by_target = [0.0] * hot.num_scales
     for i in range(args.steps):
-        for launch, (e0, e1) in zip(launches, ev_sets[args.warmup + i]):
-            d = e0.elapsed_time(e1)
+        for launch, ev in zip(launches, ev_sets[i]):
+            if ev is None:
+                continue
+            d = ev[0].elapsed_time(ev[1])
             if launch.kind == "attention":
                 att_ms += d
                 by_target[launch.target] += d / args.steps
@@ -299,32 +383,35 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     status = _native.device_status(dev)
 
     # e2e: pinned host inputs -> device, every launch through the C ABI, outputs -> host
+    in_bufs, out_buf = wl.in_bufs, wl.out_buf
     h_in = [torch.empty_like(b, device="cpu").pin_memory() for b in in_bufs]
     for hb, db in zip(h_in, in_bufs):
         hb.copy_(db)
-    h_out = torch.empty_like(out_buf, device="cpu").pin_memory()
+    h_out = torch.empty_like(out_buf, device="cpu").pin_memory() if out_buf is not None else None
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
+
+    def e2e_step():
+        for hb, db in zip(h_in, in_bufs):
+            db.copy_(hb, non_blocking=True)
+        hot.run(launches, stream)
+        if h_out is not None:
+            h_out.copy_(out_buf, non_blocking=True)
+
     with torch.cuda.stream(stream):
         for _ in range(2):  # warm the copy engines
-            for hb, db in zip(h_in, in_bufs):
-                db.copy_(hb, non_blocking=True)
-            hot.run(launches, stream)
-            h_out.copy_(out_buf, non_blocking=True)
+            e2e_step()
         stream.synchronize()
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(e2e_steps):
-            for hb, db in zip(h_in, in_bufs):
-                db.copy_(hb, non_blocking=True)
-            hot.run(launches, stream)
-            h_out.copy_(out_buf, non_blocking=True)
+            e2e_step()
         e1.record(stream)
         e1.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     h2d = sum(b.numel() * b.element_size() for b in in_bufs)
-    d2h = out_buf.numel() * out_buf.element_size()
+    d2h = out_buf.numel() * out_buf.element_size() if out_buf is not None else 0
 
     # max over ranks of the step times, sum of work
     vals = torch.tensor([step_ms, e2e_ms, att_ms, pack_ms, float(status)], dtype=torch.float64,
@@ -332,12 +419,14 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     step_ms, e2e_ms, att_ms_max, pack_ms_max, status = vals.tolist()
+    # graphs that hold NCCL work are released before the process group goes away
+    del graphs, ev_sets, step_graph
+    torch.cuda.synchronize(dev)
     if rank != 0:
         return
 
-    tflops = att_flops * world / (step_ms * 1e-3) / 1e12
-    e2e_tflops = att_flops * world / (e2e_ms * 1e-3) / 1e12
-    images_per_step = args.rows / 2 * world
+    tflops = wl.job_flops / (step_ms * 1e-3) / 1e12
+    e2e_tflops = wl.job_flops / (e2e_ms * 1e-3) / 1e12
     att_achieved = att_flops / (att_ms * 1e-3) / 1e12
     sustained = float(peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"]))
     burst = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
@@ -348,25 +437,32 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         from heatkv_b200.hotpath import LayerPlan
-        plan = LayerPlan(ctrl, 0, heads, "cpu")
-        targets = list(range(plan.first_target, plan.num_scales))[: args.ref_targets]
-        sec, flops = cpu_sample(plan, args.rows, targets)
+        sec = flops = 0.0
+        for layer in range(args.ref_layers):
+            plan = LayerPlan(ctrl, layer, heads, "cpu")
+            targets = list(range(plan.first_target, plan.num_scales))[: args.ref_targets]
+            s_, f_ = cpu_sample(plan, args.rows, targets, seed=layer)
+            sec += s_
+            flops += f_
         cpu = {"value": round(flops / sec / 1e12, 4), "unit": "TFLOP/s", "cores": cpu_threads(),
                "kind": "port",
-               "sample": (f"layer 0, targets {targets[0]}..{targets[-1]} (fused slab scales), "
-                          f"{args.rows} rows, fp32 numpy/BLAS oracle, {sec:.1f} s")}
+               "sample": (f"layers 0..{args.ref_layers - 1}, up to {args.ref_targets} fused slab "
+                          f"targets each, {args.rows} rows, fp32 numpy/BLAS oracle, "
+                          f"{flops / 1e12:.2f} TFLOP in {sec:.1f} s")}
 
+    config = {"workload": WORKLOAD if args.shard == "image" else WORKLOAD_SHARDED,
+              **wl.rows_label, "budget": args.budget, "images_per_step": wl.images,
+              "l2": "inputs 8.3 GB per image > 126 MB L2",
+              "mode": "cuda-graph replay, one graph per timed step",
+              "attention_tflop_per_step_per_gpu": round(att_flops / 1e12, 4),
+              "pack_gb_per_step_per_gpu": round(pack_bytes / 1e9, 4),
+              "slab_gb_per_gpu": round(wl.slab_bytes / 1e9, 3)}
     line = {
         "metric": METRIC, "value": round(tflops, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3),
-        "ms_per_image": round(step_ms / (args.rows / 2), 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "rows_per_gpu": args.rows, "budget": args.budget,
-                   "images_per_step": images_per_step, "l2": "inputs 8.3 GB per step > 126 MB L2",
-                   "mode": "cuda-graph replay, one graph per timed step",
-                   "attention_tflop_per_step_per_gpu": round(att_flops / 1e12, 4),
-                   "pack_gb_per_step_per_gpu": round(pack_bytes / 1e9, 4),
-                   "slab_gb_per_gpu": round(hot.slab_bytes() / 1e9, 3)},
+        "ms_per_image": round(step_ms / wl.images * (world if wl.scaling == "weak" else 1), 3),
+        "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": config,
         "roofline": {"bound": "tensor", "achieved": round(att_achieved, 1),
                      "peak": sustained, "unit": "TFLOP/s",
                      "frac": round(att_achieved / sustained, 4), "traffic": None,
@@ -374,18 +470,19 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
                      "frac_of_burst": round(att_achieved / burst, 4),
                      "kernel": "attn_sm100_kernel", "launches_per_step": n_att,
                      "ms_per_step": round(att_ms, 3),
+                     "step_ms_with_launch_events": round(step_ms_events, 3),
                      "ms_by_target": [round(x, 3) for x in by_target]},
         "roofline_pack": {"bound": "hbm", "achieved": round(pack_achieved, 1) if pack_achieved else None,
                           "peak": hbm, "unit": "GB/s",
                           "frac": round(pack_achieved / hbm, 4) if pack_achieved else None,
                           "kernel": "pack_kv_kernel", "ms_per_step": round(pack_ms, 3),
-                          "launches_per_step": len(launches) - n_att},
+                          "launches_per_step": sum(1 for l in launches if l.kind == "pack")},
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_tflops, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
                 "path": "C ABI, inputs from pinned host memory, outputs back to host"},
         "clocks": clk.summary(),
-        "gpu_launches": len(launches) * args.steps,
+        "gpu_launches": n_own * args.steps,
         "device_status": int(status),
     }
     print(json.dumps(line), flush=True)
@@ -403,7 +500,13 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--ref-targets", type=int, default=5,
                     help="fused targets in the CPU sample (bounds the CPU time)")
+    ap.add_argument("--ref-layers", type=int, default=3,
+                    help="layers in the cpu_baseline sample of the GPU arm (about 4 s each)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shard", choices=["image", "auto", "rows", "heads"], default="image",
+                    help="image: each GPU runs its own image (weak scaling); auto/rows/heads: "
+                         "one batch of --global-rows rows sharded over the GPUs (strong scaling)")
+    ap.add_argument("--global-rows", type=int, default=2)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -27,6 +27,7 @@ ATTN_AUTO, ATTN_EXACT, ATTN_TCGEN05 = 0, 1, 2
 DEVICE_PACK_OUT_OF_RANGE = 0x1
 DEVICE_WAIT_TIMEOUT = 0x2
 DEVICE_BAD_SEGMENT = 0x4
+DEVICE_GATHER_OUT_OF_RANGE = 0x8
 
 # every symbol include/heatkv.h declares, with its ctypes signature
 _i64 = ctypes.c_int64
@@ -46,6 +47,8 @@ SIGNATURES = {
     "heatkv_segmented_attention_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i,
                                                 _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float,
                                                 _i, _i, _p, _i, _p]),
+    "heatkv_gather_head_shards": (_i, [_p, _p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                       _p, _p, _p]),
     "heatkv_device_status": (_i, [ctypes.POINTER(ctypes.c_uint32), _i, _p]),
 }
 

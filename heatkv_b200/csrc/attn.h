@@ -50,4 +50,11 @@ cudaError_t launch_pack_kv(void* dst_k, void* dst_v, const void* src_k, const vo
                            const int64_t* src_starts, const int64_t* lengths, int64_t n_items,
                            int64_t max_length, unsigned int* status, cudaStream_t stream);
 
+// Head-shard reassembly (shard_gather.cu); sms = SMs of the device (grid sizing).
+cudaError_t launch_shard_gather(void* dst, const void* src, const int32_t* row_map,
+                                const int32_t* head_map, int64_t world, int64_t rows_per_rank,
+                                int64_t q_len, int64_t heads_per_rank, int64_t batch,
+                                int64_t heads, int64_t chunk_bytes, int sms,
+                                unsigned int* status, cudaStream_t stream);
+
 }  // namespace heatkv

@@ -628,6 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool active = ok && (t < it.nq) && (it.n > 0);
       float m_run = -INFINITY;
       float l_run = 0.f;
+      const bool row_live = it.q0 + t * kBM + row < Lq;
       if (active) {
         TileCursor cur;
         cur.begin(sm, it.h, stride, it.j0);
@@ -647,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           bool rescale = false;
           if (j == 0) {
             m_run = mx2;
-          } else if (__any_sync(0xffffffffu, mx2 > m_run + 8.0f)) {
+          } else if (__any_sync(0xffffffffu, row_live && mx2 > m_run + 8.0f)) {
             const float m_new = fmaxf(m_run, mx2);
             alpha = ex2(m_run - m_new);
             l_run *= alpha;

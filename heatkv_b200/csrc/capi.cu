@@ -186,6 +186,35 @@ size_t heatkv_attention_workspace_bytes(int64_t batch, int64_t heads, int64_t q_
   return heatkv::attention_workspace_bytes(batch, heads, q_len, kv_splits);
 }
 
+int heatkv_gather_head_shards(void* dst, const void* src, int dtype, int64_t world,
+                              int64_t rows_per_rank, int64_t q_len, int64_t heads_per_rank,
+                              int64_t batch, int64_t heads, int64_t head_dim,
+                              const int32_t* row_map, const int32_t* head_map, void* stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype))
+    return fail(HEATKV_ERR_UNSUPPORTED, "heatkv_gather_head_shards: unsupported dtype code");
+  if (world < 0 || rows_per_rank < 0 || q_len < 0 || heads_per_rank < 0 || batch < 0 ||
+      heads < 0 || head_dim <= 0)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_gather_head_shards: negative size");
+  if (world * rows_per_rank * q_len * heads_per_rank == 0) return HEATKV_OK;
+  if (!dst || !src || !row_map || !head_map)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_gather_head_shards: null pointer");
+  if (world * rows_per_rank * heads_per_rank > batch * heads)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT,
+                "heatkv_gather_head_shards: %lld shard units for a [%lld rows x %lld heads] output",
+                static_cast<long long>(world * rows_per_rank * heads_per_rank),
+                static_cast<long long>(batch), static_cast<long long>(heads));
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "heatkv_gather_head_shards: device query");
+  e = heatkv::launch_shard_gather(dst, src, row_map, head_map, world, rows_per_rank, q_len,
+                                  heads_per_rank, batch, heads, head_dim * dtype_size(dtype), sms,
+                                  heatkv::device_status_ptr(), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "heatkv_gather_head_shards launch");
+  return HEATKV_OK;
+}
+
 int heatkv_device_status(uint32_t* flags, int clear, void* stream) {
   g_last_error.clear();
   if (!flags) return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_device_status: null flags");

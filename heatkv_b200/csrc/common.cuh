@@ -8,7 +8,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/heatkv.h"
+#include "heatkv.h"
 
 namespace heatkv {
 

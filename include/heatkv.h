@@ -50,6 +50,7 @@ typedef enum {
 #define HEATKV_DEVICE_PACK_OUT_OF_RANGE 0x1u  /* a pack descriptor left its tensor; item skipped */
 #define HEATKV_DEVICE_WAIT_TIMEOUT 0x2u       /* a bounded pipeline wait expired; tile skipped */
 #define HEATKV_DEVICE_BAD_SEGMENT 0x4u        /* a segment lay outside the slab; it was clipped */
+#define HEATKV_DEVICE_GATHER_OUT_OF_RANGE 0x8u /* a shard map entry left dst; chunk skipped */
 
 /* Attention kernel selection for heatkv_segmented_attention. */
 typedef enum {
@@ -166,6 +167,26 @@ int heatkv_segmented_attention_noalloc(const void* q, const void* slab_k, const 
                                        int64_t capacity, int64_t head_dim, int64_t max_segments,
                                        float softmax_scale, int use_exp2, int kernel,
                                        const int32_t* head_order, int kv_splits, void* stream);
+
+/*
+ * heatkv_gather_head_shards - place head-sharded attention outputs, after their all-gather across
+ * GPUs, into the single-GPU output layout. No counterpart in the reference, which runs on one GPU.
+ *
+ * When a layer's (batch row, head) units are split over `world` GPUs, rank r computes the output
+ * of its rows_per_rank rows x heads_per_rank heads as [rows_per_rank, q_len, heads_per_rank *
+ * head_dim]; an all-gather stacks these rank after rank into
+ *   src : [world, rows_per_rank, q_len, heads_per_rank * head_dim]   (dtype `dtype`)
+ * and this call writes
+ *   dst[row_map[r * rows_per_rank + i], t, head_map[r * heads_per_rank + j] * head_dim + d]
+ *       = src[r, i, t, j * head_dim + d]
+ * with dst : [batch, q_len, heads * head_dim]. row_map / head_map are int32 device arrays of
+ * world * rows_per_rank and world * heads_per_rank entries. A chunk whose mapped row or head lies
+ * outside dst is skipped and raises HEATKV_DEVICE_GATHER_OUT_OF_RANGE.
+ */
+int heatkv_gather_head_shards(void* dst, const void* src, int dtype, int64_t world,
+                              int64_t rows_per_rank, int64_t q_len, int64_t heads_per_rank,
+                              int64_t batch, int64_t heads, int64_t head_dim,
+                              const int32_t* row_map, const int32_t* head_map, void* stream);
 
 /*
  * heatkv_device_status - read (and with clear != 0, reset) the sticky HEATKV_DEVICE_* flags of

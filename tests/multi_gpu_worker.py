@@ -1,0 +1,96 @@
+"""One rank of the multi-GPU parity check (launched by test_gpu_multi.py under torchrun).
+
+Every rank builds the same seeded global inputs of two 2B layers, keeps its (row, head) units,
+runs its part of the sharded hot path - attention, compaction, NCCL all-gather and reassembly -
+eagerly and then as a CUDA graph replay, and checks that the full outputs it received equal the
+single-GPU engine's outputs bit for bit (rank 0 computes those). Exit status 0 = parity.
+"""
+
+import datetime
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, REPO)
+
+import bench  # noqa: E402
+from heatkv_b200 import _native, sharding  # noqa: E402
+from heatkv_b200.hotpath import HotPath, allocate_io  # noqa: E402
+
+
+def main() -> int:
+    split = sys.argv[1] if len(sys.argv) > 1 else "heads"
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    ok = True
+    try:
+        ctrl, L, H = bench.build_controller("2b", 0.10)
+        layers, batch = [0, 21], 2
+        full = HotPath(ctrl, L, H, batch, dev, layers=layers)
+        inputs, ref_out, _, _ = allocate_io(full, seed=11)       # identical on every rank
+        HotPath.run(full.launches(inputs, ref_out))
+        plan = sharding.plan_shards(sharding.head_costs(ctrl, L, H), batch, world, split=split)
+        sh = sharding.ShardedHotPath(ctrl, L, H, plan, rank, dev, gather=True, layers=layers)
+        rows = plan.rows_of(rank)
+        li, lo, fo = [], [], []
+        for i, layer in enumerate(layers):
+            hs = torch.tensor(plan.heads_of(rank, layer), device=dev)
+            li.append([tuple(x[rows[0]:rows[-1] + 1].index_select(1, hs).contiguous()
+                             for x in inputs[i][t]) for t in range(full.num_scales)])
+            lo.append([torch.empty(plan.rows_per_rank, n, plan.heads_per_rank * 128, device=dev,
+                                   dtype=torch.bfloat16) for n in full.tokens])
+            fo.append([torch.full_like(ref_out[i][t], float("nan"))
+                       for t in range(full.num_scales)])
+        launches = sh.launches(li, lo, fo, sh.allocate_gather_buffer())
+        stream = torch.cuda.Stream(dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))   # the inputs were made on it
+        with torch.cuda.stream(stream):
+            HotPath.run(launches, stream)
+        stream.synchronize()
+
+        def check(tag):
+            good = True
+            for i in range(len(layers)):
+                for t in range(full.num_scales):
+                    if not torch.equal(fo[i][t], ref_out[i][t]):
+                        err = (fo[i][t].float() - ref_out[i][t].float()).abs().max().item()
+                        print(f"rank {rank} {tag}: layer {layers[i]} target {t} differs "
+                              f"(max {err})", flush=True)
+                        good = False
+            return good
+
+        ok = check("eager") and ok
+        for row in fo:
+            for x in row:
+                x.fill_(float("nan"))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            HotPath.run(launches, stream)
+        g.replay()
+        torch.cuda.synchronize(dev)
+        ok = check("graph") and ok
+        del g
+        torch.cuda.synchronize(dev)
+        flags = _native.device_status(dev)
+        if flags:
+            print(f"rank {rank}: device flags {flags:#x}", flush=True)
+            ok = False
+        res = torch.tensor([0 if ok else 1], device=dev)
+        dist.all_reduce(res)
+        ok = res.item() == 0
+        if rank == 0:
+            print(f"multi-GPU parity {'ok' if ok else 'FAILED'}: world {world}, split {split}, "
+                  f"rows x heads groups {plan.row_groups} x {plan.head_groups}", flush=True)
+    finally:
+        dist.destroy_process_group()
+    return 0 if ok else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

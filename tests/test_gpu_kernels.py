@@ -134,6 +134,34 @@ def test_tcgen05_random_layouts(dtype, B, H, L, cap, S, cuda_device, kernel):
     assert _native.device_status(cuda_device) == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("L", [5, 200, 300])
+def test_tcgen05_scores_growing_tile_by_tile(dtype, L, cuda_device, kernel):
+    """Each key tile's scores far above the previous tiles' (the running max rises by more than
+    the lazy-rescale threshold again and again, so P is recomputed and O rescaled), with query
+    rows of other heads in the last Q tile."""
+    kernel("tcgen05")
+    B, H, S, cap = 2, 3, 5, 5 * 128
+    gen = torch.Generator().manual_seed(L + 7)
+    q, ck, cv = (torch.randn(B, H, L, 128, generator=gen) for _ in range(3))
+    pk, pv = (torch.randn(B, cap, 128, generator=gen) for _ in range(2))
+    growth = torch.repeat_interleave(1.0 + 2.5 * torch.arange(S, dtype=torch.float32), 128)
+    pk = pk * growth[None, :, None]
+    ck = ck * (1.0 + 2.5 * S)
+    st = torch.tensor([[128 * i for i in range(S)]] * H, dtype=torch.int32)
+    en = st + 128
+    en[1, S - 1] = 128 * (S - 1) + 77   # a partial tile in the middle of head 1
+    ct = torch.tensor([S, S, 2], dtype=torch.int32)
+    q, ck, cv, pk, pv = (x.to(dtype).to(cuda_device) for x in (q, ck, cv, pk, pv))
+    scale = 1.0 / math.sqrt(128)
+    out = attn(q=q, persisted_k=pk, persisted_v=pv, segment_starts=st.to(cuda_device),
+               segment_ends=en.to(cuda_device), segment_counts=ct.to(cuda_device),
+               current_k=ck, current_v=cv, softmax_scale=scale)
+    ref = _torch_reference(q, pk, pv, st, en, ct, ck, cv, scale)
+    _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
+    assert _native.device_status(cuda_device) == 0
+
+
 @pytest.mark.parametrize("L,cap,S", [(1, 300, 3), (64, 700, 6), (130, 900, 5), (300, 1500, 8)])
 def test_exact_fp32_random_layouts(L, cap, S, cuda_device, kernel):
     kernel("auto")  # fp32 inputs always take the exact kernel

@@ -1,0 +1,114 @@
+"""Sharded hot path on the GPU: the head-shard reassembly kernel, and every rank's part of a
+sharded image computed on one device, gathered and reassembled, equal to the single-GPU path.
+
+The all-gather between ranks is emulated here by concatenating the rank blocks in rank order
+(exactly what ``all_gather_into_tensor`` produces); the NCCL path itself runs in
+``test_gpu_multi.py`` when two GPUs are present.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import bench
+from heatkv_b200 import _native, sharding
+from heatkv_b200.hotpath import HotPath, allocate_io
+
+pytestmark = pytest.mark.gpu
+
+DT = _native.DTYPE_CODES
+
+
+def _gather(full, recv, world, rpr, n, hpr, batch, heads, row_map, head_map):
+    lib = _native.load()
+    st = lib.heatkv_gather_head_shards(
+        _native.ptr(full), _native.ptr(recv), DT[full.dtype], world, rpr, n, hpr, batch, heads,
+        128, _native.ptr(row_map), _native.ptr(head_map), _native.stream_handle(full.device))
+    _native.check(st, "gather head shards")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("world,rpr,hpr,n", [(2, 2, 8, 4096), (8, 1, 4, 576), (4, 1, 4, 1)])
+def test_gather_head_shards_matches_indexing(dtype, world, rpr, hpr, n):
+    """rank r holds rows of row group r // (H / hpr) and a permuted head group r % (H / hpr)."""
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(world * 100 + n)
+    heads = 16
+    hg = heads // hpr
+    batch = (world // hg) * rpr
+    perm = np.random.default_rng(n).permutation(heads)
+    row_map = np.array([(r // hg) * rpr + i for r in range(world) for i in range(rpr)], np.int32)
+    head_map = np.array([perm[(r % hg) * hpr + j] for r in range(world) for j in range(hpr)],
+                        np.int32)
+    recv = torch.randn(world, rpr, n, hpr * 128, device=dev, generator=g).to(dtype)
+    full = torch.full((batch, n, heads * 128), float("nan"), device=dev, dtype=dtype)
+    _gather(full, recv, world, rpr, n, hpr, batch, heads, torch.from_numpy(row_map).to(dev),
+            torch.from_numpy(head_map).to(dev))
+    torch.cuda.synchronize()
+    ref = torch.empty_like(full)
+    for r in range(world):
+        for i in range(rpr):
+            for j in range(hpr):
+                h = int(head_map[r * hpr + j])
+                ref[int(row_map[r * rpr + i]), :, h * 128:(h + 1) * 128] = \
+                    recv[r, i, :, j * 128:(j + 1) * 128]
+    assert torch.equal(full, ref)
+    assert _native.device_status(dev) == 0
+
+
+def test_gather_head_shards_flags_out_of_range_maps():
+    dev = torch.device("cuda", 0)
+    recv = torch.ones(2, 1, 8, 8 * 128, device=dev, dtype=torch.bfloat16)
+    full = torch.zeros(2, 8, 16 * 128, device=dev, dtype=torch.bfloat16)
+    rm = torch.tensor([0, 1], dtype=torch.int32, device=dev)
+    hm = torch.tensor(list(range(8)) + [8, 9, 10, 11, 12, 13, 14, 99], dtype=torch.int32,
+                      device=dev)
+    _gather(full, recv, 2, 1, 8, 8, 2, 16, rm, hm)
+    torch.cuda.synchronize()
+    assert _native.device_status(dev) == _native.DEVICE_GATHER_OUT_OF_RANGE
+    # every in-range chunk was written, the bad one skipped
+    assert full[1, :, 15 * 128:].abs().sum().item() == 0
+    assert full[1, :, 8 * 128:15 * 128].eq(1).all()
+    assert full[0, :, :8 * 128].eq(1).all()
+
+
+@pytest.mark.parametrize("world,split", [(2, "heads"), (4, "auto"), (8, "heads")])
+def test_sharded_ranks_reassemble_the_single_gpu_outputs(world, split):
+    dev = torch.device("cuda", 0)
+    ctrl, L, H = bench.build_controller("2b", 0.10)
+    layers = [0, 21]
+    batch = 2
+    full = HotPath(ctrl, L, H, batch, dev, layers=layers)
+    inputs, outputs, _, _ = allocate_io(full, seed=5)
+    HotPath.run(full.launches(inputs, outputs))
+    costs = sharding.head_costs(ctrl, L, H)
+    plan = sharding.plan_shards(costs, batch, world, split=split)
+    assert plan.splits_heads
+    ranks = [sharding.ShardedHotPath(ctrl, L, H, plan, r, dev, layers=layers)
+             for r in range(world)]
+    local_out = []
+    for r, sh in enumerate(ranks):
+        rows = plan.rows_of(r)
+        li, lo = [], []
+        for i, layer in enumerate(layers):
+            hs = torch.tensor(plan.heads_of(r, layer), device=dev)
+            li.append([tuple(x[rows[0]:rows[-1] + 1].index_select(1, hs).contiguous()
+                             for x in inputs[i][t]) for t in range(full.num_scales)])
+            lo.append([torch.empty(plan.rows_per_rank, full.tokens[t],
+                                   plan.heads_per_rank * 128, device=dev, dtype=torch.bfloat16)
+                       for t in range(full.num_scales)])
+        HotPath.run(sh.local.launches(li, lo))
+        local_out.append((li, lo))
+    torch.cuda.synchronize()
+    for i, layer in enumerate(layers):
+        hm = ranks[0].head_maps[layer]
+        for t in range(full.num_scales):
+            n = full.tokens[t]
+            recv = torch.cat([local_out[r][1][i][t].unsqueeze(0) for r in range(world)])
+            got = torch.full_like(outputs[i][t], float("nan"))
+            _gather(got, recv, world, plan.rows_per_rank, n, plan.heads_per_rank, batch, H,
+                    ranks[0].row_map, hm)
+            torch.cuda.synchronize()
+            # the same (row, head) units with the same keys in the same order: identical bits
+            assert torch.equal(got, outputs[i][t]), (layer, t)
+    assert _native.device_status(dev) == 0
