@@ -18,9 +18,11 @@
 // which balances the uneven slab lengths across the SMs. No CTA ever waits on another.
 //
 // CTA roles (384 threads, 168 registers each, 1 CTA per SM, 211 KB shared memory):
-//   * warp 8       : TMA producer. Per item the two Q tiles (after the previous item's last QK),
-//                    then K and V tiles into a 2-stage ring. Rows past a segment's end are loaded
-//                    and masked; rows past the tensor end are zero-filled by TMA.
+//   * warp 8       : TMA producer of Q and K. Per item the two Q tiles (after the previous item's
+//                    last QK), then K tiles into a 2-stage ring. Rows past a segment's end are
+//                    loaded and masked; rows past the tensor end are zero-filled by TMA.
+//   * warp 11      : TMA producer of V tiles, into their own 2-stage ring (a K tile never waits
+//                    for a V slot, which frees later, after the second Q tile's PV).
 //   * warp 9       : TMEM allocator and single-thread tcgen05.mma issuer.
 //                    S_t = Q_t K^T (M=128, N=128, K=128, both operands K-major SW128 in smem),
 //                    O_t += P_t V (A = P_t read from TMEM, B = V as an MN-major SW128 operand).
@@ -32,7 +34,6 @@
 //                    raised when a tile exceeds it by more than 8 (factor 256); O in TMEM is then
 //                    rescaled in place. The epilogue writes O / l (or a partial) from TMEM.
 //   * warp 10      : clears the rows past the valid keys of partial V tiles (see below).
-//   * warp 11      : idle.
 //   TMEM columns: S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512).
 // Every wait is bounded (common.cuh); on expiry the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains
 // its in-flight copies and MMAs, frees TMEM and returns.
@@ -59,6 +60,7 @@ constexpr int kThreads = 384;   // 12 warps = 3 warpgroups
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kVFixWarp = 10;
+constexpr int kVLoadWarp = 11;
 constexpr uint32_t kHalfBytes = kBM * 64 * 2;    // one 128-row x 64-column 16-bit box: 16 KiB
 constexpr uint32_t kTileBytes = 2 * kHalfBytes;  // 128 x 128 x 2 bytes
 constexpr uint32_t kTmemCols = 512;
@@ -439,55 +441,55 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = sm.tmem_base;
 
 
-  if (warp == kProducerWarp) {
-    // ---------------------------------------------------------------- TMA producer
+  if (warp == kProducerWarp || warp == kVLoadWarp) {
+    // ---------------------------------------------------------------- TMA producers
+    // Warp 8 loads Q and K, warp 11 loads V, each into its own ring: a K tile is requested as
+    // soon as its slot is free (QK of both Q tiles done), without queueing behind the V slot,
+    // which frees only when the later PV of the second Q tile completes.
+    const bool loads_k = warp == kProducerWarp;
     if (lane == 0) {
-      uint32_t gk = 0, gv = 0, qcnt = 0;
+      uint32_t gx = 0, qcnt = 0;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
         const Item it = decode_item(sm, p, item);
         if (it.n == 0) continue;
-        if (qcnt > 0 && !(ok = mbar_wait(&sm.q_empty, (qcnt - 1) & 1, abort_flag, p.status))) break;
         const int bh = it.b * H + it.h;
-        const int qrow = bh * Lq + it.q0;
-        mbar_arrive_expect_tx(&sm.q_full, it.nq * kTileBytes);
-        for (int t = 0; t < it.nq; ++t) {
-          tma_load_2d(sm.q[t], &tm_q, 0, qrow + t * kBM, &sm.q_full);
-          tma_load_2d(sm.q[t] + kHalfBytes, &tm_q, 64, qrow + t * kBM, &sm.q_full);
+        if (loads_k) {
+          if (qcnt > 0 && !(ok = mbar_wait(&sm.q_empty, (qcnt - 1) & 1, abort_flag, p.status))) break;
+          const int qrow = bh * Lq + it.q0;
+          mbar_arrive_expect_tx(&sm.q_full, it.nq * kTileBytes);
+          for (int t = 0; t < it.nq; ++t) {
+            tma_load_2d(sm.q[t], &tm_q, 0, qrow + t * kBM, &sm.q_full);
+            tma_load_2d(sm.q[t] + kHalfBytes, &tm_q, 64, qrow + t * kBM, &sm.q_full);
+          }
+          ++qcnt;
         }
-        ++qcnt;
         const int cur_row0 = bh * Lq;
         const int slab_row0 = static_cast<int>(int64_t(it.b) * p.capacity);
         TileCursor cur;
         cur.begin(sm, it.h, stride, it.j0);
-        for (int j = 0; j < it.n; ++j) {
-          const CUtensorMap* mk = cur.current ? &tm_ck : &tm_sk;
-          const CUtensorMap* mv = cur.current ? &tm_cv : &tm_sv;
+        for (int j = 0; j < it.n; ++j, ++gx) {
+          const CUtensorMap* m = loads_k ? (cur.current ? &tm_ck : &tm_sk)
+                                         : (cur.current ? &tm_cv : &tm_sv);
           const int row = cur.current ? cur_row0 + cur.pos : slab_row0 + cur.pos;
-          int s = gk % kStages;
-          if (gk >= kStages && !(ok = mbar_wait(&sm.k_empty[s], ((gk / kStages) - 1) & 1, abort_flag, p.status)))
+          const int s = gx % kStages;
+          uint64_t* full = loads_k ? &sm.k_full[s] : &sm.v_full[s];
+          uint64_t* empty = loads_k ? &sm.k_empty[s] : &sm.v_empty[s];
+          uint8_t* dst = loads_k ? sm.k[s] : sm.v[s];
+          if (gx >= kStages && !(ok = mbar_wait(empty, ((gx / kStages) - 1) & 1, abort_flag, p.status)))
             break;
-          mbar_arrive_expect_tx(&sm.k_full[s], kTileBytes);
-          tma_load_2d(sm.k[s], mk, 0, row, &sm.k_full[s]);
-          tma_load_2d(sm.k[s] + kHalfBytes, mk, 64, row, &sm.k_full[s]);
-          ++gk;
-          s = gv % kStages;
-          if (gv >= kStages && !(ok = mbar_wait(&sm.v_empty[s], ((gv / kStages) - 1) & 1, abort_flag, p.status)))
-            break;
-          mbar_arrive_expect_tx(&sm.v_full[s], kTileBytes);
-          tma_load_2d(sm.v[s], mv, 0, row, &sm.v_full[s]);
-          tma_load_2d(sm.v[s] + kHalfBytes, mv, 64, row, &sm.v_full[s]);
-          ++gv;
+          mbar_arrive_expect_tx(full, kTileBytes);
+          tma_load_2d(dst, m, 0, row, full);
+          tma_load_2d(dst + kHalfBytes, m, 64, row, full);
           cur.next();
         }
       }
-      if (!ok || *abort_flag, p.status) {
+      if (!ok || *abort_flag) {
         // let every copy already issued land before the CTA's shared memory goes away
-        if (qcnt > 0) mbar_drain(&sm.q_full, (qcnt - 1) & 1, p.status);
-        for (uint32_t g = gk > kStages ? gk - kStages : 0; g < gk; ++g)
-          mbar_drain(&sm.k_full[g % kStages], (g / kStages) & 1, p.status);
-        for (uint32_t g = gv > kStages ? gv - kStages : 0; g < gv; ++g)
-          mbar_drain(&sm.v_full[g % kStages], (g / kStages) & 1, p.status);
+        if (loads_k && qcnt > 0) mbar_drain(&sm.q_full, (qcnt - 1) & 1, p.status);
+        for (uint32_t g = gx > kStages ? gx - kStages : 0; g < gx; ++g)
+          mbar_drain(loads_k ? &sm.k_full[g % kStages] : &sm.v_full[g % kStages],
+                     (g / kStages) & 1, p.status);
       }
     }
   } else if (warp == kMmaWarp) {
