@@ -38,6 +38,8 @@ SIGNATURES = {
     "heatkv_version": (ctypes.c_char_p, []),
     "heatkv_pack_kv": (_i, [_p, _p, _p, _p, _i, _i, _i64, _i64, _i64, _i64, _p, _p, _p, _i64,
                             _i64, _p]),
+    "heatkv_pack_kv_batched": (_i, [_p, _i64, _p, _p, _p, _p, _i64, _i, _i, _i64, _i64, _i64, _i,
+                                    _p]),
     "heatkv_segmented_attention": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i64, _i64,
                                         _i64, _i64, _i64, _i64, ctypes.c_float, _i, _i, _p]),
     "heatkv_segmented_attention_ws": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i64,

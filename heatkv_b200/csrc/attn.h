@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "heatkv.h"
+
 namespace heatkv {
 
 struct AttnArgs {
@@ -49,6 +51,15 @@ cudaError_t launch_pack_kv(void* dst_k, void* dst_v, const void* src_k, const vo
                            int64_t src_rows, int64_t dst_rows, const int64_t* dst_starts,
                            const int64_t* src_starts, const int64_t* lengths, int64_t n_items,
                            int64_t max_length, unsigned int* status, cudaStream_t stream);
+
+// Several packs in one launch (pack_kv.cu). max_vector_bytes: the widest vector (16, 8, 4, 2 or
+// 1 bytes) that every job's pointers allow; the row sizes may narrow it further.
+cudaError_t launch_pack_kv_batched(const heatkv_pack_job* jobs, int64_t n_jobs,
+                                   const int32_t* item_job, const int64_t* dst_starts,
+                                   const int64_t* src_starts, const int64_t* lengths,
+                                   int64_t n_items, int64_t row_bytes_k, int64_t row_bytes_v,
+                                   int64_t batch, int64_t max_length, int max_vector_bytes,
+                                   unsigned int* status, cudaStream_t stream);
 
 // Head-shard reassembly (shard_gather.cu); sms = SMs of the device (grid sizing).
 cudaError_t launch_shard_gather(void* dst, const void* src, const int32_t* row_map,

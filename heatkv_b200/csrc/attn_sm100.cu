@@ -363,6 +363,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int stride = p.seg_stride;
 
   // ---------------------------------------------------------------- setup
+  // Shared memory and TMEM are set up while the previous kernel of the stream may still run
+  // (programmatic dependent launch); no global memory is touched before pdl_wait().
+  pdl_trigger();
+  if (warp == kMmaWarp) {
+    tmem_alloc(&sm.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
   if (threadIdx.x == 0) {
     sm.abort_flag = 0;
     mbar_init(&sm.q_full, 1);
@@ -383,6 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&sm.drain, 1);
     fence_mbar_init();
   }
+  pdl_wait();
   if (warp == kProducerWarp) {
     // stage the [H, S] metadata, then compact every head's non-empty segments in place, clipped
     // to the slab, and count its key tiles
@@ -430,10 +438,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_sk);
       tma_prefetch_desc(&tm_sv);
     }
-  }
-  if (warp == kMmaWarp) {
-    tmem_alloc(&sm.tmem_base, kTmemCols);
-    tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
@@ -1016,7 +1020,9 @@ cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st
     configured[bf16].fetch_or(bit);
   }
   const int grid = static_cast<int>(std::min<int64_t>(n_items, sm_count()));
-  kern<<<grid, kThreads, smem, st>>>(tq, tck, tcv, tsk, tsv, p);
+  e = launch_pdl(kern, dim3(grid), dim3(kThreads), static_cast<size_t>(smem), st, tq, tck, tcv,
+                 tsk, tsv, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

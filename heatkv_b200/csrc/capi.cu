@@ -2,6 +2,7 @@
 // selection, error strings and the sticky device status word.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -13,6 +14,14 @@
 
 namespace heatkv {
 __device__ unsigned int g_device_status = 0;
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("HEATKV_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 unsigned int* device_status_ptr() {
   static std::atomic<unsigned int*> cache[64] = {};
@@ -88,6 +97,35 @@ int heatkv_pack_kv(void* dst_k, void* dst_v, const void* src_k, const void* src_
       batch, src_rows, dst_rows, dst_starts, src_starts, lengths, n_items, max_length,
       heatkv::device_status_ptr(), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "pack_flat_segments_kv launch");
+  return HEATKV_OK;
+}
+
+int heatkv_pack_kv_batched(const heatkv_pack_job* jobs, int64_t n_jobs, const int32_t* item_job,
+                           const int64_t* dst_starts, const int64_t* src_starts,
+                           const int64_t* lengths, int64_t n_items, int k_dtype, int v_dtype,
+                           int64_t batch, int64_t head_dim, int64_t max_length,
+                           int max_vector_bytes, void* stream) {
+  g_last_error.clear();
+  if (!valid_dtype(k_dtype) || !valid_dtype(v_dtype))
+    return fail(HEATKV_ERR_UNSUPPORTED, "heatkv_pack_kv_batched: unsupported dtype code");
+  if (n_jobs < 0 || n_items < 0 || batch < 0 || head_dim <= 0)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_pack_kv_batched: negative size");
+  if (max_vector_bytes != 16 && max_vector_bytes != 8 && max_vector_bytes != 4 &&
+      max_vector_bytes != 2 && max_vector_bytes != 1)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_pack_kv_batched: max_vector_bytes must be 16, 8, 4, 2 or 1");
+  if (n_items == 0 || batch == 0 || n_jobs == 0 || max_length <= 0) return HEATKV_OK;
+  if (!jobs || !item_job || !dst_starts || !src_starts || !lengths)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_pack_kv_batched: null pointer");
+  if (n_items > 65535 || batch > 65535)
+    return fail(HEATKV_ERR_UNSUPPORTED,
+                "heatkv_pack_kv_batched supports at most 65535 items and 65535 batch rows per call");
+  if ((max_length + 31) / 32 > 0x7fffffffLL)
+    return fail(HEATKV_ERR_UNSUPPORTED, "heatkv_pack_kv_batched: max_length too large");
+  cudaError_t e = heatkv::launch_pack_kv_batched(
+      jobs, n_jobs, item_job, dst_starts, src_starts, lengths, n_items,
+      head_dim * dtype_size(k_dtype), head_dim * dtype_size(v_dtype), batch, max_length,
+      max_vector_bytes, heatkv::device_status_ptr(), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "heatkv_pack_kv_batched launch");
   return HEATKV_OK;
 }
 

@@ -20,6 +20,37 @@ __device__ __forceinline__ void raise_status(unsigned int* status, unsigned int 
 
 __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels launched with launch_pdl may start (be scheduled, initialise shared memory and TMEM)
+// while the previous kernel of the stream is still running. Every global-memory access of such a
+// kernel comes after pdl_wait(), which returns once the previous grid has completed and its
+// writes are visible; pdl_trigger() lets the next kernel of the stream be scheduled early.
+// Without a programmatic predecessor both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launch with programmatic stream serialisation (HEATKV_PDL=0 in the environment turns it off and
+// launches plainly).
+bool pdl_enabled();
+
+template <typename... Exp, typename... Act>
+inline cudaError_t launch_pdl(void (*kernel)(Exp...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Act&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Act&&>(args)...);
+}
+
 // ---------------------------------------------------------------- element conversion
 template <typename T> struct Elem;
 template <> struct Elem<float> {

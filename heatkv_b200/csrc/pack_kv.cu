@@ -8,6 +8,7 @@
 // fp32 rows), all loads of a thread issued before its stores. The kernel is HBM-bound: every byte
 // is read once and written once. Descriptors are bounds-checked on the device; an item reaching
 // outside its tensor is skipped and flagged instead of corrupting memory.
+#include "attn.h"
 #include "common.cuh"
 
 namespace heatkv {
@@ -56,6 +57,8 @@ struct PackArgs {
 // grid = (row chunks, items, batch rows)
 template <typename VK, typename VV>
 __global__ void __launch_bounds__(kPackThreads) pack_kv_kernel(PackArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t item = blockIdx.y;
   const int64_t b = blockIdx.z;
   const int64_t len = a.lengths[item];
@@ -80,6 +83,42 @@ __global__ void __launch_bounds__(kPackThreads) pack_kv_kernel(PackArgs a) {
   }
 }
 
+// Several packs in one launch: item i belongs to job item_job[i], whose tensors and row counts
+// come from jobs[]. Used to issue the appends of every layer of one scale together.
+template <typename VK, typename VV>
+__global__ void __launch_bounds__(kPackThreads) pack_kv_batched_kernel(
+    const heatkv_pack_job* __restrict__ jobs, const int32_t* __restrict__ item_job,
+    const int64_t* __restrict__ dst_starts, const int64_t* __restrict__ src_starts,
+    const int64_t* __restrict__ lengths, int64_t n_jobs, int64_t row_bytes_k,
+    int64_t row_bytes_v, unsigned int* status) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t item = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int64_t len = lengths[item];
+  const int64_t row0 = int64_t(blockIdx.x) * kPackRowsPerBlock;
+  if (row0 >= len) return;
+  const int64_t jid = item_job[item];
+  if (jid < 0 || jid >= n_jobs) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) raise_status(status, HEATKV_DEVICE_PACK_OUT_OF_RANGE);
+    return;
+  }
+  const heatkv_pack_job& jb = jobs[jid];
+  const int64_t d0 = dst_starts[item];
+  const int64_t s0 = src_starts[item];
+  if (len < 0 || d0 < 0 || s0 < 0 || d0 + len > jb.dst_rows || s0 + len > jb.src_rows) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) raise_status(status, HEATKV_DEVICE_PACK_OUT_OF_RANGE);
+    return;
+  }
+  const int64_t rows = min(int64_t(kPackRowsPerBlock), len - row0);
+  copy_rows<VK>(static_cast<char*>(jb.dst_k) + ((b * jb.dst_rows) + d0 + row0) * row_bytes_k,
+                static_cast<const char*>(jb.src_k) + ((b * jb.src_rows) + s0 + row0) * row_bytes_k,
+                rows * row_bytes_k);
+  copy_rows<VV>(static_cast<char*>(jb.dst_v) + ((b * jb.dst_rows) + d0 + row0) * row_bytes_v,
+                static_cast<const char*>(jb.src_v) + ((b * jb.src_rows) + s0 + row0) * row_bytes_v,
+                rows * row_bytes_v);
+}
+
 static int vec_width(const void* p0, const void* p1, int64_t row_bytes) {
   const uintptr_t bits = reinterpret_cast<uintptr_t>(p0) | reinterpret_cast<uintptr_t>(p1) |
                          static_cast<uintptr_t>(row_bytes);
@@ -93,13 +132,12 @@ static int vec_width(const void* p0, const void* p1, int64_t row_bytes) {
 template <typename VK>
 static cudaError_t launch_v(int wv, dim3 grid, cudaStream_t st, const PackArgs& a) {
   switch (wv) {
-    case 16: pack_kv_kernel<VK, uint4><<<grid, kPackThreads, 0, st>>>(a); break;
-    case 8: pack_kv_kernel<VK, uint2><<<grid, kPackThreads, 0, st>>>(a); break;
-    case 4: pack_kv_kernel<VK, uint32_t><<<grid, kPackThreads, 0, st>>>(a); break;
-    case 2: pack_kv_kernel<VK, uint16_t><<<grid, kPackThreads, 0, st>>>(a); break;
-    default: pack_kv_kernel<VK, uint8_t><<<grid, kPackThreads, 0, st>>>(a); break;
+    case 16: return launch_pdl(pack_kv_kernel<VK, uint4>, grid, dim3(kPackThreads), 0, st, a);
+    case 8: return launch_pdl(pack_kv_kernel<VK, uint2>, grid, dim3(kPackThreads), 0, st, a);
+    case 4: return launch_pdl(pack_kv_kernel<VK, uint32_t>, grid, dim3(kPackThreads), 0, st, a);
+    case 2: return launch_pdl(pack_kv_kernel<VK, uint16_t>, grid, dim3(kPackThreads), 0, st, a);
+    default: return launch_pdl(pack_kv_kernel<VK, uint8_t>, grid, dim3(kPackThreads), 0, st, a);
   }
-  return cudaGetLastError();
 }
 
 cudaError_t launch_pack_kv(void* dst_k, void* dst_v, const void* src_k, const void* src_v,
@@ -122,6 +160,51 @@ cudaError_t launch_pack_kv(void* dst_k, void* dst_v, const void* src_k, const vo
     case 2: return launch_v<uint16_t>(wv, grid, stream, a);
     default: return launch_v<uint8_t>(wv, grid, stream, a);
   }
+}
+
+static int width_of(int64_t row_bytes, int max_width) {
+  int w = max_width;
+  while (w > 1 && (row_bytes % w) != 0) w /= 2;
+  return w;
+}
+
+template <typename VK>
+static void launch_batched_v(int wv, dim3 grid, cudaStream_t st, const heatkv_pack_job* jobs,
+                             const int32_t* item_job, const int64_t* dst_starts,
+                             const int64_t* src_starts, const int64_t* lengths, int64_t n_jobs,
+                             int64_t rbk, int64_t rbv, unsigned int* status) {
+#define HEATKV_PACK_B(VV) \
+  (void)launch_pdl(pack_kv_batched_kernel<VK, VV>, grid, dim3(kPackThreads), 0, st, jobs, \
+                   item_job, dst_starts, src_starts, lengths, n_jobs, rbk, rbv, status)
+  switch (wv) {
+    case 16: HEATKV_PACK_B(uint4); break;
+    case 8: HEATKV_PACK_B(uint2); break;
+    case 4: HEATKV_PACK_B(uint32_t); break;
+    case 2: HEATKV_PACK_B(uint16_t); break;
+    default: HEATKV_PACK_B(uint8_t); break;
+  }
+#undef HEATKV_PACK_B
+}
+
+cudaError_t launch_pack_kv_batched(const heatkv_pack_job* jobs, int64_t n_jobs,
+                                   const int32_t* item_job, const int64_t* dst_starts,
+                                   const int64_t* src_starts, const int64_t* lengths,
+                                   int64_t n_items, int64_t row_bytes_k, int64_t row_bytes_v,
+                                   int64_t batch, int64_t max_length, int max_vector_bytes,
+                                   unsigned int* status, cudaStream_t stream) {
+  const int64_t chunks = (max_length + kPackRowsPerBlock - 1) / kPackRowsPerBlock;
+  dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(n_items),
+            static_cast<unsigned>(batch));
+  const int wk = width_of(row_bytes_k, max_vector_bytes);
+  const int wv = width_of(row_bytes_v, max_vector_bytes);
+  switch (wk) {
+    case 16: launch_batched_v<uint4>(wv, grid, stream, jobs, item_job, dst_starts, src_starts, lengths, n_jobs, row_bytes_k, row_bytes_v, status); break;
+    case 8: launch_batched_v<uint2>(wv, grid, stream, jobs, item_job, dst_starts, src_starts, lengths, n_jobs, row_bytes_k, row_bytes_v, status); break;
+    case 4: launch_batched_v<uint32_t>(wv, grid, stream, jobs, item_job, dst_starts, src_starts, lengths, n_jobs, row_bytes_k, row_bytes_v, status); break;
+    case 2: launch_batched_v<uint16_t>(wv, grid, stream, jobs, item_job, dst_starts, src_starts, lengths, n_jobs, row_bytes_k, row_bytes_v, status); break;
+    default: launch_batched_v<uint8_t>(wv, grid, stream, jobs, item_job, dst_starts, src_starts, lengths, n_jobs, row_bytes_k, row_bytes_v, status); break;
+  }
+  return cudaGetLastError();
 }
 
 }  // namespace heatkv

@@ -72,6 +72,11 @@ def plan_attention(slots_per_segment, q_len: int, batch: int, *, sms: int = NUM_
     return order, best[1]
 
 
+# heatkv_pack_job of include/heatkv.h
+_JOB_DTYPE = np.dtype([("dst_k", "<u8"), ("dst_v", "<u8"), ("src_k", "<u8"), ("src_v", "<u8"),
+                       ("src_rows", "<i8"), ("dst_rows", "<i8")])
+
+
 @dataclasses.dataclass
 class Launch:
     kind: str            # "attention" | "pack"
@@ -80,6 +85,7 @@ class Launch:
     fn: Callable
     args: tuple          # ctypes arguments without the trailing stream
     work: float          # algorithmic FLOPs (attention) or HBM bytes (pack)
+    keep: object = None  # device arrays the arguments point into
 
     def __call__(self, stream: ctypes.c_void_p) -> None:
         status = self.fn(*self.args, stream)
@@ -222,9 +228,13 @@ class HotPath:
 
     # ------------------------------------------------------------------ launch plans
     def launches(self, inputs, outputs, *, kernel: int = _native.ATTN_AUTO,
-                 softmax_scale: Optional[float] = None) -> list:
+                 softmax_scale: Optional[float] = None, batch_packs: bool = True) -> list:
         """Launch list of one image. ``inputs[i][t] = (q, k, v)`` ([B, H, n_t, D]) and
-        ``outputs[i][t]`` ([B, n_t, H*D]) for plan index i; the tensors must stay alive."""
+        ``outputs[i][t]`` ([B, n_t, H*D]) for plan index i; the tensors must stay alive.
+
+        With ``batch_packs`` the compactions of every layer of a scale are issued as one batched
+        launch after the scale's last attention (then the slab activations, which read the dense
+        caches those appends complete): scale t's K/V are only read again at scale t + 1."""
         B, H, D = self.batch, self.num_heads, self.head_dim
         scale = float(softmax_scale) if softmax_scale is not None else D ** -0.5
         lib = self.lib
@@ -232,6 +242,7 @@ class HotPath:
         out = []
         for t in range(self.num_scales):
             n = self.tokens[t]
+            appends, activations = [], []
             for i, p in enumerate(self.plans):
                 q, k, v = inputs[i][t]
                 o = outputs[i][t]
@@ -255,26 +266,70 @@ class HotPath:
                      int(splits), _native.ptr(self.workspace), self.workspace.numel()), flops))
                 row_k = D * k.element_size()
                 row_v = D * v.element_size()
+                jobs = []
                 if dense and t in p.dense_append:
                     dst, src, ln, items, mx, slots = p.dense_append[t]
-                    out.append(self._pack(p.layer, t, self.dense_k[i], self.dense_v[i], k, v,
-                                          H * n, H * max(p.dense_len, 1), dst, src, ln, items, mx,
-                                          slots, row_k, row_v))
+                    jobs.append((appends, (self.dense_k[i], self.dense_v[i], k, v, H * n,
+                                           H * max(p.dense_len, 1), dst, src, ln, items, mx,
+                                           slots)))
                 if dense and t + 1 == p.first_target and p.activation is not None:
                     dst, src, ln, items, mx, slots = p.activation
-                    out.append(self._pack(p.layer, t, self.slab_k[i], self.slab_v[i],
-                                          self.dense_k[i], self.dense_v[i],
-                                          H * max(p.dense_len, 1), max(p.capacity, 1), dst, src,
-                                          ln, items, mx, slots, row_k, row_v, flat_src=True))
+                    jobs.append((activations, (self.slab_k[i], self.slab_v[i], self.dense_k[i],
+                                               self.dense_v[i], H * max(p.dense_len, 1),
+                                               max(p.capacity, 1), dst, src, ln, items, mx,
+                                               slots)))
                 if not dense and t in p.slab_append:
                     dst, src, ln, items, mx, slots = p.slab_append[t]
-                    out.append(self._pack(p.layer, t, self.slab_k[i], self.slab_v[i], k, v,
-                                          H * n, max(p.capacity, 1), dst, src, ln, items, mx,
-                                          slots, row_k, row_v))
+                    jobs.append((appends, (self.slab_k[i], self.slab_v[i], k, v, H * n,
+                                           max(p.capacity, 1), dst, src, ln, items, mx, slots)))
+                for group, job in jobs:
+                    if batch_packs:
+                        group.append(job)
+                    else:
+                        out.append(self._pack(p.layer, t, *job, row_k, row_v))
+            for group in (appends, activations):
+                if group:
+                    out.append(self._pack_batched(t, group))
         return out
 
+    def _pack_batched(self, t, jobs):
+        """One batched pack launch for ``jobs`` (tuples as ``_pack`` takes them)."""
+        dt = _native.DTYPE_CODES
+        B, D = self.batch, self.head_dim
+        recs = np.zeros(len(jobs), dtype=_JOB_DTYPE)
+        item_job, dsts, srcs, lens = [], [], [], []
+        align = 16
+        nbytes = 0.0
+        max_len = 0
+        kd, vd = jobs[0][0].dtype, jobs[0][1].dtype
+        for j, (dk, dv, sk, sv, src_rows, dst_rows, dst, src, ln, items, mx, slots) in \
+                enumerate(jobs):
+            if dk.dtype != kd or dv.dtype != vd:
+                raise ValueError("a batched pack needs one K dtype and one V dtype")
+            recs[j] = (dk.data_ptr(), dv.data_ptr(), sk.data_ptr(), sv.data_ptr(), src_rows,
+                       dst_rows)
+            for ptr_ in (dk.data_ptr(), dv.data_ptr(), sk.data_ptr(), sv.data_ptr()):
+                while align > 1 and ptr_ % align:
+                    align //= 2
+            item_job.append(torch.full((items,), j, dtype=torch.int32, device=self.device))
+            dsts.append(dst)
+            srcs.append(src)
+            lens.append(ln)
+            max_len = max(max_len, int(mx))
+            nbytes += 2.0 * slots * B * D * (dk.element_size() + dv.element_size())
+        job_dev = torch.from_numpy(recs.view(np.uint8).copy()).to(self.device)
+        item_job = torch.cat(item_job)
+        dsts, srcs, lens = torch.cat(dsts), torch.cat(srcs), torch.cat(lens)
+        keep = (job_dev, item_job, dsts, srcs, lens, jobs)
+        launch = Launch("pack", -1, t, self.lib.heatkv_pack_kv_batched,
+                        (_native.ptr(job_dev), len(jobs), _native.ptr(item_job),
+                         _native.ptr(dsts), _native.ptr(srcs), _native.ptr(lens),
+                         int(item_job.numel()), dt[kd], dt[vd], B, D, max_len, align), nbytes)
+        launch.keep = keep
+        return launch
+
     def _pack(self, layer, t, dk, dv, sk, sv, src_rows, dst_rows, dst, src, ln, items, mx, slots,
-              row_k, row_v, flat_src=False):
+              row_k, row_v):
         dt = _native.DTYPE_CODES
         B, D = self.batch, self.head_dim
         nbytes = 2.0 * slots * B * (row_k + row_v)

@@ -85,6 +85,37 @@ int heatkv_pack_kv(void* dst_k, void* dst_v, const void* src_k, const void* src_
                    const int64_t* lengths, int64_t n_items, int64_t max_length, void* stream);
 
 /*
+ * heatkv_pack_kv_batched - several heatkv_pack_kv copies (jobs) in one launch.
+ * No counterpart in the reference, which packs once per layer call; a caller that holds the K/V
+ * of every layer of a scale (a pre-planned step, a graph) issues all of that scale's appends at
+ * once instead of one launch per layer.
+ *
+ * jobs      : device array of n_jobs heatkv_pack_job; job j copies like heatkv_pack_kv with its
+ *             own tensors and row counts (all jobs share k_dtype, v_dtype, batch and head_dim).
+ * item_job  : int32 device array [n_items], the job of each item.
+ * dst_starts / src_starts / lengths : int64 device arrays [n_items], as in heatkv_pack_kv, relative
+ *             to the item's job. max_length >= every lengths[i].
+ * max_vector_bytes : 16, 8, 4, 2 or 1 - the widest access every job's four base pointers allow
+ *             (all aligned to it); row sizes narrow it further.
+ * Items of different jobs must not write the same rows. Out-of-range items or job indices are
+ * skipped and raise HEATKV_DEVICE_PACK_OUT_OF_RANGE.
+ */
+typedef struct {
+  void* dst_k;
+  void* dst_v;
+  const void* src_k;
+  const void* src_v;
+  int64_t src_rows; /* rows of src_* per batch row */
+  int64_t dst_rows; /* rows of dst_* per batch row */
+} heatkv_pack_job;
+
+int heatkv_pack_kv_batched(const heatkv_pack_job* jobs, int64_t n_jobs, const int32_t* item_job,
+                           const int64_t* dst_starts, const int64_t* src_starts,
+                           const int64_t* lengths, int64_t n_items, int k_dtype, int v_dtype,
+                           int64_t batch, int64_t head_dim, int64_t max_length,
+                           int max_vector_bytes, void* stream);
+
+/*
  * heatkv_segmented_attention - block-causal attention of the current scale's queries over the
  * head's slab segments plus the current scale's K/V.
  * Replaces fused_real_pruning_flat_segmented_attention (real_pruning_fused_attention.py:445-591).

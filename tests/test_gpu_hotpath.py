@@ -66,3 +66,26 @@ def test_hot_path_matches_keep_mask_attention(model, budget, layers):
             err = (outputs[i][t].float() - ref).abs().max().item()
             scale = ref.abs().max().item()
             assert err <= BF16_ATOL and err / scale <= BF16_REL, (layer, t, err, scale)
+
+
+def test_batched_scale_packs_equal_per_layer_packs():
+    """One batched compaction launch per scale leaves the same slabs and outputs, bit for bit, as
+    one pack launch per layer (the orchestrator's order)."""
+    ctrl, L, H = _controller("2b", 0.10)
+    dev = torch.device("cuda", 0)
+    layers = [0, 9, 30]
+    results = []
+    for batched in (False, True):
+        hot = HotPath(ctrl, L, H, 2, dev, layers=layers)
+        inputs, outputs, _, _ = allocate_io(hot, seed=3)
+        launches = hot.launches(inputs, outputs, batch_packs=batched)
+        packs = sum(1 for l in launches if l.kind == "pack")
+        hot.run(launches)
+        torch.cuda.synchronize()
+        results.append((packs, [o.clone() for row in outputs for o in row],
+                        [s.clone() for s in hot.slab_k + hot.slab_v]))
+    (n0, out0, slab0), (n1, out1, slab1) = results
+    assert n1 < n0
+    assert all(torch.equal(a, b) for a, b in zip(out0, out1))
+    assert all(torch.equal(a, b) for a, b in zip(slab0, slab1))
+    assert _native.device_status(dev) == 0
