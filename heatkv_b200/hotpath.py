@@ -311,14 +311,14 @@ class HotPath:
             for ptr_ in (dk.data_ptr(), dv.data_ptr(), sk.data_ptr(), sv.data_ptr()):
                 while align > 1 and ptr_ % align:
                     align //= 2
-            item_job.append(torch.full((items,), j, dtype=torch.int32, device=self.device))
+            item_job.append(np.full(items, j, dtype=np.int32))
             dsts.append(dst)
             srcs.append(src)
             lens.append(ln)
             max_len = max(max_len, int(mx))
             nbytes += 2.0 * slots * B * D * (dk.element_size() + dv.element_size())
         job_dev = torch.from_numpy(recs.view(np.uint8).copy()).to(self.device)
-        item_job = torch.cat(item_job)
+        item_job = torch.from_numpy(np.concatenate(item_job)).to(self.device)
         dsts, srcs, lens = torch.cat(dsts), torch.cat(srcs), torch.cat(lens)
         keep = (job_dev, item_job, dsts, srcs, lens, jobs)
         launch = Launch("pack", -1, t, self.lib.heatkv_pack_kv_batched,

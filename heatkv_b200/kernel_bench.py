@@ -6,6 +6,8 @@
 ``attention``: one call shaped like a fused target of the 2B model - per head six slab segments
 (1, 4, 16, 36, 64 and the rest of ``--slots`` slots) plus ``--q-len`` current tokens.
 ``pack``: the append of one scale (every head's ``--q-len`` tokens) into a slab.
+``pack-batched``: the same append for ``--layers`` layers (one slab and one source per layer) as
+one ``heatkv_pack_kv_batched`` launch, as the pre-planned step issues a scale's appends.
 Prints per-call device time (CUDA events, warm, back to back) and the achieved TFLOP/s or GB/s.
 """
 
@@ -61,7 +63,8 @@ def time_call(fn, iters, warmup=3):
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("kernel", choices=["attention", "pack"])
+    ap.add_argument("kernel", choices=["attention", "pack", "pack-batched"])
+    ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--rows", type=int, default=2)
     ap.add_argument("--heads", type=int, default=16)
     ap.add_argument("--q-len", type=int, default=4096)
@@ -78,6 +81,37 @@ def main(argv=None):
         print(f"attention rows={args.rows} heads={args.heads} q_len={args.q_len} "
               f"slots={args.slots} {args.dtype}: {ms * 1e3:.1f} us/call, "
               f"{flops / ms / 1e9:.1f} TFLOP/s", flush=True)
+    elif args.kernel == "pack-batched":
+        import numpy as np
+
+        from .hotpath import _JOB_DTYPE
+        H, n, B, L = args.heads, args.q_len, args.rows, args.layers
+        lib = _native.load()
+        srcs = [(torch.randn(B, H * n, 128, device="cuda").to(dtype),
+                 torch.randn(B, H * n, 128, device="cuda").to(dtype)) for _ in range(L)]
+        dsts = [(torch.zeros(B, H * n + 1000, 128, device="cuda", dtype=dtype),
+                 torch.zeros(B, H * n + 1000, 128, device="cuda", dtype=dtype)) for _ in range(L)]
+        jobs = np.zeros(L, dtype=_JOB_DTYPE)
+        for j in range(L):
+            jobs[j] = (dsts[j][0].data_ptr(), dsts[j][1].data_ptr(), srcs[j][0].data_ptr(),
+                       srcs[j][1].data_ptr(), H * n, H * n + 1000)
+        job_dev = torch.from_numpy(jobs.view(np.uint8).copy()).cuda()
+        item_job = torch.arange(L, device="cuda", dtype=torch.int32).repeat_interleave(H)
+        dst = (torch.arange(H, device="cuda", dtype=torch.int64) * n + 7).repeat(L)
+        src = (torch.arange(H, device="cuda", dtype=torch.int64) * n).repeat(L)
+        ln = torch.full((L * H,), n, device="cuda", dtype=torch.int64)
+        stream = _native.stream_handle(torch.device("cuda"))
+        dt = _native.DTYPE_CODES[dtype]
+
+        def fn():
+            _native.check(lib.heatkv_pack_kv_batched(
+                _native.ptr(job_dev), L, _native.ptr(item_job), _native.ptr(dst),
+                _native.ptr(src), _native.ptr(ln), L * H, dt, dt, B, 128, n, 16, stream),
+                "pack batched")
+        ms = time_call(fn, args.iters, args.warmup)
+        nbytes = 2.0 * L * B * H * n * 128 * dsts[0][0].element_size() * 2
+        print(f"pack-batched layers={L} rows={B} heads={H} tokens={n} {args.dtype}: "
+              f"{ms * 1e3:.1f} us/call, {nbytes / ms / 1e6:.1f} GB/s", flush=True)
     else:
         H, n, B = args.heads, args.q_len, args.rows
         src_k = torch.randn(B, H * n, 128, device="cuda").to(dtype)
