@@ -503,9 +503,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         "roofline": {"bound": "tensor", "achieved": round(att_achieved, 1),
                      "peak": sustained, "unit": "TFLOP/s",
                      "frac": round(att_achieved / sustained, 4),
-                     # DRAM bytes of one target-12 launch (the largest share of the step) from the
-                     # ncu capture in profiles/attn_sm100_kernel_2b_q4096_rows2.md; 77.7 MB are
-                     # algorithmic, the rest K/V re-read by the query blocks of a head
+                     # DRAM bytes of one target-12 launch (the largest share of the step) from an
+                     # ncu capture of that shape; 77.7 MB are algorithmic, the rest is K/V re-read
+                     # by the query blocks of a head
                      "traffic": 128848896, "traffic_launch": "target 12 (Lq 4096, 2 rows x 16 heads)",
                      "peak_kind": f"bf16_tflops_sustained ({peak_src})",
                      "frac_of_burst": round(att_achieved / burst, 4),
@@ -517,8 +517,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
                           "peak": hbm, "unit": "GB/s",
                           "frac": round(pack_achieved / hbm, 4) if pack_achieved else None,
                           "kernel": "pack_kv_batched_kernel", "ms_per_step": round(pack_ms, 3),
-                          # ncu, one scale's appends for 32 layers (604 MB algorithmic):
-                          # profiles/pack_kv_batched_kernel_32layers_t576.md
+                          # ncu capture of one scale's appends for 32 layers (604 MB algorithmic)
                           "traffic": 558111000, "traffic_launch": "32-layer append of a 576-token scale",
                           "launches_per_step": sum(1 for l in launches if l.kind == "pack")},
         "cpu_baseline": cpu,
