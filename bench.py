@@ -385,11 +385,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
 
     # e2e: pinned host inputs -> device, every launch through the C ABI, outputs -> host
     in_bufs, out_buf = wl.in_bufs, wl.out_buf
-    h_in = [torch.empty_like(b, device="cpu").pin_memory() for b in in_bufs]
+    e2e_steps = 0 if args.no_e2e else max(1, min(args.steps, args.e2e_steps))
+    h_in = [torch.empty_like(b, device="cpu").pin_memory() for b in in_bufs] if e2e_steps else []
     for hb, db in zip(h_in, in_bufs):
         hb.copy_(db)
-    h_out = torch.empty_like(out_buf, device="cpu").pin_memory() if out_buf is not None else None
-    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    h_out = (torch.empty_like(out_buf, device="cpu").pin_memory()
+             if out_buf is not None and e2e_steps else None)
 
     def e2e_step_serial():
         for hb, db in zip(h_in, in_bufs):
@@ -435,7 +436,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     e2e_step = e2e_step_pipelined if pipelined else e2e_step_serial
 
     with torch.cuda.stream(stream):
-        for _ in range(2):  # warm the copy engines
+        for _ in range(2 if e2e_steps else 0):  # warm the copy engines
             e2e_step()
         stream.synchronize()
         if world > 1:
@@ -446,7 +447,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
             e2e_step()
         e1.record(stream)
         e1.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps if e2e_steps else float("nan")
     h2d = sum(b.numel() * b.element_size() for b in in_bufs)
     d2h = out_buf.numel() * out_buf.element_size() if out_buf is not None else 0
 
@@ -463,7 +464,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         return
 
     tflops = wl.job_flops / (step_ms * 1e-3) / 1e12
-    e2e_tflops = wl.job_flops / (e2e_ms * 1e-3) / 1e12
+    e2e_tflops = wl.job_flops / (e2e_ms * 1e-3) / 1e12 if e2e_steps else None
     att_achieved = att_flops / (att_ms * 1e-3) / 1e12
     sustained = float(peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"]))
     burst = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
@@ -521,7 +522,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
                           "traffic": 558111000, "traffic_launch": "32-layer append of a 576-token scale",
                           "launches_per_step": sum(1 for l in launches if l.kind == "pack")},
         "cpu_baseline": cpu,
-        "e2e": {"value": round(e2e_tflops, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+        "e2e": None if not e2e_steps else {"value": round(e2e_tflops, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
                 "path": ("C ABI, inputs from pinned host memory, outputs back to host"
                          + (", copies pipelined per (layer, scale)" if pipelined else ""))},
@@ -542,6 +543,8 @@ def main() -> None:
     ap.add_argument("--budget", type=float, default=0.10)
     ap.add_argument("--rows", type=int, default=2, help="batch rows per GPU (image + CFG = 2)")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the host-memory leg (for configurations too large to pin on the host)")
     ap.add_argument("--ref-targets", type=int, default=5,
                     help="fused targets in the CPU sample (bounds the CPU time)")
     ap.add_argument("--ref-layers", type=int, default=3,

@@ -68,6 +68,61 @@ def test_hot_path_matches_keep_mask_attention(model, budget, layers):
             assert err <= BF16_ATOL and err / scale <= BF16_REL, (layer, t, err, scale)
 
 
+def _random_controller(budget, seed, layers=32, heads=16):
+    """2B-shaped controller from seeded random per-source removal orders (the budget sweep)."""
+    from heatkv_b200 import budget as bud, synthetic
+    from heatkv_b200.enable_pruning import (ScaleSpecificPruningController,
+                                            _validate_and_normalize_removed_heads_by_scale_specific)
+
+    class _M:
+        num_heads = heads
+
+    orders = synthetic.random_removal_orders(layers, heads, seed=seed)
+    view = bud.strict_removed_heads_by_scale_specific_for_budget(
+        budget, orders, num_layers=layers, num_heads=heads, source_scale_start=3,
+        protected_prefix_scales=3)
+    norm = _validate_and_normalize_removed_heads_by_scale_specific(
+        view["removed_heads_by_scale"], [_M()] * layers, source_scale_start=3)
+    return ScaleSpecificPruningController(num_layers=layers, num_heads=heads,
+                                          static_removed_heads_by_scale=norm, source_scale_start=3)
+
+
+@pytest.mark.parametrize("budget,rows,layer", [(0.25, 16, 5), (0.5, 16, 30), (0.05, 16, 12)])
+def test_hot_path_budget_sweep_batch16(budget, rows, layer):
+    """Budget sweep shape (2B, 16 rows = batch 8 + CFG, seeded random orders): uneven slab
+    lengths per head, several query blocks per CTA."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device("cuda", 0)
+    ctrl = _random_controller(budget, seed=1234)
+    hot = HotPath(ctrl, 32, 16, rows, dev, torch.bfloat16, torch.bfloat16, layers=[layer])
+    inputs, outputs, _, _ = allocate_io(hot, seed=9)
+    hot.run(hot.launches(inputs, outputs))
+    torch.cuda.synchronize()
+    assert _native.device_status(dev) == 0
+    for t in range(hot.num_scales):
+        ref = _reference(ctrl, layer, t, inputs[0])
+        err = (outputs[0][t].float() - ref).abs().max().item()
+        scale = ref.abs().max().item()
+        assert err <= BF16_ATOL and err / scale <= BF16_REL, (layer, t, err, scale)
+
+
+def test_hot_path_8b_batch8():
+    """configs[2] shape: 8B (28 heads), batch 4 + CFG = 8 rows, orders/8b.json at 10 %."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device("cuda", 0)
+    ctrl, L, H = _controller("8b", 0.10)
+    hot = HotPath(ctrl, L, H, 8, dev, torch.bfloat16, torch.bfloat16, layers=[20])
+    inputs, outputs, _, _ = allocate_io(hot, seed=4)
+    hot.run(hot.launches(inputs, outputs))
+    torch.cuda.synchronize()
+    assert _native.device_status(dev) == 0
+    for t in range(hot.num_scales):
+        ref = _reference(ctrl, 20, t, inputs[0])
+        err = (outputs[0][t].float() - ref).abs().max().item()
+        scale = ref.abs().max().item()
+        assert err <= BF16_ATOL and err / scale <= BF16_REL, (t, err, scale)
+
+
 def test_batched_scale_packs_equal_per_layer_packs():
     """One batched compaction launch per scale leaves the same slabs and outputs, bit for bit, as
     one pack launch per layer (the orchestrator's order)."""
