@@ -77,6 +77,7 @@ def set_real_pruning_fast_phase_profile_enabled(enabled: bool = True) -> None:
 
 
 def snapshot_real_pruning_fast_phase_profile(*, reset: bool = False) -> dict:
+    _resolve_phase_events()
     result = {
         "cpu_ms": {k: v / 1e6 for k, v in _PHASE_CPU_NS.items()},
         "cuda_ms": dict(_PHASE_CUDA_MS),
@@ -124,14 +125,6 @@ def _resolve_phase_events() -> None:
         e1.synchronize()
         _PHASE_CUDA_MS[name] = _PHASE_CUDA_MS.get(name, 0.0) + e0.elapsed_time(e1)
     _Phase._pending.clear()
-
-
-_orig_snapshot = snapshot_real_pruning_fast_phase_profile
-
-
-def snapshot_real_pruning_fast_phase_profile(*, reset: bool = False) -> dict:  # noqa: F811
-    _resolve_phase_events()
-    return _orig_snapshot(reset=reset)
 
 
 def _stat_add(name: str, value=1) -> None:
