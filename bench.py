@@ -271,20 +271,10 @@ def _sharded_workload(args, ctrl, layers, heads, rank, world, dev):
     costs = sharding.head_costs(ctrl, layers, heads)
     plan = sharding.plan_shards(costs, args.global_rows, world, split=args.shard)
     sh = sharding.ShardedHotPath(ctrl, layers, heads, plan, rank, dev, torch.bfloat16,
-                                 torch.bfloat16, gather=True)
+                                 torch.bfloat16, gather=True, exchange=args.exchange)
     inputs, outputs, in_bufs, _ = allocate_io(sh.local, seed=1000 + rank)
     # the full [B, n_t, H * D] outputs every rank receives
-    per_layer = sum(sh.tokens)
-    full_buf = torch.empty(layers * args.global_rows * per_layer * heads * 128,
-                           dtype=torch.bfloat16, device=dev)
-    full, off = [], 0
-    for _ in range(layers):
-        row = []
-        for n in sh.tokens:
-            sz = args.global_rows * n * heads * 128
-            row.append(full_buf[off:off + sz].view(args.global_rows, n, heads * 128))
-            off += sz
-        full.append(row)
+    full, full_buf = sh.allocate_full_outputs(args.global_rows, heads)
     gbuf = sh.allocate_gather_buffer()
     launches = sh.launches(inputs, outputs, full, gbuf)
     att = sum(l.work for l in launches if l.kind == "attention")
@@ -292,8 +282,9 @@ def _sharded_workload(args, ctrl, layers, heads, rank, world, dev):
     return _Workload(
         engine=sh.local, launches=launches, keep=(inputs, outputs, full, gbuf), in_bufs=in_bufs,
         out_buf=full_buf if rank == 0 else None, att_flops=att, job_flops=job,
-        images=args.global_rows / 2, scaling="strong",
+        images=args.global_rows / 2, scaling="strong", close=sh.close,
         rows_label={"global_rows": args.global_rows, "shard": args.shard,
+                    "exchange": args.exchange,
                     "row_groups": plan.row_groups, "head_groups": plan.head_groups,
                     "head_imbalance": round(plan.imbalance(costs), 4)},
         slab_bytes=sh.local.slab_bytes(), plan=plan)
@@ -316,7 +307,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     n_att = sum(1 for l in launches if l.kind == "attention")
     att_flops = wl.att_flops
     pack_bytes = sum(l.work for l in launches if l.kind == "pack")
-    n_own = sum(1 for l in launches if l.kind in ("attention", "pack", "gather"))
+    n_own = sum(1 for l in launches if l.kind in ("attention", "pack", "gather", "barrier"))
 
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
@@ -460,6 +451,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     # graphs that hold NCCL work are released before the process group goes away
     del graphs, ev_sets, step_graph
     torch.cuda.synchronize(dev)
+    if getattr(wl, "close", None) is not None:
+        wl.close()   # collective: peer-shared buffers are unmapped and freed on every rank
     if rank != 0:
         return
 
@@ -554,6 +547,9 @@ def main() -> None:
                     help="image: each GPU runs its own image (weak scaling); auto/rows/heads: "
                          "one batch of --global-rows rows sharded over the GPUs (strong scaling)")
     ap.add_argument("--global-rows", type=int, default=2)
+    ap.add_argument("--exchange", choices=["nccl", "p2p"], default="p2p",
+                    help="sharded modes: NCCL all-gather + reassembly, or the attention kernel "
+                         "storing into every rank's output over NVLink + a peer barrier")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -46,6 +46,15 @@ SIGNATURES = {
                                            _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _i, _i,
                                            _p, _i, _p, ctypes.c_size_t, _p]),
     "heatkv_attention_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _i64, _i]),
+    "heatkv_segmented_attention_scatter": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _p, _p,
+                                                _i64, _i64, _i, _i, _i, _i64, _i64, _i64, _i64,
+                                                _i64, _i64, ctypes.c_float, _p, _p]),
+    "heatkv_peer_barrier": (_i, [_p, _p, _i, _i, _p]),
+    "heatkv_peer_alloc": (_i, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _p]),
+    "heatkv_peer_open": (_i, [_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "heatkv_peer_close": (_i, [_p]),
+    "heatkv_peer_free": (_i, [_p]),
+    "heatkv_enable_peer_access": (_i, [_i]),
     "heatkv_segmented_attention_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i,
                                                 _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float,
                                                 _i, _i, _p, _i, _p]),

@@ -30,6 +30,13 @@ struct AttnArgs {
   void* workspace = nullptr;            // split partials and counters (zeroed before first use)
   size_t workspace_bytes = 0;
   unsigned int* status = nullptr;       // device status word (device_status_ptr())
+  // scatter epilogue (tcgen05 kernel, unsplit): rows to n_out full outputs at mapped rows/heads
+  void* const* out_ptrs = nullptr;      // [n_out] device array of base pointers
+  const int32_t* out_rows = nullptr;    // [batch] -> row of the full output
+  const int32_t* out_heads = nullptr;   // [heads] -> head of the full output
+  int n_out = 0;
+  int64_t out_batch = 0;
+  int64_t out_heads_total = 0;
 };
 
 // Device address of the sticky status word on the current device (resolved once per device);
@@ -60,6 +67,11 @@ cudaError_t launch_pack_kv_batched(const heatkv_pack_job* jobs, int64_t n_jobs,
                                    int64_t n_items, int64_t row_bytes_k, int64_t row_bytes_v,
                                    int64_t batch, int64_t max_length, int max_vector_bytes,
                                    unsigned int* status, cudaStream_t stream);
+
+// One step of the cross-GPU barrier (peer_barrier.cu): publish this rank's next epoch into every
+// rank's flag array, then wait (bounded) until every rank's epoch has arrived in its own.
+cudaError_t launch_peer_barrier(uint32_t* const* flag_ptrs, uint32_t* counter, int world,
+                                int rank, unsigned int* status, cudaStream_t stream);
 
 // Head-shard reassembly (shard_gather.cu); sms = SMs of the device (grid sizing).
 cudaError_t launch_shard_gather(void* dst, const void* src, const int32_t* row_map,

@@ -110,6 +110,15 @@ struct Params {
   int splits;                 // key-range splits per query block
   int n_items;                // heads * batch * qpairs * splits
   int seg_stride;             // segment-table row length (max_segments)
+  // scatter epilogue (n_out > 0): every output row goes to n_out full [out_batch, Lq,
+  // out_heads_total * D] tensors (e.g. every rank's copy, over NVLink) at row out_rows[b] and head
+  // out_heads[h]; otherwise to `out` in the local [batch, Lq, heads * D] layout
+  void* const* out_ptrs;
+  const int32_t* out_rows;
+  const int32_t* out_heads;
+  int n_out;
+  int out_batch;
+  int out_heads_total;
 };
 
 struct Item {
@@ -730,20 +739,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.splits == 1) {
         if (have_o) {
           const float inv = 1.f / l_run;
-          OutT* orow = static_cast<OutT*>(p.out) + ((int64_t(it.b) * p.q_len + qrow) * p.heads + it.h) * kD;
+          int64_t off = ((int64_t(it.b) * p.q_len + qrow) * p.heads + it.h) * kD;
+          int n_dst = 1;
+          bool in_range = true;
+          if (p.n_out > 0) {
+            const int grow = __ldg(p.out_rows + it.b), ghead = __ldg(p.out_heads + it.h);
+            in_range = grow >= 0 && grow < p.out_batch && ghead >= 0 && ghead < p.out_heads_total;
+            if (!in_range && row == 0) raise_status(p.status, HEATKV_DEVICE_GATHER_OUT_OF_RANGE);
+            off = ((int64_t(grow) * p.q_len + qrow) * p.out_heads_total + ghead) * kD;
+            n_dst = p.n_out;
+          }
 #pragma unroll 1
           for (int cc = 0; cc < 8; ++cc) {
             float o[16];
             tmem_ld16_sync(tO + cc * 16, o);
-            if (qrow < Lq) {
+            if (qrow < Lq && in_range) {
               uint32_t w[8];
 #pragma unroll
               for (int i = 0; i < 8; ++i) w[i] = pack2<kBF16>(o[2 * i] * inv, o[2 * i + 1] * inv);
-              uint4* dst = reinterpret_cast<uint4*>(orow + cc * 16);
-              dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-              dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+#pragma unroll 1
+              for (int r = 0; r < n_dst; ++r) {
+                OutT* base = p.n_out > 0 ? static_cast<OutT*>(p.out_ptrs[r]) : static_cast<OutT*>(p.out);
+                uint4* dst = reinterpret_cast<uint4*>(base + off + cc * 16);
+                dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+              }
             }
           }
+          // stores to other GPUs are visible system-wide before this kernel's completion is
+          if (p.n_out > 0) __threadfence_system();
         }
       } else {
         // partial result of this split: (m, l) and the unnormalised O row
@@ -983,6 +1007,13 @@ cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st
   p.seg_counts = a.seg_counts;
   p.head_order = a.head_order;
   p.out = a.out;
+  p.out_ptrs = a.out_ptrs;
+  p.out_rows = a.out_rows;
+  p.out_heads = a.out_heads;
+  p.n_out = a.n_out;
+  p.out_batch = static_cast<int>(a.out_batch);
+  p.out_heads_total = static_cast<int>(a.out_heads_total);
+  if (a.n_out > 0 && splits != 1) return cudaErrorNotSupported;
   p.status = a.status;
   uint8_t* ws = static_cast<uint8_t*>(a.workspace);
   p.ws_counter = splits > 1 ? reinterpret_cast<uint32_t*>(ws + wl.counter_off) : nullptr;

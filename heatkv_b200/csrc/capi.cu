@@ -129,13 +129,22 @@ int heatkv_pack_kv_batched(const heatkv_pack_job* jobs, int64_t n_jobs, const in
   return HEATKV_OK;
 }
 
+struct Scatter {
+  void* const* out_ptrs;
+  const int32_t* out_rows;
+  const int32_t* out_heads;
+  int n_out;
+  int64_t out_batch, out_heads_total;
+};
+
 static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
                           const int32_t* seg_starts, const int32_t* seg_ends,
                           const int32_t* seg_counts, const void* cur_k, const void* cur_v, void* out,
                           int q_dtype, int k_dtype, int v_dtype, int64_t batch, int64_t heads,
                           int64_t q_len, int64_t capacity, int64_t head_dim, int64_t max_segments,
                           float softmax_scale, int kernel, const int32_t* head_order,
-                          int kv_splits, void* workspace, size_t workspace_bytes, void* stream) {
+                          int kv_splits, void* workspace, size_t workspace_bytes, void* stream,
+                          const Scatter* scatter = nullptr) {
   g_last_error.clear();
   if (!valid_dtype(q_dtype) || !valid_dtype(k_dtype) || !valid_dtype(v_dtype))
     return fail(HEATKV_ERR_UNSUPPORTED,
@@ -147,7 +156,8 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
   if (batch < 0 || heads <= 0 || capacity < 0 || max_segments < 0 || kv_splits < 0)
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: invalid sizes");
   if (batch == 0) return HEATKV_OK;
-  if (!q || !cur_k || !cur_v || !out || !seg_counts || (max_segments > 0 && (!seg_starts || !seg_ends)))
+  if (!q || !cur_k || !cur_v || (!out && !scatter) || !seg_counts ||
+      (max_segments > 0 && (!seg_starts || !seg_ends)))
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: null pointer");
   if (capacity > 0 && (!slab_k || !slab_v))
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: null slab with capacity > 0");
@@ -167,6 +177,14 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;
   a.status = heatkv::device_status_ptr();
+  if (scatter) {
+    a.out_ptrs = scatter->out_ptrs;
+    a.out_rows = scatter->out_rows;
+    a.out_heads = scatter->out_heads;
+    a.n_out = scatter->n_out;
+    a.out_batch = scatter->out_batch;
+    a.out_heads_total = scatter->out_heads_total;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool same16 = (q_dtype == k_dtype && k_dtype == v_dtype && q_dtype != HEATKV_DTYPE_F32);
   if (kernel == HEATKV_ATTN_TCGEN05 && !same16)
@@ -175,9 +193,15 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
   if (kernel != HEATKV_ATTN_EXACT && same16) {
     cudaError_t e = heatkv::launch_attention_sm100(a, q_dtype == HEATKV_DTYPE_BF16, st);
     if (e == cudaSuccess) return HEATKV_OK;
+    if (e == cudaErrorNotSupported && scatter)
+      return fail(HEATKV_ERR_UNSUPPORTED,
+                  "heatkv_segmented_attention_scatter: these sizes need the split or exact path");
     if (e != cudaErrorNotSupported || kernel == HEATKV_ATTN_TCGEN05)
       return cuda_fail(e, "tcgen05 segmented attention launch");
   }
+  if (scatter)
+    return fail(HEATKV_ERR_UNSUPPORTED,
+                "heatkv_segmented_attention_scatter needs q, k and v all bfloat16 or all float16");
   cudaError_t e = heatkv::launch_attention_simt(a, q_dtype, k_dtype, v_dtype, st);
   if (e != cudaSuccess) return cuda_fail(e, "segmented attention launch");
   return HEATKV_OK;
@@ -216,6 +240,101 @@ int heatkv_segmented_attention_ws(const void* q, const void* slab_k, const void*
                         q_dtype, k_dtype, v_dtype, batch, heads, q_len, capacity, head_dim,
                         max_segments, softmax_scale, kernel, head_order, kv_splits, workspace,
                         workspace_bytes, stream);
+}
+
+int heatkv_segmented_attention_scatter(
+    const void* q, const void* slab_k, const void* slab_v, const int32_t* seg_starts,
+    const int32_t* seg_ends, const int32_t* seg_counts, const void* cur_k, const void* cur_v,
+    void* const* out_ptrs, int n_out, const int32_t* out_rows, const int32_t* out_heads,
+    int64_t out_batch, int64_t out_heads_total, int q_dtype, int k_dtype, int v_dtype,
+    int64_t batch, int64_t heads, int64_t q_len, int64_t capacity, int64_t head_dim,
+    int64_t max_segments, float softmax_scale, const int32_t* head_order, void* stream) {
+  g_last_error.clear();
+  if (n_out <= 0 || n_out > 64 || !out_ptrs || !out_rows || !out_heads)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT,
+                "heatkv_segmented_attention_scatter: 1..64 destinations and both maps are required");
+  if (out_batch < batch || out_heads_total < heads || out_batch > 0x7fffffff ||
+      out_heads_total > 0x7fffffff)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT,
+                "heatkv_segmented_attention_scatter: the full output is smaller than this shard");
+  const Scatter sc{out_ptrs, out_rows, out_heads, n_out, out_batch, out_heads_total};
+  return attention_impl(q, slab_k, slab_v, seg_starts, seg_ends, seg_counts, cur_k, cur_v, nullptr,
+                        q_dtype, k_dtype, v_dtype, batch, heads, q_len, capacity, head_dim,
+                        max_segments, softmax_scale, HEATKV_ATTN_TCGEN05, head_order, 1, nullptr, 0,
+                        stream, &sc);
+}
+
+int heatkv_peer_barrier(uint32_t* const* flag_ptrs, uint32_t* counter, int world, int rank,
+                        void* stream) {
+  g_last_error.clear();
+  if (world <= 0 || world > 32 || rank < 0 || rank >= world || !flag_ptrs || !counter)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_peer_barrier: invalid world, rank or pointer");
+  cudaError_t e = heatkv::launch_peer_barrier(flag_ptrs, counter, world, rank,
+                                              heatkv::device_status_ptr(),
+                                              static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "heatkv_peer_barrier launch");
+  return HEATKV_OK;
+}
+
+int heatkv_peer_alloc(size_t bytes, void** ptr, void* handle) {
+  g_last_error.clear();
+  if (!ptr || !handle || bytes == 0)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_peer_alloc: null pointer or zero size");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "heatkv_peer_alloc: cudaMalloc");
+  e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "heatkv_peer_alloc: cudaIpcGetMemHandle");
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return HEATKV_OK;
+}
+
+int heatkv_peer_open(const void* handle, void** ptr) {
+  g_last_error.clear();
+  if (!ptr || !handle) return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_peer_open: null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "heatkv_peer_open: cudaIpcOpenMemHandle");
+  return HEATKV_OK;
+}
+
+int heatkv_peer_close(void* ptr) {
+  g_last_error.clear();
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "heatkv_peer_close");
+  return HEATKV_OK;
+}
+
+int heatkv_peer_free(void* ptr) {
+  g_last_error.clear();
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "heatkv_peer_free");
+  return HEATKV_OK;
+}
+
+int heatkv_enable_peer_access(int peer_device) {
+  g_last_error.clear();
+  int dev = 0, can = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceCanAccessPeer(&can, dev, peer_device);
+  if (e != cudaSuccess) return cuda_fail(e, "heatkv_enable_peer_access: query");
+  if (!can)
+    return fail(HEATKV_ERR_UNSUPPORTED, "device %d cannot access device %d directly", dev,
+                peer_device);
+  e = cudaDeviceEnablePeerAccess(peer_device, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    (void)cudaGetLastError();
+    e = cudaSuccess;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "heatkv_enable_peer_access");
+  return HEATKV_OK;
 }
 
 size_t heatkv_attention_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len,

@@ -26,6 +26,7 @@ from __future__ import annotations
 
 import dataclasses
 import math
+import ctypes
 from typing import List, Optional
 
 import numpy as np
@@ -242,14 +243,90 @@ class HeadSubsetController:
 # engine
 # ------------------------------------------------------------------------------------------------
 
+class _DeviceArray:
+    """A raw device allocation seen by torch through the CUDA array interface (no copy)."""
+
+    _TYPESTR = {2: "<i2", 4: "<i4"}
+
+    def __init__(self, ptr: int, nbytes: int, itemsize: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes // itemsize,), "typestr":
+                                         self._TYPESTR[itemsize], "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+class PeerBuffer:
+    """A zeroed device buffer on this rank's GPU that every rank of ``group`` maps (CUDA IPC
+    handles exchanged over the group, mappings opened by libheatkv on the current device, peer
+    access enabled): ``ptrs[r]`` is rank r's buffer as seen from this process, ``local`` this
+    rank's buffer as a tensor of ``dtype``. Collective to create; ``close()`` (also collective)
+    unmaps the peers and frees the buffer once no rank uses it any more."""
+
+    def __init__(self, nbytes: int, dtype: torch.dtype, device, group=None):
+        import torch.distributed as dist
+
+        self.lib = _native.load()
+        self.group = group
+        self.device = torch.device(device)
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        ptr = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        with torch.cuda.device(self.device):
+            _native.check(self.lib.heatkv_peer_alloc(int(nbytes), ctypes.byref(ptr), handle),
+                          "peer buffer allocation")
+            got = [None] * world
+            dist.all_gather_object(got, (self.device.index, handle.raw), group=group)
+            self.ptrs, self._opened = [], []
+            for r, (dev_r, raw) in enumerate(got):
+                if r == rank:
+                    self.ptrs.append(ptr.value)
+                    continue
+                if dev_r != self.device.index:
+                    _native.check(self.lib.heatkv_enable_peer_access(int(dev_r)), "peer access")
+                peer = ctypes.c_void_p()
+                _native.check(self.lib.heatkv_peer_open(raw, ctypes.byref(peer)), "peer mapping")
+                self.ptrs.append(peer.value)
+                self._opened.append(peer.value)
+        itemsize = torch.empty(0, dtype=dtype).element_size()
+        self._own = ptr.value
+        raw_view = torch.as_tensor(_DeviceArray(ptr.value, nbytes, itemsize), device=self.device)
+        self.local = raw_view.view(dtype)
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)          # nobody stores into a peer any more
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                _native.check(self.lib.heatkv_peer_close(ctypes.c_void_p(p)), "peer unmapping")
+            dist.barrier(group=self.group)      # every mapping of this buffer is closed
+            self.local = None
+            _native.check(self.lib.heatkv_peer_free(ctypes.c_void_p(self._own)), "peer free")
+        self._own = None
+        self._opened = []
+
+
 class ShardedHotPath:
     """One rank's part of a sharded hot path: its rows x heads of every layer on ``device``, and
-    (with ``gather``) the all-gather + reassembly that gives every rank the full ``[B, Lq, H*D]``
-    output of each attention call."""
+    (with ``gather``) the exchange that gives every rank the full ``[B, Lq, H*D]`` output of each
+    attention call:
+
+    * ``exchange="nccl"``: the rank's block goes to an NCCL all-gather, then
+      ``heatkv_gather_head_shards`` places the gathered blocks;
+    * ``exchange="p2p"``: the attention kernel itself stores each output row into every rank's
+      full output over NVLink (``heatkv_segmented_attention_scatter``; the full outputs are shared
+      through CUDA IPC), then ``heatkv_peer_barrier`` makes the step's rows of every rank visible
+      before anything later runs - no collective library call and no reassembly pass."""
 
     def __init__(self, controller, num_layers: int, num_heads: int, plan: ShardPlan, rank: int,
                  device, k_dtype=torch.bfloat16, v_dtype=torch.bfloat16, head_dim: int = 128,
-                 group=None, gather: Optional[bool] = None, layers: Optional[list] = None):
+                 group=None, gather: Optional[bool] = None, layers: Optional[list] = None,
+                 exchange: str = "nccl"):
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
+        self.exchange = exchange
         self.plan = plan
         self.rank = int(rank)
         self.device = torch.device(device)
@@ -278,6 +355,41 @@ class ShardedHotPath:
             return _native.HEATKV_OK
         return run
 
+    def allocate_full_outputs(self, batch_rows: int, num_heads: int, dtype=torch.bfloat16):
+        """The ``[B, n_t, H * D]`` outputs of every (layer, scale) as views of one flat buffer,
+        ``full[i][t]``, and the flat buffer. With the p2p exchange every rank's buffer is also
+        mapped here (collective: every rank calls this once, in the same order)."""
+        n_tot = sum(self.tokens)
+        per_layer = batch_rows * n_tot * num_heads * self.head_dim
+        total = len(self.local.plans) * per_layer
+        if self.exchange == "p2p":
+            itemsize = torch.empty(0, dtype=dtype).element_size()
+            self._full_buf = PeerBuffer(total * itemsize, dtype, self.device, self.group)
+            flat = self._full_buf.local
+            self._flag_buf = PeerBuffer(self.plan.world * 4, torch.int32, self.device, self.group)
+            self._flag_ptrs = torch.tensor(self._flag_buf.ptrs, dtype=torch.int64,
+                                           device=self.device)
+            self._counter = torch.zeros(1, dtype=torch.int32, device=self.device)
+        else:
+            flat = torch.zeros(total, dtype=dtype, device=self.device)
+        full, off = [], 0
+        for _ in self.local.plans:
+            row = []
+            for n in self.tokens:
+                sz = batch_rows * n * num_heads * self.head_dim
+                row.append(flat[off:off + sz].view(batch_rows, n, num_heads * self.head_dim))
+                off += sz
+            full.append(row)
+        return full, flat
+
+    def close(self) -> None:
+        """Release the peer-shared buffers (collective; after the last step has completed)."""
+        for name in ("_full_buf", "_flag_buf"):
+            buf = getattr(self, name, None)
+            if buf is not None:
+                buf.close()
+                setattr(self, name, None)
+
     def allocate_gather_buffer(self, dtype=torch.bfloat16) -> torch.Tensor:
         """Receive buffer of the all-gather, sized for the largest scale."""
         p = self.plan
@@ -294,6 +406,8 @@ class ShardedHotPath:
         base = self.local.launches(inputs, outputs, **kw)
         if not self.gather:
             return base
+        if self.exchange == "p2p":
+            return self._p2p_launches(base, full_outputs)
         if full_outputs is None or gather_buf is None:
             raise ValueError("gathering needs full_outputs and gather_buf")
         p = self.plan
@@ -322,4 +436,42 @@ class ShardedHotPath:
                 (_native.ptr(full), _native.ptr(recv), dt[full.dtype], p.world, p.rows_per_rank,
                  n, p.heads_per_rank, p.batch, p.num_heads, self.head_dim,
                  _native.ptr(self.row_map), _native.ptr(self.head_maps[layer])), 2.0 * nbytes))
+        return out
+
+    def _p2p_launches(self, base, full_outputs):
+        """Each attention launch becomes a scatter into every rank's full output, followed by
+        the cross-GPU barrier."""
+        if getattr(self, "_full_buf", None) is None:
+            raise ValueError("the p2p exchange needs allocate_full_outputs() first")
+        p = self.plan
+        lib = self.local.lib
+        rows = torch.tensor(p.rows_of(self.rank), dtype=torch.int32, device=self.device)
+        heads = {}
+        out = []
+        for launch in base:
+            if launch.kind != "attention":
+                out.append(launch)
+                continue
+            layer, t = launch.layer, launch.target
+            i = self.plan_index[layer]
+            full = full_outputs[i][t]
+            off = full.data_ptr() - self._full_buf.local.data_ptr()
+            ptrs = torch.tensor([b + off for b in self._full_buf.ptrs], dtype=torch.int64,
+                                device=self.device)
+            if layer not in heads:
+                heads[layer] = torch.tensor(p.heads_of(self.rank, layer), dtype=torch.int32,
+                                            device=self.device)
+            a = launch.args
+            # a: q, sk, sv, st, en, ct, k, v, out, dtq, dtk, dtv, B, H, n, cap, D, S, scale,
+            #    use_exp2, kernel, order, splits, ws, ws_bytes (HotPath.launches)
+            args = (a[0], a[1], a[2], a[3], a[4], a[5], a[6], a[7], _native.ptr(ptrs), p.world,
+                    _native.ptr(rows), _native.ptr(heads[layer]), p.batch, p.num_heads,
+                    a[9], a[10], a[11], a[12], a[13], a[14], a[15], a[16], a[17], a[18], a[21])
+            scatter = Launch("attention", layer, t, lib.heatkv_segmented_attention_scatter, args,
+                             launch.work)
+            scatter.keep = (ptrs, rows, heads[layer])
+            out.append(scatter)
+            out.append(Launch("barrier", layer, t, lib.heatkv_peer_barrier,
+                              (_native.ptr(self._flag_ptrs), _native.ptr(self._counter), p.world,
+                               self.rank), 0.0))
         return out

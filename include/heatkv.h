@@ -167,6 +167,59 @@ int heatkv_segmented_attention_ws(const void* q, const void* slab_k, const void*
                                   void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * heatkv_segmented_attention_scatter - the attention of one GPU's share of a (batch row x head)
+ * sharded call, storing every output row straight into n_out full output tensors - typically every
+ * rank's copy, through peer (NVLink) pointers - instead of a local block that an all-gather would
+ * then have to move and reorder. No counterpart in the reference, which runs on one GPU.
+ *   out_ptrs        : device array of n_out (1..64) base pointers of [out_batch, q_len,
+ *                     out_heads_total * head_dim] tensors in q's dtype (local or peer memory)
+ *   out_rows        : int32 [batch] device array, the full-output row of each local batch row
+ *   out_heads       : int32 [heads] device array, the full-output head of each local head
+ * Other arguments as heatkv_segmented_attention_ws, always on the tcgen05 kernel unsplit (q, k, v
+ * all bf16 or all f16). A mapped row or head outside the full output is skipped and raises
+ * HEATKV_DEVICE_GATHER_OUT_OF_RANGE. The stores are complete and visible system-wide when the
+ * kernel completes; readers on other GPUs must still synchronise with it (heatkv_peer_barrier).
+ */
+int heatkv_segmented_attention_scatter(
+    const void* q, const void* slab_k, const void* slab_v, const int32_t* seg_starts,
+    const int32_t* seg_ends, const int32_t* seg_counts, const void* cur_k, const void* cur_v,
+    void* const* out_ptrs, int n_out, const int32_t* out_rows, const int32_t* out_heads,
+    int64_t out_batch, int64_t out_heads_total, int q_dtype, int k_dtype, int v_dtype,
+    int64_t batch, int64_t heads, int64_t q_len, int64_t capacity, int64_t head_dim,
+    int64_t max_segments, float softmax_scale, const int32_t* head_order, void* stream);
+
+/*
+ * heatkv_peer_barrier - one step of a barrier across the `world` GPUs of a sharded call, run by
+ * every rank on its own GPU after its scatter. flag_ptrs: device array of `world` pointers, entry i
+ * being rank i's array of `world` uint32 flags (peer-accessible memory, zero before the first step);
+ * counter: a uint32 in this GPU's memory (zero before the first step), advanced by one per call.
+ * The kernel publishes this rank's step into every rank's array and waits until every rank's step
+ * has arrived in its own; afterwards every peer's rows stored before its barrier are visible here.
+ * The wait is bounded (~2 s): on expiry HEATKV_DEVICE_WAIT_TIMEOUT is raised and it returns.
+ * Every rank must call it the same number of times. No counterpart in the reference.
+ */
+int heatkv_peer_barrier(uint32_t* const* flag_ptrs, uint32_t* counter, int world, int rank,
+                        void* stream);
+
+/*
+ * Device memory shared between the processes of one node (one process per GPU), for the
+ * peer-to-peer exchange of a sharded call. No counterpart in the reference.
+ *   heatkv_peer_alloc         : cudaMalloc `bytes` on the current device, zero them, and write the
+ *                               64-byte CUDA IPC handle of the allocation to `handle`.
+ *   heatkv_peer_open          : map another process's allocation (its handle) into this process for
+ *                               kernels on the current device (peer access is enabled for it).
+ *   heatkv_peer_close         : unmap a pointer returned by heatkv_peer_open.
+ *   heatkv_peer_free          : free a pointer returned by heatkv_peer_alloc (after every peer has
+ *                               closed its mapping).
+ *   heatkv_enable_peer_access : let kernels on the current device access `peer_device`'s memory.
+ */
+int heatkv_peer_alloc(size_t bytes, void** ptr, void* handle);
+int heatkv_peer_open(const void* handle, void** ptr);
+int heatkv_peer_close(void* ptr);
+int heatkv_peer_free(void* ptr);
+int heatkv_enable_peer_access(int peer_device);
+
+/*
  * heatkv_attention_workspace_bytes - scratch bytes heatkv_segmented_attention_ws needs for these
  * sizes and kv_splits (0 = the automatic choice); 0 when no scratch is needed.
  */

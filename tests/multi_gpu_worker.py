@@ -23,6 +23,7 @@ from heatkv_b200.hotpath import HotPath, allocate_io  # noqa: E402
 
 def main() -> int:
     split = sys.argv[1] if len(sys.argv) > 1 else "heads"
+    exchange = sys.argv[2] if len(sys.argv) > 2 else "nccl"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
@@ -36,7 +37,8 @@ def main() -> int:
         inputs, ref_out, _, _ = allocate_io(full, seed=11)       # identical on every rank
         HotPath.run(full.launches(inputs, ref_out))
         plan = sharding.plan_shards(sharding.head_costs(ctrl, L, H), batch, world, split=split)
-        sh = sharding.ShardedHotPath(ctrl, L, H, plan, rank, dev, gather=True, layers=layers)
+        sh = sharding.ShardedHotPath(ctrl, L, H, plan, rank, dev, gather=True, layers=layers,
+                                     exchange=exchange)
         rows = plan.rows_of(rank)
         li, lo, fo = [], [], []
         for i, layer in enumerate(layers):
@@ -45,8 +47,12 @@ def main() -> int:
                              for x in inputs[i][t]) for t in range(full.num_scales)])
             lo.append([torch.empty(plan.rows_per_rank, n, plan.heads_per_rank * 128, device=dev,
                                    dtype=torch.bfloat16) for n in full.tokens])
-            fo.append([torch.full_like(ref_out[i][t], float("nan"))
-                       for t in range(full.num_scales)])
+        fo, _flat = sh.allocate_full_outputs(batch, H)
+        for row in fo:
+            for x in row:
+                x.fill_(float("nan"))
+        torch.cuda.synchronize(dev)
+        dist.barrier()   # peers store into this rank's outputs: fill them before anyone runs
         launches = sh.launches(li, lo, fo, sh.allocate_gather_buffer())
         stream = torch.cuda.Stream(dev)
         stream.wait_stream(torch.cuda.current_stream(dev))   # the inputs were made on it
@@ -69,6 +75,8 @@ def main() -> int:
         for row in fo:
             for x in row:
                 x.fill_(float("nan"))
+        torch.cuda.synchronize(dev)
+        dist.barrier()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             HotPath.run(launches, stream)
@@ -77,6 +85,7 @@ def main() -> int:
         ok = check("graph") and ok
         del g
         torch.cuda.synchronize(dev)
+        dist.barrier()   # no rank unmaps its peers' outputs while another still writes
         flags = _native.device_status(dev)
         if flags:
             print(f"rank {rank}: device flags {flags:#x}", flush=True)
@@ -84,9 +93,11 @@ def main() -> int:
         res = torch.tensor([0 if ok else 1], device=dev)
         dist.all_reduce(res)
         ok = res.item() == 0
+        sh.close()
         if rank == 0:
             print(f"multi-GPU parity {'ok' if ok else 'FAILED'}: world {world}, split {split}, "
-                  f"rows x heads groups {plan.row_groups} x {plan.head_groups}", flush=True)
+                  f"exchange {exchange}, rows x heads groups {plan.row_groups} x "
+                  f"{plan.head_groups}", flush=True)
     finally:
         dist.destroy_process_group()
     return 0 if ok else 1

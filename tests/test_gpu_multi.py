@@ -1,7 +1,8 @@
-"""Multi-GPU parity of the sharded hot path over NCCL (skipped with fewer than two GPUs).
+"""Multi-GPU parity of the sharded hot path (skipped with fewer than two GPUs): the NCCL
+all-gather exchange and the peer-to-peer scatter + barrier exchange.
 
 Runs ``multi_gpu_worker.py`` as one process per GPU under torchrun and requires every rank's
-gathered outputs to equal the single-GPU engine's, eagerly and under CUDA-graph replay.
+full outputs to equal the single-GPU engine's, eagerly and under CUDA-graph replay.
 """
 
 import os
@@ -21,14 +22,19 @@ def _gpus():
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("split", ["heads", "auto"])
-def test_sharded_hot_path_over_nccl(split):
+@pytest.mark.parametrize("split,exchange", [("heads", "nccl"), ("auto", "nccl"),
+                                            ("heads", "p2p"), ("auto", "p2p")])
+def test_sharded_hot_path_across_gpus(split, exchange):
     n = 2
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", f"--nproc-per-node={n}", "--master-addr=127.0.0.1", "--master-port=29561",
-           os.path.join(HERE, "multi_gpu_worker.py"), split]
+           os.path.join(HERE, "multi_gpu_worker.py"), split, exchange]
     res = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    log = os.environ.get("HEATKV_MULTI_GPU_LOG")
+    if log:
+        with open(f"{log}.{split}.{exchange}", "w") as fh:
+            fh.write(res.stdout + res.stderr)
     tail = (res.stdout + res.stderr)[-3000:]
     assert res.returncode == 0, tail
     assert "multi-GPU parity ok" in res.stdout, tail

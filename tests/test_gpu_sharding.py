@@ -6,6 +6,8 @@ The all-gather between ranks is emulated here by concatenating the rank blocks i
 ``test_gpu_multi.py`` when two GPUs are present.
 """
 
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -111,4 +113,51 @@ def test_sharded_ranks_reassemble_the_single_gpu_outputs(world, split):
             torch.cuda.synchronize()
             # the same (row, head) units with the same keys in the same order: identical bits
             assert torch.equal(got, outputs[i][t]), (layer, t)
+    assert _native.device_status(dev) == 0
+
+
+def test_scatter_attention_places_rows_in_every_destination():
+    """heatkv_segmented_attention_scatter: the heads of one call split over two emulated ranks,
+    each storing its rows into two full outputs (both on this GPU), equals the unsharded call."""
+    dev = torch.device("cuda", 0)
+    lib = _native.load()
+    B, H, L, cap, S = 2, 16, 600, 5000, 8
+    rng = np.random.default_rng(17)
+    gen = torch.Generator().manual_seed(17)
+    q, k, v = (torch.randn(B, H, L, 128, generator=gen).bfloat16().to(dev) for _ in range(3))
+    pk, pv = (torch.randn(B, cap, 128, generator=gen).bfloat16().to(dev) for _ in range(2))
+    st = np.zeros((H, S), np.int32)
+    en = np.zeros((H, S), np.int32)
+    ct = rng.integers(0, S + 1, size=H).astype(np.int32)
+    for h in range(H):
+        for i in range(ct[h]):
+            n = int(rng.choice([1, 4, 64, 130, 576]))
+            s0 = int(rng.integers(0, cap - n + 1))
+            st[h, i], en[h, i] = s0, s0 + n
+    scale = ctypes.c_float(128 ** -0.5)
+    ref = torch.empty(B, L, H * 128, dtype=torch.bfloat16, device=dev)
+    meta = [torch.from_numpy(x).to(dev) for x in (st, en, ct)]
+    _native.check(lib.heatkv_segmented_attention(
+        _native.ptr(q), _native.ptr(pk), _native.ptr(pv), *[_native.ptr(m) for m in meta],
+        _native.ptr(k), _native.ptr(v), _native.ptr(ref), DT[q.dtype], DT[k.dtype], DT[v.dtype],
+        B, H, L, cap, 128, S, scale, 0, _native.ATTN_TCGEN05,
+        _native.stream_handle(dev)), "reference call")
+    dests = [torch.full_like(ref, float("nan")) for _ in range(2)]
+    ptrs = torch.tensor([d.data_ptr() for d in dests], dtype=torch.int64, device=dev)
+    rows = torch.arange(B, dtype=torch.int32, device=dev)
+    groups = [sorted(rng.permutation(H)[:H // 2].tolist())]
+    groups.append(sorted(set(range(H)) - set(groups[0])))
+    for hs in groups:
+        idx = torch.tensor(hs, device=dev)
+        qs, ks, vs = (x.index_select(1, idx).contiguous() for x in (q, k, v))
+        ms = [m.index_select(0, idx).contiguous() for m in meta]
+        heads = torch.tensor(hs, dtype=torch.int32, device=dev)
+        _native.check(lib.heatkv_segmented_attention_scatter(
+            _native.ptr(qs), _native.ptr(pk), _native.ptr(pv), *[_native.ptr(m) for m in ms],
+            _native.ptr(ks), _native.ptr(vs), _native.ptr(ptrs), 2, _native.ptr(rows),
+            _native.ptr(heads), B, H, DT[q.dtype], DT[k.dtype], DT[v.dtype], B, len(hs), L, cap,
+            128, S, scale, None, _native.stream_handle(dev)), "scatter call")
+    torch.cuda.synchronize()
+    for d in dests:
+        assert torch.equal(d, ref)
     assert _native.device_status(dev) == 0
