@@ -27,6 +27,7 @@ struct AttnArgs {
   float scale;
   const int32_t* head_order = nullptr;  // [heads] permutation, longest first; null = natural
   int kv_splits = 1;                    // key-range splits per query block; 0 = automatic
+  int64_t unsplit_blocks = 0;           // with kv_splits > 1: leading blocks left unsplit
   void* workspace = nullptr;            // split partials and counters (zeroed before first use)
   size_t workspace_bytes = 0;
   unsigned int* status = nullptr;       // device status word (device_status_ptr())

@@ -107,8 +107,9 @@ struct Params {
   unsigned int* status;       // device status word
   float scale_log2;           // softmax_scale * log2(e)
   int qpairs;                 // query blocks per (b, h): ceil(Lq / 256)
-  int splits;                 // key-range splits per query block
-  int n_items;                // heads * batch * qpairs * splits
+  int splits;                 // key-range splits of each split query block
+  int unsplit;                // leading query blocks (schedule order) that are not split
+  int n_items;                // unsplit + (heads * batch * qpairs - unsplit) * splits
   int seg_stride;             // segment-table row length (max_segments)
   // scatter epilogue (n_out > 0): every output row goes to n_out full [out_batch, Lq,
   // out_heads_total * D] tensors (e.g. every rank's copy, over NVLink) at row out_rows[b] and head
@@ -123,14 +124,24 @@ struct Params {
 
 struct Item {
   int h, b, qp, split, block;  // block = (rank * batch + b) * qpairs + qp
+  int nsplit, sblock;          // splits of this block (1 = unsplit), index among split blocks
   int q0, nq;                  // first query row, Q tiles (1 or 2)
   int j0, n;                   // first key tile of the split, number of key tiles
 };
 
 __device__ __forceinline__ Item decode_item(const Smem& sm, const Params& p, int item) {
   Item it;
-  it.split = item % p.splits;
-  it.block = item / p.splits;
+  if (item < p.unsplit) {
+    it.block = item;
+    it.split = 0;
+    it.nsplit = 1;
+  } else {
+    const int k = item - p.unsplit;
+    it.block = p.unsplit + k / p.splits;
+    it.split = k % p.splits;
+    it.nsplit = p.splits;
+  }
+  it.sblock = it.block - p.unsplit;
   it.qp = it.block % p.qpairs;
   const int rb = it.block / p.qpairs;
   it.b = rb % static_cast<int>(p.batch);
@@ -139,8 +150,8 @@ __device__ __forceinline__ Item decode_item(const Smem& sm, const Params& p, int
   it.q0 = it.qp * (kNQ * kBM);
   it.nq = (static_cast<int>(p.q_len) - it.q0) > kBM ? 2 : 1;
   const int tiles = sm.head_tiles[it.h];
-  it.j0 = static_cast<int>((int64_t(tiles) * it.split) / p.splits);
-  it.n = static_cast<int>((int64_t(tiles) * (it.split + 1)) / p.splits) - it.j0;
+  it.j0 = static_cast<int>((int64_t(tiles) * it.split) / it.nsplit);
+  it.n = static_cast<int>((int64_t(tiles) * (it.split + 1)) / it.nsplit) - it.j0;
   return it;
 }
 
@@ -736,7 +747,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool have_o = active && ok;
       if (have_o) tc_fence_after();
       const int qrow = it.q0 + t * kBM + row;
-      if (p.splits == 1) {
+      if (it.nsplit == 1) {
         if (have_o) {
           const float inv = 1.f / l_run;
           int64_t off = ((int64_t(it.b) * p.q_len + qrow) * p.heads + it.h) * kD;
@@ -771,7 +782,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
         // partial result of this split: (m, l) and the unnormalised O row
-        const int64_t slot = (int64_t(it.block) * p.splits + it.split) * (kNQ * kBM) + t * kBM + row;
+        const int64_t slot = (int64_t(it.sblock) * it.nsplit + it.split) * (kNQ * kBM) + t * kBM + row;
         if (have_o) {
           float4* dst = reinterpret_cast<float4*>(p.ws_o + slot * kD);
 #pragma unroll 1
@@ -797,10 +808,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar_softmax();
         if (threadIdx.x == 0) {
           __threadfence();
-          const unsigned old = atomicAdd(p.ws_counter + it.block, 1u);
-          const int last = (old == static_cast<unsigned>(p.splits - 1)) ? 1 : 0;
+          const unsigned old = atomicAdd(p.ws_counter + it.sblock, 1u);
+          const int last = (old == static_cast<unsigned>(it.nsplit - 1)) ? 1 : 0;
           if (last) {
-            p.ws_counter[it.block] = 0;  // every split has arrived: reset for the next call
+            p.ws_counter[it.sblock] = 0;  // every split has arrived: reset for the next call
             __threadfence();
           }
           sm.last_flag = last;
@@ -808,12 +819,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar_softmax();
         if (sm.last_flag && t < it.nq && qrow < Lq) {
           // merge the splits of this row: O = sum_k 2^(m_k - M) O_k / sum_k 2^(m_k - M) l_k
-          const int64_t base = int64_t(it.block) * p.splits * (kNQ * kBM) + t * kBM + row;
+          const int64_t base = int64_t(it.sblock) * it.nsplit * (kNQ * kBM) + t * kBM + row;
           float2 ml[kMaxSplits];
           float M = -INFINITY;
 #pragma unroll
           for (int k = 0; k < kMaxSplits; ++k) {
-            ml[k] = k < p.splits ? __ldcg(p.ws_ml + base + int64_t(k) * (kNQ * kBM))
+            ml[k] = k < it.nsplit ? __ldcg(p.ws_ml + base + int64_t(k) * (kNQ * kBM))
                                  : make_float2(-INFINITY, 0.f);
             if (ml[k].y > 0.f) M = fmaxf(M, ml[k].x);
           }
@@ -859,7 +870,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (p.splits == 1 && have_o) {
+      if (it.nsplit == 1 && have_o) {
         // O_t has been read: the MMA may start the next item's first PV into it
         tc_fence_before();
         __syncwarp();
@@ -980,13 +991,17 @@ cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st
   int splits = a.kv_splits <= 0 ? attention_auto_splits(a.batch, a.heads, a.q_len) : a.kv_splits;
   if (splits > kMaxSplits) splits = kMaxSplits;
   if (blocks > kMaxCounterBlocks) splits = 1;
-  WsLayout wl = ws_layout(blocks, splits);
+  int64_t unsplit = splits > 1 ? std::min<int64_t>(std::max<int64_t>(a.unsplit_blocks, 0), blocks)
+                               : blocks;
+  if (unsplit == blocks) splits = 1;
+  WsLayout wl = ws_layout(blocks - unsplit, splits);
   if (splits > 1 && (a.workspace == nullptr || a.workspace_bytes < wl.total ||
                      (reinterpret_cast<uintptr_t>(a.workspace) & 255u))) {
     splits = 1;  // no (or too small) workspace: run unsplit
-    wl = ws_layout(blocks, 1);
+    unsplit = blocks;
+    wl = ws_layout(0, 1);
   }
-  const int64_t n_items = blocks * splits;
+  const int64_t n_items = unsplit + (blocks - unsplit) * splits;
   if (n_items >= (int64_t(1) << 31)) return cudaErrorNotSupported;
   CUtensorMap tq, tck, tcv, tsk, tsv;
   const void* sk = a.capacity > 0 ? a.slab_k : a.cur_k;
@@ -1022,6 +1037,7 @@ cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.qpairs = qpairs;
   p.splits = splits;
+  p.unsplit = static_cast<int>(unsplit);
   p.n_items = static_cast<int>(n_items);
   p.seg_stride = static_cast<int>(std::max<int64_t>(a.max_segments, 1));
   const int smem = static_cast<int>(sizeof(Smem)) + 1024;

@@ -144,7 +144,7 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
                           int64_t q_len, int64_t capacity, int64_t head_dim, int64_t max_segments,
                           float softmax_scale, int kernel, const int32_t* head_order,
                           int kv_splits, void* workspace, size_t workspace_bytes, void* stream,
-                          const Scatter* scatter = nullptr) {
+                          const Scatter* scatter = nullptr, int64_t unsplit_blocks = 0) {
   g_last_error.clear();
   if (!valid_dtype(q_dtype) || !valid_dtype(k_dtype) || !valid_dtype(v_dtype))
     return fail(HEATKV_ERR_UNSUPPORTED,
@@ -174,6 +174,7 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
                      softmax_scale};
   a.head_order = head_order;
   a.kv_splits = kv_splits;
+  a.unsplit_blocks = unsplit_blocks;
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;
   a.status = heatkv::device_status_ptr();
@@ -335,6 +336,31 @@ int heatkv_enable_peer_access(int peer_device) {
   }
   if (e != cudaSuccess) return cuda_fail(e, "heatkv_enable_peer_access");
   return HEATKV_OK;
+}
+
+int heatkv_segmented_attention_sched(const void* q, const void* slab_k, const void* slab_v,
+                                     const int32_t* seg_starts, const int32_t* seg_ends,
+                                     const int32_t* seg_counts, const void* cur_k,
+                                     const void* cur_v, void* out, int q_dtype, int k_dtype,
+                                     int v_dtype, int64_t batch, int64_t heads, int64_t q_len,
+                                     int64_t capacity, int64_t head_dim, int64_t max_segments,
+                                     float softmax_scale, int kernel, const int32_t* head_order,
+                                     int kv_splits, int64_t unsplit_blocks, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  if (kv_splits < 1 || unsplit_blocks < 0)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT,
+                "heatkv_segmented_attention_sched: kv_splits >= 1 and unsplit_blocks >= 0 required");
+  if (kv_splits != 1 && workspace != nullptr) {
+    const size_t need = heatkv::attention_workspace_bytes(batch, heads, q_len, kv_splits);
+    if (workspace_bytes < need)
+      return fail(HEATKV_ERR_INVALID_ARGUMENT,
+                  "heatkv_segmented_attention_sched: workspace of %zu bytes, %zu needed",
+                  workspace_bytes, need);
+  }
+  return attention_impl(q, slab_k, slab_v, seg_starts, seg_ends, seg_counts, cur_k, cur_v, out,
+                        q_dtype, k_dtype, v_dtype, batch, heads, q_len, capacity, head_dim,
+                        max_segments, softmax_scale, kernel, head_order, kv_splits, workspace,
+                        workspace_bytes, stream, nullptr, unsplit_blocks);
 }
 
 size_t heatkv_attention_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len,

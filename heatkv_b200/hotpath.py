@@ -37,16 +37,27 @@ BLOCK_ROWS = 256   # query rows per block of the tcgen05 kernel (two 128-row til
 KEY_TILE = 128
 
 
+def _makespan(costs: np.ndarray, sms: int) -> float:
+    """Largest per-CTA sum when item i goes to CTA i % grid, grid = min(items, sms)."""
+    grid = min(len(costs), sms)
+    pad = (-len(costs)) % grid
+    return float(np.pad(costs, (0, pad)).reshape(-1, grid).sum(axis=0).max())
+
+
 def plan_attention(slots_per_segment, q_len: int, batch: int, *, sms: int = NUM_SMS,
-                   max_splits: int = 4):
-    """Length-aware schedule of one attention launch: heads longest first and the number of
-    key-range splits per query block that minimises the makespan of the kernel's round-robin
-    assignment of items to at most ``sms`` persistent CTAs.
+                   item_cost: float = 1.5, merge_cost: float = 8.0, min_gain: float = 0.03):
+    """Length-aware schedule of one attention launch: heads longest first, and how many query
+    blocks at the tail of the schedule to split in two key ranges so that the kernel's round-robin
+    assignment of items to at most ``sms`` persistent CTAs fills its last wave.
 
     ``slots_per_segment[h]`` lists the head's segment lengths. Cost model, in units of one
-    128 x 128 query-tile x key-tile step: key tiles x query tiles of the item, plus 2 units per
-    item (Q load, pipeline fill, epilogue) and 1 more per split item (partial write and merge).
-    Returns ``(head_order, splits)``."""
+    128 x 128 query-tile x key-tile step for the block's Q tiles: key tiles x Q tiles of the item,
+    plus ``item_cost`` per item (Q load, pipeline fill, epilogue) and ``merge_cost`` per half of a
+    split block (partial write, merge). The merge cost was calibrated on the 2B bench step: each
+    half writes a 128 KB fp32 partial and the last CTA reads both back, several tile steps of
+    time, so only the long target-12 launches gain from splitting their tail (about 0.3 ms). The blocks are enumerated in the kernel's order (head rank,
+    batch row, query block); a split of the last ``m`` blocks is taken when it lowers the makespan
+    by ``min_gain`` or more. Returns ``(head_order, splits, unsplit_blocks)``."""
     tiles = np.array([sum((int(n) + KEY_TILE - 1) // KEY_TILE for n in segs if n > 0)
                       + (q_len + KEY_TILE - 1) // KEY_TILE for segs in slots_per_segment],
                      dtype=np.int64)
@@ -55,21 +66,24 @@ def plan_attention(slots_per_segment, q_len: int, batch: int, *, sms: int = NUM_
     nq = np.full(qpairs, 2, dtype=np.int64)
     if q_len - (qpairs - 1) * BLOCK_ROWS <= BLOCK_ROWS // 2:
         nq[-1] = 1
-    best = None
-    for splits in range(1, max_splits + 1):
-        s = np.arange(splits)
-        n = tiles[order][:, None]                                     # [H, 1]
-        per_split = (n * (s + 1)) // splits - (n * s) // splits       # [H, S]
-        cost = per_split[:, None, None, :] * nq[None, None, :, None]  # [H, 1, Q, S]
-        cost = np.broadcast_to(cost, (len(order), batch, qpairs, splits)).astype(np.float64)
-        cost = cost + 2.0 + (1.0 if splits > 1 else 0.0)
-        flat = cost.reshape(-1)
-        grid = min(len(flat), sms)
-        pad = (-len(flat)) % grid
-        makespan = np.pad(flat, (0, pad)).reshape(-1, grid).sum(axis=0).max()
-        if best is None or makespan < best[0] * 0.97:
-            best = (makespan, splits)
-    return order, best[1]
+    n_head = tiles[order]                                                   # [H]
+    # block costs in kernel order; halves of a split block (the kernel's j0/n rounding)
+    t_blk = np.broadcast_to(n_head[:, None, None], (len(order), batch, qpairs)).reshape(-1)
+    q_blk = np.broadcast_to(nq[None, None, :], (len(order), batch, qpairs)).reshape(-1)
+    whole = (t_blk * q_blk).astype(np.float64) + item_cost
+    first = ((t_blk // 2) * q_blk).astype(np.float64) + item_cost + merge_cost
+    second = ((t_blk - t_blk // 2) * q_blk).astype(np.float64) + item_cost + merge_cost
+    blocks = len(whole)
+    best = (_makespan(whole, sms), blocks)
+    step = max(1, min(blocks, 2 * sms) // 64)
+    for m in range(step, min(blocks, 2 * sms) + 1, step):
+        u = blocks - m
+        halves = np.stack([first[u:], second[u:]], axis=1).reshape(-1)
+        span = _makespan(np.concatenate([whole[:u], halves]), sms)
+        if span < best[0] * (1.0 - min_gain):
+            best = (span, u)
+    unsplit = best[1]
+    return order, (2 if unsplit < blocks else 1), unsplit
 
 
 # heatkv_pack_job of include/heatkv.h
@@ -209,16 +223,20 @@ class HotPath:
         self.schedule = {}
         ws_bytes = 0
         import os
-        forced = int(os.environ.get("HEATKV_PLAN_SPLITS", "1"))
+        # HEATKV_PLAN_SPLITS: "auto" (tail splits chosen by the planner), or a fixed number of
+        # key-range splits for every block (1 = never split)
+        forced_env = os.environ.get("HEATKV_PLAN_SPLITS", "auto")
+        forced = 0 if forced_env == "auto" else int(forced_env)
         natural = os.environ.get("HEATKV_PLAN_ORDER", "lpt") == "natural"
         for i, p in enumerate(self.plans):
             for t in range(self.num_scales):
-                order, splits = plan_attention(p.segment_lengths(t), self.tokens[t], self.batch)
+                order, splits, unsplit = plan_attention(p.segment_lengths(t), self.tokens[t],
+                                                        self.batch)
                 if forced > 0:
-                    splits = forced
+                    splits, unsplit = forced, 0
                 if natural:
                     order = np.arange(self.num_heads, dtype=np.int32)
-                self.schedule[(i, t)] = (torch.from_numpy(order).to(self.device), splits)
+                self.schedule[(i, t)] = (torch.from_numpy(order).to(self.device), splits, unsplit)
                 ws_bytes = max(ws_bytes, int(self.lib.heatkv_attention_workspace_bytes(
                     self.batch, self.num_heads, self.tokens[t], splits)))
         self.workspace = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=self.device)
@@ -256,14 +274,15 @@ class HotPath:
                     sk, sv = self.slab_k[i], self.slab_v[i]
                     cap = max(p.capacity, 1)
                 flops = float(4 * n * (p.attention_slots(t) + n).sum() * D * B)
-                order, splits = self.schedule[(i, t)]
+                order, splits, unsplit = self.schedule[(i, t)]
                 out.append(Launch(
-                    "attention", p.layer, t, lib.heatkv_segmented_attention_ws,
+                    "attention", p.layer, t, lib.heatkv_segmented_attention_sched,
                     (_native.ptr(q), _native.ptr(sk), _native.ptr(sv), _native.ptr(st),
                      _native.ptr(en), _native.ptr(ct), _native.ptr(k), _native.ptr(v),
                      _native.ptr(o), dt[q.dtype], dt[k.dtype], dt[v.dtype], B, H, n, cap, D,
-                     int(st.shape[1]), ctypes.c_float(scale), 0, kernel, _native.ptr(order),
-                     int(splits), _native.ptr(self.workspace), self.workspace.numel()), flops))
+                     int(st.shape[1]), ctypes.c_float(scale), kernel, _native.ptr(order),
+                     int(splits), int(unsplit), _native.ptr(self.workspace),
+                     self.workspace.numel()), flops))
                 row_k = D * k.element_size()
                 row_v = D * v.element_size()
                 jobs = []

@@ -463,10 +463,11 @@ class ShardedHotPath:
                                             device=self.device)
             a = launch.args
             # a: q, sk, sv, st, en, ct, k, v, out, dtq, dtk, dtv, B, H, n, cap, D, S, scale,
-            #    use_exp2, kernel, order, splits, ws, ws_bytes (HotPath.launches)
+            #    kernel, order, splits, unsplit, ws, ws_bytes (HotPath.launches); the scatter
+            #    runs unsplit
             args = (a[0], a[1], a[2], a[3], a[4], a[5], a[6], a[7], _native.ptr(ptrs), p.world,
                     _native.ptr(rows), _native.ptr(heads[layer]), p.batch, p.num_heads,
-                    a[9], a[10], a[11], a[12], a[13], a[14], a[15], a[16], a[17], a[18], a[21])
+                    a[9], a[10], a[11], a[12], a[13], a[14], a[15], a[16], a[17], a[18], a[20])
             scatter = Launch("attention", layer, t, lib.heatkv_segmented_attention_scatter, args,
                              launch.work)
             scatter.keep = (ptrs, rows, heads[layer])

@@ -220,6 +220,26 @@ int heatkv_peer_free(void* ptr);
 int heatkv_enable_peer_access(int peer_device);
 
 /*
+ * heatkv_segmented_attention_sched - heatkv_segmented_attention_ws with the split applied to the
+ * tail of the schedule only: the first `unsplit_blocks` query blocks of the schedule order (head
+ * rank major, then batch row, then 256-row query block) run whole, every later block is divided
+ * into kv_splits (>= 1) key ranges that different CTAs process and the last one merges. A planner
+ * that knows the key tiles of every head chooses unsplit_blocks so that the last wave of blocks
+ * over the SMs is filled with half-size work instead of leaving SMs idle. The workspace needs at
+ * most heatkv_attention_workspace_bytes(batch, heads, q_len, kv_splits). No reference
+ * counterpart (the reference's Triton grid has no scheduler).
+ */
+int heatkv_segmented_attention_sched(const void* q, const void* slab_k, const void* slab_v,
+                                     const int32_t* seg_starts, const int32_t* seg_ends,
+                                     const int32_t* seg_counts, const void* cur_k,
+                                     const void* cur_v, void* out, int q_dtype, int k_dtype,
+                                     int v_dtype, int64_t batch, int64_t heads, int64_t q_len,
+                                     int64_t capacity, int64_t head_dim, int64_t max_segments,
+                                     float softmax_scale, int kernel, const int32_t* head_order,
+                                     int kv_splits, int64_t unsplit_blocks, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
+/*
  * heatkv_attention_workspace_bytes - scratch bytes heatkv_segmented_attention_ws needs for these
  * sizes and kv_splits (0 = the automatic choice); 0 when no scratch is needed.
  */

@@ -337,6 +337,54 @@ def test_tcgen05_split_kv_and_head_order(splits, B, H, L, cap, S, cuda_device):
     assert _native.device_status(d) == 0
 
 
+@pytest.mark.parametrize("B,H,L,cap,S,splits", [(2, 16, 1600, 5000, 12, 2), (2, 4, 576, 3000, 10, 2),
+                                                (1, 8, 4096, 2000, 6, 3)])
+def test_tcgen05_tail_split_schedule(B, H, L, cap, S, splits, cuda_device):
+    """heatkv_segmented_attention_sched: only the blocks after the first `unsplit` (schedule
+    order) are split; every choice of unsplit gives the reference's result, and the unsplit
+    blocks are bit-identical to an unsplit launch."""
+    import ctypes
+    rng = np.random.default_rng(L + H)
+    gen = torch.Generator().manual_seed(L + 3)
+    d = cuda_device
+    q, ck, cv = (torch.randn(B, H, L, 128, generator=gen).bfloat16().to(d) for _ in range(3))
+    pk, pv = (torch.randn(B, cap, 128, generator=gen).bfloat16().to(d) for _ in range(2))
+    st, en, ct = _random_layout(rng, H, S, cap)
+    st, en, ct = st.to(d), en.to(d), ct.to(d)
+    order = torch.from_numpy(rng.permutation(H).astype(np.int32)).to(d)
+    lib = _native.load()
+    nbytes = int(lib.heatkv_attention_workspace_bytes(B, H, L, splits))
+    ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=d)
+    scale = 1.0 / math.sqrt(128)
+    ref = _torch_reference(q, pk, pv, st.cpu(), en.cpu(), ct.cpu(), ck, cv, scale)
+    whole = _attention_ws(q, pk, pv, st, en, ct, ck, cv, scale, head_order=order, splits=1,
+                          workspace=None)
+    qpairs = (L + 255) // 256
+    blocks = B * H * qpairs
+    dt = _native.DTYPE_CODES
+    for unsplit in (0, 1, blocks // 2, blocks - 3, blocks):
+        out = torch.full((B, L, H * 128), float("nan"), dtype=q.dtype, device=d)
+        status = lib.heatkv_segmented_attention_sched(
+            _native.ptr(q), _native.ptr(pk), _native.ptr(pv), _native.ptr(st), _native.ptr(en),
+            _native.ptr(ct), _native.ptr(ck), _native.ptr(cv), _native.ptr(out), dt[q.dtype],
+            dt[ck.dtype], dt[cv.dtype], B, H, L, cap, 128, S, ctypes.c_float(scale),
+            _native.ATTN_TCGEN05, _native.ptr(order), splits, unsplit, _native.ptr(ws),
+            ws.numel(), _native.stream_handle(d))
+        _native.check(status, "heatkv_segmented_attention_sched")
+        torch.cuda.synchronize()
+        _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
+        # blocks [0, unsplit) in schedule order = (head rank, row, query block): same bits
+        for blk in range(unsplit):
+            rank, qp = divmod(blk, qpairs)
+            rank, b = divmod(rank, B)
+            h = int(order[rank])
+            rows = slice(qp * 256, min(L, qp * 256 + 256))
+            cols = slice(h * 128, (h + 1) * 128)
+            assert torch.equal(out[b, rows, cols], whole[b, rows, cols]), (unsplit, blk)
+        assert int(ws[: 4 * blocks].count_nonzero()) == 0, "split counters not reset"
+    assert _native.device_status(d) == 0
+
+
 def test_workspace_shared_across_shapes(cuda_device):
     """One workspace serves calls of different shapes in any order (the split counters sit in a
     region no partial result ever overwrites)."""
