@@ -188,9 +188,19 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool same16 = (q_dtype == k_dtype && k_dtype == v_dtype && q_dtype != HEATKV_DTYPE_F32);
-  if (kernel == HEATKV_ATTN_TCGEN05 && !same16)
+  // fp32 q and k with 16-bit v (the real model's dtypes): tf32 QK, P rounded to v's dtype
+  const bool qk32 = (q_dtype == HEATKV_DTYPE_F32 && k_dtype == HEATKV_DTYPE_F32 &&
+                     v_dtype != HEATKV_DTYPE_F32);
+  if (kernel == HEATKV_ATTN_TCGEN05 && !same16 && !(qk32 && !scatter))
     return fail(HEATKV_ERR_UNSUPPORTED,
-                "tcgen05 segmented attention needs q, k and v all bfloat16 or all float16");
+                "tcgen05 segmented attention needs q, k and v all bfloat16 or all float16, or q "
+                "and k float32 with 16-bit v");
+  if (kernel != HEATKV_ATTN_EXACT && qk32 && !scatter) {
+    cudaError_t e = heatkv::launch_attention_sm100_tf32(a, v_dtype == HEATKV_DTYPE_BF16, st);
+    if (e == cudaSuccess) return HEATKV_OK;
+    if (e != cudaErrorNotSupported || kernel == HEATKV_ATTN_TCGEN05)
+      return cuda_fail(e, "tcgen05 tf32 segmented attention launch");
+  }
   if (kernel != HEATKV_ATTN_EXACT && same16) {
     cudaError_t e = heatkv::launch_attention_sm100(a, q_dtype == HEATKV_DTYPE_BF16, st);
     if (e == cudaSuccess) return HEATKV_OK;

@@ -1,6 +1,7 @@
 """Micro-benchmark of one libheatkv kernel shape (used for tuning sweeps and ncu captures).
 
     python -m heatkv_b200.kernel_bench attention --rows 2 --heads 16 --q-len 4096 --slots 650
+    python -m heatkv_b200.kernel_bench attention --dtype f32qk   # fp32 q/k, bf16 v (tf32 kernel)
     python -m heatkv_b200.kernel_bench pack --rows 2 --heads 16 --q-len 4096
 
 ``attention``: one call shaped like a fused target of the 2B model - per head six slab segments
@@ -23,12 +24,17 @@ from .real_pruning_fused_attention import (fused_real_pruning_flat_segmented_att
                                            pack_flat_segments_kv)
 
 
-def attention_case(rows, heads, q_len, slots, dtype=torch.bfloat16, device="cuda", seed=0):
+def attention_case(rows, heads, q_len, slots, dtype=torch.bfloat16, device="cuda", seed=0,
+                   vdtype=None):
+    """Inputs of one attention call; q, k and the K slab in ``dtype``, v and the V slab in
+    ``vdtype`` (default ``dtype``)."""
+    vdtype = dtype if vdtype is None else vdtype
     g = torch.Generator(device=device).manual_seed(seed)
-    q, k, v = (torch.randn(rows, heads, q_len, 128, device=device, generator=g).to(dtype)
-               for _ in range(3))
+    q, k, v = (torch.randn(rows, heads, q_len, 128, device=device, generator=g).to(dt)
+               for dt in (dtype, dtype, vdtype))
     cap = heads * slots
-    pk, pv = (torch.randn(rows, cap, 128, device=device, generator=g).to(dtype) for _ in range(2))
+    pk, pv = (torch.randn(rows, cap, 128, device=device, generator=g).to(dt)
+              for dt in (dtype, vdtype))
     lens = [n for n in (1, 4, 16, 36, 64) if n <= slots]
     while sum(lens) > slots:
         lens.pop()
@@ -71,11 +77,15 @@ def main(argv=None):
     ap.add_argument("--slots", type=int, default=650)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--dtype", choices=["bf16", "f16", "f32"], default="bf16")
+    ap.add_argument("--dtype", choices=["bf16", "f16", "f32", "f32qk"], default="bf16",
+                    help="f32qk: fp32 q/k with bf16 v, the real model's cos-attention dtypes")
     args = ap.parse_args(argv)
-    dtype = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[args.dtype]
+    dtype = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32,
+             "f32qk": torch.float32}[args.dtype]
     if args.kernel == "attention":
-        kw, flops = attention_case(args.rows, args.heads, args.q_len, args.slots, dtype)
+        vdtype = torch.bfloat16 if args.dtype == "f32qk" else dtype
+        kw, flops = attention_case(args.rows, args.heads, args.q_len, args.slots, dtype,
+                                   vdtype=vdtype)
         ms = time_call(lambda: fused_real_pruning_flat_segmented_attention(**kw), args.iters,
                        args.warmup)
         print(f"attention rows={args.rows} heads={args.heads} q_len={args.q_len} "

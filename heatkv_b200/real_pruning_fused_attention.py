@@ -13,11 +13,14 @@ with no host synchronisation. There is no Triton and no CPU fallback: CPU tensor
 ``RuntimeError``.
 
 Environment knobs of the reference: ``REAL_PRUNING_FUSED_QK_DOT_MODE`` /
-``REAL_PRUNING_FUSED_VALUE_DOT_MODE`` are validated the same way; ``fp32``/``ieee`` (and ``tf32``)
-select the exact CUDA-core kernel (fp32 products), the default ``bf16`` selects the tcgen05
-tensor-core kernel for all-bf16/all-fp16 inputs. ``REAL_PRUNING_FUSED_BLOCK_M/_N/_NUM_WARPS/
-_NUM_STAGES`` tune the Triton kernel and have no meaning here. ``HEATKV_ATTENTION_KERNEL`` =
-``auto|exact|tcgen05`` forces a kernel.
+``REAL_PRUNING_FUSED_VALUE_DOT_MODE`` are validated the same way. The default ``bf16`` modes (and
+``tf32`` for QK) select a tcgen05 tensor-core kernel with the reference's precision: all-bf16 or
+all-fp16 inputs, or fp32 q/k with bf16/fp16 v (the real model's cos-attention dtypes), where the
+scores are tf32 products as ``tl.dot`` makes them on fp32 operands and P is rounded to v's dtype;
+``fp32``/``ieee`` in either knob, and every other dtype combination, select the exact CUDA-core
+kernel (fp32 products). ``REAL_PRUNING_FUSED_BLOCK_M/_N/_NUM_WARPS/_NUM_STAGES`` tune the Triton
+kernel and have no meaning here. ``HEATKV_ATTENTION_KERNEL`` = ``auto|exact|tcgen05`` forces a
+kernel.
 """
 
 from __future__ import annotations
@@ -63,7 +66,7 @@ def _kernel_selector() -> int:
             return _KERNEL_NAMES[forced.strip().lower()]
         except KeyError:
             raise ValueError("HEATKV_ATTENTION_KERNEL must be one of: auto, exact, tcgen05") from None
-    if _fused_qk_dot_mode_id() != 0 or _fused_value_dot_mode_id() != 0:
+    if _fused_qk_dot_mode_id() == 2 or _fused_value_dot_mode_id() == 2:
         return _native.ATTN_EXACT
     return _native.ATTN_AUTO
 

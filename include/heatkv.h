@@ -54,9 +54,11 @@ typedef enum {
 
 /* Attention kernel selection for heatkv_segmented_attention. */
 typedef enum {
-  HEATKV_ATTN_AUTO = 0,   /* tensor-core kernel when q/k/v are all bf16 or all f16, else exact */
+  HEATKV_ATTN_AUTO = 0,   /* tensor-core kernel when q/k/v are all bf16 or all f16, or q and k
+                             are f32 with bf16/f16 v (tf32 QK, P in v's dtype), else exact */
   HEATKV_ATTN_EXACT = 1,  /* CUDA-core kernel: fp32 products and accumulation for every dtype */
-  HEATKV_ATTN_TCGEN05 = 2 /* tcgen05/TMEM kernel; requires q/k/v all bf16 or all f16 */
+  HEATKV_ATTN_TCGEN05 = 2 /* tcgen05/TMEM kernel; requires q/k/v all bf16 or all f16, or q and k
+                             f32 with bf16/f16 v */
 } heatkv_attn_kernel;
 
 /* Message describing the last failing call made by this thread ("" if none). */

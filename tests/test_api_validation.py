@@ -58,6 +58,11 @@ def test_bad_dot_mode_env(monkeypatch):
         m._kernel_selector()
     monkeypatch.setenv("REAL_PRUNING_FUSED_QK_DOT_MODE", "fp32")
     assert m._kernel_selector() == m._native.ATTN_EXACT
+    # tf32 scores are what the tensor-core kernels compute on fp32 q/k (and exact on 16-bit ones)
+    monkeypatch.setenv("REAL_PRUNING_FUSED_QK_DOT_MODE", "tf32")
+    assert m._kernel_selector() == m._native.ATTN_AUTO
+    monkeypatch.setenv("REAL_PRUNING_FUSED_VALUE_DOT_MODE", "fp32")
+    assert m._kernel_selector() == m._native.ATTN_EXACT
     monkeypatch.setenv("HEATKV_ATTENTION_KERNEL", "tcgen05")
     assert m._kernel_selector() == m._native.ATTN_TCGEN05
 

@@ -1,9 +1,10 @@
 """GPU parity of the libheatkv kernels (run with ``pytest -m gpu`` on a B200).
 
-Attention: tcgen05 (bf16/fp16) and exact (every dtype) kernels against the float64 CPU oracle on
-the seeded edge cases, against the outputs recorded from the reference itself, and on larger
-random segment layouts against a plain PyTorch fp32 reference on the GPU. Tolerances: bf16/fp16
-max |err| <= 2e-2 and max |err| / max |ref| <= 1e-2; fp32 (exact kernel) 1e-5.
+Attention: tcgen05 (bf16/fp16, and fp32 q/k with 16-bit v through tf32 scores) and exact (every
+dtype) kernels against the float64 CPU oracle on the seeded edge cases, against the outputs
+recorded from the reference itself, and on larger random segment layouts against a plain PyTorch
+fp32 reference on the GPU. Tolerances: bf16/fp16 and tf32 max |err| <= 2e-2 and max |err| /
+max |ref| <= 1e-2; fp32 (exact kernel) 1e-5.
 Pack: bit-exact against the oracle for random descriptors and mixed K/V dtypes; out-of-range
 descriptors are skipped and flagged.
 """
@@ -181,8 +182,10 @@ def test_exact_fp32_random_layouts(L, cap, S, cuda_device, kernel):
     np.testing.assert_allclose(out.cpu().numpy(), ref, atol=FP32_ATOL, rtol=FP32_ATOL)
 
 
-def test_exact_mixed_dtypes_real_model_layout(cuda_device):
-    """q, k fp32 and v bf16: the dtypes of the real model (cos-attn under bf16 autocast)."""
+def test_exact_mixed_dtypes_real_model_layout(cuda_device, kernel):
+    """q, k fp32 and v bf16: the dtypes of the real model (cos-attn under bf16 autocast), on the
+    exact kernel (what REAL_PRUNING_FUSED_QK_DOT_MODE=fp32 selects)."""
+    kernel("exact")
     rng = np.random.default_rng(7)
     gen = torch.Generator().manual_seed(7)
     B, H, L, cap = 2, 4, 100, 600
@@ -199,6 +202,67 @@ def test_exact_mixed_dtypes_real_model_layout(cuda_device):
                current_v=cv.to(d), softmax_scale=0.09)
     assert out.dtype == torch.float32
     np.testing.assert_allclose(out.cpu().numpy(), ref, atol=FP32_ATOL, rtol=FP32_ATOL)
+
+
+@pytest.mark.parametrize("vdtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,H,L,cap,S", [
+    (1, 1, 1, 700, 3), (2, 3, 4, 400, 4), (1, 2, 127, 900, 5), (2, 2, 128, 900, 5),
+    (1, 3, 129, 1200, 6), (2, 2, 255, 800, 4), (2, 1, 257, 1500, 8), (2, 16, 576, 4000, 12),
+    (1, 4, 1024, 3000, 12), (2, 3, 64, 0, 0),
+])
+def test_tcgen05_tf32_mixed_dtypes(vdtype, B, H, L, cap, S, cuda_device, kernel):
+    """fp32 q and k with 16-bit v on the tf32 tcgen05 kernel (the reference's default dot modes on
+    these dtypes: tf32 scores, P rounded to v's dtype); the output is fp32."""
+    kernel("tcgen05")
+    rng = np.random.default_rng(B * 1000 + H * 100 + L + 5)
+    gen = torch.Generator().manual_seed(L + 5)
+    q, ck = (torch.randn(B, H, L, 128, generator=gen).to(cuda_device) for _ in range(2))
+    cv = torch.randn(B, H, L, 128, generator=gen).to(vdtype).to(cuda_device)
+    pk = torch.randn(B, cap, 128, generator=gen).to(cuda_device)
+    pv = torch.randn(B, cap, 128, generator=gen).to(vdtype).to(cuda_device)
+    if cap:
+        st, en, ct = _random_layout(rng, H, S, cap)
+    else:
+        st = en = torch.zeros(H, 0, dtype=torch.int32)
+        ct = torch.zeros(H, dtype=torch.int32)
+    scale = 1.0 / math.sqrt(128)
+    out = attn(q=q, persisted_k=pk if cap else None, persisted_v=pv if cap else None,
+               segment_starts=st.to(cuda_device), segment_ends=en.to(cuda_device),
+               segment_counts=ct.to(cuda_device), current_k=ck, current_v=cv, softmax_scale=scale)
+    assert out.dtype == torch.float32
+    ref = _torch_reference(q, pk, pv, st, en, ct, ck, cv, scale)
+    _check_lowp(out.cpu().numpy(), ref.cpu().numpy())
+    assert _native.device_status(cuda_device) == 0
+
+
+@pytest.mark.parametrize("L", [5, 200, 300])
+def test_tcgen05_tf32_scores_growing_tile_by_tile(L, cuda_device, kernel):
+    """The lazy-rescale path of the tf32 kernel: every key tile's scores far above the previous
+    tiles', both key halves of a tile exchanged between the softmax warpgroups, a partial tile in
+    the middle of a head and query rows past Lq in the last block."""
+    kernel("tcgen05")
+    B, H, S, cap = 2, 3, 5, 5 * 128
+    gen = torch.Generator().manual_seed(L + 11)
+    q, ck, cv = (torch.randn(B, H, L, 128, generator=gen) for _ in range(3))
+    pk, pv = (torch.randn(B, cap, 128, generator=gen) for _ in range(2))
+    growth = torch.repeat_interleave(1.0 + 2.5 * torch.arange(S, dtype=torch.float32), 128)
+    pk = pk * growth[None, :, None]
+    ck = ck * (1.0 + 2.5 * S)
+    st = torch.tensor([[128 * i for i in range(S)]] * H, dtype=torch.int32)
+    en = st + 128
+    en[1, S - 1] = 128 * (S - 1) + 77
+    en[2, 0] = 40   # keys only in the first half of head 2's first tile
+    ct = torch.tensor([S, S, 2], dtype=torch.int32)
+    d = cuda_device
+    q, ck, pk = (x.to(d) for x in (q, ck, pk))
+    cv, pv = (x.bfloat16().to(d) for x in (cv, pv))
+    scale = 1.0 / math.sqrt(128)
+    out = attn(q=q, persisted_k=pk, persisted_v=pv, segment_starts=st.to(d),
+               segment_ends=en.to(d), segment_counts=ct.to(d),
+               current_k=ck, current_v=cv, softmax_scale=scale)
+    ref = _torch_reference(q, pk, pv, st, en, ct, ck, cv, scale)
+    _check_lowp(out.cpu().numpy(), ref.cpu().numpy())
+    assert _native.device_status(cuda_device) == 0
 
 
 @pytest.mark.parametrize("kd,vd", [(torch.bfloat16, torch.bfloat16), (torch.float32, torch.bfloat16),

@@ -1,8 +1,11 @@
 """The drop-in installer end to end on a small Infinity-shaped model (GPU): after
 ``enable_real_pruning_scale_specific_fused_segmented`` every layer's output at every one of the 13
 scales equals attention over exactly the tokens the keep-mask retains (plain PyTorch fp32 on the
-GPU), through the model's own projections. bf16 model (tcgen05 kernel, 2e-2 / 1e-2) and fp32
-cos-attn model (exact kernel, 1e-4)."""
+GPU), through the model's own projections. bf16 model (tcgen05 kernel, 2e-2 / 1e-2), fp32
+cos-attn model (exact kernel, 1e-4), and fp32 cos-attn model under bf16 autocast, the real
+model's setting: q and k fp32, v bf16 (tf32 tcgen05 kernel, 2e-2 / 1e-2)."""
+
+import contextlib
 
 import math
 
@@ -71,10 +74,16 @@ class SelfAttention(nn.Module):
         return self.proj_drop(self.proj(out.transpose(1, 2).reshape(B, L, C)))
 
 
-def _masked_reference(module, ctrl, layer, xs, t):
-    """Attention of scale t's queries over the retained earlier tokens + scale t, fp32."""
+def _autocast(enabled):
+    return torch.autocast("cuda", dtype=torch.bfloat16) if enabled else contextlib.nullcontext()
+
+
+def _masked_reference(module, ctrl, layer, xs, t, autocast=False):
+    """Attention of scale t's queries over the retained earlier tokens + scale t, fp32 (q, k, v
+    computed as the model computes them, under autocast when the model ran under it)."""
     with torch.no_grad():
-        qkv = [module.qkv(x) for x in xs[: t + 1]]
+        with _autocast(autocast):
+            qkv = [module.qkv(x) for x in xs[: t + 1]]
         q = qkv[t][0].float()
         k = torch.cat([z[1] for z in qkv], dim=2).float()
         v = torch.cat([z[2] for z in qkv], dim=2).float()
@@ -91,9 +100,12 @@ def _masked_reference(module, ctrl, layer, xs, t):
         return module.proj(out.reshape(B, n, H * D).to(module.proj.weight.dtype)).float()
 
 
-@pytest.mark.parametrize("dtype,cos_attn,atol,rel", [(torch.bfloat16, False, 2e-2, 1e-2),
-                                                    (torch.float32, True, 1e-4, 1e-4)])
-def test_installed_model_matches_keep_mask_attention(dtype, cos_attn, atol, rel):
+@pytest.mark.parametrize("dtype,cos_attn,autocast,atol,rel", [
+    (torch.bfloat16, False, False, 2e-2, 1e-2),
+    (torch.float32, True, False, 1e-4, 1e-4),
+    (torch.float32, True, True, 2e-2, 1e-2),
+])
+def test_installed_model_matches_keep_mask_attention(dtype, cos_attn, autocast, atol, rel):
     torch.backends.cuda.matmul.allow_tf32 = False
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
@@ -110,7 +122,11 @@ def test_installed_model_matches_keep_mask_attention(dtype, cos_attn, atol, rel)
     xs = {l: [torch.randn(2, h * w, C, device=dev, dtype=dtype) for _, h, w in schedule]
           for l in range(L)}
     outs = {l: [] for l in range(L)}
-    with torch.no_grad():
+    if autocast:  # the premise: cos-attn under bf16 autocast gives fp32 q, k and bf16 v
+        with torch.no_grad(), _autocast(True):
+            q, k, v = model[0].qkv(xs[0][1])
+        assert (q.dtype, k.dtype, v.dtype) == (torch.float32, torch.float32, torch.bfloat16)
+    with torch.no_grad(), _autocast(autocast):
         for t in range(len(schedule)):
             for l, m in enumerate(model):
                 outs[l].append(m(xs[l][t], None, scale_ind=t))
@@ -121,6 +137,6 @@ def test_installed_model_matches_keep_mask_attention(dtype, cos_attn, atol, rel)
     assert _native.device_status(dev) == 0
     for l, m in enumerate(model):
         for t in range(len(schedule)):
-            ref = _masked_reference(m, ctrl, l, xs[l], t)
+            ref = _masked_reference(m, ctrl, l, xs[l], t, autocast)
             err = (outs[l][t].float() - ref).abs().max().item()
             assert err <= atol and err / ref.abs().max().item() <= rel, (l, t, err)
