@@ -18,15 +18,19 @@
 // keys [64w, 64w+64) of every row, the two half-row maxima meet in shared memory behind a named
 // barrier, each warpgroup keeps the row sum of its half and rescales its half of O. The MMA
 // thread runs one score tile ahead: QK(j+1) is issued before PV(j), so the softmax of tile j
-// overlaps QK(j+1).
+// overlaps QK(j+1). QK and PV are issued by two threads: a single issuer blocks ~85 cycles on
+// every tcgen05.mma, so with both products on one thread PV(j) waited behind the whole of
+// QK(j+1); with two, the tensor pipe takes whichever is ready.
 //
 // CTA roles (384 threads, 1 CTA per SM):
 //   * warps 0-7 : softmax (two warpgroups, one TMEM lane = query row per thread); they also stage
 //                 the next item's Q rows (fp32 -> tf32, round to nearest) into TMEM as soon as the
 //                 current item's last QK has completed, and write the output.
 //   * warp 8    : TMA producer of K tiles (four 32-column fp32 boxes, 128-byte swizzle).
-//   * warp 9    : TMEM allocator and single-thread MMA issuer.
-//   * warp 10   : clears the V rows past the valid keys of partial V tiles.
+//   * warp 9    : TMEM allocator; lane 0 issues QK(j) once K(j) has landed and PV(j-2), the
+//                 last reader of the S buffer, has completed.
+//   * warp 10   : clears the V rows past the valid keys of a partial V tile, then lane 0 issues
+//                 PV(j) once P(j) is stored.
 //   * warp 11   : TMA producer of V tiles.
 // Items are (head, batch row, 128-row query block) in longest-head-first order (head_order), CTA
 // c of a persistent grid runs items c, c + grid, ... Every wait is bounded (common.cuh); on expiry
@@ -45,8 +49,8 @@ constexpr int kD = kHeadDim;
 constexpr int kStages = 2;
 constexpr int kThreads = 384;
 constexpr int kKWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kVFixWarp = 10;
+constexpr int kQkWarp = 9;
+constexpr int kPvWarp = 10;
 constexpr int kVWarp = 11;
 constexpr uint32_t kKBox = kBN * 128;         // 128 keys x 32 fp32 columns: 16 KiB
 constexpr uint32_t kKTileBytes = 4 * kKBox;   // 128 x 128 x 4 bytes
@@ -64,16 +68,14 @@ struct __align__(1024) Smem {
   uint8_t v[kStages][kVTileBytes];
   uint64_t q_full;              // the 8 softmax warps stored the item's Q into TMEM
   uint64_t k_full[kStages];
-  uint64_t k_empty[kStages];
   uint64_t v_full[kStages];
-  uint64_t v_ready[kStages];    // V tile landed and, if partial, its tail rows cleared
-  uint64_t v_empty[kStages];
-  uint64_t s_full[2];           // scores of tile g are in S buffer g % 2
+  // K stage, S buffer and V stage of tile g are all index g % 2 (kStages == 2):
+  uint64_t s_full[2];           // QK(g) done: scores in S buffer g % 2, K stage g % 2 free
   uint64_t p_full[2];           // the 8 softmax warps stored P of tile g over S buffer g % 2
-  uint64_t o_done;              // one phase per PV product
+  uint64_t pv_done[2];          // PV(g) done: V stage and S buffer g % 2 free, O includes tile g
   uint64_t o_final;             // the item's last PV product has completed
   uint64_t o_free;              // the 8 softmax warps have read the item's O
-  uint64_t drain;
+  uint64_t drain;               // both issuers' products have completed
   uint32_t tmem_base;
   int abort_flag;
   float red_max[2][2][kBM];     // [tile parity][warpgroup][row]: half-row maxima
@@ -85,6 +87,7 @@ struct __align__(1024) Smem {
   int seg_end[kMaxSegTable];
 };
 static_assert(sizeof(Smem) + 1024 <= 227 * 1024, "shared memory of one CTA");
+static_assert(kStages == 2, "K/V stages share the index of the two S buffers");
 
 struct Params {
   int64_t batch, heads, q_len, capacity, max_segments;
@@ -180,28 +183,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---------------------------------------------------------------- setup
   pdl_trigger();
-  if (warp == kMmaWarp) {
+  if (warp == kQkWarp) {
     tmem_alloc(&sm.tmem_base, kTmemCols);
     tmem_relinquish();
   }
   if (threadIdx.x == 0) {
     sm.abort_flag = 0;
     mbar_init(&sm.q_full, 8);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.k_full[s], 1);
-      mbar_init(&sm.k_empty[s], 1);
-      mbar_init(&sm.v_full[s], 1);
-      mbar_init(&sm.v_ready[s], 1);
-      mbar_init(&sm.v_empty[s], 1);
-    }
     for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.k_full[b], 1);
+      mbar_init(&sm.v_full[b], 1);
       mbar_init(&sm.s_full[b], 1);
       mbar_init(&sm.p_full[b], 8);
+      mbar_init(&sm.pv_done[b], 1);
     }
-    mbar_init(&sm.o_done, 1);
     mbar_init(&sm.o_final, 1);
     mbar_init(&sm.o_free, 8);
-    mbar_init(&sm.drain, 1);
+    mbar_init(&sm.drain, 2);
     fence_mbar_init();
   }
   pdl_wait();
@@ -273,7 +271,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < it.n; ++j, ++gx) {
           const int s = gx % kStages;
           uint64_t* full = loads_k ? &sm.k_full[s] : &sm.v_full[s];
-          uint64_t* empty = loads_k ? &sm.k_empty[s] : &sm.v_empty[s];
+          // the stage's previous tile (gx - 2) is done with: its QK (K) or its PV (V)
+          uint64_t* empty = loads_k ? &sm.s_full[s] : &sm.pv_done[s];
           if (gx >= kStages &&
               !(ok = mbar_wait(empty, ((gx / kStages) - 1) & 1, abort_flag, p.status)))
             break;
@@ -300,90 +299,59 @@ __global__ void __launch_bounds__(kThreads, 1)
                      (g / kStages) & 1, p.status);
       }
     }
-  } else if (warp == kMmaWarp) {
-    // ---------------------------------------------------------------- MMA issuer
+  } else if (warp == kQkWarp) {
+    // ---------------------------------------------------------------- QK issuer
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_tf32(kBM, kBN);
-      constexpr uint32_t idesc_pv = idesc_f16(kBF16, kBM, kD, false, true);
-      auto issue_qk = [&](uint32_t g) {
-        // S_(g%2) = Q K^T: A = Q from TMEM (8 tf32 columns per instruction), B = K tile, K-major
-        // SW128: K step kk is 32 bytes into the 128-byte row of box kk / 4
-        const uint32_t kbase = smem_u32(sm.k[g % kStages]);
-        const uint32_t d = tmem + kColS + (g & 1u) * 128;
-#pragma unroll
-        for (int kk = 0; kk < kD / 8; ++kk) {
-          const uint64_t bdesc = smem_desc_sw128(kbase + (kk / 4) * kKBox + (kk % 4) * 32, 16, 1024);
-          umma_tf32_ts(d, tmem + kColQ + kk * 8, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
-        }
-      };
-      auto issue_pv = [&](uint32_t g, bool accumulate) {
-        // O += P V: A = P (16-bit pairs over S_(g%2)), B = V tile, MN-major SW128: 8-key groups
-        // 1 KiB apart (SBO), the two 64-column halves 16 KiB apart (LBO)
-        const uint32_t vbase = smem_u32(sm.v[g % kStages]);
-        const uint32_t a = tmem + kColS + (g & 1u) * 128;
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t bdesc = smem_desc_sw128(vbase + kk * 2048, kVHalf, 1024);
-          umma_ts(tmem + kColO, a + kk * 8, bdesc, idesc_pv, (accumulate || kk > 0) ? 1u : 0u);
-        }
-      };
-      auto qk = [&](uint32_t g) -> bool {
-        if (!mbar_wait(&sm.k_full[g % kStages], (g / kStages) & 1, abort_flag, p.status))
-          return false;
-        tc_fence_after();
-        issue_qk(g);
-        tc_commit(&sm.s_full[g & 1u]);
-        tc_commit(&sm.k_empty[g % kStages]);
-        return true;
-      };
-      uint32_t g = 0, qcnt = 0, ocnt = 0;
+      uint32_t g = 0, qcnt = 0;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
         const Item it = decode_item(sm, p, item);
         if (!(ok = mbar_wait(&sm.q_full, qcnt & 1, abort_flag, p.status))) break;
         ++qcnt;
-        tc_fence_after();
-        if (!(ok = qk(g))) break;
-        for (int j = 0; j < it.n; ++j) {
-          const uint32_t gj = g + j;
-          if (j + 1 < it.n && !(ok = qk(gj + 1))) break;
-          if (!(ok = mbar_wait(&sm.v_ready[gj % kStages], (gj / kStages) & 1, abort_flag, p.status)))
-            break;
-          if (!(ok = mbar_wait(&sm.p_full[gj & 1u], (gj >> 1) & 1, abort_flag, p.status))) break;
-          if (j == 0 && ocnt > 0 &&
-              !(ok = mbar_wait(&sm.o_free, (ocnt - 1) & 1, abort_flag, p.status)))
+        for (int j = 0; j < it.n; ++j, ++g) {
+          const uint32_t b = g & 1u;
+          if (!(ok = mbar_wait(&sm.k_full[b], (g >> 1) & 1, abort_flag, p.status))) break;
+          // S buffer b last held P(g - 2): its PV must have completed
+          if (g >= 2 && !(ok = mbar_wait(&sm.pv_done[b], ((g >> 1) - 1) & 1, abort_flag, p.status)))
             break;
           tc_fence_after();
-          issue_pv(gj, j > 0);
-          tc_commit(&sm.o_done);
-          tc_commit(&sm.v_empty[gj % kStages]);
-          if (j == it.n - 1) tc_commit(&sm.o_final);
+          // S_b = Q K^T: A = Q from TMEM (8 tf32 columns per instruction), B = K tile, K-major
+          // SW128: K step kk is 32 bytes into the 128-byte row of box kk / 4
+          const uint32_t kbase = smem_u32(sm.k[b]);
+          const uint32_t d = tmem + kColS + b * 128;
+#pragma unroll
+          for (int kk = 0; kk < kD / 8; ++kk) {
+            const uint64_t bdesc = smem_desc_sw128(kbase + (kk / 4) * kKBox + (kk % 4) * 32, 16, 1024);
+            umma_tf32_ts(d, tmem + kColQ + kk * 8, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&sm.s_full[b]);
         }
-        g += it.n;
-        ++ocnt;
       }
-      // every MMA issued by this thread has completed once `drain` fires
+      // every MMA issued by this thread has completed once `drain` fires (with the PV issuer's)
       tc_commit(&sm.drain);
       mbar_drain(&sm.drain, 0, p.status);
     }
-  } else if (warp == kVFixWarp) {
-    // ---------------------------------------------------------------- V tail clearing
+  } else if (warp == kPvWarp) {
+    // ---------------------------------------------------------------- V tail clearing, PV issuer
     // Past the end of a segment (or of the current scale) a V tile holds whatever the slab holds
     // there; P is 0 for those keys but 0 x NaN would poison O, so the tail rows are cleared (a
-    // 128-byte swizzled row keeps its bytes inside its own 128-byte line).
-    uint32_t g = 0;
+    // 128-byte swizzled row keeps its bytes inside its own 128-byte line) before lane 0 issues
+    // the tile's PV.
+    constexpr uint32_t idesc_pv = idesc_f16(kBF16, kBM, kD, false, true);
+    uint32_t g = 0, ocnt = 0;
     bool ok = true;
     for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
       const Item it = decode_item(sm, p, item);
       TileCursor cur;
       cur.begin(sm, it.h, stride, 0);
       for (int j = 0; j < it.n; ++j, ++g) {
-        const int s = g % kStages;
-        ok = __all_sync(0xffffffffu, mbar_wait(&sm.v_full[s], (g / kStages) & 1, abort_flag, p.status));
+        const uint32_t b = g & 1u;
+        ok = __all_sync(0xffffffffu, mbar_wait(&sm.v_full[b], (g >> 1) & 1, abort_flag, p.status));
         if (!ok) break;
         const int valid = cur.valid(Lq);
         if (valid < kBN) {
-          uint8_t* base = sm.v[s];
+          uint8_t* base = sm.v[b];
           const int chunks = (kBN - valid) * 2 * 8;  // rows x halves x 16-byte chunks
           for (int i = lane; i < chunks; i += 32) {
             const int line = i / 8;
@@ -391,12 +359,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             *reinterpret_cast<uint4*>(base + half * kVHalf + row * 128 + (i % 8) * 16) =
                 make_uint4(0u, 0u, 0u, 0u);
           }
+          // the cleared rows are visible to the tensor core (async proxy)
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.v_ready[s]);
+        if (lane == 0) {
+          ok = mbar_wait(&sm.p_full[b], (g >> 1) & 1, abort_flag, p.status);
+          if (ok && j == 0 && ocnt > 0) ok = mbar_wait(&sm.o_free, (ocnt - 1) & 1, abort_flag, p.status);
+          if (ok) {
+            tc_fence_after();
+            // O += P V: A = P (16-bit pairs over S_b), B = V tile, MN-major SW128: 8-key groups
+            // 1 KiB apart (SBO), the two 64-column halves 16 KiB apart (LBO)
+            const uint32_t vbase = smem_u32(sm.v[b]);
+            const uint32_t a = tmem + kColS + b * 128;
+#pragma unroll
+            for (int kk = 0; kk < kBN / 16; ++kk) {
+              const uint64_t bdesc = smem_desc_sw128(vbase + kk * 2048, kVHalf, 1024);
+              umma_ts(tmem + kColO, a + kk * 8, bdesc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+            }
+            tc_commit(&sm.pv_done[b]);
+            if (j == it.n - 1) tc_commit(&sm.o_final);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
         cur.next();
       }
+      ++ocnt;
+    }
+    if (lane == 0) {
+      tc_commit(&sm.drain);
+      mbar_drain(&sm.drain, 0, p.status);
     }
   } else {
     // ---------------------------------------------------------------- softmax warpgroups
@@ -513,7 +506,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           f2unpack(add2(s01, s23), u0, u1);
           l_run += u0 + u1;
           if (rescale) {  // warp-uniform; O must hold PV(j-1) first
-            ok = __all_sync(0xffffffffu, mbar_wait(&sm.o_done, (gj - 1) & 1, abort_flag, p.status));
+            ok = __all_sync(0xffffffffu, mbar_wait(&sm.pv_done[(gj - 1) & 1u], ((gj - 1) >> 1) & 1,
+                                                   abort_flag, p.status));
             if (ok) {
               tc_fence_after();
 #pragma unroll
@@ -571,7 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kQkWarp) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);

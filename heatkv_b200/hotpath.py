@@ -198,7 +198,7 @@ class HotPath:
 
     def __init__(self, controller, num_layers: int, num_heads: int, batch: int, device,
                  k_dtype=torch.bfloat16, v_dtype=torch.bfloat16, head_dim: int = 128,
-                 layers: Optional[list] = None):
+                 layers: Optional[list] = None, plan_splits=None):
         self.device = torch.device(device)
         self.num_layers = int(num_layers)
         self.num_heads = int(num_heads)
@@ -223,10 +223,13 @@ class HotPath:
         self.schedule = {}
         ws_bytes = 0
         import os
-        # HEATKV_PLAN_SPLITS: "auto" (tail splits chosen by the planner), or a fixed number of
-        # key-range splits for every block (1 = never split)
-        forced_env = os.environ.get("HEATKV_PLAN_SPLITS", "auto")
-        forced = 0 if forced_env == "auto" else int(forced_env)
+        # plan_splits (default: HEATKV_PLAN_SPLITS, else "auto"): "auto" = tail splits chosen by
+        # the planner, or a fixed number of key-range splits for every block (1 = never split).
+        # A split block sums its keys in a different order, so outputs are bit-reproducible
+        # across different launch shapes (e.g. head shards) only without splits.
+        if plan_splits is None:
+            plan_splits = os.environ.get("HEATKV_PLAN_SPLITS", "auto")
+        forced = 0 if str(plan_splits) == "auto" else int(plan_splits)
         natural = os.environ.get("HEATKV_PLAN_ORDER", "lpt") == "natural"
         for i, p in enumerate(self.plans):
             for t in range(self.num_scales):

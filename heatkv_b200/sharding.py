@@ -323,7 +323,7 @@ class ShardedHotPath:
     def __init__(self, controller, num_layers: int, num_heads: int, plan: ShardPlan, rank: int,
                  device, k_dtype=torch.bfloat16, v_dtype=torch.bfloat16, head_dim: int = 128,
                  group=None, gather: Optional[bool] = None, layers: Optional[list] = None,
-                 exchange: str = "nccl"):
+                 exchange: str = "nccl", plan_splits=None):
         if exchange not in ("nccl", "p2p"):
             raise ValueError("exchange must be 'nccl' or 'p2p'")
         self.exchange = exchange
@@ -335,9 +335,12 @@ class ShardedHotPath:
         if plan.splits_heads and not self.gather:
             raise ValueError("a plan that splits heads needs the output gather")
         heads_by_layer = [plan.heads_of(rank, l) for l in range(num_layers)]
+        # the scatter epilogue runs unsplit, so the p2p exchange never plans key-range splits
+        if exchange == "p2p":
+            plan_splits = 1
         self.local = HotPath(HeadSubsetController(controller, heads_by_layer), num_layers,
                              plan.heads_per_rank, plan.rows_per_rank, self.device, k_dtype,
-                             v_dtype, head_dim, layers=layers)
+                             v_dtype, head_dim, layers=layers, plan_splits=plan_splits)
         self.plan_index = {lp.layer: i for i, lp in enumerate(self.local.plans)}
         self.num_scales = self.local.num_scales
         self.tokens = self.local.tokens
