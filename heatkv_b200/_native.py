@@ -22,7 +22,7 @@ HEATKV_ERR_CUDA = -3
 
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
-ATTN_AUTO, ATTN_EXACT, ATTN_TCGEN05 = 0, 1, 2
+ATTN_AUTO, ATTN_EXACT, ATTN_TCGEN05, ATTN_TCGEN05_PAIR, ATTN_TCGEN05_CS = 0, 1, 2, 3, 4
 
 DEVICE_PACK_OUT_OF_RANGE = 0x1
 DEVICE_WAIT_TIMEOUT = 0x2

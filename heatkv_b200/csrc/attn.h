@@ -50,8 +50,11 @@ cudaError_t launch_attention_simt(const AttnArgs& a, int q_dtype, int k_dtype, i
                                   cudaStream_t st);
 // Returns cudaErrorNotSupported when the tensor-core kernel cannot take these arguments.
 cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st);
-// fp32 q and k, 16-bit v (attn_sm100_tf32.cu): kind::tf32 QK with Q in TMEM, unsplit, no
-// scatter; cudaErrorNotSupported when it cannot take these arguments.
+// Column-split kernels (attn_sm100_cs.cu): one 128-row Q tile per CTA, the softmax of a tile
+// split by columns over warpgroups, unsplit; cudaErrorNotSupported when they cannot take these
+// arguments. _cs: q, k, v all bf16 or all f16 (scatter epilogue supported); _tf32: fp32 q and k
+// with 16-bit v, kind::tf32 QK with Q in TMEM (no scatter).
+cudaError_t launch_attention_sm100_cs(const AttnArgs& a, bool bf16, cudaStream_t st);
 cudaError_t launch_attention_sm100_tf32(const AttnArgs& a, bool v_bf16, cudaStream_t st);
 // Splits chosen by kv_splits = 0 and the workspace bytes a launch with `splits` needs.
 int attention_auto_splits(int64_t batch, int64_t heads, int64_t q_len);

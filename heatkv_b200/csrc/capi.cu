@@ -23,6 +23,18 @@ bool pdl_enabled() {
   return on;
 }
 
+// HEATKV_TCGEN05_VARIANT: "pair" (two Q tiles per CTA; the kernel with key-range splits) or
+// "cs" (one Q tile per CTA, column-split softmax); unset: cs unless splits are asked for.
+static int tcgen05_variant() {
+  static const int v = [] {
+    const char* e = getenv("HEATKV_TCGEN05_VARIANT");
+    if (e && strcmp(e, "pair") == 0) return 1;
+    if (e && strcmp(e, "cs") == 0) return 2;
+    return 0;
+  }();
+  return v;
+}
+
 unsigned int* device_status_ptr() {
   static std::atomic<unsigned int*> cache[64] = {};
   static std::mutex mu;
@@ -166,8 +178,15 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
                 heatkv::kMaxSegments);
   if (heads > 65535 || batch > 65535 || (q_len + 63) / 64 > 0x7fffffffLL)
     return fail(HEATKV_ERR_UNSUPPORTED, "real_scale_fused_segmented: grid too large");
-  if (kernel != HEATKV_ATTN_AUTO && kernel != HEATKV_ATTN_EXACT && kernel != HEATKV_ATTN_TCGEN05)
+  if (kernel < HEATKV_ATTN_AUTO || kernel > HEATKV_ATTN_TCGEN05_CS)
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: unknown kernel selector");
+  // the two-tile or column-split variant asked for by name; otherwise HEATKV_TCGEN05_VARIANT
+  const int forced_variant = kernel == HEATKV_ATTN_TCGEN05_PAIR ? 1
+                           : kernel == HEATKV_ATTN_TCGEN05_CS   ? 2
+                                                                : heatkv::tcgen05_variant();
+  const bool named_pair = kernel == HEATKV_ATTN_TCGEN05_PAIR;
+  if (kernel == HEATKV_ATTN_TCGEN05_PAIR || kernel == HEATKV_ATTN_TCGEN05_CS)
+    kernel = HEATKV_ATTN_TCGEN05;
 
   heatkv::AttnArgs a{q,     slab_k,        slab_v, seg_starts, seg_ends, seg_counts, cur_k,
                      cur_v, out,           batch,  heads,      q_len,    capacity,   max_segments,
@@ -191,6 +210,9 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
   // fp32 q and k with 16-bit v (the real model's dtypes): tf32 QK, P rounded to v's dtype
   const bool qk32 = (q_dtype == HEATKV_DTYPE_F32 && k_dtype == HEATKV_DTYPE_F32 &&
                      v_dtype != HEATKV_DTYPE_F32);
+  if (named_pair && !same16)
+    return fail(HEATKV_ERR_UNSUPPORTED,
+                "the two-tile tcgen05 kernel needs q, k and v all bfloat16 or all float16");
   if (kernel == HEATKV_ATTN_TCGEN05 && !same16 && !(qk32 && !scatter))
     return fail(HEATKV_ERR_UNSUPPORTED,
                 "tcgen05 segmented attention needs q, k and v all bfloat16 or all float16, or q "
@@ -202,7 +224,19 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
       return cuda_fail(e, "tcgen05 tf32 segmented attention launch");
   }
   if (kernel != HEATKV_ATTN_EXACT && same16) {
-    cudaError_t e = heatkv::launch_attention_sm100(a, q_dtype == HEATKV_DTYPE_BF16, st);
+    // key-range splits exist only in the two-Q-tile kernel; every other call takes the
+    // column-split kernel (HEATKV_TCGEN05_VARIANT = pair | cs forces one)
+    const int variant = forced_variant;
+    bool split = false;
+    if (variant == 0) {
+      const int splits = kv_splits == 0 ? heatkv::attention_auto_splits(batch, heads, q_len)
+                                        : kv_splits;
+      const int64_t pair_blocks = batch * heads * ((q_len + 255) / 256);
+      split = splits > 1 && workspace != nullptr && unsplit_blocks < pair_blocks;
+    }
+    const bool bf16 = q_dtype == HEATKV_DTYPE_BF16;
+    cudaError_t e = (variant == 1 || split) ? heatkv::launch_attention_sm100(a, bf16, st)
+                                            : heatkv::launch_attention_sm100_cs(a, bf16, st);
     if (e == cudaSuccess) return HEATKV_OK;
     if (e == cudaErrorNotSupported && scatter)
       return fail(HEATKV_ERR_UNSUPPORTED,

@@ -223,12 +223,14 @@ class HotPath:
         self.schedule = {}
         ws_bytes = 0
         import os
-        # plan_splits (default: HEATKV_PLAN_SPLITS, else "auto"): "auto" = tail splits chosen by
-        # the planner, or a fixed number of key-range splits for every block (1 = never split).
-        # A split block sums its keys in a different order, so outputs are bit-reproducible
-        # across different launch shapes (e.g. head shards) only without splits.
+        # plan_splits (default: HEATKV_PLAN_SPLITS, else 1): "auto" = tail splits chosen by the
+        # planner, or a fixed number of key-range splits for every block (1 = never split). Only
+        # the two-tile tcgen05 kernel splits key ranges; unsplit launches take the column-split
+        # kernel, which is faster at every target of the 2B image, so the default is 1. A split
+        # block sums its keys in a different order, so outputs are bit-reproducible across
+        # different launch shapes (e.g. head shards) only without splits.
         if plan_splits is None:
-            plan_splits = os.environ.get("HEATKV_PLAN_SPLITS", "auto")
+            plan_splits = os.environ.get("HEATKV_PLAN_SPLITS", "1")
         forced = 0 if str(plan_splits) == "auto" else int(plan_splits)
         natural = os.environ.get("HEATKV_PLAN_ORDER", "lpt") == "natural"
         for i, p in enumerate(self.plans):

@@ -56,7 +56,8 @@ def _fused_qk_dot_mode_id() -> int:
 
 
 _KERNEL_NAMES = {"auto": _native.ATTN_AUTO, "exact": _native.ATTN_EXACT,
-                 "tcgen05": _native.ATTN_TCGEN05}
+                 "tcgen05": _native.ATTN_TCGEN05, "tcgen05_pair": _native.ATTN_TCGEN05_PAIR,
+                 "tcgen05_cs": _native.ATTN_TCGEN05_CS}
 
 
 def _kernel_selector() -> int:
@@ -65,7 +66,8 @@ def _kernel_selector() -> int:
         try:
             return _KERNEL_NAMES[forced.strip().lower()]
         except KeyError:
-            raise ValueError("HEATKV_ATTENTION_KERNEL must be one of: auto, exact, tcgen05") from None
+            raise ValueError("HEATKV_ATTENTION_KERNEL must be one of: auto, exact, tcgen05, "
+                             "tcgen05_pair, tcgen05_cs") from None
     if _fused_qk_dot_mode_id() == 2 or _fused_value_dot_mode_id() == 2:
         return _native.ATTN_EXACT
     return _native.ATTN_AUTO

@@ -57,8 +57,13 @@ typedef enum {
   HEATKV_ATTN_AUTO = 0,   /* tensor-core kernel when q/k/v are all bf16 or all f16, or q and k
                              are f32 with bf16/f16 v (tf32 QK, P in v's dtype), else exact */
   HEATKV_ATTN_EXACT = 1,  /* CUDA-core kernel: fp32 products and accumulation for every dtype */
-  HEATKV_ATTN_TCGEN05 = 2 /* tcgen05/TMEM kernel; requires q/k/v all bf16 or all f16, or q and k
-                             f32 with bf16/f16 v */
+  HEATKV_ATTN_TCGEN05 = 2, /* tcgen05/TMEM kernel; requires q/k/v all bf16 or all f16, or q and
+                              k f32 with bf16/f16 v. 16-bit calls take the column-split kernel
+                              (one 128-row query tile per CTA) unless they ask for key-range
+                              splits, which only the two-tile kernel has */
+  HEATKV_ATTN_TCGEN05_PAIR = 3, /* the two-tile tcgen05 kernel (256 query rows per CTA, key-range
+                                   splits); q/k/v all bf16 or all f16 */
+  HEATKV_ATTN_TCGEN05_CS = 4    /* the column-split tcgen05 kernel; never splits key ranges */
 } heatkv_attn_kernel;
 
 /* Message describing the last failing call made by this thread ("" if none). */

@@ -33,12 +33,13 @@ def main() -> int:
     try:
         ctrl, L, H = bench.build_controller("2b", 0.10)
         layers, batch = [0, 21], 2
-        full = HotPath(ctrl, L, H, batch, dev, layers=layers)
+        # no key-range splits on either side: a split block sums in a different order
+        full = HotPath(ctrl, L, H, batch, dev, layers=layers, plan_splits=1)
         inputs, ref_out, _, _ = allocate_io(full, seed=11)       # identical on every rank
         HotPath.run(full.launches(inputs, ref_out))
         plan = sharding.plan_shards(sharding.head_costs(ctrl, L, H), batch, world, split=split)
         sh = sharding.ShardedHotPath(ctrl, L, H, plan, rank, dev, gather=True, layers=layers,
-                                     exchange=exchange)
+                                     exchange=exchange, plan_splits=1)
         rows = plan.rows_of(rank)
         li, lo, fo = [], [], []
         for i, layer in enumerate(layers):

@@ -113,14 +113,17 @@ def _random_layout(rng, heads, max_segments, capacity, lengths=(1, 4, 16, 36, 64
     return [torch.from_numpy(x) for x in (starts, ends, counts)]
 
 
+@pytest.mark.parametrize("which", ["tcgen05_cs", "tcgen05_pair"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("B,H,L,cap,S", [
     (1, 1, 1, 700, 3), (2, 3, 4, 400, 4), (1, 2, 127, 900, 5), (2, 2, 128, 900, 5),
     (1, 3, 129, 1200, 6), (2, 2, 255, 800, 4), (1, 2, 256, 900, 6), (2, 1, 257, 1500, 8),
     (2, 16, 576, 4000, 12), (1, 4, 1024, 3000, 12),
 ])
-def test_tcgen05_random_layouts(dtype, B, H, L, cap, S, cuda_device, kernel):
-    kernel("tcgen05")
+def test_tcgen05_random_layouts(which, dtype, B, H, L, cap, S, cuda_device, kernel):
+    """Both 16-bit tcgen05 kernels: the column-split one (one 128-row query tile per CTA, the
+    default) and the two-tile one (256 rows per CTA, key-range splits)."""
+    kernel(which)
     rng = np.random.default_rng(B * 1000 + H * 100 + L)
     gen = torch.Generator().manual_seed(L)
     q, ck, cv = (torch.randn(B, H, L, 128, generator=gen).to(dtype).to(cuda_device) for _ in range(3))
@@ -135,13 +138,14 @@ def test_tcgen05_random_layouts(dtype, B, H, L, cap, S, cuda_device, kernel):
     assert _native.device_status(cuda_device) == 0
 
 
+@pytest.mark.parametrize("which", ["tcgen05_cs", "tcgen05_pair"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("L", [5, 200, 300])
-def test_tcgen05_scores_growing_tile_by_tile(dtype, L, cuda_device, kernel):
+def test_tcgen05_scores_growing_tile_by_tile(which, dtype, L, cuda_device, kernel):
     """Each key tile's scores far above the previous tiles' (the running max rises by more than
     the lazy-rescale threshold again and again, so P is recomputed and O rescaled), with query
     rows of other heads in the last Q tile."""
-    kernel("tcgen05")
+    kernel(which)
     B, H, S, cap = 2, 3, 5, 5 * 128
     gen = torch.Generator().manual_seed(L + 7)
     q, ck, cv = (torch.randn(B, H, L, 128, generator=gen) for _ in range(3))
@@ -233,6 +237,19 @@ def test_tcgen05_tf32_mixed_dtypes(vdtype, B, H, L, cap, S, cuda_device, kernel)
     ref = _torch_reference(q, pk, pv, st, en, ct, ck, cv, scale)
     _check_lowp(out.cpu().numpy(), ref.cpu().numpy())
     assert _native.device_status(cuda_device) == 0
+
+
+def test_two_tile_kernel_rejects_fp32_queries(cuda_device, kernel):
+    """The two-tile kernel asked for by name takes only all-bf16 or all-f16 inputs."""
+    kernel("tcgen05_pair")
+    d = cuda_device
+    q, ck = (torch.randn(1, 2, 8, 128, device=d) for _ in range(2))
+    cv = torch.randn(1, 2, 8, 128, device=d).bfloat16()
+    z = torch.zeros(2, 0, dtype=torch.int32, device=d)
+    with pytest.raises(RuntimeError, match="two-tile"):
+        attn(q=q, persisted_k=None, persisted_v=None, segment_starts=z, segment_ends=z,
+             segment_counts=torch.zeros(2, dtype=torch.int32, device=d), current_k=ck,
+             current_v=cv, softmax_scale=0.1)
 
 
 @pytest.mark.parametrize("L", [5, 200, 300])
@@ -357,7 +374,8 @@ def test_config1_pipeline_against_reference(cuda_device, golden_dir):
     assert _native.device_status(d) == 0
 
 
-def _attention_ws(q, pk, pv, st, en, ct, ck, cv, scale, *, head_order, splits, workspace):
+def _attention_ws(q, pk, pv, st, en, ct, ck, cv, scale, *, head_order, splits, workspace,
+                  kernel=_native.ATTN_TCGEN05):
     import ctypes
     lib = _native.load()
     B, H, L, D = q.shape
@@ -367,7 +385,7 @@ def _attention_ws(q, pk, pv, st, en, ct, ck, cv, scale, *, head_order, splits, w
         _native.ptr(q), _native.ptr(pk), _native.ptr(pv), _native.ptr(st), _native.ptr(en),
         _native.ptr(ct), _native.ptr(ck), _native.ptr(cv), _native.ptr(out), dt[q.dtype],
         dt[ck.dtype], dt[cv.dtype], B, H, L, pk.shape[1], D, st.shape[1], ctypes.c_float(scale), 0,
-        _native.ATTN_TCGEN05, _native.ptr(head_order), splits, _native.ptr(workspace),
+        kernel, _native.ptr(head_order), splits, _native.ptr(workspace),
         0 if workspace is None else workspace.numel(), _native.stream_handle(q.device))
     _native.check(status, "heatkv_segmented_attention_ws")
     return out
@@ -421,8 +439,10 @@ def test_tcgen05_tail_split_schedule(B, H, L, cap, S, splits, cuda_device):
     ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=d)
     scale = 1.0 / math.sqrt(128)
     ref = _torch_reference(q, pk, pv, st.cpu(), en.cpu(), ct.cpu(), ck, cv, scale)
+    # the two-tile kernel throughout: it is the one with key-range splits
+    pair = _native.ATTN_TCGEN05_PAIR
     whole = _attention_ws(q, pk, pv, st, en, ct, ck, cv, scale, head_order=order, splits=1,
-                          workspace=None)
+                          workspace=None, kernel=pair)
     qpairs = (L + 255) // 256
     blocks = B * H * qpairs
     dt = _native.DTYPE_CODES
@@ -432,7 +452,7 @@ def test_tcgen05_tail_split_schedule(B, H, L, cap, S, splits, cuda_device):
             _native.ptr(q), _native.ptr(pk), _native.ptr(pv), _native.ptr(st), _native.ptr(en),
             _native.ptr(ct), _native.ptr(ck), _native.ptr(cv), _native.ptr(out), dt[q.dtype],
             dt[ck.dtype], dt[cv.dtype], B, H, L, cap, 128, S, ctypes.c_float(scale),
-            _native.ATTN_TCGEN05, _native.ptr(order), splits, unsplit, _native.ptr(ws),
+            pair, _native.ptr(order), splits, unsplit, _native.ptr(ws),
             ws.numel(), _native.stream_handle(d))
         _native.check(status, "heatkv_segmented_attention_sched")
         torch.cuda.synchronize()

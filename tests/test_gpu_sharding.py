@@ -80,13 +80,14 @@ def test_sharded_ranks_reassemble_the_single_gpu_outputs(world, split):
     ctrl, L, H = bench.build_controller("2b", 0.10)
     layers = [0, 21]
     batch = 2
-    full = HotPath(ctrl, L, H, batch, dev, layers=layers)
+    # no key-range splits on either side: a split block sums in a different order
+    full = HotPath(ctrl, L, H, batch, dev, layers=layers, plan_splits=1)
     inputs, outputs, _, _ = allocate_io(full, seed=5)
     HotPath.run(full.launches(inputs, outputs))
     costs = sharding.head_costs(ctrl, L, H)
     plan = sharding.plan_shards(costs, batch, world, split=split)
     assert plan.splits_heads
-    ranks = [sharding.ShardedHotPath(ctrl, L, H, plan, r, dev, layers=layers)
+    ranks = [sharding.ShardedHotPath(ctrl, L, H, plan, r, dev, layers=layers, plan_splits=1)
              for r in range(world)]
     local_out = []
     for r, sh in enumerate(ranks):
