@@ -23,6 +23,7 @@ HEATKV_ERR_CUDA = -3
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
 ATTN_AUTO, ATTN_EXACT, ATTN_TCGEN05, ATTN_TCGEN05_PAIR, ATTN_TCGEN05_CS = 0, 1, 2, 3, 4
+ATTN_STATIC_META = 0x100  # OR into a selector: metadata not written by preceding work
 
 DEVICE_PACK_OUT_OF_RANGE = 0x1
 DEVICE_WAIT_TIMEOUT = 0x2

@@ -31,6 +31,7 @@ struct AttnArgs {
   void* workspace = nullptr;            // split partials and counters (zeroed before first use)
   size_t workspace_bytes = 0;
   unsigned int* status = nullptr;       // device status word (device_status_ptr())
+  bool static_meta = false;             // metadata not written by the preceding stream work
   // scatter epilogue (tcgen05 kernel, unsplit): rows to n_out full outputs at mapped rows/heads
   void* const* out_ptrs = nullptr;      // [n_out] device array of base pointers
   const int32_t* out_rows = nullptr;    // [batch] -> row of the full output

@@ -104,6 +104,7 @@ struct Params {
   int qblocks;                  // ceil(Lq / 128)
   int n_items;                  // heads * batch * qblocks
   int seg_stride;
+  int static_meta;              // stage the metadata before the dependency wait
   // scatter epilogue (16-bit mode, n_out > 0): every output row goes to n_out full [out_batch,
   // Lq, out_heads_total * D] tensors at row out_rows[b] and head out_heads[h]
   void* const* out_ptrs;
@@ -246,7 +247,9 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
     mbar_init(&sm.drain, 2);
     fence_mbar_init();
   }
-  pdl_wait();
+  // The metadata is staged before the dependency wait when the caller guarantees that the
+  // preceding work does not write it (HEATKV_ATTN_STATIC_META), else after it.
+  if (!p.static_meta) pdl_wait();
   if (warp == kKWarp) {
     // stage the [H, S] metadata, compact every head's non-empty segments in place (clipped to
     // the slab) and count its key tiles
@@ -295,6 +298,7 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
       tma_prefetch_desc(&tm_sv);
     }
   }
+  if (p.static_meta) pdl_wait();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -622,21 +626,22 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
           off = ((int64_t(grow) * Lq + qrow) * p.out_heads_total + ghead) * kD + c0;
           n_dst = p.n_out;
         }
-#pragma unroll 1
-        for (int cc = 0; cc < kCols / 16; ++cc) {
-          float o[16];
-          tmem_ld16_sync(tO + cc * 16, o);
-          if (qrow < Lq && in_range) {
+        float o[kCols];
+        tmem_ld_cols<kCols>(tO, o);  // this warpgroup's O columns in one load
+        if (qrow < Lq && in_range) {
+#pragma unroll
+          for (int cc = 0; cc < kCols / 16; ++cc) {
             if constexpr (kTf32) {
               float4* d4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off + cc * 16);
 #pragma unroll
               for (int i = 0; i < 4; ++i)
-                d4[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv,
-                                    o[4 * i + 3] * inv);
+                d4[i] = make_float4(o[cc * 16 + 4 * i] * inv, o[cc * 16 + 4 * i + 1] * inv,
+                                    o[cc * 16 + 4 * i + 2] * inv, o[cc * 16 + 4 * i + 3] * inv);
             } else {
               uint32_t wv[8];
 #pragma unroll
-              for (int i = 0; i < 8; ++i) wv[i] = pack2<kBF16>(o[2 * i] * inv, o[2 * i + 1] * inv);
+              for (int i = 0; i < 8; ++i)
+                wv[i] = pack2<kBF16>(o[cc * 16 + 2 * i] * inv, o[cc * 16 + 2 * i + 1] * inv);
 #pragma unroll 1
               for (int r = 0; r < n_dst; ++r) {
                 OutT* base = p.n_out > 0 ? static_cast<OutT*>(p.out_ptrs[r]) : static_cast<OutT*>(p.out);
@@ -764,6 +769,7 @@ static cudaError_t launch_mode(const AttnArgs& a, cudaStream_t st) {
   p.qblocks = qblocks;
   p.n_items = static_cast<int>(n_items);
   p.seg_stride = static_cast<int>(std::max<int64_t>(a.max_segments, 1));
+  p.static_meta = a.static_meta ? 1 : 0;
   p.out_ptrs = a.out_ptrs;
   p.out_rows = a.out_rows;
   p.out_heads = a.out_heads;

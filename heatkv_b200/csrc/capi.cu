@@ -178,6 +178,8 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
                 heatkv::kMaxSegments);
   if (heads > 65535 || batch > 65535 || (q_len + 63) / 64 > 0x7fffffffLL)
     return fail(HEATKV_ERR_UNSUPPORTED, "real_scale_fused_segmented: grid too large");
+  const bool static_meta = (kernel & HEATKV_ATTN_STATIC_META) != 0;
+  kernel &= ~HEATKV_ATTN_STATIC_META;
   if (kernel < HEATKV_ATTN_AUTO || kernel > HEATKV_ATTN_TCGEN05_CS)
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: unknown kernel selector");
   // the two-tile or column-split variant asked for by name; otherwise HEATKV_TCGEN05_VARIANT
@@ -197,6 +199,7 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;
   a.status = heatkv::device_status_ptr();
+  a.static_meta = static_meta;
   if (scatter) {
     a.out_ptrs = scatter->out_ptrs;
     a.out_rows = scatter->out_rows;

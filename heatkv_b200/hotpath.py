@@ -261,6 +261,9 @@ class HotPath:
         B, H, D = self.batch, self.num_heads, self.head_dim
         scale = float(softmax_scale) if softmax_scale is not None else D ** -0.5
         lib = self.lib
+        # the segment metadata and head orders were uploaded at construction and no launch of
+        # the step writes them: the attention kernel may stage them before its dependency wait
+        meta_kernel = int(kernel) | _native.ATTN_STATIC_META
         dt = _native.DTYPE_CODES
         out = []
         for t in range(self.num_scales):
@@ -285,7 +288,7 @@ class HotPath:
                     (_native.ptr(q), _native.ptr(sk), _native.ptr(sv), _native.ptr(st),
                      _native.ptr(en), _native.ptr(ct), _native.ptr(k), _native.ptr(v),
                      _native.ptr(o), dt[q.dtype], dt[k.dtype], dt[v.dtype], B, H, n, cap, D,
-                     int(st.shape[1]), ctypes.c_float(scale), kernel, _native.ptr(order),
+                     int(st.shape[1]), ctypes.c_float(scale), meta_kernel, _native.ptr(order),
                      int(splits), int(unsplit), _native.ptr(self.workspace),
                      self.workspace.numel()), flops))
                 row_k = D * k.element_size()

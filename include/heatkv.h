@@ -66,6 +66,11 @@ typedef enum {
   HEATKV_ATTN_TCGEN05_CS = 4    /* the column-split tcgen05 kernel; never splits key ranges */
 } heatkv_attn_kernel;
 
+/* OR into the kernel selector: the segment metadata (starts, ends, counts) and the head order are
+ * not written by the work that precedes the call in the stream (e.g. uploaded once at install),
+ * so the column-split kernel may stage them while the preceding kernel is still running. */
+#define HEATKV_ATTN_STATIC_META 0x100
+
 /* Message describing the last failing call made by this thread ("" if none). */
 const char* heatkv_last_error_string(void);
 
