@@ -88,4 +88,11 @@ cudaError_t launch_shard_gather(void* dst, const void* src, const int32_t* row_m
                                 int64_t heads, int64_t chunk_bytes, int sms,
                                 unsigned int* status, cudaStream_t stream);
 
+// q/k/v preparation after the QKV projection (qkv_prep.cu); sms = SMs of the device.
+cudaError_t launch_qkv_prepare(const void* qkv, void* q, void* k, void* v, int in_dtype,
+                               int qk_dtype, int64_t batch, int64_t seq_len, int64_t heads,
+                               const float* scale_mul, float eps, const float* rope_cos,
+                               const float* rope_sin, int64_t rope_row_stride, int sms,
+                               unsigned int* status, cudaStream_t st);
+
 }  // namespace heatkv

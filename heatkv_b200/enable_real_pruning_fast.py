@@ -23,7 +23,16 @@ Attention modules are found by type name ``SelfAttention`` (the reference's ``is
 RoPE function is taken from the module's defining Python module (``apply_rotary_emb``).
 
 Precision note: with cos-attn under bf16 autocast the model produces fp32 q/k and bf16 v; those
-mixed calls run the exact CUDA-core kernel. All-bf16/all-fp16 calls run the tcgen05 kernel.
+mixed calls run the tcgen05 kernel with tf32 scores (the reference's default dot mode on fp32
+operands), as do all-bf16/all-fp16 calls; ``REAL_PRUNING_FUSED_QK_DOT_MODE=fp32`` selects the exact
+CUDA-core kernel.
+
+``fused_qkv_prep=True`` (installer keyword, not in the reference) replaces the q/k/v preparation
+between the QKV projection and the attention (unbind, permute, cos-attention normalisation and
+head scale, 2-D RoPE) by one pass of ``heatkv_qkv_prepare`` (``qkv_prep.prepare_qkv``), when the
+projection is bf16/fp16, the head dim is 128 and, with cos-attention, autocast is enabled (the
+kernel normalises in fp32 as F.normalize does under autocast). Its RoPE is the one of
+infinity/models/basic.py:97-117 applied to the module's rope cache rows.
 """
 
 from __future__ import annotations
@@ -40,6 +49,7 @@ import torch.nn.functional as F
 from torch.nn.functional import scaled_dot_product_attention as slow_attn
 
 from . import budget as _budget
+from . import qkv_prep as _qkv_prep
 from .enable_pruning import (
     ScaleSpecificPruningController,
     _assign_layer_indices,
@@ -213,6 +223,13 @@ def _items_desc(items, seq_len: int, device):
     return dst, src, ln, max(it[3] for it in items), sum(it[3] for it in items)
 
 
+def _fused_prep_applies(module, qkv) -> bool:
+    """The one-pass q/k/v preparation reproduces the PyTorch chain's dtypes here."""
+    return (bool(getattr(module, "_heatkv_fused_qkv_prep", False)) and qkv.is_cuda
+            and qkv.dtype in (torch.bfloat16, torch.float16) and module.head_dim == 128
+            and (not module.cos_attn or torch.is_autocast_enabled()))
+
+
 def _rope_fn(module):
     mod = sys.modules.get(type(module).__module__)
     fn = getattr(mod, "apply_rotary_emb", None) if mod is not None else None
@@ -327,22 +344,34 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
     qkv = F.linear(input=x, weight=self.mat_qkv.weight,
                    bias=torch.cat((self.q_bias, self.zero_k_bias, self.v_bias))).view(
         batch_size, seq_len, 3, self.num_heads, self.head_dim)
-    q, k, v = qkv.unbind(dim=2)
-    q = q.permute(0, 2, 1, 3).contiguous()
-    k = k.permute(0, 2, 1, 3).contiguous()
-    v = v.permute(0, 2, 1, 3).contiguous()
-    del qkv
-    if self.cos_attn:
-        scale_mul = self.scale_mul_1H11.reshape(1, self.num_heads, 1, 1).clamp_max(
-            self.max_scale_mul).exp()
-        q = F.normalize(q, dim=-1, eps=1e-12).mul(scale_mul).contiguous()
-        k = F.normalize(k, dim=-1, eps=1e-12).contiguous()
-        v = v.contiguous()
-    if rope2d_freqs_grid is not None:
-        if scale_schedule is None:
-            raise ValueError("scale_schedule is required when rope2d_freqs_grid is provided")
-        q, k = _rope_fn(self)(q, k, scale_schedule, rope2d_freqs_grid, self.pad_to_multiplier,
-                              self.rope2d_normalized_by_hw, scale_ind)
+    if rope2d_freqs_grid is not None and scale_schedule is None:
+        raise ValueError("scale_schedule is required when rope2d_freqs_grid is provided")
+    if _fused_prep_applies(self, qkv):
+        scale_mul = None
+        if self.cos_attn:
+            scale_mul = self.scale_mul_1H11.reshape(1, self.num_heads, 1, 1).clamp_max(
+                self.max_scale_mul).exp()
+        rope = None
+        if rope2d_freqs_grid is not None:
+            rope = _qkv_prep.rope_rows(rope2d_freqs_grid, scale_schedule, scale_ind, seq_len,
+                                       qkv.device)
+        q, k, v = _qkv_prep.prepare_qkv(qkv, scale_mul=scale_mul, rope=rope)
+        del qkv
+    else:
+        q, k, v = qkv.unbind(dim=2)
+        q = q.permute(0, 2, 1, 3).contiguous()
+        k = k.permute(0, 2, 1, 3).contiguous()
+        v = v.permute(0, 2, 1, 3).contiguous()
+        del qkv
+        if self.cos_attn:
+            scale_mul = self.scale_mul_1H11.reshape(1, self.num_heads, 1, 1).clamp_max(
+                self.max_scale_mul).exp()
+            q = F.normalize(q, dim=-1, eps=1e-12).mul(scale_mul).contiguous()
+            k = F.normalize(k, dim=-1, eps=1e-12).contiguous()
+            v = v.contiguous()
+        if rope2d_freqs_grid is not None:
+            q, k = _rope_fn(self)(q, k, scale_schedule, rope2d_freqs_grid, self.pad_to_multiplier,
+                                  self.rope2d_normalized_by_hw, scale_ind)
 
     removed_now = ctrl.any_removed(layer, scale_ind)
     dense_candidate = None
@@ -426,7 +455,8 @@ def enable_real_pruning_scale_specific_fast(model, budget, scale_specific_remova
                                             skip_last_scale=True, merge_mode="exact",
                                             attention_impl="fused_segmented",
                                             requested_generation_batch_size=None,
-                                            attention_modules=None, scale_schedule=None):
+                                            attention_modules=None, scale_schedule=None,
+                                            fused_qkv_prep=False):
     """Install HeatKV scale-specific pruning (enable_real_pruning_fast.py:2279-2378)."""
     merge_mode = _validate_merge_mode(merge_mode)
     if attention_impl != "fused_segmented":
@@ -467,6 +497,7 @@ def enable_real_pruning_scale_specific_fast(model, budget, scale_specific_remova
         module._real_pruning_requested_generation_batch_size = (
             None if requested_generation_batch_size is None else int(requested_generation_batch_size))
         module._heatkv_layer = _LayerState(controller, module.layer_idx, num_heads)
+        module._heatkv_fused_qkv_prep = bool(fused_qkv_prep)
         module._real_pruning_segmented_static_schedule = module._heatkv_layer.schedule
         try:
             device = next(module.parameters()).device
@@ -491,11 +522,12 @@ def enable_real_pruning_scale_specific_fused_segmented(model, budget, scale_spec
                                                        skip_last_scale=True, merge_mode="exact",
                                                        requested_generation_batch_size=None,
                                                        attention_modules=None,
-                                                       scale_schedule=None):
+                                                       scale_schedule=None, fused_qkv_prep=False):
     """Alias of the installer with ``attention_impl='fused_segmented'`` (:2381-2402)."""
     return enable_real_pruning_scale_specific_fast(
         model, budget, scale_specific_removal_orders,
         protected_prefix_scales=protected_prefix_scales, source_scale_start=source_scale_start,
         skip_last_scale=skip_last_scale, merge_mode=merge_mode, attention_impl="fused_segmented",
         requested_generation_batch_size=requested_generation_batch_size,
-        attention_modules=attention_modules, scale_schedule=scale_schedule)
+        attention_modules=attention_modules, scale_schedule=scale_schedule,
+        fused_qkv_prep=fused_qkv_prep)

@@ -9,6 +9,8 @@
 ``pack``: the append of one scale (every head's ``--q-len`` tokens) into a slab.
 ``pack-batched``: the same append for ``--layers`` layers (one slab and one source per layer) as
 one ``heatkv_pack_kv_batched`` launch, as the pre-planned step issues a scale's appends.
+``qkv-prep``: one layer's q/k/v preparation (``heatkv_qkv_prepare``: cos-attention + RoPE under
+autocast) against the PyTorch chain it replaces.
 Prints per-call device time (CUDA events, warm, back to back) and the achieved TFLOP/s or GB/s.
 """
 
@@ -69,7 +71,7 @@ def time_call(fn, iters, warmup=3):
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("kernel", choices=["attention", "pack", "pack-batched"])
+    ap.add_argument("kernel", choices=["attention", "pack", "pack-batched", "qkv-prep"])
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--rows", type=int, default=2)
     ap.add_argument("--heads", type=int, default=16)
@@ -91,6 +93,39 @@ def main(argv=None):
         print(f"attention rows={args.rows} heads={args.heads} q_len={args.q_len} "
               f"slots={args.slots} {args.dtype}: {ms * 1e3:.1f} us/call, "
               f"{flops / ms / 1e9:.1f} TFLOP/s", flush=True)
+    elif args.kernel == "qkv-prep":
+        # one layer's q/k/v preparation at a scale: qkv [rows, Lq, 3, heads, 128] bf16 -> fp32 q, k
+        # and bf16 v with cos-attention and RoPE under autocast, against the PyTorch chain
+        import torch.nn.functional as F
+
+        from .qkv_prep import prepare_qkv
+        B, L, H = args.rows, args.q_len, args.heads
+        qkv = torch.randn(B, L, 3, H, 128, device="cuda").bfloat16()
+        sm = torch.full((1, H, 1, 1), 4.0, device="cuda")
+        ang = torch.rand(L, 64, device="cuda") * 6
+        cos, sin = torch.cos(ang), torch.sin(ang)
+
+        def torch_chain():
+            q, k, v = qkv.unbind(dim=2)
+            q, k, v = (x.permute(0, 2, 1, 3).contiguous() for x in (q, k, v))
+            q = F.normalize(q, dim=-1, eps=1e-12).mul(sm).contiguous()
+            k = F.normalize(k, dim=-1, eps=1e-12).contiguous()
+            qk = torch.stack((q, k), dim=0)
+            with torch.autocast("cuda", enabled=False):
+                qk = qk.reshape(*qk.shape[:-1], -1, 2)
+                qk = torch.stack([cos * qk[..., 0] - sin * qk[..., 1],
+                                  sin * qk[..., 0] + cos * qk[..., 1]], dim=-1)
+                qk = qk.reshape(*qk.shape[:-2], -1)
+            return qk[0], qk[1], v
+
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            ms = time_call(lambda: prepare_qkv(qkv, scale_mul=sm, rope=(cos, sin)), args.iters,
+                           args.warmup)
+            ms_t = time_call(torch_chain, args.iters, args.warmup)
+        nbytes = B * L * H * 128 * (3 * 2 + 2 * 4 + 2) + L * 64 * 2 * 4
+        print(f"qkv-prep rows={B} heads={H} q_len={L}: {ms * 1e3:.1f} us/call, "
+              f"{nbytes / ms / 1e6:.1f} GB/s; PyTorch chain {ms_t * 1e3:.1f} us "
+              f"({ms_t / ms:.1f}x)", flush=True)
     elif args.kernel == "pack-batched":
         import numpy as np
 

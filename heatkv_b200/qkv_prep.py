@@ -1,0 +1,93 @@
+"""One-pass q/k/v preparation between the QKV projection and the segmented attention.
+
+The reference's patched attention forward (enable_real_pruning_fast.py:2040-2072) turns the
+projection output ``qkv`` ``[B, L, 3, H, D]`` into contiguous ``q, k, v`` ``[B, H, L, D]`` with a
+chain of PyTorch ops: ``unbind`` + ``permute`` + ``contiguous``; with cos-attention
+``q = F.normalize(q) * scale_mul`` and ``k = F.normalize(k)``; then ``apply_rotary_emb``
+(infinity/models/basic.py:97-117), which computes in fp32 with autocast off.
+``prepare_qkv`` does the same in one HBM pass (``heatkv_qkv_prepare``, csrc/qkv_prep.cu).
+
+Result dtypes follow the PyTorch chain: q and k are fp32 when the rotary embedding is applied
+(its fp32 cache promotes them) or when cos-attention normalises under autocast, else the input
+dtype; v keeps the input dtype.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import numpy as np
+import torch
+
+from . import _native
+
+__all__ = ["prepare_qkv", "rope_rows"]
+
+
+def rope_rows(rope2d_freqs_grid, scale_schedule, scale_ind: int, seq_len: int,
+              device) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The (cos, sin) rows ``[seq_len, D/2]`` that ``apply_rotary_emb`` slices for a scale
+    (infinity/models/basic.py:104-109): the rope cache of the schedule, rows ``start ..
+    start + seq_len`` with ``start`` the tokens of the earlier scales."""
+    key = str(tuple(scale_schedule))
+    grid = rope2d_freqs_grid[key]
+    if grid.device != torch.device(device):
+        grid = rope2d_freqs_grid[key] = grid.to(device)
+    start = 0
+    if scale_ind >= 1:
+        start = int(np.sum([it[0] * it[1] * it[2] for it in scale_schedule[:scale_ind]]))
+    if start + seq_len > grid.shape[4]:
+        raise ValueError("rope cache shorter than the scale's tokens")
+    rows = grid[:, 0, 0, 0, start:start + seq_len]  # [2, seq_len, half_dim]
+    return rows[0], rows[1]
+
+
+def prepare_qkv(qkv: torch.Tensor, *, scale_mul: Optional[torch.Tensor] = None,
+                eps: float = 1e-12, rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                qk_dtype: Optional[torch.dtype] = None):
+    """``qkv`` ``[B, L, 3, H, 128]`` (bf16/f16) -> ``q, k, v`` ``[B, H, L, 128]``.
+
+    ``scale_mul``: the cos-attention head scales (any shape with H elements, e.g. the
+    ``scale_mul_1H11.clamp_max(max).exp()`` tensor), or None for no normalisation. ``rope``:
+    ``(cos, sin)`` rows ``[L, 64]`` fp32 (``rope_rows``), or None. ``qk_dtype``: defaults to fp32
+    when ``rope`` is given or autocast is enabled with ``scale_mul``, else ``qkv.dtype``."""
+    if qkv.ndim != 5 or qkv.shape[2] != 3:
+        raise ValueError("prepare_qkv expects qkv shaped [B, L, 3, H, D]")
+    B, L, _, H, D = qkv.shape
+    if D != 128:
+        raise RuntimeError("prepare_qkv only supports head_dim=128")
+    if qkv.dtype not in (torch.bfloat16, torch.float16):
+        raise RuntimeError("prepare_qkv expects a bfloat16 or float16 qkv")
+    if not qkv.is_cuda:
+        raise RuntimeError("prepare_qkv requires CUDA tensors")
+    lib = _native.load()
+    dev = qkv.device
+    qkv = qkv.contiguous()
+    if qk_dtype is None:
+        fp32 = rope is not None or (scale_mul is not None and torch.is_autocast_enabled())
+        qk_dtype = torch.float32 if fp32 else qkv.dtype
+    q = torch.empty(B, H, L, D, dtype=qk_dtype, device=dev)
+    k = torch.empty_like(q)
+    v = torch.empty(B, H, L, D, dtype=qkv.dtype, device=dev)
+    sm = None
+    if scale_mul is not None:
+        if scale_mul.numel() != H:
+            raise ValueError("scale_mul must have one value per head")
+        sm = scale_mul.detach().reshape(H).to(device=dev, dtype=torch.float32).contiguous()
+    cos = sin = None
+    stride = 0
+    if rope is not None:
+        cos, sin = rope
+        if (cos.shape != (L, D // 2) or sin.shape != (L, D // 2) or cos.dtype != torch.float32
+                or sin.dtype != torch.float32 or cos.stride(1) != 1 or sin.stride(1) != 1
+                or cos.stride(0) != sin.stride(0)):
+            raise ValueError("rope rows must be fp32 [L, 64] with unit inner stride")
+        if cos.device != dev or sin.device != dev:
+            raise ValueError("rope rows must be on the qkv device")
+        stride = int(cos.stride(0))
+    _native.check(lib.heatkv_qkv_prepare(
+        _native.ptr(qkv), _native.ptr(q), _native.ptr(k), _native.ptr(v),
+        _native.DTYPE_CODES[qkv.dtype], _native.DTYPE_CODES[qk_dtype], B, L, H, D,
+        _native.ptr(sm), float(eps), _native.ptr(cos), _native.ptr(sin), stride,
+        _native.stream_handle(dev)), "prepare_qkv")
+    return q, k, v

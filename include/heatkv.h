@@ -8,6 +8,10 @@
  *   - heatkv_segmented_attention <- fused_real_pruning_flat_segmented_attention (:445-591) and its
  *                                  Triton kernel _fused_real_pruning_segmented_attention_kernel
  *                                  (:76-267)
+ * and, on the caller's side of the attention, the PyTorch chain that prepares q, k, v after the
+ * QKV projection (enable_real_pruning_fast.py:2040-2072):
+ *   - heatkv_qkv_prepare         <- unbind/permute, F.normalize * scale_mul, apply_rotary_emb
+ *                                  (infinity/models/basic.py:97-117)
  *
  * Conventions
  *   - Every pointer argument is a device pointer unless stated otherwise; tensors are dense,
@@ -303,6 +307,25 @@ int heatkv_gather_head_shards(void* dst, const void* src, int dtype, int64_t wor
                               int64_t rows_per_rank, int64_t q_len, int64_t heads_per_rank,
                               int64_t batch, int64_t heads, int64_t head_dim,
                               const int32_t* row_map, const int32_t* head_map, void* stream);
+
+/*
+ * heatkv_qkv_prepare - the q/k/v preparation of the patched attention forward between the QKV
+ * projection and the attention call (enable_real_pruning_fast.py:2040-2072), in one pass:
+ *   qkv : [batch, seq_len, 3, heads, head_dim] (in_dtype: bf16 or f16), the projection output
+ *   q, k: [batch, heads, seq_len, head_dim] (qk_dtype: f32, bf16 or f16)
+ *   v   : [batch, heads, seq_len, head_dim] (in_dtype), a copy
+ * With scale_mul != null (cos-attention, [heads] fp32 device array of the exp'd, clamped
+ * scale_mul_1H11): q = q / max(||q||, eps) * scale_mul[h], k = k / max(||k||, eps) (norm and
+ * quotient in fp32, as F.normalize under autocast). With rope_cos != null: the 2-D rotary
+ * embedding of infinity/models/basic.py:97-117 in fp32, pair (x[2i], x[2i+1]) of token l turned by
+ * (rope_cos[l * rope_row_stride + i], rope_sin[...]): the rope cache rows of this scale
+ * (rope2d_freqs_grid[...][0/1, 0, 0, 0, start:start+seq_len, :]). head_dim must be 128; qkv, v and
+ * the rope rows 8-byte aligned, q and k 16-byte aligned when fp32.
+ */
+int heatkv_qkv_prepare(const void* qkv, void* q, void* k, void* v, int in_dtype, int qk_dtype,
+                       int64_t batch, int64_t seq_len, int64_t heads, int64_t head_dim,
+                       const float* scale_mul, float eps, const float* rope_cos,
+                       const float* rope_sin, int64_t rope_row_stride, void* stream);
 
 /*
  * heatkv_device_status - read (and with clear != 0, reset) the sticky HEATKV_DEVICE_* flags of

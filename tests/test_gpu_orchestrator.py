@@ -24,6 +24,23 @@ from heatkv_b200.enable_real_pruning_fast import (
 pytestmark = pytest.mark.gpu
 
 
+def apply_rotary_emb(q, k, scale_schedule, rope2d_freqs_grid, pad_to_multiplier,
+                     rope2d_normalized_by_hw, scale_ind):
+    """The 2-D rotary embedding of infinity/models/basic.py:97-117, restated; the drop-in looks
+    it up beside the attention class, as it does in the Infinity model."""
+    qk = torch.stack((q, k), dim=0)
+    with torch.autocast(device_type="cuda", enabled=False):
+        seq_len = qk.shape[3]
+        start = sum(a * b * c for a, b, c in scale_schedule[:scale_ind]) if scale_ind >= 1 else 0
+        cache = rope2d_freqs_grid[str(tuple(scale_schedule))].to(qk.device)[:, :, :, :, start:start + seq_len]
+        qk = qk.reshape(*qk.shape[:-1], -1, 2)
+        qk = torch.stack([cache[0] * qk[..., 0] - cache[1] * qk[..., 1],
+                          cache[1] * qk[..., 0] + cache[0] * qk[..., 1]], dim=-1)
+        qk = qk.reshape(*qk.shape[:-2], -1)
+        q, k = qk.unbind(dim=0)
+    return q, k
+
+
 class SelfAttention(nn.Module):
     """Infinity's self-attention (infinity/models/basic.py:196-316, customized_flash_attn=False)
     reduced to what the installer touches."""
@@ -64,6 +81,8 @@ class SelfAttention(nn.Module):
                 rope2d_freqs_grid=None, scale_ind=0):
         B, L, C = x.shape
         q, k, v = self.qkv(x)
+        if rope2d_freqs_grid is not None:
+            q, k = apply_rotary_emb(q, k, scale_schedule, rope2d_freqs_grid, 1, 0, scale_ind)
         if self.caching:
             if self.cached_k is None:
                 self.cached_k, self.cached_v = k, v
@@ -140,3 +159,40 @@ def test_installed_model_matches_keep_mask_attention(dtype, cos_attn, autocast, 
             ref = _masked_reference(m, ctrl, l, xs[l], t, autocast)
             err = (outs[l][t].float() - ref).abs().max().item()
             assert err <= atol and err / ref.abs().max().item() <= rel, (l, t, err)
+
+
+def test_fused_qkv_prep_matches_the_torch_chain():
+    """fused_qkv_prep=True (one-pass unbind / permute / cos-attention normalisation / RoPE) against
+    the PyTorch chain, on cos-attention models with a 2-D rope cache under bf16 autocast (fp32 q, k
+    and bf16 v: the real model's dtypes), every layer at every one of the 13 scales."""
+    dev = torch.device("cuda", 0)
+    L, H, C = 2, 16, 2048
+    schedule = synthetic.SCALE_SCHEDULE_1M
+    n_tok = sum(a * b * c for a, b, c in schedule)
+    g = torch.Generator().manual_seed(9)
+    angles = torch.rand(1, 1, 1, n_tok, 64, generator=g) * 6.0
+    freqs = {str(tuple(schedule)): torch.stack([torch.cos(angles), torch.sin(angles)]).to(dev)}
+    orders = synthetic.random_removal_orders(L, H, seed=7)
+    xs = None
+    outs = []
+    for fused in (False, True):
+        torch.manual_seed(0)
+        model = nn.ModuleList([SelfAttention(C, H, True) for _ in range(L)]).to(dev)
+        enable_real_pruning_scale_specific_fused_segmented(
+            model, 0.10, orders, protected_prefix_scales=3, source_scale_start=3,
+            fused_qkv_prep=fused)
+        for m in model:
+            m.kv_caching(True)
+        if xs is None:
+            xs = [[torch.randn(2, h * w, C, device=dev) for _, h, w in schedule] for _ in range(L)]
+        res = []
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            for t in range(len(schedule)):
+                for l, m in enumerate(model):
+                    res.append(m(xs[l][t], None, scale_schedule=schedule, rope2d_freqs_grid=freqs,
+                                 scale_ind=t).float())
+        outs.append(res)
+    assert _native.device_status(dev) == 0
+    for a, b in zip(*outs):
+        err = (a - b).abs().max().item()
+        assert err <= 2e-2 and err / b.abs().max().item() <= 1e-2, err
