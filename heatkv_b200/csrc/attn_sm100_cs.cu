@@ -40,6 +40,7 @@
 #include "common.cuh"
 #include "sm100_util.cuh"
 
+#include <cmath>
 #include <cstdlib>
 
 namespace heatkv {
@@ -782,6 +783,28 @@ static cudaError_t launch_mode(const AttnArgs& a, cudaStream_t st) {
 
 }  // namespace cs
 }  // namespace sm100
+
+// Cost model of an unsplit launch, fitted to the B200 per-target attention times of the 2B image
+// at 2, 4, 8 and 16 rows and the 8B image at 8 rows (13 targets each, both kernels): each
+// kernel's query rows padded to its block height (256 or 128), divided by the wave efficiency of
+// its block count over the SMs (blocks / (waves * SMs)); the column-split kernel's cost per row
+// relative to the two-tile kernel's is 0.85 + 0.29 * min(1, two-tile blocks / 640): lower on small
+// launches (twice the CTAs, two issuers), up to 14 % higher on large ones (both of its softmax
+// warpgroups work on one tile, so their fixed per-tile costs do not overlap). Over those 65
+// launches its choices came within 0.3 % of the per-launch best and left the 2-row image (the
+// headline configuration) entirely on the column-split kernel.
+bool attention_prefers_pair(int64_t batch, int64_t heads, int64_t q_len) {
+  using namespace sm100;
+  const double sms = static_cast<double>(sm_count());
+  auto eff = [sms](double n) { return n / (std::ceil(n / sms) * sms); };
+  const double pair_rows = static_cast<double>((q_len + 255) / 256 * 256);
+  const double cs_rows = static_cast<double>((q_len + 127) / 128 * 128);
+  const double pair_blocks = static_cast<double>(batch * heads) * (pair_rows / 256.0);
+  const double cs_items = static_cast<double>(batch * heads) * (cs_rows / 128.0);
+  if (pair_blocks <= 0.0) return false;
+  const double cs_factor = 0.85 + 0.29 * std::min(1.0, pair_blocks / 640.0);
+  return pair_rows / eff(pair_blocks) < cs_rows * cs_factor / eff(cs_items);
+}
 
 cudaError_t launch_attention_sm100_tf32(const AttnArgs& a, bool v_bf16, cudaStream_t st) {
   return v_bf16 ? sm100::cs::launch_mode<true, true>(a, st)

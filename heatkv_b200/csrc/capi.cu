@@ -235,7 +235,8 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
       const int splits = kv_splits == 0 ? heatkv::attention_auto_splits(batch, heads, q_len)
                                         : kv_splits;
       const int64_t pair_blocks = batch * heads * ((q_len + 255) / 256);
-      split = splits > 1 && workspace != nullptr && unsplit_blocks < pair_blocks;
+      split = (splits > 1 && workspace != nullptr && unsplit_blocks < pair_blocks) ||
+              heatkv::attention_prefers_pair(batch, heads, q_len);
     }
     const bool bf16 = q_dtype == HEATKV_DTYPE_BF16;
     cudaError_t e = (variant == 1 || split) ? heatkv::launch_attention_sm100(a, bf16, st)
