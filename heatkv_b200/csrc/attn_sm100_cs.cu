@@ -26,6 +26,13 @@
 // chain QK -> softmax -> PV of one buffer spans three tiles, so the tensor pipe is fed from the
 // other buffers meanwhile.
 //
+// Independent halves (kIndep, 16-bit mode, two warpgroups): TMEM = S_0 | S_1 | O_0 | O_1 and
+// warpgroup w runs its own online softmax over the keys [64w, 64w+64) of every tile - its own
+// running max and row sum, its P stored inside its own score columns, its own PV (K = 64, the
+// tile's V rows [64w, 64w+64)) into O_w - so the two warpgroups never wait on each other within
+// an item; the halves are merged once per item in the epilogue,
+//   O = (2^(m0-M) O_0 + 2^(m1-M) O_1) / (2^(m0-M) l_0 + 2^(m1-M) l_1),  M = max(m0, m1).
+//
 // CTA roles (kWG * 128 + 128 threads, 1 CTA per SM):
 //   * warps 0 .. 4kWG-1 : softmax warpgroups (and, tf32 mode, Q staging into TMEM); epilogue
 //                          (optionally scattering every row into several full outputs).
@@ -57,16 +64,17 @@ constexpr uint32_t kColO = 384;
 constexpr int kMaxHeads = 128;
 constexpr int kMaxSegTable = 2048;
 
-template <bool kTf32>
+template <bool kTf32, bool kIndep = false>
 struct Mode {
-  static constexpr int kNumS = kTf32 ? 2 : 3;           // S buffers in TMEM
+  static constexpr int kNumS = (kTf32 || kIndep) ? 2 : 3;  // S buffers in TMEM
   static constexpr uint32_t kColS = kTf32 ? 128 : 0;     // first S buffer (Q at 0 in tf32 mode)
+  static constexpr uint32_t kColO0 = kIndep ? 256 : 384;  // O (O_0 and O_1 = +128 if kIndep)
   static constexpr int kKBoxes = kTf32 ? 4 : 2;          // 32 fp32 or 64 16-bit columns a box
   static constexpr uint32_t kKTileBytes = kKBoxes * kBox;
   static constexpr uint32_t kQBytes = kTf32 ? 1024 : 2 * kBox;  // Q in shared memory (16-bit)
 };
 
-template <bool kTf32, int kWG>
+template <bool kTf32, int kWG, bool kIndep = false>
 struct __align__(1024) Smem {
   uint8_t k[2][Mode<kTf32>::kKTileBytes];
   uint8_t v[2][kVTileBytes];
@@ -75,9 +83,9 @@ struct __align__(1024) Smem {
   uint64_t q_empty;    // 16-bit mode: the item's last QK has completed (Q may be overwritten)
   uint64_t k_full[2];
   uint64_t v_full[2];
-  uint64_t s_full[Mode<kTf32>::kNumS];   // QK(g) done: scores in S buffer g % kNumS
-  uint64_t p_full[Mode<kTf32>::kNumS];   // every softmax warp stored P(g) over its S buffer
-  uint64_t pv_done[Mode<kTf32>::kNumS];  // PV(g) done: V stage g % 2, S buffer free, O has tile g
+  uint64_t s_full[Mode<kTf32, kIndep>::kNumS];     // QK(g) done: scores in S buffer g % kNumS
+  uint64_t p_full[Mode<kTf32, kIndep>::kNumS][2];  // P(g) stored (kIndep: per warpgroup)
+  uint64_t pv_done[Mode<kTf32, kIndep>::kNumS];    // PV(g) done: V stage g % 2, S buffer free
   uint64_t o_final;    // the item's last PV has completed
   uint64_t o_free;     // every softmax warp has read the item's O
   uint64_t drain;      // both issuers' products have completed
@@ -85,6 +93,7 @@ struct __align__(1024) Smem {
   int abort_flag;
   float red_max[2][kWG][kBM];  // [tile parity][warpgroup][row]: part-row maxima
   float red_sum[kWG][kBM];     // [warpgroup][row]: part-row sums of an item
+  float2 red_ml[2][2][kBM];    // kIndep: [item parity][warpgroup][row] (running max, row sum)
   int head_order[kMaxHeads];
   int head_nseg[kMaxHeads];
   int head_tiles[kMaxHeads];
@@ -194,15 +203,16 @@ __device__ __forceinline__ void named_bar_softmax_wg() {
   asm volatile("bar.sync 1, %0;" ::"n"(kWG * 128) : "memory");
 }
 
-template <bool kTf32, bool kBF16, int kWG>
+template <bool kTf32, bool kBF16, int kWG, bool kIndep>
 __global__ void __launch_bounds__(kWG * 128 + 128, 1)
     attn_sm100_cs_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_ck,
                          const __grid_constant__ CUtensorMap tm_cv,
                          const __grid_constant__ CUtensorMap tm_sk,
                          const __grid_constant__ CUtensorMap tm_sv, const Params p) {
-  using M = Mode<kTf32>;
-  using SmemT = Smem<kTf32, kWG>;
+  static_assert(!kIndep || (!kTf32 && kWG == 2), "independent halves: 16-bit, two warpgroups");
+  using M = Mode<kTf32, kIndep>;
+  using SmemT = Smem<kTf32, kWG, kIndep>;
   constexpr int kNumS = M::kNumS;
   constexpr uint32_t kColS = M::kColS;
   constexpr int kCols = kBN / kWG;        // score (and O) columns of one warpgroup
@@ -240,7 +250,8 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
     }
     for (int b = 0; b < kNumS; ++b) {
       mbar_init(&sm.s_full[b], 1);
-      mbar_init(&sm.p_full[b], kSoftmaxWarps);
+      mbar_init(&sm.p_full[b][0], kIndep ? 4 : kSoftmaxWarps);
+      mbar_init(&sm.p_full[b][1], 4);
       mbar_init(&sm.pv_done[b], 1);
     }
     mbar_init(&sm.o_final, 1);
@@ -438,19 +449,40 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
         }
         __syncwarp();
         if (lane == 0) {
-          ok = mbar_wait(&sm.p_full[b], (g / kNumS) & 1, abort_flag, p.status);
-          if (ok && j == 0 && ocnt > 0) ok = mbar_wait(&sm.o_free, (ocnt - 1) & 1, abort_flag, p.status);
-          if (ok) {
-            tc_fence_after();
-            // O += P V: A = P (16-bit pairs over S_b), B = V tile, MN-major SW128: 8-key groups
-            // 1 KiB apart (SBO), the two 64-column halves 16 KiB apart (LBO)
-            const uint32_t vbase = smem_u32(sm.v[vs]);
-            const uint32_t a = tmem + kColS + b * 128;
+          // O += P V: A = P (16-bit pairs in TMEM), B = V tile, MN-major SW128: 8-key groups
+          // 1 KiB apart (SBO), the two 64-column halves 16 KiB apart (LBO); 16 keys a step
+          const uint32_t vbase = smem_u32(sm.v[vs]);
+          const uint32_t a = tmem + kColS + b * 128;
+          if constexpr (kIndep) {
+            // each half as soon as its warpgroup has stored it: keys [64w, 64w+64) (P in pair
+            // columns [64w, 64w+32) of S_b) into O_w
 #pragma unroll
-            for (int kk = 0; kk < kBN / 16; ++kk) {
-              const uint64_t bdesc = smem_desc_sw128(vbase + kk * 2048, kBox, 1024);
-              umma_ts(tmem + kColO, a + kk * 8, bdesc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+            for (int w = 0; w < 2 && ok; ++w) {
+              ok = mbar_wait(&sm.p_full[b][w], (g / kNumS) & 1, abort_flag, p.status);
+              if (ok && w == 0 && j == 0 && ocnt > 0)
+                ok = mbar_wait(&sm.o_free, (ocnt - 1) & 1, abort_flag, p.status);
+              if (!ok) break;
+              tc_fence_after();
+#pragma unroll
+              for (int kk = 4 * w; kk < 4 * w + 4; ++kk) {
+                const uint64_t bdesc = smem_desc_sw128(vbase + kk * 2048, kBox, 1024);
+                umma_ts(tmem + M::kColO0 + 128 * w, a + 64 * w + (kk - 4 * w) * 8, bdesc,
+                        idesc_pv, (j > 0 || kk > 4 * w) ? 1u : 0u);
+              }
             }
+          } else {
+            ok = mbar_wait(&sm.p_full[b][0], (g / kNumS) & 1, abort_flag, p.status);
+            if (ok && j == 0 && ocnt > 0) ok = mbar_wait(&sm.o_free, (ocnt - 1) & 1, abort_flag, p.status);
+            if (ok) {
+              tc_fence_after();
+#pragma unroll
+              for (int kk = 0; kk < kBN / 16; ++kk) {
+                const uint64_t bdesc = smem_desc_sw128(vbase + kk * 2048, kBox, 1024);
+                umma_ts(tmem + kColO, a + kk * 8, bdesc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
+          }
+          if (ok) {
             tc_commit(&sm.pv_done[b]);
             if (j == it.n - 1) tc_commit(&sm.o_final);
           }
@@ -472,7 +504,9 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
     const int row = quad * 32 + lane;  // TMEM lane == query row
     const int c0 = w * kCols;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t tO = tmem + lane_off + kColO + c0;
+    // O columns this thread rescales: its warpgroup's share of O, or (kIndep) all of O_w
+    const uint32_t tO = kIndep ? tmem + lane_off + M::kColO0 + 128 * w : tmem + lane_off + kColO + c0;
+    constexpr int kOCols = kIndep ? 128 : kCols;
     const float c = p.scale_log2;
     // tf32 mode: Q rows of an item -> TMEM (this warpgroup's columns), zero past Lq
     auto load_q = [&](int item) {
@@ -533,14 +567,16 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
           }
           mx = row_max<kCols>(x) * c;
         }
-        sm.red_max[g & 1][w][row] = mx;
-        // every warpgroup's scores are in its registers before P is stored over them
-        tc_fence_before();
-        named_bar_softmax_wg<kWG>();
-        tc_fence_after();
-        mx = sm.red_max[g & 1][0][row];
+        if constexpr (!kIndep) {
+          sm.red_max[g & 1][w][row] = mx;
+          // every warpgroup's scores are in its registers before P is stored over them
+          tc_fence_before();
+          named_bar_softmax_wg<kWG>();
+          tc_fence_after();
+          mx = sm.red_max[g & 1][0][row];
 #pragma unroll
-        for (int v = 1; v < kWG; ++v) mx = fmaxf(mx, sm.red_max[g & 1][v][row]);
+          for (int v = 1; v < kWG; ++v) mx = fmaxf(mx, sm.red_max[g & 1][v][row]);
+        }
         if (ok) {
           float alpha = 1.f;
           bool rescale = false;
@@ -554,7 +590,10 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
             rescale = true;
           }
           const uint64_t c2 = f2pack(c, c);
-          const uint64_t nm2 = f2pack(-m_run, -m_run);
+          // kIndep: a warpgroup whose keys of the item so far are all masked has m = -inf; its
+          // P must be 0, not 2^(-inf + inf)
+          const float msub = (kIndep && m_run == -INFINITY) ? 0.f : m_run;
+          const uint64_t nm2 = f2pack(-msub, -msub);
           uint64_t acc[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k) acc[k] = f2pack(0.f, 0.f);
@@ -572,8 +611,9 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
               acc[pi & 3] = add2(acc[pi & 3], f2pack(p0, p1));
               pk[i] = pack2<kBF16>(p0, p1);
             }
-            // P of keys [c0 + 32 part, +32) -> 16-bit pair columns [c0/2 + 16 part, +16)
-            tmem_st16(tS + c0 / 2 + 16 * part, pk);
+            // P of keys [c0 + 32 part, +32) -> 16-bit pair columns [c0/2 + 16 part, +16), or
+            // (kIndep) inside this warpgroup's own score columns, [c0 + 16 part, +16)
+            tmem_st16(tS + (kIndep ? c0 : c0 / 2) + 16 * part, pk);
           }
           const uint64_t s01 = add2(acc[0], acc[1]);
           const uint64_t s23 = add2(acc[2], acc[3]);
@@ -586,7 +626,7 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
             if (ok) {
               tc_fence_after();
 #pragma unroll
-              for (int cc = 0; cc < kCols / 16; ++cc) {
+              for (int cc = 0; cc < kOCols / 16; ++cc) {
                 float o[16];
                 tmem_ld16_sync(tO + cc * 16, o);
                 uint32_t wv[16];
@@ -599,7 +639,7 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.p_full[b]);
+          if (lane == 0) mbar_arrive(&sm.p_full[b][kIndep ? w : 0]);
         }
         cur.next();
       }
@@ -607,11 +647,23 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
       // item's Q now, so its first QK overlaps this item's last PV and the epilogue
       const int next = item + gridDim.x;
       if (kTf32 && ok && next < p.n_items) load_q(next);
-      sm.red_sum[w][row] = l_run;
-      named_bar_softmax_wg<kWG>();
-      float l_tot = sm.red_sum[0][row];
+      float l_tot, a0 = 1.f, a1 = 0.f;
+      if constexpr (kIndep) {
+        // merge weights of the two halves; WG0's max is finite (key 0 of every tile is valid)
+        sm.red_ml[ocnt & 1][w][row] = make_float2(m_run, l_run);
+        named_bar_softmax_wg<kWG>();
+        const float2 h0 = sm.red_ml[ocnt & 1][0][row], h1 = sm.red_ml[ocnt & 1][1][row];
+        const float mm = fmaxf(h0.x, h1.x);
+        a0 = h0.x == -INFINITY ? 0.f : ex2(h0.x - mm);
+        a1 = h1.x == -INFINITY ? 0.f : ex2(h1.x - mm);
+        l_tot = h0.y * a0 + h1.y * a1;
+      } else {
+        sm.red_sum[w][row] = l_run;
+        named_bar_softmax_wg<kWG>();
+        l_tot = sm.red_sum[0][row];
 #pragma unroll
-      for (int v = 1; v < kWG; ++v) l_tot += sm.red_sum[v][row];
+        for (int v = 1; v < kWG; ++v) l_tot += sm.red_sum[v][row];
+      }
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.o_final, ocnt & 1, abort_flag, p.status));
       if (ok) {
         tc_fence_after();
@@ -627,29 +679,55 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
           off = ((int64_t(grow) * Lq + qrow) * p.out_heads_total + ghead) * kD + c0;
           n_dst = p.n_out;
         }
-        float o[kCols];
-        tmem_ld_cols<kCols>(tO, o);  // this warpgroup's O columns in one load
-        if (qrow < Lq && in_range) {
+        const bool write = qrow < Lq && in_range;
+        // 16 output columns [col, col + 16) of this row (already normalised)
+        auto store16 = [&](int col, const float* v) {
+          if constexpr (kTf32) {
+            float4* d4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off + col);
 #pragma unroll
-          for (int cc = 0; cc < kCols / 16; ++cc) {
-            if constexpr (kTf32) {
-              float4* d4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off + cc * 16);
+            for (int i = 0; i < 4; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          } else {
+            uint32_t wv[8];
 #pragma unroll
-              for (int i = 0; i < 4; ++i)
-                d4[i] = make_float4(o[cc * 16 + 4 * i] * inv, o[cc * 16 + 4 * i + 1] * inv,
-                                    o[cc * 16 + 4 * i + 2] * inv, o[cc * 16 + 4 * i + 3] * inv);
-            } else {
-              uint32_t wv[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i)
-                wv[i] = pack2<kBF16>(o[cc * 16 + 2 * i] * inv, o[cc * 16 + 2 * i + 1] * inv);
+            for (int i = 0; i < 8; ++i) wv[i] = pack2<kBF16>(v[2 * i], v[2 * i + 1]);
 #pragma unroll 1
-              for (int r = 0; r < n_dst; ++r) {
-                OutT* base = p.n_out > 0 ? static_cast<OutT*>(p.out_ptrs[r]) : static_cast<OutT*>(p.out);
-                uint4* dst = reinterpret_cast<uint4*>(base + off + cc * 16);
-                dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-                dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+            for (int r = 0; r < n_dst; ++r) {
+              OutT* base = p.n_out > 0 ? static_cast<OutT*>(p.out_ptrs[r]) : static_cast<OutT*>(p.out);
+              uint4* dst = reinterpret_cast<uint4*>(base + off + col);
+              dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+              dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+            }
+          }
+        };
+        if constexpr (kIndep) {
+          // output columns [c0, c0 + 64) = the merge of O_0 and O_1 there
+          const float w0 = a0 * inv, w1 = a1 * inv;
+          const uint32_t tA = tmem + lane_off + M::kColO0 + c0;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            float o0[32], o1[32];
+            tmem_ld32_sync(tA + 32 * half, o0);
+            tmem_ld32_sync(tA + 128 + 32 * half, o1);
+            if (write) {
+#pragma unroll
+              for (int cc = 0; cc < 2; ++cc) {
+                float v[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[i] = fmaf(o0[cc * 16 + i], w0, o1[cc * 16 + i] * w1);
+                store16(32 * half + 16 * cc, v);
               }
+            }
+          }
+        } else {
+          float o[kCols];
+          tmem_ld_cols<kCols>(tO, o);  // this warpgroup's O columns in one load
+          if (write) {
+#pragma unroll
+            for (int cc = 0; cc < kCols / 16; ++cc) {
+              float v[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] = o[cc * 16 + i] * inv;
+              store16(16 * cc, v);
             }
           }
         }
@@ -697,13 +775,23 @@ static int softmax_warpgroups() {
   return v;
 }
 
-template <bool kTf32, bool kBF16, int kWG>
+// 16-bit mode: independent halves (default) or one O shared by the warpgroups
+// (HEATKV_CS_INDEPENDENT = 0; 2-5 % slower, kept for measurement).
+static bool independent_halves() {
+  static const bool v = [] {
+    const char* e = getenv("HEATKV_CS_INDEPENDENT");
+    return !(e && atoi(e) == 0);
+  }();
+  return v;
+}
+
+template <bool kTf32, bool kBF16, int kWG, bool kIndep = false>
 static cudaError_t launch_t(const CUtensorMap& tq, const CUtensorMap& tck, const CUtensorMap& tcv,
                             const CUtensorMap& tsk, const CUtensorMap& tsv, const Params& p,
                             cudaStream_t st) {
-  auto kern = attn_sm100_cs_kernel<kTf32, kBF16, kWG>;
-  const int smem = static_cast<int>(sizeof(Smem<kTf32, kWG>)) + 1024;
-  static_assert(sizeof(Smem<kTf32, kWG>) + 1024 <= 227 * 1024, "shared memory of one CTA");
+  auto kern = attn_sm100_cs_kernel<kTf32, kBF16, kWG, kIndep>;
+  const int smem = static_cast<int>(sizeof(Smem<kTf32, kWG, kIndep>)) + 1024;
+  static_assert(sizeof(Smem<kTf32, kWG, kIndep>) + 1024 <= 227 * 1024, "shared memory of one CTA");
   // opt in to >48 KiB dynamic shared memory once per device (never inside a graph capture)
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -778,6 +866,9 @@ static cudaError_t launch_mode(const AttnArgs& a, cudaStream_t st) {
   p.out_batch = static_cast<int>(a.out_batch);
   p.out_heads_total = static_cast<int>(a.out_heads_total);
   if (softmax_warpgroups() == 4) return launch_t<kTf32, kBF16, 4>(tq, tck, tcv, tsk, tsv, p, st);
+  if constexpr (!kTf32) {
+    if (independent_halves()) return launch_t<false, kBF16, 2, true>(tq, tck, tcv, tsk, tsv, p, st);
+  }
   return launch_t<kTf32, kBF16, 2>(tq, tck, tcv, tsk, tsv, p, st);
 }
 
@@ -788,11 +879,11 @@ static cudaError_t launch_mode(const AttnArgs& a, cudaStream_t st) {
 // at 2, 4, 8 and 16 rows and the 8B image at 8 rows (13 targets each, both kernels): each
 // kernel's query rows padded to its block height (256 or 128), divided by the wave efficiency of
 // its block count over the SMs (blocks / (waves * SMs)); the column-split kernel's cost per row
-// relative to the two-tile kernel's is 0.85 + 0.29 * min(1, two-tile blocks / 640): lower on small
-// launches (twice the CTAs, two issuers), up to 14 % higher on large ones (both of its softmax
-// warpgroups work on one tile, so their fixed per-tile costs do not overlap). Over those 65
-// launches its choices came within 0.3 % of the per-launch best and left the 2-row image (the
-// headline configuration) entirely on the column-split kernel.
+// relative to the two-tile kernel's is 0.80 + 0.28 * min(1, two-tile blocks / 512): lower on small
+// launches (twice the CTAs, two issuers), up to 8 % higher on large ones (128-row items read each
+// K/V tile for half the rows). Over those 65 launches its choices came within 0.3 % of the
+// per-launch best and leave the 2-row image (the headline configuration) entirely on the
+// column-split kernel.
 bool attention_prefers_pair(int64_t batch, int64_t heads, int64_t q_len) {
   using namespace sm100;
   const double sms = static_cast<double>(sm_count());
@@ -802,7 +893,7 @@ bool attention_prefers_pair(int64_t batch, int64_t heads, int64_t q_len) {
   const double pair_blocks = static_cast<double>(batch * heads) * (pair_rows / 256.0);
   const double cs_items = static_cast<double>(batch * heads) * (cs_rows / 128.0);
   if (pair_blocks <= 0.0) return false;
-  const double cs_factor = 0.85 + 0.29 * std::min(1.0, pair_blocks / 640.0);
+  const double cs_factor = 0.80 + 0.28 * std::min(1.0, pair_blocks / 512.0);
   return pair_rows / eff(pair_blocks) < cs_rows * cs_factor / eff(cs_items);
 }
 
