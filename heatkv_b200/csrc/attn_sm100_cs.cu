@@ -325,14 +325,16 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
       for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
         const Item it = decode_item(sm, p, item);
         const int bh = it.b * H + it.h;
-        if (!kTf32 && loads_k) {
-          // Q rows of the item once the previous item's last QK has completed; rows past the
-          // tensor are zero-filled, rows past Lq of this head are never written out
-          if (qcnt > 0 && !(ok = mbar_wait(&sm.q_empty, (qcnt - 1) & 1, abort_flag, p.status))) break;
-          mbar_arrive_expect_tx(&sm.q_full, 2 * kBox);
-          tma_load_2d(sm.q, &tm_q, 0, bh * Lq + it.q0, &sm.q_full);
-          tma_load_2d(sm.q + kBox, &tm_q, 64, bh * Lq + it.q0, &sm.q_full);
-          ++qcnt;
+        if constexpr (!kTf32) {
+          if (loads_k) {
+            // Q rows of the item once the previous item's last QK has completed; rows past the
+            // tensor are zero-filled, rows past Lq of this head are never written out
+            if (qcnt > 0 && !(ok = mbar_wait(&sm.q_empty, (qcnt - 1) & 1, abort_flag, p.status))) break;
+            mbar_arrive_expect_tx(&sm.q_full, 2 * kBox);
+            tma_load_2d(sm.q, &tm_q, 0, bh * Lq + it.q0, &sm.q_full);
+            tma_load_2d(sm.q + kBox, &tm_q, 64, bh * Lq + it.q0, &sm.q_full);
+            ++qcnt;
+          }
         }
         const int cur_row0 = bh * Lq;
         const int slab_row0 = static_cast<int>(int64_t(it.b) * p.capacity);
