@@ -24,6 +24,7 @@ DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
 ATTN_AUTO, ATTN_EXACT, ATTN_TCGEN05, ATTN_TCGEN05_PAIR, ATTN_TCGEN05_CS = 0, 1, 2, 3, 4
 ATTN_STATIC_META = 0x100  # OR into a selector: metadata not written by preceding work
+RUN_EXACT, RUN_TCGEN05_PAIR, RUN_TCGEN05_CS, RUN_TCGEN05_TF32 = 1, 2, 3, 4  # heatkv_attn_run
 
 DEVICE_PACK_OUT_OF_RANGE = 0x1
 DEVICE_WAIT_TIMEOUT = 0x2
@@ -64,6 +65,7 @@ SIGNATURES = {
                                                 _i, _i, _p, _i, _p]),
     "heatkv_gather_head_shards": (_i, [_p, _p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                        _p, _p, _p]),
+    "heatkv_attention_kernel_for": (_i, [_i, _i, _i, _i64, _i64, _i64, _i, _i, _i, _i64]),
     "heatkv_qkv_prepare": (_i, [_p, _p, _p, _p, _i, _i, _i64, _i64, _i64, _i64, _p,
                                 ctypes.c_float, _p, _p, _i64, _p]),
     "heatkv_device_status": (_i, [ctypes.POINTER(ctypes.c_uint32), _i, _p]),

@@ -149,6 +149,60 @@ struct Scatter {
   int64_t out_batch, out_heads_total;
 };
 
+struct AttnPlan {
+  int run;      // heatkv_attn_run
+  bool strict;  // a tensor-core kernel was asked for: no fallback to the exact kernel
+};
+
+// The kernel an attention call runs, from its dtypes, sizes and selector (the launch itself may
+// still find its shape outside a tensor-core kernel's limits; see attention_impl).
+static int plan_attention(int q_dtype, int k_dtype, int v_dtype, int64_t batch, int64_t heads,
+                          int64_t q_len, int kernel, int kv_splits, bool has_workspace,
+                          int64_t unsplit_blocks, bool scatter, AttnPlan* out) {
+  kernel &= ~HEATKV_ATTN_STATIC_META;
+  if (kernel < HEATKV_ATTN_AUTO || kernel > HEATKV_ATTN_TCGEN05_CS)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: unknown kernel selector");
+  // the two-tile or column-split variant asked for by name; otherwise HEATKV_TCGEN05_VARIANT
+  const int variant = kernel == HEATKV_ATTN_TCGEN05_PAIR ? 1
+                    : kernel == HEATKV_ATTN_TCGEN05_CS   ? 2
+                                                         : heatkv::tcgen05_variant();
+  const bool named_pair = kernel == HEATKV_ATTN_TCGEN05_PAIR;
+  if (kernel == HEATKV_ATTN_TCGEN05_PAIR || kernel == HEATKV_ATTN_TCGEN05_CS)
+    kernel = HEATKV_ATTN_TCGEN05;
+  const bool same16 = (q_dtype == k_dtype && k_dtype == v_dtype && q_dtype != HEATKV_DTYPE_F32);
+  // fp32 q and k with 16-bit v (the real model's dtypes): tf32 QK, P rounded to v's dtype
+  const bool qk32 = (q_dtype == HEATKV_DTYPE_F32 && k_dtype == HEATKV_DTYPE_F32 &&
+                     v_dtype != HEATKV_DTYPE_F32);
+  if (named_pair && !same16)
+    return fail(HEATKV_ERR_UNSUPPORTED,
+                "the two-tile tcgen05 kernel needs q, k and v all bfloat16 or all float16");
+  if (kernel == HEATKV_ATTN_TCGEN05 && !same16 && !(qk32 && !scatter))
+    return fail(HEATKV_ERR_UNSUPPORTED,
+                "tcgen05 segmented attention needs q, k and v all bfloat16 or all float16, or q "
+                "and k float32 with 16-bit v");
+  out->strict = kernel == HEATKV_ATTN_TCGEN05;
+  if (kernel != HEATKV_ATTN_EXACT && qk32 && !scatter) {
+    out->run = HEATKV_RUN_TCGEN05_TF32;
+  } else if (kernel != HEATKV_ATTN_EXACT && same16) {
+    // key-range splits exist only in the two-tile kernel; otherwise the cost model chooses
+    bool pair = variant == 1;
+    if (variant == 0) {
+      const int splits = kv_splits == 0 ? heatkv::attention_auto_splits(batch, heads, q_len)
+                                        : kv_splits;
+      const int64_t pair_blocks = batch * heads * ((q_len + 255) / 256);
+      pair = (splits > 1 && has_workspace && unsplit_blocks < pair_blocks) ||
+             heatkv::attention_prefers_pair(batch, heads, q_len);
+    }
+    out->run = pair ? HEATKV_RUN_TCGEN05_PAIR : HEATKV_RUN_TCGEN05_CS;
+  } else {
+    if (scatter)
+      return fail(HEATKV_ERR_UNSUPPORTED,
+                  "heatkv_segmented_attention_scatter needs q, k and v all bfloat16 or all float16");
+    out->run = HEATKV_RUN_EXACT;
+  }
+  return HEATKV_OK;
+}
+
 static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
                           const int32_t* seg_starts, const int32_t* seg_ends,
                           const int32_t* seg_counts, const void* cur_k, const void* cur_v, void* out,
@@ -179,16 +233,10 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
   if (heads > 65535 || batch > 65535 || (q_len + 63) / 64 > 0x7fffffffLL)
     return fail(HEATKV_ERR_UNSUPPORTED, "real_scale_fused_segmented: grid too large");
   const bool static_meta = (kernel & HEATKV_ATTN_STATIC_META) != 0;
-  kernel &= ~HEATKV_ATTN_STATIC_META;
-  if (kernel < HEATKV_ATTN_AUTO || kernel > HEATKV_ATTN_TCGEN05_CS)
-    return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: unknown kernel selector");
-  // the two-tile or column-split variant asked for by name; otherwise HEATKV_TCGEN05_VARIANT
-  const int forced_variant = kernel == HEATKV_ATTN_TCGEN05_PAIR ? 1
-                           : kernel == HEATKV_ATTN_TCGEN05_CS   ? 2
-                                                                : heatkv::tcgen05_variant();
-  const bool named_pair = kernel == HEATKV_ATTN_TCGEN05_PAIR;
-  if (kernel == HEATKV_ATTN_TCGEN05_PAIR || kernel == HEATKV_ATTN_TCGEN05_CS)
-    kernel = HEATKV_ATTN_TCGEN05;
+  AttnPlan plan;
+  int rc = plan_attention(q_dtype, k_dtype, v_dtype, batch, heads, q_len, kernel, kv_splits,
+                          workspace != nullptr, unsplit_blocks, scatter != nullptr, &plan);
+  if (rc != HEATKV_OK) return rc;
 
   heatkv::AttnArgs a{q,     slab_k,        slab_v, seg_starts, seg_ends, seg_counts, cur_k,
                      cur_v, out,           batch,  heads,      q_len,    capacity,   max_segments,
@@ -209,51 +257,42 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
     a.out_heads_total = scatter->out_heads_total;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool same16 = (q_dtype == k_dtype && k_dtype == v_dtype && q_dtype != HEATKV_DTYPE_F32);
-  // fp32 q and k with 16-bit v (the real model's dtypes): tf32 QK, P rounded to v's dtype
-  const bool qk32 = (q_dtype == HEATKV_DTYPE_F32 && k_dtype == HEATKV_DTYPE_F32 &&
-                     v_dtype != HEATKV_DTYPE_F32);
-  if (named_pair && !same16)
-    return fail(HEATKV_ERR_UNSUPPORTED,
-                "the two-tile tcgen05 kernel needs q, k and v all bfloat16 or all float16");
-  if (kernel == HEATKV_ATTN_TCGEN05 && !same16 && !(qk32 && !scatter))
-    return fail(HEATKV_ERR_UNSUPPORTED,
-                "tcgen05 segmented attention needs q, k and v all bfloat16 or all float16, or q "
-                "and k float32 with 16-bit v");
-  if (kernel != HEATKV_ATTN_EXACT && qk32 && !scatter) {
+  if (plan.run == HEATKV_RUN_TCGEN05_TF32) {
     cudaError_t e = heatkv::launch_attention_sm100_tf32(a, v_dtype == HEATKV_DTYPE_BF16, st);
     if (e == cudaSuccess) return HEATKV_OK;
-    if (e != cudaErrorNotSupported || kernel == HEATKV_ATTN_TCGEN05)
+    if (e != cudaErrorNotSupported || plan.strict)
       return cuda_fail(e, "tcgen05 tf32 segmented attention launch");
-  }
-  if (kernel != HEATKV_ATTN_EXACT && same16) {
-    // key-range splits exist only in the two-Q-tile kernel; every other call takes the
-    // column-split kernel (HEATKV_TCGEN05_VARIANT = pair | cs forces one)
-    const int variant = forced_variant;
-    bool split = false;
-    if (variant == 0) {
-      const int splits = kv_splits == 0 ? heatkv::attention_auto_splits(batch, heads, q_len)
-                                        : kv_splits;
-      const int64_t pair_blocks = batch * heads * ((q_len + 255) / 256);
-      split = (splits > 1 && workspace != nullptr && unsplit_blocks < pair_blocks) ||
-              heatkv::attention_prefers_pair(batch, heads, q_len);
-    }
+  } else if (plan.run == HEATKV_RUN_TCGEN05_PAIR || plan.run == HEATKV_RUN_TCGEN05_CS) {
     const bool bf16 = q_dtype == HEATKV_DTYPE_BF16;
-    cudaError_t e = (variant == 1 || split) ? heatkv::launch_attention_sm100(a, bf16, st)
-                                            : heatkv::launch_attention_sm100_cs(a, bf16, st);
+    cudaError_t e = plan.run == HEATKV_RUN_TCGEN05_PAIR
+                        ? heatkv::launch_attention_sm100(a, bf16, st)
+                        : heatkv::launch_attention_sm100_cs(a, bf16, st);
     if (e == cudaSuccess) return HEATKV_OK;
     if (e == cudaErrorNotSupported && scatter)
       return fail(HEATKV_ERR_UNSUPPORTED,
                   "heatkv_segmented_attention_scatter: these sizes need the split or exact path");
-    if (e != cudaErrorNotSupported || kernel == HEATKV_ATTN_TCGEN05)
+    if (e != cudaErrorNotSupported || plan.strict)
       return cuda_fail(e, "tcgen05 segmented attention launch");
   }
-  if (scatter)
-    return fail(HEATKV_ERR_UNSUPPORTED,
-                "heatkv_segmented_attention_scatter needs q, k and v all bfloat16 or all float16");
+  // the exact kernel: asked for, or the fallback of an automatic choice
   cudaError_t e = heatkv::launch_attention_simt(a, q_dtype, k_dtype, v_dtype, st);
   if (e != cudaSuccess) return cuda_fail(e, "segmented attention launch");
   return HEATKV_OK;
+}
+
+int heatkv_attention_kernel_for(int q_dtype, int k_dtype, int v_dtype, int64_t batch,
+                                int64_t heads, int64_t q_len, int kernel, int kv_splits,
+                                int has_workspace, int64_t unsplit_blocks) {
+  g_last_error.clear();
+  if (!valid_dtype(q_dtype) || !valid_dtype(k_dtype) || !valid_dtype(v_dtype))
+    return fail(HEATKV_ERR_UNSUPPORTED,
+                "real_scale_fused_segmented supports only float16, bfloat16, or float32 tensors");
+  if (batch < 0 || heads <= 0 || q_len <= 0 || kv_splits < 0)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_attention_kernel_for: invalid sizes");
+  AttnPlan plan;
+  const int rc = plan_attention(q_dtype, k_dtype, v_dtype, batch, heads, q_len, kernel, kv_splits,
+                                has_workspace != 0, unsplit_blocks, false, &plan);
+  return rc != HEATKV_OK ? rc : plan.run;
 }
 
 int heatkv_segmented_attention(const void* q, const void* slab_k, const void* slab_v,

@@ -70,6 +70,14 @@ typedef enum {
   HEATKV_ATTN_TCGEN05_CS = 4    /* the column-split tcgen05 kernel; never splits key ranges */
 } heatkv_attn_kernel;
 
+/* The kernel an attention call runs (heatkv_attention_kernel_for). */
+typedef enum {
+  HEATKV_RUN_EXACT = 1,         /* attn_simt_kernel: CUDA cores, fp32 products */
+  HEATKV_RUN_TCGEN05_PAIR = 2,  /* attn_sm100_kernel: two 128-row query tiles per CTA */
+  HEATKV_RUN_TCGEN05_CS = 3,    /* attn_sm100_cs_kernel, 16-bit mode */
+  HEATKV_RUN_TCGEN05_TF32 = 4   /* attn_sm100_cs_kernel, tf32 mode (fp32 q/k, 16-bit v) */
+} heatkv_attn_run;
+
 /* OR into the kernel selector: the segment metadata (starts, ends, counts) and the head order are
  * not written by the work that precedes the call in the stream (e.g. uploaded once at install),
  * so the column-split kernel may stage them while the preceding kernel is still running. */
@@ -307,6 +315,19 @@ int heatkv_gather_head_shards(void* dst, const void* src, int dtype, int64_t wor
                               int64_t rows_per_rank, int64_t q_len, int64_t heads_per_rank,
                               int64_t batch, int64_t heads, int64_t head_dim,
                               const int32_t* row_map, const int32_t* head_map, void* stream);
+
+/*
+ * heatkv_attention_kernel_for - the kernel (heatkv_attn_run, > 0) that heatkv_segmented_attention
+ * _ws / _sched would run with these dtypes, sizes, selector (HEATKV_ATTN_STATIC_META allowed),
+ * kv_splits, workspace presence (has_workspace != 0) and unsplit_blocks; a negative
+ * heatkv_status for arguments such a call rejects. It assumes 16-byte aligned tensors and shapes
+ * within the tensor-core kernels' limits (heads <= 128, heads * max_segments <= 2048, fewer than
+ * 2^31 rows); under HEATKV_ATTN_AUTO a call outside them runs the exact kernel instead. No device
+ * is needed.
+ */
+int heatkv_attention_kernel_for(int q_dtype, int k_dtype, int v_dtype, int64_t batch,
+                                int64_t heads, int64_t q_len, int kernel, int kv_splits,
+                                int has_workspace, int64_t unsplit_blocks);
 
 /*
  * heatkv_qkv_prepare - the q/k/v preparation of the patched attention forward between the QKV

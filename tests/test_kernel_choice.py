@@ -1,0 +1,67 @@
+"""Which attention kernel a call runs (heatkv_attention_kernel_for, no GPU needed): dtype routing
+as the reference's dot modes imply it, the kernel selectors, key-range splits, and the cost model
+that chooses between the column-split and two-tile tcgen05 kernels for unsplit 16-bit calls."""
+
+import pytest
+
+from heatkv_b200 import _native
+
+F32, F16, BF16 = 0, 1, 2
+AUTO, EXACT, TC, PAIR, CS = (_native.ATTN_AUTO, _native.ATTN_EXACT, _native.ATTN_TCGEN05,
+                             _native.ATTN_TCGEN05_PAIR, _native.ATTN_TCGEN05_CS)
+
+
+def run(dt=(BF16, BF16, BF16), batch=2, heads=16, q_len=4096, kernel=AUTO, splits=1, ws=0,
+        unsplit=0):
+    return _native.load().heatkv_attention_kernel_for(*dt, batch, heads, q_len, kernel, splits, ws,
+                                                      unsplit)
+
+
+def test_two_row_image_stays_on_the_column_split_kernel():
+    for lq in (1, 4, 16, 36, 64, 144, 256, 400, 576, 1024, 1600, 2304, 4096):
+        assert run(q_len=lq) == _native.RUN_TCGEN05_CS, lq
+
+
+def test_large_launches_take_the_two_tile_kernel():
+    assert run(batch=16, q_len=4096) == _native.RUN_TCGEN05_PAIR
+    assert run(batch=8, heads=28, q_len=2304) == _native.RUN_TCGEN05_PAIR
+    # padded 256-row blocks lose: Lq 1600 stays on the column split at 16 rows
+    assert run(batch=16, q_len=1600) == _native.RUN_TCGEN05_CS
+    assert run(batch=16, q_len=64) == _native.RUN_TCGEN05_CS
+
+
+def test_key_range_splits_need_the_two_tile_kernel_and_a_workspace():
+    assert run(splits=2, ws=1) == _native.RUN_TCGEN05_PAIR
+    assert run(splits=2, ws=0) == _native.RUN_TCGEN05_CS
+    blocks = 2 * 16 * 16
+    assert run(splits=2, ws=1, unsplit=blocks) == _native.RUN_TCGEN05_CS  # nothing left to split
+
+
+def test_named_variants_and_the_static_metadata_flag():
+    assert run(kernel=PAIR) == _native.RUN_TCGEN05_PAIR
+    assert run(batch=16, kernel=CS) == _native.RUN_TCGEN05_CS
+    assert run(kernel=AUTO | _native.ATTN_STATIC_META) == _native.RUN_TCGEN05_CS
+    assert run(kernel=EXACT) == _native.RUN_EXACT
+
+
+def test_dtype_routing():
+    # fp32 q/k with 16-bit v (the real model under autocast): tf32 scores on tensor cores
+    assert run(dt=(F32, F32, BF16)) == _native.RUN_TCGEN05_TF32
+    assert run(dt=(F32, F32, F16), kernel=TC) == _native.RUN_TCGEN05_TF32
+    assert run(dt=(F32, F32, BF16), kernel=EXACT) == _native.RUN_EXACT
+    # every other mix, and all-fp32, on the exact kernel
+    assert run(dt=(F32, F32, F32)) == _native.RUN_EXACT
+    assert run(dt=(F16, BF16, BF16)) == _native.RUN_EXACT
+    assert run(dt=(F16, F16, F16)) == _native.RUN_TCGEN05_CS
+
+
+@pytest.mark.parametrize("dt,kernel", [((F32, F32, F32), TC), ((F16, BF16, BF16), TC),
+                                       ((F32, F32, BF16), PAIR)])
+def test_tensor_core_selectors_reject_other_dtypes(dt, kernel):
+    assert run(dt=dt, kernel=kernel) == _native.HEATKV_ERR_UNSUPPORTED
+
+
+def test_invalid_arguments():
+    assert run(kernel=7) == _native.HEATKV_ERR_INVALID_ARGUMENT
+    assert run(q_len=0) == _native.HEATKV_ERR_INVALID_ARGUMENT
+    assert run(dt=(5, BF16, BF16)) == _native.HEATKV_ERR_UNSUPPORTED
