@@ -91,6 +91,11 @@ cudaError_t launch_shard_gather(void* dst, const void* src, const int32_t* row_m
                                 int64_t heads, int64_t chunk_bytes, int sms,
                                 unsigned int* status, cudaStream_t stream);
 
+// S-CAS attention mass per (head, source scale) of one scale's queries (scas.cu).
+cudaError_t launch_scas_mass(const void* q, const void* k, int dtype, int64_t heads, int64_t q_len,
+                             int64_t k_len, float scale, const int32_t* bounds, int n_src,
+                             double* mass_out, int64_t mass_stride, cudaStream_t st);
+
 // q/k/v preparation after the QKV projection (qkv_prep.cu); sms = SMs of the device.
 cudaError_t launch_qkv_prepare(const void* qkv, void* q, void* k, void* v, int in_dtype,
                                int qk_dtype, int64_t batch, int64_t seq_len, int64_t heads,

@@ -485,6 +485,29 @@ int heatkv_gather_head_shards(void* dst, const void* src, int dtype, int64_t wor
   return HEATKV_OK;
 }
 
+int heatkv_scas_mass(const void* q, const void* k, int dtype, int64_t heads, int64_t q_len,
+                     int64_t k_len, int64_t head_dim, float scale, const int32_t* bounds,
+                     int n_src, double* mass_out, int64_t mass_stride, void* stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype))
+    return fail(HEATKV_ERR_UNSUPPORTED, "heatkv_scas_mass: unsupported dtype code");
+  if (head_dim != 128)
+    return fail(HEATKV_ERR_UNSUPPORTED, "heatkv_scas_mass only supports head_dim=128");
+  if (heads <= 0 || q_len < 0 || k_len < 0 || n_src < 0 || n_src > 32 ||
+      mass_stride < n_src || heads > 65535 || (q_len + 63) / 64 > 0x7fffffffLL)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_scas_mass: invalid sizes");
+  if (q_len == 0 || k_len == 0 || n_src == 0) return HEATKV_OK;
+  if (!q || !k || !bounds || !mass_out)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_scas_mass: null pointer");
+  const uintptr_t need = dtype == HEATKV_DTYPE_F32 ? 15u : 7u;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k)) & need)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_scas_mass: misaligned q or k");
+  cudaError_t e = heatkv::launch_scas_mass(q, k, dtype, heads, q_len, k_len, scale, bounds, n_src,
+                                           mass_out, mass_stride, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "heatkv_scas_mass launch");
+  return HEATKV_OK;
+}
+
 int heatkv_qkv_prepare(const void* qkv, void* q, void* k, void* v, int in_dtype, int qk_dtype,
                        int64_t batch, int64_t seq_len, int64_t heads, int64_t head_dim,
                        const float* scale_mul, float eps, const float* rope_cos,

@@ -9,6 +9,8 @@
 ``pack``: the append of one scale (every head's ``--q-len`` tokens) into a slab.
 ``pack-batched``: the same append for ``--layers`` layers (one slab and one source per layer) as
 one ``heatkv_pack_kv_batched`` launch, as the pre-planned step issues a scale's appends.
+``scas``: one layer's S-CAS update at a scale (``heatkv_scas_mass``) against the PyTorch
+probabilities it avoids.
 ``qkv-prep``: one layer's q/k/v preparation (``heatkv_qkv_prepare``: cos-attention + RoPE under
 autocast) against the PyTorch chain it replaces.
 Prints per-call device time (CUDA events, warm, back to back) and the achieved TFLOP/s or GB/s.
@@ -71,7 +73,7 @@ def time_call(fn, iters, warmup=3):
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("kernel", choices=["attention", "pack", "pack-batched", "qkv-prep"])
+    ap.add_argument("kernel", choices=["attention", "pack", "pack-batched", "qkv-prep", "scas"])
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--rows", type=int, default=2)
     ap.add_argument("--heads", type=int, default=16)
@@ -126,6 +128,32 @@ def main(argv=None):
         print(f"qkv-prep rows={B} heads={H} q_len={L}: {ms * 1e3:.1f} us/call, "
               f"{nbytes / ms / 1e6:.1f} GB/s; PyTorch chain {ms_t * 1e3:.1f} us "
               f"({ms_t / ms:.1f}x)", flush=True)
+    elif args.kernel == "scas":
+        # one layer's S-CAS update at a scale: --q-len queries over --slots earlier keys plus
+        # themselves (every key so far), fp32 q/k, 12 source scales; against the reference's form
+        # (PyTorch fp32 probabilities of both batch rows, then the per-scale sums of row 0)
+        from .scas import ScasAccumulator
+        B, L, H = args.rows, args.q_len, args.heads
+        sched = list(__import__("heatkv_b200.synthetic", fromlist=["x"]).SCALE_SCHEDULE_1M)
+        total = sum(a * b * c for a, b, c in sched)
+        acc = ScasAccumulator(num_layers=1, num_heads=H, scale_schedule=sched, sink_scales=0,
+                              device="cuda")
+        K = min(total, args.slots + L)
+        q = torch.randn(B, H, L, 128, device="cuda")
+        k = torch.randn(B, H, K, 128, device="cuda")
+        t = 12 if K == total else max(i for i in range(13) if sum(a * b * c for a, b, c in sched[:i]) + L <= K)
+        ms = time_call(lambda: acc.update_from_qk(layer_idx=0, scale_ind=t, q=q, k=k, scale=0.0884),
+                       args.iters, args.warmup)
+        torch.backends.cuda.matmul.allow_tf32 = False
+
+        def ref_form():
+            probs = torch.softmax(torch.matmul(q.float(), k.float().transpose(-2, -1)) * 0.0884, -1)
+            acc.update(layer_idx=0, scale_ind=t, probs=probs)
+        ms_r = time_call(ref_form, max(2, args.iters // 4), 1)
+        flops = 2.0 * L * K * 128 * H
+        print(f"scas rows(ref)={B} heads={H} q_len={L} keys={K}: {ms * 1e3:.1f} us/call "
+              f"({flops / ms / 1e9:.1f} TFLOP/s of row-0 QK); reference form {ms_r * 1e3:.1f} us "
+              f"({ms_r / ms:.1f}x)", flush=True)
     elif args.kernel == "pack-batched":
         import numpy as np
 

@@ -330,6 +330,21 @@ int heatkv_attention_kernel_for(int q_dtype, int k_dtype, int v_dtype, int64_t b
                                 int has_workspace, int64_t unsplit_blocks);
 
 /*
+ * heatkv_scas_mass - the S-CAS accumulation of tools/compute_scas.py:114-128 for one layer and one
+ * scale, without materialising the attention probabilities. For the queries q [heads, q_len,
+ * head_dim] of batch row 0 and every key so far k [heads, k_len, head_dim] (the cached scales,
+ * then the current one; dtype: f32, bf16 or f16, read as fp32), with probs = softmax(q k^T *
+ * scale) in fp32, adds
+ *   mass_out[h * mass_stride + s] += mean over the queries of sum_{bounds[s] <= key < bounds[s+1]} probs
+ * for every source s < n_src (<= 32). bounds: int32 device array of n_src + 1 increasing key
+ * offsets; mass_out: float64 device array (the reference's accumulator row of this layer, from
+ * its first source scale). head_dim must be 128; q and k 16-byte aligned for f32, 8 for 16-bit.
+ */
+int heatkv_scas_mass(const void* q, const void* k, int dtype, int64_t heads, int64_t q_len,
+                     int64_t k_len, int64_t head_dim, float scale, const int32_t* bounds,
+                     int n_src, double* mass_out, int64_t mass_stride, void* stream);
+
+/*
  * heatkv_qkv_prepare - the q/k/v preparation of the patched attention forward between the QKV
  * projection and the attention call (enable_real_pruning_fast.py:2040-2072), in one pass:
  *   qkv : [batch, seq_len, 3, heads, head_dim] (in_dtype: bf16 or f16), the projection output
