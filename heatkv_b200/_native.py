@@ -66,6 +66,7 @@ SIGNATURES = {
     "heatkv_gather_head_shards": (_i, [_p, _p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                        _p, _p, _p]),
     "heatkv_attention_kernel_for": (_i, [_i, _i, _i, _i64, _i64, _i64, _i, _i, _i, _i64]),
+    "heatkv_slot_schedule": (_i, [_p, _i, _i, _p, _p, _p, _p, _p, _p]),
     "heatkv_scas_mass": (_i, [_p, _p, _i, _i64, _i64, _i64, _i64, ctypes.c_float, _p, _i, _p,
                               _i64, _p]),
     "heatkv_qkv_prepare": (_i, [_p, _p, _p, _p, _i, _i, _i64, _i64, _i64, _i64, _p,

@@ -1,6 +1,6 @@
 """Build libheatkv.so in-tree with nvcc for sm_100a.
 
-``python -m heatkv_b200.build`` compiles every ``csrc/*.cu`` (whole-program device code: kernels
+``python -m heatkv_b200.build`` compiles every ``csrc/*.cu`` and ``csrc/*.cpp`` (host code) (whole-program device code: kernels
 receive the device status word's address as a parameter, and ``setmaxnreg`` register splits are
 only honoured without relocatable device code) and links ``heatkv_b200/libheatkv.so``. Objects go to
 ``heatkv_b200/_build/``; a file is recompiled only when it or a header changed. The build needs no
@@ -62,8 +62,8 @@ def _compile(src: str, obj: str, verbose: bool, extra) -> None:
 
 def build(force: bool = False, verbose: bool = False, extra=()) -> str:
     os.makedirs(BUILD, exist_ok=True)
-    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
-    objs = [os.path.join(BUILD, os.path.basename(s)[:-3] + ".o") for s in srcs]
+    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
+    objs = [os.path.join(BUILD, os.path.splitext(os.path.basename(s))[0] + ".o") for s in srcs]
     todo = [(s, o) for s, o in zip(srcs, objs) if force or _stale(o, s)]
     if todo:
         with cf.ThreadPoolExecutor(max_workers=min(len(todo), os.cpu_count() or 4)) as ex:

@@ -12,6 +12,8 @@ bit for bit:
    placement the intervals that ended by its start are freed and the free list is coalesced
    (:324-337, merge rule :1033-1047); the segment takes the best-fitting free block - least
    leftover, then lowest offset - from its front, else the high-water mark grows (:338-370).
+   Steps 1-2 and the capacity bound run in native code (``heatkv_slot_schedule``,
+   csrc/slot_schedule.cpp).
 3. Per target ``t``: ``[H, S]`` starts/ends and ``[H]`` counts of the live segments, each head's
    segments in source-scale order (:383-412).
 4. Copy descriptors, sorted by destination slot (:414-482): the activation pack of target ``t``
@@ -26,33 +28,49 @@ mark is used even when it exceeds the bound.
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
+
+from . import _native
+
+
+def _placement(controller, *, layer_idx: int, num_heads: int):
+    """Placed segments (placement order), high-water mark and capacity bound of a layer, from
+    libheatkv's ``heatkv_slot_schedule`` (the reference's placement and capacity bound, :206-370,
+    in native code)."""
+    mask = np.ascontiguousarray(controller.removed_mask_for_layer(layer_idx), dtype=np.uint8)
+    ranges = controller.scale_ranges
+    num_scales = len(controller.scale_schedule)
+    if mask.shape != (num_scales, num_scales, num_heads):
+        raise ValueError("removed mask must be [scales, scales, heads]")
+    lo = np.array([int(ranges[s][0]) if s in ranges else 0 for s in range(num_scales)], np.int64)
+    hi = np.array([int(ranges[s][1]) if s in ranges else 0 for s in range(num_scales)], np.int64)
+    offset = np.empty(num_scales * num_heads, dtype=np.int64)
+    end_t = np.empty(num_scales * num_heads, dtype=np.int32)
+    cap, bound = ctypes.c_int64(0), ctypes.c_int64(0)
+    _native.check(_native.load().heatkv_slot_schedule(
+        mask.ctypes.data, num_scales, num_heads, lo.ctypes.data, hi.ctypes.data,
+        offset.ctypes.data, end_t.ctypes.data, ctypes.byref(cap), ctypes.byref(bound)),
+        "heatkv_slot_schedule")
+    segs = []
+    for s in range(num_scales):
+        for h in range(num_heads):
+            off = int(offset[s * num_heads + h])
+            if off < 0:
+                continue
+            segs.append({"source_scale": s, "head": h, "start_target": s + 1,
+                         "end_target": int(end_t[s * num_heads + h]), "length": int(hi[s] - lo[s]),
+                         "scale_start": int(lo[s]), "scale_end": int(hi[s]), "offset": off})
+    segs.sort(key=lambda it: (it["start_target"], it["end_target"], -it["length"],
+                              it["source_scale"], it["head"]))
+    return segs, int(cap.value), int(bound.value)
 
 
 def capacity_bound_for_layer(controller, *, layer_idx: int, num_heads: int) -> int:
     """``_segmented_flat_cache_capacity_for_layer``: max over targets of sum over earlier
     sources of (heads kept) x tokens."""
-    mask = controller.removed_mask_for_layer(layer_idx)  # [t, s, h]
-    ranges = controller.scale_ranges
-    num_scales = len(controller.scale_schedule)
-    tokens = np.array([ranges[s][1] - ranges[s][0] for s in range(num_scales)], dtype=np.int64)
-    best = 0
-    for t in range(1, num_scales):
-        kept = num_heads - mask[t, :t, :].sum(axis=1).astype(np.int64)
-        best = max(best, int((kept * np.maximum(tokens[:t], 0)).sum()))
-    return best
-
-
-def merge_free_blocks(blocks):
-    """Sort by offset and coalesce overlapping or touching blocks; zero-length blocks vanish."""
-    out = []
-    for off, length in sorted((int(o), int(n)) for o, n in blocks if int(n) > 0):
-        if out and off <= out[-1][0] + out[-1][1]:
-            last_off, last_len = out[-1]
-            out[-1] = (last_off, max(last_off + last_len, off + length) - last_off)
-        else:
-            out.append((off, length))
-    return out
+    return _placement(controller, layer_idx=layer_idx, num_heads=num_heads)[2]
 
 
 def _copy_runs(items, sequence_len: int):
@@ -103,60 +121,9 @@ def build_static_slot_schedule(controller, *, layer_idx: int, num_heads: int,
     ``segments_by_target``, ``metadata_cpu_by_target``, ``old_pack_runs_by_target``,
     ``old_pack_cache_lens_by_target``, ``append_runs_by_key``); metadata values are numpy int32."""
     num_heads = int(num_heads)
-    bound = capacity_bound_for_layer(controller, layer_idx=layer_idx, num_heads=num_heads)
     ranges = controller.scale_ranges
     num_scales = len(controller.scale_schedule)
-    mask = controller.removed_mask_for_layer(layer_idx)  # [t, s, h]
-
-    intervals = []
-    for s in sorted(ranges):
-        start_t = s + 1
-        if start_t >= num_scales:
-            continue
-        lo, hi = ranges[s]
-        length = int(hi) - int(lo)
-        if length <= 0:
-            continue
-        removed_later = mask[start_t:, s, :]  # [t - start_t, h]
-        for h in range(num_heads):
-            hits = np.flatnonzero(removed_later[:, h])
-            end_t = start_t + int(hits[0]) if hits.size else num_scales
-            if end_t <= start_t:
-                continue
-            intervals.append({"source_scale": s, "head": h, "start_target": start_t,
-                              "end_target": end_t, "length": length,
-                              "scale_start": int(lo), "scale_end": int(hi)})
-
-    free, active, assigned, high_water = [], [], [], 0
-    for seg in sorted(intervals, key=lambda it: (it["start_target"], it["end_target"],
-                                                 -it["length"], it["source_scale"], it["head"])):
-        still = []
-        for a in active:
-            if a["end_target"] <= seg["start_target"]:
-                free.append((a["offset"], a["length"]))
-            else:
-                still.append(a)
-        active = still
-        free = merge_free_blocks(free)
-        need = seg["length"]
-        best = None
-        for i, (off, length) in enumerate(free):
-            if length >= need and (best is None or (length - need, off) < (best[0], best[2])):
-                best = (length - need, i, off, length)
-        if best is not None:
-            _, i, off, length = best
-            if length == need:
-                del free[i]
-            else:
-                free[i] = (off + need, length - need)
-            offset = off
-        else:
-            offset = high_water
-            high_water += need
-        placed = dict(seg)
-        placed["offset"] = int(offset)
-        assigned.append(placed)
-        active.append(placed)
+    assigned, high_water, bound = _placement(controller, layer_idx=layer_idx, num_heads=num_heads)
 
     if high_water > bound and not allow_overalloc:
         return {"enabled": False, "capacity": bound, "capacity_bound": bound,

@@ -364,6 +364,22 @@ int heatkv_qkv_prepare(const void* qkv, void* q, void* k, void* v, int in_dtype,
                        const float* rope_sin, int64_t rope_row_stride, void* stream);
 
 /*
+ * heatkv_slot_schedule - host-side slab placement of one layer's static schedule, replacing the
+ * placement core of _segmented_flat_build_static_slot_schedule (enable_real_pruning_fast.py:
+ * 260-370) and _segmented_flat_cache_capacity_for_layer (:206-234), bit for bit.
+ *   removed      : uint8 [num_scales (target), num_scales (source), num_heads], 1 where the head
+ *                  of that source scale is removed at that target (host memory)
+ *   scale_start/_end : int64 [num_scales] token range of every scale (host)
+ *   offset_out   : int64 [num_scales * num_heads] slab offset of (source, head), -1 if never live
+ *   end_target_out : int32 [num_scales * num_heads] first target without it (exclusive), -1
+ *   capacity_out : the high-water mark; bound_out : the capacity bound
+ * No device is touched.
+ */
+int heatkv_slot_schedule(const uint8_t* removed, int num_scales, int num_heads,
+                         const int64_t* scale_start, const int64_t* scale_end, int64_t* offset_out,
+                         int32_t* end_target_out, int64_t* capacity_out, int64_t* bound_out);
+
+/*
  * heatkv_device_status - read (and with clear != 0, reset) the sticky HEATKV_DEVICE_* flags of
  * the current CUDA device. This call synchronises `stream`. Not part of the reference interface:
  * the reference's Triton kernels do not check descriptors on the device.
