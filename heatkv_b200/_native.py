@@ -71,6 +71,8 @@ SIGNATURES = {
                               _i64, _p]),
     "heatkv_qkv_prepare": (_i, [_p, _p, _p, _p, _i, _i, _i64, _i64, _i64, _i64, _p,
                                 ctypes.c_float, _p, _p, _i64, _p]),
+    "heatkv_qkv_prepare_append": (_i, [_p, _p, _p, _p, _i, _i, _i64, _i64, _i64, _i64, _p,
+                                       ctypes.c_float, _p, _p, _i64, _p, _p, _i64, _p, _p]),
     "heatkv_device_status": (_i, [ctypes.POINTER(ctypes.c_uint32), _i, _p]),
 }
 

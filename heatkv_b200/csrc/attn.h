@@ -100,7 +100,8 @@ cudaError_t launch_scas_mass(const void* q, const void* k, int dtype, int64_t he
 cudaError_t launch_qkv_prepare(const void* qkv, void* q, void* k, void* v, int in_dtype,
                                int qk_dtype, int64_t batch, int64_t seq_len, int64_t heads,
                                const float* scale_mul, float eps, const float* rope_cos,
-                               const float* rope_sin, int64_t rope_row_stride, int sms,
-                               unsigned int* status, cudaStream_t st);
+                               const float* rope_sin, int64_t rope_row_stride, void* slab_k,
+                               void* slab_v, int64_t slab_rows, const int64_t* slab_offset,
+                               int sms, unsigned int* status, cudaStream_t st);
 
 }  // namespace heatkv

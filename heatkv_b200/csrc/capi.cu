@@ -508,41 +508,81 @@ int heatkv_scas_mass(const void* q, const void* k, int dtype, int64_t heads, int
   return HEATKV_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+int qkv_prepare_impl(const char* name, const void* qkv, void* q, void* k, void* v, int in_dtype,
+                     int qk_dtype, int64_t batch, int64_t seq_len, int64_t heads, int64_t head_dim,
+                     const float* scale_mul, float eps, const float* rope_cos,
+                     const float* rope_sin, int64_t rope_row_stride, void* slab_k, void* slab_v,
+                     int64_t slab_rows, const int64_t* slab_offset, void* stream) {
+  g_last_error.clear();
+  if ((in_dtype != HEATKV_DTYPE_BF16 && in_dtype != HEATKV_DTYPE_F16) || !valid_dtype(qk_dtype))
+    return fail(HEATKV_ERR_UNSUPPORTED,
+                "%s: qkv must be bfloat16 or float16, q/k float32, bfloat16 or float16",
+                name);
+  if (head_dim != 128)
+    return fail(HEATKV_ERR_UNSUPPORTED, "%s only supports head_dim=128", name);
+  if (batch < 0 || seq_len < 0 || heads < 0 || slab_rows < 0)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: negative size", name);
+  if (batch * seq_len * heads == 0) return HEATKV_OK;
+  if (!qkv || !q || !k || !v || (rope_cos && !rope_sin) || (!rope_cos && rope_sin))
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (slab_offset && (!slab_k || !slab_v))
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: slab offsets given without slab_k/slab_v",
+                name);
+  if (rope_cos && (rope_row_stride < head_dim / 2 || (rope_row_stride & 1)))
+    return fail(HEATKV_ERR_INVALID_ARGUMENT,
+                "%s: rope_row_stride must be even and at least head_dim / 2", name);
+  if (!(eps >= 0.f)) return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: eps must be >= 0", name);
+  const uintptr_t a8 = reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(v) |
+                       reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin) |
+                       reinterpret_cast<uintptr_t>(slab_v) |
+                       reinterpret_cast<uintptr_t>(slab_offset);
+  const uintptr_t aqk = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                        reinterpret_cast<uintptr_t>(slab_k);
+  if ((a8 & 7u) || (aqk & (qk_dtype == HEATKV_DTYPE_F32 ? 15u : 7u)))
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: misaligned pointer", name);
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail(e, name);
+  e = heatkv::launch_qkv_prepare(qkv, q, k, v, in_dtype, qk_dtype, batch, seq_len, heads,
+                                 scale_mul, eps, rope_cos, rope_sin, rope_row_stride,
+                                 slab_offset ? slab_k : nullptr, slab_offset ? slab_v : nullptr,
+                                 slab_rows, slab_offset, sms, heatkv::device_status_ptr(),
+                                 static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, name);
+  return HEATKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 int heatkv_qkv_prepare(const void* qkv, void* q, void* k, void* v, int in_dtype, int qk_dtype,
                        int64_t batch, int64_t seq_len, int64_t heads, int64_t head_dim,
                        const float* scale_mul, float eps, const float* rope_cos,
                        const float* rope_sin, int64_t rope_row_stride, void* stream) {
-  g_last_error.clear();
-  if ((in_dtype != HEATKV_DTYPE_BF16 && in_dtype != HEATKV_DTYPE_F16) || !valid_dtype(qk_dtype))
-    return fail(HEATKV_ERR_UNSUPPORTED,
-                "heatkv_qkv_prepare: qkv must be bfloat16 or float16, q/k float32, bfloat16 or "
-                "float16");
-  if (head_dim != 128)
-    return fail(HEATKV_ERR_UNSUPPORTED, "heatkv_qkv_prepare only supports head_dim=128");
-  if (batch < 0 || seq_len < 0 || heads < 0)
-    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_qkv_prepare: negative size");
-  if (batch * seq_len * heads == 0) return HEATKV_OK;
-  if (!qkv || !q || !k || !v || (rope_cos && !rope_sin) || (!rope_cos && rope_sin))
-    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_qkv_prepare: null pointer");
-  if (rope_cos && (rope_row_stride < head_dim / 2 || (rope_row_stride & 1)))
-    return fail(HEATKV_ERR_INVALID_ARGUMENT,
-                "heatkv_qkv_prepare: rope_row_stride must be even and at least head_dim / 2");
-  if (!(eps >= 0.f))
-    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_qkv_prepare: eps must be >= 0");
-  const uintptr_t a8 = reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(v) |
-                       reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin);
-  const uintptr_t aqk = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k);
-  if ((a8 & 7u) || (aqk & (qk_dtype == HEATKV_DTYPE_F32 ? 15u : 7u)))
-    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_qkv_prepare: misaligned pointer");
-  int dev = 0, sms = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (e != cudaSuccess) return cuda_fail(e, "heatkv_qkv_prepare: device query");
-  e = heatkv::launch_qkv_prepare(qkv, q, k, v, in_dtype, qk_dtype, batch, seq_len, heads,
-                                 scale_mul, eps, rope_cos, rope_sin, rope_row_stride, sms,
-                                 heatkv::device_status_ptr(), static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "heatkv_qkv_prepare launch");
-  return HEATKV_OK;
+  return qkv_prepare_impl("heatkv_qkv_prepare", qkv, q, k, v, in_dtype, qk_dtype, batch, seq_len,
+                          heads, head_dim, scale_mul, eps, rope_cos, rope_sin, rope_row_stride,
+                          nullptr, nullptr, 0, nullptr, stream);
+}
+
+int heatkv_qkv_prepare_append(const void* qkv, void* q, void* k, void* v, int in_dtype,
+                              int qk_dtype, int64_t batch, int64_t seq_len, int64_t heads,
+                              int64_t head_dim, const float* scale_mul, float eps,
+                              const float* rope_cos, const float* rope_sin,
+                              int64_t rope_row_stride, void* slab_k, void* slab_v,
+                              int64_t slab_rows, const int64_t* slab_offset, void* stream) {
+  if (!slab_offset) {
+    g_last_error.clear();
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_qkv_prepare_append: null slab_offset");
+  }
+  return qkv_prepare_impl("heatkv_qkv_prepare_append", qkv, q, k, v, in_dtype, qk_dtype, batch,
+                          seq_len, heads, head_dim, scale_mul, eps, rope_cos, rope_sin,
+                          rope_row_stride, slab_k, slab_v, slab_rows, slab_offset, stream);
 }
 
 int heatkv_device_status(uint32_t* flags, int clear, void* stream) {

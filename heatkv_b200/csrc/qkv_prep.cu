@@ -14,6 +14,15 @@
 // the squared norm is reduced over the warp. Rows are 128 elements (the only head dim of the
 // path). HBM-bound: per (token, head) it reads 3 x 128 input elements (+ the rope row, shared by
 // the heads of a token and served by L1/L2) and writes q, k in their dtype and v in the input's.
+//
+// Slab append (optional): the append after the attention (enable_real_pruning_fast.py:2218-2225 ->
+// :969-1024) copies the scale's K/V rows of every retained head into that head's slab segment,
+// slab[b, offset[h] + l, :] = k[b, h, l, :] (and v). For the heads whose segment shares no slot
+// with the segments the attention of this scale reads, the caller passes offset[h] >= 0 and this
+// kernel writes those rows here, from the registers that hold the final k and v; the slab ends up
+// with the same bytes as after the reference's copy. offset[h] = -1 leaves head h to that copy.
+// A segment that would leave the slab (offset + seq_len > slab_rows) is skipped and raises
+// HEATKV_DEVICE_PACK_OUT_OF_RANGE.
 #include "attn.h"
 #include "common.cuh"
 
@@ -70,7 +79,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
                        TIn* __restrict__ v, int64_t batch, int64_t seq_len, int64_t heads,
                        const float* __restrict__ scale_mul, float eps,
                        const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
-                       int64_t rope_row_stride) {
+                       int64_t rope_row_stride, TQK* __restrict__ slab_k, TIn* __restrict__ slab_v,
+                       int64_t slab_rows, const int64_t* __restrict__ slab_offset,
+                       unsigned int* status) {
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x % 32;
@@ -104,15 +115,27 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     store4(q + dst, xq);
     store4(k + dst, xk);
     store4(v + dst, xv);
+    if (slab_offset != nullptr) {
+      const int64_t off = __ldg(slab_offset + h);
+      if (off >= 0) {
+        if (off > slab_rows - seq_len) {
+          if (lane == 0 && l == 0 && status) atomicOr(status, HEATKV_DEVICE_PACK_OUT_OF_RANGE);
+        } else {
+          const int64_t row = (b * slab_rows + off + l) * kD + 4 * lane;
+          store4(slab_k + row, xk);
+          store4(slab_v + row, xv);
+        }
+      }
+    }
   }
 }
 
 template <typename TIn, typename TQK>
 cudaError_t launch_t(const void* qkv, void* q, void* k, void* v, int64_t batch, int64_t seq_len,
                      int64_t heads, const float* scale_mul, float eps, const float* rope_cos,
-                     const float* rope_sin, int64_t rope_row_stride, int sms,
-                     unsigned int* status, cudaStream_t st) {
-  (void)status;
+                     const float* rope_sin, int64_t rope_row_stride, void* slab_k, void* slab_v,
+                     int64_t slab_rows, const int64_t* slab_offset, int sms, unsigned int* status,
+                     cudaStream_t st) {
   const int64_t units = batch * seq_len * heads;
   const int64_t want = (units + kWarpsPerBlock - 1) / kWarpsPerBlock;
   const int grid = static_cast<int>(std::min<int64_t>(want, int64_t(sms) * 8));
@@ -120,10 +143,13 @@ cudaError_t launch_t(const void* qkv, void* q, void* k, void* v, int64_t batch, 
   TQK* qo = static_cast<TQK*>(q);
   TQK* ko = static_cast<TQK*>(k);
   TIn* vo = static_cast<TIn*>(v);
+  TQK* sk = static_cast<TQK*>(slab_k);
+  TIn* sv = static_cast<TIn*>(slab_v);
   const bool cos = scale_mul != nullptr, rp = rope_cos != nullptr;
   auto go = [&](auto kern) {
     return launch_pdl(kern, dim3(grid), dim3(kWarpsPerBlock * 32), 0, st, in, qo, ko, vo, batch,
-                      seq_len, heads, scale_mul, eps, rope_cos, rope_sin, rope_row_stride);
+                      seq_len, heads, scale_mul, eps, rope_cos, rope_sin, rope_row_stride, sk, sv,
+                      slab_rows, slab_offset, status);
   };
   cudaError_t e;
   if (cos && rp) e = go(qkv_prepare_kernel<TIn, TQK, true, true>);
@@ -139,30 +165,28 @@ cudaError_t launch_t(const void* qkv, void* q, void* k, void* v, int64_t batch, 
 cudaError_t launch_qkv_prepare(const void* qkv, void* q, void* k, void* v, int in_dtype,
                                int qk_dtype, int64_t batch, int64_t seq_len, int64_t heads,
                                const float* scale_mul, float eps, const float* rope_cos,
-                               const float* rope_sin, int64_t rope_row_stride, int sms,
-                               unsigned int* status, cudaStream_t st) {
+                               const float* rope_sin, int64_t rope_row_stride, void* slab_k,
+                               void* slab_v, int64_t slab_rows, const int64_t* slab_offset,
+                               int sms, unsigned int* status, cudaStream_t st) {
   const bool bf16 = in_dtype == HEATKV_DTYPE_BF16;
+#define HEATKV_QKV_PREP(TI, TQ)                                                               \
+  launch_t<TI, TQ>(qkv, q, k, v, batch, seq_len, heads, scale_mul, eps, rope_cos, rope_sin,   \
+                   rope_row_stride, slab_k, slab_v, slab_rows, slab_offset, sms, status, st)
+  cudaError_t e;
   switch (qk_dtype) {
     case HEATKV_DTYPE_F32:
-      return bf16 ? launch_t<__nv_bfloat16, float>(qkv, q, k, v, batch, seq_len, heads, scale_mul,
-                                                   eps, rope_cos, rope_sin, rope_row_stride, sms,
-                                                   status, st)
-                  : launch_t<__half, float>(qkv, q, k, v, batch, seq_len, heads, scale_mul, eps,
-                                            rope_cos, rope_sin, rope_row_stride, sms, status, st);
+      e = bf16 ? HEATKV_QKV_PREP(__nv_bfloat16, float) : HEATKV_QKV_PREP(__half, float);
+      break;
     case HEATKV_DTYPE_BF16:
-      return bf16 ? launch_t<__nv_bfloat16, __nv_bfloat16>(qkv, q, k, v, batch, seq_len, heads,
-                                                           scale_mul, eps, rope_cos, rope_sin,
-                                                           rope_row_stride, sms, status, st)
-                  : launch_t<__half, __nv_bfloat16>(qkv, q, k, v, batch, seq_len, heads,
-                                                    scale_mul, eps, rope_cos, rope_sin,
-                                                    rope_row_stride, sms, status, st);
+      e = bf16 ? HEATKV_QKV_PREP(__nv_bfloat16, __nv_bfloat16)
+               : HEATKV_QKV_PREP(__half, __nv_bfloat16);
+      break;
     default:
-      return bf16 ? launch_t<__nv_bfloat16, __half>(qkv, q, k, v, batch, seq_len, heads, scale_mul,
-                                                    eps, rope_cos, rope_sin, rope_row_stride, sms,
-                                                    status, st)
-                  : launch_t<__half, __half>(qkv, q, k, v, batch, seq_len, heads, scale_mul, eps,
-                                             rope_cos, rope_sin, rope_row_stride, sms, status, st);
+      e = bf16 ? HEATKV_QKV_PREP(__nv_bfloat16, __half) : HEATKV_QKV_PREP(__half, __half);
+      break;
   }
+#undef HEATKV_QKV_PREP
+  return e;
 }
 
 }  // namespace heatkv

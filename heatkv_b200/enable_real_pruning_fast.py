@@ -32,7 +32,10 @@ between the QKV projection and the attention (unbind, permute, cos-attention nor
 head scale, 2-D RoPE) by one pass of ``heatkv_qkv_prepare`` (``qkv_prep.prepare_qkv``), when the
 projection is bf16/fp16, the head dim is 128 and, with cos-attention, autocast is enabled (the
 kernel normalises in fp32 as F.normalize does under autocast). Its RoPE is the one of
-infinity/models/basic.py:97-117 applied to the module's rope cache rows.
+infinity/models/basic.py:97-117 applied to the module's rope cache rows. On scales whose slab is
+already active, the same pass writes the slab append of every head whose new segment shares no
+slot with the segments this scale's attention reads (``scheduler.prep_append_split``); the pack
+after the attention then copies only the other heads. The slab holds the same bytes afterwards.
 """
 
 from __future__ import annotations
@@ -60,7 +63,7 @@ from .real_pruning_fused_attention import (
     fused_real_pruning_flat_segmented_attention,
     pack_flat_segments_kv,
 )
-from .scheduler import build_static_slot_schedule, copy_descriptors
+from .scheduler import build_static_slot_schedule, copy_descriptors, prep_append_split
 
 # ------------------------------------------------------------------------------------------------
 # phase profiler and slab counters (enable_real_pruning_fast.py:32-163)
@@ -173,10 +176,12 @@ class _LayerState:
         self.schedule = build_static_slot_schedule(controller, layer_idx=layer_idx,
                                                    num_heads=num_heads)
         self.capacity = int(self.schedule["capacity"])
+        self.num_heads = int(num_heads)
         self.device = None
         self.meta = {}
         self.old_pack = {}
         self.append = {}
+        self.prep_append = {}
 
     def to(self, device: torch.device) -> None:
         if self.device == device:
@@ -195,6 +200,14 @@ class _LayerState:
 
         self.old_pack = {t: desc(r) for t, r in sched["old_pack_runs_by_target"].items()}
         self.append = {k: desc(r) for k, r in sched["append_runs_by_key"].items()}
+        # per scale: heads the q/k/v preparation may append before the attention, and the rest
+        self.prep_append = {}
+        for s, _ in sched["append_runs_by_key"]:
+            split = prep_append_split(sched, s, self.num_heads)
+            if split is None or split["early_slots"] == 0:
+                continue
+            self.prep_append[s] = (torch.from_numpy(split["offsets"]).to(device),
+                                   desc(split["rest_runs"]), split["early_slots"])
         self.device = device
 
 
@@ -355,9 +368,21 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
         if rope2d_freqs_grid is not None:
             rope = _qkv_prep.rope_rows(rope2d_freqs_grid, scale_schedule, scale_ind, seq_len,
                                        qkv.device)
-        q, k, v = _qkv_prep.prepare_qkv(qkv, scale_mul=scale_mul, rope=rope)
+        early = None
+        if active and not final_scale:
+            early = self._heatkv_layer.prep_append.get(scale_ind)
+            dts = _qkv_prep.prepared_dtypes(qkv.dtype, cos_attention=scale_mul is not None,
+                                            rope=rope is not None)
+            if early is not None and (self._heatkv_slab_k.dtype, self._heatkv_slab_v.dtype) != dts:
+                early = None
+        append = None if early is None else (self._heatkv_slab_k, self._heatkv_slab_v, early[0])
+        q, k, v = _qkv_prep.prepare_qkv(qkv, scale_mul=scale_mul, rope=rope, append=append)
+        if early is not None:
+            _stat_add("prep_append_calls")
+            _record_kv_copy("prep_append", early[2], self._heatkv_slab_k, self._heatkv_slab_v)
         del qkv
     else:
+        early = None
         q, k, v = qkv.unbind(dim=2)
         q = q.permute(0, 2, 1, 3).contiguous()
         k = k.permute(0, 2, 1, 3).contiguous()
@@ -418,8 +443,10 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
                     self.cached_k = torch.cat((self.cached_k, k), dim=2)
                     self.cached_v = torch.cat((self.cached_v, v), dim=2)
             elif active:
-                _pack(self._heatkv_layer.append.get((scale_ind, scale_ind + 1)),
-                      self._heatkv_slab_k, self._heatkv_slab_v, k, v, "append_copy")
+                # heads already appended by the q/k/v preparation leave only the rest here
+                desc = (early[1] if early is not None
+                        else self._heatkv_layer.append.get((scale_ind, scale_ind + 1)))
+                _pack(desc, self._heatkv_slab_k, self._heatkv_slab_v, k, v, "append_copy")
             else:
                 _activate_from_dense_and_current(self, self.cached_k, self.cached_v, k, v,
                                                  scale_ind, old_len, scale_ind + 1)

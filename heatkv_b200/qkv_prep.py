@@ -5,7 +5,10 @@ projection output ``qkv`` ``[B, L, 3, H, D]`` into contiguous ``q, k, v`` ``[B, 
 chain of PyTorch ops: ``unbind`` + ``permute`` + ``contiguous``; with cos-attention
 ``q = F.normalize(q) * scale_mul`` and ``k = F.normalize(k)``; then ``apply_rotary_emb``
 (infinity/models/basic.py:97-117), which computes in fp32 with autocast off.
-``prepare_qkv`` does the same in one HBM pass (``heatkv_qkv_prepare``, csrc/qkv_prep.cu).
+``prepare_qkv`` does the same in one HBM pass (``heatkv_qkv_prepare``, csrc/qkv_prep.cu). With
+``append=`` the same pass also writes the scale's K/V rows of the given heads into the layer's slab
+(``heatkv_qkv_prepare_append``), the part of the reference's post-attention append
+(enable_real_pruning_fast.py:2218-2225) that ``scheduler.prep_append_split`` shows may run first.
 
 Result dtypes follow the PyTorch chain: q and k are fp32 when the rotary embedding is applied
 (its fp32 cache promotes them) or when cos-attention normalises under autocast, else the input
@@ -21,7 +24,14 @@ import torch
 
 from . import _native
 
-__all__ = ["prepare_qkv", "rope_rows"]
+__all__ = ["prepare_qkv", "prepared_dtypes", "rope_rows"]
+
+
+def prepared_dtypes(qkv_dtype: torch.dtype, *, cos_attention: bool, rope: bool):
+    """(q/k dtype, v dtype) that ``prepare_qkv`` returns by default, as the PyTorch chain gives
+    them: fp32 q/k when the rotary embedding runs or cos-attention normalises under autocast."""
+    fp32 = rope or (cos_attention and torch.is_autocast_enabled())
+    return (torch.float32 if fp32 else qkv_dtype), qkv_dtype
 
 
 def rope_rows(rope2d_freqs_grid, scale_schedule, scale_ind: int, seq_len: int,
@@ -44,13 +54,17 @@ def rope_rows(rope2d_freqs_grid, scale_schedule, scale_ind: int, seq_len: int,
 
 def prepare_qkv(qkv: torch.Tensor, *, scale_mul: Optional[torch.Tensor] = None,
                 eps: float = 1e-12, rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
-                qk_dtype: Optional[torch.dtype] = None):
+                qk_dtype: Optional[torch.dtype] = None,
+                append: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None):
     """``qkv`` ``[B, L, 3, H, 128]`` (bf16/f16) -> ``q, k, v`` ``[B, H, L, 128]``.
 
     ``scale_mul``: the cos-attention head scales (any shape with H elements, e.g. the
     ``scale_mul_1H11.clamp_max(max).exp()`` tensor), or None for no normalisation. ``rope``:
     ``(cos, sin)`` rows ``[L, 64]`` fp32 (``rope_rows``), or None. ``qk_dtype``: defaults to fp32
-    when ``rope`` is given or autocast is enabled with ``scale_mul``, else ``qkv.dtype``."""
+    when ``rope`` is given or autocast is enabled with ``scale_mul``, else ``qkv.dtype``.
+    ``append``: ``(slab_k, slab_v, offsets)`` - the layer's slab ``[B, capacity, 128]`` (K in the
+    q/k dtype, V in ``qkv.dtype``) and an int64 ``[H]`` device tensor of slab offsets (-1 = head
+    not written); head h's rows then also land in ``slab[:, offsets[h] + l]``."""
     if qkv.ndim != 5 or qkv.shape[2] != 3:
         raise ValueError("prepare_qkv expects qkv shaped [B, L, 3, H, D]")
     B, L, _, H, D = qkv.shape
@@ -64,8 +78,8 @@ def prepare_qkv(qkv: torch.Tensor, *, scale_mul: Optional[torch.Tensor] = None,
     dev = qkv.device
     qkv = qkv.contiguous()
     if qk_dtype is None:
-        fp32 = rope is not None or (scale_mul is not None and torch.is_autocast_enabled())
-        qk_dtype = torch.float32 if fp32 else qkv.dtype
+        qk_dtype = prepared_dtypes(qkv.dtype, cos_attention=scale_mul is not None,
+                                   rope=rope is not None)[0]
     q = torch.empty(B, H, L, D, dtype=qk_dtype, device=dev)
     k = torch.empty_like(q)
     v = torch.empty(B, H, L, D, dtype=qkv.dtype, device=dev)
@@ -85,9 +99,24 @@ def prepare_qkv(qkv: torch.Tensor, *, scale_mul: Optional[torch.Tensor] = None,
         if cos.device != dev or sin.device != dev:
             raise ValueError("rope rows must be on the qkv device")
         stride = int(cos.stride(0))
-    _native.check(lib.heatkv_qkv_prepare(
-        _native.ptr(qkv), _native.ptr(q), _native.ptr(k), _native.ptr(v),
-        _native.DTYPE_CODES[qkv.dtype], _native.DTYPE_CODES[qk_dtype], B, L, H, D,
-        _native.ptr(sm), float(eps), _native.ptr(cos), _native.ptr(sin), stride,
-        _native.stream_handle(dev)), "prepare_qkv")
+    args = (_native.ptr(qkv), _native.ptr(q), _native.ptr(k), _native.ptr(v),
+            _native.DTYPE_CODES[qkv.dtype], _native.DTYPE_CODES[qk_dtype], B, L, H, D,
+            _native.ptr(sm), float(eps), _native.ptr(cos), _native.ptr(sin), stride)
+    if append is None:
+        _native.check(lib.heatkv_qkv_prepare(*args, _native.stream_handle(dev)), "prepare_qkv")
+        return q, k, v
+    slab_k, slab_v, offsets = append
+    if (slab_k.ndim != 3 or slab_k.shape != slab_v.shape or slab_k.shape[0] != B
+            or slab_k.shape[2] != D):
+        raise ValueError("append slabs must be [B, capacity, 128] and alike")
+    if slab_k.dtype != qk_dtype or slab_v.dtype != qkv.dtype:
+        raise ValueError("append slab dtypes must be the prepared k and v dtypes")
+    if not (slab_k.is_contiguous() and slab_v.is_contiguous()):
+        raise ValueError("append slabs must be contiguous")
+    if (offsets.dtype != torch.int64 or offsets.numel() != H or not offsets.is_contiguous()
+            or offsets.device != dev or slab_k.device != dev or slab_v.device != dev):
+        raise ValueError("append offsets must be a contiguous int64 [H] tensor on the qkv device")
+    _native.check(lib.heatkv_qkv_prepare_append(
+        *args, _native.ptr(slab_k), _native.ptr(slab_v), int(slab_k.shape[1]),
+        _native.ptr(offsets), _native.stream_handle(dev)), "prepare_qkv")
     return q, k, v

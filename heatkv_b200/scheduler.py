@@ -114,6 +114,44 @@ def copy_descriptors(runs):
             "item_count": len(items)}
 
 
+def prep_append_split(schedule, scale: int, num_heads: int):
+    """Split the append after ``scale`` (``append_runs_by_key[(scale, scale + 1)]``) into the heads
+    whose rows the q/k/v preparation of that scale may write straight into the slab
+    (``heatkv_qkv_prepare_append``) and the copy runs left for the pack after the attention.
+
+    The reference appends after the attention of ``scale`` (enable_real_pruning_fast.py:2218-2225),
+    because a new segment may take slots freed by segments that the attention of ``scale`` still
+    reads (their live interval ends at ``scale + 1``). A head's rows can be written before that
+    attention only when its segment shares no slot with any segment live at ``scale``; the slab
+    then holds the same bytes after the attention as with the reference's order.
+
+    Returns None when nothing is appended, else ``{"offsets": int64 [num_heads] (-1 = not written
+    by the preparation), "early_slots": int, "rest_runs": runs for ``copy_descriptors``}``."""
+    runs = schedule["append_runs_by_key"].get((scale, scale + 1))
+    if not runs:
+        return None
+    reads = sorted((seg["offset"], seg["offset"] + seg["length"])
+                   for seg in schedule["segments_by_target"].get(scale, []) if seg["length"] > 0)
+    starts = np.array([r[0] for r in reads], dtype=np.int64)
+    ends = np.array([r[1] for r in reads], dtype=np.int64)
+    offsets = np.full(int(num_heads), -1, dtype=np.int64)
+    early, rest = 0, []
+    for run in runs:
+        seq_len = run["sequence_len"]
+        for it in run["copy_items"]:
+            lo, hi = it["dst_start"], it["dst_start"] + it["length"]
+            clash = bool(np.any((starts < hi) & (ends > lo)))
+            whole = it["src_start"] % seq_len == 0 and it["length"] == seq_len
+            if clash or not whole:
+                rest.append({"dst_offset": lo, "head": it["src_start"] // seq_len,
+                             "src_start": it["src_start"] % seq_len, "length": it["length"]})
+            else:
+                offsets[it["src_start"] // seq_len] = lo
+                early += it["length"]
+    seq_len = runs[0]["sequence_len"]
+    return {"offsets": offsets, "early_slots": int(early), "rest_runs": _copy_runs(rest, seq_len)}
+
+
 def build_static_slot_schedule(controller, *, layer_idx: int, num_heads: int,
                                allow_overalloc: bool = True):
     """Return the reference's schedule dict (keys ``enabled``, ``capacity``, ``capacity_bound``,

@@ -12,6 +12,8 @@
  * QKV projection (enable_real_pruning_fast.py:2040-2072):
  *   - heatkv_qkv_prepare         <- unbind/permute, F.normalize * scale_mul, apply_rotary_emb
  *                                  (infinity/models/basic.py:97-117)
+ *   - heatkv_qkv_prepare_append  <- the same, plus the slab append of the scale
+ *                                  (enable_real_pruning_fast.py:2218-2225) for hazard-free heads
  *
  * Conventions
  *   - Every pointer argument is a device pointer unless stated otherwise; tensors are dense,
@@ -362,6 +364,25 @@ int heatkv_qkv_prepare(const void* qkv, void* q, void* k, void* v, int in_dtype,
                        int64_t batch, int64_t seq_len, int64_t heads, int64_t head_dim,
                        const float* scale_mul, float eps, const float* rope_cos,
                        const float* rope_sin, int64_t rope_row_stride, void* stream);
+
+/*
+ * heatkv_qkv_prepare_append - heatkv_qkv_prepare that also writes the slab append of this scale
+ * (enable_real_pruning_fast.py:2218-2225 -> _segmented_flat_static_append_current :969-1024) for
+ * the heads given an offset: slab_k[b, slab_offset[h] + l, :] = k[b, h, l, :] and the same for v,
+ * for every b and l, with slab_offset an int64 [heads] device array (-1 = head not written here).
+ *   slab_k : [batch, slab_rows, head_dim] (qk_dtype); slab_v : [batch, slab_rows, head_dim]
+ *            (in_dtype) - the layer's flat slab.
+ * Only heads whose segment shares no slot with the segments the same scale's attention reads may
+ * be given here (the attention runs after this call); the rest stay with heatkv_pack_kv after the
+ * attention. A head whose segment leaves the slab is skipped and raises
+ * HEATKV_DEVICE_PACK_OUT_OF_RANGE. slab_k is aligned like q, slab_v and slab_offset 8-byte aligned.
+ */
+int heatkv_qkv_prepare_append(const void* qkv, void* q, void* k, void* v, int in_dtype,
+                              int qk_dtype, int64_t batch, int64_t seq_len, int64_t heads,
+                              int64_t head_dim, const float* scale_mul, float eps,
+                              const float* rope_cos, const float* rope_sin,
+                              int64_t rope_row_stride, void* slab_k, void* slab_v,
+                              int64_t slab_rows, const int64_t* slab_offset, void* stream);
 
 /*
  * heatkv_slot_schedule - host-side slab placement of one layer's static schedule, replacing the

@@ -196,3 +196,57 @@ def test_fused_qkv_prep_matches_the_torch_chain():
     for a, b in zip(*outs):
         err = (a - b).abs().max().item()
         assert err <= 2e-2 and err / b.abs().max().item() <= 1e-2, err
+
+
+def test_prep_append_leaves_outputs_and_slabs_bit_identical():
+    """With fused_qkv_prep the preparation writes the append heads whose new segment is clear of
+    the scale's live segments into the slab before the attention (scheduler.prep_append_split).
+    Against the same model with every append left to the pack after the attention (the
+    reference's order, :2218-2225), every output and every slab segment live at the next scale is
+    bit-identical, and the slot counters add up: early + packed = the reference's append slots."""
+    dev = torch.device("cuda", 0)
+    L, H, C = 3, 16, 2048
+    schedule = synthetic.SCALE_SCHEDULE_1M
+    n_tok = sum(a * b * c for a, b, c in schedule)
+    g = torch.Generator().manual_seed(3)
+    angles = torch.rand(1, 1, 1, n_tok, 64, generator=g) * 6.0
+    freqs = {str(tuple(schedule)): torch.stack([torch.cos(angles), torch.sin(angles)]).to(dev)}
+    orders = synthetic.random_removal_orders(L, H, seed=11)
+    xs = [[torch.randn(2, h * w, C, device=dev) for _, h, w in schedule] for _ in range(L)]
+    runs = []
+    for early in (True, False):
+        torch.manual_seed(0)
+        model = nn.ModuleList([SelfAttention(C, H, True) for _ in range(L)]).to(dev)
+        enable_real_pruning_scale_specific_fused_segmented(
+            model, 0.10, orders, protected_prefix_scales=3, source_scale_start=3,
+            fused_qkv_prep=True)
+        for m in model:
+            m.kv_caching(True)
+        set_real_pruning_fast_phase_profile_enabled(True)
+        snapshot_real_pruning_fast_phase_profile(reset=True)
+        outs, slabs = [], []
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            for t in range(len(schedule)):
+                for l, m in enumerate(model):
+                    if not early:
+                        m._heatkv_layer.prep_append.clear()
+                    outs.append(m(xs[l][t], None, scale_schedule=schedule,
+                                  rope2d_freqs_grid=freqs, scale_ind=t))
+                    if getattr(m, "_real_pruning_segmented_cache_active", False):
+                        for seg in m._heatkv_layer.schedule["segments_by_target"][t + 1]:
+                            lo, hi = seg["offset"], seg["offset"] + seg["length"]
+                            slabs.append((l, t, seg["source_scale"], seg["head"],
+                                          m._heatkv_slab_k[:, lo:hi].clone(),
+                                          m._heatkv_slab_v[:, lo:hi].clone()))
+        stats = snapshot_real_pruning_fast_phase_profile(reset=True)["segmented_flat_stats"]
+        set_real_pruning_fast_phase_profile_enabled(False)
+        runs.append((outs, slabs, stats))
+    assert _native.device_status(dev) == 0
+    (oa, sa, ca), (ob, sb, cb) = runs
+    assert ca.get("prep_append_slots", 0) > 0 and cb.get("prep_append_slots", 0) == 0
+    assert ca["prep_append_slots"] + ca.get("append_copy_slots", 0) == cb["append_copy_slots"]
+    assert len(oa) == len(ob) and all(torch.equal(a, b) for a, b in zip(oa, ob))
+    assert len(sa) == len(sb) > 0
+    for a, b in zip(sa, sb):
+        assert a[:4] == b[:4]
+        assert torch.equal(a[4], b[4]) and torch.equal(a[5], b[5]), a[:4]

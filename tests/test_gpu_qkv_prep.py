@@ -6,7 +6,9 @@ infinity/models/basic.py:97-117, restated below.
 Without cos-attention every output is bit-identical (the permute is a copy and the rotary
 embedding rounds each product and sum exactly as the elementwise ops do). With cos-attention the
 row norm is a reduction whose order differs from PyTorch's, so q and k agree to fp32 rounding:
-max |err| <= 1e-6 on unit-norm rows scaled by at most 100.
+max |err| <= 1e-6 on unit-norm rows scaled by at most 100. With ``append=`` the given heads' k/v
+rows also land in the slab, bit for bit (the reference's append copy,
+enable_real_pruning_fast.py:969-1024).
 """
 
 import math
@@ -115,4 +117,64 @@ def test_validation_errors():
         prepare_qkv(qkv, rope=(bad, bad))
     with pytest.raises(ValueError, match="one value per head"):
         prepare_qkv(qkv, scale_mul=torch.ones(3, device="cuda"))
+    assert _native.device_status() == 0
+
+
+def _append_case(B, L, H, rope, seed):
+    qkv, _, grid = _inputs(B, L, H, torch.bfloat16, seed=seed)
+    rows = (grid[0, 0, 0, 0, :L], grid[1, 0, 0, 0, :L]) if rope else None
+    qk_dtype = torch.float32 if rope else torch.bfloat16
+    cap = 3 * H * L + 11
+    slab_k = torch.full((B, cap, 128), 7.0, dtype=qk_dtype, device="cuda")
+    slab_v = torch.full((B, cap, 128), -7.0, dtype=torch.bfloat16, device="cuda")
+    return qkv, rows, slab_k, slab_v, cap
+
+
+@pytest.mark.parametrize("rope", [False, True])
+@pytest.mark.parametrize("B,L,H", [(2, 1, 16), (2, 36, 16), (1, 576, 28)])
+def test_append_writes_the_given_heads_into_the_slab(rope, B, L, H):
+    """``append=``: head h's k/v rows land in slab[:, offsets[h] + l] bit for bit, heads with
+    offset -1 and every other slot keep their contents, and q/k/v are those of the plain call."""
+    qkv, rows, slab_k, slab_v, cap = _append_case(B, L, H, rope, seed=L + H)
+    offs = np.full(H, -1, dtype=np.int64)
+    for j, h in enumerate(range(0, H, 3)):
+        offs[h] = 11 + (2 * j + 1) * L  # disjoint segments, gaps between them
+    offsets = torch.from_numpy(offs).cuda()
+    want_k, want_v = slab_k.clone(), slab_v.clone()
+    q, k, v = prepare_qkv(qkv, rope=rows, append=(slab_k, slab_v, offsets))
+    rq, rk, rv = prepare_qkv(qkv, rope=rows)
+    assert torch.equal(q, rq) and torch.equal(k, rk) and torch.equal(v, rv)
+    for h in range(H):
+        if offs[h] >= 0:
+            want_k[:, offs[h]:offs[h] + L] = k[:, h]
+            want_v[:, offs[h]:offs[h] + L] = v[:, h]
+    assert torch.equal(slab_k, want_k) and torch.equal(slab_v, want_v)
+    assert _native.device_status() == 0
+
+
+def test_append_outside_the_slab_is_skipped_and_flagged():
+    """A segment that would leave the slab is not written (the other heads are) and raises
+    HEATKV_DEVICE_PACK_OUT_OF_RANGE (0x1)."""
+    B, L, H = 2, 36, 16
+    qkv, rows, slab_k, slab_v, cap = _append_case(B, L, H, False, seed=4)
+    offs = np.full(H, -1, dtype=np.int64)
+    offs[2], offs[5] = 0, cap - L + 1
+    want_k, want_v = slab_k.clone(), slab_v.clone()
+    _, k, v = prepare_qkv(qkv, append=(slab_k, slab_v, torch.from_numpy(offs).cuda()))
+    want_k[:, :L] = k[:, 2]
+    want_v[:, :L] = v[:, 2]
+    assert _native.device_status() == 0x1
+    assert torch.equal(slab_k, want_k) and torch.equal(slab_v, want_v)
+
+
+def test_append_validation():
+    qkv = torch.zeros(1, 4, 3, 2, 128, dtype=torch.bfloat16, device="cuda")
+    sk = torch.zeros(1, 8, 128, dtype=torch.bfloat16, device="cuda")
+    offs = torch.zeros(2, dtype=torch.int64, device="cuda")
+    with pytest.raises(ValueError, match="dtypes"):
+        prepare_qkv(qkv, rope=(torch.zeros(4, 64, device="cuda"),) * 2, append=(sk, sk, offs))
+    with pytest.raises(ValueError, match="int64"):
+        prepare_qkv(qkv, append=(sk, sk, offs.int()))
+    with pytest.raises(ValueError, match="capacity"):
+        prepare_qkv(qkv, append=(sk, sk[:, :4, :64], offs))
     assert _native.device_status() == 0
