@@ -51,6 +51,10 @@ SIGNATURES = {
     "heatkv_segmented_attention_sched": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i,
                                               _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float,
                                               _i, _p, _i, _i64, _p, ctypes.c_size_t, _p]),
+    "heatkv_segmented_attention_mapped": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i,
+                                               _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float,
+                                               _i, _p, _i, _i64, _p, _i64, _i, _p, ctypes.c_size_t,
+                                               _p]),
     "heatkv_segmented_attention_scatter": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _p, _p,
                                                 _i64, _i64, _i, _i, _i, _i64, _i64, _i64, _i64,
                                                 _i64, _i64, ctypes.c_float, _p, _p]),

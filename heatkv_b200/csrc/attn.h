@@ -32,6 +32,10 @@ struct AttnArgs {
   size_t workspace_bytes = 0;
   unsigned int* status = nullptr;       // device status word (device_status_ptr())
   bool static_meta = false;             // metadata not written by the preceding stream work
+  // column-split kernel: CTA c of map_grid runs items item_map[c + k * map_grid] (-1 = none)
+  const int32_t* item_map = nullptr;
+  int64_t map_len = 0;
+  int map_grid = 0;
   // scatter epilogue (tcgen05 kernel, unsplit): rows to n_out full outputs at mapped rows/heads
   void* const* out_ptrs = nullptr;      // [n_out] device array of base pointers
   const int32_t* out_rows = nullptr;    // [batch] -> row of the full output
@@ -61,7 +65,25 @@ cudaError_t launch_attention_sm100_cs(const AttnArgs& a, bool bf16, cudaStream_t
 bool attention_prefers_pair(int64_t batch, int64_t heads, int64_t q_len);
 cudaError_t launch_attention_sm100_tf32(const AttnArgs& a, bool v_bf16, cudaStream_t st);
 // Splits chosen by kv_splits = 0 and the workspace bytes a launch with `splits` needs.
+// Key-range split scratch shared by the tcgen05 kernels: per split block a counter (zero between
+// calls, in a fixed region at the start of the workspace), and per row of every split its (m, l)
+// and unnormalised fp32 O row.
+constexpr int kMaxKvSplits = 4;
+constexpr int64_t kSplitCounterBlocks = 16384;
+struct SplitScratch {
+  uint32_t* counter;
+  float2* ml;
+  float* o;
+};
+// Carve the scratch of split_blocks blocks of rows_per_block query rows, split `splits` ways, out
+// of the workspace; false when splits <= 1, the workspace is absent, small or misaligned, or there
+// are more split blocks than counters.
+bool split_scratch(void* ws, size_t bytes, int64_t split_blocks, int splits, int rows_per_block,
+                   SplitScratch* out);
+
 int attention_auto_splits(int64_t batch, int64_t heads, int64_t q_len);
+// kv_splits = 0 for the column-split kernel: enough splits of every 128-row block for two waves
+int attention_cs_auto_splits(int64_t batch, int64_t heads, int64_t q_len);
 size_t attention_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int splits);
 
 cudaError_t launch_pack_kv(void* dst_k, void* dst_v, const void* src_k, const void* src_v,

@@ -67,7 +67,7 @@ constexpr uint32_t kTileBytes = 2 * kHalfBytes;  // 128 x 128 x 2 bytes
 constexpr uint32_t kTmemCols = 512;
 constexpr int kMaxHeads = 128;
 constexpr int kMaxSegTable = 2048;               // heads x segments kept in shared memory
-constexpr int kMaxSplits = 4;             // key-range splits per query block
+constexpr int kMaxSplits = kMaxKvSplits;  // key-range splits per query block
 
 struct __align__(1024) Smem {
   uint8_t q[kNQ][kTileBytes];
@@ -686,23 +686,35 @@ struct WsLayout {
 };
 
 // The per-block counters live in a fixed region at the start of the workspace that nothing else
-// ever writes: calls of different shapes share one workspace, and a counter must find zero
-// where an earlier call may have left partial results had the regions moved with the shape.
-constexpr int64_t kMaxCounterBlocks = 16384;
-
-static WsLayout ws_layout(int64_t blocks, int splits) {
+// ever writes: calls of different shapes (and both tcgen05 kernels) share one workspace, and a
+// counter must find zero where an earlier call may have left partial results had the regions
+// moved with the shape.
+static WsLayout ws_layout(int64_t blocks, int splits, int rows_per_block) {
   WsLayout w{};
   if (splits <= 1) return w;
   auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
   w.counter_off = 0;
-  w.ml_off = size_t(kMaxCounterBlocks) * sizeof(uint32_t);
-  const size_t rows = size_t(blocks) * size_t(splits) * (kNQ * kBM);
+  w.ml_off = size_t(kSplitCounterBlocks) * sizeof(uint32_t);
+  const size_t rows = size_t(blocks) * size_t(splits) * size_t(rows_per_block);
   w.o_off = w.ml_off + up(rows * sizeof(float2));
   w.total = w.o_off + up(rows * kD * sizeof(float));
   return w;
 }
 
 }  // namespace sm100
+
+bool split_scratch(void* ws, size_t bytes, int64_t split_blocks, int splits, int rows_per_block,
+                   SplitScratch* out) {
+  const sm100::WsLayout wl = sm100::ws_layout(split_blocks, splits, rows_per_block);
+  if (splits <= 1 || split_blocks > kSplitCounterBlocks || ws == nullptr || bytes < wl.total ||
+      (reinterpret_cast<uintptr_t>(ws) & 255u))
+    return false;
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  out->counter = reinterpret_cast<uint32_t*>(base + wl.counter_off);
+  out->ml = reinterpret_cast<float2*>(base + wl.ml_off);
+  out->o = reinterpret_cast<float*>(base + wl.o_off);
+  return true;
+}
 
 int attention_auto_splits(int64_t batch, int64_t heads, int64_t q_len) {
   using namespace sm100;
@@ -715,9 +727,15 @@ int attention_auto_splits(int64_t batch, int64_t heads, int64_t q_len) {
 size_t attention_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int splits) {
   using namespace sm100;
   if (splits <= 0) splits = attention_auto_splits(batch, heads, q_len);
-  const int64_t blocks = batch * heads * ((q_len + kNQ * kBM - 1) / (kNQ * kBM));
-  if (blocks > kMaxCounterBlocks) return 0;
-  return ws_layout(blocks, std::min(splits, kMaxSplits)).total;
+  splits = std::min(splits, kMaxKvSplits);
+  // enough for either kernel: 256-row blocks (two-tile) or 128-row blocks (column split)
+  const int64_t pair_blocks = batch * heads * ((q_len + kNQ * kBM - 1) / (kNQ * kBM));
+  const int64_t cs_blocks = batch * heads * ((q_len + kBM - 1) / kBM);
+  size_t need = 0;
+  if (pair_blocks <= kSplitCounterBlocks) need = ws_layout(pair_blocks, splits, kNQ * kBM).total;
+  if (cs_blocks <= kSplitCounterBlocks)
+    need = std::max(need, ws_layout(cs_blocks, splits, kBM).total);
+  return need;
 }
 
 cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st) {
@@ -737,16 +755,14 @@ cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st
   const int64_t blocks = a.batch * a.heads * qpairs;
   int splits = a.kv_splits <= 0 ? attention_auto_splits(a.batch, a.heads, a.q_len) : a.kv_splits;
   if (splits > kMaxSplits) splits = kMaxSplits;
-  if (blocks > kMaxCounterBlocks) splits = 1;
   int64_t unsplit = splits > 1 ? std::min<int64_t>(std::max<int64_t>(a.unsplit_blocks, 0), blocks)
                                : blocks;
   if (unsplit == blocks) splits = 1;
-  WsLayout wl = ws_layout(blocks - unsplit, splits);
-  if (splits > 1 && (a.workspace == nullptr || a.workspace_bytes < wl.total ||
-                     (reinterpret_cast<uintptr_t>(a.workspace) & 255u))) {
+  SplitScratch scratch{};
+  if (splits > 1 && !split_scratch(a.workspace, a.workspace_bytes, blocks - unsplit, splits,
+                                   kNQ * kBM, &scratch)) {
     splits = 1;  // no (or too small) workspace: run unsplit
     unsplit = blocks;
-    wl = ws_layout(0, 1);
   }
   const int64_t n_items = unsplit + (blocks - unsplit) * splits;
   if (n_items >= (int64_t(1) << 31)) return cudaErrorNotSupported;
@@ -777,10 +793,9 @@ cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st
   p.out_heads_total = static_cast<int>(a.out_heads_total);
   if (a.n_out > 0 && splits != 1) return cudaErrorNotSupported;
   p.status = a.status;
-  uint8_t* ws = static_cast<uint8_t*>(a.workspace);
-  p.ws_counter = splits > 1 ? reinterpret_cast<uint32_t*>(ws + wl.counter_off) : nullptr;
-  p.ws_ml = splits > 1 ? reinterpret_cast<float2*>(ws + wl.ml_off) : nullptr;
-  p.ws_o = splits > 1 ? reinterpret_cast<float*>(ws + wl.o_off) : nullptr;
+  p.ws_counter = splits > 1 ? scratch.counter : nullptr;
+  p.ws_ml = splits > 1 ? scratch.ml : nullptr;
+  p.ws_o = splits > 1 ? scratch.o : nullptr;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.qpairs = qpairs;
   p.splits = splits;

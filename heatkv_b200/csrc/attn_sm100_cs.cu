@@ -43,6 +43,20 @@
 // Items are (head, batch row, 128-row query block) in longest-head-first order (head_order); CTA c
 // of a persistent grid runs items c, c + grid, ... Every wait is bounded (common.cuh); on expiry
 // the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains its copies and MMAs, frees TMEM and returns.
+//
+// Key-range splits (16-bit mode): the blocks after the first `unsplit` (schedule order) are cut
+// into `splits` contiguous ranges of their key tiles, one item each. A split writes its row
+// maxima and sums (m, l) and its unnormalised O rows (fp32) to the workspace; the CTA that
+// completes a block's last split (an atomic counter per block) merges them,
+//   O = sum_k 2^(m_k - M) O_k / sum_k 2^(m_k - M) l_k,  M = max over splits with l_k > 0,
+// and writes the block's output. A split without key tiles (a block with fewer tiles than splits)
+// only publishes (m, l) = (-inf, 0).
+//
+// Item map (optional, planned on the host from the static segment tables): CTA c runs the items
+// item_map[c], item_map[c + grid], ... instead of c, c + grid, ...; -1 marks an empty slot. The
+// pre-planned hot path assigns items greedily, longest first, to the least-loaded CTA, which a
+// fixed round-robin order cannot do. Entries outside the item space are skipped and raise
+// HEATKV_DEVICE_BAD_ITEM_MAP.
 #include "attn.h"
 #include "common.cuh"
 #include "sm100_util.cuh"
@@ -63,6 +77,7 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 384;
 constexpr int kMaxHeads = 128;
 constexpr int kMaxSegTable = 2048;
+constexpr int kMapRounds = 64;    // item map slots of a CTA staged in shared memory
 
 template <bool kTf32, bool kIndep = false>
 struct Mode {
@@ -91,6 +106,7 @@ struct __align__(1024) Smem {
   uint64_t drain;      // both issuers' products have completed
   uint32_t tmem_base;
   int abort_flag;
+  int last_flag;       // this CTA completed the last split of its block
   float red_max[2][kWG][kBM];  // [tile parity][warpgroup][row]: part-row maxima
   float red_sum[kWG][kBM];     // [warpgroup][row]: part-row sums of an item
   float2 red_ml[2][2][kBM];    // kIndep: [item parity][warpgroup][row] (running max, row sum)
@@ -99,6 +115,7 @@ struct __align__(1024) Smem {
   int head_tiles[kMaxHeads];
   int seg_start[kMaxSegTable];
   int seg_end[kMaxSegTable];
+  int slot_items[kMapRounds];  // item map: this CTA's first kMapRounds slots, checked
 };
 
 struct Params {
@@ -112,7 +129,14 @@ struct Params {
   unsigned int* status;
   float scale_log2;             // softmax_scale * log2(e)
   int qblocks;                  // ceil(Lq / 128)
-  int n_items;                  // heads * batch * qblocks
+  int n_items;                  // unsplit + (heads * batch * qblocks - unsplit) * splits
+  int splits;                   // key-range splits of each split block (1 = none)
+  const int32_t* item_map;      // [n_slots] item of every slot, -1 = none; null = slot i is item i
+  int n_slots;                  // slots the CTAs walk (n_items without a map)
+  int unsplit;                  // leading blocks (schedule order) that are not split
+  uint32_t* ws_counter;         // [split blocks], zero between calls
+  float2* ws_ml;                // [split blocks * splits * 128]
+  float* ws_o;                  // [split blocks * splits * 128 * 128]
   int seg_stride;
   int static_meta;              // stage the metadata before the dependency wait
   // scatter epilogue (16-bit mode, n_out > 0): every output row goes to n_out full [out_batch,
@@ -126,18 +150,55 @@ struct Params {
 };
 
 struct Item {
-  int h, b, q0, n;  // head, batch row, first query row, key tiles
+  int h, b, q0;       // head, batch row, first query row
+  int j0, n;          // first key tile of the item, key tiles
+  int split, nsplit;  // split index, splits of the block (1 = unsplit)
+  int sblock;         // index of the block among the split blocks
 };
+
+// The item of a map entry (-1: none); an entry outside the item space is skipped and reported.
+__device__ __forceinline__ int checked_item(const Params& p, int item) {
+  if (item >= p.n_items || item < -1) {
+    raise_status(p.status, HEATKV_DEVICE_BAD_ITEM_MAP);
+    return -1;
+  }
+  return item;
+}
+
+// The item of one of this CTA's slots (-1: none): the slot itself without a map, else the map
+// entry, staged in shared memory for the first kMapRounds slots of the CTA.
+template <class SmemT>
+__device__ __forceinline__ int slot_item(const SmemT& sm, const Params& p, int slot) {
+  if (p.item_map == nullptr) return slot;
+  const int k = (slot - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x);
+  if (k < kMapRounds) return sm.slot_items[k];
+  const int item = __ldg(p.item_map + slot);
+  return (item >= p.n_items || item < -1) ? -1 : item;
+}
 
 template <class SmemT>
 __device__ __forceinline__ Item decode_item(const SmemT& sm, const Params& p, int item) {
   Item it;
-  const int qb = item % p.qblocks;
-  const int rb = item / p.qblocks;
+  int block;
+  if (item < p.unsplit) {
+    block = item;
+    it.split = 0;
+    it.nsplit = 1;
+  } else {
+    const int k = item - p.unsplit;
+    block = p.unsplit + k / p.splits;
+    it.split = k % p.splits;
+    it.nsplit = p.splits;
+  }
+  it.sblock = block - p.unsplit;
+  const int qb = block % p.qblocks;
+  const int rb = block / p.qblocks;
   it.b = rb % static_cast<int>(p.batch);
   it.h = sm.head_order[rb / static_cast<int>(p.batch)];
   it.q0 = qb * kBM;
-  it.n = sm.head_tiles[it.h];
+  const int tiles = sm.head_tiles[it.h];
+  it.j0 = static_cast<int>((int64_t(tiles) * it.split) / it.nsplit);
+  it.n = static_cast<int>((int64_t(tiles) * (it.split + 1)) / it.nsplit) - it.j0;
   return it;
 }
 
@@ -302,6 +363,18 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0 && blockIdx.x == 0)
       raise_status(p.status, HEATKV_DEVICE_BAD_SEGMENT);
+    // this CTA's item map slots (static like the metadata: read before the dependency wait
+    // under HEATKV_ATTN_STATIC_META, so the first item is known as soon as the wait ends); slots
+    // past the first kMapRounds are read and checked from global memory when reached
+    if (p.item_map != nullptr) {
+      for (int k = lane; k < kMapRounds; k += 32) {
+        const int slot = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+        sm.slot_items[k] = slot < p.n_slots ? checked_item(p, __ldg(p.item_map + slot)) : -1;
+      }
+      for (int slot = static_cast<int>(blockIdx.x) + (kMapRounds + lane) * static_cast<int>(gridDim.x);
+           slot < p.n_slots; slot += 32 * static_cast<int>(gridDim.x))
+        checked_item(p, __ldg(p.item_map + slot));
+    }
     if (lane == 0) {
       if (!kTf32) tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_ck);
@@ -322,8 +395,11 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
     if (lane == 0) {
       uint32_t gx = 0, qcnt = 0;
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+      for (int slot = blockIdx.x; ok && slot < p.n_slots; slot += gridDim.x) {
+        const int item = slot_item(sm, p, slot);
+        if (item < 0) continue;
         const Item it = decode_item(sm, p, item);
+        if (it.n == 0) continue;  // an empty split: no Q, no tiles
         const int bh = it.b * H + it.h;
         if constexpr (!kTf32) {
           if (loads_k) {
@@ -339,7 +415,7 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
         const int cur_row0 = bh * Lq;
         const int slab_row0 = static_cast<int>(int64_t(it.b) * p.capacity);
         TileCursor cur;
-        cur.begin(sm, it.h, stride, 0);
+        cur.begin(sm, it.h, stride, it.j0);
         for (int j = 0; j < it.n; ++j, ++gx) {
           const int s = gx % 2;
           // the stage's previous tile (gx - 2) is done with: its QK (K) or its PV (V)
@@ -377,8 +453,11 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
       constexpr uint32_t idesc_qk = kTf32 ? idesc_tf32(kBM, kBN) : idesc_f16(kBF16, kBM, kBN, false, false);
       uint32_t g = 0, qcnt = 0;
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+      for (int slot = blockIdx.x; ok && slot < p.n_slots; slot += gridDim.x) {
+        const int item = slot_item(sm, p, slot);
+        if (item < 0) continue;
         const Item it = decode_item(sm, p, item);
+        if (it.n == 0) continue;
         if (!(ok = mbar_wait(&sm.q_full, qcnt & 1, abort_flag, p.status))) break;
         ++qcnt;
         for (int j = 0; j < it.n; ++j, ++g) {
@@ -427,10 +506,13 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
     constexpr uint32_t idesc_pv = idesc_f16(kBF16, kBM, kD, false, true);
     uint32_t g = 0, ocnt = 0;
     bool ok = true;
-    for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+    for (int slot = blockIdx.x; ok && slot < p.n_slots; slot += gridDim.x) {
+      const int item = slot_item(sm, p, slot);
+      if (item < 0) continue;
       const Item it = decode_item(sm, p, item);
+      if (it.n == 0) continue;
       TileCursor cur;
-      cur.begin(sm, it.h, stride, 0);
+      cur.begin(sm, it.h, stride, it.j0);
       for (int j = 0; j < it.n; ++j, ++g) {
         const uint32_t vs = g % 2;
         const uint32_t b = g % kNumS;
@@ -541,16 +623,117 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
         if (lane == 0) mbar_arrive(&sm.q_full);
       }
     };
+    // workspace row of this thread's query row in split `split` of split block `sblock`
+    auto split_slot = [&](const Item& it, int split) {
+      return (int64_t(it.sblock) * it.nsplit + split) * kBM + row;
+    };
+    // After every softmax thread has published its split's partial rows: count the split in, and
+    // if it was the block's last, merge the partials of this thread's row and columns
+    // [c0, c0 + kCols) into the output. Every softmax thread takes both barriers.
+    auto split_finish = [&](const Item& it) {
+      named_bar_softmax_wg<kWG>();
+      if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(p.ws_counter + it.sblock, 1u);
+        const int last = old == static_cast<unsigned>(it.nsplit - 1) ? 1 : 0;
+        if (last) {
+          p.ws_counter[it.sblock] = 0;  // every split has arrived: reset for the next call
+          __threadfence();
+        }
+        sm.last_flag = last;
+      }
+      named_bar_softmax_wg<kWG>();
+      const int qrow = it.q0 + row;
+      if (!sm.last_flag || qrow >= Lq) return;
+      float2 ml[kMaxKvSplits];
+      float mmax = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < kMaxKvSplits; ++k) {
+        ml[k] = k < it.nsplit ? __ldcg(p.ws_ml + split_slot(it, k)) : make_float2(-INFINITY, 0.f);
+        if (ml[k].y > 0.f) mmax = fmaxf(mmax, ml[k].x);
+      }
+      float wk[kMaxKvSplits];
+      float lsum = 0.f;
+#pragma unroll
+      for (int k = 0; k < kMaxKvSplits; ++k) {
+        wk[k] = ml[k].y > 0.f ? ex2(ml[k].x - mmax) : 0.f;
+        lsum = fmaf(wk[k], ml[k].y, lsum);
+      }
+      const float inv = 1.f / lsum;
+#pragma unroll
+      for (int k = 0; k < kMaxKvSplits; ++k) wk[k] *= inv;
+      OutT* orow = static_cast<OutT*>(p.out) + ((int64_t(it.b) * Lq + qrow) * H + it.h) * kD + c0;
+#pragma unroll 1
+      for (int cc = 0; cc < kCols / 16; ++cc) {  // 16 columns a step, every split's loads in flight
+        float4 v[kMaxKvSplits][4];
+#pragma unroll
+        for (int k = 0; k < kMaxKvSplits; ++k) {
+          const float4* src =
+              reinterpret_cast<const float4*>(p.ws_o + split_slot(it, k) * kD + c0) + cc * 4;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            v[k][i] = wk[k] != 0.f ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float a[16];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int k = 0; k < kMaxKvSplits; ++k) {
+            acc.x = fmaf(wk[k], v[k][i].x, acc.x);
+            acc.y = fmaf(wk[k], v[k][i].y, acc.y);
+            acc.z = fmaf(wk[k], v[k][i].z, acc.z);
+            acc.w = fmaf(wk[k], v[k][i].w, acc.w);
+          }
+          a[4 * i] = acc.x;
+          a[4 * i + 1] = acc.y;
+          a[4 * i + 2] = acc.z;
+          a[4 * i + 3] = acc.w;
+        }
+        if constexpr (kTf32) {
+          float4* d4 = reinterpret_cast<float4*>(orow + cc * 16);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d4[i] = make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]);
+        } else {
+          uint32_t wv[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) wv[i] = pack2<kBF16>(a[2 * i], a[2 * i + 1]);
+          uint4* dst = reinterpret_cast<uint4*>(orow + cc * 16);
+          dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+        }
+      }
+    };
     uint32_t g = 0, ocnt = 0;
     bool ok = true;
-    if (kTf32 && static_cast<int>(blockIdx.x) < p.n_items) load_q(blockIdx.x);
-    for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+    // tf32 mode: the next item of this CTA after slot `slot` (-1: none)
+    auto next_item = [&](int slot) {
+      for (slot += gridDim.x; slot < p.n_slots; slot += gridDim.x) {
+        const int item = slot_item(sm, p, slot);
+        if (item >= 0) return item;
+      }
+      return -1;
+    };
+    if constexpr (kTf32) {
+      const int first = next_item(static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x));
+      if (first >= 0) load_q(first);
+    }
+    for (int slot = blockIdx.x; slot < p.n_slots; slot += gridDim.x) {
+      const int item = slot_item(sm, p, slot);
+      if (item < 0) continue;
       const Item it = decode_item(sm, p, item);
+      if (it.n == 0) {
+        // a split without key tiles (16-bit mode only): it contributes nothing to its block
+        if (w == 0 && it.q0 + row < Lq)
+          __stcg(p.ws_ml + split_slot(it, it.split), make_float2(-INFINITY, 0.f));
+        split_finish(it);
+        continue;
+      }
       float m_run = -INFINITY;
       float l_run = 0.f;
       const bool row_live = it.q0 + row < Lq;
       TileCursor cur;
-      cur.begin(sm, it.h, stride, 0);
+      cur.begin(sm, it.h, stride, it.j0);
       // Every softmax warp takes the same named barriers in the same order, including after an
       // abort (the work is skipped, the barriers are not).
       for (int j = 0; j < it.n; ++j, ++g) {
@@ -647,15 +830,19 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
       }
       // tf32 mode: the item's last QK has completed (its scores were read): stage the next
       // item's Q now, so its first QK overlaps this item's last PV and the epilogue
-      const int next = item + gridDim.x;
-      if (kTf32 && ok && next < p.n_items) load_q(next);
+      if constexpr (kTf32) {
+        const int next = next_item(slot);
+        if (ok && next >= 0) load_q(next);
+      }
       float l_tot, a0 = 1.f, a1 = 0.f;
+      float m_fin = m_run;  // the row's max over the item's keys (scaled, log2 units)
       if constexpr (kIndep) {
         // merge weights of the two halves; WG0's max is finite (key 0 of every tile is valid)
         sm.red_ml[ocnt & 1][w][row] = make_float2(m_run, l_run);
         named_bar_softmax_wg<kWG>();
         const float2 h0 = sm.red_ml[ocnt & 1][0][row], h1 = sm.red_ml[ocnt & 1][1][row];
         const float mm = fmaxf(h0.x, h1.x);
+        m_fin = mm;
         a0 = h0.x == -INFINITY ? 0.f : ex2(h0.x - mm);
         a1 = h1.x == -INFINITY ? 0.f : ex2(h1.x - mm);
         l_tot = h0.y * a0 + h1.y * a1;
@@ -666,11 +853,16 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
 #pragma unroll
         for (int v = 1; v < kWG; ++v) l_tot += sm.red_sum[v][row];
       }
+      const bool split = it.nsplit > 1;
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.o_final, ocnt & 1, abort_flag, p.status));
+      if (split && w == 0 && it.q0 + row < Lq)
+        __stcg(p.ws_ml + split_slot(it, it.split),
+               ok ? make_float2(m_fin, l_tot) : make_float2(-INFINITY, 0.f));
       if (ok) {
         tc_fence_after();
         const int qrow = it.q0 + row;
-        const float inv = 1.f / l_tot;
+        // a split writes its O rows unnormalised (the merge divides by the combined sum)
+        const float inv = split ? 1.f : 1.f / l_tot;
         int64_t off = ((int64_t(it.b) * Lq + qrow) * H + it.h) * kD + c0;
         int n_dst = 1;
         bool in_range = true;
@@ -682,9 +874,16 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
           n_dst = p.n_out;
         }
         const bool write = qrow < Lq && in_range;
-        // 16 output columns [col, col + 16) of this row (already normalised)
+        float* ws_row = split ? p.ws_o + split_slot(it, it.split) * kD + c0 : nullptr;
+        // 16 output columns [col, col + 16) of this row (already normalised), or of a split's
+        // partial row
         auto store16 = [&](int col, const float* v) {
-          if constexpr (kTf32) {
+          if (split) {
+            float4* d4 = reinterpret_cast<float4*>(ws_row + col);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              __stcg(d4 + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+          } else if constexpr (kTf32) {
             float4* d4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off + col);
 #pragma unroll
             for (int i = 0; i < 4; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
@@ -740,6 +939,7 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
         if (lane == 0) mbar_arrive(&sm.o_free);
       }
       ++ocnt;
+      if (split) split_finish(it);
     }
   }
 
@@ -790,7 +990,7 @@ static bool independent_halves() {
 template <bool kTf32, bool kBF16, int kWG, bool kIndep = false>
 static cudaError_t launch_t(const CUtensorMap& tq, const CUtensorMap& tck, const CUtensorMap& tcv,
                             const CUtensorMap& tsk, const CUtensorMap& tsv, const Params& p,
-                            cudaStream_t st) {
+                            int map_grid, cudaStream_t st) {
   auto kern = attn_sm100_cs_kernel<kTf32, kBF16, kWG, kIndep>;
   const int smem = static_cast<int>(sizeof(Smem<kTf32, kWG, kIndep>)) + 1024;
   static_assert(sizeof(Smem<kTf32, kWG, kIndep>) + 1024 <= 227 * 1024, "shared memory of one CTA");
@@ -805,7 +1005,8 @@ static cudaError_t launch_t(const CUtensorMap& tq, const CUtensorMap& tck, const
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit);
   }
-  const int grid = static_cast<int>(std::min<int>(p.n_items, sm_count()));
+  // a map fixes the grid it was planned for; otherwise at most one CTA per SM
+  const int grid = p.item_map ? map_grid : static_cast<int>(std::min<int>(p.n_items, sm_count()));
   e = launch_pdl(kern, dim3(grid), dim3(kWG * 128 + 128), static_cast<size_t>(smem), st, tq, tck,
                  tcv, tsk, tsv, p);
   if (e != cudaSuccess) return e;
@@ -826,8 +1027,27 @@ static cudaError_t launch_mode(const AttnArgs& a, cudaStream_t st) {
                           reinterpret_cast<uintptr_t>(a.slab_v) | reinterpret_cast<uintptr_t>(a.out);
   if (align & 15u) return cudaErrorNotSupported;
   const int qblocks = static_cast<int>((a.q_len + kBM - 1) / kBM);
-  const int64_t n_items = a.batch * a.heads * qblocks;
+  const int64_t blocks = a.batch * a.heads * qblocks;
+  // key-range splits: 16-bit mode with the plain epilogue only
+  int splits = a.kv_splits <= 0 ? attention_cs_auto_splits(a.batch, a.heads, a.q_len) : a.kv_splits;
+  splits = std::min(splits, kMaxKvSplits);
+  if (kTf32 || a.n_out > 0) splits = 1;
+  int64_t unsplit = splits > 1 ? std::min<int64_t>(std::max<int64_t>(a.unsplit_blocks, 0), blocks)
+                               : blocks;
+  if (unsplit == blocks) splits = 1;
+  const int requested = splits;
+  SplitScratch scratch{};
+  if (splits > 1 &&
+      !split_scratch(a.workspace, a.workspace_bytes, blocks - unsplit, splits, kBM, &scratch)) {
+    splits = 1;  // no (or too small) workspace: run unsplit
+    unsplit = blocks;
+  }
+  const int64_t n_items = unsplit + (blocks - unsplit) * splits;
   if (n_items >= (int64_t(1) << 31)) return cudaErrorNotSupported;
+  // an item map numbers the items of the requested split layout: kept only when that layout runs
+  // and the map has a slot for every item
+  const bool use_map = a.item_map != nullptr && a.map_grid > 0 && splits == requested &&
+                       a.map_len >= n_items && a.map_len < (int64_t(1) << 31);
   const bool slab = a.capacity > 0;
   const void* sk = slab ? a.slab_k : a.cur_k;
   const void* sv = slab ? a.slab_v : a.cur_v;
@@ -859,6 +1079,13 @@ static cudaError_t launch_mode(const AttnArgs& a, cudaStream_t st) {
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.qblocks = qblocks;
   p.n_items = static_cast<int>(n_items);
+  p.splits = splits;
+  p.unsplit = static_cast<int>(unsplit);
+  p.item_map = use_map ? a.item_map : nullptr;
+  p.n_slots = static_cast<int>(use_map ? a.map_len : n_items);
+  p.ws_counter = splits > 1 ? scratch.counter : nullptr;
+  p.ws_ml = splits > 1 ? scratch.ml : nullptr;
+  p.ws_o = splits > 1 ? scratch.o : nullptr;
   p.seg_stride = static_cast<int>(std::max<int64_t>(a.max_segments, 1));
   p.static_meta = a.static_meta ? 1 : 0;
   p.out_ptrs = a.out_ptrs;
@@ -867,11 +1094,13 @@ static cudaError_t launch_mode(const AttnArgs& a, cudaStream_t st) {
   p.n_out = a.n_out;
   p.out_batch = static_cast<int>(a.out_batch);
   p.out_heads_total = static_cast<int>(a.out_heads_total);
-  if (softmax_warpgroups() == 4) return launch_t<kTf32, kBF16, 4>(tq, tck, tcv, tsk, tsv, p, st);
+  const int mg = a.map_grid;
+  if (softmax_warpgroups() == 4) return launch_t<kTf32, kBF16, 4>(tq, tck, tcv, tsk, tsv, p, mg, st);
   if constexpr (!kTf32) {
-    if (independent_halves()) return launch_t<false, kBF16, 2, true>(tq, tck, tcv, tsk, tsv, p, st);
+    if (independent_halves())
+      return launch_t<false, kBF16, 2, true>(tq, tck, tcv, tsk, tsv, p, mg, st);
   }
-  return launch_t<kTf32, kBF16, 2>(tq, tck, tcv, tsk, tsv, p, st);
+  return launch_t<kTf32, kBF16, 2>(tq, tck, tcv, tsk, tsv, p, mg, st);
 }
 
 }  // namespace cs
@@ -886,6 +1115,13 @@ static cudaError_t launch_mode(const AttnArgs& a, cudaStream_t st) {
 // K/V tile for half the rows). Over those 65 launches its choices came within 0.3 % of the
 // per-launch best and leave the 2-row image (the headline configuration) entirely on the
 // column-split kernel.
+int attention_cs_auto_splits(int64_t batch, int64_t heads, int64_t q_len) {
+  const int64_t blocks = batch * heads * ((q_len + sm100::cs::kBM - 1) / sm100::cs::kBM);
+  const int64_t target = 2 * int64_t(sm100::sm_count());
+  if (blocks <= 0 || blocks >= target) return 1;
+  return static_cast<int>(std::min<int64_t>(kMaxKvSplits, (target + blocks - 1) / blocks));
+}
+
 bool attention_prefers_pair(int64_t batch, int64_t heads, int64_t q_len) {
   using namespace sm100;
   const double sms = static_cast<double>(sm_count());

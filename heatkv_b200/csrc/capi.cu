@@ -184,15 +184,13 @@ static int plan_attention(int q_dtype, int k_dtype, int v_dtype, int64_t batch, 
   if (kernel != HEATKV_ATTN_EXACT && qk32 && !scatter) {
     out->run = HEATKV_RUN_TCGEN05_TF32;
   } else if (kernel != HEATKV_ATTN_EXACT && same16) {
-    // key-range splits exist only in the two-tile kernel; otherwise the cost model chooses
+    // both kernels take key-range splits (unsplit_blocks counts the chosen kernel's blocks:
+    // 256 query rows for the two-tile kernel, 128 for the column split); the cost model chooses
+    (void)kv_splits;
+    (void)has_workspace;
+    (void)unsplit_blocks;
     bool pair = variant == 1;
-    if (variant == 0) {
-      const int splits = kv_splits == 0 ? heatkv::attention_auto_splits(batch, heads, q_len)
-                                        : kv_splits;
-      const int64_t pair_blocks = batch * heads * ((q_len + 255) / 256);
-      pair = (splits > 1 && has_workspace && unsplit_blocks < pair_blocks) ||
-             heatkv::attention_prefers_pair(batch, heads, q_len);
-    }
+    if (variant == 0) pair = heatkv::attention_prefers_pair(batch, heads, q_len);
     out->run = pair ? HEATKV_RUN_TCGEN05_PAIR : HEATKV_RUN_TCGEN05_CS;
   } else {
     if (scatter)
@@ -210,7 +208,9 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
                           int64_t q_len, int64_t capacity, int64_t head_dim, int64_t max_segments,
                           float softmax_scale, int kernel, const int32_t* head_order,
                           int kv_splits, void* workspace, size_t workspace_bytes, void* stream,
-                          const Scatter* scatter = nullptr, int64_t unsplit_blocks = 0) {
+                          const Scatter* scatter = nullptr, int64_t unsplit_blocks = 0,
+                          const int32_t* item_map = nullptr, int64_t map_len = 0,
+                          int map_grid = 0) {
   g_last_error.clear();
   if (!valid_dtype(q_dtype) || !valid_dtype(k_dtype) || !valid_dtype(v_dtype))
     return fail(HEATKV_ERR_UNSUPPORTED,
@@ -248,6 +248,9 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
   a.workspace_bytes = workspace_bytes;
   a.status = heatkv::device_status_ptr();
   a.static_meta = static_meta;
+  a.item_map = item_map;
+  a.map_len = map_len;
+  a.map_grid = map_grid;
   if (scatter) {
     a.out_ptrs = scatter->out_ptrs;
     a.out_rows = scatter->out_rows;
@@ -448,6 +451,34 @@ int heatkv_segmented_attention_sched(const void* q, const void* slab_k, const vo
                         q_dtype, k_dtype, v_dtype, batch, heads, q_len, capacity, head_dim,
                         max_segments, softmax_scale, kernel, head_order, kv_splits, workspace,
                         workspace_bytes, stream, nullptr, unsplit_blocks);
+}
+
+int heatkv_segmented_attention_mapped(
+    const void* q, const void* slab_k, const void* slab_v, const int32_t* seg_starts,
+    const int32_t* seg_ends, const int32_t* seg_counts, const void* cur_k, const void* cur_v,
+    void* out, int q_dtype, int k_dtype, int v_dtype, int64_t batch, int64_t heads, int64_t q_len,
+    int64_t capacity, int64_t head_dim, int64_t max_segments, float softmax_scale, int kernel,
+    const int32_t* head_order, int kv_splits, int64_t unsplit_blocks, const int32_t* item_map,
+    int64_t map_len, int map_grid, void* workspace, size_t workspace_bytes, void* stream) {
+  if (kv_splits < 1 || unsplit_blocks < 0)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT,
+                "heatkv_segmented_attention_mapped: kv_splits >= 1 and unsplit_blocks >= 0 required");
+  if (!item_map || map_len <= 0 || map_len >= (int64_t(1) << 31) || map_grid <= 0 ||
+      map_grid > 65535 || map_len % map_grid != 0)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT,
+                "heatkv_segmented_attention_mapped: item_map of rounds x map_grid slots required");
+  if (kv_splits != 1 && workspace != nullptr) {
+    const size_t need = heatkv::attention_workspace_bytes(batch, heads, q_len, kv_splits);
+    if (workspace_bytes < need)
+      return fail(HEATKV_ERR_INVALID_ARGUMENT,
+                  "heatkv_segmented_attention_mapped: workspace of %zu bytes, %zu needed",
+                  workspace_bytes, need);
+  }
+  return attention_impl(q, slab_k, slab_v, seg_starts, seg_ends, seg_counts, cur_k, cur_v, out,
+                        q_dtype, k_dtype, v_dtype, batch, heads, q_len, capacity, head_dim,
+                        max_segments, softmax_scale, kernel, head_order, kv_splits, workspace,
+                        workspace_bytes, stream, nullptr, unsplit_blocks, item_map, map_len,
+                        map_grid);
 }
 
 size_t heatkv_attention_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len,

@@ -23,6 +23,7 @@ from __future__ import annotations
 
 import ctypes
 import dataclasses
+import heapq
 from typing import Callable, Optional
 
 import numpy as np
@@ -45,31 +46,38 @@ def _makespan(costs: np.ndarray, sms: int) -> float:
 
 
 def plan_attention(slots_per_segment, q_len: int, batch: int, *, sms: int = NUM_SMS,
-                   item_cost: float = 1.5, merge_cost: float = 8.0, min_gain: float = 0.03):
+                   block_rows: int = BLOCK_ROWS, item_cost: float = 1.5,
+                   merge_cost: Optional[float] = None, min_gain: float = 0.03):
     """Length-aware schedule of one attention launch: heads longest first, and how many query
     blocks at the tail of the schedule to split in two key ranges so that the kernel's round-robin
     assignment of items to at most ``sms`` persistent CTAs fills its last wave.
 
-    ``slots_per_segment[h]`` lists the head's segment lengths. Cost model, in units of one
-    128 x 128 query-tile x key-tile step for the block's Q tiles: key tiles x Q tiles of the item,
+    ``slots_per_segment[h]`` lists the head's segment lengths; ``block_rows`` is the kernel's query
+    block (256 rows = two Q tiles for the two-tile kernel, 128 for the column-split kernel). Cost
+    model, in units of one 128 x 128 query-tile x key-tile step: key tiles x Q tiles of the item,
     plus ``item_cost`` per item (Q load, pipeline fill, epilogue) and ``merge_cost`` per half of a
-    split block (partial write, merge). The merge cost was calibrated on the 2B bench step: each
-    half writes a 128 KB fp32 partial and the last CTA reads both back, several tile steps of
-    time, so only the long target-12 launches gain from splitting their tail (about 0.3 ms). The blocks are enumerated in the kernel's order (head rank,
-    batch row, query block); a split of the last ``m`` blocks is taken when it lowers the makespan
-    by ``min_gain`` or more. Returns ``(head_order, splits, unsplit_blocks)``."""
+    split block (partial write, merge; default 8 for 256-row blocks, 4 for 128-row blocks). Each
+    half writes an fp32 partial of its rows (128 KB for 256 rows) and the block's last CTA reads
+    them back, several tile steps of time, so only tails that leave CTAs idle gain. The blocks are
+    enumerated in the kernel's order (head rank, batch row, query block); a split of the last ``m``
+    blocks is taken when it lowers the makespan by ``min_gain`` or more. Returns ``(head_order,
+    splits, unsplit_blocks)``, the blocks counted in ``block_rows`` units."""
+    if block_rows not in (KEY_TILE, 2 * KEY_TILE):
+        raise ValueError("block_rows must be 128 or 256")
+    if merge_cost is None:
+        merge_cost = 8.0 if block_rows == 2 * KEY_TILE else 4.0
     tiles = np.array([sum((int(n) + KEY_TILE - 1) // KEY_TILE for n in segs if n > 0)
                       + (q_len + KEY_TILE - 1) // KEY_TILE for segs in slots_per_segment],
                      dtype=np.int64)
     order = np.argsort(-tiles, kind="stable").astype(np.int32)
-    qpairs = (q_len + BLOCK_ROWS - 1) // BLOCK_ROWS
-    nq = np.full(qpairs, 2, dtype=np.int64)
-    if q_len - (qpairs - 1) * BLOCK_ROWS <= BLOCK_ROWS // 2:
-        nq[-1] = 1
+    nblk = (q_len + block_rows - 1) // block_rows
+    per = block_rows // KEY_TILE
+    nq = np.full(nblk, per, dtype=np.int64)
+    nq[-1] = (q_len - (nblk - 1) * block_rows + KEY_TILE - 1) // KEY_TILE
     n_head = tiles[order]                                                   # [H]
     # block costs in kernel order; halves of a split block (the kernel's j0/n rounding)
-    t_blk = np.broadcast_to(n_head[:, None, None], (len(order), batch, qpairs)).reshape(-1)
-    q_blk = np.broadcast_to(nq[None, None, :], (len(order), batch, qpairs)).reshape(-1)
+    t_blk = np.broadcast_to(n_head[:, None, None], (len(order), batch, nblk)).reshape(-1)
+    q_blk = np.broadcast_to(nq[None, None, :], (len(order), batch, nblk)).reshape(-1)
     whole = (t_blk * q_blk).astype(np.float64) + item_cost
     first = ((t_blk // 2) * q_blk).astype(np.float64) + item_cost + merge_cost
     second = ((t_blk - t_blk // 2) * q_blk).astype(np.float64) + item_cost + merge_cost
@@ -84,6 +92,73 @@ def plan_attention(slots_per_segment, q_len: int, batch: int, *, sms: int = NUM_
             best = (span, u)
     unsplit = best[1]
     return order, (2 if unsplit < blocks else 1), unsplit
+
+
+def _greedy_map(costs: np.ndarray, sms: int):
+    """Items longest first (ties: lower item first), each to the least-loaded CTA (ties: lower
+    CTA); returns the slot map ``[rounds * grid]`` (CTA c's k-th item at ``c + k * grid``, -1 =
+    empty), the grid and the makespan."""
+    n = len(costs)
+    grid = max(1, min(n, sms))
+    heap = [(0.0, c) for c in range(grid)]
+    per_cta = [[] for _ in range(grid)]
+    for item in np.argsort(-costs, kind="stable"):
+        load, c = heapq.heappop(heap)
+        per_cta[c].append(int(item))
+        heapq.heappush(heap, (load + float(costs[item]), c))
+    rounds = max(len(x) for x in per_cta)
+    item_map = np.full(rounds * grid, -1, dtype=np.int32)
+    for c, items in enumerate(per_cta):
+        for k, item in enumerate(items):
+            item_map[c + k * grid] = item
+    return item_map, grid, max(load for load, _ in heap)
+
+
+def plan_column_split(slots_per_segment, q_len: int, batch: int, *, sms: int = NUM_SMS,
+                      splits: Optional[int] = None, item_cost: float = 1.5,
+                      merge_cost: float = 4.0, min_gain: float = 0.03):
+    """Schedule of one column-split launch (128-row blocks): head order, key-range splits, and the
+    item map that assigns the launch's items to its CTAs.
+
+    Heads are ordered shortest first, so the split tail of the block order holds the longest
+    blocks. Cost model as ``plan_attention`` (key tiles + ``item_cost`` per item, + ``merge_cost``
+    per split item). With ``splits=None`` the longest ``k`` blocks are split in two for the ``k``
+    (from a fixed candidate set, 0 included) whose greedy assignment has the lowest makespan, a
+    split taken only when it gains ``min_gain``; a given ``splits`` splits every block that many
+    ways (1 = none). Items then go longest first to the least-loaded CTA.
+    Returns ``(head_order, splits, unsplit_blocks, item_map, grid)``."""
+    tiles = np.array([sum((int(n) + KEY_TILE - 1) // KEY_TILE for n in segs if n > 0)
+                      + (q_len + KEY_TILE - 1) // KEY_TILE for segs in slots_per_segment],
+                     dtype=np.int64)
+    order = np.argsort(tiles, kind="stable").astype(np.int32)
+    nblk = (q_len + KEY_TILE - 1) // KEY_TILE
+    t_blk = np.repeat(tiles[order], batch * nblk)             # blocks in kernel order
+    blocks = len(t_blk)
+
+    def items(unsplit: int, nsplit: int) -> np.ndarray:
+        whole = t_blk[:unsplit].astype(np.float64) + item_cost
+        if nsplit <= 1 or unsplit == blocks:
+            return whole
+        t = t_blk[unsplit:, None]
+        j = np.arange(nsplit)[None, :]
+        n = (t * (j + 1)) // nsplit - (t * j) // nsplit
+        return np.concatenate([whole, (n + item_cost + merge_cost).reshape(-1)])
+
+    if splits is not None:
+        nsplit = max(1, min(int(splits), 4))
+        unsplit = blocks if nsplit == 1 else 0
+    else:
+        nsplit, unsplit = 1, blocks
+        best = _greedy_map(items(blocks, 1), sms)[2]
+        limit = best * (1.0 - min_gain)
+        for k in sorted({1, 2, 4, 8, 12, 16, 24, 32, 48, 64, 96, 128, 192, 256, blocks}):
+            if k > blocks:
+                continue
+            span = _greedy_map(items(blocks - k, 2), sms)[2]
+            if span < limit and span < best:
+                best, nsplit, unsplit = span, 2, blocks - k
+    item_map, grid, _ = _greedy_map(items(unsplit, nsplit), sms)
+    return order, nsplit, unsplit, item_map, grid
 
 
 # heatkv_pack_job of include/heatkv.h
@@ -224,24 +299,41 @@ class HotPath:
         ws_bytes = 0
         import os
         # plan_splits (default: HEATKV_PLAN_SPLITS, else 1): "auto" = tail splits chosen by the
-        # planner, or a fixed number of key-range splits for every block (1 = never split). Only
-        # the two-tile tcgen05 kernel splits key ranges; unsplit launches take the column-split
-        # kernel, which is faster at every target of the 2B image, so the default is 1. A split
-        # block sums its keys in a different order, so outputs are bit-reproducible across
-        # different launch shapes (e.g. head shards) only without splits.
+        # planner for the kernel each launch runs, or a fixed number of key-range splits for
+        # every block (1 = never split). Column-split launches always get an item map (greedy,
+        # longest first); on the 2B image auto splits measured the same as none (665 / 667
+        # TFLOP/s), so the default is 1. A split block sums its keys in a different order, so
+        # outputs are bit-reproducible across launch shapes (e.g. head shards) only unsplit.
         if plan_splits is None:
             plan_splits = os.environ.get("HEATKV_PLAN_SPLITS", "1")
         forced = 0 if str(plan_splits) == "auto" else int(plan_splits)
         natural = os.environ.get("HEATKV_PLAN_ORDER", "lpt") == "natural"
+        dt = _native.DTYPE_CODES
         for i, p in enumerate(self.plans):
             for t in range(self.num_scales):
-                order, splits, unsplit = plan_attention(p.segment_lengths(t), self.tokens[t],
-                                                        self.batch)
-                if forced > 0:
-                    splits, unsplit = forced, 0
-                if natural:
-                    order = np.arange(self.num_heads, dtype=np.int32)
-                self.schedule[(i, t)] = (torch.from_numpy(order).to(self.device), splits, unsplit)
+                # the planner counts blocks of the kernel the launch will run
+                run = self.lib.heatkv_attention_kernel_for(
+                    dt[k_dtype], dt[k_dtype], dt[v_dtype], self.batch, self.num_heads,
+                    self.tokens[t], _native.ATTN_AUTO, 1, 1, 0)
+                imap = None
+                if run == _native.RUN_TCGEN05_CS and not natural:
+                    # column-split kernel: greedy item map (and tail splits of the longest blocks)
+                    order, splits, unsplit, imap, grid = plan_column_split(
+                        p.segment_lengths(t), self.tokens[t], self.batch,
+                        splits=forced if forced > 0 else None)
+                    imap = (torch.from_numpy(imap).to(self.device), grid)
+                else:
+                    rows = 2 * KEY_TILE if run == _native.RUN_TCGEN05_PAIR else KEY_TILE
+                    order, splits, unsplit = plan_attention(p.segment_lengths(t), self.tokens[t],
+                                                            self.batch, block_rows=rows)
+                    if run not in (_native.RUN_TCGEN05_PAIR, _native.RUN_TCGEN05_CS):
+                        splits, unsplit = 1, 0  # tf32 and exact launches run unsplit
+                    if forced > 0:
+                        splits, unsplit = forced, 0
+                    if natural:
+                        order = np.arange(self.num_heads, dtype=np.int32)
+                self.schedule[(i, t)] = (torch.from_numpy(order).to(self.device), splits, unsplit,
+                                         imap)
                 ws_bytes = max(ws_bytes, int(self.lib.heatkv_attention_workspace_bytes(
                     self.batch, self.num_heads, self.tokens[t], splits)))
         self.workspace = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=self.device)
@@ -282,15 +374,21 @@ class HotPath:
                     sk, sv = self.slab_k[i], self.slab_v[i]
                     cap = max(p.capacity, 1)
                 flops = float(4 * n * (p.attention_slots(t) + n).sum() * D * B)
-                order, splits, unsplit = self.schedule[(i, t)]
-                out.append(Launch(
-                    "attention", p.layer, t, lib.heatkv_segmented_attention_sched,
-                    (_native.ptr(q), _native.ptr(sk), _native.ptr(sv), _native.ptr(st),
-                     _native.ptr(en), _native.ptr(ct), _native.ptr(k), _native.ptr(v),
-                     _native.ptr(o), dt[q.dtype], dt[k.dtype], dt[v.dtype], B, H, n, cap, D,
-                     int(st.shape[1]), ctypes.c_float(scale), meta_kernel, _native.ptr(order),
-                     int(splits), int(unsplit), _native.ptr(self.workspace),
-                     self.workspace.numel()), flops))
+                order, splits, unsplit, imap = self.schedule[(i, t)]
+                head = (_native.ptr(q), _native.ptr(sk), _native.ptr(sv), _native.ptr(st),
+                        _native.ptr(en), _native.ptr(ct), _native.ptr(k), _native.ptr(v),
+                        _native.ptr(o), dt[q.dtype], dt[k.dtype], dt[v.dtype], B, H, n, cap, D,
+                        int(st.shape[1]), ctypes.c_float(scale), meta_kernel, _native.ptr(order),
+                        int(splits), int(unsplit))
+                ws = (_native.ptr(self.workspace), self.workspace.numel())
+                if imap is not None:
+                    launch = Launch("attention", p.layer, t, lib.heatkv_segmented_attention_mapped,
+                                    head + (_native.ptr(imap[0]), imap[0].numel(), imap[1]) + ws,
+                                    flops)
+                else:
+                    launch = Launch("attention", p.layer, t, lib.heatkv_segmented_attention_sched,
+                                    head + ws, flops)
+                out.append(launch)
                 row_k = D * k.element_size()
                 row_v = D * v.element_size()
                 jobs = []

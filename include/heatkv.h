@@ -57,6 +57,7 @@ typedef enum {
 #define HEATKV_DEVICE_WAIT_TIMEOUT 0x2u       /* a bounded pipeline wait expired; tile skipped */
 #define HEATKV_DEVICE_BAD_SEGMENT 0x4u        /* a segment lay outside the slab; it was clipped */
 #define HEATKV_DEVICE_GATHER_OUT_OF_RANGE 0x8u /* a shard map entry left dst; chunk skipped */
+#define HEATKV_DEVICE_BAD_ITEM_MAP 0x10u      /* an item map entry outside the launch; skipped */
 
 /* Attention kernel selection for heatkv_segmented_attention. */
 typedef enum {
@@ -248,12 +249,14 @@ int heatkv_enable_peer_access(int peer_device);
 /*
  * heatkv_segmented_attention_sched - heatkv_segmented_attention_ws with the split applied to the
  * tail of the schedule only: the first `unsplit_blocks` query blocks of the schedule order (head
- * rank major, then batch row, then 256-row query block) run whole, every later block is divided
- * into kv_splits (>= 1) key ranges that different CTAs process and the last one merges. A planner
- * that knows the key tiles of every head chooses unsplit_blocks so that the last wave of blocks
- * over the SMs is filled with half-size work instead of leaving SMs idle. The workspace needs at
- * most heatkv_attention_workspace_bytes(batch, heads, q_len, kv_splits). No reference
- * counterpart (the reference's Triton grid has no scheduler).
+ * rank major, then batch row, then query block of the kernel that runs: 256 rows for the
+ * two-tile kernel, 128 for the column-split kernel; heatkv_attention_kernel_for names it) run
+ * whole, every later block is divided into kv_splits (>= 1) key ranges that different CTAs
+ * process and the last one merges. A planner that knows the key tiles of every head chooses
+ * unsplit_blocks so that the last wave of blocks over the SMs is filled with half-size work
+ * instead of leaving SMs idle. The workspace needs at most
+ * heatkv_attention_workspace_bytes(batch, heads, q_len, kv_splits). No reference counterpart
+ * (the reference's Triton grid has no scheduler).
  */
 int heatkv_segmented_attention_sched(const void* q, const void* slab_k, const void* slab_v,
                                      const int32_t* seg_starts, const int32_t* seg_ends,
@@ -264,6 +267,27 @@ int heatkv_segmented_attention_sched(const void* q, const void* slab_k, const vo
                                      float softmax_scale, int kernel, const int32_t* head_order,
                                      int kv_splits, int64_t unsplit_blocks, void* workspace,
                                      size_t workspace_bytes, void* stream);
+
+/*
+ * heatkv_segmented_attention_mapped - heatkv_segmented_attention_sched with an explicit
+ * assignment of the column-split kernel's items to its CTAs: the launch has map_grid CTAs and CTA
+ * c runs, in order, the items item_map[c], item_map[c + map_grid], ... (-1 = empty slot); map_len
+ * (a multiple of map_grid) is the number of slots. Items are numbered as the kernel numbers them:
+ * the first unsplit_blocks blocks of 128 query rows (schedule order), then kv_splits items per
+ * later block. Every item must appear exactly once; an entry outside the item space is skipped
+ * and raises HEATKV_DEVICE_BAD_ITEM_MAP. A planner that knows every block's key tiles fills the
+ * map (e.g. longest first to the least-loaded CTA) so that no CTA runs long while others idle.
+ * The map is a schedule only: the output is the same with or without it, and launches that do
+ * not run the column-split kernel with this split layout (another kernel, tf32 operands, a
+ * workspace too small for the splits) ignore it. No reference counterpart.
+ */
+int heatkv_segmented_attention_mapped(
+    const void* q, const void* slab_k, const void* slab_v, const int32_t* seg_starts,
+    const int32_t* seg_ends, const int32_t* seg_counts, const void* cur_k, const void* cur_v,
+    void* out, int q_dtype, int k_dtype, int v_dtype, int64_t batch, int64_t heads, int64_t q_len,
+    int64_t capacity, int64_t head_dim, int64_t max_segments, float softmax_scale, int kernel,
+    const int32_t* head_order, int kv_splits, int64_t unsplit_blocks, const int32_t* item_map,
+    int64_t map_len, int map_grid, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * heatkv_attention_workspace_bytes - scratch bytes heatkv_segmented_attention_ws needs for these

@@ -391,12 +391,19 @@ def _attention_ws(q, pk, pv, st, en, ct, ck, cv, scale, *, head_order, splits, w
     return out
 
 
+SPLIT_KERNELS = {"pair": (_native.ATTN_TCGEN05_PAIR, 256), "cs": (_native.ATTN_TCGEN05_CS, 128)}
+
+
+@pytest.mark.parametrize("variant", sorted(SPLIT_KERNELS))
 @pytest.mark.parametrize("splits", [1, 2, 3, 4])
 @pytest.mark.parametrize("B,H,L,cap,S", [(1, 3, 129, 1500, 6), (2, 4, 576, 3000, 10),
                                          (2, 16, 1600, 5000, 12), (1, 2, 20, 900, 4)])
-def test_tcgen05_split_kv_and_head_order(splits, B, H, L, cap, S, cuda_device):
+def test_tcgen05_split_kv_and_head_order(variant, splits, B, H, L, cap, S, cuda_device):
     """Split-KV partials merged by the last CTA and a shuffled head order give the same result as
-    the reference; the workspace counters are back to zero after every call."""
+    the reference, in both tcgen05 kernels (blocks of 256 or 128 query rows); splits without key
+    tiles (heads with fewer tiles than splits) contribute nothing; the workspace counters are back
+    to zero after every call."""
+    kern, block_rows = SPLIT_KERNELS[variant]
     rng = np.random.default_rng(splits * 7 + L)
     gen = torch.Generator().manual_seed(L + splits)
     d = cuda_device
@@ -411,20 +418,22 @@ def test_tcgen05_split_kv_and_head_order(splits, B, H, L, cap, S, cuda_device):
     ref = _torch_reference(q, pk, pv, st, en, ct, ck, cv, scale)
     for _ in range(2):  # second call reuses the workspace the first one left zeroed
         out = _attention_ws(q, pk, pv, st.to(d), en.to(d), ct.to(d), ck, cv, scale,
-                            head_order=order, splits=splits, workspace=ws)
+                            head_order=order, splits=splits, workspace=ws, kernel=kern)
         _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
     if splits > 1:
-        blocks = B * H * ((L + 255) // 256)
+        blocks = B * H * ((L + block_rows - 1) // block_rows)
         assert int(ws[: 4 * blocks].count_nonzero()) == 0, "split counters not reset"
     assert _native.device_status(d) == 0
 
 
+@pytest.mark.parametrize("variant", sorted(SPLIT_KERNELS))
 @pytest.mark.parametrize("B,H,L,cap,S,splits", [(2, 16, 1600, 5000, 12, 2), (2, 4, 576, 3000, 10, 2),
                                                 (1, 8, 4096, 2000, 6, 3)])
-def test_tcgen05_tail_split_schedule(B, H, L, cap, S, splits, cuda_device):
+def test_tcgen05_tail_split_schedule(variant, B, H, L, cap, S, splits, cuda_device):
     """heatkv_segmented_attention_sched: only the blocks after the first `unsplit` (schedule
-    order) are split; every choice of unsplit gives the reference's result, and the unsplit
-    blocks are bit-identical to an unsplit launch."""
+    order, blocks of the kernel's 256 or 128 query rows) are split; every choice of unsplit gives
+    the reference's result, and the unsplit blocks are bit-identical to an unsplit launch."""
+    kern, block_rows = SPLIT_KERNELS[variant]
     import ctypes
     rng = np.random.default_rng(L + H)
     gen = torch.Generator().manual_seed(L + 3)
@@ -439,11 +448,9 @@ def test_tcgen05_tail_split_schedule(B, H, L, cap, S, splits, cuda_device):
     ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=d)
     scale = 1.0 / math.sqrt(128)
     ref = _torch_reference(q, pk, pv, st.cpu(), en.cpu(), ct.cpu(), ck, cv, scale)
-    # the two-tile kernel throughout: it is the one with key-range splits
-    pair = _native.ATTN_TCGEN05_PAIR
     whole = _attention_ws(q, pk, pv, st, en, ct, ck, cv, scale, head_order=order, splits=1,
-                          workspace=None, kernel=pair)
-    qpairs = (L + 255) // 256
+                          workspace=None, kernel=kern)
+    qpairs = (L + block_rows - 1) // block_rows
     blocks = B * H * qpairs
     dt = _native.DTYPE_CODES
     for unsplit in (0, 1, blocks // 2, blocks - 3, blocks):
@@ -452,7 +459,7 @@ def test_tcgen05_tail_split_schedule(B, H, L, cap, S, splits, cuda_device):
             _native.ptr(q), _native.ptr(pk), _native.ptr(pv), _native.ptr(st), _native.ptr(en),
             _native.ptr(ct), _native.ptr(ck), _native.ptr(cv), _native.ptr(out), dt[q.dtype],
             dt[ck.dtype], dt[cv.dtype], B, H, L, cap, 128, S, ctypes.c_float(scale),
-            pair, _native.ptr(order), splits, unsplit, _native.ptr(ws),
+            kern, _native.ptr(order), splits, unsplit, _native.ptr(ws),
             ws.numel(), _native.stream_handle(d))
         _native.check(status, "heatkv_segmented_attention_sched")
         torch.cuda.synchronize()
@@ -462,16 +469,18 @@ def test_tcgen05_tail_split_schedule(B, H, L, cap, S, splits, cuda_device):
             rank, qp = divmod(blk, qpairs)
             rank, b = divmod(rank, B)
             h = int(order[rank])
-            rows = slice(qp * 256, min(L, qp * 256 + 256))
+            rows = slice(qp * block_rows, min(L, (qp + 1) * block_rows))
             cols = slice(h * 128, (h + 1) * 128)
             assert torch.equal(out[b, rows, cols], whole[b, rows, cols]), (unsplit, blk)
         assert int(ws[: 4 * blocks].count_nonzero()) == 0, "split counters not reset"
     assert _native.device_status(d) == 0
 
 
-def test_workspace_shared_across_shapes(cuda_device):
+@pytest.mark.parametrize("variant", sorted(SPLIT_KERNELS))
+def test_workspace_shared_across_shapes(variant, cuda_device):
     """One workspace serves calls of different shapes in any order (the split counters sit in a
     region no partial result ever overwrites)."""
+    kern = SPLIT_KERNELS[variant][0]
     d = cuda_device
     lib = _native.load()
     shapes = [(2, 4, 576, 3000, 10, 3), (2, 16, 1600, 5000, 12, 2), (1, 3, 129, 1500, 6, 5),
@@ -488,7 +497,7 @@ def test_workspace_shared_across_shapes(cuda_device):
             st, en, ct = _random_layout(rng, H, S, cap)
             order = torch.from_numpy(rng.permutation(H).astype(np.int32)).to(d)
             out = _attention_ws(q, pk, pv, st.to(d), en.to(d), ct.to(d), ck, cv, scale,
-                                head_order=order, splits=sp, workspace=ws)
+                                head_order=order, splits=sp, workspace=ws, kernel=kern)
             ref = _torch_reference(q, pk, pv, st, en, ct, ck, cv, scale)
             _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
     assert _native.device_status(d) == 0
@@ -523,3 +532,116 @@ def test_slab_rows_outside_segments_are_never_used(which, dtype, cuda_device, ke
         np.testing.assert_allclose(out.cpu().numpy(), ref.cpu().numpy(), atol=FP32_ATOL, rtol=FP32_ATOL)
     else:
         _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
+
+
+def _attention_mapped(q, pk, pv, st, en, ct, ck, cv, scale, *, order, splits, unsplit, item_map,
+                      grid, workspace, kernel=_native.ATTN_TCGEN05_CS):
+    import ctypes
+    lib = _native.load()
+    B, H, L, D = q.shape
+    out = torch.full((B, L, H * D), float("nan"), dtype=q.dtype, device=q.device)
+    dt = _native.DTYPE_CODES
+    _native.check(lib.heatkv_segmented_attention_mapped(
+        _native.ptr(q), _native.ptr(pk), _native.ptr(pv), _native.ptr(st), _native.ptr(en),
+        _native.ptr(ct), _native.ptr(ck), _native.ptr(cv), _native.ptr(out), dt[q.dtype],
+        dt[ck.dtype], dt[cv.dtype], B, H, L, pk.shape[1], D, st.shape[1], ctypes.c_float(scale),
+        kernel, _native.ptr(order), splits, unsplit, _native.ptr(item_map), item_map.numel(), grid,
+        _native.ptr(workspace), 0 if workspace is None else workspace.numel(),
+        _native.stream_handle(q.device)), "heatkv_segmented_attention_mapped")
+    return out
+
+
+@pytest.mark.parametrize("splits,unsplit_frac", [(1, 1.0), (2, 0.5), (3, 0.0)])
+@pytest.mark.parametrize("B,H,L,cap,S", [(2, 16, 1600, 5000, 12), (2, 4, 576, 3000, 10),
+                                         (1, 3, 129, 1500, 6)])
+def test_item_map_is_a_schedule_only(splits, unsplit_frac, B, H, L, cap, S, cuda_device):
+    """heatkv_segmented_attention_mapped: any assignment of the column-split kernel's items to its
+    CTAs (a random one, with empty slots, on a grid of 37 CTAs) gives the same bits as the
+    launch without a map; the counters are reset."""
+    rng = np.random.default_rng(L + splits)
+    gen = torch.Generator().manual_seed(L + 7 * splits)
+    d = cuda_device
+    q, ck, cv = (torch.randn(B, H, L, 128, generator=gen).bfloat16().to(d) for _ in range(3))
+    pk, pv = (torch.randn(B, cap, 128, generator=gen).bfloat16().to(d) for _ in range(2))
+    st, en, ct = (x.to(d) for x in _random_layout(rng, H, S, cap))
+    order = torch.from_numpy(rng.permutation(H).astype(np.int32)).to(d)
+    blocks = B * H * ((L + 127) // 128)
+    unsplit = int(blocks * unsplit_frac)
+    n_items = unsplit + (blocks - unsplit) * splits
+    lib = _native.load()
+    ws = torch.zeros(max(int(lib.heatkv_attention_workspace_bytes(B, H, L, splits)), 256),
+                     dtype=torch.uint8, device=d)
+    scale = 1.0 / math.sqrt(128)
+    grid = 37
+    per_cta = [[] for _ in range(grid)]
+    for item in rng.permutation(n_items):
+        per_cta[int(rng.integers(grid))].append(int(item))
+    rounds = max(len(x) for x in per_cta)
+    imap = np.full(rounds * grid, -1, dtype=np.int32)
+    for c, items in enumerate(per_cta):
+        for k, item in enumerate(items):
+            imap[c + k * grid] = item
+    imap = torch.from_numpy(imap).to(d)
+    import ctypes
+    plain = torch.full((B, L, H * 128), float("nan"), dtype=q.dtype, device=d)
+    dt = _native.DTYPE_CODES
+    _native.check(lib.heatkv_segmented_attention_sched(
+        _native.ptr(q), _native.ptr(pk), _native.ptr(pv), _native.ptr(st), _native.ptr(en),
+        _native.ptr(ct), _native.ptr(ck), _native.ptr(cv), _native.ptr(plain), dt[q.dtype],
+        dt[ck.dtype], dt[cv.dtype], B, H, L, cap, 128, S, ctypes.c_float(scale),
+        _native.ATTN_TCGEN05_CS, _native.ptr(order), splits, unsplit, _native.ptr(ws), ws.numel(),
+        _native.stream_handle(d)), "heatkv_segmented_attention_sched")
+    mapped = _attention_mapped(q, pk, pv, st, en, ct, ck, cv, scale, order=order, splits=splits,
+                               unsplit=unsplit, item_map=imap, grid=grid, workspace=ws)
+    torch.cuda.synchronize()
+    assert not torch.isnan(mapped.float()).any()
+    assert torch.equal(mapped, plain)
+    ref = _torch_reference(q, pk, pv, st.cpu(), en.cpu(), ct.cpu(), ck, cv, scale)
+    _check_lowp(mapped.float().cpu().numpy(), ref.cpu().numpy())
+    assert int(ws[: 4 * blocks].count_nonzero()) == 0, "split counters not reset"
+    assert _native.device_status(d) == 0
+
+
+def test_planned_item_map_matches_the_reference(cuda_device):
+    """The hot path's planner (greedy item map, tail splits of the longest blocks) on a layout
+    with uneven heads."""
+    from heatkv_b200.hotpath import plan_column_split
+    rng = np.random.default_rng(5)
+    gen = torch.Generator().manual_seed(5)
+    d = cuda_device
+    B, H, L, cap, S = 2, 16, 576, 6000, 12
+    q, ck, cv = (torch.randn(B, H, L, 128, generator=gen).bfloat16().to(d) for _ in range(3))
+    pk, pv = (torch.randn(B, cap, 128, generator=gen).bfloat16().to(d) for _ in range(2))
+    st, en, ct = _random_layout(rng, H, S, cap)
+    lengths = [[int(en[h, i]) - int(st[h, i]) for i in range(int(ct[h]))] for h in range(H)]
+    for splits in (None, 2):
+        order, ns, unsplit, imap, grid = plan_column_split(lengths, L, B, splits=splits)
+        lib = _native.load()
+        ws = torch.zeros(max(int(lib.heatkv_attention_workspace_bytes(B, H, L, ns)), 256),
+                         dtype=torch.uint8, device=d)
+        out = _attention_mapped(q, pk, pv, st.to(d), en.to(d), ct.to(d), ck, cv,
+                                1.0 / math.sqrt(128), order=torch.from_numpy(order).to(d),
+                                splits=ns, unsplit=unsplit,
+                                item_map=torch.from_numpy(imap).to(d), grid=grid, workspace=ws)
+        ref = _torch_reference(q, pk, pv, st, en, ct, ck, cv, 1.0 / math.sqrt(128))
+        _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
+    assert _native.device_status(d) == 0
+
+
+def test_item_map_entry_outside_the_launch_is_skipped_and_flagged(cuda_device):
+    """An entry past the item space is skipped (HEATKV_DEVICE_BAD_ITEM_MAP = 0x10); the items
+    the map does hold are computed."""
+    rng = np.random.default_rng(8)
+    gen = torch.Generator().manual_seed(8)
+    d = cuda_device
+    B, H, L, cap, S = 1, 2, 256, 1000, 4
+    q, ck, cv = (torch.randn(B, H, L, 128, generator=gen).bfloat16().to(d) for _ in range(3))
+    pk, pv = (torch.randn(B, cap, 128, generator=gen).bfloat16().to(d) for _ in range(2))
+    st, en, ct = (x.to(d) for x in _random_layout(rng, H, S, cap))
+    order = torch.arange(H, dtype=torch.int32, device=d)
+    imap = torch.tensor([0, 1, 2, 3, 1000, -1], dtype=torch.int32, device=d)  # 4 items, grid 2
+    out = _attention_mapped(q, pk, pv, st, en, ct, ck, cv, 1.0 / math.sqrt(128), order=order,
+                            splits=1, unsplit=4, item_map=imap, grid=2, workspace=None)
+    assert _native.device_status(d) == 0x10
+    ref = _torch_reference(q, pk, pv, st.cpu(), en.cpu(), ct.cpu(), ck, cv, 1.0 / math.sqrt(128))
+    _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())

@@ -30,11 +30,12 @@ def test_large_launches_take_the_two_tile_kernel():
     assert run(batch=16, q_len=64) == _native.RUN_TCGEN05_CS
 
 
-def test_key_range_splits_need_the_two_tile_kernel_and_a_workspace():
-    assert run(splits=2, ws=1) == _native.RUN_TCGEN05_PAIR
-    assert run(splits=2, ws=0) == _native.RUN_TCGEN05_CS
-    blocks = 2 * 16 * 16
-    assert run(splits=2, ws=1, unsplit=blocks) == _native.RUN_TCGEN05_CS  # nothing left to split
+def test_key_range_splits_do_not_change_the_kernel():
+    """Both tcgen05 kernels split key ranges, so splits, the workspace and unsplit_blocks leave
+    the choice to the cost model (unsplit_blocks counts the chosen kernel's blocks)."""
+    for splits, ws, unsplit in ((2, 1, 0), (2, 0, 0), (4, 1, 100), (3, 1, 2 * 16 * 32)):
+        assert run(splits=splits, ws=ws, unsplit=unsplit) == _native.RUN_TCGEN05_CS
+        assert run(batch=16, splits=splits, ws=ws, unsplit=unsplit) == _native.RUN_TCGEN05_PAIR
 
 
 def test_named_variants_and_the_static_metadata_flag():
