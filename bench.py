@@ -403,15 +403,25 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         inputs, outputs = wl.keep[0], wl.keep[1]
         copy_s.wait_stream(stream)
         handle = ctypes.c_void_p(stream.cuda_stream)
-        for launch in launches:
-            if launch.kind == "attention":
-                xs = inputs[launch.layer][launch.target]
+        copied = {}
+
+        def bring(key):
+            # the Q/K/V of one (layer, scale), copied once, when a launch first needs them
+            if key not in copied:
                 with torch.cuda.stream(copy_s):
-                    for x, hb, db in zip(xs, h_in, in_bufs):
+                    for x, hb, db in zip(inputs[key[0]][key[1]], h_in, in_bufs):
                         x.copy_(host_view(hb, x, db), non_blocking=True)
-                    ev = torch.cuda.Event()
-                    ev.record(copy_s)
-                stream.wait_event(ev)
+                    copied[key] = torch.cuda.Event()
+                    copied[key].record(copy_s)
+            return copied[key]
+
+        for launch in launches:
+            # an attention reads its own inputs; a pack before the attentions (dense appends)
+            # reads the K/V of the layers it appends
+            keys = ([(launch.layer, launch.target)] if launch.kind == "attention"
+                    else list(launch.sources))
+            for key in keys:
+                stream.wait_event(bring(key))
             launch(handle)
             if launch.kind == "attention":
                 o = outputs[launch.layer][launch.target]

@@ -32,6 +32,7 @@ struct AttnArgs {
   size_t workspace_bytes = 0;
   unsigned int* status = nullptr;       // device status word (device_status_ptr())
   bool static_meta = false;             // metadata not written by the preceding stream work
+  bool current_in_segments = false;     // current keys end every non-empty head's segments
   // column-split kernel: CTA c of map_grid runs items item_map[c + k * map_grid] (-1 = none)
   const int32_t* item_map = nullptr;
   int64_t map_len = 0;

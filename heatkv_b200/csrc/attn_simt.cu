@@ -122,7 +122,8 @@ __global__ void __launch_bounds__(kThreads, 2) attn_simt_kernel(AttnArgs a) {
   const TV* cur_v = static_cast<const TV*>(a.cur_v);
   const int nseg = sm.nseg;
   const int64_t n_slab = sm.seg_cum[nseg];
-  const int64_t total = n_slab + Lq;
+  // with current_in_segments the current keys already end the head's segments
+  const int64_t total = n_slab + ((a.current_in_segments && nseg > 0) ? 0 : Lq);
   const float scale = a.scale;
 
   float o[4][8];

@@ -111,6 +111,7 @@ struct Params {
   int unsplit;                // leading query blocks (schedule order) that are not split
   int n_items;                // unsplit + (heads * batch * qpairs - unsplit) * splits
   int seg_stride;             // segment-table row length (max_segments)
+  int current_in_segments;    // the current keys end every non-empty head's segments
   // scatter epilogue (n_out > 0): every output row goes to n_out full [out_batch, Lq,
   // out_heads_total * D] tensors (e.g. every rank's copy, over NVLink) at row out_rows[b] and head
   // out_heads[h]; otherwise to `out` in the local [batch, Lq, heads * D] layout
@@ -237,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tiles += (e0 - s0 + kBN - 1) / kBN;
       }
       sm.head_nseg[h] = n;
-      sm.head_tiles[h] = tiles + (Lq + kBN - 1) / kBN;
+      sm.head_tiles[h] = tiles + ((p.current_in_segments && n > 0) ? 0 : (Lq + kBN - 1) / kBN);
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0 && blockIdx.x == 0)
       raise_status(p.status, HEATKV_DEVICE_BAD_SEGMENT);
@@ -802,6 +803,7 @@ cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st
   p.unsplit = static_cast<int>(unsplit);
   p.n_items = static_cast<int>(n_items);
   p.seg_stride = static_cast<int>(std::max<int64_t>(a.max_segments, 1));
+  p.current_in_segments = a.current_in_segments ? 1 : 0;
   const int smem = static_cast<int>(sizeof(Smem)) + 1024;
   // exp2 variant: HEATKV_EXP2_POLY = 0 (fp32 MUFU), 1-2 (quarters of the pairs on the FMA
   // pipe), 3 (packed half-precision MUFU for every pair); default 0

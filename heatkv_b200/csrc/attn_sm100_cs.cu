@@ -139,6 +139,7 @@ struct Params {
   float* ws_o;                  // [split blocks * splits * 128 * 128]
   int seg_stride;
   int static_meta;              // stage the metadata before the dependency wait
+  int current_in_segments;      // the current keys end every non-empty head's segments
   // scatter epilogue (16-bit mode, n_out > 0): every output row goes to n_out full [out_batch,
   // Lq, out_heads_total * D] tensors at row out_rows[b] and head out_heads[h]
   void* const* out_ptrs;
@@ -359,7 +360,7 @@ __global__ void __launch_bounds__(kWG * 128 + 128, 1)
         tiles += (e0 - s0 + kBN - 1) / kBN;
       }
       sm.head_nseg[h] = n;
-      sm.head_tiles[h] = tiles + (Lq + kBN - 1) / kBN;
+      sm.head_tiles[h] = tiles + ((p.current_in_segments && n > 0) ? 0 : (Lq + kBN - 1) / kBN);
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0 && blockIdx.x == 0)
       raise_status(p.status, HEATKV_DEVICE_BAD_SEGMENT);
@@ -1088,6 +1089,7 @@ static cudaError_t launch_mode(const AttnArgs& a, cudaStream_t st) {
   p.ws_o = splits > 1 ? scratch.o : nullptr;
   p.seg_stride = static_cast<int>(std::max<int64_t>(a.max_segments, 1));
   p.static_meta = a.static_meta ? 1 : 0;
+  p.current_in_segments = a.current_in_segments ? 1 : 0;
   p.out_ptrs = a.out_ptrs;
   p.out_rows = a.out_rows;
   p.out_heads = a.out_heads;

@@ -159,7 +159,7 @@ struct AttnPlan {
 static int plan_attention(int q_dtype, int k_dtype, int v_dtype, int64_t batch, int64_t heads,
                           int64_t q_len, int kernel, int kv_splits, bool has_workspace,
                           int64_t unsplit_blocks, bool scatter, AttnPlan* out) {
-  kernel &= ~HEATKV_ATTN_STATIC_META;
+  kernel &= ~(HEATKV_ATTN_STATIC_META | HEATKV_ATTN_CURRENT_IN_SEGMENTS);
   if (kernel < HEATKV_ATTN_AUTO || kernel > HEATKV_ATTN_TCGEN05_CS)
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: unknown kernel selector");
   // the two-tile or column-split variant asked for by name; otherwise HEATKV_TCGEN05_VARIANT
@@ -233,6 +233,7 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
   if (heads > 65535 || batch > 65535 || (q_len + 63) / 64 > 0x7fffffffLL)
     return fail(HEATKV_ERR_UNSUPPORTED, "real_scale_fused_segmented: grid too large");
   const bool static_meta = (kernel & HEATKV_ATTN_STATIC_META) != 0;
+  const bool current_in_segments = (kernel & HEATKV_ATTN_CURRENT_IN_SEGMENTS) != 0;
   AttnPlan plan;
   int rc = plan_attention(q_dtype, k_dtype, v_dtype, batch, heads, q_len, kernel, kv_splits,
                           workspace != nullptr, unsplit_blocks, scatter != nullptr, &plan);
@@ -248,6 +249,7 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
   a.workspace_bytes = workspace_bytes;
   a.status = heatkv::device_status_ptr();
   a.static_meta = static_meta;
+  a.current_in_segments = current_in_segments;
   a.item_map = item_map;
   a.map_len = map_len;
   a.map_grid = map_grid;

@@ -45,9 +45,21 @@ def _makespan(costs: np.ndarray, sms: int) -> float:
     return float(np.pad(costs, (0, pad)).reshape(-1, grid).sum(axis=0).max())
 
 
+def _head_tiles(slots_per_segment, q_len: int, current_in_segments: bool = False) -> np.ndarray:
+    """Key tiles of every head: its segments' tiles, then the current scale's (unless the current
+    keys already end a non-empty head's segments)."""
+    cur = (q_len + KEY_TILE - 1) // KEY_TILE
+    out = []
+    for segs in slots_per_segment:
+        seg = sum((int(n) + KEY_TILE - 1) // KEY_TILE for n in segs if n > 0)
+        out.append(seg + (0 if current_in_segments and seg > 0 else cur))
+    return np.array(out, dtype=np.int64)
+
+
 def plan_attention(slots_per_segment, q_len: int, batch: int, *, sms: int = NUM_SMS,
                    block_rows: int = BLOCK_ROWS, item_cost: float = 1.5,
-                   merge_cost: Optional[float] = None, min_gain: float = 0.03):
+                   merge_cost: Optional[float] = None, min_gain: float = 0.03,
+                   current_in_segments: bool = False):
     """Length-aware schedule of one attention launch: heads longest first, and how many query
     blocks at the tail of the schedule to split in two key ranges so that the kernel's round-robin
     assignment of items to at most ``sms`` persistent CTAs fills its last wave.
@@ -66,9 +78,7 @@ def plan_attention(slots_per_segment, q_len: int, batch: int, *, sms: int = NUM_
         raise ValueError("block_rows must be 128 or 256")
     if merge_cost is None:
         merge_cost = 8.0 if block_rows == 2 * KEY_TILE else 4.0
-    tiles = np.array([sum((int(n) + KEY_TILE - 1) // KEY_TILE for n in segs if n > 0)
-                      + (q_len + KEY_TILE - 1) // KEY_TILE for segs in slots_per_segment],
-                     dtype=np.int64)
+    tiles = _head_tiles(slots_per_segment, q_len, current_in_segments)
     order = np.argsort(-tiles, kind="stable").astype(np.int32)
     nblk = (q_len + block_rows - 1) // block_rows
     per = block_rows // KEY_TILE
@@ -116,7 +126,8 @@ def _greedy_map(costs: np.ndarray, sms: int):
 
 def plan_column_split(slots_per_segment, q_len: int, batch: int, *, sms: int = NUM_SMS,
                       splits: Optional[int] = None, item_cost: float = 1.5,
-                      merge_cost: float = 4.0, min_gain: float = 0.03):
+                      merge_cost: float = 4.0, min_gain: float = 0.03,
+                      current_in_segments: bool = False):
     """Schedule of one column-split launch (128-row blocks): head order, key-range splits, and the
     item map that assigns the launch's items to its CTAs.
 
@@ -127,9 +138,7 @@ def plan_column_split(slots_per_segment, q_len: int, batch: int, *, sms: int = N
     split taken only when it gains ``min_gain``; a given ``splits`` splits every block that many
     ways (1 = none). Items then go longest first to the least-loaded CTA.
     Returns ``(head_order, splits, unsplit_blocks, item_map, grid)``."""
-    tiles = np.array([sum((int(n) + KEY_TILE - 1) // KEY_TILE for n in segs if n > 0)
-                      + (q_len + KEY_TILE - 1) // KEY_TILE for segs in slots_per_segment],
-                     dtype=np.int64)
+    tiles = _head_tiles(slots_per_segment, q_len, current_in_segments)
     order = np.argsort(tiles, kind="stable").astype(np.int32)
     nblk = (q_len + KEY_TILE - 1) // KEY_TILE
     t_blk = np.repeat(tiles[order], batch * nblk)             # blocks in kernel order
@@ -175,6 +184,7 @@ class Launch:
     args: tuple          # ctypes arguments without the trailing stream
     work: float          # algorithmic FLOPs (attention) or HBM bytes (pack)
     keep: object = None  # device arrays the arguments point into
+    sources: tuple = ()  # (plan index, target) of the step inputs a pack reads
 
     def __call__(self, stream: ctypes.c_void_p) -> None:
         status = self.fn(*self.args, stream)
@@ -225,6 +235,14 @@ class LayerPlan:
             ln = np.full(H, n, dtype=np.int64)
             self.dense_append[t] = (_dev(dst, device), _dev(src, device), _dev(ln, device), H, n,
                                     H * n)
+        # dense targets whose scale is appended before its attention: one segment per head holds
+        # the cached tokens and the scale, [h*Ld, h*Ld + T_t + n_t) (HEATKV_ATTN_CURRENT_IN_SEGMENTS)
+        self.dense_meta_cur = {}
+        for t in self.dense_append:
+            end = int(self.ranges[t][1])
+            st = (np.arange(H, dtype=np.int32) * Ld).reshape(H, 1)
+            meta = (st, st + end, np.ones(H, dtype=np.int32))
+            self.dense_meta_cur[t] = tuple(_dev(m, device) for m in meta) + (meta,)
         # activation: retained segments live at t0, read from the dense cache layout
         self.activation = None
         if t0 < self.num_scales:
@@ -250,6 +268,14 @@ class LayerPlan:
                                    _dev(d["lengths"], device), d["item_count"], d["max_length"],
                                    d["slots"])
 
+    def kernel_segment_lengths(self, t: int, current_in_cache: bool):
+        """Per head, the segment lengths the kernel walks at target t, and whether the current
+        scale's keys are inside them (a dense target appended before its attention)."""
+        if current_in_cache and t in self.dense_meta_cur:
+            end = int(self.ranges[t][1])
+            return [[end] for _ in range(self.num_heads)], True
+        return self.segment_lengths(t), False
+
     def segment_lengths(self, t: int):
         """Per head, the lengths of the slab segments attended at target t."""
         meta = self.dense_meta[t][3] if t < self.first_target else self.slab_meta[t][3]
@@ -273,8 +299,16 @@ class HotPath:
 
     def __init__(self, controller, num_layers: int, num_heads: int, batch: int, device,
                  k_dtype=torch.bfloat16, v_dtype=torch.bfloat16, head_dim: int = 128,
-                 layers: Optional[list] = None, plan_splits=None):
+                 layers: Optional[list] = None, plan_splits=None,
+                 dense_append_first: Optional[bool] = None):
+        import os
         self.device = torch.device(device)
+        # dense targets: append the scale to the dense cache before its attention, which then
+        # walks one segment [cached tokens + scale] per head (default: HEATKV_DENSE_APPEND_FIRST,
+        # else on)
+        if dense_append_first is None:
+            dense_append_first = os.environ.get("HEATKV_DENSE_APPEND_FIRST", "1") != "0"
+        self.dense_append_first = bool(dense_append_first)
         self.num_layers = int(num_layers)
         self.num_heads = int(num_heads)
         self.batch = int(batch)
@@ -297,7 +331,6 @@ class HotPath:
         # length-aware schedule of every attention launch (host planner, device head orders)
         self.schedule = {}
         ws_bytes = 0
-        import os
         # plan_splits (default: HEATKV_PLAN_SPLITS, else 1): "auto" = tail splits chosen by the
         # planner for the kernel each launch runs, or a fixed number of key-range splits for
         # every block (1 = never split). Column-split launches always get an item map (greedy,
@@ -316,16 +349,18 @@ class HotPath:
                     dt[k_dtype], dt[k_dtype], dt[v_dtype], self.batch, self.num_heads,
                     self.tokens[t], _native.ATTN_AUTO, 1, 1, 0)
                 imap = None
+                lens, cis = p.kernel_segment_lengths(t, self.dense_append_first)
                 if run == _native.RUN_TCGEN05_CS and not natural:
                     # column-split kernel: greedy item map (and tail splits of the longest blocks)
                     order, splits, unsplit, imap, grid = plan_column_split(
-                        p.segment_lengths(t), self.tokens[t], self.batch,
-                        splits=forced if forced > 0 else None)
+                        lens, self.tokens[t], self.batch, splits=forced if forced > 0 else None,
+                        current_in_segments=cis)
                     imap = (torch.from_numpy(imap).to(self.device), grid)
                 else:
                     rows = 2 * KEY_TILE if run == _native.RUN_TCGEN05_PAIR else KEY_TILE
-                    order, splits, unsplit = plan_attention(p.segment_lengths(t), self.tokens[t],
-                                                            self.batch, block_rows=rows)
+                    order, splits, unsplit = plan_attention(lens, self.tokens[t], self.batch,
+                                                            block_rows=rows,
+                                                            current_in_segments=cis)
                     if run not in (_native.RUN_TCGEN05_PAIR, _native.RUN_TCGEN05_CS):
                         splits, unsplit = 1, 0  # tf32 and exact launches run unsplit
                     if forced > 0:
@@ -349,7 +384,10 @@ class HotPath:
 
         With ``batch_packs`` the compactions of every layer of a scale are issued as one batched
         launch after the scale's last attention (then the slab activations, which read the dense
-        caches those appends complete): scale t's K/V are only read again at scale t + 1."""
+        caches those appends complete): scale t's K/V are only read again at scale t + 1. With
+        ``dense_append_first`` the dense-cache appends of a scale go before its attentions
+        instead (one batched launch), and those attentions walk one segment per head that already
+        ends with the scale (``HEATKV_ATTN_CURRENT_IN_SEGMENTS``)."""
         B, H, D = self.batch, self.num_heads, self.head_dim
         scale = float(softmax_scale) if softmax_scale is not None else D ** -0.5
         lib = self.lib
@@ -360,13 +398,16 @@ class HotPath:
         out = []
         for t in range(self.num_scales):
             n = self.tokens[t]
-            appends, activations = [], []
+            first, appends, activations = [], [], []
+            attn = []
             for i, p in enumerate(self.plans):
                 q, k, v = inputs[i][t]
                 o = outputs[i][t]
                 dense = t < p.first_target
+                cur_in = dense and self.dense_append_first and t in p.dense_meta_cur
+                sel = meta_kernel | (_native.ATTN_CURRENT_IN_SEGMENTS if cur_in else 0)
                 if dense:
-                    st, en, ct, _ = p.dense_meta[t]
+                    st, en, ct, _ = p.dense_meta_cur[t] if cur_in else p.dense_meta[t]
                     sk, sv = self.dense_k[i], self.dense_v[i]
                     cap = H * max(p.dense_len, 1)
                 else:
@@ -378,7 +419,7 @@ class HotPath:
                 head = (_native.ptr(q), _native.ptr(sk), _native.ptr(sv), _native.ptr(st),
                         _native.ptr(en), _native.ptr(ct), _native.ptr(k), _native.ptr(v),
                         _native.ptr(o), dt[q.dtype], dt[k.dtype], dt[v.dtype], B, H, n, cap, D,
-                        int(st.shape[1]), ctypes.c_float(scale), meta_kernel, _native.ptr(order),
+                        int(st.shape[1]), ctypes.c_float(scale), sel, _native.ptr(order),
                         int(splits), int(unsplit))
                 ws = (_native.ptr(self.workspace), self.workspace.numel())
                 if imap is not None:
@@ -388,15 +429,23 @@ class HotPath:
                 else:
                     launch = Launch("attention", p.layer, t, lib.heatkv_segmented_attention_sched,
                                     head + ws, flops)
-                out.append(launch)
                 row_k = D * k.element_size()
                 row_v = D * v.element_size()
                 jobs = []
                 if dense and t in p.dense_append:
                     dst, src, ln, items, mx, slots = p.dense_append[t]
-                    jobs.append((appends, (self.dense_k[i], self.dense_v[i], k, v, H * n,
-                                           H * max(p.dense_len, 1), dst, src, ln, items, mx,
-                                           slots)))
+                    job = (self.dense_k[i], self.dense_v[i], k, v, H * n, H * max(p.dense_len, 1),
+                           dst, src, ln, items, mx, slots)
+                    if cur_in:
+                        if batch_packs:
+                            first.append((job, i))
+                        else:
+                            pre = self._pack(p.layer, t, *job, row_k, row_v)
+                            pre.sources = ((i, t),)
+                            attn.append(pre)
+                    else:
+                        jobs.append((appends, job))
+                attn.append(launch)
                 if dense and t + 1 == p.first_target and p.activation is not None:
                     dst, src, ln, items, mx, slots = p.activation
                     jobs.append((activations, (self.slab_k[i], self.slab_v[i], self.dense_k[i],
@@ -411,7 +460,12 @@ class HotPath:
                     if batch_packs:
                         group.append(job)
                     else:
-                        out.append(self._pack(p.layer, t, *job, row_k, row_v))
+                        attn.append(self._pack(p.layer, t, *job, row_k, row_v))
+            if first:
+                pre = self._pack_batched(t, [job for job, _ in first])
+                pre.sources = tuple((i, t) for _, i in first)
+                out.append(pre)
+            out.extend(attn)
             for group in (appends, activations):
                 if group:
                     out.append(self._pack_batched(t, group))

@@ -86,6 +86,13 @@ typedef enum {
  * so the column-split kernel may stage them while the preceding kernel is still running. */
 #define HEATKV_ATTN_STATIC_META 0x100
 
+/* OR into the kernel selector: the current scale's keys are already the last rows of the last
+ * segment of every head that has a segment (e.g. a dense cache the scale was appended to before
+ * its attention), so the kernel reads no separate current tiles for those heads; heads without a
+ * segment still attend the current K/V. Same keys in the same order, one tile fewer wherever the
+ * cached prefix and the scale together fit fewer 128-key tiles. */
+#define HEATKV_ATTN_CURRENT_IN_SEGMENTS 0x200
+
 /* Message describing the last failing call made by this thread ("" if none). */
 const char* heatkv_last_error_string(void);
 

@@ -144,3 +144,31 @@ def test_batched_scale_packs_equal_per_layer_packs():
     assert all(torch.equal(a, b) for a, b in zip(out0, out1))
     assert all(torch.equal(a, b) for a, b in zip(slab0, slab1))
     assert _native.device_status(dev) == 0
+
+
+def test_dense_append_first_matches_append_after():
+    """Appending each dense scale to the dense cache before its attention, which then walks one
+    segment of cached tokens + scale per head (HEATKV_ATTN_CURRENT_IN_SEGMENTS), against the
+    reference's order (append after the attention, current scale as separate tiles): the same
+    slabs bit for bit and the outputs within bf16 tolerance of each other (only the key-tile
+    partition of the dense targets differs)."""
+    ctrl, L, H = _controller("2b", 0.10)
+    dev = torch.device("cuda", 0)
+    layers = [0, 17]
+    results = []
+    for first in (False, True):
+        hot = HotPath(ctrl, L, H, 2, dev, layers=layers, dense_append_first=first)
+        inputs, outputs, _, _ = allocate_io(hot, seed=9)
+        launches = hot.launches(inputs, outputs)
+        pre = [l for l in launches if l.kind == "pack" and l.sources]
+        assert bool(pre) == first
+        hot.run(launches)
+        torch.cuda.synchronize()
+        results.append(([o.clone() for row in outputs for o in row],
+                        [s.clone() for s in hot.slab_k + hot.slab_v]))
+    (out0, slab0), (out1, slab1) = results
+    assert all(torch.equal(a, b) for a, b in zip(slab0, slab1))
+    for a, b in zip(out0, out1):
+        err = (a.float() - b.float()).abs().max().item()
+        assert err <= BF16_ATOL and err / max(b.float().abs().max().item(), 1e-6) <= BF16_REL
+    assert _native.device_status(dev) == 0

@@ -645,3 +645,54 @@ def test_item_map_entry_outside_the_launch_is_skipped_and_flagged(cuda_device):
     assert _native.device_status(d) == 0x10
     ref = _torch_reference(q, pk, pv, st.cpu(), en.cpu(), ct.cpu(), ck, cv, 1.0 / math.sqrt(128))
     _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
+
+
+@pytest.mark.parametrize("sel", ["cs", "pair", "exact"])
+def test_current_in_segments_flag(sel, cuda_device):
+    """HEATKV_ATTN_CURRENT_IN_SEGMENTS: with every head's current keys copied into the slab right
+    after its last segment (extending it), the flagged call reads no separate current tiles and
+    matches the reference; a head without segments still attends the current K/V."""
+    import ctypes
+    rng = np.random.default_rng(21)
+    gen = torch.Generator().manual_seed(21)
+    d = cuda_device
+    B, H, L, S = 2, 6, 96, 5
+    q, ck, cv = (torch.randn(B, H, L, 128, generator=gen).bfloat16().to(d) for _ in range(3))
+    cap = 6000
+    pk, pv = (torch.randn(B, cap, 128, generator=gen).bfloat16().to(d) for _ in range(2))
+    st, en, ct = _random_layout(rng, H, S, 4000)
+    ct[H - 1] = 0  # no segment: the current K/V come from cur_k / cur_v
+    ref = _torch_reference(q, pk, pv, st, en, ct, ck, cv, 1.0 / math.sqrt(128))
+    # extended layout: each head with segments gets its current keys as a last segment of its own
+    st2, en2, ct2 = (x.numpy().copy() for x in (st, en, ct))
+    st2 = np.concatenate([st2, np.zeros((H, 1), np.int32)], axis=1)
+    en2 = np.concatenate([en2, np.zeros((H, 1), np.int32)], axis=1)
+    pk2, pv2 = pk.clone(), pv.clone()
+    base = 4000
+    for h in range(H):
+        if ct2[h] == 0:
+            continue
+        # append the current keys right after the head's last non-empty segment, copied there
+        i = int(ct2[h])
+        st2[h, i], en2[h, i] = base, base + L
+        pk2[:, base:base + L] = ck[:, h]
+        pv2[:, base:base + L] = cv[:, h]
+        ct2[h] = i + 1
+        base += L
+    st2, en2, ct2 = (torch.from_numpy(np.ascontiguousarray(x, dtype=np.int32)).to(d)
+                     for x in (st2, en2, ct2))
+    kern = {"cs": _native.ATTN_TCGEN05_CS, "pair": _native.ATTN_TCGEN05_PAIR,
+            "exact": _native.ATTN_EXACT}[sel]
+    out = torch.empty(B, L, H * 128, dtype=q.dtype, device=d)
+    dt = _native.DTYPE_CODES
+    order = torch.arange(H, dtype=torch.int32, device=d)
+    _native.check(_native.load().heatkv_segmented_attention_sched(
+        _native.ptr(q), _native.ptr(pk2), _native.ptr(pv2), _native.ptr(st2), _native.ptr(en2),
+        _native.ptr(ct2), _native.ptr(ck), _native.ptr(cv), _native.ptr(out), dt[q.dtype],
+        dt[ck.dtype], dt[cv.dtype], B, H, L, cap, 128, st2.shape[1],
+        ctypes.c_float(1.0 / math.sqrt(128)), kern | _native.ATTN_CURRENT_IN_SEGMENTS,
+        _native.ptr(order), 1, 0, None, 0, _native.stream_handle(d)),
+        "heatkv_segmented_attention_sched")
+    torch.cuda.synchronize()
+    _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
+    assert _native.device_status(d) == 0
