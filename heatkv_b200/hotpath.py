@@ -7,8 +7,11 @@ baseline-prefix activation) as prepared C-ABI calls:
 
 * target ``t`` before the layer's first pruned target ``t0``: attention over the layer's dense
   cache (the reference's SDPA + ``torch.cat`` path, :2073-2121), here run by the same kernel with
-  the dense cache ``[B, H, Ld, D]`` viewed as a flat slab and one segment per head, then the
-  current scale's K/V appended into the preallocated dense cache (no concatenation copy);
+  the dense cache ``[B, H, Ld, D]`` viewed as a flat slab and one segment per head. The current
+  scale's K/V are appended into the preallocated dense cache (no concatenation copy) before the
+  attention, so the head's one segment already ends with them (``HEATKV_ATTN_CURRENT_IN_SEGMENTS``:
+  the same keys in the same order, in fewer 128-key tiles - one instead of two at targets 1-4);
+  ``dense_append_first=False`` keeps the reference's order (append after the attention);
 * end of scale ``t0 - 1``: activation pack of the retained (source, head) segments from the dense
   cache into the slab (``old_pack_runs_by_target[t0]``, :1999-2037 -> :871-967);
 * targets ``t >= t0``: fused segmented attention over the slab (:2123-2155), then the append of the
