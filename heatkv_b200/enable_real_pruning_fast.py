@@ -59,7 +59,10 @@ from .enable_pruning import (
     _validate_and_normalize_removed_heads_by_scale_specific,
     _validate_and_normalize_scale_specific_removal_orders,
 )
+from . import _native
+from .hotpath import plan_column_split
 from .real_pruning_fused_attention import (
+    _kernel_selector,
     fused_real_pruning_flat_segmented_attention,
     pack_flat_segments_kv,
 )
@@ -182,6 +185,29 @@ class _LayerState:
         self.old_pack = {}
         self.append = {}
         self.prep_append = {}
+        self.plans = {}
+
+    def attention_plan(self, target: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+        """Launch schedule of this layer's fused attention at ``target`` for these tensors, planned
+        once per (target, batch, dtypes) from the static segment tables: ``(head_order, item_map,
+        grid)`` when the call runs the column-split kernel, else None."""
+        key = (target, q.shape[0], q.dtype, k.dtype, v.dtype, q.device)
+        if key in self.plans:
+            return self.plans[key]
+        plan = None
+        dt = _native.DTYPE_CODES
+        run = _native.load().heatkv_attention_kernel_for(
+            dt[q.dtype], dt[k.dtype], dt[v.dtype], q.shape[0], q.shape[1], q.shape[2],
+            _kernel_selector(), 1, 0, 0)
+        if run in (_native.RUN_TCGEN05_CS, _native.RUN_TCGEN05_TF32):
+            st, en, ct = self.schedule["metadata_cpu_by_target"][target]
+            lens = [[int(en[h, i]) - int(st[h, i]) for i in range(int(ct[h]))]
+                    for h in range(self.num_heads)]
+            order, _, _, item_map, grid = plan_column_split(lens, q.shape[2], q.shape[0], splits=1)
+            plan = (torch.from_numpy(order).to(q.device), torch.from_numpy(item_map).to(q.device),
+                    grid)
+        self.plans[key] = plan
+        return plan
 
     def to(self, device: torch.device) -> None:
         if self.device == device:
@@ -424,7 +450,8 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
             output = fused_real_pruning_flat_segmented_attention(
                 q=q, persisted_k=self._heatkv_slab_k, persisted_v=self._heatkv_slab_v,
                 segment_starts=starts, segment_ends=ends, segment_counts=counts, current_k=k,
-                current_v=v, softmax_scale=self.scale, softmax_mode=_fused_softmax_mode())
+                current_v=v, softmax_scale=self.scale, softmax_mode=_fused_softmax_mode(),
+                _schedule=self._heatkv_layer.attention_plan(scale_ind, q, k, v))
     del q
     output = self.proj_drop(self.proj(output))
 

@@ -174,12 +174,18 @@ def fused_real_pruning_flat_segmented_attention(
     softmax_scale: float,
     allow_cpu_fallback: bool = False,
     softmax_mode: str = "exp",
+    _schedule: Optional[tuple] = None,
 ) -> torch.Tensor:
     """Attention over a flat K/V segment slab without compacting old K/V.
 
     ``persisted_k/v`` are ``[B, capacity_slots, D]`` (or None for an empty slab). Segment
     starts/ends are flat slot offsets into that slab, ``[H, S]`` per head, with ``[H]`` counts;
-    entries with ``start >= end`` are skipped. Returns ``[B, Lq, H*D]`` in q's dtype."""
+    entries with ``start >= end`` are skipped. Returns ``[B, Lq, H*D]`` in q's dtype.
+
+    ``_schedule`` (not in the reference; used by the installer, which knows the static segment
+    tables): ``(head_order, item_map, grid)`` device tensors of a column-split launch planned by
+    ``hotpath.plan_column_split`` - the same result, with the heads' query blocks assigned to
+    the CTAs longest first instead of in a fixed round robin."""
     if q.ndim != 4 or current_k.ndim != 4 or current_v.ndim != 4:
         raise ValueError("q, current_k, and current_v must have shape [B, H, L, D]")
     if q.shape != current_k.shape or q.shape != current_v.shape:
@@ -253,6 +259,20 @@ def fused_real_pruning_flat_segmented_attention(
     current_v = current_v.contiguous()
     capacity = int(persisted_k.shape[1])
     output = q.new_empty((batch_size, current_len, num_heads * head_dim))
+    if _schedule is not None:
+        order, item_map, grid = _schedule
+        status = lib.heatkv_segmented_attention_mapped(
+            _native.ptr(q), _native.ptr(persisted_k) if capacity else None,
+            _native.ptr(persisted_v) if capacity else None, _native.ptr(segment_starts),
+            _native.ptr(segment_ends), _native.ptr(segment_counts), _native.ptr(current_k),
+            _native.ptr(current_v), _native.ptr(output), _native.DTYPE_CODES[q.dtype],
+            _native.DTYPE_CODES[current_k.dtype], _native.DTYPE_CODES[current_v.dtype],
+            int(batch_size), int(num_heads), int(current_len), capacity, int(head_dim),
+            int(segment_starts.shape[1]), float(softmax_scale), kernel, _native.ptr(order), 1, 0,
+            _native.ptr(item_map), item_map.numel(), int(grid), None, 0,
+            _native.stream_handle(q.device))
+        _native.check(status, "fused_real_pruning_flat_segmented_attention")
+        return output
     splits = int(os.environ.get("HEATKV_KV_SPLITS", "1"))
     need = int(lib.heatkv_attention_workspace_bytes(batch_size, num_heads, current_len, splits))
     ws = _workspace(q.device, need) if need > 0 else None

@@ -250,3 +250,39 @@ def test_prep_append_leaves_outputs_and_slabs_bit_identical():
     for a, b in zip(sa, sb):
         assert a[:4] == b[:4]
         assert torch.equal(a[4], b[4]) and torch.equal(a[5], b[5]), a[:4]
+
+
+@pytest.mark.parametrize("dtype,autocast", [(torch.bfloat16, False), (torch.float32, True)])
+def test_planned_schedule_is_bit_identical(dtype, autocast):
+    """The installer's per-(layer, target) launch plans (longest-first item maps of the
+    column-split kernel, from the static segment tables) change only which CTA runs which query
+    block: every output at every scale is bit-identical to the round-robin launch."""
+    from heatkv_b200.enable_real_pruning_fast import _LayerState
+    dev = torch.device("cuda", 0)
+    L, H, C = 2, 16, 2048
+    schedule = synthetic.SCALE_SCHEDULE_1M
+    orders = synthetic.random_removal_orders(L, H, seed=5)
+    xs = [[torch.randn(2, h * w, C, device=dev, dtype=dtype) for _, h, w in schedule]
+          for _ in range(L)]
+    runs = []
+    original = _LayerState.attention_plan
+    for planned in (True, False):
+        if not planned:
+            _LayerState.attention_plan = lambda self, *a, **k: None
+        try:
+            torch.manual_seed(0)
+            model = nn.ModuleList([SelfAttention(C, H, True) for _ in range(L)]).to(dev, dtype)
+            enable_real_pruning_scale_specific_fused_segmented(
+                model, 0.10, orders, protected_prefix_scales=3, source_scale_start=3)
+            for m in model:
+                m.kv_caching(True)
+            outs = []
+            with torch.no_grad(), _autocast(autocast):
+                for t in range(len(schedule)):
+                    for l, m in enumerate(model):
+                        outs.append(m(xs[l][t], None, scale_ind=t))
+            runs.append(outs)
+        finally:
+            _LayerState.attention_plan = original
+    assert _native.device_status(dev) == 0
+    assert all(torch.equal(a, b) for a, b in zip(*runs))
