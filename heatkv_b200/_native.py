@@ -23,9 +23,11 @@ HEATKV_ERR_CUDA = -3
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
 ATTN_AUTO, ATTN_EXACT, ATTN_TCGEN05, ATTN_TCGEN05_PAIR, ATTN_TCGEN05_CS = 0, 1, 2, 3, 4
+ATTN_TCGEN05_CS64 = 5
 ATTN_STATIC_META = 0x100  # OR into a selector: metadata not written by preceding work
 ATTN_CURRENT_IN_SEGMENTS = 0x200  # OR into a selector: current keys end every head's segments
 RUN_EXACT, RUN_TCGEN05_PAIR, RUN_TCGEN05_CS, RUN_TCGEN05_TF32 = 1, 2, 3, 4  # heatkv_attn_run
+RUN_TCGEN05_CS64 = 5
 
 DEVICE_PACK_OUT_OF_RANGE = 0x1
 DEVICE_WAIT_TIMEOUT = 0x2

@@ -30,6 +30,7 @@ static int tcgen05_variant() {
     const char* e = getenv("HEATKV_TCGEN05_VARIANT");
     if (e && strcmp(e, "pair") == 0) return 1;
     if (e && strcmp(e, "cs") == 0) return 2;
+    if (e && strcmp(e, "cs64") == 0) return 3;
     return 0;
   }();
   return v;
@@ -160,14 +161,17 @@ static int plan_attention(int q_dtype, int k_dtype, int v_dtype, int64_t batch, 
                           int64_t q_len, int kernel, int kv_splits, bool has_workspace,
                           int64_t unsplit_blocks, bool scatter, AttnPlan* out) {
   kernel &= ~(HEATKV_ATTN_STATIC_META | HEATKV_ATTN_CURRENT_IN_SEGMENTS);
-  if (kernel < HEATKV_ATTN_AUTO || kernel > HEATKV_ATTN_TCGEN05_CS)
+  if (kernel < HEATKV_ATTN_AUTO || kernel > HEATKV_ATTN_TCGEN05_CS64)
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: unknown kernel selector");
-  // the two-tile or column-split variant asked for by name; otherwise HEATKV_TCGEN05_VARIANT
-  const int variant = kernel == HEATKV_ATTN_TCGEN05_PAIR ? 1
-                    : kernel == HEATKV_ATTN_TCGEN05_CS   ? 2
-                                                         : heatkv::tcgen05_variant();
-  const bool named_pair = kernel == HEATKV_ATTN_TCGEN05_PAIR;
-  if (kernel == HEATKV_ATTN_TCGEN05_PAIR || kernel == HEATKV_ATTN_TCGEN05_CS)
+  // the two-tile, column-split or 64-key variant asked for by name; otherwise
+  // HEATKV_TCGEN05_VARIANT
+  const int variant = kernel == HEATKV_ATTN_TCGEN05_PAIR   ? 1
+                    : kernel == HEATKV_ATTN_TCGEN05_CS     ? 2
+                    : kernel == HEATKV_ATTN_TCGEN05_CS64   ? 3
+                                                           : heatkv::tcgen05_variant();
+  const bool named_pair = kernel == HEATKV_ATTN_TCGEN05_PAIR || kernel == HEATKV_ATTN_TCGEN05_CS64;
+  if (kernel == HEATKV_ATTN_TCGEN05_PAIR || kernel == HEATKV_ATTN_TCGEN05_CS ||
+      kernel == HEATKV_ATTN_TCGEN05_CS64)
     kernel = HEATKV_ATTN_TCGEN05;
   const bool same16 = (q_dtype == k_dtype && k_dtype == v_dtype && q_dtype != HEATKV_DTYPE_F32);
   // fp32 q and k with 16-bit v (the real model's dtypes): tf32 QK, P rounded to v's dtype
@@ -175,7 +179,8 @@ static int plan_attention(int q_dtype, int k_dtype, int v_dtype, int64_t batch, 
                      v_dtype != HEATKV_DTYPE_F32);
   if (named_pair && !same16)
     return fail(HEATKV_ERR_UNSUPPORTED,
-                "the two-tile tcgen05 kernel needs q, k and v all bfloat16 or all float16");
+                "the two-tile and 64-key tcgen05 kernels need q, k and v all bfloat16 or all "
+                "float16");
   if (kernel == HEATKV_ATTN_TCGEN05 && !same16 && !(qk32 && !scatter))
     return fail(HEATKV_ERR_UNSUPPORTED,
                 "tcgen05 segmented attention needs q, k and v all bfloat16 or all float16, or q "
@@ -184,14 +189,18 @@ static int plan_attention(int q_dtype, int k_dtype, int v_dtype, int64_t batch, 
   if (kernel != HEATKV_ATTN_EXACT && qk32 && !scatter) {
     out->run = HEATKV_RUN_TCGEN05_TF32;
   } else if (kernel != HEATKV_ATTN_EXACT && same16) {
-    // both kernels take key-range splits (unsplit_blocks counts the chosen kernel's blocks:
-    // 256 query rows for the two-tile kernel, 128 for the column split); the cost model chooses
-    (void)kv_splits;
-    (void)has_workspace;
+    // Default: the 64-key kernel (two CTAs per SM), faster at every launch size measured. It
+    // has no key-range splits and no scatter epilogue: calls asking for splits (with a
+    // workspace) or scattering take the column-split or two-tile kernel, as the cost model
+    // chooses (unsplit_blocks counts the chosen kernel's blocks: 256 query rows for the two-tile
+    // kernel, 128 for the column split).
     (void)unsplit_blocks;
+    const bool wants_splits = kv_splits > 1 && has_workspace;
     bool pair = variant == 1;
     if (variant == 0) pair = heatkv::attention_prefers_pair(batch, heads, q_len);
     out->run = pair ? HEATKV_RUN_TCGEN05_PAIR : HEATKV_RUN_TCGEN05_CS;
+    if (!scatter && (variant == 3 || (variant == 0 && !wants_splits)))
+      out->run = HEATKV_RUN_TCGEN05_CS64;
   } else {
     if (scatter)
       return fail(HEATKV_ERR_UNSUPPORTED,
@@ -267,11 +276,21 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
     if (e == cudaSuccess) return HEATKV_OK;
     if (e != cudaErrorNotSupported || plan.strict)
       return cuda_fail(e, "tcgen05 tf32 segmented attention launch");
-  } else if (plan.run == HEATKV_RUN_TCGEN05_PAIR || plan.run == HEATKV_RUN_TCGEN05_CS) {
+  } else if (plan.run == HEATKV_RUN_TCGEN05_PAIR || plan.run == HEATKV_RUN_TCGEN05_CS ||
+             plan.run == HEATKV_RUN_TCGEN05_CS64) {
     const bool bf16 = q_dtype == HEATKV_DTYPE_BF16;
-    cudaError_t e = plan.run == HEATKV_RUN_TCGEN05_PAIR
-                        ? heatkv::launch_attention_sm100(a, bf16, st)
-                        : heatkv::launch_attention_sm100_cs(a, bf16, st);
+    cudaError_t e = cudaErrorNotSupported;
+    if (plan.run == HEATKV_RUN_TCGEN05_CS64) {
+      // outside the 64-key kernel's limits (segment table, splits asked with a map): column split
+      e = heatkv::launch_attention_sm100_cs64(a, bf16, st);
+      if (e == cudaErrorNotSupported) {
+        a.item_map = nullptr;  // a map planned for the 64-key kernel numbers different items
+        e = heatkv::launch_attention_sm100_cs(a, bf16, st);
+      }
+    } else {
+      e = plan.run == HEATKV_RUN_TCGEN05_PAIR ? heatkv::launch_attention_sm100(a, bf16, st)
+                                              : heatkv::launch_attention_sm100_cs(a, bf16, st);
+    }
     if (e == cudaSuccess) return HEATKV_OK;
     if (e == cudaErrorNotSupported && scatter)
       return fail(HEATKV_ERR_UNSUPPORTED,

@@ -17,8 +17,9 @@ constexpr int kKeyTile = 128;  // keys per K/V tile of both kernels
 constexpr int kHeadDim = 128;  // the only head dim of the path
 constexpr int kNumSms = 148;
 
-// Walks the key tiles of one head: each segment in 128-row steps, then the current scale.
-struct TileCursor {
+// Walks the key tiles of one head: each segment in kTile-row steps, then the current scale.
+template <int kTile>
+struct TileCursorT {
   const int* st;
   const int* en;
   int nseg, seg, pos;
@@ -32,23 +33,23 @@ struct TileCursor {
     seg = 0;
     current = false;
     while (seg < nseg) {
-      const int t = (en[seg] - st[seg] + kKeyTile - 1) / kKeyTile;
+      const int t = (en[seg] - st[seg] + kTile - 1) / kTile;
       if (j0 < t) break;
       j0 -= t;
       ++seg;
     }
     if (seg < nseg) {
-      pos = st[seg] + j0 * kKeyTile;
+      pos = st[seg] + j0 * kTile;
     } else {
       current = true;
-      pos = j0 * kKeyTile;
+      pos = j0 * kTile;
     }
   }
   __device__ int valid(int q_len) const {
-    return current ? min(kKeyTile, q_len - pos) : min(kKeyTile, en[seg] - pos);
+    return current ? min(kTile, q_len - pos) : min(kTile, en[seg] - pos);
   }
   __device__ void next() {
-    pos += kKeyTile;
+    pos += kTile;
     if (!current && pos >= en[seg]) {
       ++seg;
       if (seg < nseg) {
@@ -60,6 +61,7 @@ struct TileCursor {
     }
   }
 };
+using TileCursor = TileCursorT<kKeyTile>;
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -130,6 +132,57 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
+
+// 64 consecutive TMEM columns of this thread's lane, waited on inside the same asm.
+__device__ __forceinline__ void tmem_ld_row64(uint32_t taddr, float (&x)[64]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,"
+      "%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,"
+      "%59,%60,%61,%62,%63}, [%64];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]),
+        "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]),
+        "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]),
+        "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]),
+        "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) x[i] = __uint_as_float(r[i]);
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&x)[N]) {
+  if constexpr (N == 64) {
+    tmem_ld_row64(taddr, x);
+  } else {
+    static_assert(N == 32, "32 or 64 columns per warpgroup");
+    tmem_ld32_sync(taddr, x);
+  }
+}
+
+// Row max of N (a multiple of 16) scores: 8 independent chains of 3-input max.
+template <int N>
+__device__ __forceinline__ float row_max(const float (&x)[N]) {
+  float a[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) a[k] = fmaxf(x[k], x[k + 8]);
+#pragma unroll
+  for (int i = 2; i < N / 8; i += 2) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = max3f(a[k], x[k + 8 * i], x[k + 8 * i + 8]);
+  }
+  return max3f(max3f(a[0], a[1], a[2]), max3f(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+}
+
 
 // packed pairs of fp32 (sm_100 f32x2 arithmetic)
 __device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
@@ -243,14 +296,15 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-// rows x 128 16-bit matrix, box 64 x 128 with 128-byte swizzle
-static bool encode_rows(CUtensorMap* map, const void* base, int64_t rows, bool bf16) {
+// rows x 128 16-bit matrix, box 64 columns x box_rows rows with 128-byte swizzle
+static bool encode_rows(CUtensorMap* map, const void* base, int64_t rows, bool bf16,
+                        int box_rows = kKeyTile) {
   auto enc = get_encode();
   if (!enc) return false;
   if (rows <= 0) rows = 1;  // an empty tensor is never read; keep the map well-formed
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(kHeadDim * 2)};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kKeyTile)};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t elem[2] = {1, 1};
   CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                    2, const_cast<void*>(base), dims, strides, box, elem,

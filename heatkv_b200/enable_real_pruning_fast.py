@@ -60,7 +60,7 @@ from .enable_pruning import (
     _validate_and_normalize_scale_specific_removal_orders,
 )
 from . import _native
-from .hotpath import plan_column_split
+from .hotpath import NUM_SMS, plan_column_split
 from .real_pruning_fused_attention import (
     _kernel_selector,
     fused_real_pruning_flat_segmented_attention,
@@ -199,11 +199,14 @@ class _LayerState:
         run = _native.load().heatkv_attention_kernel_for(
             dt[q.dtype], dt[k.dtype], dt[v.dtype], q.shape[0], q.shape[1], q.shape[2],
             _kernel_selector(), 1, 0, 0)
-        if run in (_native.RUN_TCGEN05_CS, _native.RUN_TCGEN05_TF32):
+        if run in (_native.RUN_TCGEN05_CS, _native.RUN_TCGEN05_TF32, _native.RUN_TCGEN05_CS64):
             st, en, ct = self.schedule["metadata_cpu_by_target"][target]
             lens = [[int(en[h, i]) - int(st[h, i]) for i in range(int(ct[h]))]
                     for h in range(self.num_heads)]
-            order, _, _, item_map, grid = plan_column_split(lens, q.shape[2], q.shape[0], splits=1)
+            cs64 = run == _native.RUN_TCGEN05_CS64
+            order, _, _, item_map, grid = plan_column_split(
+                lens, q.shape[2], q.shape[0], splits=1, sms=(2 if cs64 else 1) * NUM_SMS,
+                key_tile=64 if cs64 else 128)
             plan = (torch.from_numpy(order).to(q.device), torch.from_numpy(item_map).to(q.device),
                     grid)
         self.plans[key] = plan

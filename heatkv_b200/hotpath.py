@@ -48,13 +48,14 @@ def _makespan(costs: np.ndarray, sms: int) -> float:
     return float(np.pad(costs, (0, pad)).reshape(-1, grid).sum(axis=0).max())
 
 
-def _head_tiles(slots_per_segment, q_len: int, current_in_segments: bool = False) -> np.ndarray:
+def _head_tiles(slots_per_segment, q_len: int, current_in_segments: bool = False,
+                key_tile: int = KEY_TILE) -> np.ndarray:
     """Key tiles of every head: its segments' tiles, then the current scale's (unless the current
     keys already end a non-empty head's segments)."""
-    cur = (q_len + KEY_TILE - 1) // KEY_TILE
+    cur = (q_len + key_tile - 1) // key_tile
     out = []
     for segs in slots_per_segment:
-        seg = sum((int(n) + KEY_TILE - 1) // KEY_TILE for n in segs if n > 0)
+        seg = sum((int(n) + key_tile - 1) // key_tile for n in segs if n > 0)
         out.append(seg + (0 if current_in_segments and seg > 0 else cur))
     return np.array(out, dtype=np.int64)
 
@@ -130,7 +131,7 @@ def _greedy_map(costs: np.ndarray, sms: int):
 def plan_column_split(slots_per_segment, q_len: int, batch: int, *, sms: int = NUM_SMS,
                       splits: Optional[int] = None, item_cost: float = 1.5,
                       merge_cost: float = 4.0, min_gain: float = 0.03,
-                      current_in_segments: bool = False):
+                      current_in_segments: bool = False, key_tile: int = KEY_TILE):
     """Schedule of one column-split launch (128-row blocks): head order, key-range splits, and the
     item map that assigns the launch's items to its CTAs.
 
@@ -140,10 +141,11 @@ def plan_column_split(slots_per_segment, q_len: int, batch: int, *, sms: int = N
     (from a fixed candidate set, 0 included) whose greedy assignment has the lowest makespan, a
     split taken only when it gains ``min_gain``; a given ``splits`` splits every block that many
     ways (1 = none). Items then go longest first to the least-loaded CTA.
+    ``key_tile`` = 64 plans the 64-key kernel (costs in its tile steps, ``sms`` = its CTAs).
     Returns ``(head_order, splits, unsplit_blocks, item_map, grid)``."""
-    tiles = _head_tiles(slots_per_segment, q_len, current_in_segments)
+    tiles = _head_tiles(slots_per_segment, q_len, current_in_segments, key_tile)
     order = np.argsort(tiles, kind="stable").astype(np.int32)
-    nblk = (q_len + KEY_TILE - 1) // KEY_TILE
+    nblk = (q_len + KEY_TILE - 1) // KEY_TILE                  # 128-row query blocks
     t_blk = np.repeat(tiles[order], batch * nblk)             # blocks in kernel order
     blocks = len(t_blk)
 
@@ -358,6 +360,12 @@ class HotPath:
                     order, splits, unsplit, imap, grid = plan_column_split(
                         lens, self.tokens[t], self.batch, splits=forced if forced > 0 else None,
                         current_in_segments=cis)
+                    imap = (torch.from_numpy(imap).to(self.device), grid)
+                elif run == _native.RUN_TCGEN05_CS64 and not natural:
+                    # 64-key kernel: two CTAs per SM, no splits
+                    order, splits, unsplit, imap, grid = plan_column_split(
+                        lens, self.tokens[t], self.batch, splits=1, sms=2 * NUM_SMS,
+                        current_in_segments=cis, key_tile=KEY_TILE // 2)
                     imap = (torch.from_numpy(imap).to(self.device), grid)
                 else:
                     rows = 2 * KEY_TILE if run == _native.RUN_TCGEN05_PAIR else KEY_TILE

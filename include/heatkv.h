@@ -66,11 +66,14 @@ typedef enum {
   HEATKV_ATTN_EXACT = 1,  /* CUDA-core kernel: fp32 products and accumulation for every dtype */
   HEATKV_ATTN_TCGEN05 = 2, /* tcgen05/TMEM kernel; requires q/k/v all bf16 or all f16, or q and
                               k f32 with bf16/f16 v. 16-bit calls take the column-split kernel
-                              (one 128-row query tile per CTA) unless they ask for key-range
-                              splits, which only the two-tile kernel has */
-  HEATKV_ATTN_TCGEN05_PAIR = 3, /* the two-tile tcgen05 kernel (256 query rows per CTA, key-range
-                                   splits); q/k/v all bf16 or all f16 */
-  HEATKV_ATTN_TCGEN05_CS = 4    /* the column-split tcgen05 kernel; never splits key ranges */
+                              (one 128-row query tile per CTA) or the two-tile kernel, as a cost
+                              model of the launch size decides */
+  HEATKV_ATTN_TCGEN05_PAIR = 3, /* the two-tile tcgen05 kernel (256 query rows per CTA); q/k/v all
+                                   bf16 or all f16 */
+  HEATKV_ATTN_TCGEN05_CS = 4,   /* the column-split tcgen05 kernel (128 query rows per CTA) */
+  HEATKV_ATTN_TCGEN05_CS64 = 5  /* 64-key tiles, two CTAs per SM (128 query rows each); q/k/v all
+                                   bf16 or all f16, no key-range splits, no scatter epilogue (such
+                                   calls take the column-split kernel) */
 } heatkv_attn_kernel;
 
 /* The kernel an attention call runs (heatkv_attention_kernel_for). */
@@ -78,7 +81,8 @@ typedef enum {
   HEATKV_RUN_EXACT = 1,         /* attn_simt_kernel: CUDA cores, fp32 products */
   HEATKV_RUN_TCGEN05_PAIR = 2,  /* attn_sm100_kernel: two 128-row query tiles per CTA */
   HEATKV_RUN_TCGEN05_CS = 3,    /* attn_sm100_cs_kernel, 16-bit mode */
-  HEATKV_RUN_TCGEN05_TF32 = 4   /* attn_sm100_cs_kernel, tf32 mode (fp32 q/k, 16-bit v) */
+  HEATKV_RUN_TCGEN05_TF32 = 4,  /* attn_sm100_cs_kernel, tf32 mode (fp32 q/k, 16-bit v) */
+  HEATKV_RUN_TCGEN05_CS64 = 5   /* attn_sm100_cs64_kernel: 64-key tiles, two CTAs per SM */
 } heatkv_attn_run;
 
 /* OR into the kernel selector: the segment metadata (starts, ends, counts) and the head order are

@@ -113,7 +113,7 @@ def _random_layout(rng, heads, max_segments, capacity, lengths=(1, 4, 16, 36, 64
     return [torch.from_numpy(x) for x in (starts, ends, counts)]
 
 
-@pytest.mark.parametrize("which", ["tcgen05_cs", "tcgen05_pair"])
+@pytest.mark.parametrize("which", ["tcgen05_cs", "tcgen05_pair", "tcgen05_cs64"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("B,H,L,cap,S", [
     (1, 1, 1, 700, 3), (2, 3, 4, 400, 4), (1, 2, 127, 900, 5), (2, 2, 128, 900, 5),
@@ -138,7 +138,7 @@ def test_tcgen05_random_layouts(which, dtype, B, H, L, cap, S, cuda_device, kern
     assert _native.device_status(cuda_device) == 0
 
 
-@pytest.mark.parametrize("which", ["tcgen05_cs", "tcgen05_pair"])
+@pytest.mark.parametrize("which", ["tcgen05_cs", "tcgen05_pair", "tcgen05_cs64"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("L", [5, 200, 300])
 def test_tcgen05_scores_growing_tile_by_tile(which, dtype, L, cuda_device, kernel):
@@ -647,7 +647,7 @@ def test_item_map_entry_outside_the_launch_is_skipped_and_flagged(cuda_device):
     _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
 
 
-@pytest.mark.parametrize("sel", ["cs", "pair", "exact"])
+@pytest.mark.parametrize("sel", ["cs", "pair", "exact", "cs64"])
 def test_current_in_segments_flag(sel, cuda_device):
     """HEATKV_ATTN_CURRENT_IN_SEGMENTS: with every head's current keys copied into the slab right
     after its last segment (extending it), the flagged call reads no separate current tiles and
@@ -682,7 +682,7 @@ def test_current_in_segments_flag(sel, cuda_device):
     st2, en2, ct2 = (torch.from_numpy(np.ascontiguousarray(x, dtype=np.int32)).to(d)
                      for x in (st2, en2, ct2))
     kern = {"cs": _native.ATTN_TCGEN05_CS, "pair": _native.ATTN_TCGEN05_PAIR,
-            "exact": _native.ATTN_EXACT}[sel]
+            "exact": _native.ATTN_EXACT, "cs64": _native.ATTN_TCGEN05_CS64}[sel]
     out = torch.empty(B, L, H * 128, dtype=q.dtype, device=d)
     dt = _native.DTYPE_CODES
     order = torch.arange(H, dtype=torch.int32, device=d)
@@ -695,4 +695,52 @@ def test_current_in_segments_flag(sel, cuda_device):
         "heatkv_segmented_attention_sched")
     torch.cuda.synchronize()
     _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
+    assert _native.device_status(d) == 0
+
+
+def test_cs64_item_map_and_kernel_choice(cuda_device):
+    """The 64-key kernel (two CTAs per SM) runs when named (heatkv_attention_kernel_for), a random
+    item map over its 128-row items on 296 CTAs gives the same bits as its launch without one,
+    and both match the reference."""
+    import ctypes
+    lib = _native.load()
+    dt = _native.DTYPE_CODES
+    B, H, L, cap, S = 2, 16, 576, 4000, 12
+    assert lib.heatkv_attention_kernel_for(dt[torch.bfloat16], dt[torch.bfloat16],
+                                           dt[torch.bfloat16], B, H, L,
+                                           _native.ATTN_TCGEN05_CS64, 1, 0, 0) == \
+        _native.RUN_TCGEN05_CS64
+    rng = np.random.default_rng(31)
+    gen = torch.Generator().manual_seed(31)
+    d = cuda_device
+    q, ck, cv = (torch.randn(B, H, L, 128, generator=gen).bfloat16().to(d) for _ in range(3))
+    pk, pv = (torch.randn(B, cap, 128, generator=gen).bfloat16().to(d) for _ in range(2))
+    st, en, ct = (x.to(d) for x in _random_layout(rng, H, S, cap))
+    order = torch.from_numpy(rng.permutation(H).astype(np.int32)).to(d)
+    n_items = B * H * ((L + 127) // 128)
+    grid = 296
+    per_cta = [[] for _ in range(grid)]
+    for item in rng.permutation(n_items):
+        per_cta[int(rng.integers(grid))].append(int(item))
+    rounds = max(len(x) for x in per_cta)
+    imap = np.full(rounds * grid, -1, dtype=np.int32)
+    for c, items in enumerate(per_cta):
+        for k, item in enumerate(items):
+            imap[c + k * grid] = item
+    imap = torch.from_numpy(imap).to(d)
+    scale = 1.0 / math.sqrt(128)
+    plain = torch.full((B, L, H * 128), float("nan"), dtype=q.dtype, device=d)
+    _native.check(lib.heatkv_segmented_attention_sched(
+        _native.ptr(q), _native.ptr(pk), _native.ptr(pv), _native.ptr(st), _native.ptr(en),
+        _native.ptr(ct), _native.ptr(ck), _native.ptr(cv), _native.ptr(plain), dt[q.dtype],
+        dt[ck.dtype], dt[cv.dtype], B, H, L, cap, 128, S, ctypes.c_float(scale),
+        _native.ATTN_TCGEN05_CS64, _native.ptr(order), 1, 0, None, 0,
+        _native.stream_handle(d)), "heatkv_segmented_attention_sched")
+    mapped = _attention_mapped(q, pk, pv, st, en, ct, ck, cv, scale, order=order, splits=1,
+                               unsplit=0, item_map=imap, grid=grid, workspace=None,
+                               kernel=_native.ATTN_TCGEN05_CS64)
+    torch.cuda.synchronize()
+    assert torch.equal(mapped, plain)
+    ref = _torch_reference(q, pk, pv, st.cpu(), en.cpu(), ct.cpu(), ck, cv, scale)
+    _check_lowp(mapped.float().cpu().numpy(), ref.cpu().numpy())
     assert _native.device_status(d) == 0

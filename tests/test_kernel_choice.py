@@ -1,14 +1,16 @@
 """Which attention kernel a call runs (heatkv_attention_kernel_for, no GPU needed): dtype routing
-as the reference's dot modes imply it, the kernel selectors, key-range splits, and the cost model
-that chooses between the column-split and two-tile tcgen05 kernels for unsplit 16-bit calls."""
+as the reference's dot modes imply it, the kernel selectors, the 64-key kernel as the default for
+16-bit calls, and the cost model that chooses between the column-split and two-tile tcgen05
+kernels for calls the 64-key kernel does not take (key-range splits with a workspace)."""
 
 import pytest
 
 from heatkv_b200 import _native
 
 F32, F16, BF16 = 0, 1, 2
-AUTO, EXACT, TC, PAIR, CS = (_native.ATTN_AUTO, _native.ATTN_EXACT, _native.ATTN_TCGEN05,
-                             _native.ATTN_TCGEN05_PAIR, _native.ATTN_TCGEN05_CS)
+AUTO, EXACT, TC, PAIR, CS, CS64 = (_native.ATTN_AUTO, _native.ATTN_EXACT, _native.ATTN_TCGEN05,
+                                   _native.ATTN_TCGEN05_PAIR, _native.ATTN_TCGEN05_CS,
+                                   _native.ATTN_TCGEN05_CS64)
 
 
 def run(dt=(BF16, BF16, BF16), batch=2, heads=16, q_len=4096, kernel=AUTO, splits=1, ws=0,
@@ -17,31 +19,35 @@ def run(dt=(BF16, BF16, BF16), batch=2, heads=16, q_len=4096, kernel=AUTO, split
                                                       unsplit)
 
 
-def test_two_row_image_stays_on_the_column_split_kernel():
-    for lq in (1, 4, 16, 36, 64, 144, 256, 400, 576, 1024, 1600, 2304, 4096):
-        assert run(q_len=lq) == _native.RUN_TCGEN05_CS, lq
+def test_sixteen_bit_calls_take_the_64_key_kernel():
+    for batch in (2, 8, 16):
+        for lq in (1, 4, 16, 36, 64, 144, 256, 400, 576, 1024, 1600, 2304, 4096):
+            assert run(batch=batch, q_len=lq) == _native.RUN_TCGEN05_CS64, (batch, lq)
+    assert run(kernel=TC) == _native.RUN_TCGEN05_CS64
+    # splits without a workspace cannot run split: the 64-key kernel runs them whole
+    assert run(splits=2, ws=0) == _native.RUN_TCGEN05_CS64
 
 
-def test_large_launches_take_the_two_tile_kernel():
-    assert run(batch=16, q_len=4096) == _native.RUN_TCGEN05_PAIR
-    assert run(batch=8, heads=28, q_len=2304) == _native.RUN_TCGEN05_PAIR
+def test_split_calls_take_the_cost_model_choice():
+    """Key-range splits with a workspace leave the 64-key kernel (it has none) for the column-split
+    or two-tile kernel, as the cost model of the launch size chooses (unsplit_blocks counts the
+    chosen kernel's blocks)."""
+    for splits, unsplit in ((2, 0), (4, 100), (3, 2 * 16 * 32)):
+        assert run(splits=splits, ws=1, unsplit=unsplit) == _native.RUN_TCGEN05_CS
+        assert run(batch=16, splits=splits, ws=1, unsplit=unsplit) == _native.RUN_TCGEN05_PAIR
+    assert run(batch=8, heads=28, q_len=2304, splits=2, ws=1) == _native.RUN_TCGEN05_PAIR
     # padded 256-row blocks lose: Lq 1600 stays on the column split at 16 rows
-    assert run(batch=16, q_len=1600) == _native.RUN_TCGEN05_CS
-    assert run(batch=16, q_len=64) == _native.RUN_TCGEN05_CS
+    assert run(batch=16, q_len=1600, splits=2, ws=1) == _native.RUN_TCGEN05_CS
+    assert run(batch=16, q_len=64, splits=2, ws=1) == _native.RUN_TCGEN05_CS
 
 
-def test_key_range_splits_do_not_change_the_kernel():
-    """Both tcgen05 kernels split key ranges, so splits, the workspace and unsplit_blocks leave
-    the choice to the cost model (unsplit_blocks counts the chosen kernel's blocks)."""
-    for splits, ws, unsplit in ((2, 1, 0), (2, 0, 0), (4, 1, 100), (3, 1, 2 * 16 * 32)):
-        assert run(splits=splits, ws=ws, unsplit=unsplit) == _native.RUN_TCGEN05_CS
-        assert run(batch=16, splits=splits, ws=ws, unsplit=unsplit) == _native.RUN_TCGEN05_PAIR
-
-
-def test_named_variants_and_the_static_metadata_flag():
+def test_named_variants_and_the_flags():
     assert run(kernel=PAIR) == _native.RUN_TCGEN05_PAIR
     assert run(batch=16, kernel=CS) == _native.RUN_TCGEN05_CS
-    assert run(kernel=AUTO | _native.ATTN_STATIC_META) == _native.RUN_TCGEN05_CS
+    assert run(kernel=CS64) == _native.RUN_TCGEN05_CS64
+    assert run(kernel=CS64, splits=2, ws=1) == _native.RUN_TCGEN05_CS64
+    assert run(kernel=AUTO | _native.ATTN_STATIC_META) == _native.RUN_TCGEN05_CS64
+    assert run(kernel=AUTO | _native.ATTN_CURRENT_IN_SEGMENTS) == _native.RUN_TCGEN05_CS64
     assert run(kernel=EXACT) == _native.RUN_EXACT
 
 
@@ -53,16 +59,17 @@ def test_dtype_routing():
     # every other mix, and all-fp32, on the exact kernel
     assert run(dt=(F32, F32, F32)) == _native.RUN_EXACT
     assert run(dt=(F16, BF16, BF16)) == _native.RUN_EXACT
-    assert run(dt=(F16, F16, F16)) == _native.RUN_TCGEN05_CS
+    assert run(dt=(F16, F16, F16)) == _native.RUN_TCGEN05_CS64
 
 
 @pytest.mark.parametrize("dt,kernel", [((F32, F32, F32), TC), ((F16, BF16, BF16), TC),
-                                       ((F32, F32, BF16), PAIR)])
+                                       ((F32, F32, BF16), PAIR), ((F32, F32, BF16), CS64)])
 def test_tensor_core_selectors_reject_other_dtypes(dt, kernel):
     assert run(dt=dt, kernel=kernel) == _native.HEATKV_ERR_UNSUPPORTED
 
 
 def test_invalid_arguments():
     assert run(kernel=7) == _native.HEATKV_ERR_INVALID_ARGUMENT
+    assert run(kernel=6) == _native.HEATKV_ERR_INVALID_ARGUMENT
     assert run(q_len=0) == _native.HEATKV_ERR_INVALID_ARGUMENT
     assert run(dt=(5, BF16, BF16)) == _native.HEATKV_ERR_UNSUPPORTED
