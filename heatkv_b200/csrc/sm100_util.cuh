@@ -1,6 +1,7 @@
 // Device and host helpers shared by the tcgen05 attention kernels (attn_sm100.cu,
-// attn_sm100_tf32.cu): the key-tile cursor over a head's slab segments, TMEM row loads, packed
-// fp32x2 arithmetic and exp2 variants, bounded drain waits, and tensor-map encoding.
+// attn_sm100_cs.cu, attn_sm100_cs64.cu): the key-tile cursor over a head's slab segments, TMEM row
+// loads, row maxima, packed fp32x2 arithmetic and exp2 variants, bounded drain waits, and
+// tensor-map encoding.
 #pragma once
 
 #include "common.cuh"
