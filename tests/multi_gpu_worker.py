@@ -36,7 +36,9 @@ def main() -> int:
         # no key-range splits on either side: a split block sums in a different order
         full = HotPath(ctrl, L, H, batch, dev, layers=layers, plan_splits=1)
         inputs, ref_out, _, _ = allocate_io(full, seed=11)       # identical on every rank
-        HotPath.run(full.launches(inputs, ref_out))
+        # the peer-to-peer exchange scatters from the column-split kernel: compare bits with it
+        ref_kernel = _native.ATTN_TCGEN05_CS if exchange == "p2p" else _native.ATTN_AUTO
+        HotPath.run(full.launches(inputs, ref_out, kernel=ref_kernel))
         plan = sharding.plan_shards(sharding.head_costs(ctrl, L, H), batch, world, split=split)
         sh = sharding.ShardedHotPath(ctrl, L, H, plan, rank, dev, gather=True, layers=layers,
                                      exchange=exchange, plan_splits=1)

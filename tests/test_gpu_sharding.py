@@ -119,7 +119,8 @@ def test_sharded_ranks_reassemble_the_single_gpu_outputs(world, split):
 
 def test_scatter_attention_places_rows_in_every_destination():
     """heatkv_segmented_attention_scatter: the heads of one call split over two emulated ranks,
-    each storing its rows into two full outputs (both on this GPU), equals the unsharded call."""
+    each storing its rows into two full outputs (both on this GPU), equals the unsharded call of
+    the kernel the scatter runs (the column-split one), bit for bit."""
     dev = torch.device("cuda", 0)
     lib = _native.load()
     B, H, L, cap, S = 2, 16, 600, 5000, 8
@@ -141,7 +142,7 @@ def test_scatter_attention_places_rows_in_every_destination():
     _native.check(lib.heatkv_segmented_attention(
         _native.ptr(q), _native.ptr(pk), _native.ptr(pv), *[_native.ptr(m) for m in meta],
         _native.ptr(k), _native.ptr(v), _native.ptr(ref), DT[q.dtype], DT[k.dtype], DT[v.dtype],
-        B, H, L, cap, 128, S, scale, 0, _native.ATTN_TCGEN05,
+        B, H, L, cap, 128, S, scale, 0, _native.ATTN_TCGEN05_CS,
         _native.stream_handle(dev)), "reference call")
     dests = [torch.full_like(ref, float("nan")) for _ in range(2)]
     ptrs = torch.tensor([d.data_ptr() for d in dests], dtype=torch.int64, device=dev)
