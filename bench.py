@@ -508,12 +508,11 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
                      "peak": sustained, "unit": "TFLOP/s",
                      "frac": round(att_achieved / sustained, 4),
                      # DRAM bytes of one target-12 launch (the largest share of the step) from an
-                     # ncu capture of that shape; 77.7 MB are algorithmic, the rest is K/V re-read
-                     # by the query blocks of a head
-                     "traffic": 127081728, "traffic_launch": "target 12 (Lq 4096, 2 rows x 16 heads)",
+                     # ncu capture of that shape (read + write)
+                     "traffic": 124575232, "traffic_launch": "target 12 (Lq 4096, 2 rows x 16 heads)",
                      "peak_kind": f"bf16_tflops_sustained ({peak_src})",
                      "frac_of_burst": round(att_achieved / burst, 4),
-                     "kernel": "attn_sm100_cs_kernel", "launches_per_step": n_att,
+                     "kernel": "attn_sm100_cs64_kernel", "launches_per_step": n_att,
                      "ms_per_step": round(att_ms, 3),
                      "step_ms_with_launch_events": round(step_ms_events, 3),
                      "ms_by_target": [round(x, 3) for x in by_target]},
