@@ -26,10 +26,13 @@
 //                slots would poison O; P is 0 there), then issues PV(g) once P(g) is stored.
 //   * warp 7   : TMA producer of V tiles.
 // Items are (head rank, batch row, 128-row query block); CTA c runs items c, c + grid, ... or, with
-// an item map, item_map[c], item_map[c + grid], ... (-1 = empty slot). No key-range splits and no
-// scatter epilogue (callers that need them take attn_sm100_cs.cu). Every wait is bounded; on
-// expiry the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains its copies and MMAs, frees TMEM and
-// returns.
+// an item map, item_map[c], item_map[c + grid], ... (-1 = empty slot). Key-range splits as in
+// attn_sm100_cs.cu: the blocks after the first `unsplit` are cut into `splits` ranges of their key
+// tiles; a split writes (m, l) and its unnormalised O rows to the workspace, and the CTA that
+// completes a block's last split (an atomic counter per block) merges them; a split without key
+// tiles only publishes (-inf, 0). No scatter epilogue (such callers take attn_sm100_cs.cu). Every
+// wait is bounded; on expiry the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains its copies and
+// MMAs, frees TMEM and returns.
 #include "attn.h"
 #include "common.cuh"
 #include "sm100_util.cuh"
@@ -76,6 +79,7 @@ struct __align__(1024) Smem {
   uint64_t drain;       // both issuers' products have completed
   uint32_t tmem_base;
   int abort_flag;
+  int last_flag;        // this CTA completed the last split of its block
   int head_order[kMaxHeads];
   int head_nseg[kMaxHeads];
   int head_tiles[kMaxHeads];
@@ -94,7 +98,12 @@ struct Params {
   unsigned int* status;
   float scale_log2;
   int qblocks;
-  int n_items;
+  int n_items;          // unsplit + (blocks - unsplit) * splits
+  int splits;           // key-range splits of each split block (1 = none)
+  int unsplit;          // leading blocks (schedule order) that are not split
+  uint32_t* ws_counter; // [split blocks], zero between calls
+  float2* ws_ml;        // [split blocks * splits * 128]
+  float* ws_o;          // [split blocks * splits * 128 * 128]
   const int32_t* item_map;
   int n_slots;
   int seg_stride;
@@ -103,17 +112,34 @@ struct Params {
 };
 
 struct Item {
-  int h, b, q0, n;
+  int h, b, q0;       // head, batch row, first query row
+  int j0, n;          // first key tile of the item, key tiles
+  int split, nsplit;  // split index, splits of the block (1 = unsplit)
+  int sblock;         // index of the block among the split blocks
 };
 
 __device__ __forceinline__ Item decode_item(const Smem& sm, const Params& p, int item) {
   Item it;
-  const int qb = item % p.qblocks;
-  const int rb = item / p.qblocks;
+  int block;
+  if (item < p.unsplit) {
+    block = item;
+    it.split = 0;
+    it.nsplit = 1;
+  } else {
+    const int k = item - p.unsplit;
+    block = p.unsplit + k / p.splits;
+    it.split = k % p.splits;
+    it.nsplit = p.splits;
+  }
+  it.sblock = block - p.unsplit;
+  const int qb = block % p.qblocks;
+  const int rb = block / p.qblocks;
   it.b = rb % static_cast<int>(p.batch);
   it.h = sm.head_order[rb / static_cast<int>(p.batch)];
   it.q0 = qb * kBM;
-  it.n = sm.head_tiles[it.h];
+  const int tiles = sm.head_tiles[it.h];
+  it.j0 = static_cast<int>((int64_t(tiles) * it.split) / it.nsplit);
+  it.n = static_cast<int>((int64_t(tiles) * (it.split + 1)) / it.nsplit) - it.j0;
   return it;
 }
 
@@ -247,6 +273,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int item = slot_item(sm, p, slot);
         if (item < 0) continue;
         const Item it = decode_item(sm, p, item);
+        if (it.n == 0) continue;  // an empty split: no Q, no tiles
         const int bh = it.b * H + it.h;
         if (loads_k) {
           // Q rows of the item once the previous item's last QK has completed; rows past the
@@ -260,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int cur_row0 = bh * Lq;
         const int slab_row0 = static_cast<int>(int64_t(it.b) * p.capacity);
         Cursor cur;
-        cur.begin(sm, it.h, stride, 0);
+        cur.begin(sm, it.h, stride, it.j0);
         for (int j = 0; j < it.n; ++j, ++gx) {
           const int s = gx % 2;
           // the stage's previous tile (gx - 2) is done with: its QK (K) or its PV (V)
@@ -297,6 +324,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int item = slot_item(sm, p, slot);
         if (item < 0) continue;
         const Item it = decode_item(sm, p, item);
+        if (it.n == 0) continue;
         if (!(ok = mbar_wait(&sm.q_full, qcnt & 1, abort_flag, p.status))) break;
         ++qcnt;
         for (int j = 0; j < it.n; ++j, ++g) {
@@ -334,8 +362,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int item = slot_item(sm, p, slot);
       if (item < 0) continue;
       const Item it = decode_item(sm, p, item);
+      if (it.n == 0) continue;
       Cursor cur;
-      cur.begin(sm, it.h, stride, 0);
+      cur.begin(sm, it.h, stride, it.j0);
       for (int j = 0; j < it.n; ++j, ++g) {
         const uint32_t b = g % 2;
         ok = __all_sync(0xffffffffu, mbar_wait(&sm.v_full[b], (g / 2) & 1, abort_flag, p.status));
@@ -388,17 +417,92 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
     const uint32_t tO = tmem + lane_off + kColO;
     const float c = p.scale_log2;
+    // workspace row of this thread's query row in split `split` of the item's block
+    auto split_slot = [&](const Item& it, int split) {
+      return (int64_t(it.sblock) * it.nsplit + split) * kBM + row;
+    };
+    // After every softmax thread has published its split's partial row: count the split in, and
+    // if it was the block's last, merge the partials of this thread's row into the output. All
+    // four softmax warps take both barriers.
+    auto split_finish = [&](const Item& it) {
+      asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
+      if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(p.ws_counter + it.sblock, 1u);
+        const int last = old == static_cast<unsigned>(it.nsplit - 1) ? 1 : 0;
+        if (last) {
+          p.ws_counter[it.sblock] = 0;  // every split has arrived: reset for the next call
+          __threadfence();
+        }
+        sm.last_flag = last;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
+      const int qrow = it.q0 + row;
+      if (!sm.last_flag || qrow >= Lq) return;
+      float2 ml[kMaxKvSplits];
+      float mmax = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < kMaxKvSplits; ++k) {
+        ml[k] = k < it.nsplit ? __ldcg(p.ws_ml + split_slot(it, k)) : make_float2(-INFINITY, 0.f);
+        if (ml[k].y > 0.f) mmax = fmaxf(mmax, ml[k].x);
+      }
+      float wk[kMaxKvSplits];
+      float lsum = 0.f;
+#pragma unroll
+      for (int k = 0; k < kMaxKvSplits; ++k) {
+        wk[k] = ml[k].y > 0.f ? ex2(ml[k].x - mmax) : 0.f;
+        lsum = fmaf(wk[k], ml[k].y, lsum);
+      }
+      const float inv = 1.f / lsum;
+#pragma unroll
+      for (int k = 0; k < kMaxKvSplits; ++k) wk[k] *= inv;
+      OutT* orow = static_cast<OutT*>(p.out) + ((int64_t(it.b) * Lq + qrow) * H + it.h) * kD;
+#pragma unroll 1
+      for (int cc = 0; cc < kD / 16; ++cc) {  // 16 columns a step, every split's loads in flight
+        float4 v[kMaxKvSplits][4];
+#pragma unroll
+        for (int k = 0; k < kMaxKvSplits; ++k) {
+          const float4* src = reinterpret_cast<const float4*>(p.ws_o + split_slot(it, k) * kD) + cc * 4;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            v[k][i] = wk[k] != 0.f ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        uint32_t wv[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int k = 0; k < kMaxKvSplits; ++k) {
+            acc.x = fmaf(wk[k], v[k][i].x, acc.x);
+            acc.y = fmaf(wk[k], v[k][i].y, acc.y);
+            acc.z = fmaf(wk[k], v[k][i].z, acc.z);
+            acc.w = fmaf(wk[k], v[k][i].w, acc.w);
+          }
+          wv[2 * i] = pack2<kBF16>(acc.x, acc.y);
+          wv[2 * i + 1] = pack2<kBF16>(acc.z, acc.w);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(orow + cc * 16);
+        dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+      }
+    };
     uint32_t g = 0, ocnt = 0;
     bool ok = true;
     for (int slot = blockIdx.x; slot < p.n_slots; slot += gridDim.x) {
       const int item = slot_item(sm, p, slot);
       if (item < 0) continue;
       const Item it = decode_item(sm, p, item);
+      if (it.n == 0) {
+        // a split without key tiles: it contributes nothing to its block
+        if (it.q0 + row < Lq) __stcg(p.ws_ml + split_slot(it, it.split), make_float2(-INFINITY, 0.f));
+        split_finish(it);
+        continue;
+      }
       float m_run = -INFINITY;
       float l_run = 0.f;
       const bool row_live = it.q0 + row < Lq;
       Cursor cur;
-      cur.begin(sm, it.h, stride, 0);
+      cur.begin(sm, it.h, stride, it.j0);
       for (int j = 0; j < it.n; ++j, ++g) {
         const uint32_t b = g % 2;
         const uint32_t tS = tmem + lane_off + b * kBN;
@@ -473,17 +577,30 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         cur.next();
       }
+      const bool split = it.nsplit > 1;
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.o_final, ocnt & 1, abort_flag, p.status));
+      if (split && it.q0 + row < Lq)
+        __stcg(p.ws_ml + split_slot(it, it.split),
+               ok ? make_float2(m_run, l_run) : make_float2(-INFINITY, 0.f));
       if (ok) {
         tc_fence_after();
         const int qrow = it.q0 + row;
         const float inv = 1.f / l_run;
         OutT* orow = static_cast<OutT*>(p.out) + ((int64_t(it.b) * Lq + qrow) * H + it.h) * kD;
+        float* prow = split ? p.ws_o + split_slot(it, it.split) * kD : nullptr;
 #pragma unroll 1
         for (int half = 0; half < 4; ++half) {
           float o[32];
           tmem_ld32_sync(tO + 32 * half, o);
-          if (qrow < Lq) {
+          if (split) {
+            // a split's partial row, unnormalised (the merge divides by the combined sum)
+            if (qrow < Lq) {
+              float4* d4 = reinterpret_cast<float4*>(prow + 32 * half);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                __stcg(d4 + i, make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]));
+            }
+          } else if (qrow < Lq) {
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
               uint32_t wv[8];
@@ -501,6 +618,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (lane == 0) mbar_arrive(&sm.o_free);
       }
       ++ocnt;
+      if (split) split_finish(it);
     }
   }
 
@@ -540,6 +658,14 @@ static cudaError_t launch_t(const CUtensorMap& tq, const CUtensorMap& tck, const
 }  // namespace cs64
 }  // namespace sm100
 
+int attention_cs64_auto_splits(int64_t batch, int64_t heads, int64_t q_len) {
+  // enough splits of every 128-row block for two waves of the kernel's two CTAs per SM
+  const int64_t blocks = batch * heads * ((q_len + sm100::cs64::kBM - 1) / sm100::cs64::kBM);
+  const int64_t target = 4 * int64_t(sm100::sm_count());
+  if (blocks <= 0 || blocks >= target) return 1;
+  return static_cast<int>(std::min<int64_t>(kMaxKvSplits, (target + blocks - 1) / blocks));
+}
+
 cudaError_t launch_attention_sm100_cs64(const AttnArgs& a, bool bf16, cudaStream_t st) {
   using namespace sm100::cs64;
   const int64_t cur_rows = a.batch * a.heads * a.q_len;
@@ -554,11 +680,26 @@ cudaError_t launch_attention_sm100_cs64(const AttnArgs& a, bool bf16, cudaStream
                           reinterpret_cast<uintptr_t>(a.slab_v) | reinterpret_cast<uintptr_t>(a.out);
   if (align & 15u) return cudaErrorNotSupported;
   const int qblocks = static_cast<int>((a.q_len + kBM - 1) / kBM);
-  const int64_t n_items = a.batch * a.heads * qblocks;
+  const int64_t blocks = a.batch * a.heads * qblocks;
+  // key-range splits of the blocks after the first unsplit_blocks (128-row blocks)
+  int splits = a.kv_splits <= 0 ? attention_cs64_auto_splits(a.batch, a.heads, a.q_len)
+                                : a.kv_splits;
+  splits = std::min(splits, kMaxKvSplits);
+  int64_t unsplit = splits > 1 ? std::min<int64_t>(std::max<int64_t>(a.unsplit_blocks, 0), blocks)
+                               : blocks;
+  if (unsplit == blocks) splits = 1;
+  const int requested = splits;
+  SplitScratch scratch{};
+  if (splits > 1 &&
+      !split_scratch(a.workspace, a.workspace_bytes, blocks - unsplit, splits, kBM, &scratch)) {
+    splits = 1;  // no (or too small) workspace: run unsplit
+    unsplit = blocks;
+  }
+  const int64_t n_items = unsplit + (blocks - unsplit) * splits;
   if (n_items >= (int64_t(1) << 31)) return cudaErrorNotSupported;
-  // an item map numbers this kernel's unsplit items; a call asking for key-range splits runs
-  // unsplit here and drops the map planned for the split layout
-  const bool use_map = a.item_map != nullptr && a.map_grid > 0 && a.kv_splits <= 1 &&
+  // an item map numbers the items of the requested split layout: kept only when that layout runs
+  // and the map has a slot for every item
+  const bool use_map = a.item_map != nullptr && a.map_grid > 0 && splits == requested &&
                        a.map_len >= n_items && a.map_len < (int64_t(1) << 31);
   const bool slab = a.capacity > 0;
   const void* sk = slab ? a.slab_k : a.cur_k;
@@ -586,6 +727,11 @@ cudaError_t launch_attention_sm100_cs64(const AttnArgs& a, bool bf16, cudaStream
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.qblocks = qblocks;
   p.n_items = static_cast<int>(n_items);
+  p.splits = splits;
+  p.unsplit = static_cast<int>(unsplit);
+  p.ws_counter = splits > 1 ? scratch.counter : nullptr;
+  p.ws_ml = splits > 1 ? scratch.ml : nullptr;
+  p.ws_o = splits > 1 ? scratch.o : nullptr;
   p.item_map = use_map ? a.item_map : nullptr;
   p.n_slots = static_cast<int>(use_map ? a.map_len : n_items);
   p.seg_stride = static_cast<int>(std::max<int64_t>(a.max_segments, 1));

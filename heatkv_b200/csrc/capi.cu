@@ -189,18 +189,17 @@ static int plan_attention(int q_dtype, int k_dtype, int v_dtype, int64_t batch, 
   if (kernel != HEATKV_ATTN_EXACT && qk32 && !scatter) {
     out->run = HEATKV_RUN_TCGEN05_TF32;
   } else if (kernel != HEATKV_ATTN_EXACT && same16) {
-    // Default: the 64-key kernel (two CTAs per SM), faster at every launch size measured. It
-    // has no key-range splits and no scatter epilogue: calls asking for splits (with a
-    // workspace) or scattering take the column-split or two-tile kernel, as the cost model
-    // chooses (unsplit_blocks counts the chosen kernel's blocks: 256 query rows for the two-tile
-    // kernel, 128 for the column split).
+    // Default: the 64-key kernel (two CTAs per SM), faster at every launch size measured, with
+    // or without key-range splits (unsplit_blocks counts 128-row blocks for it and the column
+    // split, 256-row blocks for the two-tile kernel). It has no scatter epilogue: scattering calls
+    // take the column-split or two-tile kernel, as the cost model chooses.
+    (void)kv_splits;
+    (void)has_workspace;
     (void)unsplit_blocks;
-    const bool wants_splits = kv_splits > 1 && has_workspace;
     bool pair = variant == 1;
     if (variant == 0) pair = heatkv::attention_prefers_pair(batch, heads, q_len);
     out->run = pair ? HEATKV_RUN_TCGEN05_PAIR : HEATKV_RUN_TCGEN05_CS;
-    if (!scatter && (variant == 3 || (variant == 0 && !wants_splits)))
-      out->run = HEATKV_RUN_TCGEN05_CS64;
+    if (!scatter && (variant == 3 || variant == 0)) out->run = HEATKV_RUN_TCGEN05_CS64;
   } else {
     if (scatter)
       return fail(HEATKV_ERR_UNSUPPORTED,

@@ -336,12 +336,14 @@ class HotPath:
         # length-aware schedule of every attention launch (host planner, device head orders)
         self.schedule = {}
         ws_bytes = 0
-        # plan_splits (default: HEATKV_PLAN_SPLITS, else 1): "auto" = tail splits chosen by the
-        # planner for the kernel each launch runs, or a fixed number of key-range splits for
-        # every block (1 = never split). Column-split launches always get an item map (greedy,
-        # longest first); on the 2B image auto splits measured the same as none (665 / 667
-        # TFLOP/s), so the default is 1. A split block sums its keys in a different order, so
-        # outputs are bit-reproducible across launch shapes (e.g. head shards) only unsplit.
+        # plan_splits (default: HEATKV_PLAN_SPLITS, else 1): "auto" = splits of the longest
+        # blocks chosen by the planner for the kernel each launch runs, or a fixed number of
+        # key-range splits for every block (1 = never split). Column-split and 64-key launches
+        # always get an item map (greedy, longest first). On the 2B image the planner's splits
+        # lost to none with both kernels (64-key: 659.6 against 702.5 TFLOP/s: a split block's
+        # partial writes and merge cost more than the idle CTAs they fill), so the default is 1.
+        # A split block sums its keys in a different order, so outputs are bit-reproducible
+        # across launch shapes (e.g. head shards) only unsplit.
         if plan_splits is None:
             plan_splits = os.environ.get("HEATKV_PLAN_SPLITS", "1")
         forced = 0 if str(plan_splits) == "auto" else int(plan_splits)
@@ -362,10 +364,12 @@ class HotPath:
                         current_in_segments=cis)
                     imap = (torch.from_numpy(imap).to(self.device), grid)
                 elif run == _native.RUN_TCGEN05_CS64 and not natural:
-                    # 64-key kernel: two CTAs per SM, no splits
+                    # 64-key kernel: two CTAs per SM; costs in its 64-key tile steps (an item's
+                    # fill and drain ~3 of them, a split half's partial write and merge ~4)
                     order, splits, unsplit, imap, grid = plan_column_split(
-                        lens, self.tokens[t], self.batch, splits=1, sms=2 * NUM_SMS,
-                        current_in_segments=cis, key_tile=KEY_TILE // 2)
+                        lens, self.tokens[t], self.batch, splits=forced if forced > 0 else None,
+                        sms=2 * NUM_SMS, item_cost=3.0, merge_cost=4.0, current_in_segments=cis,
+                        key_tile=KEY_TILE // 2)
                     imap = (torch.from_numpy(imap).to(self.device), grid)
                 else:
                     rows = 2 * KEY_TILE if run == _native.RUN_TCGEN05_PAIR else KEY_TILE

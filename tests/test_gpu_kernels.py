@@ -391,7 +391,8 @@ def _attention_ws(q, pk, pv, st, en, ct, ck, cv, scale, *, head_order, splits, w
     return out
 
 
-SPLIT_KERNELS = {"pair": (_native.ATTN_TCGEN05_PAIR, 256), "cs": (_native.ATTN_TCGEN05_CS, 128)}
+SPLIT_KERNELS = {"pair": (_native.ATTN_TCGEN05_PAIR, 256), "cs": (_native.ATTN_TCGEN05_CS, 128),
+                 "cs64": (_native.ATTN_TCGEN05_CS64, 128)}
 
 
 @pytest.mark.parametrize("variant", sorted(SPLIT_KERNELS))

@@ -1,7 +1,6 @@
 """Which attention kernel a call runs (heatkv_attention_kernel_for, no GPU needed): dtype routing
-as the reference's dot modes imply it, the kernel selectors, the 64-key kernel as the default for
-16-bit calls, and the cost model that chooses between the column-split and two-tile tcgen05
-kernels for calls the 64-key kernel does not take (key-range splits with a workspace)."""
+as the reference's dot modes imply it, the kernel selectors, and the 64-key kernel as the default
+for 16-bit calls, with or without key-range splits."""
 
 import pytest
 
@@ -28,17 +27,18 @@ def test_sixteen_bit_calls_take_the_64_key_kernel():
     assert run(splits=2, ws=0) == _native.RUN_TCGEN05_CS64
 
 
-def test_split_calls_take_the_cost_model_choice():
-    """Key-range splits with a workspace leave the 64-key kernel (it has none) for the column-split
-    or two-tile kernel, as the cost model of the launch size chooses (unsplit_blocks counts the
-    chosen kernel's blocks)."""
+def test_split_calls_take_the_64_key_kernel():
+    """The 64-key kernel takes key-range splits too (unsplit_blocks counts its 128-row blocks),
+    so splits, the workspace and unsplit_blocks leave 16-bit calls on it at every size. (Only
+    scattering calls, which it cannot serve, go to the column-split or two-tile kernel by the
+    cost model; the GPU scatter tests cover those.)"""
     for splits, unsplit in ((2, 0), (4, 100), (3, 2 * 16 * 32)):
-        assert run(splits=splits, ws=1, unsplit=unsplit) == _native.RUN_TCGEN05_CS
-        assert run(batch=16, splits=splits, ws=1, unsplit=unsplit) == _native.RUN_TCGEN05_PAIR
-    assert run(batch=8, heads=28, q_len=2304, splits=2, ws=1) == _native.RUN_TCGEN05_PAIR
-    # padded 256-row blocks lose: Lq 1600 stays on the column split at 16 rows
-    assert run(batch=16, q_len=1600, splits=2, ws=1) == _native.RUN_TCGEN05_CS
-    assert run(batch=16, q_len=64, splits=2, ws=1) == _native.RUN_TCGEN05_CS
+        assert run(splits=splits, ws=1, unsplit=unsplit) == _native.RUN_TCGEN05_CS64
+        assert run(batch=16, splits=splits, ws=1, unsplit=unsplit) == _native.RUN_TCGEN05_CS64
+    assert run(batch=8, heads=28, q_len=2304, splits=2, ws=1) == _native.RUN_TCGEN05_CS64
+    # named variants keep their own kernel with splits
+    assert run(kernel=PAIR, splits=2, ws=1) == _native.RUN_TCGEN05_PAIR
+    assert run(kernel=CS, splits=2, ws=1) == _native.RUN_TCGEN05_CS
 
 
 def test_named_variants_and_the_flags():
