@@ -190,6 +190,10 @@ class Launch:
     work: float          # algorithmic FLOPs (attention) or HBM bytes (pack)
     keep: object = None  # device arrays the arguments point into
     sources: tuple = ()  # (plan index, target) of the step inputs a pack reads
+    # an attention launch flagged HEATKV_ATTN_CURRENT_IN_SEGMENTS: the (starts, ends, counts)
+    # pointers of the same keys without the current scale inside the segments, for callers that
+    # re-issue it through an entry point without a kernel selector (the scatter)
+    unflagged_meta: Optional[tuple] = None
 
     def __call__(self, stream: ctypes.c_void_p) -> None:
         status = self.fn(*self.args, stream)
@@ -444,6 +448,9 @@ class HotPath:
                 else:
                     launch = Launch("attention", p.layer, t, lib.heatkv_segmented_attention_sched,
                                     head + ws, flops)
+                if cur_in:
+                    st0, en0, ct0, _ = p.dense_meta[t]
+                    launch.unflagged_meta = (_native.ptr(st0), _native.ptr(en0), _native.ptr(ct0))
                 row_k = D * k.element_size()
                 row_v = D * v.element_size()
                 jobs = []

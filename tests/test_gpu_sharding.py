@@ -163,3 +163,45 @@ def test_scatter_attention_places_rows_in_every_destination():
     for d in dests:
         assert torch.equal(d, ref)
     assert _native.device_status(dev) == 0
+
+
+def test_scatter_of_dense_launches_uses_prefix_only_segments():
+    """The hot path's dense-prefix launches walk one segment per head that already ends with the
+    current scale (HEATKV_ATTN_CURRENT_IN_SEGMENTS). The scatter entry point of the peer-to-peer
+    exchange takes no kernel selector, so the exchange re-issues those launches with their
+    prefix-only segments (Launch.unflagged_meta). Re-issued that way into one full output on this
+    GPU, every dense target of a layer matches the hot path's own output (bf16 tolerance: the
+    scatter runs the column-split kernel, the hot path the 64-key one)."""
+    dev = torch.device("cuda", 0)
+    lib = _native.load()
+    ctrl, L, H = bench.build_controller("2b", 0.10)
+    hot = HotPath(ctrl, L, H, 2, dev, layers=[21], plan_splits=1)
+    inputs, outputs, _, _ = allocate_io(hot, seed=4)
+    launches = hot.launches(inputs, outputs)
+    HotPath.run(launches)
+    torch.cuda.synchronize()
+    rows = torch.arange(2, dtype=torch.int32, device=dev)
+    heads = torch.arange(H, dtype=torch.int32, device=dev)
+    checked = 0
+    for launch in launches:
+        # dense targets only: their dense-cache rows stay as they were; later appends reuse the
+        # slots of fused targets, so those cannot be re-run after the step
+        if launch.kind != "attention" or launch.target >= hot.plans[0].first_target:
+            continue
+        a = launch.args
+        meta = launch.unflagged_meta or (a[3], a[4], a[5])
+        if launch.target in hot.plans[0].dense_append:
+            assert launch.unflagged_meta is not None
+        ref = outputs[0][launch.target]
+        out = torch.full_like(ref, float("nan"))
+        ptrs = torch.tensor([out.data_ptr()], dtype=torch.int64, device=dev)
+        _native.check(lib.heatkv_segmented_attention_scatter(
+            a[0], a[1], a[2], meta[0], meta[1], meta[2], a[6], a[7], _native.ptr(ptrs), 1,
+            _native.ptr(rows), _native.ptr(heads), 2, H, a[9], a[10], a[11], a[12], a[13], a[14],
+            a[15], a[16], a[17], a[18], a[20], _native.stream_handle(dev)), "scatter")
+        torch.cuda.synchronize()
+        err = (out.float() - ref.float()).abs().max().item()
+        assert err <= 2e-2 and err / ref.float().abs().max().item() <= 1e-2, (launch.target, err)
+        checked += 1
+    assert checked >= 7
+    assert _native.device_status(dev) == 0
