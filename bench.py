@@ -71,36 +71,54 @@ def build_controller(model: str, budget: float):
 
 
 class ClockSampler:
-    """nvidia-smi samples every 200 ms while the timed region runs."""
+    """nvidia-smi samples every 100 ms while the timed region runs. The sampler waits (at most
+    3 s) for nvidia-smi's first line before the region starts and keeps only the lines that
+    arrive after that, so the summary describes the timed region, not the idle GPU before it."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, period_ms: int = 100):
         self.gpu = gpu_index
+        self.period_ms = period_ms
         self.proc = None
+        self._raw = []
+        self.lines = []
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self._raw.append((time.monotonic(), line))
 
     def __enter__(self):
+        import threading
+        self._raw = []
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "--format=csv,noheader,nounits", "-lms", str(self.period_ms)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True, bufsize=1)
         except (OSError, ValueError):
             self.proc = None
+        if self.proc is not None:
+            self._thread = threading.Thread(target=self._read, daemon=True)
+            self._thread.start()
+            t0 = time.monotonic()
+            while not self._raw and self.proc.poll() is None and time.monotonic() - t0 < 3.0:
+                time.sleep(0.01)
+        self.t_start = time.monotonic()
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+                self.proc.wait()
+            self._thread.join(timeout=5)
+        self.lines = [l for t, l in self._raw if t >= self.t_start and l.strip()]
 
     def summary(self):
         sm, mx, reasons = [], None, set()
