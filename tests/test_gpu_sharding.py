@@ -171,7 +171,9 @@ def test_scatter_of_dense_launches_uses_prefix_only_segments():
     exchange takes no kernel selector, so the exchange re-issues those launches with their
     prefix-only segments (Launch.unflagged_meta). Re-issued that way into one full output on this
     GPU, every dense target of a layer matches the hot path's own output (bf16 tolerance: the
-    scatter runs the column-split kernel, the hot path the 64-key one)."""
+    scatter runs the column-split kernel, the hot path the 64-key one) and, bit for bit, the hot
+    path built without dense appends first and run on the column-split kernel (the reference the
+    2-GPU peer-to-peer test compares with)."""
     dev = torch.device("cuda", 0)
     lib = _native.load()
     ctrl, L, H = bench.build_controller("2b", 0.10)
@@ -179,6 +181,9 @@ def test_scatter_of_dense_launches_uses_prefix_only_segments():
     inputs, outputs, _, _ = allocate_io(hot, seed=4)
     launches = hot.launches(inputs, outputs)
     HotPath.run(launches)
+    plain = HotPath(ctrl, L, H, 2, dev, layers=[21], plan_splits=1, dense_append_first=False)
+    _, plain_out, _, _ = allocate_io(plain, seed=4, fill=False)
+    HotPath.run(plain.launches(inputs, plain_out, kernel=_native.ATTN_TCGEN05_CS))
     torch.cuda.synchronize()
     rows = torch.arange(2, dtype=torch.int32, device=dev)
     heads = torch.arange(H, dtype=torch.int32, device=dev)
@@ -202,6 +207,7 @@ def test_scatter_of_dense_launches_uses_prefix_only_segments():
         torch.cuda.synchronize()
         err = (out.float() - ref.float()).abs().max().item()
         assert err <= 2e-2 and err / ref.float().abs().max().item() <= 1e-2, (launch.target, err)
+        assert torch.equal(out, plain_out[0][launch.target]), launch.target
         checked += 1
     assert checked >= 7
     assert _native.device_status(dev) == 0
