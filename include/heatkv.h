@@ -191,7 +191,9 @@ int heatkv_segmented_attention(const void* q, const void* slab_k, const void* sl
  *   workspace       : device scratch of workspace_bytes >= heatkv_attention_workspace_bytes(...)
  *                     for kv_splits > 1, 256-byte aligned, zero-filled once before its first use
  *                     (every call leaves it zeroed again). Concurrent calls need separate
- *                     workspaces. NULL runs unsplit.
+ *                     workspaces. NULL runs unsplit. A call whose CTAs gave up on a bounded
+ *                     wait (heatkv_device_status reports HEATKV_DEVICE_WAIT_TIMEOUT) can leave
+ *                     split counters non-zero: zero the workspace again before reusing it.
  * Extends fused_real_pruning_flat_segmented_attention (real_pruning_fused_attention.py:445-591);
  * the reference's Triton grid has no scheduler options.
  */
@@ -316,7 +318,9 @@ size_t heatkv_attention_workspace_bytes(int64_t batch, int64_t heads, int64_t q_
  * kernel needs no scratch).
  *   - Allocates nothing: no cudaMalloc/cudaFree and no allocating library routine. The first call
  *     made with a device current looks up that device's scratch address (cudaGetSymbolAddress);
- *     make that first call before any stream capture.
+ *     make that first call before any stream capture. The address is kept per device index for
+ *     the life of the process: it is not valid across cudaDeviceReset (or any other teardown of
+ *     the device's primary context), after which this entry point must not be called again.
  *   - kv_splits whose scratch would exceed 32 MiB (heatkv_attention_workspace_bytes(...) >
  *     33554432) are rejected with HEATKV_ERR_UNSUPPORTED; kv_splits = 1 needs no scratch.
  *   - Every call shares the one array and leaves its last contents there; the split counters are

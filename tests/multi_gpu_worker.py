@@ -3,7 +3,10 @@
 Every rank builds the same seeded global inputs of two 2B layers, keeps its (row, head) units,
 runs its part of the sharded hot path - attention, compaction, NCCL all-gather and reassembly -
 eagerly and then as a CUDA graph replay, and checks that the full outputs it received equal the
-single-GPU engine's outputs bit for bit (rank 0 computes those). Exit status 0 = parity.
+single-GPU engine's outputs bit for bit. Rank 0 also checks the gathered outputs of one layer at
+every scale against attention over exactly the tokens the keep-mask retains (plain PyTorch fp32,
+``_keepmask.keep_mask_attention``) at the bf16 tolerance, so the exchange is pinned to the
+keep-mask semantics and not only to the engine it mirrors. Exit status 0 = parity.
 """
 
 import datetime
@@ -13,12 +16,17 @@ import sys
 import torch
 import torch.distributed as dist
 
-REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
 sys.path.insert(0, REPO)
+sys.path.insert(0, HERE)
 
 import bench  # noqa: E402
 from heatkv_b200 import _native, sharding  # noqa: E402
 from heatkv_b200.hotpath import HotPath, allocate_io  # noqa: E402
+from _keepmask import keep_mask_attention  # noqa: E402
+
+BF16_ATOL, BF16_REL = 2e-2, 1e-2
 
 
 def main() -> int:
@@ -78,6 +86,17 @@ def main() -> int:
             return good
 
         ok = check("eager") and ok
+        if rank == 0:
+            # the last layer of the pair (it has pruned targets) against the keep-mask semantics
+            i = len(layers) - 1
+            for t in range(full.num_scales):
+                ref = keep_mask_attention(ctrl, layers[i], t, inputs[i])
+                err = (fo[i][t].float() - ref).abs().max().item()
+                scale = ref.abs().max().item()
+                if not (err <= BF16_ATOL and err / scale <= BF16_REL):
+                    print(f"rank 0: layer {layers[i]} target {t} vs keep-mask attention: max "
+                          f"{err} (scale {scale})", flush=True)
+                    ok = False
         for row in fo:
             for x in row:
                 x.fill_(float("nan"))

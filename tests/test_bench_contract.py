@@ -34,3 +34,23 @@ def test_warmup_below_three_is_rejected():
     res = subprocess.run(cmd, capture_output=True, text=True, timeout=300, cwd=REPO)
     assert res.returncode != 0
     assert "--warmup must be >= 3" in res.stderr
+
+
+def test_reference_arm_loads_no_code_of_this_package():
+    """The reference arm times the reference's CPU path on the recorded schedule: neither the
+    package nor its native library may be loaded in that process."""
+    code = (
+        "import sys, types, bench\n"
+        "args = types.SimpleNamespace(workload='c5', shard='auto', global_rows=64, budget=0.10,\n"
+        "    model='2b', rows=2, exchange='p2p', ref_layers=1, ref_targets=1, steps=1, warmup=3)\n"
+        "bench.run_reference(args, 0, 1)\n"
+        "bad = [m for m in sys.modules if m.startswith('heatkv_b200')]\n"
+        "so = [m for m in bench._loaded_native() if 'heatkv' in m]\n"
+        "assert not bad and not so, (bad, so)\n"
+        "print('clean')\n")
+    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=600, cwd=REPO)
+    assert res.returncode == 0, res.stderr[-2000:]
+    assert res.stdout.strip().endswith("clean")
+    line = json.loads(res.stdout.strip().splitlines()[0])
+    assert line["cpu_baseline"]["sample"].startswith("2B 10% layers/targets 0:8..8")

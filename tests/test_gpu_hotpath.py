@@ -5,13 +5,13 @@ the controller removes (s, head) at that target - computed with plain PyTorch fp
 This checks the slab schedule, the pack descriptors and the kernel together at full 13-scale size.
 """
 
-import math
-
 import pytest
 import torch
 
 from heatkv_b200 import _native
 from heatkv_b200.hotpath import HotPath, allocate_io
+
+from _keepmask import keep_mask_attention
 
 pytestmark = pytest.mark.gpu
 
@@ -23,30 +23,8 @@ def _controller(model, budget):
     return bench.build_controller(model, budget)
 
 
-def _retained_tokens(ctrl, layer, target, head):
-    ranges = ctrl.scale_ranges
-    mask = ctrl.removed_mask_for_layer(layer)
-    idx = []
-    for s in range(target):
-        if mask[target, s, head]:
-            continue
-        idx.append(torch.arange(ranges[s][0], ranges[s][1]))
-    return torch.cat(idx) if idx else torch.zeros(0, dtype=torch.long)
-
-
 def _reference(ctrl, layer, t, inputs_layer, head_dim=128):
-    q, k, v = inputs_layer[t]
-    B, H, n, D = q.shape
-    full_k = torch.cat([inputs_layer[s][1] for s in range(t + 1)], dim=2).float()
-    full_v = torch.cat([inputs_layer[s][2] for s in range(t + 1)], dim=2).float()
-    start = ctrl.scale_ranges[t][0]
-    out = torch.empty(B, n, H, D, device=q.device)
-    for h in range(H):
-        idx = torch.cat([_retained_tokens(ctrl, layer, t, h),
-                         torch.arange(start, start + n)]).to(q.device)
-        s = torch.einsum("bnd,bsd->bns", q[:, h].float(), full_k[:, h, idx]) / math.sqrt(D)
-        out[:, :, h] = torch.softmax(s, -1) @ full_v[:, h, idx]
-    return out.reshape(B, n, H * D)
+    return keep_mask_attention(ctrl, layer, t, inputs_layer)
 
 
 @pytest.mark.parametrize("model,budget,layers", [("2b", 0.10, [0, 21]), ("2b", 0.05, [3]),
