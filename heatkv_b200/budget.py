@@ -14,10 +14,12 @@ Same entry points, argument meaning, results and error messages as the reference
 * ``strict_removed_heads_by_scale_specific_for_budget`` (utils.py:525-597) - the per-target
   removed-head view: atoms finalised after the previous target plus atoms activated early.
 
-The reference re-sums the whole cache after every activation; here the cache total is kept as an
-integer and decremented by ``tokens[source]`` per activated atom, and the activation candidates
-are walked once per target in their fixed priority order. The arithmetic (Python ints compared
-with the float threshold) is the same, so the removed sets are identical.
+The per-target loop of the strict schedule runs in native code (``heatkv_strict_budget``,
+csrc/install_plan.cpp). The reference re-sums the whole cache after every activation; there the
+cache total is kept as an integer and decremented by ``tokens[source]`` per activated atom, and
+the activation candidates are walked once per target in their fixed priority order. The
+arithmetic (integers compared with the double threshold) is the same, so the removed sets are
+identical.
 """
 
 from __future__ import annotations
@@ -185,96 +187,46 @@ def strict_pruning_schedule_for_budget_scale_specific(
         budget, retained_tokens=protected_tokens, num_layers=num_layers, num_heads=num_heads,
         skip_last_scale=skip_last_scale, scale_schedule=schedule)
 
+    # the per-target loop (final removals, early activations, feasibility) in native code
+    import ctypes
+
+    import numpy as np
+
+    from . import _native
+    L, H, S = num_layers, num_heads, num_scales
+    n_src = s1 - s0 + 1
+    orders_arr = np.ascontiguousarray(np.array(seq, dtype=np.int32).reshape(n_src, L * H, 2))
+    tok = np.array(tokens, dtype=np.int64)
+    counts = np.array([int(prune_counts.get(i, 0)) for i in range(S)], dtype=np.int64)
+    final_mask = np.empty((S, S, L, H), dtype=np.uint8)
+    cap = max(1, S * n_src * L * H)
+    early_arr = np.empty((cap, 5), dtype=np.int32)
+    n_early = ctypes.c_int64(0)
+    err = np.zeros(3, dtype=np.int64)
+    status = _native.load().heatkv_strict_budget(
+        orders_arr.ctypes.data, n_src, L, H, S, tok.ctypes.data, s0, int(protected_prefix_scales),
+        budgeted, ctypes.c_double(threshold), counts.ctypes.data, final_mask.ctypes.data,
+        early_arr.ctypes.data, cap, ctypes.byref(n_early), err.ctypes.data)
+    if status != _native.HEATKV_OK:
+        kind, t_err, l_err = (int(x) for x in err)
+        if kind == 1:
+            raise ValueError(f"budget {budget} is infeasible at scale index {t_err}, layer {l_err}")
+        if kind == 2:
+            raise ValueError(f"budget {budget} is infeasible at end of scale index {t_err}")
+        if kind == 3:
+            raise RuntimeError("strict scale-specific schedule failed to activate "
+                               f"end-of-scale removals at scale index {t_err}")
+        _native.check(status, "heatkv_strict_budget")
     final_counts, final_by_scale, early_by_scale = {}, {}, {}
-    active = set()
-    for t in range(num_scales):
-        nxt = min(t + 1, num_scales - 1)
-        count = int(prune_counts.get(nxt, prune_counts.get(t, 0)))
-        if t >= budgeted:
-            final_counts[t] = len(active)
-            final_by_scale[t] = _atoms_by_source_and_layer(
-                active, num_layers=num_layers, source_scale_indices=sources)
-            early_by_scale[t] = {}
-            continue
-        target_atoms = set()
-        for s in range(s0, min(s1, t) + 1):
-            for head, layer in order_of[s][:count]:
-                target_atoms.add((s, head, layer))
-
-        # removed-atom count per (source, layer) among the active set
-        removed_sl = {}
-        for s, _, l in active:
-            removed_sl[(s, l)] = removed_sl.get((s, l), 0) + 1
-        cur_active = set(active)
-
-        def add_active(atom):
-            cur_active.add(atom)
-            key = (atom[0], atom[2])
-            removed_sl[key] = removed_sl.get(key, 0) + 1
-
-        for atom in target_atoms:
-            if atom[2] < 0:  # pragma: no cover - layers are validated non-negative
-                raise AssertionError
-        by_layer = {}
-        for atom in target_atoms:
-            by_layer.setdefault(atom[2], []).append(atom)
-
-        # cache total with the current scale's K/V written for layers <= l
-        protected_cached = sum(tokens[:min(int(protected_prefix_scales), t)])
-        base = num_layers * num_heads * protected_cached
-        for s in range(s0, min(s1, t) + 1):
-            if s == t:
-                continue
-            for l in range(num_layers):
-                base += (num_heads - removed_sl.get((s, l), 0)) * tokens[s]
-
-        # early-activation candidates in priority order: last layer, larger source, order rank
-        candidates = sorted(
-            (a for a in target_atoms if a[0] != t),
-            key=lambda a: (-a[2], -a[0], rank_of[a[0]][(a[1], a[2])]),
-        )
-        cursor = 0
-        total = base
-        early = {}
-        for l in range(num_layers):
-            # newly "passed" atoms of this layer count as removed at this checkpoint
-            for atom in by_layer.get(l, ()):
-                if atom not in cur_active:
-                    add_active(atom)
-                    if atom[0] != t:
-                        total -= tokens[atom[0]]
-            if s0 <= t <= s1:  # the current scale's K/V of layer l is now in the cache
-                total += (num_heads - removed_sl.get((t, l), 0)) * tokens[t]
-            if total <= threshold:
-                continue
-            activated = []
-            while cursor < len(candidates):
-                atom = candidates[cursor]
-                if atom[2] <= l:
-                    break
-                cursor += 1
-                if atom in cur_active:
-                    continue
-                add_active(atom)
-                activated.append(atom)
-                total -= tokens[atom[0]]
-                if total <= threshold:
-                    break
-            if total > threshold:
-                raise ValueError(f"budget {budget} is infeasible at scale index {t}, layer {l}")
-            if activated:
-                early[l] = activated
-        if total > threshold:
-            raise ValueError(f"budget {budget} is infeasible at end of scale index {t}")
-        if cur_active != target_atoms:
-            raise RuntimeError(
-                "strict scale-specific schedule failed to activate "
-                f"end-of-scale removals at scale index {t}")
-        active = set(target_atoms)
-        final_counts[t] = len(active)
+    for t in range(S):
+        idx = np.argwhere(final_mask[t])             # (source, layer, head), sorted
+        atoms = [(int(a), int(c), int(b)) for a, b, c in idx]
+        final_counts[t] = len(atoms)
         final_by_scale[t] = _atoms_by_source_and_layer(
-            active, num_layers=num_layers, source_scale_indices=sources)
-        early_by_scale[t] = early
+            atoms, num_layers=num_layers, source_scale_indices=sources)
+        early_by_scale[t] = {}
+    for t, l, src, h, layer in early_arr[:n_early.value].tolist():
+        early_by_scale[t].setdefault(l, []).append((src, h, layer))
     return {"final_removed_counts": final_counts, "final_removed_by_scale": final_by_scale,
             "early_activation_by_scale": early_by_scale}
 

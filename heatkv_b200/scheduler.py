@@ -35,10 +35,11 @@ import numpy as np
 from . import _native
 
 
-def _placement(controller, *, layer_idx: int, num_heads: int):
+def _placement(controller, *, layer_idx: int, num_heads: int, arrays: bool = False):
     """Placed segments (placement order), high-water mark and capacity bound of a layer, from
     libheatkv's ``heatkv_slot_schedule`` (the reference's placement and capacity bound, :206-370,
-    in native code)."""
+    in native code); with ``arrays`` also the raw ``(scale_start, scale_end, offset, end_target)``
+    arrays."""
     mask = np.ascontiguousarray(controller.removed_mask_for_layer(layer_idx), dtype=np.uint8)
     ranges = controller.scale_ranges
     num_scales = len(controller.scale_schedule)
@@ -64,6 +65,8 @@ def _placement(controller, *, layer_idx: int, num_heads: int):
                          "scale_start": int(lo[s]), "scale_end": int(hi[s]), "offset": off})
     segs.sort(key=lambda it: (it["start_target"], it["end_target"], -it["length"],
                               it["source_scale"], it["head"]))
+    if arrays:
+        return segs, int(cap.value), int(bound.value), (lo, hi, offset, end_t)
     return segs, int(cap.value), int(bound.value)
 
 
@@ -157,64 +160,57 @@ def build_static_slot_schedule(controller, *, layer_idx: int, num_heads: int,
     """Return the reference's schedule dict (keys ``enabled``, ``capacity``, ``capacity_bound``,
     ``allocated_capacity``, ``overalloc_slots``, ``segments``, ``segments_by_key``,
     ``segments_by_target``, ``metadata_cpu_by_target``, ``old_pack_runs_by_target``,
-    ``old_pack_cache_lens_by_target``, ``append_runs_by_key``); metadata values are numpy int32."""
+    ``old_pack_cache_lens_by_target``, ``append_runs_by_key``); metadata values are numpy int32.
+    The placement (``heatkv_slot_schedule``), the per-target segment tables and the copy items
+    (``heatkv_slot_tables``) are computed in native code; this function only shapes them into the
+    reference's dict."""
     num_heads = int(num_heads)
     ranges = controller.scale_ranges
     num_scales = len(controller.scale_schedule)
-    assigned, high_water, bound = _placement(controller, layer_idx=layer_idx, num_heads=num_heads)
+    assigned, high_water, bound, placed = _placement(controller, layer_idx=layer_idx,
+                                                     num_heads=num_heads, arrays=True)
 
     if high_water > bound and not allow_overalloc:
         return {"enabled": False, "capacity": bound, "capacity_bound": bound,
                 "allocated_capacity": high_water}
 
+    S, H = num_scales, num_heads
+    lo, hi, offset, end_t = placed
+    m_st = np.empty((S, H, S), dtype=np.int32)
+    m_en = np.empty((S, H, S), dtype=np.int32)
+    m_ct = np.empty((S, H), dtype=np.int32)
+    pack_items = np.empty((S * S * H, 3), dtype=np.int64)
+    pack_index = np.empty(S + 1, dtype=np.int64)
+    app_items = np.empty((S * H, 3), dtype=np.int64)
+    app_index = np.empty(S + 1, dtype=np.int64)
+    _native.check(_native.load().heatkv_slot_tables(
+        S, H, lo.ctypes.data, hi.ctypes.data, offset.ctypes.data, end_t.ctypes.data,
+        m_st.ctypes.data, m_en.ctypes.data, m_ct.ctypes.data, pack_items.ctypes.data,
+        pack_index.ctypes.data, app_items.ctypes.data, app_index.ctypes.data),
+        "heatkv_slot_tables")
+
     by_key = {(seg["source_scale"], seg["head"]): seg for seg in assigned}
     by_target, metadata = {}, {}
     for t in range(1, num_scales):
-        live = [seg for seg in assigned if seg["start_target"] <= t < seg["end_target"]]
-        by_target[t] = live
-        per_head = [[] for _ in range(num_heads)]
-        for seg in live:
-            per_head[seg["head"]].append(seg)
-        width = max((len(x) for x in per_head), default=0)
-        starts = np.zeros((num_heads, width), dtype=np.int32)
-        ends = np.zeros((num_heads, width), dtype=np.int32)
-        counts = np.zeros((num_heads,), dtype=np.int32)
-        for h, segs in enumerate(per_head):
-            segs.sort(key=lambda x: x["source_scale"])
-            counts[h] = len(segs)
-            for i, seg in enumerate(segs):
-                starts[h, i] = seg["offset"]
-                ends[h, i] = seg["offset"] + seg["length"]
-        metadata[t] = (starts, ends, counts)
+        by_target[t] = [seg for seg in assigned if seg["start_target"] <= t < seg["end_target"]]
+        width = int(m_ct[t].max()) if H else 0
+        metadata[t] = (np.ascontiguousarray(m_st[t, :, :width]),
+                       np.ascontiguousarray(m_en[t, :, :width]), m_ct[t].copy())
 
     old_runs, old_lens = {}, {}
-    for t, live in by_target.items():
+    for t in by_target:
         if t not in ranges:
             continue
         old_len = int(ranges[t][0])
         old_lens[t] = old_len
-        items = []
-        for seg in live:
-            hi = min(seg["scale_end"], old_len)
-            if seg["scale_start"] < hi:
-                items.append({"dst_offset": seg["offset"], "head": seg["head"],
-                              "src_start": seg["scale_start"], "length": hi - seg["scale_start"]})
-        old_runs[t] = _copy_runs(items, old_len)
+        old_runs[t] = _runs_from_items(pack_items[pack_index[t]:pack_index[t + 1]], old_len)
 
     append_runs = {}
-    for s, (lo, hi) in ranges.items():
-        nxt = s + 1
-        if nxt >= num_scales or int(hi) - int(lo) <= 0:
+    for s_, (a, b) in ranges.items():
+        if s_ + 1 >= num_scales or int(b) - int(a) <= 0:
             continue
-        cur_len = int(hi) - int(lo)
-        items = []
-        for h in range(num_heads):
-            seg = by_key.get((s, h))
-            if seg is None or not (seg["start_target"] <= nxt < seg["end_target"]):
-                continue
-            items.append({"dst_offset": seg["offset"], "head": h, "src_start": 0,
-                          "length": cur_len})
-        append_runs[(s, nxt)] = _copy_runs(items, cur_len)
+        append_runs[(s_, s_ + 1)] = _runs_from_items(app_items[app_index[s_]:app_index[s_ + 1]],
+                                                     int(b) - int(a))
 
     return {
         "enabled": True, "capacity": int(high_water), "capacity_bound": int(bound),
@@ -225,3 +221,28 @@ def build_static_slot_schedule(controller, *, layer_idx: int, num_heads: int,
         "old_pack_runs_by_target": old_runs, "old_pack_cache_lens_by_target": old_lens,
         "append_runs_by_key": append_runs,
     }
+
+
+def _runs_from_items(items: np.ndarray, sequence_len: int):
+    """Destination-contiguous runs (the reference's run dicts, :414-482) of copy items
+    ``(dst, src, length)`` already sorted by destination."""
+    runs = []
+    for dst, src, length in items.tolist():
+        if length <= 0:
+            continue
+        if runs and runs[-1]["dst_end"] == dst:
+            run = runs[-1]
+        else:
+            run = {"dst_start": dst, "dst_end": dst, "sequence_len": int(sequence_len),
+                   "copy_items": []}
+            runs.append(run)
+        run["copy_items"].append({"dst_start": dst, "src_start": src, "length": length})
+        run["dst_end"] += length
+    for run in runs:
+        ci = run["copy_items"]
+        contiguous = all(ci[i + 1]["src_start"] == ci[i]["src_start"] + ci[i]["length"]
+                         for i in range(len(ci) - 1))
+        run["contiguous_src_start"] = ci[0]["src_start"] if contiguous else None
+        run["contiguous_src_end"] = (ci[0]["src_start"] + run["dst_end"] - run["dst_start"]
+                                     if contiguous else None)
+    return runs

@@ -440,6 +440,52 @@ int heatkv_slot_schedule(const uint8_t* removed, int num_scales, int num_heads,
                          int32_t* end_target_out, int64_t* capacity_out, int64_t* bound_out);
 
 /*
+ * heatkv_slot_tables - the per-target segment tables and copy items of one layer's static slab
+ * schedule, from a placement made by heatkv_slot_schedule; replaces the derivations of
+ * _segmented_flat_build_static_slot_schedule (enable_real_pruning_fast.py:383-558). Host memory.
+ *   offset, end_target : heatkv_slot_schedule's outputs ([num_scales * num_heads])
+ *   meta_starts/meta_ends : int32 [num_scales (target), num_heads, num_scales] slab ranges of the
+ *                  segments live at each target, per head in source-scale order; meta_counts :
+ *                  int32 [num_scales, num_heads] (target 0 has none)
+ *   pack_items   : int64 [n, 3] (dst slot, src row, length) of every target's activation copy from
+ *                  the dense cache of the tokens before it (src = head * tokens_before + start),
+ *                  sorted by dst; target t's items are rows pack_index[t] .. pack_index[t + 1]
+ *                  (pack_index: int64 [num_scales + 1]); at most num_scales * num_heads per target
+ *   append_items : int64 [n, 3] of the append after each scale s (src = head * n_s), rows
+ *                  append_index[s] .. append_index[s + 1]; at most num_heads per scale
+ */
+int heatkv_slot_tables(int num_scales, int num_heads, const int64_t* scale_start,
+                       const int64_t* scale_end, const int64_t* offset, const int32_t* end_target,
+                       int32_t* meta_starts, int32_t* meta_ends, int32_t* meta_counts,
+                       int64_t* pack_items, int64_t* pack_index, int64_t* append_items,
+                       int64_t* append_index);
+
+/*
+ * heatkv_strict_budget - the main loop of strict_pruning_schedule_for_budget_scale_specific
+ * (tools/utils.py:308-522): which (source scale, head, layer) atoms are removed after each target
+ * and which are activated early inside it so every layer checkpoint's cache stays at or under
+ * `threshold` (= budget * num_layers * num_heads * peak tokens). Host memory.
+ *   orders        : int32 [num_sources, num_layers * num_heads, 2] (head, layer) removal order of
+ *                   source scales source_start .. source_start + num_sources - 1 (validated)
+ *   tokens        : int64 [num_scales] tokens per scale; budgeted = scales under the budget
+ *                   (num_scales - 1 when the last scale is not cached)
+ *   prune_count   : int64 [num_scales] pruned_heads_for_budget's counts
+ *   final_mask    : uint8 [num_scales (target), num_scales (source), num_layers, num_heads], 1 for
+ *                   atoms removed after the target
+ *   early         : int32 [early_capacity, 5] (target, checkpoint layer, source, head, layer) of
+ *                   every early activation in activation order; early_count receives their number
+ *   error_info    : int64 [3]: on HEATKV_ERR_INVALID_ARGUMENT from an infeasible budget,
+ *                   (1, target, layer) - over budget at that layer checkpoint, (2, target, 0) -
+ *                   over budget at the end of the target, or (3, target, 0) - the end-of-scale
+ *                   removals were not all activated; (0, 0, 0) otherwise
+ */
+int heatkv_strict_budget(const int32_t* orders, int num_sources, int num_layers, int num_heads,
+                         int num_scales, const int64_t* tokens, int source_start,
+                         int protected_prefix_scales, int budgeted, double threshold,
+                         const int64_t* prune_count, uint8_t* final_mask, int32_t* early,
+                         int64_t early_capacity, int64_t* early_count, int64_t* error_info);
+
+/*
  * heatkv_device_status - read (and with clear != 0, reset) the sticky HEATKV_DEVICE_* flags of
  * the current CUDA device. This call synchronises `stream`. Not part of the reference interface:
  * the reference's Triton kernels do not check descriptors on the device.
