@@ -1,22 +1,30 @@
 #!/usr/bin/env python
-"""Benchmark of the HeatKV hot path on B200: segmented attention + slab compaction per image.
+"""Benchmark of the HeatKV hot path on B200: segmented attention + slab compaction.
 
-Workload: Infinity-2B attention stack at 1024x1024 - 32 layers x 16
-heads x head_dim 128, 13 scales (10,521 tokens), batch 1 doubled to 2 rows for CFG, keep-mask of
-the 10 % budget from orders/2b.json (strict schedule, 3 protected scales, source scales 3..11).
-Q/K/V are seeded N(0, 1) bf16 tensors for every (layer, scale) - no weights exist on the box.
+Default workload (``--workload c5``, BASELINE.json configs[4], the metric's "at 1/2/4/8 GPU"
+configuration): Infinity-2B at 1024x1024 - 32 layers x 16 heads x head_dim 128, 13 scales (10,521
+tokens), batch 32 doubled to 64 rows for CFG, keep-mask of the 10 % budget from orders/2b.json
+(strict schedule, 3 protected scales, source scales 3..11). Every (scale, layer) generates its
+Q/K/V on the device from random-init N(0, 0.02) Infinity-2B QKV weights (``heatkv_b200.projected``:
+projection GEMM, cos-attention normalisation and 2-D RoPE with the early cache appends, then the
+segmented attention and the rest of the compaction). The layer inputs are seeded N(0, 1) per row.
+With N GPUs the 64 rows are sharded over the ranks by the (row, head) planner
+(``heatkv_b200.sharding``), rows only when they divide: every output row is then used on the GPU
+that computed it, so no exchange is needed (strong scaling: the total work is fixed).
 
-One step = one image: for every scale and layer, the attention call (dense-prefix scales and
-fused-segmented scales, both through the tcgen05 kernel) and every compaction pack (dense-cache
-append, slab activation, slab append). The step is captured once per timed step as a CUDA graph
-with timing events around every launch; the inputs of a step (8.3 GB) exceed the 126 MB L2.
+``--workload c2``: one image (2 rows) of pre-generated N(0, 1) bf16 Q/K/V per
+(layer, scale); ``--shard`` splits one batch over the GPUs by (row, head) with an output exchange.
 
+One step = the whole workload once (every layer and scale). The step is replayed as a CUDA graph;
+a second set of graphs with timing events around every launch gives the per-kernel figures.
 Output: one JSON line (rank 0). ``value`` = algorithmic attention TFLOP/s of the whole job
-(sum over ranks of FLOPs / max over ranks of the step time), ``ms_per_image`` beside it;
-``roofline`` for the attention kernel (tensor-bound) and ``roofline_pack`` for compaction
-(HBM-bound); ``e2e`` = the same metric through the C-ABI with Q/K/V copied from pinned host memory
-and outputs copied back every step; ``cpu_baseline`` = the CPU oracle on a bounded sample.
-``--impl reference`` times the reference's CPU algorithm (the oracle port) instead.
+(attention FLOPs of all ranks / max over ranks of the step time, the step including the QKV
+generation), ``ms_per_image`` beside it; ``roofline`` for the attention kernel (tensor-bound),
+``roofline_pack`` for compaction and ``roofline_prep`` for the preparation (HBM-bound);
+``e2e`` = the same step with the layer inputs copied from pinned host memory and the step's
+outputs copied back; ``cpu_baseline`` = the reference's CPU path restated in torch CPU fp32
+(``oracle/bench_sample.py``) on a bounded sample. ``--impl reference`` times that CPU path alone,
+on the same sample, without loading any code of ``heatkv_b200``.
 """
 
 from __future__ import annotations
@@ -36,6 +44,10 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 METRIC = "segmented-attn TFLOP/s & ms/image (2B shape, 1024^2, 10% budget)"
+WORKLOAD_C5 = ("configs[4]: Infinity-2B at 1024^2 - 32 layers x 16 heads x 128, 13 scales, "
+               "batch 32 + CFG = 64 rows, 10% budget from orders/2b.json; Q/K/V generated per "
+               "(layer, scale) from random-init N(0, 0.02) QKV weights (cos-attention, 2-D RoPE); "
+               "rows sharded over the GPUs")
 WORKLOAD = ("configs[1]: Infinity-2B attention stack at 1024^2 - 32 layers x 16 heads x 128, "
             "13 scales, batch 1 (+CFG = 2 rows) per GPU, 10% budget from orders/2b.json")
 WORKLOAD_SHARDED = ("Infinity-2B attention stack at 1024^2, 10% budget from orders/2b.json: one "
@@ -140,103 +152,90 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------------
-# CPU baseline: the oracle (numpy restatement of the reference's torch CPU path)
+# CPU baseline and reference arm: the reference's CPU path restated in torch CPU fp32 on the slab
+# schedule recorded from the reference (oracle/bench_sample.py) - no code of heatkv_b200 loads
 # ------------------------------------------------------------------------------------------------
 
-def cpu_sample(hot_cpu_plan, batch: int, layer_targets, seed: int = 0):
-    """Run the oracle on one layer's fused targets (slab built by the oracle pack from the dense
-    cache + appends), fp32 like the reference's CPU path. Returns (seconds, flops)."""
+def config_of(args) -> dict:
+    """The ``config`` object of the JSON line, identical in both arms (derived from the command
+    line only)."""
+    if args.workload == "c5":
+        return {"workload": WORKLOAD_C5, "global_rows": args.global_rows, "budget": args.budget,
+                "qkv": "generated on the device every step (projection + cos-norm + RoPE)",
+                "l2": "inputs and caches far larger than the 126 MB L2"}
+    if args.shard == "image":
+        return {"workload": WORKLOAD, "rows_per_gpu": args.rows, "budget": args.budget,
+                "l2": "inputs 8.3 GB per image > 126 MB L2"}
+    return {"workload": WORKLOAD_SHARDED, "global_rows": args.global_rows, "shard": args.shard,
+            "exchange": args.exchange, "budget": args.budget,
+            "l2": "inputs 8.3 GB per image > 126 MB L2"}
+
+
+def cpu_baseline_sample(args):
+    """The bounded CPU sample both arms time: the first ``--ref-targets`` fused targets of layers
+    ``0..--ref-layers-1``, 2 rows (one image), with the projection when the workload has it.
+    Returns ``(seconds, flops, description)``."""
+    from oracle.bench_sample import cpu_sample
+    return cpu_sample(layers=tuple(range(args.ref_layers)), n_targets=args.ref_targets, rows=2,
+                      model=args.model, budget=args.budget, project=args.workload == "c5")
+
+
+def cpu_baseline_line(args, world: int):
+    """The GPU arm's ``cpu_baseline`` object (rank 0 at N = 1 only, unless disabled)."""
+    if world != 1 or args.no_cpu_baseline:
+        return None
     import torch
-
-    from oracle.attention import segmented_attention
-    from oracle.pack import pack_flat_segments
-
-    p = hot_cpu_plan
-    H, D = p.num_heads, 128
-    rng = np.random.default_rng(seed)
-    tok = p.tokens
-    t0 = p.first_target
-    sched = p.schedule
-    cap = max(p.capacity, 1)
-    # dense cache of scales < t0 and the activation pack (not timed: install-like preparation)
-    ld = int(p.ranges[t0][0])
-    dense_k = rng.standard_normal((batch, H * ld, D), dtype=np.float32)
-    dense_v = rng.standard_normal((batch, H * ld, D), dtype=np.float32)
-    slab_k = np.zeros((batch, cap, D), np.float32)
-    slab_v = np.zeros((batch, cap, D), np.float32)
-    items = [(s["offset"], s["head"] * ld + s["scale_start"], s["length"])
-             for s in sched["segments_by_target"][t0]]
-    if items:
-        a = np.array(items)
-        pack_flat_segments(slab_k, slab_v, dense_k, dense_v, a[:, 0], a[:, 1], a[:, 2])
-    flops = 0
-    elapsed = 0.0
-    from heatkv_b200.scheduler import copy_descriptors
-    for t in layer_targets:
-        n = tok[t]
-        q, k, v = (rng.standard_normal((batch, H, n, D), dtype=np.float32) for _ in range(3))
-        st, en, ct = sched["metadata_cpu_by_target"][t]
-        t1 = time.perf_counter()
-        segmented_attention(q=q, persisted_k=slab_k, persisted_v=slab_v, segment_starts=st,
-                            segment_ends=en, segment_counts=ct, current_k=k, current_v=v,
-                            softmax_scale=D ** -0.5, compute_dtype=np.float32)
-        if t + 1 < p.num_scales:
-            d = copy_descriptors(sched["append_runs_by_key"].get((t, t + 1), []))
-            if d is not None:
-                pack_flat_segments(slab_k, slab_v, k.reshape(batch, H * n, D),
-                                   v.reshape(batch, H * n, D), d["dst_starts"], d["src_starts"],
-                                   d["lengths"])
-        elapsed += time.perf_counter() - t1
-        flops += 4 * n * int((p.attention_slots(t) + n).sum()) * D * batch
-    del torch
-    return elapsed, flops
-
-
-def cpu_threads() -> int:
-    try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
-        if n:
-            return int(max(n))
-    except Exception:  # pragma: no cover
-        pass
-    return os.cpu_count() or 1
+    sec, flops, desc = cpu_baseline_sample(args)
+    return {"value": round(flops / sec / 1e12, 4), "unit": "TFLOP/s",
+            "cores": int(torch.get_num_threads()), "kind": "port", "sample": desc}
 
 
 def run_reference(args, rank: int, world: int) -> None:
-    """``--impl reference``: the reference's CPU algorithm (oracle port), rank 0 only."""
+    """``--impl reference``: the reference's CPU path (restated in torch CPU fp32), rank 0 only;
+    each warm-up and timed step runs the same bounded sample as the GPU arm's ``cpu_baseline``."""
     if rank != 0:
         return
-    import torch  # noqa: F401  (same interpreter state as the GPU arm)
-    from heatkv_b200.hotpath import LayerPlan
-    ctrl, layers, heads = build_controller(args.model, args.budget)
-    plan = LayerPlan(ctrl, 0, heads, "cpu")
-    targets = list(range(plan.first_target, plan.num_scales))[: args.ref_targets]
-    total_flops = image_flops(ctrl, layers, heads, args.rows)
+    import torch
+
+    from oracle.bench_sample import image_attention_flops
     times = []
+    desc = ""
     for i in range(args.warmup + args.steps):
-        sec, flops = cpu_sample(plan, args.rows, targets, seed=i)
+        sec, flops, desc = cpu_baseline_sample(args)
         if i >= args.warmup:
             times.append((sec, flops))
     sec = sum(t for t, _ in times)
     flops = sum(f for _, f in times)
     tflops = flops / sec / 1e12
-    ms_image = total_flops / (tflops * 1e12) * 1e3 / (args.rows / 2)
-    sample = (f"layer 0 of {args.model.upper()}, targets {targets[0]}..{targets[-1]} "
-              f"(fused slab scales), {args.rows} rows, fp32 numpy/BLAS attention + pack")
+    ms_image = image_attention_flops(rows=2, model=args.model, budget=args.budget) / (
+        tflops * 1e12) * 1e3
+    leaked = [m for m in _loaded_native() if "heatkv" in m]
+    if leaked:
+        raise SystemExit(f"reference arm loaded native code of this repository: {leaked}")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(tflops, 4), "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sec / len(times) * 1e3, 3),
-        "ms_per_image": round(ms_image, 1), "higher_is_better": True, "scaling": "weak",
+        "ms_per_image": round(ms_image, 1), "higher_is_better": True,
+        "scaling": "strong" if args.workload == "c5" or args.shard != "image" else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "rows_per_gpu": args.rows, "budget": args.budget},
-        "cpu_baseline": {"value": round(tflops, 4), "unit": "TFLOP/s", "cores": cpu_threads(),
-                         "kind": "port", "sample": sample},
+        "config": config_of(args),
+        "cpu_baseline": {"value": round(tflops, 4), "unit": "TFLOP/s",
+                         "cores": int(torch.get_num_threads()), "kind": "port",
+                         "sample": desc},
         "e2e": {"value": round(tflops, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def _loaded_native():
+    """Shared objects mapped into this process (Linux), for the reference arm's self-check."""
+    try:
+        with open("/proc/self/maps") as fh:
+            return sorted({l.split()[-1] for l in fh if l.rstrip().endswith(".so")})
+    except OSError:
+        return []
 
 
 def image_flops(ctrl, layers, heads, rows) -> float:
@@ -521,36 +520,19 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     hbm = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
     pack_achieved = pack_bytes / (pack_ms * 1e-3) / 1e9 if pack_ms > 0 else None
 
-    # CPU baseline (rank 0, N = 1 only): the oracle on a bounded sample
-    cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        from heatkv_b200.hotpath import LayerPlan
-        sec = flops = 0.0
-        for layer in range(args.ref_layers):
-            plan = LayerPlan(ctrl, layer, heads, "cpu")
-            targets = list(range(plan.first_target, plan.num_scales))[: args.ref_targets]
-            s_, f_ = cpu_sample(plan, args.rows, targets, seed=layer)
-            sec += s_
-            flops += f_
-        cpu = {"value": round(flops / sec / 1e12, 4), "unit": "TFLOP/s", "cores": cpu_threads(),
-               "kind": "port",
-               "sample": (f"layers 0..{args.ref_layers - 1}, up to {args.ref_targets} fused slab "
-                          f"targets each, {args.rows} rows, fp32 numpy/BLAS oracle, "
-                          f"{flops / 1e12:.2f} TFLOP in {sec:.1f} s")}
-
-    config = {"workload": WORKLOAD if args.shard == "image" else WORKLOAD_SHARDED,
-              **wl.rows_label, "budget": args.budget, "images_per_step": wl.images,
-              "l2": "inputs 8.3 GB per image > 126 MB L2",
-              "mode": "cuda-graph replay, one graph per timed step",
-              "attention_tflop_per_step_per_gpu": round(att_flops / 1e12, 4),
-              "pack_gb_per_step_per_gpu": round(pack_bytes / 1e9, 4),
-              "slab_gb_per_gpu": round(wl.slab_bytes / 1e9, 3)}
+    cpu = cpu_baseline_line(args, world)
+    config = config_of(args)
+    details = {**wl.rows_label, "images_per_step": wl.images,
+               "mode": "cuda-graph replay, one graph per timed step",
+               "attention_tflop_per_step_per_gpu": round(att_flops / 1e12, 4),
+               "pack_gb_per_step_per_gpu": round(pack_bytes / 1e9, 4),
+               "slab_gb_per_gpu": round(wl.slab_bytes / 1e9, 3)}
     line = {
         "metric": METRIC, "value": round(tflops, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3),
         "ms_per_image": round(step_ms / wl.images * (world if wl.scaling == "weak" else 1), 3),
         "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic", "config": config,
+        "data": "synthetic", "config": config, "details": details,
         "roofline": {"bound": "tensor", "achieved": round(att_achieved, 1),
                      "peak": sustained, "unit": "TFLOP/s",
                      "frac": round(att_achieved / sustained, 4),
@@ -582,6 +564,387 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def _timed_replays(graph, steps, stream, dev, world, local_rank):
+    """Replay ``graph`` ``steps`` times between CUDA events on ``stream`` (barrier + synchronise
+    before), sampling the clocks meanwhile. Returns (ms per step, clock summary)."""
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk, torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+    torch.cuda.synchronize(dev)
+    return start.elapsed_time(end) / steps, clk.summary()
+
+
+def _attribution(proj, launches, stream, steps, kinds):
+    """Per-launch CUDA-event times (ms per step, summed by kind and by (kind, target)) from
+    ``steps`` replays of graphs that bracket every launch with external events."""
+    import torch
+    mk = lambda: torch.cuda.Event(enable_timing=True, external=True)  # noqa: E731
+    graphs, ev_sets = [], []
+    for _ in range(steps):
+        evs = [(mk(), mk()) if l.kind in kinds else None for l in launches]
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            proj.run(launches, stream, evs)
+        graphs.append(g)
+        ev_sets.append(evs)
+    with torch.cuda.stream(stream):
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for g in graphs:
+            g.replay()
+        a1.record(stream)
+        a1.synchronize()
+    by_kind, by_target = {k: 0.0 for k in kinds}, {}
+    for evs in ev_sets:
+        for launch, ev in zip(launches, evs):
+            if ev is None:
+                continue
+            d = ev[0].elapsed_time(ev[1]) / steps
+            by_kind[launch.kind] += d
+            key = (launch.kind, launch.target)
+            by_target[key] = by_target.get(key, 0.0) + d
+    del graphs
+    return by_kind, by_target, a0.elapsed_time(a1) / steps
+
+
+def c2_history(args, dev, peaks):
+    """configs[1] (one 2-row image of pre-generated Q/K/V, the previous headline) on this GPU: a
+    short graph-replay timing kept beside the main line so results stay comparable over time."""
+    import torch
+
+    from heatkv_b200.hotpath import HotPath, allocate_io
+    ctrl, layers, heads = build_controller(args.model, args.budget)
+    hot = HotPath(ctrl, layers, heads, 2, dev, torch.bfloat16, torch.bfloat16)
+    inputs, outputs, _, _ = allocate_io(hot, seed=1000)
+    launches = hot.launches(inputs, outputs)
+    att = sum(l.work for l in launches if l.kind == "attention")
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            hot.run(launches, stream)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        hot.run(launches, stream)
+    for _ in range(3):
+        g.replay()
+    ms, _ = _timed_replays(g, max(5, args.steps), stream, dev, 1, dev.index)
+    by_kind, _, _ = _attribution(hot, launches, stream, 1, ("attention", "pack"))
+    sustained = float(peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"]))
+    out = {"workload": WORKLOAD, "value": round(att / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+           "ms_per_image": round(ms, 3),
+           "attention_frac_of_sustained": round(att / (by_kind["attention"] * 1e-3) / 1e12
+                                                / sustained, 4)}
+    del g, inputs, outputs, hot
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+    return out
+
+
+def apply_rotary_emb(q, k, scale_schedule, rope2d_freqs_grid, pad_to_multiplier,
+                     rope2d_normalized_by_hw, scale_ind):
+    """Infinity's 2-D rotary embedding (infinity/models/basic.py:97-117) beside the stand-in
+    attention module below: the installer looks it up in the module's defining Python module."""
+    import torch
+    qk = torch.stack((q, k), dim=0)
+    with torch.autocast(device_type="cuda", enabled=False):
+        seq_len = qk.shape[3]
+        start = sum(a * b * c for a, b, c in scale_schedule[:scale_ind]) if scale_ind >= 1 else 0
+        cache = rope2d_freqs_grid[str(tuple(scale_schedule))][:, :, :, :, start:start + seq_len]
+        qk = qk.reshape(*qk.shape[:-1], -1, 2)
+        qk = torch.stack([cache[0] * qk[..., 0] - cache[1] * qk[..., 1],
+                          cache[1] * qk[..., 0] + cache[0] * qk[..., 1]], dim=-1)
+        q, k = qk.reshape(*qk.shape[:-2], -1).unbind(dim=0)
+    return q, k
+
+
+def dropin_image(args, dev):
+    """One image (2 rows) through the public installer on 32 Infinity-2B-shaped self-attention
+    modules (random N(0, 0.02) weights, fp32 parameters under bf16 autocast as the model runs:
+    fp32 q/k after cos-attention, bf16 v), every scale's forward of every layer: QKV projection,
+    fused preparation, the segmented kernel (dense prefix included) and the output projection.
+    Returns the attention TFLOP/s of the image and its time."""
+    import math
+
+    import torch
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    from heatkv_b200 import budget as bud, synthetic
+    from heatkv_b200.enable_real_pruning_fast import \
+        enable_real_pruning_scale_specific_fused_segmented
+    from oracle.bench_sample import image_attention_flops
+
+    class SelfAttention(nn.Module):
+        """The attributes and forward of infinity/models/basic.py:196-316 that the installer
+        uses (cos-attention, no flash)."""
+
+        def __init__(self, C, H):
+            super().__init__()
+            self.num_heads, self.head_dim, self.cos_attn, self.scale = H, C // H, True, 1
+            self.scale_mul_1H11 = nn.Parameter(torch.full((1, H, 1, 1), 4.0).log())
+            self.max_scale_mul = math.log(100)
+            self.mat_qkv = nn.Linear(C, 3 * C, bias=False)
+            self.q_bias, self.v_bias = nn.Parameter(torch.zeros(C)), nn.Parameter(torch.zeros(C))
+            self.register_buffer("zero_k_bias", torch.zeros(C))
+            self.proj, self.proj_drop = nn.Linear(C, C), nn.Identity()
+            self.caching, self.cached_k, self.cached_v = False, None, None
+            self.pad_to_multiplier, self.rope2d_normalized_by_hw = 1, 2
+
+        def kv_caching(self, enable):
+            self.caching, self.cached_k, self.cached_v = enable, None, None
+
+        def forward(self, x, attn_bias_or_two_vector, attn_fn=None, scale_schedule=None,
+                    rope2d_freqs_grid=None, scale_ind=0):
+            raise NotImplementedError("replaced by the installer")
+
+    SelfAttention.__module__ = __name__
+    layers, heads, C = 32, 16, 2048
+    torch.manual_seed(0)
+    model = nn.ModuleList([SelfAttention(C, heads) for _ in range(layers)])
+    for m in model:
+        nn.init.normal_(m.mat_qkv.weight, 0.0, 0.02)
+        nn.init.normal_(m.proj.weight, 0.0, 0.02)
+    model = model.to(dev)
+    enable_real_pruning_scale_specific_fused_segmented(
+        model, args.budget, bud.orders(model_type=2), protected_prefix_scales=3,
+        source_scale_start=3, fused_qkv_prep=True)
+    sched = [tuple(x) for x in synthetic.SCALE_SCHEDULE_1M]
+    cos, sin = synthetic.rope2d_rows()
+    grid = {str(tuple(sched)): torch.stack([cos, sin])[:, None, None, None].to(dev)}
+    gen = torch.Generator(device=dev).manual_seed(2)
+    xs = [torch.randn(2, h * w, C, device=dev, generator=gen) for _, h, w in sched]
+
+    def image():
+        for m in model:
+            m.kv_caching(True)
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            for t in range(len(sched)):
+                for m in model:
+                    m(xs[t], None, scale_schedule=sched, rope2d_freqs_grid=grid, scale_ind=t)
+
+    for _ in range(3):
+        image()
+    torch.cuda.synchronize(dev)
+    n = max(3, min(args.steps, 10))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        image()
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    flops = image_attention_flops(rows=2, budget=args.budget)
+    del model, xs
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+    return {"value": round(flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "ms_per_image": round(ms, 3), "images": n,
+            "path": ("enable_real_pruning_scale_specific_fused_segmented(fused_qkv_prep=True) on "
+                     "32 Infinity-2B-shaped self-attention modules, fp32 parameters under bf16 "
+                     "autocast (fp32 q/k, bf16 v: the tf32 tcgen05 mode), eager PyTorch forward "
+                     "per (scale, layer) including the QKV and output projections")}
+
+
+def run_projected(args, rank: int, world: int, local_rank: int) -> None:
+    """64 rows, Q/K/V generated every (layer, scale) from the QKV projection."""
+    import torch
+    import torch.distributed as dist
+
+    from heatkv_b200 import _native, sharding
+    from heatkv_b200.hotpath import HotPath
+    from heatkv_b200.projected import ProjectedHotPath
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    peaks, peak_src = load_peaks()
+    history = dropin = None
+    if world == 1 and not args.no_c2_history:
+        history = c2_history(args, dev, peaks)
+    if world == 1 and not args.no_dropin:
+        dropin = dropin_image(args, dev)
+    ctrl, layers, heads = build_controller(args.model, args.budget)
+    costs = sharding.head_costs(ctrl, layers, heads)
+    plan = sharding.plan_shards(costs, args.global_rows, world, split=args.shard)
+    if plan.splits_heads:
+        raise SystemExit("the projected workload shards rows only: use a row count that divides "
+                         "over the GPUs")
+    rows = plan.rows_per_rank
+    hot = HotPath(ctrl, layers, heads, rows, dev, torch.bfloat16, torch.bfloat16)
+    proj = ProjectedHotPath(hot, weight_seed=0)
+    x, x_flat = proj.allocate_inputs(plan.rows_of(rank), seed=1)
+    out, out_flat = proj.allocate_outputs()
+    launches = proj.launches(x, out)
+    att_flops = sum(l.work for l in launches if l.kind == "attention")
+    gemm_flops = sum(l.work for l in launches if l.kind == "gemm")
+    pack_bytes = sum(l.work for l in launches if l.kind == "pack")
+    prep_bytes = sum(l.work for l in launches if l.kind == "prep")
+    n_att = sum(1 for l in launches if l.kind == "attention")
+    n_own = sum(1 for l in launches if l.kind in ("attention", "pack", "prep"))
+
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            proj.run(launches, stream)
+    stream.synchronize()
+    step_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(step_graph, stream=stream):
+        proj.run(launches, stream)
+    step_graph.replay()       # one untimed replay of the captured step
+    step_ms, clocks = _timed_replays(step_graph, args.steps, stream, dev, world, local_rank)
+    if world > 1:
+        dist.barrier()
+    kinds = ("gemm", "prep", "attention", "pack")
+    by_kind, by_target, step_ms_events = _attribution(proj, launches, stream,
+                                                      max(1, args.attrib_steps), kinds)
+    status = _native.device_status(dev)
+
+    # e2e: the layer inputs of each scale come from pinned host memory (copy stream, in scale
+    # order), the step's outputs (the last layer's attention output of every scale) go back to
+    # pinned host memory (third stream) as soon as the scale's last attention is done
+    e2e_steps = 0 if args.no_e2e else max(1, min(args.steps, args.e2e_steps))
+    h_x = torch.empty_like(x_flat, device="cpu").pin_memory() if e2e_steps else None
+    h_out = torch.empty_like(out_flat, device="cpu").pin_memory() if e2e_steps else None
+    if e2e_steps:
+        h_x.copy_(x_flat)
+    copy_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    first_of = {}
+    last_att = {}
+    for j, l in enumerate(launches):
+        first_of.setdefault(l.target, j)
+        if l.kind == "attention":
+            last_att[l.target] = j
+    offs_x = [t_.data_ptr() - x_flat.data_ptr() for t_ in x]
+    offs_o = [t_.data_ptr() - out_flat.data_ptr() for t_ in out]
+    esz = x_flat.element_size()
+
+    def e2e_step():
+        copy_s.wait_stream(stream)          # the device buffers are reused step after step
+        ready = {}
+        for t in range(proj.num_scales):
+            with torch.cuda.stream(copy_s):
+                n = x[t].numel()
+                x[t].view(-1).copy_(h_x[offs_x[t] // esz: offs_x[t] // esz + n],
+                                    non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_s)
+            ready[t] = ev
+        for j, l in enumerate(launches):
+            if first_of.get(l.target) == j:
+                stream.wait_event(ready[l.target])
+            proj.run([l], stream)
+            if last_att.get(l.target) == j:
+                t = l.target
+                ev = torch.cuda.Event()
+                ev.record(stream)
+                d2h_s.wait_event(ev)
+                with torch.cuda.stream(d2h_s):
+                    n = out[t].numel()
+                    h_out[offs_o[t] // esz: offs_o[t] // esz + n].copy_(out[t].view(-1),
+                                                                       non_blocking=True)
+        stream.wait_stream(d2h_s)
+
+    e2e_ms = float("nan")
+    if e2e_steps:
+        with torch.cuda.stream(stream):
+            e2e_step()                      # warm the copy engines
+            stream.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(e2e_steps):
+                e2e_step()
+            e1.record(stream)
+            e1.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    h2d = x_flat.numel() * x_flat.element_size()
+    d2h = out_flat.numel() * out_flat.element_size()
+
+    vals = torch.tensor([step_ms, e2e_ms, by_kind["attention"], by_kind["pack"], by_kind["prep"],
+                         by_kind["gemm"], float(status)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    step_ms, e2e_ms, att_ms, pack_ms, prep_ms, gemm_ms, status = vals.tolist()
+    del step_graph
+    torch.cuda.synchronize(dev)
+    if rank != 0:
+        return
+
+    job_att = att_flops * world
+    images = args.global_rows / 2
+    tflops = job_att / (step_ms * 1e-3) / 1e12
+    sustained = float(peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"]))
+    burst = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+    hbm = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    att_achieved = att_flops / (att_ms * 1e-3) / 1e12
+    ms_by_target = [round(by_target.get(("attention", t), 0.0), 3)
+                    for t in range(proj.num_scales)]
+    line = {
+        "metric": METRIC, "value": round(tflops, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3),
+        "ms_per_image": round(step_ms / images, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config_of(args),
+        "details": {
+            "rows_per_gpu": rows, "row_groups": plan.row_groups, "head_groups": plan.head_groups,
+            "exchange": "none: rows only, every output row is used on the GPU that computed it",
+            "images_per_step": images, "mode": "cuda-graph replay of the whole step",
+            "attention_tflop_per_step_per_gpu": round(att_flops / 1e12, 3),
+            "qkv_gemm_tflop_per_step_per_gpu": round(gemm_flops / 1e12, 3),
+            "slab_gb_per_gpu": round(hot.slab_bytes() / 1e9, 3),
+            "early_append_slots_per_row": proj.early_slots,
+            "pack_append_slots_per_row": proj.rest_slots,
+            "ms_by_stage": {"qkv_gemm_cublas": round(gemm_ms, 3), "prep": round(prep_ms, 3),
+                            "attention": round(att_ms, 3), "pack": round(pack_ms, 3),
+                            "step_with_launch_events": round(step_ms_events, 3)},
+            "qkv_gemm_tflops": round(gemm_flops / (gemm_ms * 1e-3) / 1e12, 1),
+            "configs1_image": history,
+            "dropin_image": dropin,
+        },
+        "roofline": {"bound": "tensor", "achieved": round(att_achieved, 1), "peak": sustained,
+                     "unit": "TFLOP/s", "frac": round(att_achieved / sustained, 4),
+                     "traffic": args.att_traffic or None,
+                     "traffic_launch": "target 12 (Lq 4096), scaled to the rows of one GPU",
+                     "peak_kind": f"bf16_tflops_sustained ({peak_src})",
+                     "frac_of_burst": round(att_achieved / burst, 4),
+                     "kernel": "attn_sm100_cs64_kernel", "launches_per_step": n_att,
+                     "ms_per_step": round(att_ms, 3), "ms_by_target": ms_by_target},
+        "roofline_pack": {"bound": "hbm", "peak": hbm, "unit": "GB/s",
+                          "achieved": round(pack_bytes / (pack_ms * 1e-3) / 1e9, 1),
+                          "frac": round(pack_bytes / (pack_ms * 1e-3) / 1e9 / hbm, 4),
+                          "kernel": "pack_kv_kernel / pack_kv_batched_kernel",
+                          "ms_per_step": round(pack_ms, 3),
+                          "gb_per_step": round(pack_bytes / 1e9, 3),
+                          "launches_per_step": sum(1 for l in launches if l.kind == "pack")},
+        "roofline_prep": {"bound": "hbm", "peak": hbm, "unit": "GB/s",
+                          "achieved": round(prep_bytes / (prep_ms * 1e-3) / 1e9, 1),
+                          "frac": round(prep_bytes / (prep_ms * 1e-3) / 1e9 / hbm, 4),
+                          "kernel": "qkv_prepare_kernel", "ms_per_step": round(prep_ms, 3),
+                          "gb_per_step": round(prep_bytes / 1e9, 3)},
+        "cpu_baseline": cpu_baseline_line(args, world),
+        "e2e": None if not e2e_steps else {
+            "value": round(job_att / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
+            "path": ("eager launches through the C ABI; layer inputs of every scale from pinned "
+                     "host memory, the last layer's attention outputs back to pinned host memory, "
+                     "copies on their own streams overlapping the compute")},
+        "clocks": clocks,
+        "gpu_launches": n_own * args.steps,
+        "device_status": int(status),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description="HeatKV hot-path benchmark")
     ap.add_argument("--gpus", type=int, default=1)
@@ -594,21 +957,37 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the host-memory leg (for configurations too large to pin on the host)")
+    ap.add_argument("--workload", choices=["c5", "c2"], default="c5",
+                    help="c5: configs[4] (64 rows, Q/K/V from the QKV projection); c2: configs[1] "
+                         "(one 2-row image of pre-generated Q/K/V)")
     ap.add_argument("--ref-targets", type=int, default=5,
-                    help="fused targets in the CPU sample (bounds the CPU time)")
-    ap.add_argument("--ref-layers", type=int, default=3,
-                    help="layers in the cpu_baseline sample of the GPU arm (about 4 s each)")
+                    help="fused targets per layer in the CPU sample (bounds the CPU time)")
+    ap.add_argument("--ref-layers", type=int, default=2,
+                    help="layers in the CPU sample (both arms)")
+    ap.add_argument("--attrib-steps", type=int, default=1,
+                    help="replays of the per-launch event graphs for the per-kernel figures")
+    ap.add_argument("--no-c2-history", action="store_true",
+                    help="skip the configs[1] timing kept beside the configs[4] line")
+    ap.add_argument("--no-dropin", action="store_true",
+                    help="skip the one-image timing through the public installer")
+    ap.add_argument("--att-traffic", type=float, default=0.0,
+                    help="DRAM bytes of one target-12 attention launch at this GPU's rows (ncu)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--shard", choices=["image", "auto", "rows", "heads"], default="image",
                     help="image: each GPU runs its own image (weak scaling); auto/rows/heads: "
                          "one batch of --global-rows rows sharded over the GPUs (strong scaling)")
-    ap.add_argument("--global-rows", type=int, default=2)
+    ap.add_argument("--global-rows", type=int, default=None,
+                    help="rows of the whole job (default 64 for c5, 2 for a sharded c2)")
     ap.add_argument("--exchange", choices=["nccl", "p2p"], default="p2p",
                     help="sharded modes: NCCL all-gather + reassembly, or the attention kernel "
                          "storing into every rank's output over NVLink + a peer barrier")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.global_rows is None:
+        args.global_rows = 64 if args.workload == "c5" else 2
+    if args.workload == "c5" and args.shard == "image":
+        args.shard = "auto"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -624,7 +1003,10 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_gpu(args, rank, world, local_rank)
+        if args.workload == "c5":
+            run_projected(args, rank, world, local_rank)
+        else:
+            run_gpu(args, rank, world, local_rank)
     finally:
         if world > 1:
             dist.destroy_process_group()

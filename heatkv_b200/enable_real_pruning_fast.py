@@ -8,11 +8,16 @@ Entry points (same names, arguments and errors as the reference):
   strict budget view (``budget.strict_removed_heads_by_scale_specific_for_budget``), build the
   controller and, per layer, the static slab schedule (``scheduler.build_static_slot_schedule``),
   then patch every self-attention module's ``forward`` and ``kv_caching``.
-* the patched ``forward`` (:1951-2254): dense scales run the module's own forward until a layer's
-  first target with removed heads; the end of the scale before it packs the retained segments of
-  the dense cache into the slab (activation, :2020-2037); every later scale runs the fused
-  segmented attention over the slab and appends its own K/V into its slab segments (:2218-2225);
-  the final scale frees the slab (:2176-2185).
+* the patched ``forward`` (:1951-2254): the scales before a layer's first target with removed
+  heads are dense. By default (``dense_prefix="kernel"``) they run through the same segmented
+  kernel as the pruned scales, over a dense cache ``[B, H * dense_len, D]`` allocated once per
+  layer (one segment per head: the cached tokens, then the current scale) into which each scale's
+  K/V are appended; ``dense_prefix="sdpa"`` keeps the reference's route (the module's own forward,
+  or SDPA over ``torch.cat`` of the cache and the scale, :2073-2121). The end of the scale before
+  the first pruned target packs the retained segments of the dense cache into the slab
+  (activation, :2020-2037); every later scale runs the fused segmented attention over the slab
+  and appends its own K/V into its slab segments (:2218-2225); the final scale frees the slab
+  (:2176-2185).
 * ``reset_/set_/snapshot_real_pruning_fast_phase_profile`` (:40-62) - CUDA-event phase timers for
   ``materialize``, ``attention`` and ``compact`` and the slab byte counters (:102-163).
 
@@ -180,37 +185,67 @@ class _LayerState:
                                                    num_heads=num_heads)
         self.capacity = int(self.schedule["capacity"])
         self.num_heads = int(num_heads)
+        ranges = controller.scale_ranges
+        num_scales = len(controller.scale_schedule)
+        # dense prefix: scales before the layer's first target with removed heads; their K/V
+        # live in a preallocated cache [B, H * dense_len, D] (head h at rows h * dense_len + ...)
+        # that holds every token before that target (or before the last scale)
+        self.first_target = next((t for t in range(1, num_scales)
+                                  if controller.any_removed(layer_idx, t)), num_scales)
+        self.dense_len = int(ranges[min(self.first_target, num_scales - 1)][0])
         self.device = None
         self.meta = {}
         self.old_pack = {}
         self.append = {}
         self.prep_append = {}
         self.plans = {}
+        self.dense_meta = {}
+
+    def dense_segments(self, old_len: int, device):
+        """``[H, 1]`` starts/ends and ``[H]`` counts of the dense-prefix attention after
+        ``old_len`` cached tokens: head h reads rows ``[h * dense_len, h * dense_len + old_len)``
+        of the dense cache (no segment when nothing is cached yet)."""
+        key = (int(old_len), device)
+        if key not in self.dense_meta:
+            H, ld = self.num_heads, max(self.dense_len, 1)
+            st = (torch.arange(H, dtype=torch.int32) * ld).reshape(H, 1)
+            ct = torch.full((H,), 1 if old_len > 0 else 0, dtype=torch.int32)
+            self.dense_meta[key] = (st.to(device), (st + int(old_len)).to(device), ct.to(device))
+        return self.dense_meta[key]
+
+    def dense_plan(self, old_len: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+        """``attention_plan`` of a dense-prefix call over ``old_len`` cached tokens per head."""
+        key = ("dense", old_len, q.shape[0], q.shape[2], q.dtype, k.dtype, v.dtype, q.device)
+        if key not in self.plans:
+            lens = [[int(old_len)] if old_len > 0 else [] for _ in range(self.num_heads)]
+            self.plans[key] = self._plan_for(lens, q, k, v)
+        return self.plans[key]
+
+    def _plan_for(self, lens, q, k, v):
+        dt = _native.DTYPE_CODES
+        run = _native.load().heatkv_attention_kernel_for(
+            dt[q.dtype], dt[k.dtype], dt[v.dtype], q.shape[0], q.shape[1], q.shape[2],
+            _kernel_selector(), 1, 0, 0)
+        if run not in (_native.RUN_TCGEN05_CS, _native.RUN_TCGEN05_TF32, _native.RUN_TCGEN05_CS64):
+            return None
+        cs64 = run == _native.RUN_TCGEN05_CS64
+        order, _, _, item_map, grid = plan_column_split(
+            lens, q.shape[2], q.shape[0], splits=1, sms=(2 if cs64 else 1) * NUM_SMS,
+            key_tile=64 if cs64 else 128)
+        return (torch.from_numpy(order).to(q.device), torch.from_numpy(item_map).to(q.device),
+                grid)
 
     def attention_plan(self, target: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
         """Launch schedule of this layer's fused attention at ``target`` for these tensors, planned
         once per (target, batch, dtypes) from the static segment tables: ``(head_order, item_map,
         grid)`` when the call runs the column-split kernel, else None."""
         key = (target, q.shape[0], q.dtype, k.dtype, v.dtype, q.device)
-        if key in self.plans:
-            return self.plans[key]
-        plan = None
-        dt = _native.DTYPE_CODES
-        run = _native.load().heatkv_attention_kernel_for(
-            dt[q.dtype], dt[k.dtype], dt[v.dtype], q.shape[0], q.shape[1], q.shape[2],
-            _kernel_selector(), 1, 0, 0)
-        if run in (_native.RUN_TCGEN05_CS, _native.RUN_TCGEN05_TF32, _native.RUN_TCGEN05_CS64):
+        if key not in self.plans:
             st, en, ct = self.schedule["metadata_cpu_by_target"][target]
             lens = [[int(en[h, i]) - int(st[h, i]) for i in range(int(ct[h]))]
                     for h in range(self.num_heads)]
-            cs64 = run == _native.RUN_TCGEN05_CS64
-            order, _, _, item_map, grid = plan_column_split(
-                lens, q.shape[2], q.shape[0], splits=1, sms=(2 if cs64 else 1) * NUM_SMS,
-                key_tile=64 if cs64 else 128)
-            plan = (torch.from_numpy(order).to(q.device), torch.from_numpy(item_map).to(q.device),
-                    grid)
-        self.plans[key] = plan
-        return plan
+            self.plans[key] = self._plan_for(lens, q, k, v)
+        return self.plans[key]
 
     def to(self, device: torch.device) -> None:
         if self.device == device:
@@ -299,6 +334,7 @@ def _reset_state(self) -> None:
     self._real_pruning_logical_len = 0
     self._heatkv_slab_k = None
     self._heatkv_slab_v = None
+    self._heatkv_dense_live = False
 
 
 def _activate_from_dense(self, dense_k, dense_v, target: int) -> None:
@@ -350,6 +386,37 @@ def _activate_from_dense_and_current(self, dense_k, dense_v, cur_k, cur_v, curre
 # ------------------------------------------------------------------------------------------------
 
 
+def _dense_prefix_mode(module) -> str:
+    """``"kernel"``: scales before a layer's first pruned target run the segmented kernel over a
+    preallocated dense cache (one segment per head); ``"sdpa"``: the reference's route (the
+    module's own forward, or SDPA over a concatenated cache). Installer keyword ``dense_prefix``;
+    ``HEATKV_DENSE_PREFIX`` overrides it."""
+    env = os.environ.get("HEATKV_DENSE_PREFIX")
+    if env in ("kernel", "sdpa"):
+        return env
+    return getattr(module, "_heatkv_dense_prefix", "kernel")
+
+
+def _ensure_dense(self, batch: int, head_dim: int, device, k_dtype, v_dtype):
+    """The layer's dense-prefix cache ``[B, H * dense_len, D]`` (kept across images)."""
+    ld = max(int(self._heatkv_layer.dense_len), 1)
+    shape = (batch, self.num_heads * ld, head_dim)
+    dk, dv = getattr(self, "_heatkv_dense_k", None), getattr(self, "_heatkv_dense_v", None)
+    if (dk is None or tuple(dk.shape) != shape or dk.device != device or dk.dtype != k_dtype
+            or dv.dtype != v_dtype):
+        dk = self._heatkv_dense_k = torch.empty(shape, device=device, dtype=k_dtype)
+        dv = self._heatkv_dense_v = torch.empty(shape, device=device, dtype=v_dtype)
+        _stat_add("dense_cache_allocations")
+    return dk, dv
+
+
+def _dense_append_desc(layer, old_len: int, n: int, device):
+    """Copy items of a scale's ``[B, H, n, D]`` K/V into the dense cache after ``old_len`` cached
+    tokens: head h's rows to ``h * dense_len + old_len``."""
+    ld = max(layer.dense_len, 1)
+    return _items_desc([(h * ld + old_len, h, 0, n) for h in range(layer.num_heads)], n, device)
+
+
 def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=None, attn_fn=None,
                                                scale_schedule=None, rope2d_freqs_grid=None,
                                                scale_ind=0):
@@ -361,13 +428,17 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
         raise NotImplementedError("real pruning fused segmented does not support custom attention functions")
     ctrl = self._real_pruning_scale_specific_controller
     layer = self.layer_idx
+    state = self._heatkv_layer
     batch_size, seq_len, channels = x.shape
     final_scale = self._num_scales == scale_ind + 1
     old_len = int(getattr(self, "_real_pruning_logical_len", 0))
     logical_len = old_len + seq_len
     active = bool(getattr(self, "_real_pruning_segmented_cache_active", False))
+    removed_now = ctrl.any_removed(layer, scale_ind)
+    dense_kernel = (_dense_prefix_mode(self) == "kernel" and x.is_cuda and
+                    self.head_dim == 128 and not active and not removed_now)
 
-    if not active and not ctrl.any_removed(layer, scale_ind) and _baseline_prefix_enabled():
+    if (not active and not removed_now and not dense_kernel and _baseline_prefix_enabled()):
         # dense scale: the module's own forward (SDPA over its cat cache)
         output = self._pre_real_prune_scale_specific_fast_forward(
             x, attn_bias_or_two_vector, attn_fn=attn_fn, scale_schedule=scale_schedule,
@@ -388,6 +459,10 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
         batch_size, seq_len, 3, self.num_heads, self.head_dim)
     if rope2d_freqs_grid is not None and scale_schedule is None:
         raise ValueError("scale_schedule is required when rope2d_freqs_grid is provided")
+    # the dense cache receives this scale (all heads) unless it is the last one or does not fit
+    dense_append = (dense_kernel and not final_scale
+                    and logical_len <= max(state.dense_len, 0))
+    early_dense = False
     if _fused_prep_applies(self, qkv):
         scale_mul = None
         if self.cos_attn:
@@ -397,18 +472,30 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
         if rope2d_freqs_grid is not None:
             rope = _qkv_prep.rope_rows(rope2d_freqs_grid, scale_schedule, scale_ind, seq_len,
                                        qkv.device)
-        early = None
+        dts = _qkv_prep.prepared_dtypes(qkv.dtype, cos_attention=scale_mul is not None,
+                                        rope=rope is not None)
+        early, append = None, None
         if active and not final_scale:
             early = self._heatkv_layer.prep_append.get(scale_ind)
-            dts = _qkv_prep.prepared_dtypes(qkv.dtype, cos_attention=scale_mul is not None,
-                                            rope=rope is not None)
             if early is not None and (self._heatkv_slab_k.dtype, self._heatkv_slab_v.dtype) != dts:
                 early = None
-        append = None if early is None else (self._heatkv_slab_k, self._heatkv_slab_v, early[0])
+            if early is not None:
+                append = (self._heatkv_slab_k, self._heatkv_slab_v, early[0])
+        elif dense_append:
+            # the preparation writes the scale straight into the dense cache (rows past the
+            # segments this scale's attention reads)
+            dk, dv = _ensure_dense(self, batch_size, self.head_dim, qkv.device, *dts)
+            ld = max(state.dense_len, 1)
+            offs = torch.arange(self.num_heads, dtype=torch.int64, device=qkv.device) * ld + old_len
+            append = (dk, dv, offs)
+            early_dense = True
         q, k, v = _qkv_prep.prepare_qkv(qkv, scale_mul=scale_mul, rope=rope, append=append)
         if early is not None:
             _stat_add("prep_append_calls")
             _record_kv_copy("prep_append", early[2], self._heatkv_slab_k, self._heatkv_slab_v)
+        if early_dense:
+            _stat_add("prep_dense_append_calls")
+            _record_kv_copy("prep_dense_append", self.num_heads * seq_len, dk, dv)
         del qkv
     else:
         early = None
@@ -427,9 +514,21 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
             q, k = _rope_fn(self)(q, k, scale_schedule, rope2d_freqs_grid, self.pad_to_multiplier,
                                   self.rope2d_normalized_by_hw, scale_ind)
 
-    removed_now = ctrl.any_removed(layer, scale_ind)
     dense_candidate = None
-    if old_len == 0:
+    if dense_kernel:
+        # dense-prefix scale through the segmented kernel: one segment per head over the cached
+        # tokens of the preallocated dense cache, then the current scale (the keys of the
+        # reference's SDPA over cat(cache, scale), in the same order)
+        with _Phase("materialize"):
+            dk, dv = _ensure_dense(self, batch_size, self.head_dim, k.device, k.dtype, v.dtype)
+            starts, ends, counts = state.dense_segments(old_len, k.device)
+        with _Phase("attention"):
+            output = fused_real_pruning_flat_segmented_attention(
+                q=q, persisted_k=dk, persisted_v=dv, segment_starts=starts, segment_ends=ends,
+                segment_counts=counts, current_k=k, current_v=v, softmax_scale=self.scale,
+                softmax_mode=_fused_softmax_mode(),
+                _schedule=state.dense_plan(old_len, q, k, v))
+    elif old_len == 0:
         with _Phase("attention"):
             output = slow_attn(query=q, key=k, value=v, scale=self.scale, dropout_p=0.0).transpose(
                 1, 2).reshape(batch_size, seq_len, channels)
@@ -444,7 +543,16 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
     else:
         with _Phase("materialize"):
             if not active:
-                _activate_from_dense(self, self.cached_k, self.cached_v, scale_ind)
+                if getattr(self, "_heatkv_dense_live", False):
+                    B_, _, D_ = self._heatkv_dense_k.shape
+                    ld = max(state.dense_len, 1)
+                    _activate_from_dense(
+                        self, self._heatkv_dense_k.view(B_, self.num_heads, ld, D_)[:, :, :old_len],
+                        self._heatkv_dense_v.view(B_, self.num_heads, ld, D_)[:, :, :old_len],
+                        scale_ind)
+                    self._heatkv_dense_live = False
+                else:
+                    _activate_from_dense(self, self.cached_k, self.cached_v, scale_ind)
                 self.cached_k = self.cached_v = None
                 active = True
             self._heatkv_layer.to(k.device)
@@ -462,6 +570,21 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
         if final_scale:
             _reset_state(self)
             self.cached_k = self.cached_v = None
+        elif dense_kernel:
+            dk, dv = self._heatkv_dense_k, self._heatkv_dense_v
+            if dense_append and not early_dense:
+                _pack(_dense_append_desc(state, old_len, seq_len, k.device), dk, dv, k, v,
+                      "dense_append_copy")
+            self._heatkv_dense_live = True
+            if ctrl.any_removed(layer, scale_ind + 1):
+                # activation: the dense cache holds exactly the tokens before the next scale
+                ld = max(state.dense_len, 1)
+                B_, _, D_ = dk.shape
+                _activate_from_dense(self, dk.view(B_, self.num_heads, ld, D_)[:, :, :logical_len],
+                                     dv.view(B_, self.num_heads, ld, D_)[:, :, :logical_len],
+                                     scale_ind + 1)
+                self._heatkv_dense_live = False
+            self._real_pruning_logical_len = logical_len
         else:
             removed_next = ctrl.any_removed(layer, scale_ind + 1)
             if not active and not removed_next:
@@ -513,9 +636,14 @@ def enable_real_pruning_scale_specific_fast(model, budget, scale_specific_remova
                                             attention_impl="fused_segmented",
                                             requested_generation_batch_size=None,
                                             attention_modules=None, scale_schedule=None,
-                                            fused_qkv_prep=False):
-    """Install HeatKV scale-specific pruning (enable_real_pruning_fast.py:2279-2378)."""
+                                            fused_qkv_prep=False, dense_prefix="kernel"):
+    """Install HeatKV scale-specific pruning (enable_real_pruning_fast.py:2279-2378).
+    ``dense_prefix``: ``"kernel"`` (default) runs the scales before each layer's first pruned
+    target through the segmented kernel over a preallocated dense cache; ``"sdpa"`` keeps the
+    reference's route for them (the module's own forward, or SDPA over a concatenated cache)."""
     merge_mode = _validate_merge_mode(merge_mode)
+    if dense_prefix not in ("kernel", "sdpa"):
+        raise ValueError("dense_prefix must be 'kernel' or 'sdpa'")
     if attention_impl != "fused_segmented":
         raise ValueError(f"unsupported real pruning fast attention_impl: {attention_impl!r}")
     modules = list(attention_modules) if attention_modules is not None else _attention_modules(model)
@@ -555,6 +683,7 @@ def enable_real_pruning_scale_specific_fast(model, budget, scale_specific_remova
             None if requested_generation_batch_size is None else int(requested_generation_batch_size))
         module._heatkv_layer = _LayerState(controller, module.layer_idx, num_heads)
         module._heatkv_fused_qkv_prep = bool(fused_qkv_prep)
+        module._heatkv_dense_prefix = dense_prefix
         module._real_pruning_segmented_static_schedule = module._heatkv_layer.schedule
         try:
             device = next(module.parameters()).device
@@ -579,7 +708,8 @@ def enable_real_pruning_scale_specific_fused_segmented(model, budget, scale_spec
                                                        skip_last_scale=True, merge_mode="exact",
                                                        requested_generation_batch_size=None,
                                                        attention_modules=None,
-                                                       scale_schedule=None, fused_qkv_prep=False):
+                                                       scale_schedule=None, fused_qkv_prep=False,
+                                                       dense_prefix="kernel"):
     """Alias of the installer with ``attention_impl='fused_segmented'`` (:2381-2402)."""
     return enable_real_pruning_scale_specific_fast(
         model, budget, scale_specific_removal_orders,
@@ -587,4 +717,4 @@ def enable_real_pruning_scale_specific_fused_segmented(model, budget, scale_spec
         skip_last_scale=skip_last_scale, merge_mode=merge_mode, attention_impl="fused_segmented",
         requested_generation_batch_size=requested_generation_batch_size,
         attention_modules=attention_modules, scale_schedule=scale_schedule,
-        fused_qkv_prep=fused_qkv_prep)
+        fused_qkv_prep=fused_qkv_prep, dense_prefix=dense_prefix)

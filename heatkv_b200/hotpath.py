@@ -409,11 +409,6 @@ class HotPath:
         ends with the scale (``HEATKV_ATTN_CURRENT_IN_SEGMENTS``)."""
         B, H, D = self.batch, self.num_heads, self.head_dim
         scale = float(softmax_scale) if softmax_scale is not None else D ** -0.5
-        lib = self.lib
-        # the segment metadata and head orders were uploaded at construction and no launch of
-        # the step writes them: the attention kernel may stage them before its dependency wait
-        meta_kernel = int(kernel) | _native.ATTN_STATIC_META
-        dt = _native.DTYPE_CODES
         out = []
         for t in range(self.num_scales):
             n = self.tokens[t]
@@ -424,33 +419,8 @@ class HotPath:
                 o = outputs[i][t]
                 dense = t < p.first_target
                 cur_in = dense and self.dense_append_first and t in p.dense_meta_cur
-                sel = meta_kernel | (_native.ATTN_CURRENT_IN_SEGMENTS if cur_in else 0)
-                if dense:
-                    st, en, ct, _ = p.dense_meta_cur[t] if cur_in else p.dense_meta[t]
-                    sk, sv = self.dense_k[i], self.dense_v[i]
-                    cap = H * max(p.dense_len, 1)
-                else:
-                    st, en, ct, _ = p.slab_meta[t]
-                    sk, sv = self.slab_k[i], self.slab_v[i]
-                    cap = max(p.capacity, 1)
-                flops = float(4 * n * (p.attention_slots(t) + n).sum() * D * B)
-                order, splits, unsplit, imap = self.schedule[(i, t)]
-                head = (_native.ptr(q), _native.ptr(sk), _native.ptr(sv), _native.ptr(st),
-                        _native.ptr(en), _native.ptr(ct), _native.ptr(k), _native.ptr(v),
-                        _native.ptr(o), dt[q.dtype], dt[k.dtype], dt[v.dtype], B, H, n, cap, D,
-                        int(st.shape[1]), ctypes.c_float(scale), sel, _native.ptr(order),
-                        int(splits), int(unsplit))
-                ws = (_native.ptr(self.workspace), self.workspace.numel())
-                if imap is not None:
-                    launch = Launch("attention", p.layer, t, lib.heatkv_segmented_attention_mapped,
-                                    head + (_native.ptr(imap[0]), imap[0].numel(), imap[1]) + ws,
-                                    flops)
-                else:
-                    launch = Launch("attention", p.layer, t, lib.heatkv_segmented_attention_sched,
-                                    head + ws, flops)
-                if cur_in:
-                    st0, en0, ct0, _ = p.dense_meta[t]
-                    launch.unflagged_meta = (_native.ptr(st0), _native.ptr(en0), _native.ptr(ct0))
+                launch = self.attention_launch(i, t, q, k, v, o, kernel=kernel,
+                                               softmax_scale=scale)
                 row_k = D * k.element_size()
                 row_v = D * v.element_size()
                 jobs = []
@@ -492,6 +462,51 @@ class HotPath:
                 if group:
                     out.append(self._pack_batched(t, group))
         return out
+
+    def attention_launch(self, i: int, t: int, q, k, v, o, *, kernel: int = _native.ATTN_AUTO,
+                         softmax_scale: Optional[float] = None) -> Launch:
+        """The attention launch of plan ``i`` at target ``t`` (current ``q, k, v`` ``[B, H, n_t,
+        D]``, output ``o`` ``[B, n_t, H * D]``): over the dense cache before the layer's first
+        pruned target (one segment per head, already ending with the current scale when
+        ``dense_append_first``), over the slab after it."""
+        p = self.plans[i]
+        B, H, D = self.batch, self.num_heads, self.head_dim
+        n = self.tokens[t]
+        scale = float(softmax_scale) if softmax_scale is not None else D ** -0.5
+        dt = _native.DTYPE_CODES
+        dense = t < p.first_target
+        cur_in = dense and self.dense_append_first and t in p.dense_meta_cur
+        # the segment metadata and head orders were uploaded at construction and no launch of
+        # the step writes them: the attention kernel may stage them before its dependency wait
+        sel = (int(kernel) | _native.ATTN_STATIC_META
+               | (_native.ATTN_CURRENT_IN_SEGMENTS if cur_in else 0))
+        if dense:
+            st, en, ct, _ = p.dense_meta_cur[t] if cur_in else p.dense_meta[t]
+            sk, sv = self.dense_k[i], self.dense_v[i]
+            cap = H * max(p.dense_len, 1)
+        else:
+            st, en, ct, _ = p.slab_meta[t]
+            sk, sv = self.slab_k[i], self.slab_v[i]
+            cap = max(p.capacity, 1)
+        flops = float(4 * n * (p.attention_slots(t) + n).sum() * D * B)
+        order, splits, unsplit, imap = self.schedule[(i, t)]
+        head = (_native.ptr(q), _native.ptr(sk), _native.ptr(sv), _native.ptr(st),
+                _native.ptr(en), _native.ptr(ct), _native.ptr(k), _native.ptr(v),
+                _native.ptr(o), dt[q.dtype], dt[k.dtype], dt[v.dtype], B, H, n, cap, D,
+                int(st.shape[1]), ctypes.c_float(scale), sel, _native.ptr(order),
+                int(splits), int(unsplit))
+        ws = (_native.ptr(self.workspace), self.workspace.numel())
+        lib = self.lib
+        if imap is not None:
+            launch = Launch("attention", p.layer, t, lib.heatkv_segmented_attention_mapped,
+                            head + (_native.ptr(imap[0]), imap[0].numel(), imap[1]) + ws, flops)
+        else:
+            launch = Launch("attention", p.layer, t, lib.heatkv_segmented_attention_sched,
+                            head + ws, flops)
+        if cur_in:
+            st0, en0, ct0, _ = p.dense_meta[t]
+            launch.unflagged_meta = (_native.ptr(st0), _native.ptr(en0), _native.ptr(ct0))
+        return launch
 
     def _pack_batched(self, t, jobs):
         """One batched pack launch for ``jobs`` (tuples as ``_pack`` takes them)."""

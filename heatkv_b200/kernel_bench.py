@@ -13,6 +13,9 @@ one ``heatkv_pack_kv_batched`` launch, as the pre-planned step issues a scale's 
 probabilities it avoids.
 ``qkv-prep``: one layer's q/k/v preparation (``heatkv_qkv_prepare``: cos-attention + RoPE under
 autocast) against the PyTorch chain it replaces.
+``projected-step``: the whole projection-driven step of ``bench.py``'s default workload
+(``heatkv_b200.projected``: 2B, 10 % budget, every layer and scale) for ``--rows`` rows, run
+eagerly ``--iters`` times after ``--warmup`` (for ncu launch lists of exactly one step).
 Prints per-call device time (CUDA events, warm, back to back) and the achieved TFLOP/s or GB/s.
 """
 
@@ -73,7 +76,8 @@ def time_call(fn, iters, warmup=3):
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("kernel", choices=["attention", "pack", "pack-batched", "qkv-prep", "scas"])
+    ap.add_argument("kernel", choices=["attention", "pack", "pack-batched", "qkv-prep", "scas",
+                                       "projected-step"])
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--rows", type=int, default=2)
     ap.add_argument("--heads", type=int, default=16)
@@ -86,7 +90,34 @@ def main(argv=None):
     args = ap.parse_args(argv)
     dtype = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32,
              "f32qk": torch.float32}[args.dtype]
-    if args.kernel == "attention":
+    if args.kernel == "projected-step":
+        import os
+        import sys
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        import bench
+        from .hotpath import HotPath
+        from .projected import ProjectedHotPath
+        ctrl, layers, heads = bench.build_controller("2b", 0.10)
+        hot = HotPath(ctrl, layers, heads, args.rows, torch.device("cuda"))
+        proj = ProjectedHotPath(hot)
+        x, _ = proj.allocate_inputs(list(range(args.rows)), seed=1)
+        out, _ = proj.allocate_outputs()
+        launches = proj.launches(x, out)
+        stream = torch.cuda.current_stream()
+        for _ in range(args.warmup):
+            proj.run(launches, stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.iters):
+            proj.run(launches, stream)
+        e1.record()
+        e1.synchronize()
+        att = sum(l.work for l in launches if l.kind == "attention")
+        ms = e0.elapsed_time(e1) / args.iters
+        print(f"projected step rows={args.rows}: {len(launches)} launches, {ms:.2f} ms/step, "
+              f"attention {att / ms / 1e9:.1f} TFLOP/s over the step", flush=True)
+    elif args.kernel == "attention":
         vdtype = torch.bfloat16 if args.dtype == "f32qk" else dtype
         kw, flops = attention_case(args.rows, args.heads, args.q_len, args.slots, dtype,
                                    vdtype=vdtype)

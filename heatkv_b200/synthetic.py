@@ -186,3 +186,76 @@ def attention_case_inputs(case: AttentionCase) -> dict:
         "segment_counts": torch.from_numpy(counts), "current_k": k, "current_v": v,
         "softmax_scale": 1.0 / math.sqrt(HEAD_DIM),
     }
+
+
+# ------------------------------------------------------------------------------------------------
+# Config 5: Q/K/V generated by random-init Infinity-2B QKV projections.
+# ------------------------------------------------------------------------------------------------
+
+
+def rope2d_rows(schedule=SCALE_SCHEDULE_1M, *, head_dim: int = HEAD_DIM,
+                normalized_by_hw: int = 2, max_side: int = 2048 // 16, base: float = 10000.0,
+                pad_to_multiplier: int = 128):
+    """``(cos, sin)`` fp32 ``[padded_tokens, head_dim / 2]``: the 2-D rotary table Infinity builds
+    for a square schedule (``precompute_rope2d_freqs_grid``, infinity/models/basic.py:39-94, with
+    the inference defaults ``rope2d_normalized_by_hw=2`` and ``pad_to_multiplier=128`` of
+    tools/run_infinity.py:248, :469). Row ``i`` of a scale ``(1, ph, pw)`` holds the height angles
+    ``y * theta_j`` then the width angles ``x * theta_j`` (``theta_j = base^(-2j / (head_dim /
+    2))``), where ``(y, x)`` is the token's grid position mapped onto the last scale's grid
+    (``round(i * last / ph)``, mode 2) or taken as is (mode 0)."""
+    half = head_dim // 2
+    inv_freq = 1.0 / (base ** (torch.arange(0, half, 2, dtype=torch.int64).float() / half))
+    pos = torch.arange(max_side, dtype=torch.int64).type_as(inv_freq)
+    f_h = torch.outer(pos, inv_freq)
+    f_w = torch.outer(pos, inv_freq)
+    grid = torch.cat([f_h[:, None, :].expand(-1, max_side, -1),
+                      f_w[None, :, :].expand(max_side, -1, -1)], dim=-1)
+    grid = torch.stack([torch.cos(grid), torch.sin(grid)], dim=0)    # [2, side, side, half]
+    _, last_h, last_w = schedule[-1]
+    parts = []
+    for _, ph, pw in schedule:
+        if normalized_by_hw == 2:
+            idx = torch.stack([
+                (torch.arange(ph) * (last_h / ph)).reshape(ph, 1).expand(ph, pw),
+                (torch.arange(pw) * (last_w / pw)).reshape(1, pw).expand(ph, pw)],
+                dim=-1).round().int().reshape(-1, 2)
+            part = grid[:, idx[:, 0], idx[:, 1], :]
+        elif normalized_by_hw == 0:
+            part = grid[:, :ph, :pw, :].reshape(2, ph * pw, half)
+        else:
+            raise ValueError("normalized_by_hw must be 0 or 2")
+        parts.append(part.reshape(2, ph * pw, half))
+    table = torch.cat(parts, dim=1)
+    if pad_to_multiplier > 1 and table.shape[1] % pad_to_multiplier:
+        pad = pad_to_multiplier - table.shape[1] % pad_to_multiplier
+        table = torch.cat([table, torch.zeros(2, pad, half)], dim=1)
+    return table[0].contiguous(), table[1].contiguous()
+
+
+def qkv_weight(layer: int, embed_dim: int, *, seed: int = 0, std: float = 0.02,
+               dtype=torch.bfloat16, device="cpu") -> torch.Tensor:
+    """Random-init ``mat_qkv.weight`` ``[3 * embed_dim, embed_dim]`` ~ N(0, std) of one layer (the
+    ``nn.Linear`` layout: the projection is ``x @ W^T``), drawn from ``seed`` and the layer index on
+    ``device``'s generator."""
+    gen = torch.Generator(device=device).manual_seed(seed * 1000003 + layer)
+    w = torch.empty(3 * embed_dim, embed_dim, dtype=torch.float32, device=device)
+    w.normal_(0.0, std, generator=gen)
+    return w.to(dtype)
+
+
+COS_ATTN_SCALE_MUL = 4.0   # exp(log(4)): the init value of scale_mul_1H11 (basic.py:216-221)
+
+
+def scas_inputs(prompt: int, layer: int, schedule, *, heads: int = 16):
+    """Seeded cos-attention-like q, k of every scale for one (prompt, layer) of an S-CAS capture:
+    q = normalize(x) * 4, k = normalize(y), each ``[2, heads, n_s, 128]`` fp32 (row 1 plays the CFG
+    row; the accumulator reads row 0 only), from the CPU generator."""
+    gen = torch.Generator().manual_seed(10007 * prompt + 101 * layer + 5)
+    out = []
+    for _, h, w in schedule:
+        q = torch.nn.functional.normalize(torch.randn(2, heads, h * w, HEAD_DIM, generator=gen),
+                                          dim=-1) * 4.0
+        k = torch.nn.functional.normalize(torch.randn(2, heads, h * w, HEAD_DIM, generator=gen),
+                                          dim=-1)
+        out.append((q, k))
+    return out

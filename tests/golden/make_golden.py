@@ -22,6 +22,9 @@ What it records (every value comes from the reference's own Python functions):
   seeded cases, including empty segments, zero-count heads and an empty slab.
 * ``attention_c1.npz`` - per fused call of the config-1 pipeline: the reference oracle's
   output checksums plus its first rows verbatim.
+* ``scas_c1.npz`` - the reference's S-CAS ``ScasAccumulator`` (tools/compute_scas.py:92-152) on
+  the 7-scale schedule, fed the capture forward's fp32 probabilities of seeded cos-attention-like
+  q/k (``synthetic.scas_inputs``): ``accum``, ``scores`` and ``orders``.
 
 Inputs are generated with ``heatkv_b200.synthetic`` so the tests regenerate the identical tensors.
 """
@@ -315,14 +318,52 @@ def make_attention_cases(rpfa) -> None:
     print(f"attention cases: {sorted(arrays)}")
 
 
+# --------------------------------------------------------------------------------------------
+# S-CAS accumulation (tools/compute_scas.py:92-152)
+# --------------------------------------------------------------------------------------------
+
+SCAS_LAYERS, SCAS_HEADS, SCAS_SINK, SCAS_PROMPTS = 2, 16, 3, 2
+
+
+def make_scas(reference_path: str) -> None:
+    """The reference's ScasAccumulator fed, per (prompt, layer, scale), the probabilities of its
+    capture forward (softmax of q k^T in fp32 over every key so far, :217-218): accum, scores and
+    orders on the 7-scale schedule."""
+    import tools  # type: ignore  (the reference's package; run_infinity is not needed here)
+
+    stub = types.ModuleType("tools.run_infinity")
+    sys.modules.setdefault("tools.run_infinity", stub)
+    tools.run_infinity = sys.modules["tools.run_infinity"]
+    from tools import compute_scas  # type: ignore
+
+    schedule = list(synthetic.C1_SCALE_SCHEDULE)
+    acc = compute_scas.ScasAccumulator(num_layers=SCAS_LAYERS, num_heads=SCAS_HEADS,
+                                       scale_schedule=schedule, sink_scales=SCAS_SINK,
+                                       device=torch.device("cpu"))
+    for prompt in range(SCAS_PROMPTS):
+        for layer in range(SCAS_LAYERS):
+            qk = synthetic.scas_inputs(prompt, layer, schedule, heads=SCAS_HEADS)
+            for t in range(len(schedule)):
+                q = qk[t][0]
+                k = torch.cat([qk[s][1] for s in range(t + 1)], dim=2)
+                probs = torch.softmax(torch.matmul(q.float(), k.float().transpose(-2, -1)) * 1.0,
+                                      dim=-1)
+                acc.update(layer_idx=layer, scale_ind=t, probs=probs)
+    scores = acc.scores(SCAS_PROMPTS)
+    orders = acc.orders_from_scores(scores)
+    np.savez_compressed(os.path.join(HERE, "scas_c1.npz"), accum=acc.accum.numpy(),
+                        scores=scores.numpy(), orders=np.array(orders, dtype=np.int16))
+    print(f"scas: accum {tuple(acc.accum.shape)}, {len(orders)} orders")
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     parser.add_argument("--reference", required=True, help="path of the reference checkout")
-    parser.add_argument("--only", default=None, help="comma list: budget,c1,attention")
+    parser.add_argument("--only", default=None, help="comma list: budget,c1,attention,scas")
     args = parser.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     erpf, ep, rpfa, utils = _load_reference(args.reference)
-    only = set(args.only.split(",")) if args.only else {"budget", "c1", "attention"}
+    only = set(args.only.split(",")) if args.only else {"budget", "c1", "attention", "scas"}
     if "budget" in only:
         for name in BUDGET_CONFIGS:
             make_budget_and_schedule(erpf, ep, utils, name)
@@ -330,6 +371,8 @@ def main() -> None:
         make_config1(erpf, ep, rpfa)
     if "attention" in only:
         make_attention_cases(rpfa)
+    if "scas" in only:
+        make_scas(args.reference)
 
 
 if __name__ == "__main__":

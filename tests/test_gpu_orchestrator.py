@@ -2,8 +2,11 @@
 ``enable_real_pruning_scale_specific_fused_segmented`` every layer's output at every one of the 13
 scales equals attention over exactly the tokens the keep-mask retains (plain PyTorch fp32 on the
 GPU), through the model's own projections. bf16 model (tcgen05 kernel, 2e-2 / 1e-2), fp32
-cos-attn model (exact kernel, 1e-4), and fp32 cos-attn model under bf16 autocast, the real
-model's setting: q and k fp32, v bf16 (tf32 tcgen05 kernel, 2e-2 / 1e-2)."""
+cos-attn model (exact kernel; the attention output itself, the output projection set to the
+identity, at 1e-5), and fp32 cos-attn model under bf16 autocast, the real model's setting: q and
+k fp32, v bf16 (tf32 tcgen05 kernel, 2e-2 / 1e-2). The scales before a layer's first pruned target
+run through the segmented kernel over a preallocated dense cache by default, and through the
+reference's SDPA route with ``dense_prefix="sdpa"``; both are checked."""
 
 import contextlib
 
@@ -116,23 +119,32 @@ def _masked_reference(module, ctrl, layer, xs, t, autocast=False):
             idx = torch.cat(idx).to(q.device)
             att = torch.softmax((q[:, h] @ k[:, h, idx].transpose(-1, -2)) * module.scale, -1)
             out[:, :, h] = att @ v[:, h, idx]
-        return module.proj(out.reshape(B, n, H * D).to(module.proj.weight.dtype)).float()
+        out = out.reshape(B, n, H * D)
+        if isinstance(module.proj, nn.Linear):
+            out = module.proj(out.to(module.proj.weight.dtype))
+        return out.float()
 
 
+@pytest.mark.parametrize("dense_prefix", ["kernel", "sdpa"])
 @pytest.mark.parametrize("dtype,cos_attn,autocast,atol,rel", [
     (torch.bfloat16, False, False, 2e-2, 1e-2),
-    (torch.float32, True, False, 1e-4, 1e-4),
+    (torch.float32, True, False, 1e-5, 1e-5),
     (torch.float32, True, True, 2e-2, 1e-2),
 ])
-def test_installed_model_matches_keep_mask_attention(dtype, cos_attn, autocast, atol, rel):
+def test_installed_model_matches_keep_mask_attention(dtype, cos_attn, autocast, atol, rel,
+                                                     dense_prefix):
     torch.backends.cuda.matmul.allow_tf32 = False
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
     L, H, C = 3, 16, 2048
     model = nn.ModuleList([SelfAttention(C, H, cos_attn) for _ in range(L)]).to(dev, dtype)
+    if dtype == torch.float32 and not autocast:
+        for m in model:   # compare the attention output itself at the fp32 tolerance
+            m.proj = nn.Identity()
     orders = synthetic.random_removal_orders(L, H, seed=7)
     enable_real_pruning_scale_specific_fused_segmented(
-        model, 0.10, orders, protected_prefix_scales=3, source_scale_start=3)
+        model, 0.10, orders, protected_prefix_scales=3, source_scale_start=3,
+        dense_prefix=dense_prefix)
     ctrl = model[0]._real_pruning_scale_specific_controller
     for m in model:
         m.kv_caching(True)
@@ -286,3 +298,68 @@ def test_planned_schedule_is_bit_identical(dtype, autocast):
             _LayerState.attention_plan = original
     assert _native.device_status(dev) == 0
     assert all(torch.equal(a, b) for a, b in zip(*runs))
+
+
+@pytest.mark.parametrize("dtype,autocast,fused", [(torch.bfloat16, False, False),
+                                                  (torch.float32, True, False),
+                                                  (torch.float32, True, True)])
+def test_dense_prefix_kernel_route_matches_sdpa_route(dtype, autocast, fused):
+    """The dense-prefix scales through the segmented kernel (default) against the reference's SDPA
+    route: outputs of the dense scales agree within the bf16 tolerance. Without the fused
+    preparation both routes compute and cache the same K/V, so every slab segment after the
+    activation and every output of the pruned scales is bit-identical; with it (the SDPA route's
+    dense scales run the module's own forward, whose q/k normalisation rounds differently)
+    those agree within the tolerance too."""
+    dev = torch.device("cuda", 0)
+    L, H, C = 2, 16, 2048
+    schedule = synthetic.SCALE_SCHEDULE_1M
+    n_tok = sum(a * b * c for a, b, c in schedule)
+    g = torch.Generator().manual_seed(4)
+    angles = torch.rand(1, 1, 1, n_tok, 64, generator=g) * 6.0
+    freqs = {str(tuple(schedule)): torch.stack([torch.cos(angles), torch.sin(angles)]).to(dev)}
+    if not autocast:
+        freqs = None   # the fp32 rope cache would promote q/k of a bf16 model to fp32
+    orders = synthetic.random_removal_orders(L, H, seed=21)
+    xs = [[torch.randn(2, h * w, C, device=dev, dtype=dtype) for _, h, w in schedule]
+          for _ in range(L)]
+    runs = []
+    for route in ("kernel", "sdpa"):
+        torch.manual_seed(0)
+        model = nn.ModuleList([SelfAttention(C, H, True) for _ in range(L)]).to(dev, dtype)
+        enable_real_pruning_scale_specific_fused_segmented(
+            model, 0.10, orders, protected_prefix_scales=3, source_scale_start=3,
+            fused_qkv_prep=fused, dense_prefix=route)
+        for m in model:
+            m.kv_caching(True)
+        outs, slabs = [], []
+        with torch.no_grad(), _autocast(autocast):
+            for t in range(len(schedule)):
+                for l, m in enumerate(model):
+                    dense = not m._real_pruning_segmented_cache_active
+                    outs.append((l, t, dense, m(xs[l][t], None, scale_schedule=schedule,
+                                                rope2d_freqs_grid=freqs, scale_ind=t)))
+                    if m._real_pruning_segmented_cache_active and t + 1 < len(schedule):
+                        for seg in m._heatkv_layer.schedule["segments_by_target"][t + 1]:
+                            lo, hi = seg["offset"], seg["offset"] + seg["length"]
+                            slabs.append((l, t, m._heatkv_slab_k[:, lo:hi].clone(),
+                                          m._heatkv_slab_v[:, lo:hi].clone()))
+        runs.append((outs, slabs))
+    assert _native.device_status(dev) == 0
+    (oa, sa), (ob, sb) = runs
+    assert any(d for _, _, d, _ in oa) and not all(d for _, _, d, _ in oa)
+    def close(a, b):
+        err = (a.float() - b.float()).abs().max().item()
+        return err <= 2e-2 and err <= 1e-2 * max(b.float().abs().max().item(), 1e-6)
+
+    for (l, t, dense, a), (_, _, dense_b, b) in zip(oa, ob):
+        assert dense == dense_b
+        if dense or fused:
+            assert close(a, b), (l, t)
+        else:
+            assert torch.equal(a, b), (l, t)
+    assert len(sa) == len(sb) > 0
+    for a, b in zip(sa, sb):
+        if fused:
+            assert close(a[2], b[2]) and close(a[3], b[3]), a[:2]
+        else:
+            assert torch.equal(a[2], b[2]) and torch.equal(a[3], b[3]), a[:2]

@@ -73,3 +73,29 @@ def test_sources_missing_from_the_keys_are_skipped():
                           device=dev)
     ref.update(layer_idx=0, scale_ind=3, probs=_probs(q, k, 0.1))
     np.testing.assert_allclose(acc.accum.cpu().numpy(), ref.accum.cpu().numpy(), rtol=1e-5)
+
+
+def test_update_from_qk_matches_the_reference_fixture(golden_dir):
+    """``update_from_qk`` on the GPU against the reference's own ScasAccumulator
+    (tests/golden/scas_c1.npz, recorded from tools/compute_scas.py:92-152 on the capture
+    forward's fp32 probabilities of the same seeded q/k): accum within 1e-5 relative, the removal
+    orders identical."""
+    import os
+    fx = np.load(os.path.join(golden_dir, "scas_c1.npz"))
+    dev = torch.device("cuda", 0)
+    sched = list(synthetic.C1_SCALE_SCHEDULE)
+    acc = ScasAccumulator(num_layers=2, num_heads=16, scale_schedule=sched, sink_scales=3,
+                          device=dev)
+    for prompt in range(2):
+        for layer in range(2):
+            qk = synthetic.scas_inputs(prompt, layer, sched, heads=16)
+            for t in range(len(sched)):
+                k = torch.cat([qk[s][1] for s in range(t + 1)], dim=2).to(dev)
+                acc.update_from_qk(layer_idx=layer, scale_ind=t, q=qk[t][0].to(dev), k=k,
+                                   scale=1.0)
+    torch.cuda.synchronize()
+    assert np.abs(fx["accum"]).max() > 0
+    np.testing.assert_allclose(acc.accum.cpu().numpy(), fx["accum"], rtol=1e-5, atol=1e-9)
+    orders = np.array(acc.orders_from_scores(acc.scores(2)), dtype=np.int16)
+    assert np.array_equal(orders, fx["orders"])
+    assert _native.device_status(dev) == 0

@@ -47,3 +47,41 @@ def test_update_scores_and_orders_on_cpu_probabilities():
     tie = torch.zeros_like(sc)
     assert acc.orders_from_scores(tie)[0] == [(0, 0), (0, 1), (1, 0), (1, 1), (2, 0), (2, 1)]
     assert not math.isnan(float(sc[0, 0, 1]))
+
+
+def _replay_fixture_inputs(acc, update):
+    from heatkv_b200 import synthetic
+    sched = list(synthetic.C1_SCALE_SCHEDULE)
+    for prompt in range(2):
+        for layer in range(2):
+            qk = synthetic.scas_inputs(prompt, layer, sched, heads=16)
+            for t in range(len(sched)):
+                q = qk[t][0]
+                k = torch.cat([qk[s][1] for s in range(t + 1)], dim=2)
+                update(acc, layer, t, q, k)
+
+
+def test_probability_update_matches_the_reference_fixture(golden_dir):
+    """``update`` from the capture forward's fp32 probabilities against the reference's own
+    ScasAccumulator (tests/golden/scas_c1.npz): accum and scores within 1e-12 relative, orders
+    identical."""
+    import os
+
+    import numpy as np
+
+    from heatkv_b200 import synthetic
+    fx = np.load(os.path.join(golden_dir, "scas_c1.npz"))
+    acc = ScasAccumulator(num_layers=2, num_heads=16, scale_schedule=list(synthetic.C1_SCALE_SCHEDULE),
+                          sink_scales=3, device="cpu")
+
+    def update(a, layer, t, q, k):
+        probs = torch.softmax(torch.matmul(q.float(), k.float().transpose(-2, -1)), dim=-1)
+        a.update(layer_idx=layer, scale_ind=t, probs=probs)
+
+    _replay_fixture_inputs(acc, update)
+    assert np.allclose(acc.accum.numpy(), fx["accum"], rtol=1e-12, atol=0)
+    sc = acc.scores(2).numpy()
+    assert np.array_equal(np.isnan(sc), np.isnan(fx["scores"]))
+    assert np.allclose(np.nan_to_num(sc), np.nan_to_num(fx["scores"]), rtol=1e-12, atol=0)
+    assert np.array_equal(np.array(acc.orders_from_scores(acc.scores(2)), dtype=np.int16),
+                          fx["orders"])
