@@ -779,16 +779,17 @@ def run_projected(args, rank: int, world: int, local_rank: int) -> None:
                          "over the GPUs")
     rows = plan.rows_per_rank
     hot = HotPath(ctrl, layers, heads, rows, dev, torch.bfloat16, torch.bfloat16)
-    proj = ProjectedHotPath(hot, weight_seed=0)
+    proj = ProjectedHotPath(hot, weight_seed=0, fused_projection=not args.unfused_projection)
     x, x_flat = proj.allocate_inputs(plan.rows_of(rank), seed=1)
     out, out_flat = proj.allocate_outputs()
     launches = proj.launches(x, out)
     att_flops = sum(l.work for l in launches if l.kind == "attention")
-    gemm_flops = sum(l.work for l in launches if l.kind == "gemm")
+    gemm_flops = sum(l.work for l in launches if l.kind in ("gemm", "proj"))
     pack_bytes = sum(l.work for l in launches if l.kind == "pack")
     prep_bytes = sum(l.work for l in launches if l.kind == "prep")
+    proj_bytes = sum(l.nbytes for l in launches if l.kind == "proj")
     n_att = sum(1 for l in launches if l.kind == "attention")
-    n_own = sum(1 for l in launches if l.kind in ("attention", "pack", "prep"))
+    n_own = sum(1 for l in launches if l.kind in ("attention", "pack", "prep", "proj"))
 
     stream = torch.cuda.Stream(dev)
     stream.wait_stream(torch.cuda.current_stream(dev))
@@ -803,7 +804,7 @@ def run_projected(args, rank: int, world: int, local_rank: int) -> None:
     step_ms, clocks = _timed_replays(step_graph, args.steps, stream, dev, world, local_rank)
     if world > 1:
         dist.barrier()
-    kinds = ("gemm", "prep", "attention", "pack")
+    kinds = ("proj", "gemm", "prep", "attention", "pack")
     by_kind, by_target, step_ms_events = _attribution(proj, launches, stream,
                                                       max(1, args.attrib_steps), kinds)
     status = _native.device_status(dev)
@@ -871,10 +872,11 @@ def run_projected(args, rank: int, world: int, local_rank: int) -> None:
     d2h = out_flat.numel() * out_flat.element_size()
 
     vals = torch.tensor([step_ms, e2e_ms, by_kind["attention"], by_kind["pack"], by_kind["prep"],
-                         by_kind["gemm"], float(status)], dtype=torch.float64, device=dev)
+                         by_kind["gemm"], by_kind["proj"], float(status)], dtype=torch.float64,
+                        device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    step_ms, e2e_ms, att_ms, pack_ms, prep_ms, gemm_ms, status = vals.tolist()
+    step_ms, e2e_ms, att_ms, pack_ms, prep_ms, gemm_ms, proj_ms, status = vals.tolist()
     del step_graph
     torch.cuda.synchronize(dev)
     if rank != 0:
@@ -904,10 +906,14 @@ def run_projected(args, rank: int, world: int, local_rank: int) -> None:
             "slab_gb_per_gpu": round(hot.slab_bytes() / 1e9, 3),
             "early_append_slots_per_row": proj.early_slots,
             "pack_append_slots_per_row": proj.rest_slots,
-            "ms_by_stage": {"qkv_gemm_cublas": round(gemm_ms, 3), "prep": round(prep_ms, 3),
+            "qkv": ("fused: heatkv_qkv_project (tcgen05 projection, preparation and early "
+                    "appends in its epilogue)" if proj.fused_projection else
+                    "unfused: cuBLAS GEMM + heatkv_qkv_prepare_append"),
+            "ms_by_stage": {"qkv_project_fused": round(proj_ms, 3),
+                            "qkv_gemm_cublas": round(gemm_ms, 3), "prep": round(prep_ms, 3),
                             "attention": round(att_ms, 3), "pack": round(pack_ms, 3),
                             "step_with_launch_events": round(step_ms_events, 3)},
-            "qkv_gemm_tflops": round(gemm_flops / (gemm_ms * 1e-3) / 1e12, 1),
+            "qkv_projection_tflops": round(gemm_flops / ((gemm_ms + proj_ms) * 1e-3) / 1e12, 1),
             "configs1_image": history,
             "dropin_image": dropin,
         },
@@ -926,11 +932,18 @@ def run_projected(args, rank: int, world: int, local_rank: int) -> None:
                           "ms_per_step": round(pack_ms, 3),
                           "gb_per_step": round(pack_bytes / 1e9, 3),
                           "launches_per_step": sum(1 for l in launches if l.kind == "pack")},
-        "roofline_prep": {"bound": "hbm", "peak": hbm, "unit": "GB/s",
+        "roofline_qkv": ({"bound": "tensor", "peak": sustained, "unit": "TFLOP/s",
+                          "achieved": round(gemm_flops / (proj_ms * 1e-3) / 1e12, 1),
+                          "frac": round(gemm_flops / (proj_ms * 1e-3) / 1e12 / sustained, 4),
+                          "kernel": "qkv_project_kernel", "ms_per_step": round(proj_ms, 3),
+                          "hbm_gb_per_step": round(proj_bytes / 1e9, 3)}
+                         if proj.fused_projection else
+                         {"bound": "hbm", "peak": hbm, "unit": "GB/s",
                           "achieved": round(prep_bytes / (prep_ms * 1e-3) / 1e9, 1),
                           "frac": round(prep_bytes / (prep_ms * 1e-3) / 1e9 / hbm, 4),
-                          "kernel": "qkv_prepare_kernel", "ms_per_step": round(prep_ms, 3),
-                          "gb_per_step": round(prep_bytes / 1e9, 3)},
+                          "kernel": "qkv_prepare_kernel (after a cuBLAS GEMM)",
+                          "ms_per_step": round(prep_ms, 3),
+                          "gb_per_step": round(prep_bytes / 1e9, 3)}),
         "cpu_baseline": cpu_baseline_line(args, world),
         "e2e": None if not e2e_steps else {
             "value": round(job_att / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
@@ -968,6 +981,9 @@ def main() -> None:
                     help="replays of the per-launch event graphs for the per-kernel figures")
     ap.add_argument("--no-c2-history", action="store_true",
                     help="skip the configs[1] timing kept beside the configs[4] line")
+    ap.add_argument("--unfused-projection", action="store_true",
+                    help="configs[4]: cuBLAS GEMM + heatkv_qkv_prepare_append instead of the fused "
+                         "heatkv_qkv_project")
     ap.add_argument("--no-dropin", action="store_true",
                     help="skip the one-image timing through the public installer")
     ap.add_argument("--att-traffic", type=float, default=0.0,

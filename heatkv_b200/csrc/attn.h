@@ -124,6 +124,14 @@ cudaError_t launch_scas_mass(const void* q, const void* k, int dtype, int64_t he
                              double* mass_out, int64_t mass_stride, cudaStream_t st);
 
 // q/k/v preparation after the QKV projection (qkv_prep.cu); sms = SMs of the device.
+cudaError_t launch_qkv_project(const void* x, const void* w, void* q, void* k, void* v,
+                               bool bf16, int64_t batch, int64_t seq_len, int64_t heads,
+                               int64_t embed_dim, const float* scale_mul, float eps,
+                               const float* rope_cos, const float* rope_sin,
+                               int64_t rope_row_stride, void* cache_k, void* cache_v,
+                               int64_t cache_rows, const int64_t* cache_offset,
+                               unsigned int* status, cudaStream_t st);
+
 cudaError_t launch_qkv_prepare(const void* qkv, void* q, void* k, void* v, int in_dtype,
                                int qk_dtype, int64_t batch, int64_t seq_len, int64_t heads,
                                const float* scale_mul, float eps, const float* rope_cos,

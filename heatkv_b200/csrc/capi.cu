@@ -636,6 +636,50 @@ int heatkv_qkv_prepare_append(const void* qkv, void* q, void* k, void* v, int in
                           rope_row_stride, slab_k, slab_v, slab_rows, slab_offset, stream);
 }
 
+int heatkv_qkv_project(const void* x, const void* w, void* q, void* k, void* v, int dtype,
+                       int64_t batch, int64_t seq_len, int64_t heads, int64_t embed_dim,
+                       const float* scale_mul, float eps, const float* rope_cos,
+                       const float* rope_sin, int64_t rope_row_stride, void* cache_k,
+                       void* cache_v, int64_t cache_rows, const int64_t* cache_offset,
+                       void* stream) {
+  static const char* name = "heatkv_qkv_project";
+  g_last_error.clear();
+  if (dtype != HEATKV_DTYPE_BF16 && dtype != HEATKV_DTYPE_F16)
+    return fail(HEATKV_ERR_UNSUPPORTED, "%s: x and W must be bfloat16 or float16", name);
+  if (batch < 0 || seq_len < 0 || heads < 0 || embed_dim < 0 || cache_rows < 0)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: negative size", name);
+  if (heads % 2 != 0)
+    return fail(HEATKV_ERR_UNSUPPORTED, "%s: the number of heads must be even", name);
+  if (embed_dim % 64 != 0 || embed_dim == 0)
+    return fail(HEATKV_ERR_UNSUPPORTED, "%s: embed_dim must be a positive multiple of 64", name);
+  if (batch * seq_len * heads == 0) return HEATKV_OK;
+  if ((batch * seq_len + 127) / 128 * (3 * heads / 2) > INT32_MAX)
+    return fail(HEATKV_ERR_UNSUPPORTED, "%s: too many tiles", name);
+  if (!x || !w || !q || !k || !v || (rope_cos && !rope_sin) || (!rope_cos && rope_sin))
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (cache_offset && (!cache_k || !cache_v))
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: cache offsets given without caches", name);
+  if (rope_cos && (rope_row_stride < 64 || (rope_row_stride & 3)))
+    return fail(HEATKV_ERR_INVALID_ARGUMENT,
+                "%s: rope_row_stride must be a multiple of 4 and at least 64", name);
+  if (!(eps >= 0.f)) return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: eps must be >= 0", name);
+  const uintptr_t a16 = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+                        reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(rope_cos) |
+                        reinterpret_cast<uintptr_t>(rope_sin) |
+                        reinterpret_cast<uintptr_t>(cache_offset ? cache_k : nullptr) |
+                        reinterpret_cast<uintptr_t>(cache_offset ? cache_v : nullptr);
+  if ((a16 & 15u) || (reinterpret_cast<uintptr_t>(cache_offset) & 7u))
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: misaligned pointer", name);
+  cudaError_t e = heatkv::launch_qkv_project(
+      x, w, q, k, v, dtype == HEATKV_DTYPE_BF16, batch, seq_len, heads, embed_dim, scale_mul, eps,
+      rope_cos, rope_sin, rope_row_stride, cache_offset ? cache_k : nullptr,
+      cache_offset ? cache_v : nullptr, cache_rows, cache_offset, heatkv::device_status_ptr(),
+      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, name);
+  return HEATKV_OK;
+}
+
 int heatkv_device_status(uint32_t* flags, int clear, void* stream) {
   g_last_error.clear();
   if (!flags) return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_device_status: null flags");

@@ -1,0 +1,379 @@
+// The QKV projection with the q/k/v preparation and the cache append in its epilogue, on
+// Blackwell tensor cores.
+//
+// The patched attention forward computes, per call (enable_real_pruning_fast.py:2040-2072 and the
+// append of :2218-2225):
+//   qkv = x @ W^T                     x [M = batch * seq_len, C], W [3 * H * 128, C] (nn.Linear)
+//   q, k, v = qkv.view(B, L, 3, H, 128) permuted to [B, H, L, 128]
+//   q = normalize(q) * scale_mul[h], k = normalize(k)          (cos-attention, fp32)
+//   q, k = 2-D rotary embedding (infinity/models/basic.py:97-117, fp32)
+// then appends k and v of the scale into the layer's cache. This kernel does all of it in one
+// pass: the GEMM accumulates in TMEM, and the epilogue turns each accumulator row into the
+// prepared q/k/v rows, written once, plus the cache rows of the heads given an offset (the dense
+// cache before a layer's first pruned target, or the slab heads whose segment no live segment of
+// the scale overlaps). The projection output is rounded to x's 16-bit type first, as the unfused
+// path stores it, and the preparation then follows heatkv_qkv_prepare's arithmetic (fp32 norm,
+// x / max(norm, eps), separately rounded rotary products). Only the summation order of the GEMM
+// and of the row norm differ from the unfused path.
+//
+// Tiles are 128 rows x 256 columns (two heads of one of q, k, v) over K steps of 64; a persistent
+// grid of one CTA per SM walks the tiles row panel by row panel (the 24 column tiles of a panel
+// run on neighbouring CTAs, so the x panel is read from HBM once and the weight stays in L2).
+// CTA (256 threads, 1 per SM): warp 0 issues the TMA loads of a 4-stage ring (x box 64 x 128 rows,
+// W box 64 x 256 rows, 128-byte swizzle); warp 1 allocates TMEM (two 256-column accumulators) and
+// issues tcgen05.mma kind::f16 M=128 N=256 K=16, four per stage; warps 4-7 are the epilogue, one
+// TMEM lane (accumulator row) per thread, working on one accumulator while the MMAs fill the
+// other. Every wait is bounded; on expiry the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains its
+// copies and MMAs, frees TMEM and returns.
+#include "attn.h"
+#include "common.cuh"
+#include "sm100_util.cuh"
+
+namespace heatkv {
+namespace sm100 {
+namespace qkvproj {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KiB
+constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KiB
+constexpr int kThreads = 256;
+constexpr int kLoadWarp = 0;
+constexpr int kMmaWarp = 1;
+constexpr int kEpiWarp0 = 4;
+constexpr uint32_t kTmemCols = 512;           // two 256-column accumulators
+
+struct __align__(1024) Smem {
+  uint8_t a[kStages][kABytes];
+  uint8_t b[kStages][kBBytes];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct Params {
+  int64_t rows;          // M = batch * seq_len
+  int64_t seq_len;
+  int64_t heads;         // local heads H (output columns 3 * H * 128)
+  int k_blocks;          // C / 64
+  int n_tiles;           // 3 * H * 128 / 256
+  int tiles;             // ceil(M / 128) * n_tiles
+  void* q;
+  void* k;
+  void* v;
+  const float* scale_mul;
+  float eps;
+  const float* rope_cos;
+  const float* rope_sin;
+  int64_t rope_stride;
+  void* cache_k;
+  void* cache_v;
+  int64_t cache_rows;
+  const int64_t* cache_offset;
+  unsigned int* status;
+};
+
+template <bool kBF16>
+__device__ __forceinline__ float round16(float x) {
+  if constexpr (kBF16) return __bfloat162float(__float2bfloat16_rn(x));
+  else return __half2float(__float2half_rn(x));
+}
+
+// The epilogue of one 128-column head block of this thread's accumulator row: round to the
+// projection dtype, prepare (q/k), store the row and the cache row. The row is read from TMEM in
+// two 64-column halves (twice for q/k with cos-attention: once for the norm, once to write), which
+// keeps the live registers of the epilogue warps low. tcgen05.ld is warp-collective, so rows past
+// the end still load and only skip their stores.
+template <bool kBF16, bool kCos, bool kRope>
+__device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int64_t m, int col0) {
+  using T = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
+  const bool live = m < p.rows;
+  const int64_t mm = live ? m : 0;
+  const int64_t H = p.heads;
+  const int64_t C = H * 128;
+  const int sec = static_cast<int>(col0 / C);          // 0 q, 1 k, 2 v
+  const int64_t h = (col0 % C) / 128;
+  const int64_t b = mm / p.seq_len, l = mm % p.seq_len;
+  const bool prep = sec < 2;
+  float inv_scale = 1.f, n = 1.f;
+  if (kCos && prep) {
+    float ss = 0.f;
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      float x[64];
+      tmem_ld_row64(taddr + half * 64, x);
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float r = round16<kBF16>(x[i]);
+        ss = fmaf(r, r, ss);
+      }
+    }
+    n = fmaxf(sqrtf(ss), p.eps);
+    inv_scale = sec == 0 ? __ldg(p.scale_mul + h) : 1.f;
+  }
+  T* out = static_cast<T*>(sec == 0 ? p.q : sec == 1 ? p.k : p.v);
+  uint4* dst = reinterpret_cast<uint4*>(out + ((b * H + h) * p.seq_len + l) * 128);
+  uint4* cd = nullptr;
+  if (live && sec >= 1 && p.cache_offset != nullptr) {
+    const int64_t off = __ldg(p.cache_offset + h);
+    if (off >= 0) {
+      if (off > p.cache_rows - p.seq_len) {
+        if (l == 0) raise_status(p.status, HEATKV_DEVICE_PACK_OUT_OF_RANGE);
+      } else {
+        T* cache = static_cast<T*>(sec == 1 ? p.cache_k : p.cache_v);
+        cd = reinterpret_cast<uint4*>(cache + (b * p.cache_rows + off + l) * 128);
+      }
+    }
+  }
+#pragma unroll 1
+  for (int half = 0; half < 2; ++half) {
+    float x[64];
+    tmem_ld_row64(taddr + half * 64, x);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) x[i] = round16<kBF16>(x[i]);
+    if (kCos && prep) {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        x[i] = __fdiv_rn(x[i], n);
+        if (sec == 0) x[i] = __fmul_rn(x[i], inv_scale);
+      }
+    }
+    if (kRope && prep) {
+      const float4* cr = reinterpret_cast<const float4*>(p.rope_cos + l * p.rope_stride) + half * 8;
+      const float4* sr = reinterpret_cast<const float4*>(p.rope_sin + l * p.rope_stride) + half * 8;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {  // pairs 4j .. 4j + 3 of this half
+        const float4 c = __ldg(cr + j), s = __ldg(sr + j);
+        const float cc[4] = {c.x, c.y, c.z, c.w}, sc[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = 4 * j + e;
+          const float a0 = x[2 * i], a1 = x[2 * i + 1];
+          x[2 * i] = __fsub_rn(__fmul_rn(cc[e], a0), __fmul_rn(sc[e], a1));
+          x[2 * i + 1] = __fadd_rn(__fmul_rn(sc[e], a0), __fmul_rn(cc[e], a1));
+        }
+      }
+    }
+    if (live) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint4 w = make_uint4(pack2<kBF16>(x[8 * j], x[8 * j + 1]),
+                                   pack2<kBF16>(x[8 * j + 2], x[8 * j + 3]),
+                                   pack2<kBF16>(x[8 * j + 4], x[8 * j + 5]),
+                                   pack2<kBF16>(x[8 * j + 6], x[8 * j + 7]));
+        dst[half * 8 + j] = w;
+        if (cd != nullptr) cd[half * 8 + j] = w;
+      }
+    }
+  }
+}
+
+template <bool kBF16, bool kCos, bool kRope>
+__global__ void __launch_bounds__(kThreads, 1)
+    qkv_project_kernel(const __grid_constant__ CUtensorMap tm_x,
+                       const __grid_constant__ CUtensorMap tm_w, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                      ~uintptr_t(1023));
+  volatile int* abort_flag = &sm.abort_flag;
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sm.acc_full[a], 1);
+      mbar_init(&sm.acc_empty[a], 4);   // one arrival per epilogue warp
+    }
+    mbar_init(&sm.drain, 1);
+    sm.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(&sm.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == kLoadWarp && lane == 0) {
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+  }
+  pdl_trigger();
+  pdl_wait();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const int KB = p.k_blocks;
+
+  if (warp == kLoadWarp) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
+        const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const uint32_t s = it % kStages;
+          if (it >= kStages &&
+              !(ok = mbar_wait(&sm.empty[s], ((it / kStages) - 1) & 1, abort_flag, p.status)))
+            break;
+          mbar_arrive_expect_tx(&sm.full[s], kABytes + kBBytes);
+          tma_load_2d(sm.a[s], &tm_x, kb * kBK, mt * kBM, &sm.full[s]);
+          tma_load_2d(sm.b[s], &tm_w, kb * kBK, nt * kBN, &sm.full[s]);
+        }
+      }
+      if (!ok || *abort_flag) {
+        // every copy already issued lands before the CTA's shared memory goes away
+        for (uint32_t g = it > kStages ? it - kStages : 0; g < it; ++g)
+          mbar_drain(&sm.full[g % kStages], (g / kStages) & 1, p.status);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(kBF16, kBM, kBN, false, false);
+      uint32_t it = 0, tcount = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x, ++tcount) {
+        const uint32_t acc = tcount % 2;
+        if (tcount >= 2 &&
+            !(ok = mbar_wait(&sm.acc_empty[acc], ((tcount / 2) - 1) & 1, abort_flag, p.status)))
+          break;
+        tc_fence_after();
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const uint32_t s = it % kStages;
+          if (!(ok = mbar_wait(&sm.full[s], (it / kStages) & 1, abort_flag, p.status))) break;
+          tc_fence_after();
+          const uint32_t abase = smem_u32(sm.a[s]);
+          const uint32_t bbase = smem_u32(sm.b[s]);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // a K step is 32 bytes into the 128-byte swizzled rows of both operands
+            umma_ss(tmem + acc * kBN, smem_desc_sw128(abase + kk * 32, 16, 1024),
+                    smem_desc_sw128(bbase + kk * 32, 16, 1024), idesc,
+                    (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&sm.empty[s]);
+        }
+        if (ok) tc_commit(&sm.acc_full[acc]);
+      }
+      tc_commit(&sm.drain);
+      mbar_drain(&sm.drain, 0, p.status);
+    }
+  } else if (warp >= kEpiWarp0) {
+    const int quarter = warp - kEpiWarp0;         // TMEM lanes [32 quarter, +32)
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    uint32_t tcount = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++tcount) {
+      const uint32_t acc = tcount % 2;
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(&sm.acc_full[acc], (tcount / 2) & 1, abort_flag, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
+      const int64_t m = int64_t(mt) * kBM + quarter * 32 + lane;
+#pragma unroll 1
+      for (int hb = 0; hb < kBN / 128; ++hb)
+        head_block<kBF16, kCos, kRope>(p, tmem + lane_off + acc * kBN + hb * 128, m,
+                                       nt * kBN + hb * 128);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+}
+
+// rows x cols 16-bit matrix, box 64 columns x box_rows rows, 128-byte swizzle
+bool encode_matrix(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, bool bf16,
+                   int box_rows) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   2, const_cast<void*>(base), dims, strides, box, elem,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <bool kBF16, bool kCos, bool kRope>
+cudaError_t launch_t(const CUtensorMap& tx, const CUtensorMap& tw, const Params& p, int grid,
+                     cudaStream_t st) {
+  auto kern = qkv_project_kernel<kBF16, kCos, kRope>;
+  const size_t smem = sizeof(Smem) + 1024;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    attr_set[dev & 63] = true;
+  }
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, st, tx, tw, p);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+}  // namespace qkvproj
+}  // namespace sm100
+
+cudaError_t launch_qkv_project(const void* x, const void* w, void* q, void* k, void* v,
+                               bool bf16, int64_t batch, int64_t seq_len, int64_t heads,
+                               int64_t embed_dim, const float* scale_mul, float eps,
+                               const float* rope_cos, const float* rope_sin,
+                               int64_t rope_row_stride, void* cache_k, void* cache_v,
+                               int64_t cache_rows, const int64_t* cache_offset,
+                               unsigned int* status, cudaStream_t st) {
+  using namespace sm100::qkvproj;
+  CUtensorMap tx, tw;
+  const int64_t M = batch * seq_len;
+  if (!encode_matrix(&tx, x, M, embed_dim, bf16, kBM) ||
+      !encode_matrix(&tw, w, 3 * heads * 128, embed_dim, bf16, kBN))
+    return cudaErrorInvalidValue;
+  Params p{};
+  p.rows = M;
+  p.seq_len = seq_len;
+  p.heads = heads;
+  p.k_blocks = static_cast<int>(embed_dim / kBK);
+  p.n_tiles = static_cast<int>(3 * heads * 128 / kBN);
+  p.tiles = static_cast<int>((M + kBM - 1) / kBM) * p.n_tiles;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.scale_mul = scale_mul;
+  p.eps = eps;
+  p.rope_cos = rope_cos;
+  p.rope_sin = rope_sin;
+  p.rope_stride = rope_row_stride;
+  p.cache_k = cache_k;
+  p.cache_v = cache_v;
+  p.cache_rows = cache_rows;
+  p.cache_offset = cache_offset;
+  p.status = status;
+  const int grid = static_cast<int>(std::min<int64_t>(p.tiles, sm100::sm_count()));
+  const bool cos = scale_mul != nullptr, rope = rope_cos != nullptr;
+#define HEATKV_QKV_PROJ(B)                                                           \
+  (cos && rope ? launch_t<B, true, true>(tx, tw, p, grid, st)                        \
+   : cos       ? launch_t<B, true, false>(tx, tw, p, grid, st)                       \
+   : rope      ? launch_t<B, false, true>(tx, tw, p, grid, st)                       \
+               : launch_t<B, false, false>(tx, tw, p, grid, st))
+  return bf16 ? HEATKV_QKV_PROJ(true) : HEATKV_QKV_PROJ(false);
+#undef HEATKV_QKV_PROJ
+}
+
+}  // namespace heatkv

@@ -182,18 +182,19 @@ _JOB_DTYPE = np.dtype([("dst_k", "<u8"), ("dst_v", "<u8"), ("src_k", "<u8"), ("s
 
 @dataclasses.dataclass
 class Launch:
-    kind: str            # "attention" | "pack"
+    kind: str            # "attention" | "pack" | "proj" | "prep" | "gemm" | exchange kinds
     layer: int
     target: int
     fn: Callable
     args: tuple          # ctypes arguments without the trailing stream
-    work: float          # algorithmic FLOPs (attention) or HBM bytes (pack)
+    work: float          # algorithmic FLOPs (attention, proj, gemm) or HBM bytes (pack, prep)
     keep: object = None  # device arrays the arguments point into
     sources: tuple = ()  # (plan index, target) of the step inputs a pack reads
     # an attention launch flagged HEATKV_ATTN_CURRENT_IN_SEGMENTS: the (starts, ends, counts)
     # pointers of the same keys without the current scale inside the segments, for callers that
     # re-issue it through an entry point without a kernel selector (the scatter)
     unflagged_meta: Optional[tuple] = None
+    nbytes: float = 0.0  # algorithmic HBM bytes of a launch whose work counts FLOPs (proj)
 
     def __call__(self, stream: ctypes.c_void_p) -> None:
         status = self.fn(*self.args, stream)

@@ -13,6 +13,9 @@ one ``heatkv_pack_kv_batched`` launch, as the pre-planned step issues a scale's 
 probabilities it avoids.
 ``qkv-prep``: one layer's q/k/v preparation (``heatkv_qkv_prepare``: cos-attention + RoPE under
 autocast) against the PyTorch chain it replaces.
+``qkv-project``: one layer's fused projection (``heatkv_qkv_project``: tcgen05 GEMM with cos-attention,
+RoPE and the q/k/v layout in its epilogue) for ``--rows`` x ``--q-len`` tokens and ``--heads``
+heads of 128 (embed dim = heads x 128), against cuBLAS (``torch.mm``) of the same projection.
 ``projected-step``: the whole projection-driven step of ``bench.py``'s default workload
 (``heatkv_b200.projected``: 2B, 10 % budget, every layer and scale) for ``--rows`` rows, run
 eagerly ``--iters`` times after ``--warmup`` (for ncu launch lists of exactly one step).
@@ -77,7 +80,7 @@ def time_call(fn, iters, warmup=3):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("kernel", choices=["attention", "pack", "pack-batched", "qkv-prep", "scas",
-                                       "projected-step"])
+                                       "projected-step", "qkv-project"])
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--rows", type=int, default=2)
     ap.add_argument("--heads", type=int, default=16)
@@ -90,7 +93,35 @@ def main(argv=None):
     args = ap.parse_args(argv)
     dtype = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32,
              "f32qk": torch.float32}[args.dtype]
-    if args.kernel == "projected-step":
+    if args.kernel == "qkv-project":
+        import ctypes
+        B, L, H = args.rows, args.q_len, args.heads
+        C = H * 128
+        g = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn(B * L, C, device="cuda", generator=g).bfloat16()
+        w = (torch.randn(3 * C, C, device="cuda", generator=g) * 0.02).bfloat16()
+        q, k, v = (torch.empty(B, H, L, 128, device="cuda", dtype=torch.bfloat16)
+                   for _ in range(3))
+        sm = torch.full((H,), 4.0, device="cuda")
+        ang = torch.rand(L, 64, device="cuda", generator=g) * 6
+        cos, sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()
+        lib = _native.load()
+        stream = _native.stream_handle(torch.device("cuda"))
+        out = torch.empty(B * L, 3 * C, device="cuda", dtype=torch.bfloat16)
+
+        def fused():
+            _native.check(lib.heatkv_qkv_project(
+                _native.ptr(x), _native.ptr(w), _native.ptr(q), _native.ptr(k), _native.ptr(v),
+                _native.DTYPE_CODES[torch.bfloat16], B, L, H, C, _native.ptr(sm),
+                ctypes.c_float(1e-12), _native.ptr(cos), _native.ptr(sin), 64, None, None, 0,
+                None, stream), "heatkv_qkv_project")
+        flops = 2.0 * B * L * C * 3 * C
+        ms = time_call(fused, args.iters, args.warmup)
+        ms_mm = time_call(lambda: torch.mm(x, w.t(), out=out), args.iters, args.warmup)
+        print(f"qkv-project rows={B} q_len={L} heads={H}: fused {ms * 1e3:.1f} us "
+              f"({flops / ms / 1e9:.1f} TFLOP/s), cuBLAS GEMM alone {ms_mm * 1e3:.1f} us "
+              f"({flops / ms_mm / 1e9:.1f} TFLOP/s)", flush=True)
+    elif args.kernel == "projected-step":
         import os
         import sys
         sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))

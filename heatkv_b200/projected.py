@@ -5,15 +5,16 @@ attention, :2218-2225 for the append), for every layer of a model and all 13 sca
 
 Per (scale ``t``, layer ``l``), on one stream:
 
-1. ``qkv = x_t @ W_l^T`` - the layer's ``mat_qkv`` projection of the scale's layer input ``x_t``
-   ``[rows, n_t, C]`` (a plain GEMM: cuBLAS through ``torch.mm``; the q/v biases of the reference's
-   ``F.linear`` are zero at initialisation and left out);
-2. ``heatkv_qkv_prepare_append`` - cos-attention normalisation (``scale_mul``), 2-D RoPE and the
-   ``[B, H, L, D]`` layout in one pass. The same pass writes the scale's K/V rows into the layer's
-   cache wherever that is safe before the attention: into the dense cache at every scale before
-   the layer's first pruned target (the attention then reads the scale as the tail of each head's
-   one segment), and into the slab for the heads whose new segment overlaps no slot the scale's
-   attention reads (``scheduler.prep_append_split``);
+1.-2. ``heatkv_qkv_project`` - the layer's ``mat_qkv`` projection of the scale's layer input
+   ``x_t`` ``[rows, n_t, C]`` on the tensor cores, whose epilogue does the cos-attention
+   normalisation (``scale_mul``), the 2-D RoPE and the ``[B, H, L, D]`` layout (the q/v biases of
+   the reference's ``F.linear`` are zero at initialisation and left out). The same epilogue writes
+   the scale's K/V rows into the layer's cache wherever that is safe before the attention: into
+   the dense cache at every scale before the layer's first pruned target (the attention then reads
+   the scale as the tail of each head's one segment), and into the slab for the heads whose new
+   segment overlaps no slot the scale's attention reads (``scheduler.prep_append_split``). With
+   ``fused_projection=False`` these are two launches: a cuBLAS GEMM (``torch.mm``) and
+   ``heatkv_qkv_prepare_append``;
 3. the segmented attention (``HotPath.attention_launch``; softmax scale 1 with cos-attention, as
    the model's ``self.scale``);
 4. the rest of the append (heads whose slots the attention still reads) with ``heatkv_pack_kv``.
@@ -49,7 +50,7 @@ class ProjectedHotPath:
     def __init__(self, hot: HotPath, *, global_heads: Optional[Sequence[Sequence[int]]] = None,
                  embed_dim: Optional[int] = None, weight_seed: int = 0,
                  cos_attention: bool = True, rope: bool = True, scale_mul: float = None,
-                 weights: Optional[List[torch.Tensor]] = None):
+                 weights: Optional[List[torch.Tensor]] = None, fused_projection: bool = True):
         if hot.head_dim != 128:
             raise ValueError("the projected path needs head_dim 128")
         if not hot.dense_append_first:
@@ -57,6 +58,9 @@ class ProjectedHotPath:
         if hot.k_dtype not in (torch.bfloat16, torch.float16) or hot.v_dtype != hot.k_dtype:
             raise ValueError("the projected path runs 16-bit q/k/v")
         self.hot = hot
+        # one heatkv_qkv_project launch per (scale, layer) (projection with the preparation and
+        # the early appends in its epilogue), or a cuBLAS GEMM followed by heatkv_qkv_prepare*
+        self.fused_projection = bool(fused_projection) and hot.num_heads % 2 == 0
         self.device = hot.device
         self.dtype = hot.k_dtype
         H, D = hot.num_heads, hot.head_dim
@@ -100,8 +104,10 @@ class ProjectedHotPath:
             self.rope_cos, self.rope_sin = cos.to(self.device), sin.to(self.device)
         else:
             self.rope_cos = self.rope_sin = None
-        # scratch shared by every (scale, layer) call
-        self.qkv = torch.empty(B * nmax * 3 * H * D, dtype=self.dtype, device=self.device)
+        # scratch shared by every (scale, layer) call (the projection output only without the
+        # fused projection)
+        self.qkv = torch.empty(0 if self.fused_projection else B * nmax * 3 * H * D,
+                               dtype=self.dtype, device=self.device)
         self.q, self.k, self.v = (torch.empty(B * H * nmax * D, dtype=self.dtype,
                                               device=self.device) for _ in range(3))
         # per plan and scale: where the preparation writes the scale's K/V (dense cache, slab or
@@ -177,10 +183,12 @@ class ProjectedHotPath:
 
     def current(self, t: int):
         """The scratch q, k, v ``[rows, H, n_t, D]`` and projection output ``[rows * n_t, 3C_l]``
-        of scale ``t``."""
+        (None with the fused projection) of scale ``t``."""
         B, H, D, n = self.rows, self.num_heads, self.hot.head_dim, self.tokens[t]
         q, k, v = (b[:B * H * n * D].view(B, H, n, D) for b in (self.q, self.k, self.v))
-        return q, k, v, self.qkv[:B * n * 3 * H * D].view(B * n, 3 * H * D)
+        qkv = (None if self.fused_projection
+               else self.qkv[:B * n * 3 * H * D].view(B * n, 3 * H * D))
+        return q, k, v, qkv
 
     # ------------------------------------------------------------------ launches
     def launches(self, x, out, *, kernel: int = _native.ATTN_AUTO) -> list:
@@ -207,29 +215,40 @@ class ProjectedHotPath:
             for i, p in enumerate(hot.plans):
                 w = self.weights[i]
                 flops = 2.0 * B * n * C * w.shape[0]
-
-                def gemm(stream, x2d=x2d, w=w, qkv=qkv):
-                    torch.mm(x2d, w.t(), out=qkv)
-                    return _native.HEATKV_OK
-                out_launches.append(Launch("gemm", p.layer, t, gemm, (), flops))
                 target = self.prep_target.get((i, t))
                 cos = sin = None
                 if self.rope_cos is not None:
                     cos = ctypes.c_void_p(self.rope_cos.data_ptr() + self.starts[t] * 64 * 4)
                     sin = ctypes.c_void_p(self.rope_sin.data_ptr() + self.starts[t] * 64 * 4)
-                common = (_native.ptr(qkv), _native.ptr(q), _native.ptr(k), _native.ptr(v), code,
-                          code, B, n, H, D, _native.ptr(self.scale_mul), ctypes.c_float(1e-12),
-                          cos, sin, 64)
-                nbytes = float(B * n * H * (3 * row + 3 * row))
-                if target is None:
-                    prep = Launch("prep", p.layer, t, lib.heatkv_qkv_prepare, common, nbytes)
+                written = 0 if target is None else target[4]
+                if self.fused_projection:
+                    # x read once per column panel from HBM, q/k/v and the early cache rows written
+                    nbytes = float(B * n * (C * 2 + H * 3 * row + written * 2 * row))
+                    sk, sv, rows_, offs = (None, None, 0, None) if target is None else target[:4]
+                    out_launches.append(Launch(
+                        "proj", p.layer, t, lib.heatkv_qkv_project,
+                        (_native.ptr(x2d), _native.ptr(w), _native.ptr(q), _native.ptr(k),
+                         _native.ptr(v), code, B, n, H, C, _native.ptr(self.scale_mul),
+                         ctypes.c_float(1e-12), cos, sin, 64, _native.ptr(sk), _native.ptr(sv),
+                         rows_, _native.ptr(offs)), flops))
+                    out_launches[-1].nbytes = nbytes
                 else:
-                    sk, sv, rows_, offs, written = target
-                    nbytes += float(B * n * written * 2 * row)
-                    prep = Launch("prep", p.layer, t, lib.heatkv_qkv_prepare_append,
-                                  common + (_native.ptr(sk), _native.ptr(sv), rows_,
-                                            _native.ptr(offs)), nbytes)
-                out_launches.append(prep)
+                    def gemm(stream, x2d=x2d, w=w, qkv=qkv):
+                        torch.mm(x2d, w.t(), out=qkv)
+                        return _native.HEATKV_OK
+                    out_launches.append(Launch("gemm", p.layer, t, gemm, (), flops))
+                    common = (_native.ptr(qkv), _native.ptr(q), _native.ptr(k), _native.ptr(v),
+                              code, code, B, n, H, D, _native.ptr(self.scale_mul),
+                              ctypes.c_float(1e-12), cos, sin, 64)
+                    nbytes = float(B * n * H * (3 * row + 3 * row) + B * n * written * 2 * row)
+                    if target is None:
+                        prep = Launch("prep", p.layer, t, lib.heatkv_qkv_prepare, common, nbytes)
+                    else:
+                        sk, sv, rows_, offs, written = target
+                        prep = Launch("prep", p.layer, t, lib.heatkv_qkv_prepare_append,
+                                      common + (_native.ptr(sk), _native.ptr(sv), rows_,
+                                                _native.ptr(offs)), nbytes)
+                    out_launches.append(prep)
                 o = out[i][t] if isinstance(out[0], (list, tuple)) else out[t]
                 out_launches.append(hot.attention_launch(i, t, q, k, v, o, kernel=kernel,
                                                          softmax_scale=self.softmax_scale))

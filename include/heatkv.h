@@ -14,6 +14,8 @@
  *                                  (infinity/models/basic.py:97-117)
  *   - heatkv_qkv_prepare_append  <- the same, plus the slab append of the scale
  *                                  (enable_real_pruning_fast.py:2218-2225) for hazard-free heads
+ *   - heatkv_qkv_project         <- the QKV projection (F.linear, :2040-2043) with the two above
+ *                                  in its epilogue
  *
  * Conventions
  *   - Every pointer argument is a device pointer unless stated otherwise; tensors are dense,
@@ -422,6 +424,30 @@ int heatkv_qkv_prepare_append(const void* qkv, void* q, void* k, void* v, int in
                               const float* rope_cos, const float* rope_sin,
                               int64_t rope_row_stride, void* slab_k, void* slab_v,
                               int64_t slab_rows, const int64_t* slab_offset, void* stream);
+
+/*
+ * heatkv_qkv_project - the QKV projection of the patched attention forward with the q/k/v
+ * preparation and the cache append in its epilogue, on the tensor cores: replaces
+ * F.linear(x, mat_qkv.weight) (enable_real_pruning_fast.py:2040-2043) followed by
+ * heatkv_qkv_prepare_append (the chain of :2044-2072 and the append of :2218-2225).
+ *   x       : [batch * seq_len, embed_dim] (dtype: bf16 or f16), the layer input of one scale
+ *   w       : [3 * heads * 128, embed_dim] (dtype), the nn.Linear weight rows of the q, k and v
+ *             heads (the biases are not applied: they are zero in the models this serves)
+ *   q, k, v : [batch, heads, seq_len, 128] (dtype). The projection is rounded to dtype, then
+ *             prepared as heatkv_qkv_prepare does (scale_mul: cos-attention; rope: the rotary
+ *             rows of the scale's tokens, rope_row_stride floats apart)
+ *   cache_* : as heatkv_qkv_prepare_append's slab (cache_offset -1 = head not written); rows of
+ *             the heads given an offset are written from the same registers
+ * heads must be even, embed_dim a multiple of 64; x, w, q, k, v, the rope rows and the caches
+ * 16-byte aligned. Results equal heatkv_qkv_prepare_append applied to the rounded projection up
+ * to the summation order of the projection and of the row norms.
+ */
+int heatkv_qkv_project(const void* x, const void* w, void* q, void* k, void* v, int dtype,
+                       int64_t batch, int64_t seq_len, int64_t heads, int64_t embed_dim,
+                       const float* scale_mul, float eps, const float* rope_cos,
+                       const float* rope_sin, int64_t rope_row_stride, void* cache_k,
+                       void* cache_v, int64_t cache_rows, const int64_t* cache_offset,
+                       void* stream);
 
 /*
  * heatkv_slot_schedule - host-side slab placement of one layer's static schedule, replacing the

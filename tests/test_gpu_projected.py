@@ -49,9 +49,9 @@ def _chain_qkv(x_t, w, start, n, cos, sin, scale_mul=4.0, heads=16):
     return rope(q).bfloat16(), rope(k).bfloat16(), v.contiguous()
 
 
-def _run(ctrl, L, H, rows, layers, dev, row_ids=None):
+def _run(ctrl, L, H, rows, layers, dev, row_ids=None, fused=True):
     hot = HotPath(ctrl, L, H, rows, dev, layers=layers)
-    proj = ProjectedHotPath(hot)
+    proj = ProjectedHotPath(hot, fused_projection=fused)
     x, _ = proj.allocate_inputs(row_ids if row_ids is not None else list(range(rows)), seed=3)
     outs = [proj.allocate_outputs()[0] for _ in layers]
     proj.run(proj.launches(x, outs))
@@ -59,12 +59,13 @@ def _run(ctrl, L, H, rows, layers, dev, row_ids=None):
     return hot, proj, x, outs
 
 
-def test_projected_path_matches_keep_mask_attention():
+@pytest.mark.parametrize("fused", [True, False])
+def test_projected_path_matches_keep_mask_attention(fused):
     torch.backends.cuda.matmul.allow_tf32 = False
     dev = torch.device("cuda", 0)
     ctrl, L, H = _controller()
     layers = [0, 21]
-    hot, proj, x, outs = _run(ctrl, L, H, 4, layers, dev)
+    hot, proj, x, outs = _run(ctrl, L, H, 4, layers, dev, fused=fused)
     assert _native.device_status(dev) == 0
     assert proj.early_slots > 0 and proj.rest_slots > 0
     for i, layer in enumerate(layers):
@@ -78,10 +79,12 @@ def test_projected_path_matches_keep_mask_attention():
 
 
 def test_projected_path_equals_prepare_then_hot_path():
+    """Unfused projection (cuBLAS + heatkv_qkv_prepare_append): bit-identical to the preparation
+    and the engine run separately."""
     dev = torch.device("cuda", 0)
     ctrl, L, H = _controller()
     layers = [3, 30]
-    hot, proj, x, outs = _run(ctrl, L, H, 2, layers, dev)
+    hot, proj, x, outs = _run(ctrl, L, H, 2, layers, dev, fused=False)
     # the same preparation per (layer, scale), then the engine with its own appends
     ref_hot = HotPath(ctrl, L, H, 2, dev, layers=layers)
     inputs, ref_out = [], []
@@ -129,3 +132,26 @@ def test_projected_64_rows_match_4_rows():
                 err = (a - b).abs().max().item()
                 assert err <= BF16_ATOL and err / max(b.abs().max().item(), 1e-6) <= BF16_REL, \
                     (layers[i], t, err)
+
+
+def test_fused_projection_path_matches_unfused_path():
+    """The fused projection (tcgen05 GEMM with the preparation and early appends in its epilogue)
+    against the unfused path on the same rows: every output and every live slab segment after the
+    step within the bf16 tolerance."""
+    dev = torch.device("cuda", 0)
+    ctrl, L, H = _controller()
+    layers = [0, 17]
+    runs = [_run(ctrl, L, H, 4, layers, dev, fused=f) for f in (True, False)]
+    assert _native.device_status(dev) == 0
+    (ha, _, _, oa), (hb, _, _, ob) = runs
+    for i in range(len(layers)):
+        for a, b in zip(oa[i], ob[i]):
+            err = (a.float() - b.float()).abs().max().item()
+            assert err <= BF16_ATOL and err <= BF16_REL * b.float().abs().max().item(), err
+        for seg in ha.plans[i].schedule["segments"]:
+            if seg["end_target"] < ha.num_scales:
+                continue
+            lo, hi = seg["offset"], seg["offset"] + seg["length"]
+            for sa, sb in ((ha.slab_k[i], hb.slab_k[i]), (ha.slab_v[i], hb.slab_v[i])):
+                err = (sa[:, lo:hi].float() - sb[:, lo:hi].float()).abs().max().item()
+                assert err <= BF16_ATOL, (seg, err)

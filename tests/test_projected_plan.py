@@ -7,6 +7,7 @@ copies left for after the attention add up to the reference's append runs
 """
 
 import numpy as np
+import pytest
 import torch
 
 from heatkv_b200.hotpath import HotPath
@@ -49,25 +50,29 @@ def test_projected_appends_cover_the_schedule():
                 assert off + n <= seg["offset"] or seg["offset"] + seg["length"] <= off
 
 
-def test_projected_launch_order():
+@pytest.mark.parametrize("fused", [True, False])
+def test_projected_launch_order(fused):
     ctrl, L, H = _controller()
     layers = [0, 21]
     hot = HotPath(ctrl, L, H, 2, "cpu", layers=layers)
-    proj = ProjectedHotPath(hot)
+    proj = ProjectedHotPath(hot, fused_projection=fused)
     x = [torch.empty(2, n, H * 128, dtype=torch.bfloat16) for n in hot.tokens]
     out = [torch.empty(2, n, H * 128, dtype=torch.bfloat16) for n in hot.tokens]
     launches = proj.launches(x, out)
     kinds = [l.kind for l in launches]
-    assert kinds.count("gemm") == kinds.count("prep") == kinds.count("attention") == \
-        len(layers) * hot.num_scales
-    # per (scale, layer): gemm, prep, attention, then optional packs
+    first = ("proj",) if fused else ("gemm", "prep")
+    for k in first + ("attention",):
+        assert kinds.count(k) == len(layers) * hot.num_scales
+    # per (scale, layer): the projection (one or two launches), attention, then optional packs
     seq = [(l.kind, l.layer, l.target) for l in launches if l.kind != "pack"]
-    for j in range(0, len(seq), 3):
-        (a, la, ta), (b, lb, tb), (c, lc, tc) = seq[j:j + 3]
-        assert (a, b, c) == ("gemm", "prep", "attention") and la == lb == lc and ta == tb == tc
+    step = len(first) + 1
+    for j in range(0, len(seq), step):
+        group = seq[j:j + step]
+        assert tuple(g[0] for g in group) == first + ("attention",)
+        assert len({(g[1], g[2]) for g in group}) == 1
     # one activation pack per scale that precedes some layer's first pruned target
     acts = {p.first_target - 1 for p in hot.plans if p.activation is not None}
     batched = [l for l in launches if l.kind == "pack" and l.layer == -1]
     assert sorted(l.target for l in batched) == sorted(acts)
-    assert np.isclose(sum(l.work for l in launches if l.kind == "gemm"),
+    assert np.isclose(sum(l.work for l in launches if l.kind in ("gemm", "proj")),
                       sum(2.0 * 2 * n * 2048 * 6144 for n in hot.tokens) * len(layers))
