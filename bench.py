@@ -919,8 +919,9 @@ def run_projected(args, rank: int, world: int, local_rank: int) -> None:
         },
         "roofline": {"bound": "tensor", "achieved": round(att_achieved, 1), "peak": sustained,
                      "unit": "TFLOP/s", "frac": round(att_achieved / sustained, 4),
-                     "traffic": args.att_traffic or None,
-                     "traffic_launch": "target 12 (Lq 4096), scaled to the rows of one GPU",
+                     "traffic": round(args.att_traffic_per_row * rows),
+                     "traffic_launch": ("target 12 (Lq 4096): ncu DRAM read + write of the 8-row "
+                                        "launch, scaled by rows to this GPU's rows"),
                      "peak_kind": f"bf16_tflops_sustained ({peak_src})",
                      "frac_of_burst": round(att_achieved / burst, 4),
                      "kernel": "attn_sm100_cs64_kernel", "launches_per_step": n_att,
@@ -986,8 +987,9 @@ def main() -> None:
                          "heatkv_qkv_project")
     ap.add_argument("--no-dropin", action="store_true",
                     help="skip the one-image timing through the public installer")
-    ap.add_argument("--att-traffic", type=float, default=0.0,
-                    help="DRAM bytes of one target-12 attention launch at this GPU's rows (ncu)")
+    ap.add_argument("--att-traffic-per-row", type=float, default=565.5e6 / 8,
+                    help="DRAM bytes per batch row of the target-12 attention launch (ncu capture "
+                         "at 8 rows, profiles/attn_sm100_cs64_kernel_2b_q4096_rows8.md)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--shard", choices=["image", "auto", "rows", "heads"], default="image",
                     help="image: each GPU runs its own image (weak scaling); auto/rows/heads: "

@@ -13,18 +13,21 @@
 // cache before a layer's first pruned target, or the slab heads whose segment no live segment of
 // the scale overlaps). The projection output is rounded to x's 16-bit type first, as the unfused
 // path stores it, and the preparation then follows heatkv_qkv_prepare's arithmetic (fp32 norm,
-// x / max(norm, eps), separately rounded rotary products). Only the summation order of the GEMM
-// and of the row norm differ from the unfused path.
+// separately rounded rotary products) except that x / max(norm, eps) is taken as x times the
+// correctly rounded reciprocal (one fp32 rounding step at most). Those and the summation order of
+// the GEMM and of the row norm are the only differences from the unfused path.
 //
 // Tiles are 128 rows x 256 columns (two heads of one of q, k, v) over K steps of 64; a persistent
 // grid of one CTA per SM walks the tiles row panel by row panel (the 24 column tiles of a panel
 // run on neighbouring CTAs, so the x panel is read from HBM once and the weight stays in L2).
-// CTA (256 threads, 1 per SM): warp 0 issues the TMA loads of a 4-stage ring (x box 64 x 128 rows,
+// CTA (384 threads, 1 per SM): warp 0 issues the TMA loads of a 4-stage ring (x box 64 x 128 rows,
 // W box 64 x 256 rows, 128-byte swizzle); warp 1 allocates TMEM (two 256-column accumulators) and
-// issues tcgen05.mma kind::f16 M=128 N=256 K=16, four per stage; warps 4-7 are the epilogue, one
-// TMEM lane (accumulator row) per thread, working on one accumulator while the MMAs fill the
-// other. Every wait is bounded; on expiry the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains its
+// issues tcgen05.mma kind::f16 M=128 N=256 K=16, four per stage; warps 4-11 are the epilogue, one
+// TMEM lane (accumulator row) and one head block per thread, two warps per SM sub-partition,
+// working on one accumulator while the MMAs fill the other. Every wait is bounded; on expiry the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains its
 // copies and MMAs, frees TMEM and returns.
+#include <cstdlib>
+
 #include "attn.h"
 #include "common.cuh"
 #include "sm100_util.cuh"
@@ -39,10 +42,11 @@ constexpr int kBK = 64;
 constexpr int kStages = 4;
 constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KiB
 constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KiB
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
 constexpr int kLoadWarp = 0;
 constexpr int kMmaWarp = 1;
-constexpr int kEpiWarp0 = 4;
+constexpr int kEpiWarp0 = 4;    // warps 4-11: epilogue; warp 4 + 4 j + q reads TMEM lanes
+constexpr int kEpiWarps = 8;    // [32 q, +32) of head block j (two warps per SM sub-partition)
 constexpr uint32_t kTmemCols = 512;           // two 256-column accumulators
 
 struct __align__(1024) Smem {
@@ -115,6 +119,9 @@ __device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int6
       }
     }
     n = fmaxf(sqrtf(ss), p.eps);
+    // one correctly rounded reciprocal per row, then products: within one fp32 rounding of
+    // x / n, far below the 16-bit rounding of the result
+    n = __frcp_rn(n);
     inv_scale = sec == 0 ? __ldg(p.scale_mul + h) : 1.f;
   }
   T* out = static_cast<T*>(sec == 0 ? p.q : sec == 1 ? p.k : p.v);
@@ -140,7 +147,7 @@ __device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int6
     if (kCos && prep) {
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
-        x[i] = __fdiv_rn(x[i], n);
+        x[i] = __fmul_rn(x[i], n);
         if (sec == 0) x[i] = __fmul_rn(x[i], inv_scale);
       }
     }
@@ -191,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&sm.acc_full[a], 1);
-      mbar_init(&sm.acc_empty[a], 4);   // one arrival per epilogue warp
+      mbar_init(&sm.acc_empty[a], kEpiWarps);   // one arrival per epilogue warp
     }
     mbar_init(&sm.drain, 1);
     sm.abort_flag = 0;
@@ -267,7 +274,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_drain(&sm.drain, 0, p.status);
     }
   } else if (warp >= kEpiWarp0) {
-    const int quarter = warp - kEpiWarp0;         // TMEM lanes [32 quarter, +32)
+    const int quarter = (warp - kEpiWarp0) % 4;   // TMEM lanes [32 quarter, +32)
+    const int hb = (warp - kEpiWarp0) / 4;        // head block (128 columns) of the tile
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     uint32_t tcount = 0;
     bool ok = true;
@@ -279,10 +287,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
       const int64_t m = int64_t(mt) * kBM + quarter * 32 + lane;
-#pragma unroll 1
-      for (int hb = 0; hb < kBN / 128; ++hb)
-        head_block<kBF16, kCos, kRope>(p, tmem + lane_off + acc * kBN + hb * 128, m,
-                                       nt * kBN + hb * 128);
+      head_block<kBF16, kCos, kRope>(p, tmem + lane_off + acc * kBN + hb * 128, m,
+                                     nt * kBN + hb * 128);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
@@ -292,6 +298,216 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ------------------------------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs on two SMs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 M=256 N=256 K=16. Each CTA loads its own 128 rows of x and its own 128
+// rows of W per K step (every load copies this GPU's memory into the loading CTA's own shared
+// memory), so an SM receives 32 KiB of operands per 512 tensor cycles instead of 48 KiB:
+// one CTA alone with a 128 x 256 tile needs 96 B per cycle from L2, more than it gets, and ran at
+// ~70 % of the tensor rate. The even CTA of the pair (the leader) issues the MMAs, which read both
+// CTAs' shared memory and write each CTA's 128 accumulator rows into its own TMEM. Protocol:
+//   * both CTAs' TMA loads of a stage complete on the leader's full[s] barrier (the leader posts
+//     the transaction bytes of both); the MMA's stage release is committed to empty[s] of both
+//     CTAs (tcgen05.commit multicast), so each producer reuses its own stage;
+//   * the accumulator completion is committed to acc_full[a] of both CTAs; each CTA's epilogue
+//     warps arrive on the leader's acc_empty[a] (8 arrivals) when they have read it;
+//   * TMEM is allocated and freed with cta_group::2 by one warp of each CTA; cluster barriers
+//     after the set-up and before the exit keep either CTA from running ahead of its peer's
+//     barriers or freeing memory its peer still uses.
+// ------------------------------------------------------------------------------------------------
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairABytes = 128 * kBK * 2;   // this CTA's 128 rows of x, 16 KiB
+constexpr uint32_t kPairBBytes = 128 * kBK * 2;   // this CTA's 128 rows of W, 16 KiB
+
+struct __align__(1024) PairSmem {
+  uint8_t a[kPairStages][kPairABytes];
+  uint8_t b[kPairStages][kPairBBytes];
+  uint64_t full[kPairStages];
+  uint64_t empty[kPairStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+// shared::cluster address of the same shared variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+// 2-D tiled load into this CTA's shared memory whose completion counts on the mbarrier at
+// `bar_cluster_addr`, which may be the peer CTA's (cta_group::2).
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int c0,
+                                                 int c1, uint32_t bar_cluster_addr) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster_addr)
+      : "memory");
+}
+__device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on the barrier at this shared offset in both CTAs once the issued MMAs complete
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)), "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+template <bool kBF16, bool kCos, bool kRope>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    qkv_project_pair_kernel(const __grid_constant__ CUtensorMap tm_x,
+                            const __grid_constant__ CUtensorMap tm_w, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  PairSmem& sm = *reinterpret_cast<PairSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  volatile int* abort_flag = &sm.abort_flag;
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x / 2), npairs = static_cast<int>(gridDim.x / 2);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sm.acc_full[a], 1);
+      mbar_init(&sm.acc_empty[a], 2 * kEpiWarps);   // the epilogue warps of both CTAs
+    }
+    mbar_init(&sm.drain, 1);
+    sm.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&sm.tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  if (warp == kLoadWarp && lane == 0) {
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+  }
+  pdl_trigger();
+  tc_fence_before();
+  cluster_sync_all();   // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  pdl_wait();
+  const uint32_t tmem = sm.tmem_base;
+  const int KB = p.k_blocks;
+  const int m_tiles = static_cast<int>((p.rows + 255) / 256);
+  const int tiles = m_tiles * p.n_tiles;
+
+  if (warp == kLoadWarp) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < tiles; tile += npairs) {
+        const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const uint32_t s = it % kPairStages;
+          if (it >= kPairStages &&
+              !(ok = mbar_wait(&sm.empty[s], ((it / kPairStages) - 1) & 1, abort_flag, p.status)))
+            break;
+          if (leader) mbar_arrive_expect_tx(&sm.full[s], 2 * (kPairABytes + kPairBBytes));
+          const uint32_t bar = peer_addr(&sm.full[s], 0);
+          tma_load_2d_pair(sm.a[s], &tm_x, kb * kBK, mt * 256 + static_cast<int>(rank) * 128, bar);
+          tma_load_2d_pair(sm.b[s], &tm_w, kb * kBK, nt * kBN + static_cast<int>(rank) * 128, bar);
+        }
+      }
+      if (leader && (!ok || *abort_flag)) {
+        // the leader's full barriers count both CTAs' copies: wait for all issued ones to land
+        for (uint32_t g = it > kPairStages ? it - kPairStages : 0; g < it; ++g)
+          mbar_drain(&sm.full[g % kPairStages], (g / kPairStages) & 1, p.status);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_f16(kBF16, 256, kBN, false, false);
+      uint32_t it = 0, tcount = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < tiles; tile += npairs, ++tcount) {
+        const uint32_t acc = tcount % 2;
+        if (tcount >= 2 &&
+            !(ok = mbar_wait(&sm.acc_empty[acc], ((tcount / 2) - 1) & 1, abort_flag, p.status)))
+          break;
+        tc_fence_after();
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const uint32_t s = it % kPairStages;
+          if (!(ok = mbar_wait(&sm.full[s], (it / kPairStages) & 1, abort_flag, p.status))) break;
+          tc_fence_after();
+          const uint32_t abase = smem_u32(sm.a[s]);
+          const uint32_t bbase = smem_u32(sm.b[s]);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_ss_pair(tmem + acc * kBN, smem_desc_sw128(abase + kk * 32, 16, 1024),
+                         smem_desc_sw128(bbase + kk * 32, 16, 1024), idesc,
+                         (kb > 0 || kk > 0) ? 1u : 0u);
+          tc_commit_pair(&sm.empty[s]);
+        }
+        if (ok) tc_commit_pair(&sm.acc_full[acc]);
+      }
+      // every MMA issued here has completed once `drain` fires (a cta_group::2 commit: the kernel
+      // uses one CTA-group width for all its tcgen05 operations)
+      asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                   ::"r"(smem_u32(&sm.drain)) : "memory");
+      mbar_drain(&sm.drain, 0, p.status);
+    }
+  } else if (warp >= kEpiWarp0) {
+    const int quarter = (warp - kEpiWarp0) % 4;
+    const int hb = (warp - kEpiWarp0) / 4;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    uint32_t tcount = 0;
+    bool ok = true;
+    for (int tile = pair; tile < tiles; tile += npairs, ++tcount) {
+      const uint32_t acc = tcount % 2;
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(&sm.acc_full[acc], (tcount / 2) & 1, abort_flag, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
+      const int64_t m = int64_t(mt) * 256 + rank * 128 + quarter * 32 + lane;
+      head_block<kBF16, kCos, kRope>(p, tmem + lane_off + acc * kBN + hb * 128, m,
+                                     nt * kBN + hb * 128);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(peer_addr(&sm.acc_empty[acc], 0));
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();   // the peer is done with this CTA's memory and TMEM
+  tc_fence_after();
+  if (warp == kMmaWarp)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
 }
 
 // rows x cols 16-bit matrix, box 64 columns x box_rows rows, 128-byte swizzle
@@ -329,6 +545,25 @@ cudaError_t launch_t(const CUtensorMap& tx, const CUtensorMap& tw, const Params&
   return cudaGetLastError();
 }
 
+template <bool kBF16, bool kCos, bool kRope>
+cudaError_t launch_pair_t(const CUtensorMap& tx, const CUtensorMap& tw, const Params& p, int grid,
+                          cudaStream_t st) {
+  auto kern = qkv_project_pair_kernel<kBF16, kCos, kRope>;
+  const size_t smem = sizeof(PairSmem) + 1024;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    attr_set[dev & 63] = true;
+  }
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, st, tx, tw, p);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 }  // namespace qkvproj
 }  // namespace sm100
 
@@ -342,8 +577,12 @@ cudaError_t launch_qkv_project(const void* x, const void* w, void* q, void* k, v
   using namespace sm100::qkvproj;
   CUtensorMap tx, tw;
   const int64_t M = batch * seq_len;
+  // CTA pairs (256 x 256 tiles) unless HEATKV_QKV_PROJECT_PAIR=0
+  const char* pair_env = std::getenv("HEATKV_QKV_PROJECT_PAIR");
+  const bool use_pair = !(pair_env && pair_env[0] == '0');
+  const int wbox = use_pair ? 128 : kBN;
   if (!encode_matrix(&tx, x, M, embed_dim, bf16, kBM) ||
-      !encode_matrix(&tw, w, 3 * heads * 128, embed_dim, bf16, kBN))
+      !encode_matrix(&tw, w, 3 * heads * 128, embed_dim, bf16, wbox))
     return cudaErrorInvalidValue;
   Params p{};
   p.rows = M;
@@ -365,8 +604,19 @@ cudaError_t launch_qkv_project(const void* x, const void* w, void* q, void* k, v
   p.cache_rows = cache_rows;
   p.cache_offset = cache_offset;
   p.status = status;
-  const int grid = static_cast<int>(std::min<int64_t>(p.tiles, sm100::sm_count()));
   const bool cos = scale_mul != nullptr, rope = rope_cos != nullptr;
+  if (use_pair) {
+    const int64_t pair_tiles = (M + 255) / 256 * p.n_tiles;
+    const int grid = 2 * static_cast<int>(std::min<int64_t>(pair_tiles, sm100::sm_count() / 2));
+#define HEATKV_QKV_PROJ_PAIR(B)                                                      \
+  (cos && rope ? launch_pair_t<B, true, true>(tx, tw, p, grid, st)                   \
+   : cos       ? launch_pair_t<B, true, false>(tx, tw, p, grid, st)                  \
+   : rope      ? launch_pair_t<B, false, true>(tx, tw, p, grid, st)                  \
+               : launch_pair_t<B, false, false>(tx, tw, p, grid, st))
+    return bf16 ? HEATKV_QKV_PROJ_PAIR(true) : HEATKV_QKV_PROJ_PAIR(false);
+#undef HEATKV_QKV_PROJ_PAIR
+  }
+  const int grid = static_cast<int>(std::min<int64_t>(p.tiles, sm100::sm_count()));
 #define HEATKV_QKV_PROJ(B)                                                           \
   (cos && rope ? launch_t<B, true, true>(tx, tw, p, grid, st)                        \
    : cos       ? launch_t<B, true, false>(tx, tw, p, grid, st)                       \

@@ -38,3 +38,22 @@ def test_sharded_hot_path_across_gpus(split, exchange):
     tail = (res.stdout + res.stderr)[-3000:]
     assert res.returncode == 0, tail
     assert "multi-GPU parity ok" in res.stdout, tail
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+def test_projected_workload_sharded_by_rows_across_gpus():
+    """configs[4]'s projection-driven path with the batch sharded by rows over two GPUs: the
+    gathered outputs equal one GPU's bit for bit, and match keep-mask attention."""
+    n = 2
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", f"--nproc-per-node={n}", "--master-addr=127.0.0.1", "--master-port=29563",
+           os.path.join(HERE, "projected_multi_worker.py")]
+    res = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    log = os.environ.get("HEATKV_MULTI_GPU_LOG")
+    if log:
+        with open(f"{log}.projected", "w") as fh:
+            fh.write(res.stdout + res.stderr)
+    tail = (res.stdout + res.stderr)[-3000:]
+    assert res.returncode == 0, tail
+    assert "projected multi-GPU parity ok" in res.stdout, tail
