@@ -774,22 +774,38 @@ def run_projected(args, rank: int, world: int, local_rank: int) -> None:
     ctrl, layers, heads = build_controller(args.model, args.budget)
     costs = sharding.head_costs(ctrl, layers, heads)
     plan = sharding.plan_shards(costs, args.global_rows, world, split=args.shard)
-    if plan.splits_heads:
-        raise SystemExit("the projected workload shards rows only: use a row count that divides "
-                         "over the GPUs")
     rows = plan.rows_per_rank
-    hot = HotPath(ctrl, layers, heads, rows, dev, torch.bfloat16, torch.bfloat16)
-    proj = ProjectedHotPath(hot, weight_seed=0, fused_projection=not args.unfused_projection)
+    sh = None
+    if plan.splits_heads:
+        # heads split over the GPUs: each rank projects and attends its heads of its rows, and
+        # every attention output is exchanged so each rank holds the full [rows, n, H * D]
+        sh = sharding.ShardedHotPath(ctrl, layers, heads, plan, rank, dev, torch.bfloat16,
+                                     torch.bfloat16, gather=True, exchange=args.exchange)
+        hot = sh.local
+        proj = ProjectedHotPath(hot, global_heads=[plan.heads_of(rank, l) for l in range(layers)],
+                                embed_dim=heads * 128, weight_seed=0,
+                                fused_projection=not args.unfused_projection)
+    else:
+        hot = HotPath(ctrl, layers, heads, rows, dev, torch.bfloat16, torch.bfloat16)
+        proj = ProjectedHotPath(hot, weight_seed=0, fused_projection=not args.unfused_projection)
     x, x_flat = proj.allocate_inputs(plan.rows_of(rank), seed=1)
     out, out_flat = proj.allocate_outputs()
     launches = proj.launches(x, out)
+    if sh is not None:
+        full, full_flat = sh.allocate_full_outputs(plan.batch, heads, per_layer=False)
+        gbuf = sh.allocate_gather_buffer()
+        launches = sh.exchange(launches, out, full, gbuf)
+        out, out_flat = full, full_flat   # the step's result: every rank's full outputs
+    xchg_kinds = ("allgather", "gather", "barrier")
+    xchg_bytes = sum(l.work for l in launches if l.kind == "allgather")
     att_flops = sum(l.work for l in launches if l.kind == "attention")
     gemm_flops = sum(l.work for l in launches if l.kind in ("gemm", "proj"))
     pack_bytes = sum(l.work for l in launches if l.kind == "pack")
     prep_bytes = sum(l.work for l in launches if l.kind == "prep")
     proj_bytes = sum(l.nbytes for l in launches if l.kind == "proj")
     n_att = sum(1 for l in launches if l.kind == "attention")
-    n_own = sum(1 for l in launches if l.kind in ("attention", "pack", "prep", "proj"))
+    n_own = sum(1 for l in launches if l.kind in ("attention", "pack", "prep", "proj", "gather",
+                                                   "barrier"))
 
     stream = torch.cuda.Stream(dev)
     stream.wait_stream(torch.cuda.current_stream(dev))
@@ -804,9 +820,10 @@ def run_projected(args, rank: int, world: int, local_rank: int) -> None:
     step_ms, clocks = _timed_replays(step_graph, args.steps, stream, dev, world, local_rank)
     if world > 1:
         dist.barrier()
-    kinds = ("proj", "gemm", "prep", "attention", "pack")
+    kinds = ("proj", "gemm", "prep", "attention", "pack") + xchg_kinds
     by_kind, by_target, step_ms_events = _attribution(proj, launches, stream,
                                                       max(1, args.attrib_steps), kinds)
+    xchg_ms = sum(by_kind[k] for k in xchg_kinds)
     status = _native.device_status(dev)
 
     # e2e: the layer inputs of each scale come from pinned host memory (copy stream, in scale
@@ -872,13 +889,16 @@ def run_projected(args, rank: int, world: int, local_rank: int) -> None:
     d2h = out_flat.numel() * out_flat.element_size()
 
     vals = torch.tensor([step_ms, e2e_ms, by_kind["attention"], by_kind["pack"], by_kind["prep"],
-                         by_kind["gemm"], by_kind["proj"], float(status)], dtype=torch.float64,
-                        device=dev)
+                         by_kind["gemm"], by_kind["proj"], xchg_ms, float(status)],
+                        dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    step_ms, e2e_ms, att_ms, pack_ms, prep_ms, gemm_ms, proj_ms, status = vals.tolist()
+    step_ms, e2e_ms, att_ms, pack_ms, prep_ms, gemm_ms, proj_ms, xchg_ms, status = vals.tolist()
+    # graphs that hold NCCL work are released before the process group goes away
     del step_graph
     torch.cuda.synchronize(dev)
+    if sh is not None:
+        sh.close()   # collective: peer-shared buffers are unmapped and freed on every rank
     if rank != 0:
         return
 
@@ -899,7 +919,11 @@ def run_projected(args, rank: int, world: int, local_rank: int) -> None:
         "config": config_of(args),
         "details": {
             "rows_per_gpu": rows, "row_groups": plan.row_groups, "head_groups": plan.head_groups,
-            "exchange": "none: rows only, every output row is used on the GPU that computed it",
+            "exchange": ({"kind": args.exchange, "ms_per_step": round(xchg_ms, 3),
+                          "gb_all_gathered_per_step_per_gpu": round(xchg_bytes / 1e9, 3),
+                          "head_imbalance": round(plan.imbalance(costs), 4)}
+                         if sh is not None else
+                         "none: rows only, every output row is used on the GPU that computed it"),
             "images_per_step": images, "mode": "cuda-graph replay of the whole step",
             "attention_tflop_per_step_per_gpu": round(att_flops / 1e12, 3),
             "qkv_gemm_tflop_per_step_per_gpu": round(gemm_flops / 1e12, 3),

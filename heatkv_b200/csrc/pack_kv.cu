@@ -3,11 +3,13 @@
 // Same copy as the reference's _pack_flat_segments_kv_kernel (real_pruning_fused_attention.py:33-73):
 //   dst[b, dst_start + t, :] = src[b, src_start + t, :]   for every item, t < length, K and V.
 // The reference launches a (batch, item, 32-token chunk) grid of masked scalar element copies.
-// Here the copy is pure bytes: each block moves a chunk of rows of one item for one batch row,
+// Here the copy is pure bytes: each block moves chunks of rows of one item for one batch row,
 // K then V, with 16-byte vector loads/stores when the rows allow it (256-byte bf16 rows, 512-byte
 // fp32 rows), all loads of a thread issued before its stores. The kernel is HBM-bound: every byte
 // is read once and written once. Descriptors are bounds-checked on the device; an item reaching
 // outside its tensor is skipped and flagged instead of corrupting memory.
+#include <algorithm>
+
 #include "attn.h"
 #include "common.cuh"
 
@@ -54,7 +56,9 @@ struct PackArgs {
   unsigned int* status;
 };
 
-// grid = (row chunks, items, batch rows)
+// grid = (chunk slots, items, batch rows): block x copies row chunks x, x + gridDim.x, ... of its
+// item, so the launcher sizes gridDim.x to the work (many items: one block per item and batch
+// row, none idle on short items; few items: the chunks of long ones spread over many blocks)
 template <typename VK, typename VV>
 __global__ void __launch_bounds__(kPackThreads) pack_kv_kernel(PackArgs a) {
   pdl_trigger();
@@ -62,24 +66,26 @@ __global__ void __launch_bounds__(kPackThreads) pack_kv_kernel(PackArgs a) {
   const int64_t item = blockIdx.y;
   const int64_t b = blockIdx.z;
   const int64_t len = a.lengths[item];
-  const int64_t row0 = int64_t(blockIdx.x) * kPackRowsPerBlock;
-  if (row0 >= len) return;
+  if (int64_t(blockIdx.x) * kPackRowsPerBlock >= len) return;
   const int64_t d0 = a.dst_starts[item];
   const int64_t s0 = a.src_starts[item];
   if (len < 0 || d0 < 0 || s0 < 0 || d0 + len > a.dst_rows || s0 + len > a.src_rows) {
     if (blockIdx.x == 0 && threadIdx.x == 0) raise_status(a.status, HEATKV_DEVICE_PACK_OUT_OF_RANGE);
     return;
   }
-  const int64_t rows = min(int64_t(kPackRowsPerBlock), len - row0);
-  {
-    const int64_t rb = a.row_bytes_k;
-    copy_rows<VK>(a.dst_k + ((b * a.dst_rows) + d0 + row0) * rb,
-                  a.src_k + ((b * a.src_rows) + s0 + row0) * rb, rows * rb);
-  }
-  {
-    const int64_t rb = a.row_bytes_v;
-    copy_rows<VV>(a.dst_v + ((b * a.dst_rows) + d0 + row0) * rb,
-                  a.src_v + ((b * a.src_rows) + s0 + row0) * rb, rows * rb);
+  for (int64_t row0 = int64_t(blockIdx.x) * kPackRowsPerBlock; row0 < len;
+       row0 += int64_t(gridDim.x) * kPackRowsPerBlock) {
+    const int64_t rows = min(int64_t(kPackRowsPerBlock), len - row0);
+    {
+      const int64_t rb = a.row_bytes_k;
+      copy_rows<VK>(a.dst_k + ((b * a.dst_rows) + d0 + row0) * rb,
+                    a.src_k + ((b * a.src_rows) + s0 + row0) * rb, rows * rb);
+    }
+    {
+      const int64_t rb = a.row_bytes_v;
+      copy_rows<VV>(a.dst_v + ((b * a.dst_rows) + d0 + row0) * rb,
+                    a.src_v + ((b * a.src_rows) + s0 + row0) * rb, rows * rb);
+    }
   }
 }
 
@@ -96,8 +102,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kv_batched_kernel(
   const int64_t item = blockIdx.y;
   const int64_t b = blockIdx.z;
   const int64_t len = lengths[item];
-  const int64_t row0 = int64_t(blockIdx.x) * kPackRowsPerBlock;
-  if (row0 >= len) return;
+  if (int64_t(blockIdx.x) * kPackRowsPerBlock >= len) return;
   const int64_t jid = item_job[item];
   if (jid < 0 || jid >= n_jobs) {
     if (blockIdx.x == 0 && threadIdx.x == 0) raise_status(status, HEATKV_DEVICE_PACK_OUT_OF_RANGE);
@@ -110,13 +115,25 @@ __global__ void __launch_bounds__(kPackThreads) pack_kv_batched_kernel(
     if (blockIdx.x == 0 && threadIdx.x == 0) raise_status(status, HEATKV_DEVICE_PACK_OUT_OF_RANGE);
     return;
   }
-  const int64_t rows = min(int64_t(kPackRowsPerBlock), len - row0);
-  copy_rows<VK>(static_cast<char*>(jb.dst_k) + ((b * jb.dst_rows) + d0 + row0) * row_bytes_k,
-                static_cast<const char*>(jb.src_k) + ((b * jb.src_rows) + s0 + row0) * row_bytes_k,
-                rows * row_bytes_k);
-  copy_rows<VV>(static_cast<char*>(jb.dst_v) + ((b * jb.dst_rows) + d0 + row0) * row_bytes_v,
-                static_cast<const char*>(jb.src_v) + ((b * jb.src_rows) + s0 + row0) * row_bytes_v,
-                rows * row_bytes_v);
+  for (int64_t row0 = int64_t(blockIdx.x) * kPackRowsPerBlock; row0 < len;
+       row0 += int64_t(gridDim.x) * kPackRowsPerBlock) {
+    const int64_t rows = min(int64_t(kPackRowsPerBlock), len - row0);
+    copy_rows<VK>(static_cast<char*>(jb.dst_k) + ((b * jb.dst_rows) + d0 + row0) * row_bytes_k,
+                  static_cast<const char*>(jb.src_k) + ((b * jb.src_rows) + s0 + row0) * row_bytes_k,
+                  rows * row_bytes_k);
+    copy_rows<VV>(static_cast<char*>(jb.dst_v) + ((b * jb.dst_rows) + d0 + row0) * row_bytes_v,
+                  static_cast<const char*>(jb.src_v) + ((b * jb.src_rows) + s0 + row0) * row_bytes_v,
+                  rows * row_bytes_v);
+  }
+}
+
+// Blocks per (item, batch row): enough that the launch has ~32 blocks per SM when the items are
+// few, one when there are many (each block then loops over its item's chunks).
+static unsigned chunk_slots(int64_t max_length, int64_t n_items, int64_t batch) {
+  const int64_t chunks = (max_length + kPackRowsPerBlock - 1) / kPackRowsPerBlock;
+  const int64_t want = int64_t(148) * 32;
+  const int64_t per = (want + n_items * batch - 1) / (n_items * batch);
+  return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(chunks, per)));
 }
 
 static int vec_width(const void* p0, const void* p1, int64_t row_bytes) {
@@ -148,8 +165,7 @@ cudaError_t launch_pack_kv(void* dst_k, void* dst_v, const void* src_k, const vo
   PackArgs a{static_cast<char*>(dst_k), static_cast<char*>(dst_v),
              static_cast<const char*>(src_k), static_cast<const char*>(src_v),
              row_bytes_k, row_bytes_v, src_rows, dst_rows, dst_starts, src_starts, lengths, status};
-  const int64_t chunks = (max_length + kPackRowsPerBlock - 1) / kPackRowsPerBlock;
-  dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(n_items),
+  dim3 grid(chunk_slots(max_length, n_items, batch), static_cast<unsigned>(n_items),
             static_cast<unsigned>(batch));
   const int wk = vec_width(dst_k, src_k, row_bytes_k);
   const int wv = vec_width(dst_v, src_v, row_bytes_v);
@@ -192,8 +208,7 @@ cudaError_t launch_pack_kv_batched(const heatkv_pack_job* jobs, int64_t n_jobs,
                                    int64_t n_items, int64_t row_bytes_k, int64_t row_bytes_v,
                                    int64_t batch, int64_t max_length, int max_vector_bytes,
                                    unsigned int* status, cudaStream_t stream) {
-  const int64_t chunks = (max_length + kPackRowsPerBlock - 1) / kPackRowsPerBlock;
-  dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(n_items),
+  dim3 grid(chunk_slots(max_length, n_items, batch), static_cast<unsigned>(n_items),
             static_cast<unsigned>(batch));
   const int wk = width_of(row_bytes_k, max_vector_bytes);
   const int wv = width_of(row_bytes_v, max_vector_bytes);

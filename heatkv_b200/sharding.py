@@ -326,7 +326,7 @@ class ShardedHotPath:
                  exchange: str = "nccl", plan_splits=None):
         if exchange not in ("nccl", "p2p"):
             raise ValueError("exchange must be 'nccl' or 'p2p'")
-        self.exchange = exchange
+        self.exchange_kind = exchange
         self.plan = plan
         self.rank = int(rank)
         self.device = torch.device(device)
@@ -358,14 +358,16 @@ class ShardedHotPath:
             return _native.HEATKV_OK
         return run
 
-    def allocate_full_outputs(self, batch_rows: int, num_heads: int, dtype=torch.bfloat16):
+    def allocate_full_outputs(self, batch_rows: int, num_heads: int, dtype=torch.bfloat16,
+                              per_layer: bool = True):
         """The ``[B, n_t, H * D]`` outputs of every (layer, scale) as views of one flat buffer,
-        ``full[i][t]``, and the flat buffer. With the p2p exchange every rank's buffer is also
-        mapped here (collective: every rank calls this once, in the same order)."""
+        ``full[i][t]``, and the flat buffer; with ``per_layer=False`` one output per scale shared
+        by the layers, ``full[t]``. With the p2p exchange every rank's buffer is also mapped here
+        (collective: every rank calls this once, in the same order)."""
         n_tot = sum(self.tokens)
-        per_layer = batch_rows * n_tot * num_heads * self.head_dim
-        total = len(self.local.plans) * per_layer
-        if self.exchange == "p2p":
+        per_layer_elems = batch_rows * n_tot * num_heads * self.head_dim
+        total = (len(self.local.plans) if per_layer else 1) * per_layer_elems
+        if self.exchange_kind == "p2p":
             itemsize = torch.empty(0, dtype=dtype).element_size()
             self._full_buf = PeerBuffer(total * itemsize, dtype, self.device, self.group)
             flat = self._full_buf.local
@@ -376,14 +378,14 @@ class ShardedHotPath:
         else:
             flat = torch.zeros(total, dtype=dtype, device=self.device)
         full, off = [], 0
-        for _ in self.local.plans:
+        for _ in (self.local.plans if per_layer else [None]):
             row = []
             for n in self.tokens:
                 sz = batch_rows * n * num_heads * self.head_dim
                 row.append(flat[off:off + sz].view(batch_rows, n, num_heads * self.head_dim))
                 off += sz
             full.append(row)
-        return full, flat
+        return (full if per_layer else full[0]), flat
 
     def close(self) -> None:
         """Release the peer-shared buffers (collective; after the last step has completed)."""
@@ -409,13 +411,22 @@ class ShardedHotPath:
         base = self.local.launches(inputs, outputs, **kw)
         if not self.gather:
             return base
-        if self.exchange == "p2p":
+        return self.exchange(base, outputs, full_outputs, gather_buf)
+
+    def exchange(self, base, outputs, full_outputs, gather_buf=None) -> list:
+        """``base`` (any launch list of ``self.local`` whose attention launches write
+        ``outputs[i][t]``, or ``outputs[t]`` when one output per scale is shared by the layers)
+        with the exchange that gives every rank the full output ``full_outputs[i][t]`` (or
+        ``full_outputs[t]``) of each attention: NCCL all-gather + placement, or the peer-to-peer
+        scatter + barrier."""
+        if self.exchange_kind == "p2p":
             return self._p2p_launches(base, full_outputs)
         if full_outputs is None or gather_buf is None:
             raise ValueError("gathering needs full_outputs and gather_buf")
         p = self.plan
         lib = self.local.lib
         dt = _native.DTYPE_CODES
+        shared = not isinstance(outputs[0], (list, tuple))
         out = []
         for launch in base:
             out.append(launch)
@@ -424,8 +435,8 @@ class ShardedHotPath:
             layer, t = launch.layer, launch.target
             i = self.plan_index[layer]
             n = self.tokens[t]
-            local = outputs[i][t]
-            full = full_outputs[i][t]
+            local = outputs[t] if shared else outputs[i][t]
+            full = full_outputs[t] if shared else full_outputs[i][t]
             nbytes = float(p.world * local.numel() * local.element_size())
             if not p.splits_heads:
                 # rank r holds rows [r * rows, (r + 1) * rows): the gather is the output itself
@@ -457,7 +468,8 @@ class ShardedHotPath:
                 continue
             layer, t = launch.layer, launch.target
             i = self.plan_index[layer]
-            full = full_outputs[i][t]
+            shared = not isinstance(full_outputs[0], (list, tuple))
+            full = full_outputs[t] if shared else full_outputs[i][t]
             off = full.data_ptr() - self._full_buf.local.data_ptr()
             ptrs = torch.tensor([b + off for b in self._full_buf.ptrs], dtype=torch.int64,
                                 device=self.device)
