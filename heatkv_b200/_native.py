@@ -22,11 +22,11 @@ HEATKV_ERR_CUDA = -3
 
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
-ATTN_AUTO, ATTN_EXACT, ATTN_TCGEN05, ATTN_TCGEN05_PAIR, ATTN_TCGEN05_CS = 0, 1, 2, 3, 4
+ATTN_AUTO, ATTN_EXACT, ATTN_TCGEN05, ATTN_TCGEN05_CS = 0, 1, 2, 4  # 3: retired
 ATTN_TCGEN05_CS64 = 5
 ATTN_STATIC_META = 0x100  # OR into a selector: metadata not written by preceding work
 ATTN_CURRENT_IN_SEGMENTS = 0x200  # OR into a selector: current keys end every head's segments
-RUN_EXACT, RUN_TCGEN05_PAIR, RUN_TCGEN05_CS, RUN_TCGEN05_TF32 = 1, 2, 3, 4  # heatkv_attn_run
+RUN_EXACT, RUN_TCGEN05_CS, RUN_TCGEN05_TF32 = 1, 3, 4  # heatkv_attn_run (2: retired)
 RUN_TCGEN05_CS64 = 5
 
 DEVICE_PACK_OUT_OF_RANGE = 0x1
@@ -80,7 +80,7 @@ SIGNATURES = {
                                 ctypes.c_float, _p, _p, _i64, _p]),
     "heatkv_qkv_prepare_append": (_i, [_p, _p, _p, _p, _i, _i, _i64, _i64, _i64, _i64, _p,
                                        ctypes.c_float, _p, _p, _i64, _p, _p, _i64, _p, _p]),
-    "heatkv_qkv_project": (_i, [_p, _p, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p,
+    "heatkv_qkv_project": (_i, [_p, _p, _p, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p,
                                 ctypes.c_float, _p, _p, _i64, _p, _p, _i64, _p, _p]),
     "heatkv_slot_tables": (_i, [_i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "heatkv_strict_budget": (_i, [_p, _i, _i, _i, _i, _p, _i, _i, _i, ctypes.c_double, _p, _p,

@@ -54,8 +54,6 @@ constexpr int kMaxSegments = 256;
 
 cudaError_t launch_attention_simt(const AttnArgs& a, int q_dtype, int k_dtype, int v_dtype,
                                   cudaStream_t st);
-// Returns cudaErrorNotSupported when the tensor-core kernel cannot take these arguments.
-cudaError_t launch_attention_sm100(const AttnArgs& a, bool bf16, cudaStream_t st);
 // Column-split kernels (attn_sm100_cs.cu): one 128-row Q tile per CTA, the softmax of a tile
 // split by columns over warpgroups, unsplit; cudaErrorNotSupported when they cannot take these
 // arguments. _cs: q, k, v all bf16 or all f16 (scatter epilogue supported); _tf32: fp32 q and k
@@ -65,9 +63,6 @@ cudaError_t launch_attention_sm100_cs(const AttnArgs& a, bool bf16, cudaStream_t
 cudaError_t launch_attention_sm100_cs64(const AttnArgs& a, bool bf16, cudaStream_t st);
 // kv_splits = 0 for the 64-key kernel: enough splits of every 128-row block for two waves
 int attention_cs64_auto_splits(int64_t batch, int64_t heads, int64_t q_len);
-// Unsplit 16-bit calls: whether the two-tile kernel (256-row blocks) is expected to beat the
-// column-split kernel (128-row items) on this shape.
-bool attention_prefers_pair(int64_t batch, int64_t heads, int64_t q_len);
 cudaError_t launch_attention_sm100_tf32(const AttnArgs& a, bool v_bf16, cudaStream_t st);
 // Splits chosen by kv_splits = 0 and the workspace bytes a launch with `splits` needs.
 // Key-range split scratch shared by the tcgen05 kernels: per split block a counter (zero between
@@ -86,7 +81,6 @@ struct SplitScratch {
 bool split_scratch(void* ws, size_t bytes, int64_t split_blocks, int splits, int rows_per_block,
                    SplitScratch* out);
 
-int attention_auto_splits(int64_t batch, int64_t heads, int64_t q_len);
 // kv_splits = 0 for the column-split kernel: enough splits of every 128-row block for two waves
 int attention_cs_auto_splits(int64_t batch, int64_t heads, int64_t q_len);
 size_t attention_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int splits);
@@ -124,8 +118,8 @@ cudaError_t launch_scas_mass(const void* q, const void* k, int dtype, int64_t he
                              double* mass_out, int64_t mass_stride, cudaStream_t st);
 
 // q/k/v preparation after the QKV projection (qkv_prep.cu); sms = SMs of the device.
-cudaError_t launch_qkv_project(const void* x, const void* w, void* q, void* k, void* v,
-                               bool bf16, int64_t batch, int64_t seq_len, int64_t heads,
+cudaError_t launch_qkv_project(const void* x, const void* w, const float* bias, void* q, void* k,
+                               void* v, bool bf16, int64_t batch, int64_t seq_len, int64_t heads,
                                int64_t embed_dim, const float* scale_mul, float eps,
                                const float* rope_cos, const float* rope_sin,
                                int64_t rope_row_stride, void* cache_k, void* cache_v,

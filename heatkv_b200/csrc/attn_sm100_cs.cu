@@ -12,9 +12,12 @@
 //     is kind::tf32. An fp32 Q tile (64 KiB) does not fit shared memory beside an fp32 K ring, so
 //     Q is the A operand from TMEM, staged (fp32 -> tf32, round to nearest) by the softmax warps.
 //
-// TMEM (512 columns): 16-bit: S_0 S_1 S_2 | O; tf32: Q | S_0 S_1 | O. Key tile g uses S buffer
-// g % kNumS and K/V stage g % 2. P of tile g is stored as 16-bit pairs over the first 64 columns
-// of its S buffer once every warpgroup holds its scores in registers.
+// TMEM (512 columns): tf32: Q | S_0 S_1 | O (one O shared by the warpgroups); 16-bit: the
+// independent halves below. Key tile g uses S buffer g % kNumS and K/V stage g % 2. P of tile g
+// is stored as 16-bit pairs over the first 64 columns of its S buffer once every warpgroup holds
+// its scores in registers. (The kernel is written for kWG warpgroups and a shared O in 16-bit mode
+// too - S_0 S_1 S_2 | O -, but the library instantiates two warpgroups, the shared O for tf32 and
+// the independent halves for 16-bit, the fastest measured.)
 //
 // Per key tile, warpgroup w of kWG takes the keys [w*128/kWG, (w+1)*128/kWG) of every query row
 // (one TMEM lane per thread); the part-row maxima meet in shared memory behind a named barrier;
@@ -919,25 +922,6 @@ static bool encode_rows_f32(CUtensorMap* map, const void* base, int64_t rows) {
   return r == CUDA_SUCCESS;
 }
 
-// Softmax warpgroups per CTA: HEATKV_CS_WARPGROUPS = 2 or 4 (default 2).
-static int softmax_warpgroups() {
-  static const int v = [] {
-    const char* e = getenv("HEATKV_CS_WARPGROUPS");
-    return (e && atoi(e) == 4) ? 4 : 2;
-  }();
-  return v;
-}
-
-// 16-bit mode: independent halves (default) or one O shared by the warpgroups
-// (HEATKV_CS_INDEPENDENT = 0; 2-5 % slower, kept for measurement).
-static bool independent_halves() {
-  static const bool v = [] {
-    const char* e = getenv("HEATKV_CS_INDEPENDENT");
-    return !(e && atoi(e) == 0);
-  }();
-  return v;
-}
-
 template <bool kTf32, bool kBF16, int kWG, bool kIndep = false>
 static cudaError_t launch_t(const CUtensorMap& tq, const CUtensorMap& tck, const CUtensorMap& tcv,
                             const CUtensorMap& tsk, const CUtensorMap& tsv, const Params& p,
@@ -1047,44 +1031,20 @@ static cudaError_t launch_mode(const AttnArgs& a, cudaStream_t st) {
   p.out_batch = static_cast<int>(a.out_batch);
   p.out_heads_total = static_cast<int>(a.out_heads_total);
   const int mg = a.map_grid;
-  if (softmax_warpgroups() == 4) return launch_t<kTf32, kBF16, 4>(tq, tck, tcv, tsk, tsv, p, mg, st);
-  if constexpr (!kTf32) {
-    if (independent_halves())
-      return launch_t<false, kBF16, 2, true>(tq, tck, tcv, tsk, tsv, p, mg, st);
-  }
+  // two softmax warpgroups; 16-bit mode with independent halves (each warpgroup its own keys and
+  // its own O), tf32 mode with one O shared by the warpgroups
+  if constexpr (!kTf32) return launch_t<false, kBF16, 2, true>(tq, tck, tcv, tsk, tsv, p, mg, st);
   return launch_t<kTf32, kBF16, 2>(tq, tck, tcv, tsk, tsv, p, mg, st);
 }
 
 }  // namespace cs
 }  // namespace sm100
 
-// Cost model of an unsplit launch, fitted to the B200 per-target attention times of the 2B image
-// at 2, 4, 8 and 16 rows and the 8B image at 8 rows (13 targets each, both kernels): each
-// kernel's query rows padded to its block height (256 or 128), divided by the wave efficiency of
-// its block count over the SMs (blocks / (waves * SMs)); the column-split kernel's cost per row
-// relative to the two-tile kernel's is 0.80 + 0.28 * min(1, two-tile blocks / 512): lower on small
-// launches (twice the CTAs, two issuers), up to 8 % higher on large ones (128-row items read each
-// K/V tile for half the rows). Over those 65 launches its choices came within 0.3 % of the
-// per-launch best and leave the 2-row image (the headline configuration) entirely on the
-// column-split kernel.
 int attention_cs_auto_splits(int64_t batch, int64_t heads, int64_t q_len) {
   const int64_t blocks = batch * heads * ((q_len + sm100::cs::kBM - 1) / sm100::cs::kBM);
   const int64_t target = 2 * int64_t(sm100::sm_count());
   if (blocks <= 0 || blocks >= target) return 1;
   return static_cast<int>(std::min<int64_t>(kMaxKvSplits, (target + blocks - 1) / blocks));
-}
-
-bool attention_prefers_pair(int64_t batch, int64_t heads, int64_t q_len) {
-  using namespace sm100;
-  const double sms = static_cast<double>(sm_count());
-  auto eff = [sms](double n) { return n / (std::ceil(n / sms) * sms); };
-  const double pair_rows = static_cast<double>((q_len + 255) / 256 * 256);
-  const double cs_rows = static_cast<double>((q_len + 127) / 128 * 128);
-  const double pair_blocks = static_cast<double>(batch * heads) * (pair_rows / 256.0);
-  const double cs_items = static_cast<double>(batch * heads) * (cs_rows / 128.0);
-  if (pair_blocks <= 0.0) return false;
-  const double cs_factor = 0.80 + 0.28 * std::min(1.0, pair_blocks / 512.0);
-  return pair_rows / eff(pair_blocks) < cs_rows * cs_factor / eff(cs_items);
 }
 
 cudaError_t launch_attention_sm100_tf32(const AttnArgs& a, bool v_bf16, cudaStream_t st) {

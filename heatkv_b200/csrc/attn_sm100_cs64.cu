@@ -109,6 +109,7 @@ struct Params {
   int seg_stride;
   int static_meta;
   int current_in_segments;
+  int out_align32;      // out is 32-byte aligned: 32-byte stores in the epilogue
 };
 
 struct Item {
@@ -573,7 +574,9 @@ __global__ void __launch_bounds__(kThreads, 2)
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.p_full[b]);
+          // P is in TMEM (tcgen05.wait::st): as for o_free, a relaxed arrive, which does not wait
+          // for the previous item's output stores
+          if (lane == 0) mbar_arrive_relaxed(&sm.p_full[b]);
         }
         cur.next();
       }
@@ -607,15 +610,23 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
               for (int i = 0; i < 8; ++i)
                 wv[i] = pack2<kBF16>(o[cc * 16 + 2 * i] * inv, o[cc * 16 + 2 * i + 1] * inv);
-              uint4* dst = reinterpret_cast<uint4*>(orow + 32 * half + 16 * cc);
-              dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-              dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+              if (p.out_align32) {
+                // one full 32-byte sector per store: half the store instructions of 16-byte
+                // vectors, and no partial-sector writes (each thread writes its own row)
+                st_global_v8(orow + 32 * half + 16 * cc, wv);
+              } else {
+                uint4* dst = reinterpret_cast<uint4*>(orow + 32 * half + 16 * cc);
+                dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+              }
             }
           }
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.o_free);
+        // O has been read into registers (tcgen05.wait::ld): the hand-off to the next item's PV
+        // orders nothing else, so the arrive does not wait for the output stores to drain
+        if (lane == 0) mbar_arrive_relaxed(&sm.o_free);
       }
       ++ocnt;
       if (split) split_finish(it);
@@ -737,6 +748,7 @@ cudaError_t launch_attention_sm100_cs64(const AttnArgs& a, bool bf16, cudaStream
   p.seg_stride = static_cast<int>(std::max<int64_t>(a.max_segments, 1));
   p.static_meta = a.static_meta ? 1 : 0;
   p.current_in_segments = a.current_in_segments ? 1 : 0;
+  p.out_align32 = (reinterpret_cast<uintptr_t>(a.out) & 31u) == 0 ? 1 : 0;
   const int grid = use_map ? a.map_grid
                            : static_cast<int>(std::min<int64_t>(n_items, 2 * sm100::sm_count()));
   return bf16 ? launch_t<true>(tq, tck, tcv, tsk, tsv, p, grid, st)

@@ -23,12 +23,11 @@ bool pdl_enabled() {
   return on;
 }
 
-// HEATKV_TCGEN05_VARIANT: "pair" (two Q tiles per CTA; the kernel with key-range splits) or
-// "cs" (one Q tile per CTA, column-split softmax); unset: cs unless splits are asked for.
+// HEATKV_TCGEN05_VARIANT: "cs" (column-split kernel) or "cs64" (64-key kernel) for 16-bit calls
+// that name neither; unset: the 64-key kernel, scattering calls the column-split kernel.
 static int tcgen05_variant() {
   static const int v = [] {
     const char* e = getenv("HEATKV_TCGEN05_VARIANT");
-    if (e && strcmp(e, "pair") == 0) return 1;
     if (e && strcmp(e, "cs") == 0) return 2;
     if (e && strcmp(e, "cs64") == 0) return 3;
     return 0;
@@ -161,26 +160,23 @@ static int plan_attention(int q_dtype, int k_dtype, int v_dtype, int64_t batch, 
                           int64_t q_len, int kernel, int kv_splits, bool has_workspace,
                           int64_t unsplit_blocks, bool scatter, AttnPlan* out) {
   kernel &= ~(HEATKV_ATTN_STATIC_META | HEATKV_ATTN_CURRENT_IN_SEGMENTS);
-  if (kernel < HEATKV_ATTN_AUTO || kernel > HEATKV_ATTN_TCGEN05_CS64)
+  // 3 (the retired two-tile kernel) is no longer a selector
+  if (kernel < HEATKV_ATTN_AUTO || kernel > HEATKV_ATTN_TCGEN05_CS64 || kernel == 3)
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "real_scale_fused_segmented: unknown kernel selector");
-  // the two-tile, column-split or 64-key variant asked for by name; otherwise
-  // HEATKV_TCGEN05_VARIANT
-  const int variant = kernel == HEATKV_ATTN_TCGEN05_PAIR   ? 1
-                    : kernel == HEATKV_ATTN_TCGEN05_CS     ? 2
+  // the column-split or 64-key variant asked for by name; otherwise HEATKV_TCGEN05_VARIANT
+  const int variant = kernel == HEATKV_ATTN_TCGEN05_CS     ? 2
                     : kernel == HEATKV_ATTN_TCGEN05_CS64   ? 3
                                                            : heatkv::tcgen05_variant();
-  const bool named_pair = kernel == HEATKV_ATTN_TCGEN05_PAIR || kernel == HEATKV_ATTN_TCGEN05_CS64;
-  if (kernel == HEATKV_ATTN_TCGEN05_PAIR || kernel == HEATKV_ATTN_TCGEN05_CS ||
-      kernel == HEATKV_ATTN_TCGEN05_CS64)
+  const bool named_cs64 = kernel == HEATKV_ATTN_TCGEN05_CS64;
+  if (kernel == HEATKV_ATTN_TCGEN05_CS || kernel == HEATKV_ATTN_TCGEN05_CS64)
     kernel = HEATKV_ATTN_TCGEN05;
   const bool same16 = (q_dtype == k_dtype && k_dtype == v_dtype && q_dtype != HEATKV_DTYPE_F32);
   // fp32 q and k with 16-bit v (the real model's dtypes): tf32 QK, P rounded to v's dtype
   const bool qk32 = (q_dtype == HEATKV_DTYPE_F32 && k_dtype == HEATKV_DTYPE_F32 &&
                      v_dtype != HEATKV_DTYPE_F32);
-  if (named_pair && !same16)
+  if (named_cs64 && !same16)
     return fail(HEATKV_ERR_UNSUPPORTED,
-                "the two-tile and 64-key tcgen05 kernels need q, k and v all bfloat16 or all "
-                "float16");
+                "the 64-key tcgen05 kernel needs q, k and v all bfloat16 or all float16");
   if (kernel == HEATKV_ATTN_TCGEN05 && !same16 && !(qk32 && !scatter))
     return fail(HEATKV_ERR_UNSUPPORTED,
                 "tcgen05 segmented attention needs q, k and v all bfloat16 or all float16, or q "
@@ -190,16 +186,15 @@ static int plan_attention(int q_dtype, int k_dtype, int v_dtype, int64_t batch, 
     out->run = HEATKV_RUN_TCGEN05_TF32;
   } else if (kernel != HEATKV_ATTN_EXACT && same16) {
     // Default: the 64-key kernel (two CTAs per SM), faster at every launch size measured, with
-    // or without key-range splits (unsplit_blocks counts 128-row blocks for it and the column
-    // split, 256-row blocks for the two-tile kernel). It has no scatter epilogue: scattering calls
-    // take the column-split or two-tile kernel, as the cost model chooses.
+    // or without key-range splits (unsplit_blocks counts 128-row blocks for both kernels). It
+    // has no scatter epilogue: scattering calls take the column-split kernel.
     (void)kv_splits;
     (void)has_workspace;
     (void)unsplit_blocks;
-    bool pair = variant == 1;
-    if (variant == 0) pair = heatkv::attention_prefers_pair(batch, heads, q_len);
-    out->run = pair ? HEATKV_RUN_TCGEN05_PAIR : HEATKV_RUN_TCGEN05_CS;
-    if (!scatter && (variant == 3 || variant == 0)) out->run = HEATKV_RUN_TCGEN05_CS64;
+    (void)batch;
+    (void)heads;
+    (void)q_len;
+    out->run = (!scatter && variant != 2) ? HEATKV_RUN_TCGEN05_CS64 : HEATKV_RUN_TCGEN05_CS;
   } else {
     if (scatter)
       return fail(HEATKV_ERR_UNSUPPORTED,
@@ -275,8 +270,7 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
     if (e == cudaSuccess) return HEATKV_OK;
     if (e != cudaErrorNotSupported || plan.strict)
       return cuda_fail(e, "tcgen05 tf32 segmented attention launch");
-  } else if (plan.run == HEATKV_RUN_TCGEN05_PAIR || plan.run == HEATKV_RUN_TCGEN05_CS ||
-             plan.run == HEATKV_RUN_TCGEN05_CS64) {
+  } else if (plan.run == HEATKV_RUN_TCGEN05_CS || plan.run == HEATKV_RUN_TCGEN05_CS64) {
     const bool bf16 = q_dtype == HEATKV_DTYPE_BF16;
     cudaError_t e = cudaErrorNotSupported;
     if (plan.run == HEATKV_RUN_TCGEN05_CS64) {
@@ -287,8 +281,7 @@ static int attention_impl(const void* q, const void* slab_k, const void* slab_v,
         e = heatkv::launch_attention_sm100_cs(a, bf16, st);
       }
     } else {
-      e = plan.run == HEATKV_RUN_TCGEN05_PAIR ? heatkv::launch_attention_sm100(a, bf16, st)
-                                              : heatkv::launch_attention_sm100_cs(a, bf16, st);
+      e = heatkv::launch_attention_sm100_cs(a, bf16, st);
     }
     if (e == cudaSuccess) return HEATKV_OK;
     if (e == cudaErrorNotSupported && scatter)
@@ -636,7 +629,8 @@ int heatkv_qkv_prepare_append(const void* qkv, void* q, void* k, void* v, int in
                           rope_row_stride, slab_k, slab_v, slab_rows, slab_offset, stream);
 }
 
-int heatkv_qkv_project(const void* x, const void* w, void* q, void* k, void* v, int dtype,
+int heatkv_qkv_project(const void* x, const void* w, const float* bias, void* q, void* k, void* v,
+                       int dtype,
                        int64_t batch, int64_t seq_len, int64_t heads, int64_t embed_dim,
                        const float* scale_mul, float eps, const float* rope_cos,
                        const float* rope_sin, int64_t rope_row_stride, void* cache_k,
@@ -664,7 +658,7 @@ int heatkv_qkv_project(const void* x, const void* w, void* q, void* k, void* v, 
                 "%s: rope_row_stride must be a multiple of 4 and at least 64", name);
   if (!(eps >= 0.f)) return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: eps must be >= 0", name);
   const uintptr_t a16 = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
-                        reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                        reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
                         reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(rope_cos) |
                         reinterpret_cast<uintptr_t>(rope_sin) |
                         reinterpret_cast<uintptr_t>(cache_offset ? cache_k : nullptr) |
@@ -672,7 +666,7 @@ int heatkv_qkv_project(const void* x, const void* w, void* q, void* k, void* v, 
   if ((a16 & 15u) || (reinterpret_cast<uintptr_t>(cache_offset) & 7u))
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: misaligned pointer", name);
   cudaError_t e = heatkv::launch_qkv_project(
-      x, w, q, k, v, dtype == HEATKV_DTYPE_BF16, batch, seq_len, heads, embed_dim, scale_mul, eps,
+      x, w, bias, q, k, v, dtype == HEATKV_DTYPE_BF16, batch, seq_len, heads, embed_dim, scale_mul, eps,
       rope_cos, rope_sin, rope_row_stride, cache_offset ? cache_k : nullptr,
       cache_offset ? cache_v : nullptr, cache_rows, cache_offset, heatkv::device_status_ptr(),
       static_cast<cudaStream_t>(stream));

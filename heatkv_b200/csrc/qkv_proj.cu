@@ -3,7 +3,8 @@
 //
 // The patched attention forward computes, per call (enable_real_pruning_fast.py:2040-2072 and the
 // append of :2218-2225):
-//   qkv = x @ W^T                     x [M = batch * seq_len, C], W [3 * H * 128, C] (nn.Linear)
+//   qkv = x @ W^T + bias              x [M = batch * seq_len, C], W [3 * H * 128, C] (nn.Linear),
+//                                     bias = cat(q_bias, 0, v_bias) or none
 //   q, k, v = qkv.view(B, L, 3, H, 128) permuted to [B, H, L, 128]
 //   q = normalize(q) * scale_mul[h], k = normalize(k)          (cos-attention, fp32)
 //   q, k = 2-D rotary embedding (infinity/models/basic.py:97-117, fp32)
@@ -71,6 +72,7 @@ struct Params {
   void* q;
   void* k;
   void* v;
+  const float* bias;     // [3 * H * 128] fp32, or null
   const float* scale_mul;
   float eps;
   const float* rope_cos;
@@ -83,14 +85,26 @@ struct Params {
   unsigned int* status;
 };
 
+// x[i] += bias[i] for 64 columns (fp32 add, as the GEMM's bias epilogue does before rounding)
+__device__ __forceinline__ void add_bias64(const float4* bias, float (&x)[64]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float4 b = __ldg(bias + j);
+    x[4 * j] += b.x;
+    x[4 * j + 1] += b.y;
+    x[4 * j + 2] += b.z;
+    x[4 * j + 3] += b.w;
+  }
+}
+
 template <bool kBF16>
 __device__ __forceinline__ float round16(float x) {
   if constexpr (kBF16) return __bfloat162float(__float2bfloat16_rn(x));
   else return __half2float(__float2half_rn(x));
 }
 
-// The epilogue of one 128-column head block of this thread's accumulator row: round to the
-// projection dtype, prepare (q/k), store the row and the cache row. The row is read from TMEM in
+// The epilogue of one 128-column head block of this thread's accumulator row: add the bias, round
+// to the projection dtype, prepare (q/k), store the row and the cache row. The row is read from TMEM in
 // two 64-column halves (twice for q/k with cos-attention: once for the norm, once to write), which
 // keeps the live registers of the epilogue warps low. tcgen05.ld is warp-collective, so rows past
 // the end still load and only skip their stores.
@@ -105,6 +119,7 @@ __device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int6
   const int64_t h = (col0 % C) / 128;
   const int64_t b = mm / p.seq_len, l = mm % p.seq_len;
   const bool prep = sec < 2;
+  const float4* bias = p.bias != nullptr ? reinterpret_cast<const float4*>(p.bias + col0) : nullptr;
   float inv_scale = 1.f, n = 1.f;
   if (kCos && prep) {
     float ss = 0.f;
@@ -112,6 +127,7 @@ __device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int6
     for (int half = 0; half < 2; ++half) {
       float x[64];
       tmem_ld_row64(taddr + half * 64, x);
+      if (bias != nullptr) add_bias64(bias + half * 16, x);
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
         const float r = round16<kBF16>(x[i]);
@@ -142,6 +158,7 @@ __device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int6
   for (int half = 0; half < 2; ++half) {
     float x[64];
     tmem_ld_row64(taddr + half * 64, x);
+    if (bias != nullptr) add_bias64(bias + half * 16, x);
 #pragma unroll
     for (int i = 0; i < 64; ++i) x[i] = round16<kBF16>(x[i]);
     if (kCos && prep) {
@@ -567,8 +584,8 @@ cudaError_t launch_pair_t(const CUtensorMap& tx, const CUtensorMap& tw, const Pa
 }  // namespace qkvproj
 }  // namespace sm100
 
-cudaError_t launch_qkv_project(const void* x, const void* w, void* q, void* k, void* v,
-                               bool bf16, int64_t batch, int64_t seq_len, int64_t heads,
+cudaError_t launch_qkv_project(const void* x, const void* w, const float* bias, void* q, void* k,
+                               void* v, bool bf16, int64_t batch, int64_t seq_len, int64_t heads,
                                int64_t embed_dim, const float* scale_mul, float eps,
                                const float* rope_cos, const float* rope_sin,
                                int64_t rope_row_stride, void* cache_k, void* cache_v,
@@ -594,6 +611,7 @@ cudaError_t launch_qkv_project(const void* x, const void* w, void* q, void* k, v
   p.q = q;
   p.k = k;
   p.v = v;
+  p.bias = bias;
   p.scale_mul = scale_mul;
   p.eps = eps;
   p.rope_cos = rope_cos;

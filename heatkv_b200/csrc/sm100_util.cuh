@@ -1,7 +1,6 @@
-// Device and host helpers shared by the tcgen05 attention kernels (attn_sm100.cu,
-// attn_sm100_cs.cu, attn_sm100_cs64.cu): the key-tile cursor over a head's slab segments, TMEM row
-// loads, row maxima, packed fp32x2 arithmetic and exp2 variants, bounded drain waits, and
-// tensor-map encoding.
+// Device and host helpers shared by the tcgen05 kernels (attn_sm100_cs.cu, attn_sm100_cs64.cu,
+// qkv_proj.cu): the key-tile cursor over a head's slab segments, TMEM row loads, row maxima,
+// packed fp32x2 arithmetic, bounded drain waits, and tensor-map encoding.
 #pragma once
 
 #include "common.cuh"
@@ -18,12 +17,14 @@ constexpr int kKeyTile = 128;  // keys per K/V tile of both kernels
 constexpr int kHeadDim = 128;  // the only head dim of the path
 constexpr int kNumSms = 148;
 
-// Walks the key tiles of one head: each segment in kTile-row steps, then the current scale.
+// Walks the key tiles of one head: each segment in kTile-row steps, then the current scale. The
+// end of the segment being walked is held in a register: shared-memory loads wait behind the
+// tensor core's operand reads, so the table is read only when the walk enters a segment.
 template <int kTile>
 struct TileCursorT {
   const int* st;
   const int* en;
-  int nseg, seg, pos;
+  int nseg, seg, pos, end;
   bool current;
   // position on tile j0 of head h
   template <class SmemT>
@@ -41,20 +42,23 @@ struct TileCursorT {
     }
     if (seg < nseg) {
       pos = st[seg] + j0 * kTile;
+      end = en[seg];
     } else {
       current = true;
       pos = j0 * kTile;
+      end = 0;
     }
   }
   __device__ int valid(int q_len) const {
-    return current ? min(kTile, q_len - pos) : min(kTile, en[seg] - pos);
+    return current ? min(kTile, q_len - pos) : min(kTile, end - pos);
   }
   __device__ void next() {
     pos += kTile;
-    if (!current && pos >= en[seg]) {
+    if (!current && pos >= end) {
       ++seg;
       if (seg < nseg) {
         pos = st[seg];
+        end = en[seg];
       } else {
         current = true;
         pos = 0;
@@ -113,20 +117,6 @@ __device__ __forceinline__ void tmem_ld32_sync(uint32_t taddr, float (&x)[32]) {
   for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r[i]);
 }
 
-
-// All 128 TMEM columns of this thread's lane in one load, waited on inside the same asm so no use
-// of the registers can be scheduled before the data has arrived.
-__device__ __forceinline__ void tmem_ld_row128(uint32_t taddr, float (&x)[128]) {
-  uint32_t r[128];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]), "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]), "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]), "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
-      : "r"(taddr)
-      : "memory");
-#pragma unroll
-  for (int i = 0; i < 128; ++i) x[i] = __uint_as_float(r[i]);
-}
 
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
@@ -205,67 +195,6 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   return d;
 }
 
-// 2^y for a pair on the FMA pipe (offloads MUFU). y is rounded to the nearest integer n with the
-// 1.5*2^23 shift, 2^(y-n) on [-0.5, 0.5] comes from a cubic fitted here by weighted least squares
-// (max relative error 7.5e-5, far below the bf16 rounding P receives), and n is added to the
-// exponent field. Inputs below -125 are clamped (2^-125 is negligible next to the row sum >= 1).
-__device__ __forceinline__ void exp2_poly_x2(uint64_t y, float& r0, float& r1) {
-  float y0, y1;
-  f2unpack(y, y0, y1);
-  y = f2pack(fmaxf(y0, -125.f), fmaxf(y1, -125.f));
-  const uint64_t magic = f2pack(12582912.f, 12582912.f);
-  const uint64_t neg_magic = f2pack(-12582912.f, -12582912.f);
-  const uint64_t t = add2(y, magic);
-  const uint64_t n = add2(t, neg_magic);
-  const uint64_t f = fma2(n, f2pack(-1.f, -1.f), y);
-  uint64_t p = fma2(f, f2pack(0.055186375975608826f, 0.055186375975608826f),
-                    f2pack(0.24261236190795898f, 0.24261236190795898f));
-  p = fma2(p, f, f2pack(0.6932582855224609f, 0.6932582855224609f));
-  p = fma2(p, f, f2pack(0.9999279379844666f, 0.9999279379844666f));
-  float p0, p1, t0, t1;
-  f2unpack(p, p0, p1);
-  f2unpack(t, t0, t1);
-  r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-  r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-}
-
-// 2^y for a pair with one MUFU operation: the arguments are rounded to fp16 and the packed
-// half-precision exp2 returns both results. With the lazy running max the argument is at most 8,
-// so rounding it to fp16 changes any p > 2^-8 by at most 0.14 %, below the bf16 rounding that P
-// receives before the PV product (0.39 %); smaller p are below 2^-8 of the row maximum.
-__device__ __forceinline__ void exp2_half_x2(float y0, float y1, float& r0, float& r1) {
-  uint32_t h, e;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(y1), "f"(y0));
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(h));
-  __half2 v = *reinterpret_cast<__half2*>(&e);
-  r0 = __low2float(v);
-  r1 = __high2float(v);
-}
-
-// Pairs of P columns whose exp2 runs on the FMA pipe: pair i with (i % kPolyMod) >= kPolyMod -
-// kPolyCount, kPolyCount being a template parameter of the kernel (0..kPolyMod).
-constexpr int kPolyMod = 4;
-
-// Row max of 128 scores: 8 independent chains of 3-input max.
-__device__ __forceinline__ float row_max128(const float (&x)[128]) {
-  float a[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) a[k] = fmaxf(x[k], x[k + 8]);
-#pragma unroll
-  for (int i = 2; i < 16; i += 2) {
-#pragma unroll
-    for (int k = 0; k < 8; ++k) a[k] = max3f(a[k], x[k + 8 * i], x[k + 8 * i + 8]);
-  }
-  return max3f(max3f(a[0], a[1], a[2]), max3f(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
-}
-
-__device__ __forceinline__ void mask_tail(float (&x)[128], int valid) {
-  if (valid < 128) {
-#pragma unroll
-    for (int i = 0; i < 128; ++i) x[i] = (i < valid) ? x[i] : -INFINITY;
-  }
-}
-
 // A drain wait for the error path: bounded, ignores the abort flag.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, unsigned int* status) {
   const long long t0 = clock64();
@@ -277,10 +206,6 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, unsig
   }
 }
 
-
-__device__ __forceinline__ void named_bar_softmax() {
-  asm volatile("bar.sync 1, 256;" ::: "memory");
-}
 
 // ---------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {

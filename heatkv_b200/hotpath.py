@@ -37,7 +37,7 @@ from .scheduler import build_static_slot_schedule, copy_descriptors
 
 
 NUM_SMS = 148
-BLOCK_ROWS = 256   # query rows per block of the tcgen05 kernel (two 128-row tiles)
+BLOCK_ROWS = 128   # query rows per block of the tcgen05 kernels
 KEY_TILE = 128
 
 
@@ -69,19 +69,18 @@ def plan_attention(slots_per_segment, q_len: int, batch: int, *, sms: int = NUM_
     assignment of items to at most ``sms`` persistent CTAs fills its last wave.
 
     ``slots_per_segment[h]`` lists the head's segment lengths; ``block_rows`` is the kernel's query
-    block (256 rows = two Q tiles for the two-tile kernel, 128 for the column-split kernel). Cost
-    model, in units of one 128 x 128 query-tile x key-tile step: key tiles x Q tiles of the item,
-    plus ``item_cost`` per item (Q load, pipeline fill, epilogue) and ``merge_cost`` per half of a
-    split block (partial write, merge; default 8 for 256-row blocks, 4 for 128-row blocks). Each
-    half writes an fp32 partial of its rows (128 KB for 256 rows) and the block's last CTA reads
-    them back, several tile steps of time, so only tails that leave CTAs idle gain. The blocks are
+    block (128 rows, one Q tile). Cost model, in units of one 128 x 128 query-tile x key-tile step:
+    key tiles of the item, plus ``item_cost`` per item (Q load, pipeline fill, epilogue) and
+    ``merge_cost`` (default 4) per half of a split block: each half writes an fp32 partial of its
+    rows (64 KB) and the block's last CTA reads them back, several tile steps of time, so only
+    tails that leave CTAs idle gain. The blocks are
     enumerated in the kernel's order (head rank, batch row, query block); a split of the last ``m``
     blocks is taken when it lowers the makespan by ``min_gain`` or more. Returns ``(head_order,
     splits, unsplit_blocks)``, the blocks counted in ``block_rows`` units."""
-    if block_rows not in (KEY_TILE, 2 * KEY_TILE):
-        raise ValueError("block_rows must be 128 or 256")
+    if block_rows != KEY_TILE:
+        raise ValueError("block_rows must be 128")
     if merge_cost is None:
-        merge_cost = 8.0 if block_rows == 2 * KEY_TILE else 4.0
+        merge_cost = 4.0
     tiles = _head_tiles(slots_per_segment, q_len, current_in_segments)
     order = np.argsort(-tiles, kind="stable").astype(np.int32)
     nblk = (q_len + block_rows - 1) // block_rows
@@ -377,11 +376,10 @@ class HotPath:
                         key_tile=KEY_TILE // 2)
                     imap = (torch.from_numpy(imap).to(self.device), grid)
                 else:
-                    rows = 2 * KEY_TILE if run == _native.RUN_TCGEN05_PAIR else KEY_TILE
                     order, splits, unsplit = plan_attention(lens, self.tokens[t], self.batch,
-                                                            block_rows=rows,
+                                                            block_rows=KEY_TILE,
                                                             current_in_segments=cis)
-                    if run not in (_native.RUN_TCGEN05_PAIR, _native.RUN_TCGEN05_CS):
+                    if run != _native.RUN_TCGEN05_CS:
                         splits, unsplit = 1, 0  # tf32 and exact launches run unsplit
                     if forced > 0:
                         splits, unsplit = forced, 0

@@ -111,8 +111,8 @@ def main(argv=None):
 
         def fused():
             _native.check(lib.heatkv_qkv_project(
-                _native.ptr(x), _native.ptr(w), _native.ptr(q), _native.ptr(k), _native.ptr(v),
-                _native.DTYPE_CODES[torch.bfloat16], B, L, H, C, _native.ptr(sm),
+                _native.ptr(x), _native.ptr(w), None, _native.ptr(q), _native.ptr(k),
+                _native.ptr(v), _native.DTYPE_CODES[torch.bfloat16], B, L, H, C, _native.ptr(sm),
                 ctypes.c_float(1e-12), _native.ptr(cos), _native.ptr(sin), 64, None, None, 0,
                 None, stream), "heatkv_qkv_project")
         flops = 2.0 * B * L * C * 3 * C

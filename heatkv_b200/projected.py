@@ -45,12 +45,16 @@ class ProjectedHotPath:
     local heads). ``global_heads[i]`` lists the model heads behind plan ``i``'s local heads (default:
     all heads, identity): the projection then uses those heads' rows of ``W_l`` and the
     cos-attention scale of those heads. ``embed_dim`` is the model width ``C`` (default: local
-    heads x 128)."""
+    heads x 128). ``biases[i]`` is plan ``i``'s ``[3C]`` projection bias, ``cat(q_bias,
+    zero_k_bias, v_bias)`` (infinity/models/basic.py:226-227, :278); ``None`` applies none, which
+    equals the zero biases of a random-initialised model."""
 
     def __init__(self, hot: HotPath, *, global_heads: Optional[Sequence[Sequence[int]]] = None,
                  embed_dim: Optional[int] = None, weight_seed: int = 0,
                  cos_attention: bool = True, rope: bool = True, scale_mul: float = None,
-                 weights: Optional[List[torch.Tensor]] = None, fused_projection: bool = True):
+                 weights: Optional[List[torch.Tensor]] = None,
+                 biases: Optional[List[Optional[torch.Tensor]]] = None,
+                 fused_projection: bool = True):
         if hot.head_dim != 128:
             raise ValueError("the projected path needs head_dim 128")
         if not hot.dense_append_first:
@@ -81,6 +85,7 @@ class ProjectedHotPath:
         B = self.rows
         # projection weights: the [3, H_local, D] rows of the layer's [3C, C] mat_qkv weight
         self.weights = []
+        self.biases = []
         for i, p in enumerate(hot.plans):
             w = weights[i] if weights is not None else synthetic.qkv_weight(
                 p.layer, C, seed=weight_seed, dtype=self.dtype, device=self.device)
@@ -93,6 +98,13 @@ class ProjectedHotPath:
                 self.weights.append(w.to(self.device, self.dtype).contiguous())
             else:
                 self.weights.append(w.to(self.device, self.dtype)[rows.to(w.device)].contiguous())
+            b = biases[i] if biases is not None else None
+            if b is not None:
+                if tuple(b.shape) != (3 * C,):
+                    raise ValueError("a QKV bias must be [3 * embed_dim]")
+                # the values F.linear adds: the bias in the projection dtype, held as fp32
+                b = b.to(self.device, self.dtype)[rows.to(b.device)].float().contiguous()
+            self.biases.append(b)
         self.softmax_scale = 1.0 if cos_attention else D ** -0.5
         sm = synthetic.COS_ATTN_SCALE_MUL if scale_mul is None else float(scale_mul)
         self.scale_mul = (torch.full((H,), sm, dtype=torch.float32, device=self.device)
@@ -227,14 +239,18 @@ class ProjectedHotPath:
                     sk, sv, rows_, offs = (None, None, 0, None) if target is None else target[:4]
                     out_launches.append(Launch(
                         "proj", p.layer, t, lib.heatkv_qkv_project,
-                        (_native.ptr(x2d), _native.ptr(w), _native.ptr(q), _native.ptr(k),
+                        (_native.ptr(x2d), _native.ptr(w), _native.ptr(self.biases[i]),
+                         _native.ptr(q), _native.ptr(k),
                          _native.ptr(v), code, B, n, H, C, _native.ptr(self.scale_mul),
                          ctypes.c_float(1e-12), cos, sin, 64, _native.ptr(sk), _native.ptr(sv),
                          rows_, _native.ptr(offs)), flops))
                     out_launches[-1].nbytes = nbytes
                 else:
-                    def gemm(stream, x2d=x2d, w=w, qkv=qkv):
-                        torch.mm(x2d, w.t(), out=qkv)
+                    def gemm(stream, x2d=x2d, w=w, qkv=qkv, b=self.biases[i]):
+                        if b is None:
+                            torch.mm(x2d, w.t(), out=qkv)
+                        else:
+                            torch.addmm(b.to(qkv.dtype), x2d, w.t(), out=qkv)
                         return _native.HEATKV_OK
                     out_launches.append(Launch("gemm", p.layer, t, gemm, (), flops))
                     common = (_native.ptr(qkv), _native.ptr(q), _native.ptr(k), _native.ptr(v),

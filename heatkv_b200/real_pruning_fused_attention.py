@@ -20,7 +20,7 @@ scores are tf32 products as ``tl.dot`` makes them on fp32 operands and P is roun
 ``fp32``/``ieee`` in either knob, and every other dtype combination, select the exact CUDA-core
 kernel (fp32 products). ``REAL_PRUNING_FUSED_BLOCK_M/_N/_NUM_WARPS/_NUM_STAGES`` tune the Triton
 kernel and have no meaning here. ``HEATKV_ATTENTION_KERNEL`` = ``auto|exact|tcgen05`` (or a named
-tcgen05 variant: ``tcgen05_pair``, ``tcgen05_cs``, ``tcgen05_cs64``) forces a kernel.
+tcgen05 variant: ``tcgen05_cs``, ``tcgen05_cs64``) forces a kernel.
 """
 
 from __future__ import annotations
@@ -56,7 +56,7 @@ def _fused_qk_dot_mode_id() -> int:
 
 
 _KERNEL_NAMES = {"auto": _native.ATTN_AUTO, "exact": _native.ATTN_EXACT,
-                 "tcgen05": _native.ATTN_TCGEN05, "tcgen05_pair": _native.ATTN_TCGEN05_PAIR,
+                 "tcgen05": _native.ATTN_TCGEN05,
                  "tcgen05_cs": _native.ATTN_TCGEN05_CS, "tcgen05_cs64": _native.ATTN_TCGEN05_CS64}
 
 
@@ -67,7 +67,7 @@ def _kernel_selector() -> int:
             return _KERNEL_NAMES[forced.strip().lower()]
         except KeyError:
             raise ValueError("HEATKV_ATTENTION_KERNEL must be one of: auto, exact, tcgen05, "
-                             "tcgen05_pair, tcgen05_cs, tcgen05_cs64") from None
+                             "tcgen05_cs, tcgen05_cs64") from None
     if _fused_qk_dot_mode_id() == 2 or _fused_value_dot_mode_id() == 2:
         return _native.ATTN_EXACT
     return _native.ATTN_AUTO

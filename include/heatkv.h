@@ -67,21 +67,20 @@ typedef enum {
                              are f32 with bf16/f16 v (tf32 QK, P in v's dtype), else exact */
   HEATKV_ATTN_EXACT = 1,  /* CUDA-core kernel: fp32 products and accumulation for every dtype */
   HEATKV_ATTN_TCGEN05 = 2, /* tcgen05/TMEM kernel; requires q/k/v all bf16 or all f16, or q and
-                              k f32 with bf16/f16 v. 16-bit calls take the column-split kernel
-                              (one 128-row query tile per CTA) or the two-tile kernel, as a cost
-                              model of the launch size decides */
-  HEATKV_ATTN_TCGEN05_PAIR = 3, /* the two-tile tcgen05 kernel (256 query rows per CTA); q/k/v all
-                                   bf16 or all f16 */
+                              k f32 with bf16/f16 v. 16-bit calls take the 64-key kernel,
+                              scattering calls the column-split kernel; f32 q/k the column-split
+                              kernel's tf32 mode */
+  /* 3 is retired (a two-tile kernel of 256 query rows per CTA) and rejected */
   HEATKV_ATTN_TCGEN05_CS = 4,   /* the column-split tcgen05 kernel (128 query rows per CTA) */
   HEATKV_ATTN_TCGEN05_CS64 = 5  /* 64-key tiles, two CTAs per SM (128 query rows each); q/k/v all
-                                   bf16 or all f16, no key-range splits, no scatter epilogue (such
-                                   calls take the column-split kernel) */
+                                   bf16 or all f16; no scatter epilogue (such calls take the
+                                   column-split kernel) */
 } heatkv_attn_kernel;
 
 /* The kernel an attention call runs (heatkv_attention_kernel_for). */
 typedef enum {
   HEATKV_RUN_EXACT = 1,         /* attn_simt_kernel: CUDA cores, fp32 products */
-  HEATKV_RUN_TCGEN05_PAIR = 2,  /* attn_sm100_kernel: two 128-row query tiles per CTA */
+  /* 2 is retired (the two-tile kernel) */
   HEATKV_RUN_TCGEN05_CS = 3,    /* attn_sm100_cs_kernel, 16-bit mode */
   HEATKV_RUN_TCGEN05_TF32 = 4,  /* attn_sm100_cs_kernel, tf32 mode (fp32 q/k, 16-bit v) */
   HEATKV_RUN_TCGEN05_CS64 = 5   /* attn_sm100_cs64_kernel: 64-key tiles, two CTAs per SM */
@@ -428,21 +427,26 @@ int heatkv_qkv_prepare_append(const void* qkv, void* q, void* k, void* v, int in
 /*
  * heatkv_qkv_project - the QKV projection of the patched attention forward with the q/k/v
  * preparation and the cache append in its epilogue, on the tensor cores: replaces
- * F.linear(x, mat_qkv.weight) (enable_real_pruning_fast.py:2040-2043) followed by
+ * F.linear(x, mat_qkv.weight, cat(q_bias, zero_k_bias, v_bias)) (enable_real_pruning_fast.py:
+ * 2040-2043) followed by
  * heatkv_qkv_prepare_append (the chain of :2044-2072 and the append of :2218-2225).
  *   x       : [batch * seq_len, embed_dim] (dtype: bf16 or f16), the layer input of one scale
  *   w       : [3 * heads * 128, embed_dim] (dtype), the nn.Linear weight rows of the q, k and v
- *             heads (the biases are not applied: they are zero in the models this serves)
+ *             heads
+ *   bias    : fp32 [3 * heads * 128] (the concatenated q, zero k and v biases, in the values the
+ *             reference's F.linear sees, e.g. rounded to dtype under autocast), or NULL for none;
+ *             added to the fp32 accumulator before the rounding to dtype
  *   q, k, v : [batch, heads, seq_len, 128] (dtype). The projection is rounded to dtype, then
  *             prepared as heatkv_qkv_prepare does (scale_mul: cos-attention; rope: the rotary
  *             rows of the scale's tokens, rope_row_stride floats apart)
  *   cache_* : as heatkv_qkv_prepare_append's slab (cache_offset -1 = head not written); rows of
  *             the heads given an offset are written from the same registers
- * heads must be even, embed_dim a multiple of 64; x, w, q, k, v, the rope rows and the caches
- * 16-byte aligned. Results equal heatkv_qkv_prepare_append applied to the rounded projection up
+ * heads must be even, embed_dim a multiple of 64; x, w, bias, q, k, v, the rope rows and the
+ * caches 16-byte aligned. Results equal heatkv_qkv_prepare_append applied to the rounded projection up
  * to the summation order of the projection and of the row norms.
  */
-int heatkv_qkv_project(const void* x, const void* w, void* q, void* k, void* v, int dtype,
+int heatkv_qkv_project(const void* x, const void* w, const float* bias, void* q, void* k, void* v,
+                       int dtype,
                        int64_t batch, int64_t seq_len, int64_t heads, int64_t embed_dim,
                        const float* scale_mul, float eps, const float* rope_cos,
                        const float* rope_sin, int64_t rope_row_stride, void* cache_k,

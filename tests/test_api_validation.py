@@ -65,8 +65,9 @@ def test_bad_dot_mode_env(monkeypatch):
     assert m._kernel_selector() == m._native.ATTN_EXACT
     monkeypatch.setenv("HEATKV_ATTENTION_KERNEL", "tcgen05")
     assert m._kernel_selector() == m._native.ATTN_TCGEN05
-    monkeypatch.setenv("HEATKV_ATTENTION_KERNEL", "tcgen05_pair")
-    assert m._kernel_selector() == m._native.ATTN_TCGEN05_PAIR
+    monkeypatch.setenv("HEATKV_ATTENTION_KERNEL", "tcgen05_pair")   # retired
+    with pytest.raises(ValueError, match="HEATKV_ATTENTION_KERNEL"):
+        m._kernel_selector()
     monkeypatch.setenv("HEATKV_ATTENTION_KERNEL", "tcgen05_cs")
     assert m._kernel_selector() == m._native.ATTN_TCGEN05_CS
     monkeypatch.setenv("HEATKV_ATTENTION_KERNEL", "fast")

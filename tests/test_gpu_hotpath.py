@@ -46,6 +46,25 @@ def test_hot_path_matches_keep_mask_attention(model, budget, layers):
             assert err <= BF16_ATOL and err / scale <= BF16_REL, (layer, t, err, scale)
 
 
+def test_hot_path_every_layer_of_configs1():
+    """configs[1] at full size: all 32 layers of the 2B model at 10 %, 2 rows, every target."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device("cuda", 0)
+    ctrl, L, H = _controller("2b", 0.10)
+    layers = list(range(L))
+    hot = HotPath(ctrl, L, H, 2, dev, torch.bfloat16, torch.bfloat16, layers=layers)
+    inputs, outputs, _, _ = allocate_io(hot, seed=11)
+    hot.run(hot.launches(inputs, outputs))
+    torch.cuda.synchronize()
+    assert _native.device_status(dev) == 0
+    for i, layer in enumerate(layers):
+        for t in range(hot.num_scales):
+            ref = _reference(ctrl, layer, t, inputs[i])
+            err = (outputs[i][t].float() - ref).abs().max().item()
+            scale = ref.abs().max().item()
+            assert err <= BF16_ATOL and err / scale <= BF16_REL, (layer, t, err, scale)
+
+
 def _random_controller(budget, seed, layers=32, heads=16):
     """2B-shaped controller from seeded random per-source removal orders (the budget sweep)."""
     from heatkv_b200 import budget as bud, synthetic
@@ -65,7 +84,8 @@ def _random_controller(budget, seed, layers=32, heads=16):
                                           static_removed_heads_by_scale=norm, source_scale_start=3)
 
 
-@pytest.mark.parametrize("budget,rows,layer", [(0.25, 16, 5), (0.5, 16, 30), (0.05, 16, 12)])
+@pytest.mark.parametrize("budget,rows,layer", [(0.25, 16, 5), (0.5, 16, 30), (0.05, 16, 12),
+                                               (0.10, 16, 17), (1.00, 16, 25)])
 def test_hot_path_budget_sweep_batch16(budget, rows, layer):
     """Budget sweep shape (2B, 16 rows = batch 8 + CFG, seeded random orders): uneven slab
     lengths per head, several query blocks per CTA."""

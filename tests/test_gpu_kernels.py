@@ -113,7 +113,7 @@ def _random_layout(rng, heads, max_segments, capacity, lengths=(1, 4, 16, 36, 64
     return [torch.from_numpy(x) for x in (starts, ends, counts)]
 
 
-@pytest.mark.parametrize("which", ["tcgen05_cs", "tcgen05_pair", "tcgen05_cs64"])
+@pytest.mark.parametrize("which", ["tcgen05_cs", "tcgen05_cs64"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("B,H,L,cap,S", [
     (1, 1, 1, 700, 3), (2, 3, 4, 400, 4), (1, 2, 127, 900, 5), (2, 2, 128, 900, 5),
@@ -121,8 +121,8 @@ def _random_layout(rng, heads, max_segments, capacity, lengths=(1, 4, 16, 36, 64
     (2, 16, 576, 4000, 12), (1, 4, 1024, 3000, 12),
 ])
 def test_tcgen05_random_layouts(which, dtype, B, H, L, cap, S, cuda_device, kernel):
-    """Both 16-bit tcgen05 kernels: the column-split one (one 128-row query tile per CTA, the
-    default) and the two-tile one (256 rows per CTA, key-range splits)."""
+    """Both 16-bit tcgen05 kernels: the 64-key one (two CTAs per SM, the default) and the
+    column-split one (the scatter kernel)."""
     kernel(which)
     rng = np.random.default_rng(B * 1000 + H * 100 + L)
     gen = torch.Generator().manual_seed(L)
@@ -138,7 +138,7 @@ def test_tcgen05_random_layouts(which, dtype, B, H, L, cap, S, cuda_device, kern
     assert _native.device_status(cuda_device) == 0
 
 
-@pytest.mark.parametrize("which", ["tcgen05_cs", "tcgen05_pair", "tcgen05_cs64"])
+@pytest.mark.parametrize("which", ["tcgen05_cs", "tcgen05_cs64"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("L", [5, 200, 300])
 def test_tcgen05_scores_growing_tile_by_tile(which, dtype, L, cuda_device, kernel):
@@ -239,14 +239,14 @@ def test_tcgen05_tf32_mixed_dtypes(vdtype, B, H, L, cap, S, cuda_device, kernel)
     assert _native.device_status(cuda_device) == 0
 
 
-def test_two_tile_kernel_rejects_fp32_queries(cuda_device, kernel):
-    """The two-tile kernel asked for by name takes only all-bf16 or all-f16 inputs."""
-    kernel("tcgen05_pair")
+def test_64_key_kernel_rejects_fp32_queries(cuda_device, kernel):
+    """The 64-key kernel asked for by name takes only all-bf16 or all-f16 inputs."""
+    kernel("tcgen05_cs64")
     d = cuda_device
     q, ck = (torch.randn(1, 2, 8, 128, device=d) for _ in range(2))
     cv = torch.randn(1, 2, 8, 128, device=d).bfloat16()
     z = torch.zeros(2, 0, dtype=torch.int32, device=d)
-    with pytest.raises(RuntimeError, match="two-tile"):
+    with pytest.raises(RuntimeError, match="64-key"):
         attn(q=q, persisted_k=None, persisted_v=None, segment_starts=z, segment_ends=z,
              segment_counts=torch.zeros(2, dtype=torch.int32, device=d), current_k=ck,
              current_v=cv, softmax_scale=0.1)
@@ -391,8 +391,7 @@ def _attention_ws(q, pk, pv, st, en, ct, ck, cv, scale, *, head_order, splits, w
     return out
 
 
-SPLIT_KERNELS = {"pair": (_native.ATTN_TCGEN05_PAIR, 256), "cs": (_native.ATTN_TCGEN05_CS, 128),
-                 "cs64": (_native.ATTN_TCGEN05_CS64, 128)}
+SPLIT_KERNELS = {"cs": (_native.ATTN_TCGEN05_CS, 128), "cs64": (_native.ATTN_TCGEN05_CS64, 128)}
 
 
 @pytest.mark.parametrize("variant", sorted(SPLIT_KERNELS))
@@ -401,7 +400,7 @@ SPLIT_KERNELS = {"pair": (_native.ATTN_TCGEN05_PAIR, 256), "cs": (_native.ATTN_T
                                          (2, 16, 1600, 5000, 12), (1, 2, 20, 900, 4)])
 def test_tcgen05_split_kv_and_head_order(variant, splits, B, H, L, cap, S, cuda_device):
     """Split-KV partials merged by the last CTA and a shuffled head order give the same result as
-    the reference, in both tcgen05 kernels (blocks of 256 or 128 query rows); splits without key
+    the reference, in both tcgen05 kernels (blocks of 128 query rows); splits without key
     tiles (heads with fewer tiles than splits) contribute nothing; the workspace counters are back
     to zero after every call."""
     kern, block_rows = SPLIT_KERNELS[variant]
@@ -432,7 +431,7 @@ def test_tcgen05_split_kv_and_head_order(variant, splits, B, H, L, cap, S, cuda_
                                                 (1, 8, 4096, 2000, 6, 3)])
 def test_tcgen05_tail_split_schedule(variant, B, H, L, cap, S, splits, cuda_device):
     """heatkv_segmented_attention_sched: only the blocks after the first `unsplit` (schedule
-    order, blocks of the kernel's 256 or 128 query rows) are split; every choice of unsplit gives
+    order, blocks of the kernel's 128 query rows) are split; every choice of unsplit gives
     the reference's result, and the unsplit blocks are bit-identical to an unsplit launch."""
     kern, block_rows = SPLIT_KERNELS[variant]
     import ctypes
@@ -648,7 +647,7 @@ def test_item_map_entry_outside_the_launch_is_skipped_and_flagged(cuda_device):
     _check_lowp(out.float().cpu().numpy(), ref.cpu().numpy())
 
 
-@pytest.mark.parametrize("sel", ["cs", "pair", "exact", "cs64"])
+@pytest.mark.parametrize("sel", ["cs", "exact", "cs64"])
 def test_current_in_segments_flag(sel, cuda_device):
     """HEATKV_ATTN_CURRENT_IN_SEGMENTS: with every head's current keys copied into the slab right
     after its last segment (extending it), the flagged call reads no separate current tiles and
@@ -682,8 +681,8 @@ def test_current_in_segments_flag(sel, cuda_device):
         base += L
     st2, en2, ct2 = (torch.from_numpy(np.ascontiguousarray(x, dtype=np.int32)).to(d)
                      for x in (st2, en2, ct2))
-    kern = {"cs": _native.ATTN_TCGEN05_CS, "pair": _native.ATTN_TCGEN05_PAIR,
-            "exact": _native.ATTN_EXACT, "cs64": _native.ATTN_TCGEN05_CS64}[sel]
+    kern = {"cs": _native.ATTN_TCGEN05_CS, "exact": _native.ATTN_EXACT,
+            "cs64": _native.ATTN_TCGEN05_CS64}[sel]
     out = torch.empty(B, L, H * 128, dtype=q.dtype, device=d)
     dt = _native.DTYPE_CODES
     order = torch.arange(H, dtype=torch.int32, device=d)

@@ -17,7 +17,7 @@ from heatkv_b200.qkv_prep import prepare_qkv
 pytestmark = pytest.mark.gpu
 
 
-def _project(x, w, B, L, H, scale_mul=None, rope=None, cache=None):
+def _project(x, w, B, L, H, scale_mul=None, rope=None, cache=None, bias=None):
     lib = _native.load()
     dev = x.device
     q, k, v = (torch.empty(B, H, L, 128, dtype=x.dtype, device=dev) for _ in range(3))
@@ -26,8 +26,8 @@ def _project(x, w, B, L, H, scale_mul=None, rope=None, cache=None):
         cos, sin = rope
     ck, cv, rows, offs = cache if cache is not None else (None, None, 0, None)
     _native.check(lib.heatkv_qkv_project(
-        _native.ptr(x), _native.ptr(w), _native.ptr(q), _native.ptr(k), _native.ptr(v),
-        _native.DTYPE_CODES[x.dtype], B, L, H, x.shape[-1], _native.ptr(scale_mul),
+        _native.ptr(x), _native.ptr(w), _native.ptr(bias), _native.ptr(q), _native.ptr(k),
+        _native.ptr(v), _native.DTYPE_CODES[x.dtype], B, L, H, x.shape[-1], _native.ptr(scale_mul),
         ctypes.c_float(1e-12), _native.ptr(cos), _native.ptr(sin),
         0 if cos is None else cos.stride(0), _native.ptr(ck), _native.ptr(cv), rows,
         _native.ptr(offs), _native.stream_handle(dev)), "heatkv_qkv_project")
@@ -104,3 +104,30 @@ def test_fused_projection_flags_a_cache_offset_past_the_end(variant):
     torch.cuda.synchronize()
     assert _native.device_status(dev) == _native.DEVICE_PACK_OUT_OF_RANGE
     assert (ck[:, L:] == 0).all() and (ck[:, :L] != 0).any()
+
+
+def test_fused_projection_adds_the_bias(variant):
+    """``bias`` = cat(q_bias, zero_k_bias, v_bias) as the reference's F.linear adds it
+    (enable_real_pruning_fast.py:2040-2043), against cuBLAS addmm then the preparation."""
+    torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+    dev = torch.device("cuda", 0)
+    B, L, H, C = 2, 100, 4, 512
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn(B * L, C, device=dev, generator=g).bfloat16()
+    w = (torch.randn(3 * H * 128, C, device=dev, generator=g) * 0.02).bfloat16()
+    qb, vb = (torch.randn(H * 128, device=dev, generator=g) * 0.5 for _ in range(2))
+    bias = torch.cat((qb, torch.zeros_like(qb), vb)).bfloat16()
+    sm = torch.rand(H, device=dev, generator=g) * 4 + 1
+    ang = torch.rand(L, 64, device=dev, generator=g) * 6
+    rp = (torch.cos(ang).contiguous(), torch.sin(ang).contiguous())
+    qkv = torch.addmm(bias, x, w.t()).view(B, L, 3, H, 128)
+    rq, rk, rv = prepare_qkv(qkv, scale_mul=sm, rope=rp, qk_dtype=torch.bfloat16)
+    q, k, v = _project(x, w, B, L, H, sm, rp, bias=bias.float().contiguous())
+    torch.cuda.synchronize()
+    assert _native.device_status(dev) == 0
+    for name, a, b in (("q", q, rq), ("k", k, rk), ("v", v, rv)):
+        ok, info = _close(a, b)
+        assert ok, (name, info)
+    # without the bias the v rows differ by it
+    _, _, v0 = _project(x, w, B, L, H, sm, rp)
+    assert not _close(v0, rv)[0]

@@ -7,9 +7,8 @@ import pytest
 from heatkv_b200 import _native
 
 F32, F16, BF16 = 0, 1, 2
-AUTO, EXACT, TC, PAIR, CS, CS64 = (_native.ATTN_AUTO, _native.ATTN_EXACT, _native.ATTN_TCGEN05,
-                                   _native.ATTN_TCGEN05_PAIR, _native.ATTN_TCGEN05_CS,
-                                   _native.ATTN_TCGEN05_CS64)
+AUTO, EXACT, TC, CS, CS64 = (_native.ATTN_AUTO, _native.ATTN_EXACT, _native.ATTN_TCGEN05,
+                             _native.ATTN_TCGEN05_CS, _native.ATTN_TCGEN05_CS64)
 
 
 def run(dt=(BF16, BF16, BF16), batch=2, heads=16, q_len=4096, kernel=AUTO, splits=1, ws=0,
@@ -30,19 +29,17 @@ def test_sixteen_bit_calls_take_the_64_key_kernel():
 def test_split_calls_take_the_64_key_kernel():
     """The 64-key kernel takes key-range splits too (unsplit_blocks counts its 128-row blocks),
     so splits, the workspace and unsplit_blocks leave 16-bit calls on it at every size. (Only
-    scattering calls, which it cannot serve, go to the column-split or two-tile kernel by the
-    cost model; the GPU scatter tests cover those.)"""
+    scattering calls, which it cannot serve, go to the column-split kernel; the GPU scatter tests
+    cover those.)"""
     for splits, unsplit in ((2, 0), (4, 100), (3, 2 * 16 * 32)):
         assert run(splits=splits, ws=1, unsplit=unsplit) == _native.RUN_TCGEN05_CS64
         assert run(batch=16, splits=splits, ws=1, unsplit=unsplit) == _native.RUN_TCGEN05_CS64
     assert run(batch=8, heads=28, q_len=2304, splits=2, ws=1) == _native.RUN_TCGEN05_CS64
-    # named variants keep their own kernel with splits
-    assert run(kernel=PAIR, splits=2, ws=1) == _native.RUN_TCGEN05_PAIR
+    # a named variant keeps its own kernel with splits
     assert run(kernel=CS, splits=2, ws=1) == _native.RUN_TCGEN05_CS
 
 
 def test_named_variants_and_the_flags():
-    assert run(kernel=PAIR) == _native.RUN_TCGEN05_PAIR
     assert run(batch=16, kernel=CS) == _native.RUN_TCGEN05_CS
     assert run(kernel=CS64) == _native.RUN_TCGEN05_CS64
     assert run(kernel=CS64, splits=2, ws=1) == _native.RUN_TCGEN05_CS64
@@ -63,7 +60,7 @@ def test_dtype_routing():
 
 
 @pytest.mark.parametrize("dt,kernel", [((F32, F32, F32), TC), ((F16, BF16, BF16), TC),
-                                       ((F32, F32, BF16), PAIR), ((F32, F32, BF16), CS64)])
+                                       ((F32, F32, BF16), CS64)])
 def test_tensor_core_selectors_reject_other_dtypes(dt, kernel):
     assert run(dt=dt, kernel=kernel) == _native.HEATKV_ERR_UNSUPPORTED
 
@@ -71,5 +68,6 @@ def test_tensor_core_selectors_reject_other_dtypes(dt, kernel):
 def test_invalid_arguments():
     assert run(kernel=7) == _native.HEATKV_ERR_INVALID_ARGUMENT
     assert run(kernel=6) == _native.HEATKV_ERR_INVALID_ARGUMENT
+    assert run(kernel=3) == _native.HEATKV_ERR_INVALID_ARGUMENT  # the retired two-tile selector
     assert run(q_len=0) == _native.HEATKV_ERR_INVALID_ARGUMENT
     assert run(dt=(5, BF16, BF16)) == _native.HEATKV_ERR_UNSUPPORTED

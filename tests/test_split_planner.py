@@ -1,6 +1,5 @@
 """The length-aware launch planner (``hotpath.plan_attention``, CPU): head order, and the tail of
-query blocks split in two key ranges, for the two-tile kernel's 256-row blocks and the column-split
-kernel's 128-row blocks."""
+query blocks split in two key ranges, for the kernels' 128-row blocks."""
 
 import numpy as np
 import pytest
@@ -35,7 +34,7 @@ def _first_pruned_target_lengths():
     return plan.segment_lengths(8)
 
 
-@pytest.mark.parametrize("block_rows,merge_cost", [(128, 4.0), (256, 8.0)])
+@pytest.mark.parametrize("block_rows,merge_cost", [(128, 4.0)])
 def test_plan_lowers_the_makespan_it_models(block_rows, merge_cost):
     lengths = _first_pruned_target_lengths()
     q_len, batch = 576, 2
@@ -67,8 +66,9 @@ def test_full_waves_stay_unsplit():
 
 
 def test_block_rows_must_be_a_kernel_block():
-    with pytest.raises(ValueError):
-        plan_attention([[10]], 64, 1, block_rows=64)
+    for rows in (64, 256):
+        with pytest.raises(ValueError):
+            plan_attention([[10]], 64, 1, block_rows=rows)
 
 
 @pytest.mark.parametrize("splits", [None, 1, 2, 3])
