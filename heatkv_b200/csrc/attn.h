@@ -117,6 +117,13 @@ cudaError_t launch_scas_mass(const void* q, const void* k, int dtype, int64_t he
                              int64_t k_len, float scale, const int32_t* bounds, int n_src,
                              double* mass_out, int64_t mass_stride, cudaStream_t st);
 
+// The same on the tensor cores for fp32 q and k (scas_tc.cu: kind::tf32, three products a score);
+// cudaErrorNotSupported outside its limits.
+cudaError_t launch_scas_mass_tc(const float* q, const float* k, int64_t heads, int64_t q_len,
+                                int64_t k_len, float scale, const int32_t* bounds, int n_src,
+                                double* mass_out, int64_t mass_stride, unsigned int* status,
+                                cudaStream_t st);
+
 // q/k/v preparation after the QKV projection (qkv_prep.cu); sms = SMs of the device.
 cudaError_t launch_qkv_project(const void* x, const void* w, const float* bias, void* q, void* k,
                                void* v, bool bf16, int64_t batch, int64_t seq_len, int64_t heads,

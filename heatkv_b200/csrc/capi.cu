@@ -546,8 +546,18 @@ int heatkv_scas_mass(const void* q, const void* k, int dtype, int64_t heads, int
   const uintptr_t need = dtype == HEATKV_DTYPE_F32 ? 15u : 7u;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k)) & need)
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "heatkv_scas_mass: misaligned q or k");
-  cudaError_t e = heatkv::launch_scas_mass(q, k, dtype, heads, q_len, k_len, scale, bounds, n_src,
-                                           mass_out, mass_stride, static_cast<cudaStream_t>(stream));
+  // fp32: the tensor-core kernel (three tf32 products a score) unless HEATKV_SCAS_KERNEL=cuda_cores
+  // (read per call); 16-bit inputs, and fp32 calls outside its limits, the CUDA-core kernel
+  cudaError_t e = cudaErrorNotSupported;
+  const char* sel = getenv("HEATKV_SCAS_KERNEL");
+  if (dtype == HEATKV_DTYPE_F32 && !(sel && strcmp(sel, "cuda_cores") == 0))
+    e = heatkv::launch_scas_mass_tc(static_cast<const float*>(q), static_cast<const float*>(k),
+                                    heads, q_len, k_len, scale, bounds, n_src, mass_out,
+                                    mass_stride, heatkv::device_status_ptr(),
+                                    static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorNotSupported)
+    e = heatkv::launch_scas_mass(q, k, dtype, heads, q_len, k_len, scale, bounds, n_src, mass_out,
+                                 mass_stride, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "heatkv_scas_mass launch");
   return HEATKV_OK;
 }

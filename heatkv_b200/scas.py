@@ -67,7 +67,9 @@ class ScasAccumulator:
                        scale: float) -> None:
         """From the scale's queries ``q [B, H, L, 128]`` and every key so far ``k [B, H, K, 128]``
         (the cached scales, then the current one): probs = softmax(q k^T * scale) in fp32,
-        computed and reduced on the GPU without being stored."""
+        computed and reduced on the GPU without being stored. q and k are widened to fp32 as the
+        reference does (``q.float() @ k.float()^T``, tools/compute_scas.py:217), which runs the
+        tensor-core kernel (three tf32 products a score)."""
         if q.ndim != 4 or k.ndim != 4 or q.shape[:2] != k.shape[:2] or q.shape[3] != k.shape[3]:
             raise ValueError("update_from_qk expects q [B, H, L, D] and k [B, H, K, D]")
         if not (q.is_cuda and k.is_cuda):
@@ -76,11 +78,9 @@ class ScasAccumulator:
         if not sources:
             return
         lib = _native.load()
-        dtype = q.dtype if q.dtype == k.dtype else torch.float32
-        q0 = q[0].to(dtype).contiguous()
-        k0 = k[0].to(dtype).contiguous()
-        if dtype not in _native.DTYPE_CODES:
-            q0, k0, dtype = q0.float(), k0.float(), torch.float32
+        dtype = torch.float32
+        q0 = q[0].float().contiguous()
+        k0 = k[0].float().contiguous()
         key = (sources[0], len(sources), q.device)
         b = self._bounds_dev.get(key)
         if b is None:

@@ -381,6 +381,9 @@ int heatkv_attention_kernel_for(int q_dtype, int k_dtype, int v_dtype, int64_t b
  * for every source s < n_src (<= 32). bounds: int32 device array of n_src + 1 increasing key
  * offsets; mass_out: float64 device array (the reference's accumulator row of this layer, from
  * its first source scale). head_dim must be 128; q and k 16-byte aligned for f32, 8 for 16-bit.
+ * f32 inputs run on the tensor cores: kind::tf32 MMAs with each operand split into a tf32 head
+ * and its fp32 remainder, three products a score (fp32-level scores; HEATKV_SCAS_KERNEL=cuda_cores
+ * selects the CUDA-core kernel instead); 16-bit inputs on CUDA cores with fp32 products.
  */
 int heatkv_scas_mass(const void* q, const void* k, int dtype, int64_t heads, int64_t q_len,
                      int64_t k_len, int64_t head_dim, float scale, const int32_t* bounds,

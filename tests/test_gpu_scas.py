@@ -17,6 +17,14 @@ pytestmark = pytest.mark.gpu
 SCHED_7 = [(1, 1, 1), (1, 2, 2), (1, 4, 4), (1, 6, 6), (1, 8, 8), (1, 12, 12), (1, 16, 16)]
 
 
+@pytest.fixture(params=["tensor_cores", "cuda_cores"])
+def scas_kernel(request, monkeypatch):
+    """The tensor-core kernel (default for fp32: three tf32 products a score) and the CUDA-core
+    kernel (fp32 products)."""
+    monkeypatch.setenv("HEATKV_SCAS_KERNEL", request.param)
+    return request.param
+
+
 def _probs(q, k, scale):
     scores = torch.matmul(q.float(), k.float().transpose(-2, -1)) * float(scale)
     return torch.softmax(scores, dim=-1)
@@ -24,7 +32,7 @@ def _probs(q, k, scale):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("schedule,sink,layers", [(SCHED_7, 1, 2), (synthetic.SCALE_SCHEDULE_1M[:11], 2, 1)])
-def test_update_from_qk_matches_probabilities(dtype, schedule, sink, layers):
+def test_update_from_qk_matches_probabilities(dtype, schedule, sink, layers, scas_kernel):
     dev = torch.device("cuda", 0)
     torch.backends.cuda.matmul.allow_tf32 = False
     H = 16
@@ -75,7 +83,7 @@ def test_sources_missing_from_the_keys_are_skipped():
     np.testing.assert_allclose(acc.accum.cpu().numpy(), ref.accum.cpu().numpy(), rtol=1e-5)
 
 
-def test_update_from_qk_matches_the_reference_fixture(golden_dir):
+def test_update_from_qk_matches_the_reference_fixture(golden_dir, scas_kernel):
     """``update_from_qk`` on the GPU against the reference's own ScasAccumulator
     (tests/golden/scas_c1.npz, recorded from tools/compute_scas.py:92-152 on the capture
     forward's fp32 probabilities of the same seeded q/k): accum within 1e-5 relative, the removal
