@@ -83,6 +83,7 @@ struct Params {
   int64_t cache_rows;
   const int64_t* cache_offset;
   unsigned int* status;
+  int align32;           // q, k, v and the caches 32-byte aligned: 32-byte stores
 };
 
 // x[i] += bias[i] for 64 columns (fp32 add, as the GEMM's bias epilogue does before rounding)
@@ -184,7 +185,17 @@ __device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int6
         }
       }
     }
-    if (live) {
+    if (live && p.align32) {
+      // one full 32-byte sector per store (each thread writes its own row)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t w[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) w[e] = pack2<kBF16>(x[16 * j + 2 * e], x[16 * j + 2 * e + 1]);
+        st_global_v8(dst + half * 8 + 2 * j, w);
+        if (cd != nullptr) st_global_v8(cd + half * 8 + 2 * j, w);
+      }
+    } else if (live) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const uint4 w = make_uint4(pack2<kBF16>(x[8 * j], x[8 * j + 1]),
@@ -622,6 +633,9 @@ cudaError_t launch_qkv_project(const void* x, const void* w, const float* bias, 
   p.cache_rows = cache_rows;
   p.cache_offset = cache_offset;
   p.status = status;
+  p.align32 = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(cache_k) |
+                reinterpret_cast<uintptr_t>(cache_v)) & 31u) == 0 ? 1 : 0;
   const bool cos = scale_mul != nullptr, rope = rope_cos != nullptr;
   if (use_pair) {
     const int64_t pair_tiles = (M + 255) / 256 * p.n_tiles;
