@@ -139,8 +139,13 @@ __device__ __forceinline__ Item decode_item(const Smem& sm, const Params& p, int
   it.h = sm.head_order[rb / static_cast<int>(p.batch)];
   it.q0 = qb * kBM;
   const int tiles = sm.head_tiles[it.h];
-  it.j0 = static_cast<int>((int64_t(tiles) * it.split) / it.nsplit);
-  it.n = static_cast<int>((int64_t(tiles) * (it.split + 1)) / it.nsplit) - it.j0;
+  if (it.nsplit == 1) {  // unsplit (the common case): no 64-bit divisions on the item's path
+    it.j0 = 0;
+    it.n = tiles;
+  } else {
+    it.j0 = static_cast<int>((int64_t(tiles) * it.split) / it.nsplit);
+    it.n = static_cast<int>((int64_t(tiles) * (it.split + 1)) / it.nsplit) - it.j0;
+  }
   return it;
 }
 
