@@ -283,15 +283,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&sm.s_free[b]);
         const int t0 = j * kBN;
         const int nvalid = static_cast<int>(min64(kBN, p.k_len - t0));
+        // scores in base-2 units: exp(s * scale - m) = 2^(s * scale * log2(e) - m')
+        const float c = p.scale * 1.4426950408889634f;
         float mx = -INFINITY;
 #pragma unroll
         for (int i = 0; i < kBN; ++i) {
-          x[i] = i < nvalid ? x[i] * p.scale : -INFINITY;
+          x[i] = i < nvalid ? x[i] * c : -INFINITY;
           mx = fmaxf(mx, x[i]);
         }
         // key 0 of every tile is valid, so mx is finite
         if (mx > m_run) {
-          const float alpha = expf(m_run - mx);  // 0 on the first tile
+          const float alpha = ex2(m_run - mx);  // 0 on the first tile
           l_run *= alpha;
           for (int s = 0; s < p.n_src; ++s) part[s] *= alpha;
           m_run = mx;
@@ -299,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float sum = 0.f;
 #pragma unroll
         for (int i = 0; i < kBN; ++i) {
-          x[i] = expf(x[i] - m_run);
+          x[i] = ex2(x[i] - m_run);
           sum += x[i];
         }
         l_run += sum;
