@@ -1011,7 +1011,7 @@ def main() -> None:
                          "heatkv_qkv_project")
     ap.add_argument("--no-dropin", action="store_true",
                     help="skip the one-image timing through the public installer")
-    ap.add_argument("--att-traffic-per-row", type=float, default=565.5e6 / 8,
+    ap.add_argument("--att-traffic-per-row", type=float, default=569.9e6 / 8,
                     help="DRAM bytes per batch row of the target-12 attention launch (ncu capture "
                          "at 8 rows, profiles/attn_sm100_cs64_kernel_2b_q4096_rows8.md)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
