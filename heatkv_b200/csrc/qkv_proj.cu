@@ -18,17 +18,17 @@
 // correctly rounded reciprocal (one fp32 rounding step at most). Those and the summation order of
 // the GEMM and of the row norm are the only differences from the unfused path.
 //
-// Tiles are 128 rows x 256 columns (two heads of one of q, k, v) over K steps of 64; a persistent
-// grid of one CTA per SM walks the tiles row panel by row panel (the 24 column tiles of a panel
-// run on neighbouring CTAs, so the x panel is read from HBM once and the weight stays in L2).
-// CTA (384 threads, 1 per SM): warp 0 issues the TMA loads of a 4-stage ring (x box 64 x 128 rows,
-// W box 64 x 256 rows, 128-byte swizzle); warp 1 allocates TMEM (two 256-column accumulators) and
-// issues tcgen05.mma kind::f16 M=128 N=256 K=16, four per stage; warps 4-11 are the epilogue, one
-// TMEM lane (accumulator row) and one head block per thread, two warps per SM sub-partition,
-// working on one accumulator while the MMAs fill the other. Every wait is bounded; on expiry the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains its
-// copies and MMAs, frees TMEM and returns.
-#include <cstdlib>
-
+// Tiles are 256 rows x 256 columns (two heads of one of q, k, v) over K steps of 64, each computed
+// by a cluster of two CTAs on two SMs with tcgen05.mma.cta_group::2 (the protocol is described
+// above qkv_project_pair_kernel); a persistent grid of pairs walks the tiles row panel by row panel
+// (the 24 column tiles of a panel run on neighbouring pairs, so the x panel is read from HBM once
+// and the weight stays in L2). CTA (384 threads, 1 per SM): warp 0 issues the TMA loads of a
+// 6-stage ring (this CTA's 128 rows of x and of W per stage, 128-byte swizzle); warp 1 allocates
+// TMEM (two 256-column accumulators) and, in the leader, issues the MMAs; warps 4-11 are the
+// epilogue, one TMEM lane (accumulator row) and one head block per thread, two warps per SM
+// sub-partition, working on one accumulator while the MMAs fill the other. Every wait is bounded;
+// on expiry the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains its copies and MMAs, frees TMEM and
+// returns.
 #include "attn.h"
 #include "common.cuh"
 #include "sm100_util.cuh"
@@ -40,27 +40,12 @@ namespace qkvproj {
 constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;
-constexpr int kStages = 4;
-constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KiB
-constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KiB
 constexpr int kThreads = 384;
 constexpr int kLoadWarp = 0;
 constexpr int kMmaWarp = 1;
 constexpr int kEpiWarp0 = 4;    // warps 4-11: epilogue; warp 4 + 4 j + q reads TMEM lanes
 constexpr int kEpiWarps = 8;    // [32 q, +32) of head block j (two warps per SM sub-partition)
 constexpr uint32_t kTmemCols = 512;           // two 256-column accumulators
-
-struct __align__(1024) Smem {
-  uint8_t a[kStages][kABytes];
-  uint8_t b[kStages][kBBytes];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
-  uint64_t acc_full[2];
-  uint64_t acc_empty[2];
-  uint64_t drain;
-  uint32_t tmem_base;
-  int abort_flag;
-};
 
 struct Params {
   int64_t rows;          // M = batch * seq_len
@@ -207,125 +192,6 @@ __device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int6
       }
     }
   }
-}
-
-template <bool kBF16, bool kCos, bool kRope>
-__global__ void __launch_bounds__(kThreads, 1)
-    qkv_project_kernel(const __grid_constant__ CUtensorMap tm_x,
-                       const __grid_constant__ CUtensorMap tm_w, const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                      ~uintptr_t(1023));
-  volatile int* abort_flag = &sm.abort_flag;
-  const int warp = threadIdx.x / 32;
-  const int lane = threadIdx.x % 32;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&sm.acc_full[a], 1);
-      mbar_init(&sm.acc_empty[a], kEpiWarps);   // one arrival per epilogue warp
-    }
-    mbar_init(&sm.drain, 1);
-    sm.abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == kMmaWarp) {
-    tmem_alloc(&sm.tmem_base, kTmemCols);
-    tmem_relinquish();
-  }
-  if (warp == kLoadWarp && lane == 0) {
-    tma_prefetch_desc(&tm_x);
-    tma_prefetch_desc(&tm_w);
-  }
-  pdl_trigger();
-  pdl_wait();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = sm.tmem_base;
-  const int KB = p.k_blocks;
-
-  if (warp == kLoadWarp) {
-    if (lane == 0) {
-      uint32_t it = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
-        const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const uint32_t s = it % kStages;
-          if (it >= kStages &&
-              !(ok = mbar_wait(&sm.empty[s], ((it / kStages) - 1) & 1, abort_flag, p.status)))
-            break;
-          mbar_arrive_expect_tx(&sm.full[s], kABytes + kBBytes);
-          tma_load_2d(sm.a[s], &tm_x, kb * kBK, mt * kBM, &sm.full[s]);
-          tma_load_2d(sm.b[s], &tm_w, kb * kBK, nt * kBN, &sm.full[s]);
-        }
-      }
-      if (!ok || *abort_flag) {
-        // every copy already issued lands before the CTA's shared memory goes away
-        for (uint32_t g = it > kStages ? it - kStages : 0; g < it; ++g)
-          mbar_drain(&sm.full[g % kStages], (g / kStages) & 1, p.status);
-      }
-    }
-  } else if (warp == kMmaWarp) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(kBF16, kBM, kBN, false, false);
-      uint32_t it = 0, tcount = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x, ++tcount) {
-        const uint32_t acc = tcount % 2;
-        if (tcount >= 2 &&
-            !(ok = mbar_wait(&sm.acc_empty[acc], ((tcount / 2) - 1) & 1, abort_flag, p.status)))
-          break;
-        tc_fence_after();
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const uint32_t s = it % kStages;
-          if (!(ok = mbar_wait(&sm.full[s], (it / kStages) & 1, abort_flag, p.status))) break;
-          tc_fence_after();
-          const uint32_t abase = smem_u32(sm.a[s]);
-          const uint32_t bbase = smem_u32(sm.b[s]);
-#pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            // a K step is 32 bytes into the 128-byte swizzled rows of both operands
-            umma_ss(tmem + acc * kBN, smem_desc_sw128(abase + kk * 32, 16, 1024),
-                    smem_desc_sw128(bbase + kk * 32, 16, 1024), idesc,
-                    (kb > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(&sm.empty[s]);
-        }
-        if (ok) tc_commit(&sm.acc_full[acc]);
-      }
-      tc_commit(&sm.drain);
-      mbar_drain(&sm.drain, 0, p.status);
-    }
-  } else if (warp >= kEpiWarp0) {
-    const int quarter = (warp - kEpiWarp0) % 4;   // TMEM lanes [32 quarter, +32)
-    const int hb = (warp - kEpiWarp0) / 4;        // head block (128 columns) of the tile
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    uint32_t tcount = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++tcount) {
-      const uint32_t acc = tcount % 2;
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait(&sm.acc_full[acc], (tcount / 2) & 1, abort_flag, p.status));
-      if (!ok) break;
-      tc_fence_after();
-      const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
-      const int64_t m = int64_t(mt) * kBM + quarter * 32 + lane;
-      head_block<kBF16, kCos, kRope>(p, tmem + lane_off + acc * kBN + hb * 128, m,
-                                     nt * kBN + hb * 128);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -555,25 +421,6 @@ bool encode_matrix(CUtensorMap* map, const void* base, int64_t rows, int64_t col
 }
 
 template <bool kBF16, bool kCos, bool kRope>
-cudaError_t launch_t(const CUtensorMap& tx, const CUtensorMap& tw, const Params& p, int grid,
-                     cudaStream_t st) {
-  auto kern = qkv_project_kernel<kBF16, kCos, kRope>;
-  const size_t smem = sizeof(Smem) + 1024;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    attr_set[dev & 63] = true;
-  }
-  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, st, tx, tw, p);
-  if (e != cudaSuccess) return e;
-  return cudaGetLastError();
-}
-
-template <bool kBF16, bool kCos, bool kRope>
 cudaError_t launch_pair_t(const CUtensorMap& tx, const CUtensorMap& tw, const Params& p, int grid,
                           cudaStream_t st) {
   auto kern = qkv_project_pair_kernel<kBF16, kCos, kRope>;
@@ -605,12 +452,9 @@ cudaError_t launch_qkv_project(const void* x, const void* w, const float* bias, 
   using namespace sm100::qkvproj;
   CUtensorMap tx, tw;
   const int64_t M = batch * seq_len;
-  // CTA pairs (256 x 256 tiles) unless HEATKV_QKV_PROJECT_PAIR=0
-  const char* pair_env = std::getenv("HEATKV_QKV_PROJECT_PAIR");
-  const bool use_pair = !(pair_env && pair_env[0] == '0');
-  const int wbox = use_pair ? 128 : kBN;
+  // each CTA of a pair loads 128 rows of x and 128 rows of W per K step
   if (!encode_matrix(&tx, x, M, embed_dim, bf16, kBM) ||
-      !encode_matrix(&tw, w, 3 * heads * 128, embed_dim, bf16, wbox))
+      !encode_matrix(&tw, w, 3 * heads * 128, embed_dim, bf16, 128))
     return cudaErrorInvalidValue;
   Params p{};
   p.rows = M;
@@ -637,25 +481,15 @@ cudaError_t launch_qkv_project(const void* x, const void* w, const float* bias, 
                 reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(cache_k) |
                 reinterpret_cast<uintptr_t>(cache_v)) & 31u) == 0 ? 1 : 0;
   const bool cos = scale_mul != nullptr, rope = rope_cos != nullptr;
-  if (use_pair) {
-    const int64_t pair_tiles = (M + 255) / 256 * p.n_tiles;
-    const int grid = 2 * static_cast<int>(std::min<int64_t>(pair_tiles, sm100::sm_count() / 2));
+  const int64_t pair_tiles = (M + 255) / 256 * p.n_tiles;
+  const int grid = 2 * static_cast<int>(std::min<int64_t>(pair_tiles, sm100::sm_count() / 2));
 #define HEATKV_QKV_PROJ_PAIR(B)                                                      \
   (cos && rope ? launch_pair_t<B, true, true>(tx, tw, p, grid, st)                   \
    : cos       ? launch_pair_t<B, true, false>(tx, tw, p, grid, st)                  \
    : rope      ? launch_pair_t<B, false, true>(tx, tw, p, grid, st)                  \
                : launch_pair_t<B, false, false>(tx, tw, p, grid, st))
-    return bf16 ? HEATKV_QKV_PROJ_PAIR(true) : HEATKV_QKV_PROJ_PAIR(false);
+  return bf16 ? HEATKV_QKV_PROJ_PAIR(true) : HEATKV_QKV_PROJ_PAIR(false);
 #undef HEATKV_QKV_PROJ_PAIR
-  }
-  const int grid = static_cast<int>(std::min<int64_t>(p.tiles, sm100::sm_count()));
-#define HEATKV_QKV_PROJ(B)                                                           \
-  (cos && rope ? launch_t<B, true, true>(tx, tw, p, grid, st)                        \
-   : cos       ? launch_t<B, true, false>(tx, tw, p, grid, st)                       \
-   : rope      ? launch_t<B, false, true>(tx, tw, p, grid, st)                       \
-               : launch_t<B, false, false>(tx, tw, p, grid, st))
-  return bf16 ? HEATKV_QKV_PROJ(true) : HEATKV_QKV_PROJ(false);
-#undef HEATKV_QKV_PROJ
 }
 
 }  // namespace heatkv

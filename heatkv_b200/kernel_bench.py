@@ -86,6 +86,9 @@ def main(argv=None):
     ap.add_argument("--heads", type=int, default=16)
     ap.add_argument("--q-len", type=int, default=4096)
     ap.add_argument("--slots", type=int, default=650)
+    ap.add_argument("--no-cos", action="store_true",
+                    help="qkv-project: without the cos-attention normalisation")
+    ap.add_argument("--no-rope", action="store_true", help="qkv-project: without the RoPE")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--dtype", choices=["bf16", "f16", "f32", "f32qk"], default="bf16",
@@ -112,13 +115,15 @@ def main(argv=None):
         def fused():
             _native.check(lib.heatkv_qkv_project(
                 _native.ptr(x), _native.ptr(w), None, _native.ptr(q), _native.ptr(k),
-                _native.ptr(v), _native.DTYPE_CODES[torch.bfloat16], B, L, H, C, _native.ptr(sm),
-                ctypes.c_float(1e-12), _native.ptr(cos), _native.ptr(sin), 64, None, None, 0,
-                None, stream), "heatkv_qkv_project")
+                _native.ptr(v), _native.DTYPE_CODES[torch.bfloat16], B, L, H, C,
+                None if args.no_cos else _native.ptr(sm), ctypes.c_float(1e-12),
+                None if args.no_rope else _native.ptr(cos), None if args.no_rope else _native.ptr(sin),
+                64, None, None, 0, None, stream), "heatkv_qkv_project")
         flops = 2.0 * B * L * C * 3 * C
         ms = time_call(fused, args.iters, args.warmup)
         ms_mm = time_call(lambda: torch.mm(x, w.t(), out=out), args.iters, args.warmup)
-        print(f"qkv-project rows={B} q_len={L} heads={H}: fused {ms * 1e3:.1f} us "
+        mode = ("" if not args.no_cos else " no-cos") + ("" if not args.no_rope else " no-rope")
+        print(f"qkv-project rows={B} q_len={L} heads={H}{mode}: fused {ms * 1e3:.1f} us "
               f"({flops / ms / 1e9:.1f} TFLOP/s), cuBLAS GEMM alone {ms_mm * 1e3:.1f} us "
               f"({flops / ms_mm / 1e9:.1f} TFLOP/s)", flush=True)
     elif args.kernel == "projected-step":

@@ -41,20 +41,13 @@ def _close(a, b):
     return err <= 1e-2 * max(b.abs().max().item(), 1e-6) and same >= 0.99, (err, same)
 
 
-@pytest.fixture(params=["pair", "single"])
-def variant(request, monkeypatch):
-    """The CTA-pair kernel (256 x 256 tiles, default) and the single-CTA kernel."""
-    monkeypatch.setenv("HEATKV_QKV_PROJECT_PAIR", "1" if request.param == "pair" else "0")
-    return request.param
-
-
 @pytest.mark.parametrize("dtype,B,L,H,C,cos_attn,rope", [
     (torch.bfloat16, 2, 400, 16, 2048, True, True),
     (torch.bfloat16, 3, 64, 2, 512, True, False),
     (torch.float16, 1, 257, 4, 256, False, True),
     (torch.bfloat16, 2, 1, 16, 2048, False, False),
 ])
-def test_fused_projection_matches_gemm_then_prepare(dtype, B, L, H, C, cos_attn, rope, variant):
+def test_fused_projection_matches_gemm_then_prepare(dtype, B, L, H, C, cos_attn, rope):
     torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
     torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
     dev = torch.device("cuda", 0)
@@ -91,7 +84,7 @@ def test_fused_projection_matches_gemm_then_prepare(dtype, B, L, H, C, cos_attn,
         assert ok, info
 
 
-def test_fused_projection_flags_a_cache_offset_past_the_end(variant):
+def test_fused_projection_flags_a_cache_offset_past_the_end():
     dev = torch.device("cuda", 0)
     B, L, H, C = 1, 64, 2, 256
     x = torch.randn(B * L, C, device=dev).bfloat16()
@@ -106,7 +99,7 @@ def test_fused_projection_flags_a_cache_offset_past_the_end(variant):
     assert (ck[:, L:] == 0).all() and (ck[:, :L] != 0).any()
 
 
-def test_fused_projection_adds_the_bias(variant):
+def test_fused_projection_adds_the_bias():
     """``bias`` = cat(q_bias, zero_k_bias, v_bias) as the reference's F.linear adds it
     (enable_real_pruning_fast.py:2040-2043), against cuBLAS addmm then the preparation."""
     torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
