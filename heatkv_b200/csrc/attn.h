@@ -129,7 +129,7 @@ cudaError_t launch_qkv_project(const void* x, const void* w, const float* bias, 
                                void* v, bool bf16, int64_t batch, int64_t seq_len, int64_t heads,
                                int64_t embed_dim, const float* scale_mul, float eps,
                                const float* rope_cos, const float* rope_sin,
-                               int64_t rope_row_stride, void* cache_k, void* cache_v,
+                               int64_t rope_group_stride, void* cache_k, void* cache_v,
                                int64_t cache_rows, const int64_t* cache_offset,
                                unsigned int* status, cudaStream_t st);
 

@@ -643,7 +643,7 @@ int heatkv_qkv_project(const void* x, const void* w, const float* bias, void* q,
                        int dtype,
                        int64_t batch, int64_t seq_len, int64_t heads, int64_t embed_dim,
                        const float* scale_mul, float eps, const float* rope_cos,
-                       const float* rope_sin, int64_t rope_row_stride, void* cache_k,
+                       const float* rope_sin, int64_t rope_group_stride, void* cache_k,
                        void* cache_v, int64_t cache_rows, const int64_t* cache_offset,
                        void* stream) {
   static const char* name = "heatkv_qkv_project";
@@ -663,9 +663,9 @@ int heatkv_qkv_project(const void* x, const void* w, const float* bias, void* q,
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
   if (cache_offset && (!cache_k || !cache_v))
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: cache offsets given without caches", name);
-  if (rope_cos && (rope_row_stride < 64 || (rope_row_stride & 3)))
+  if (rope_cos && (rope_group_stride < 4 * seq_len || (rope_group_stride & 3)))
     return fail(HEATKV_ERR_INVALID_ARGUMENT,
-                "%s: rope_row_stride must be a multiple of 4 and at least 64", name);
+                "%s: rope_group_stride must be a multiple of 4 and at least 4 * seq_len", name);
   if (!(eps >= 0.f)) return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: eps must be >= 0", name);
   const uintptr_t a16 = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
                         reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
@@ -677,7 +677,7 @@ int heatkv_qkv_project(const void* x, const void* w, const float* bias, void* q,
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: misaligned pointer", name);
   cudaError_t e = heatkv::launch_qkv_project(
       x, w, bias, q, k, v, dtype == HEATKV_DTYPE_BF16, batch, seq_len, heads, embed_dim, scale_mul, eps,
-      rope_cos, rope_sin, rope_row_stride, cache_offset ? cache_k : nullptr,
+      rope_cos, rope_sin, rope_group_stride, cache_offset ? cache_k : nullptr,
       cache_offset ? cache_v : nullptr, cache_rows, cache_offset, heatkv::device_status_ptr(),
       static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, name);

@@ -60,9 +60,9 @@ struct Params {
   const float* bias;     // [3 * H * 128] fp32, or null
   const float* scale_mul;
   float eps;
-  const float* rope_cos;
+  const float* rope_cos;  // pair-group-major: pairs 4g..4g+3 of token l at (g * stride + l) * 4
   const float* rope_sin;
-  int64_t rope_stride;
+  int64_t rope_stride;    // floats between consecutive pair groups
   void* cache_k;
   void* cache_v;
   int64_t cache_rows;
@@ -155,11 +155,14 @@ __device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int6
       }
     }
     if (kRope && prep) {
-      const float4* cr = reinterpret_cast<const float4*>(p.rope_cos + l * p.rope_stride) + half * 8;
-      const float4* sr = reinterpret_cast<const float4*>(p.rope_sin + l * p.rope_stride) + half * 8;
+      // pair-group-major tables: the 32 lanes (consecutive tokens) of a warp load 512 contiguous
+      // bytes per group, where a token-major table made every load touch 32 cache lines
+      const float* cbase = p.rope_cos + l * 4 + int64_t(half) * 8 * p.rope_stride;
+      const float* sbase = p.rope_sin + l * 4 + int64_t(half) * 8 * p.rope_stride;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {  // pairs 4j .. 4j + 3 of this half
-        const float4 c = __ldg(cr + j), s = __ldg(sr + j);
+        const float4 c = __ldg(reinterpret_cast<const float4*>(cbase + j * p.rope_stride));
+        const float4 s = __ldg(reinterpret_cast<const float4*>(sbase + j * p.rope_stride));
         const float cc[4] = {c.x, c.y, c.z, c.w}, sc[4] = {s.x, s.y, s.z, s.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -446,7 +449,7 @@ cudaError_t launch_qkv_project(const void* x, const void* w, const float* bias, 
                                void* v, bool bf16, int64_t batch, int64_t seq_len, int64_t heads,
                                int64_t embed_dim, const float* scale_mul, float eps,
                                const float* rope_cos, const float* rope_sin,
-                               int64_t rope_row_stride, void* cache_k, void* cache_v,
+                               int64_t rope_group_stride, void* cache_k, void* cache_v,
                                int64_t cache_rows, const int64_t* cache_offset,
                                unsigned int* status, cudaStream_t st) {
   using namespace sm100::qkvproj;
@@ -471,7 +474,7 @@ cudaError_t launch_qkv_project(const void* x, const void* w, const float* bias, 
   p.eps = eps;
   p.rope_cos = rope_cos;
   p.rope_sin = rope_sin;
-  p.rope_stride = rope_row_stride;
+  p.rope_stride = rope_group_stride;
   p.cache_k = cache_k;
   p.cache_v = cache_v;
   p.cache_rows = cache_rows;

@@ -107,7 +107,8 @@ def main(argv=None):
                    for _ in range(3))
         sm = torch.full((H,), 4.0, device="cuda")
         ang = torch.rand(L, 64, device="cuda", generator=g) * 6
-        cos, sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()
+        from .qkv_prep import rope_pair_groups
+        cos, sin = rope_pair_groups(torch.cos(ang)), rope_pair_groups(torch.sin(ang))
         lib = _native.load()
         stream = _native.stream_handle(torch.device("cuda"))
         out = torch.empty(B * L, 3 * C, device="cuda", dtype=torch.bfloat16)
@@ -118,7 +119,7 @@ def main(argv=None):
                 _native.ptr(v), _native.DTYPE_CODES[torch.bfloat16], B, L, H, C,
                 None if args.no_cos else _native.ptr(sm), ctypes.c_float(1e-12),
                 None if args.no_rope else _native.ptr(cos), None if args.no_rope else _native.ptr(sin),
-                64, None, None, 0, None, stream), "heatkv_qkv_project")
+                4 * L, None, None, 0, None, stream), "heatkv_qkv_project")
         flops = 2.0 * B * L * C * 3 * C
         ms = time_call(fused, args.iters, args.warmup)
         ms_mm = time_call(lambda: torch.mm(x, w.t(), out=out), args.iters, args.warmup)

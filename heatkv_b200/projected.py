@@ -37,6 +37,7 @@ import torch
 
 from . import _native, synthetic
 from .hotpath import HotPath, Launch, _dev
+from .qkv_prep import rope_pair_groups
 from .scheduler import copy_descriptors, prep_append_split
 
 
@@ -114,6 +115,9 @@ class ProjectedHotPath:
             if cos.shape[0] < total:
                 raise ValueError("rope table shorter than the schedule")
             self.rope_cos, self.rope_sin = cos.to(self.device), sin.to(self.device)
+            # the fused projection reads the pair-group-major order (coalesced per warp)
+            self.rope_cos_g = rope_pair_groups(self.rope_cos)
+            self.rope_sin_g = rope_pair_groups(self.rope_sin)
         else:
             self.rope_cos = self.rope_sin = None
         # scratch shared by every (scale, layer) call (the projection output only without the
@@ -228,10 +232,13 @@ class ProjectedHotPath:
                 w = self.weights[i]
                 flops = 2.0 * B * n * C * w.shape[0]
                 target = self.prep_target.get((i, t))
-                cos = sin = None
+                cos = sin = cos_g = sin_g = None
                 if self.rope_cos is not None:
                     cos = ctypes.c_void_p(self.rope_cos.data_ptr() + self.starts[t] * 64 * 4)
                     sin = ctypes.c_void_p(self.rope_sin.data_ptr() + self.starts[t] * 64 * 4)
+                    cos_g = ctypes.c_void_p(self.rope_cos_g.data_ptr() + self.starts[t] * 4 * 4)
+                    sin_g = ctypes.c_void_p(self.rope_sin_g.data_ptr() + self.starts[t] * 4 * 4)
+                    group_stride = 4 * self.rope_cos_g.shape[1]
                 written = 0 if target is None else target[4]
                 if self.fused_projection:
                     # x read once per column panel from HBM, q/k/v and the early cache rows written
@@ -242,8 +249,9 @@ class ProjectedHotPath:
                         (_native.ptr(x2d), _native.ptr(w), _native.ptr(self.biases[i]),
                          _native.ptr(q), _native.ptr(k),
                          _native.ptr(v), code, B, n, H, C, _native.ptr(self.scale_mul),
-                         ctypes.c_float(1e-12), cos, sin, 64, _native.ptr(sk), _native.ptr(sv),
-                         rows_, _native.ptr(offs)), flops))
+                         ctypes.c_float(1e-12), cos_g, sin_g,
+                         group_stride if cos_g is not None else 0, _native.ptr(sk),
+                         _native.ptr(sv), rows_, _native.ptr(offs)), flops))
                     out_launches[-1].nbytes = nbytes
                 else:
                     def gemm(stream, x2d=x2d, w=w, qkv=qkv, b=self.biases[i]):

@@ -52,6 +52,18 @@ def rope_rows(rope2d_freqs_grid, scale_schedule, scale_ind: int, seq_len: int,
     return rows[0], rows[1]
 
 
+def rope_pair_groups(table: torch.Tensor) -> torch.Tensor:
+    """A token-major rope table ``[T, 64]`` (cos or sin of the 64 rotary pairs of each token) in
+    the pair-group-major order ``heatkv_qkv_project`` reads, ``[16, T, 4]``: pairs ``4g .. 4g+3``
+    of token ``l`` at ``[g, l]``, so the consecutive tokens of a warp's rows are contiguous. The
+    scale starting at token ``s`` passes ``table[:, s:]`` (the pointer ``s * 4`` floats in) and
+    ``rope_group_stride = 4 * T``."""
+    if table.ndim != 2 or table.shape[1] != 64:
+        raise ValueError("rope_pair_groups expects a [T, 64] table")
+    T = table.shape[0]
+    return table.float().reshape(T, 16, 4).permute(1, 0, 2).contiguous()
+
+
 def prepare_qkv(qkv: torch.Tensor, *, scale_mul: Optional[torch.Tensor] = None,
                 eps: float = 1e-12, rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
                 qk_dtype: Optional[torch.dtype] = None,

@@ -441,7 +441,10 @@ int heatkv_qkv_prepare_append(const void* qkv, void* q, void* k, void* v, int in
  *             added to the fp32 accumulator before the rounding to dtype
  *   q, k, v : [batch, heads, seq_len, 128] (dtype). The projection is rounded to dtype, then
  *             prepared as heatkv_qkv_prepare does (scale_mul: cos-attention; rope: the rotary
- *             rows of the scale's tokens, rope_row_stride floats apart)
+ *             angles of the scale's tokens in pair-group-major order - the cos (sin) of pairs
+ *             4g .. 4g+3 of token l at rope_cos[(g * rope_group_stride) + 4 * l + 0..3], g < 16,
+ *             i.e. a [16, tokens, 4] table with rope_group_stride = 4 * its tokens, from the
+ *             scale's first token; rope_group_stride >= 4 * seq_len, a multiple of 4)
  *   cache_* : as heatkv_qkv_prepare_append's slab (cache_offset -1 = head not written); rows of
  *             the heads given an offset are written from the same registers
  * heads must be even, embed_dim a multiple of 64; x, w, bias, q, k, v, the rope rows and the
@@ -452,7 +455,7 @@ int heatkv_qkv_project(const void* x, const void* w, const float* bias, void* q,
                        int dtype,
                        int64_t batch, int64_t seq_len, int64_t heads, int64_t embed_dim,
                        const float* scale_mul, float eps, const float* rope_cos,
-                       const float* rope_sin, int64_t rope_row_stride, void* cache_k,
+                       const float* rope_sin, int64_t rope_group_stride, void* cache_k,
                        void* cache_v, int64_t cache_rows, const int64_t* cache_offset,
                        void* stream);
 

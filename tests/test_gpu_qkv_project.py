@@ -12,7 +12,7 @@ import pytest
 import torch
 
 from heatkv_b200 import _native
-from heatkv_b200.qkv_prep import prepare_qkv
+from heatkv_b200.qkv_prep import prepare_qkv, rope_pair_groups
 
 pytestmark = pytest.mark.gpu
 
@@ -23,13 +23,13 @@ def _project(x, w, B, L, H, scale_mul=None, rope=None, cache=None, bias=None):
     q, k, v = (torch.empty(B, H, L, 128, dtype=x.dtype, device=dev) for _ in range(3))
     cos = sin = None
     if rope is not None:
-        cos, sin = rope
+        cos, sin = (rope_pair_groups(t) for t in rope)
     ck, cv, rows, offs = cache if cache is not None else (None, None, 0, None)
     _native.check(lib.heatkv_qkv_project(
         _native.ptr(x), _native.ptr(w), _native.ptr(bias), _native.ptr(q), _native.ptr(k),
         _native.ptr(v), _native.DTYPE_CODES[x.dtype], B, L, H, x.shape[-1], _native.ptr(scale_mul),
         ctypes.c_float(1e-12), _native.ptr(cos), _native.ptr(sin),
-        0 if cos is None else cos.stride(0), _native.ptr(ck), _native.ptr(cv), rows,
+        0 if cos is None else 4 * cos.shape[1], _native.ptr(ck), _native.ptr(cv), rows,
         _native.ptr(offs), _native.stream_handle(dev)), "heatkv_qkv_project")
     return q, k, v
 
