@@ -960,7 +960,7 @@ def run_projected(args, rank: int, world: int, local_rank: int) -> None:
         "roofline_qkv": ({"bound": "tensor", "peak": sustained, "unit": "TFLOP/s",
                           "achieved": round(gemm_flops / (proj_ms * 1e-3) / 1e12, 1),
                           "frac": round(gemm_flops / (proj_ms * 1e-3) / 1e12 / sustained, 4),
-                          "kernel": "qkv_project_kernel", "ms_per_step": round(proj_ms, 3),
+                          "kernel": "qkv_project_pair_kernel", "ms_per_step": round(proj_ms, 3),
                           "hbm_gb_per_step": round(proj_bytes / 1e9, 3)}
                          if proj.fused_projection else
                          {"bound": "hbm", "peak": hbm, "unit": "GB/s",
