@@ -209,9 +209,18 @@ def _dev(x: np.ndarray, device, dtype=None) -> torch.Tensor:
 
 
 class LayerPlan:
-    """Slab schedule of one layer, resident on ``device``."""
+    """Slab schedule of one layer, resident on ``device``.
 
-    def __init__(self, controller, layer_idx: int, num_heads: int, device, schedule=None):
+    ``merge_prefix``: the leading source scales that every head keeps at every fused target (the
+    protected prefix, scales 0-2 = 21 tokens at 1024^2) sit in the reference's slab layout as one
+    short segment each - three 64-key tiles for 21 keys. With the flag, the activation also copies
+    each head's prefix tokens into an extra region past the reference layout (rows ``capacity_ref
+    + h * prefix_len``), and the segment tables of the fused targets name that contiguous copy as
+    one segment instead: the same keys in the same order, in one tile. The reference-layout region
+    of the slab keeps its bytes."""
+
+    def __init__(self, controller, layer_idx: int, num_heads: int, device, schedule=None,
+                 merge_prefix: bool = False):
         self.layer = int(layer_idx)
         self.num_heads = int(num_heads)
         self.ranges = controller.scale_ranges
@@ -264,9 +273,14 @@ class LayerPlan:
                                    _dev(arr[:, 2], device), len(items), int(arr[:, 2].max()),
                                    int(arr[:, 2].sum()))
         # fused targets: slab metadata and appends
+        self.capacity_ref = self.capacity
+        self.prefix_scales, self.prefix_len = 0, 0
+        metas = {t: sched["metadata_cpu_by_target"][t] for t in range(t0, self.num_scales)}
+        if merge_prefix and t0 < self.num_scales:
+            metas = self._merge_prefix(metas, device,
+                                       int(getattr(controller, "source_scale_start", 0) or 0))
         self.slab_meta = {}
-        for t in range(t0, self.num_scales):
-            st, en, ct = sched["metadata_cpu_by_target"][t]
+        for t, (st, en, ct) in metas.items():
             self.slab_meta[t] = (_dev(st, device), _dev(en, device), _dev(ct, device), (st, en, ct))
         self.slab_append = {}
         for t in range(t0, self.num_scales - 1):
@@ -276,6 +290,56 @@ class LayerPlan:
             self.slab_append[t] = (_dev(d["dst_starts"], device), _dev(d["src_starts"], device),
                                    _dev(d["lengths"], device), d["item_count"], d["max_length"],
                                    d["slots"])
+
+    def _merge_prefix(self, metas, device, protected: int):
+        """The protected prefix scales (``protected`` = the controller's first source scale: the
+        scales before it are never removed), merged into one segment per head over a contiguous
+        copy past the reference layout (see the class doc). Only the protected prefix, not every
+        scale a particular set of heads happens to keep, so that a layer's tiles - and results -
+        do not depend on which heads a plan holds (a head-sharded rank computes the same bits as
+        one GPU)."""
+        H, Ld, t0 = self.num_heads, self.dense_len, self.first_target
+        sched = self.schedule
+        live = [{(seg["source_scale"], seg["head"]): seg["offset"]
+                 for seg in sched["segments_by_target"][t]} for t in range(t0, self.num_scales)]
+        P = 0
+        while P < min(protected, t0) and all((P, h) in lv for lv in live for h in range(H)):
+            P += 1
+        if P < 2:
+            return metas
+        plen = int(self.ranges[P][0])
+        # the first P segments of every head, in source order, must be exactly those scales
+        for (st, en, ct), lv in zip(metas.values(), live):
+            for h in range(H):
+                if int(ct[h]) < P:
+                    return metas
+                for s in range(P):
+                    if int(st[h, s]) != lv[(s, h)] or int(en[h, s] - st[h, s]) != self.tokens[s]:
+                        return metas
+        base = self.capacity_ref
+        out = {}
+        for t, (st, en, ct) in metas.items():
+            S = st.shape[1]
+            st2 = np.zeros((H, max(S - P + 1, 1)), dtype=st.dtype)
+            en2 = np.zeros_like(st2)
+            st2[:, 0] = base + np.arange(H) * plen
+            en2[:, 0] = st2[:, 0] + plen
+            st2[:, 1:] = st[:, P:]
+            en2[:, 1:] = en[:, P:]
+            out[t] = (st2, en2, (ct - P + 1).astype(ct.dtype))
+        # the activation also writes the contiguous prefix copy (dense rows h*Ld .. h*Ld + plen)
+        items = [(base + h * plen, h * Ld, plen) for h in range(H)]
+        if self.activation is not None:
+            d, s_, l_ = (x.cpu().numpy() for x in self.activation[:3])
+            items += list(zip(d.tolist(), s_.tolist(), l_.tolist()))
+        items.sort()
+        arr = np.array(items, dtype=np.int64)
+        self.activation = (_dev(arr[:, 0], device), _dev(arr[:, 1], device),
+                           _dev(arr[:, 2], device), len(items), int(arr[:, 2].max()),
+                           int(arr[:, 2].sum()))
+        self.capacity = base + H * plen
+        self.prefix_scales, self.prefix_len = P, plen
+        return out
 
     def kernel_segment_lengths(self, t: int, current_in_cache: bool):
         """Per head, the segment lengths the kernel walks at target t, and whether the current
@@ -309,7 +373,7 @@ class HotPath:
     def __init__(self, controller, num_layers: int, num_heads: int, batch: int, device,
                  k_dtype=torch.bfloat16, v_dtype=torch.bfloat16, head_dim: int = 128,
                  layers: Optional[list] = None, plan_splits=None,
-                 dense_append_first: Optional[bool] = None):
+                 dense_append_first: Optional[bool] = None, merge_prefix: bool = True):
         import os
         self.device = torch.device(device)
         # dense targets: append the scale to the dense cache before its attention, which then
@@ -323,7 +387,10 @@ class HotPath:
         self.batch = int(batch)
         self.head_dim = int(head_dim)
         self.k_dtype, self.v_dtype = k_dtype, v_dtype
-        self.plans = [LayerPlan(controller, l, num_heads, self.device) for l in
+        # the protected prefix scales as one segment per head at the fused targets (LayerPlan)
+        self.merge_prefix = bool(merge_prefix)
+        self.plans = [LayerPlan(controller, l, num_heads, self.device,
+                                merge_prefix=self.merge_prefix) for l in
                       (layers if layers is not None else range(num_layers))]
         self.num_scales = self.plans[0].num_scales
         self.tokens = self.plans[0].tokens

@@ -170,3 +170,32 @@ def test_dense_append_first_matches_append_after():
         err = (a.float() - b.float()).abs().max().item()
         assert err <= BF16_ATOL and err / max(b.float().abs().max().item(), 1e-6) <= BF16_REL
     assert _native.device_status(dev) == 0
+
+
+def test_merged_prefix_matches_reference_layout():
+    """The protected prefix scales read as one segment per head from a contiguous copy past the
+    reference slab layout (HotPath(merge_prefix=True), the default) against the reference layout's
+    three segments: the reference region of every slab bit for bit, outputs within bf16 tolerance
+    (only the key-tile partition differs), and fewer key tiles."""
+    ctrl, L, H = _controller("2b", 0.10)
+    dev = torch.device("cuda", 0)
+    layers = [2, 21]
+    results = []
+    for merge in (False, True):
+        hot = HotPath(ctrl, L, H, 2, dev, layers=layers, merge_prefix=merge)
+        inputs, outputs, _, _ = allocate_io(hot, seed=13)
+        hot.run(hot.launches(inputs, outputs))
+        torch.cuda.synchronize()
+        assert _native.device_status(dev) == 0
+        results.append((hot, [o.clone() for row in outputs for o in row],
+                        [s.clone() for s in hot.slab_k + hot.slab_v]))
+    (h0, out0, slab0), (h1, out1, slab1) = results
+    for p0, p1 in zip(h0.plans, h1.plans):
+        assert p1.prefix_scales == 3 and p1.capacity == p0.capacity + H * p1.prefix_len
+        t = p1.first_target
+        assert sum(map(len, p1.segment_lengths(t))) == sum(map(len, p0.segment_lengths(t))) - 2 * H
+    for a, b in zip(slab0, slab1):
+        assert torch.equal(a, b[:, :a.shape[1]])
+    for a, b in zip(out0, out1):
+        err = (a.float() - b.float()).abs().max().item()
+        assert err <= BF16_ATOL and err / max(b.float().abs().max().item(), 1e-6) <= BF16_REL
