@@ -300,6 +300,38 @@ def _items_desc(items, seq_len: int, device):
     return dst, src, ln, max(it[3] for it in items), sum(it[3] for it in items)
 
 
+def _derived(module, name: str, params, make):
+    """``make()`` computed once per module and reused while ``params`` (tensors it is derived
+    from) keep their data pointer and version: inference calls need not rebuild the QKV bias
+    (torch.cat of three parameters) or the cos-attention head scale (clamp_max + exp) every
+    scale and layer, while an update of a parameter still takes effect. With autograd enabled the
+    value is rebuilt every call, so gradients still reach the parameters."""
+    if torch.is_grad_enabled():
+        return make()
+    key = tuple((p.data_ptr(), p._version, p.device, p.dtype) for p in params)
+    cache = module.__dict__.setdefault("_heatkv_derived", {})
+    hit = cache.get(name)
+    if hit is not None and hit[0] == key:
+        return hit[1]
+    value = make()
+    cache[name] = (key, value)
+    return value
+
+
+def _qkv_bias(module) -> torch.Tensor:
+    """``cat(q_bias, zero_k_bias, v_bias)`` (enable_real_pruning_fast.py:2043)."""
+    ps = (module.q_bias, module.zero_k_bias, module.v_bias)
+    return _derived(module, "qkv_bias", ps, lambda: torch.cat(ps))
+
+
+def _head_scale(module) -> torch.Tensor:
+    """The cos-attention head scale ``scale_mul_1H11.clamp_max(max_scale_mul).exp()``
+    (:2051-2055) as ``[1, H, 1, 1]``."""
+    p = module.scale_mul_1H11
+    return _derived(module, "scale_mul", (p,), lambda: p.reshape(
+        1, module.num_heads, 1, 1).clamp_max(module.max_scale_mul).exp())
+
+
 def _fused_prep_applies(module, qkv) -> bool:
     """The one-pass q/k/v preparation reproduces the PyTorch chain's dtypes here."""
     return (bool(getattr(module, "_heatkv_fused_qkv_prep", False)) and qkv.is_cuda
@@ -455,7 +487,7 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
         return output
 
     qkv = F.linear(input=x, weight=self.mat_qkv.weight,
-                   bias=torch.cat((self.q_bias, self.zero_k_bias, self.v_bias))).view(
+                   bias=_qkv_bias(self)).view(
         batch_size, seq_len, 3, self.num_heads, self.head_dim)
     if rope2d_freqs_grid is not None and scale_schedule is None:
         raise ValueError("scale_schedule is required when rope2d_freqs_grid is provided")
@@ -466,8 +498,7 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
     if _fused_prep_applies(self, qkv):
         scale_mul = None
         if self.cos_attn:
-            scale_mul = self.scale_mul_1H11.reshape(1, self.num_heads, 1, 1).clamp_max(
-                self.max_scale_mul).exp()
+            scale_mul = _head_scale(self)
         rope = None
         if rope2d_freqs_grid is not None:
             rope = _qkv_prep.rope_rows(rope2d_freqs_grid, scale_schedule, scale_ind, seq_len,
@@ -505,8 +536,7 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
         v = v.permute(0, 2, 1, 3).contiguous()
         del qkv
         if self.cos_attn:
-            scale_mul = self.scale_mul_1H11.reshape(1, self.num_heads, 1, 1).clamp_max(
-                self.max_scale_mul).exp()
+            scale_mul = _head_scale(self)
             q = F.normalize(q, dim=-1, eps=1e-12).mul(scale_mul).contiguous()
             k = F.normalize(k, dim=-1, eps=1e-12).contiguous()
             v = v.contiguous()
