@@ -80,7 +80,7 @@ SIGNATURES = {
                                 ctypes.c_float, _p, _p, _i64, _p]),
     "heatkv_qkv_prepare_append": (_i, [_p, _p, _p, _p, _i, _i, _i64, _i64, _i64, _i64, _p,
                                        ctypes.c_float, _p, _p, _i64, _p, _p, _i64, _p, _p]),
-    "heatkv_qkv_project": (_i, [_p, _p, _p, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p,
+    "heatkv_qkv_project": (_i, [_p, _p, _p, _p, _p, _p, _i, _i, _i64, _i64, _i64, _i64, _p,
                                 ctypes.c_float, _p, _p, _i64, _p, _p, _i64, _p, _p]),
     "heatkv_slot_tables": (_i, [_i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "heatkv_strict_budget": (_i, [_p, _i, _i, _i, _i, _p, _i, _i, _i, ctypes.c_double, _p, _p,

@@ -126,7 +126,7 @@ cudaError_t launch_scas_mass_tc(const float* q, const float* k, int64_t heads, i
 
 // q/k/v preparation after the QKV projection (qkv_prep.cu); sms = SMs of the device.
 cudaError_t launch_qkv_project(const void* x, const void* w, const float* bias, void* q, void* k,
-                               void* v, bool bf16, int64_t batch, int64_t seq_len, int64_t heads,
+                               void* v, bool bf16, bool qk32, int64_t batch, int64_t seq_len, int64_t heads,
                                int64_t embed_dim, const float* scale_mul, float eps,
                                const float* rope_cos, const float* rope_sin,
                                int64_t rope_group_stride, void* cache_k, void* cache_v,

@@ -640,7 +640,7 @@ int heatkv_qkv_prepare_append(const void* qkv, void* q, void* k, void* v, int in
 }
 
 int heatkv_qkv_project(const void* x, const void* w, const float* bias, void* q, void* k, void* v,
-                       int dtype,
+                       int dtype, int qk_dtype,
                        int64_t batch, int64_t seq_len, int64_t heads, int64_t embed_dim,
                        const float* scale_mul, float eps, const float* rope_cos,
                        const float* rope_sin, int64_t rope_group_stride, void* cache_k,
@@ -650,6 +650,8 @@ int heatkv_qkv_project(const void* x, const void* w, const float* bias, void* q,
   g_last_error.clear();
   if (dtype != HEATKV_DTYPE_BF16 && dtype != HEATKV_DTYPE_F16)
     return fail(HEATKV_ERR_UNSUPPORTED, "%s: x and W must be bfloat16 or float16", name);
+  if (qk_dtype != dtype && qk_dtype != HEATKV_DTYPE_F32)
+    return fail(HEATKV_ERR_UNSUPPORTED, "%s: q and k must be float32 or the dtype of x", name);
   if (batch < 0 || seq_len < 0 || heads < 0 || embed_dim < 0 || cache_rows < 0)
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: negative size", name);
   if (heads % 2 != 0)
@@ -676,7 +678,7 @@ int heatkv_qkv_project(const void* x, const void* w, const float* bias, void* q,
   if ((a16 & 15u) || (reinterpret_cast<uintptr_t>(cache_offset) & 7u))
     return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: misaligned pointer", name);
   cudaError_t e = heatkv::launch_qkv_project(
-      x, w, bias, q, k, v, dtype == HEATKV_DTYPE_BF16, batch, seq_len, heads, embed_dim, scale_mul, eps,
+      x, w, bias, q, k, v, dtype == HEATKV_DTYPE_BF16, qk_dtype == HEATKV_DTYPE_F32, batch, seq_len, heads, embed_dim, scale_mul, eps,
       rope_cos, rope_sin, rope_group_stride, cache_offset ? cache_k : nullptr,
       cache_offset ? cache_v : nullptr, cache_rows, cache_offset, heatkv::device_status_ptr(),
       static_cast<cudaStream_t>(stream));

@@ -94,9 +94,8 @@ __device__ __forceinline__ float round16(float x) {
 // two 64-column halves (twice for q/k with cos-attention: once for the norm, once to write), which
 // keeps the live registers of the epilogue warps low. tcgen05.ld is warp-collective, so rows past
 // the end still load and only skip their stores.
-template <bool kBF16, bool kCos, bool kRope>
+template <bool kBF16, bool kCos, bool kRope, bool kQK32>
 __device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int64_t m, int col0) {
-  using T = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
   const bool live = m < p.rows;
   const int64_t mm = live ? m : 0;
   const int64_t H = p.heads;
@@ -126,20 +125,26 @@ __device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int6
     n = __frcp_rn(n);
     inv_scale = sec == 0 ? __ldg(p.scale_mul + h) : 1.f;
   }
-  T* out = static_cast<T*>(sec == 0 ? p.q : sec == 1 ? p.k : p.v);
-  uint4* dst = reinterpret_cast<uint4*>(out + ((b * H + h) * p.seq_len + l) * 128);
-  uint4* cd = nullptr;
+  // q and k as fp32 (the reference's chain under autocast normalises and rotates in fp32) or in
+  // the 16-bit dtype; v always in the 16-bit dtype. Row bytes: 128 elements of esz bytes.
+  const bool f32out = kQK32 && prep;
+  const int64_t esz = f32out ? 4 : 2;
+  uint8_t* outb = static_cast<uint8_t*>(sec == 0 ? p.q : sec == 1 ? p.k : p.v);
+  uint8_t* dstb = outb + ((b * H + h) * p.seq_len + l) * 128 * esz;
+  uint8_t* cdb = nullptr;
   if (live && sec >= 1 && p.cache_offset != nullptr) {
     const int64_t off = __ldg(p.cache_offset + h);
     if (off >= 0) {
       if (off > p.cache_rows - p.seq_len) {
         if (l == 0) raise_status(p.status, HEATKV_DEVICE_PACK_OUT_OF_RANGE);
       } else {
-        T* cache = static_cast<T*>(sec == 1 ? p.cache_k : p.cache_v);
-        cd = reinterpret_cast<uint4*>(cache + (b * p.cache_rows + off + l) * 128);
+        uint8_t* cache = static_cast<uint8_t*>(sec == 1 ? p.cache_k : p.cache_v);
+        cdb = cache + (b * p.cache_rows + off + l) * 128 * esz;
       }
     }
   }
+  uint4* dst = reinterpret_cast<uint4*>(dstb);
+  uint4* cd = reinterpret_cast<uint4*>(cdb);
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
     float x[64];
@@ -173,7 +178,26 @@ __device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int6
         }
       }
     }
-    if (live && p.align32) {
+    if (live && f32out) {
+      // 64 fp32 values = 256 bytes of this half's row
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t w[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) w[e] = __float_as_uint(x[8 * j + e]);
+        if (p.align32) {
+          st_global_v8(dstb + half * 256 + j * 32, w);
+          if (cdb != nullptr) st_global_v8(cdb + half * 256 + j * 32, w);
+        } else {
+          dst[half * 16 + 2 * j] = make_uint4(w[0], w[1], w[2], w[3]);
+          dst[half * 16 + 2 * j + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+          if (cd != nullptr) {
+            cd[half * 16 + 2 * j] = make_uint4(w[0], w[1], w[2], w[3]);
+            cd[half * 16 + 2 * j + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+          }
+        }
+      }
+    } else if (live && p.align32) {
       // one full 32-byte sector per store (each thread writes its own row)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -181,7 +205,7 @@ __device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int6
 #pragma unroll
         for (int e = 0; e < 8; ++e) w[e] = pack2<kBF16>(x[16 * j + 2 * e], x[16 * j + 2 * e + 1]);
         st_global_v8(dst + half * 8 + 2 * j, w);
-        if (cd != nullptr) st_global_v8(cd + half * 8 + 2 * j, w);
+        if (cdb != nullptr) st_global_v8(cd + half * 8 + 2 * j, w);
       }
     } else if (live) {
 #pragma unroll
@@ -191,7 +215,7 @@ __device__ __forceinline__ void head_block(const Params& p, uint32_t taddr, int6
                                    pack2<kBF16>(x[8 * j + 4], x[8 * j + 5]),
                                    pack2<kBF16>(x[8 * j + 6], x[8 * j + 7]));
         dst[half * 8 + j] = w;
-        if (cd != nullptr) cd[half * 8 + j] = w;
+        if (cdb != nullptr) cd[half * 8 + j] = w;
       }
     }
   }
@@ -275,7 +299,7 @@ __device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
       : "memory");
 }
 
-template <bool kBF16, bool kCos, bool kRope>
+template <bool kBF16, bool kCos, bool kRope, bool kQK32>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     qkv_project_pair_kernel(const __grid_constant__ CUtensorMap tm_x,
                             const __grid_constant__ CUtensorMap tm_w, const Params p) {
@@ -391,7 +415,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
       const int64_t m = int64_t(mt) * 256 + rank * 128 + quarter * 32 + lane;
-      head_block<kBF16, kCos, kRope>(p, tmem + lane_off + acc * kBN + hb * 128, m,
+      head_block<kBF16, kCos, kRope, kQK32>(p, tmem + lane_off + acc * kBN + hb * 128, m,
                                      nt * kBN + hb * 128);
       tc_fence_before();
       __syncwarp();
@@ -423,10 +447,10 @@ bool encode_matrix(CUtensorMap* map, const void* base, int64_t rows, int64_t col
   return r == CUDA_SUCCESS;
 }
 
-template <bool kBF16, bool kCos, bool kRope>
+template <bool kBF16, bool kCos, bool kRope, bool kQK32>
 cudaError_t launch_pair_t(const CUtensorMap& tx, const CUtensorMap& tw, const Params& p, int grid,
                           cudaStream_t st) {
-  auto kern = qkv_project_pair_kernel<kBF16, kCos, kRope>;
+  auto kern = qkv_project_pair_kernel<kBF16, kCos, kRope, kQK32>;
   const size_t smem = sizeof(PairSmem) + 1024;
   static bool attr_set[64] = {};
   int dev = 0;
@@ -446,7 +470,7 @@ cudaError_t launch_pair_t(const CUtensorMap& tx, const CUtensorMap& tw, const Pa
 }  // namespace sm100
 
 cudaError_t launch_qkv_project(const void* x, const void* w, const float* bias, void* q, void* k,
-                               void* v, bool bf16, int64_t batch, int64_t seq_len, int64_t heads,
+                               void* v, bool bf16, bool qk32, int64_t batch, int64_t seq_len, int64_t heads,
                                int64_t embed_dim, const float* scale_mul, float eps,
                                const float* rope_cos, const float* rope_sin,
                                int64_t rope_group_stride, void* cache_k, void* cache_v,
@@ -486,12 +510,14 @@ cudaError_t launch_qkv_project(const void* x, const void* w, const float* bias, 
   const bool cos = scale_mul != nullptr, rope = rope_cos != nullptr;
   const int64_t pair_tiles = (M + 255) / 256 * p.n_tiles;
   const int grid = 2 * static_cast<int>(std::min<int64_t>(pair_tiles, sm100::sm_count() / 2));
-#define HEATKV_QKV_PROJ_PAIR(B)                                                      \
-  (cos && rope ? launch_pair_t<B, true, true>(tx, tw, p, grid, st)                   \
-   : cos       ? launch_pair_t<B, true, false>(tx, tw, p, grid, st)                  \
-   : rope      ? launch_pair_t<B, false, true>(tx, tw, p, grid, st)                  \
-               : launch_pair_t<B, false, false>(tx, tw, p, grid, st))
-  return bf16 ? HEATKV_QKV_PROJ_PAIR(true) : HEATKV_QKV_PROJ_PAIR(false);
+#define HEATKV_QKV_PROJ_PAIR(B, Q)                                                   \
+  (cos && rope ? launch_pair_t<B, true, true, Q>(tx, tw, p, grid, st)                \
+   : cos       ? launch_pair_t<B, true, false, Q>(tx, tw, p, grid, st)               \
+   : rope      ? launch_pair_t<B, false, true, Q>(tx, tw, p, grid, st)               \
+               : launch_pair_t<B, false, false, Q>(tx, tw, p, grid, st))
+  if (qk32)
+    return bf16 ? HEATKV_QKV_PROJ_PAIR(true, true) : HEATKV_QKV_PROJ_PAIR(false, true);
+  return bf16 ? HEATKV_QKV_PROJ_PAIR(true, false) : HEATKV_QKV_PROJ_PAIR(false, false);
 #undef HEATKV_QKV_PROJ_PAIR
 }
 

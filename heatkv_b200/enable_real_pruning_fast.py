@@ -213,6 +213,16 @@ class _LayerState:
             self.dense_meta[key] = (st.to(device), (st + int(old_len)).to(device), ct.to(device))
         return self.dense_meta[key]
 
+    def dense_offsets(self, old_len: int, device):
+        """int64 ``[H]`` dense-cache rows where a scale starting after ``old_len`` cached tokens
+        begins for each head (``h * dense_len + old_len``), built once per scale."""
+        key = ("offs", int(old_len), device)
+        if key not in self.dense_meta:
+            ld = max(self.dense_len, 1)
+            self.dense_meta[key] = (torch.arange(self.num_heads, dtype=torch.int64) * ld
+                                    + int(old_len)).to(device)
+        return self.dense_meta[key]
+
     def dense_plan(self, old_len: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
         """``attention_plan`` of a dense-prefix call over ``old_len`` cached tokens per head."""
         key = ("dense", old_len, q.shape[0], q.shape[2], q.dtype, k.dtype, v.dtype, q.device)
@@ -330,6 +340,38 @@ def _head_scale(module) -> torch.Tensor:
     p = module.scale_mul_1H11
     return _derived(module, "scale_mul", (p,), lambda: p.reshape(
         1, module.num_heads, 1, 1).clamp_max(module.max_scale_mul).exp())
+
+
+def _fused_project_dtype(module, x):
+    """The 16-bit dtype in which ``heatkv_qkv_project`` can stand for this call's QKV linear and
+    preparation (None when it cannot): inference (no autograd) on CUDA with the one-pass
+    preparation enabled, head_dim 128, an even head count, a width that is a multiple of 64, and
+    the linear computed in bf16/f16 - autocast's dtype, or x's own when x and the weight share it."""
+    if (not getattr(module, "_heatkv_fused_qkv_prep", False) or not x.is_cuda
+            or torch.is_grad_enabled() or module.head_dim != 128 or module.num_heads % 2
+            or x.ndim != 3 or x.shape[-1] % 64):
+        return None
+    w = module.mat_qkv.weight
+    if tuple(w.shape) != (3 * module.num_heads * 128, x.shape[-1]):
+        return None
+    if torch.is_autocast_enabled():
+        dt = torch.get_autocast_dtype("cuda")
+    else:
+        if module.cos_attn:
+            return None  # the preparation's fp32 norm reproduces autocast only (as prepare_qkv)
+        dt = x.dtype if x.dtype == w.dtype else None
+    return dt if dt in (torch.bfloat16, torch.float16) else None
+
+
+def _project_weights(module, dt):
+    """The QKV weight and bias as F.linear uses them in ``dt``: the weight cast to ``dt``, the
+    bias ``cat(q_bias, zero_k_bias, v_bias)`` cast to ``dt`` and held in fp32."""
+    w = module.mat_qkv.weight
+    wd = _derived(module, f"qkv_weight_{dt}", (w,), lambda: w.detach().to(dt).contiguous())
+    ps = (module.q_bias, module.zero_k_bias, module.v_bias)
+    bd = _derived(module, f"qkv_bias32_{dt}", ps,
+                  lambda: torch.cat(ps).detach().to(dt).float().contiguous())
+    return wd, bd
 
 
 def _fused_prep_applies(module, qkv) -> bool:
@@ -486,24 +528,33 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
             self.cached_k = self.cached_v = None
         return output
 
-    qkv = F.linear(input=x, weight=self.mat_qkv.weight,
-                   bias=_qkv_bias(self)).view(
-        batch_size, seq_len, 3, self.num_heads, self.head_dim)
+    # the QKV linear and the preparation in one tensor-core kernel when it can stand for them
+    pdt = _fused_project_dtype(self, x)
+    qkv = None
+    if pdt is None:
+        qkv = F.linear(input=x, weight=self.mat_qkv.weight,
+                       bias=_qkv_bias(self)).view(
+            batch_size, seq_len, 3, self.num_heads, self.head_dim)
     if rope2d_freqs_grid is not None and scale_schedule is None:
         raise ValueError("scale_schedule is required when rope2d_freqs_grid is provided")
     # the dense cache receives this scale (all heads) unless it is the last one or does not fit
     dense_append = (dense_kernel and not final_scale
                     and logical_len <= max(state.dense_len, 0))
     early_dense = False
-    if _fused_prep_applies(self, qkv):
+    if pdt is not None or _fused_prep_applies(self, qkv):
+        in_dtype = pdt if pdt is not None else qkv.dtype
         scale_mul = None
         if self.cos_attn:
             scale_mul = _head_scale(self)
         rope = None
         if rope2d_freqs_grid is not None:
-            rope = _qkv_prep.rope_rows(rope2d_freqs_grid, scale_schedule, scale_ind, seq_len,
-                                       qkv.device)
-        dts = _qkv_prep.prepared_dtypes(qkv.dtype, cos_attention=scale_mul is not None,
+            if pdt is not None:
+                cg, sg = _qkv_prep.rope_groups(rope2d_freqs_grid, scale_schedule, x.device)
+                rope = (cg, sg, int(sum(a * b * c for a, b, c in scale_schedule[:scale_ind])))
+            else:
+                rope = _qkv_prep.rope_rows(rope2d_freqs_grid, scale_schedule, scale_ind,
+                                           seq_len, qkv.device)
+        dts = _qkv_prep.prepared_dtypes(in_dtype, cos_attention=scale_mul is not None,
                                         rope=rope is not None)
         early, append = None, None
         if active and not final_scale:
@@ -515,12 +566,18 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
         elif dense_append:
             # the preparation writes the scale straight into the dense cache (rows past the
             # segments this scale's attention reads)
-            dk, dv = _ensure_dense(self, batch_size, self.head_dim, qkv.device, *dts)
-            ld = max(state.dense_len, 1)
-            offs = torch.arange(self.num_heads, dtype=torch.int64, device=qkv.device) * ld + old_len
+            dk, dv = _ensure_dense(self, batch_size, self.head_dim, x.device, *dts)
+            offs = state.dense_offsets(old_len, x.device)
             append = (dk, dv, offs)
             early_dense = True
-        q, k, v = _qkv_prep.prepare_qkv(qkv, scale_mul=scale_mul, rope=rope, append=append)
+        if pdt is not None:
+            wd, bd = _project_weights(self, pdt)
+            q, k, v = _qkv_prep.project_qkv(x.to(pdt), wd, bd, self.num_heads,
+                                            scale_mul=scale_mul, rope=rope, qk_dtype=dts[0],
+                                            append=append)
+            _stat_add("qkv_project_calls")
+        else:
+            q, k, v = _qkv_prep.prepare_qkv(qkv, scale_mul=scale_mul, rope=rope, append=append)
         if early is not None:
             _stat_add("prep_append_calls")
             _record_kv_copy("prep_append", early[2], self._heatkv_slab_k, self._heatkv_slab_v)

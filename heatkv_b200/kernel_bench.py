@@ -116,7 +116,8 @@ def main(argv=None):
         def fused():
             _native.check(lib.heatkv_qkv_project(
                 _native.ptr(x), _native.ptr(w), None, _native.ptr(q), _native.ptr(k),
-                _native.ptr(v), _native.DTYPE_CODES[torch.bfloat16], B, L, H, C,
+                _native.ptr(v), _native.DTYPE_CODES[torch.bfloat16],
+                _native.DTYPE_CODES[torch.bfloat16], B, L, H, C,
                 None if args.no_cos else _native.ptr(sm), ctypes.c_float(1e-12),
                 None if args.no_rope else _native.ptr(cos), None if args.no_rope else _native.ptr(sin),
                 4 * L, None, None, 0, None, stream), "heatkv_qkv_project")

@@ -248,7 +248,7 @@ class ProjectedHotPath:
                         "proj", p.layer, t, lib.heatkv_qkv_project,
                         (_native.ptr(x2d), _native.ptr(w), _native.ptr(self.biases[i]),
                          _native.ptr(q), _native.ptr(k),
-                         _native.ptr(v), code, B, n, H, C, _native.ptr(self.scale_mul),
+                         _native.ptr(v), code, code, B, n, H, C, _native.ptr(self.scale_mul),
                          ctypes.c_float(1e-12), cos_g, sin_g,
                          group_stride if cos_g is not None else 0, _native.ptr(sk),
                          _native.ptr(sv), rows_, _native.ptr(offs)), flops))

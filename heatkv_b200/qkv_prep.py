@@ -17,6 +17,7 @@ dtype; v keeps the input dtype.
 
 from __future__ import annotations
 
+import ctypes
 from typing import Optional, Tuple
 
 import numpy as np
@@ -131,4 +132,96 @@ def prepare_qkv(qkv: torch.Tensor, *, scale_mul: Optional[torch.Tensor] = None,
     _native.check(lib.heatkv_qkv_prepare_append(
         *args, _native.ptr(slab_k), _native.ptr(slab_v), int(slab_k.shape[1]),
         _native.ptr(offsets), _native.stream_handle(dev)), "prepare_qkv")
+    return q, k, v
+
+
+_ROPE_GROUPS = {}
+
+
+def rope_groups(rope2d_freqs_grid, scale_schedule, device):
+    """The schedule's whole rope cache (cos, sin) in pair-group-major order ``[16, T, 4]``
+    (``rope_pair_groups``), built once per cache tensor and device; a scale starting at token
+    ``s`` is read from token offset ``s``."""
+    key = str(tuple(scale_schedule))
+    grid = rope2d_freqs_grid[key]
+    ck = (key, grid.data_ptr(), grid._version, str(device))
+    hit = _ROPE_GROUPS.get(ck)
+    if hit is None:
+        rows = grid.to(device)[:, 0, 0, 0]  # [2, T, 64]
+        hit = (rope_pair_groups(rows[0]), rope_pair_groups(rows[1]))
+        if len(_ROPE_GROUPS) > 8:
+            _ROPE_GROUPS.clear()
+        _ROPE_GROUPS[ck] = hit
+    return hit
+
+
+def project_qkv(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], heads: int,
+                *, scale_mul: Optional[torch.Tensor] = None, eps: float = 1e-12,
+                rope: Optional[Tuple[torch.Tensor, torch.Tensor, int]] = None,
+                qk_dtype: Optional[torch.dtype] = None,
+                append: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None):
+    """``F.linear(x, weight, bias)`` followed by ``prepare_qkv`` in one tensor-core kernel
+    (``heatkv_qkv_project``). ``x`` ``[B, L, C]`` and ``weight`` ``[3 * heads * 128, C]`` in one
+    16-bit dtype (the casts autocast would make are the caller's); ``bias``: fp32 ``[3 * heads *
+    128]`` holding the values F.linear adds (e.g. the bf16 bias widened), or None. ``rope``:
+    ``(cos_groups, sin_groups, start)`` - ``rope_groups`` tables and the scale's first token.
+    ``qk_dtype`` defaults as in ``prepare_qkv``; ``append`` as in ``prepare_qkv`` (K slab in the q/k
+    dtype). Returns ``q, k, v`` ``[B, H, L, 128]``."""
+    if x.ndim != 3:
+        raise ValueError("project_qkv expects x shaped [B, L, C]")
+    B, L, C = x.shape
+    H, D = int(heads), 128
+    if x.dtype not in (torch.bfloat16, torch.float16) or weight.dtype != x.dtype:
+        raise RuntimeError("project_qkv expects x and weight in one 16-bit dtype")
+    if tuple(weight.shape) != (3 * H * D, C):
+        raise ValueError("project_qkv weight must be [3 * heads * 128, C]")
+    if not (x.is_cuda and weight.is_cuda):
+        raise RuntimeError("project_qkv requires CUDA tensors")
+    lib = _native.load()
+    dev = x.device
+    x2 = x.reshape(B * L, C).contiguous()
+    w = weight.contiguous()
+    if qk_dtype is None:
+        qk_dtype = prepared_dtypes(x.dtype, cos_attention=scale_mul is not None,
+                                   rope=rope is not None)[0]
+    q = torch.empty(B, H, L, D, dtype=qk_dtype, device=dev)
+    k = torch.empty_like(q)
+    v = torch.empty(B, H, L, D, dtype=x.dtype, device=dev)
+    b32 = None
+    if bias is not None:
+        if bias.numel() != 3 * H * D or bias.dtype != torch.float32 or bias.device != dev:
+            raise ValueError("project_qkv bias must be fp32 [3 * heads * 128] on x's device")
+        b32 = bias.contiguous()
+    sm = None
+    if scale_mul is not None:
+        if scale_mul.numel() != H:
+            raise ValueError("scale_mul must have one value per head")
+        sm = scale_mul.detach().reshape(H).to(device=dev, dtype=torch.float32).contiguous()
+    cos = sin = None
+    gstride = 0
+    if rope is not None:
+        cg, sg, start = rope
+        if cg.ndim != 3 or cg.shape[0] != 16 or cg.shape[2] != 4 or cg.shape != sg.shape:
+            raise ValueError("rope tables must be [16, T, 4] pair groups (rope_groups)")
+        if start < 0 or start + L > cg.shape[1]:
+            raise ValueError("rope table shorter than the scale's tokens")
+        cos = ctypes.c_void_p(cg.data_ptr() + start * 16)
+        sin = ctypes.c_void_p(sg.data_ptr() + start * 16)
+        gstride = 4 * int(cg.shape[1])
+    ck = cv = offs = None
+    rows = 0
+    if append is not None:
+        ck, cv, offs = append
+        if (ck.ndim != 3 or ck.shape[0] != B or ck.shape[2] != D or cv.shape != ck.shape
+                or ck.dtype != qk_dtype or cv.dtype != x.dtype or not ck.is_contiguous()
+                or not cv.is_contiguous()):
+            raise ValueError("append caches must be contiguous [B, rows, 128] in the k and v dtypes")
+        if offs.dtype != torch.int64 or offs.numel() != H or offs.device != dev:
+            raise ValueError("append offsets must be an int64 [H] tensor on x's device")
+        rows = int(ck.shape[1])
+    _native.check(lib.heatkv_qkv_project(
+        _native.ptr(x2), _native.ptr(w), _native.ptr(b32), _native.ptr(q), _native.ptr(k),
+        _native.ptr(v), _native.DTYPE_CODES[x.dtype], _native.DTYPE_CODES[qk_dtype], B, L, H, C,
+        _native.ptr(sm), ctypes.c_float(eps), cos, sin, gstride, _native.ptr(ck), _native.ptr(cv),
+        rows, _native.ptr(offs), _native.stream_handle(dev)), "project_qkv")
     return q, k, v

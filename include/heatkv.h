@@ -439,20 +439,22 @@ int heatkv_qkv_prepare_append(const void* qkv, void* q, void* k, void* v, int in
  *   bias    : fp32 [3 * heads * 128] (the concatenated q, zero k and v biases, in the values the
  *             reference's F.linear sees, e.g. rounded to dtype under autocast), or NULL for none;
  *             added to the fp32 accumulator before the rounding to dtype
- *   q, k, v : [batch, heads, seq_len, 128] (dtype). The projection is rounded to dtype, then
+ *   q, k, v : [batch, heads, seq_len, 128]; v in dtype, q and k in qk_dtype (dtype, or f32 as the
+ *             reference's chain gives them under autocast). The projection is rounded to dtype, then
  *             prepared as heatkv_qkv_prepare does (scale_mul: cos-attention; rope: the rotary
  *             angles of the scale's tokens in pair-group-major order - the cos (sin) of pairs
  *             4g .. 4g+3 of token l at rope_cos[(g * rope_group_stride) + 4 * l + 0..3], g < 16,
  *             i.e. a [16, tokens, 4] table with rope_group_stride = 4 * its tokens, from the
  *             scale's first token; rope_group_stride >= 4 * seq_len, a multiple of 4)
- *   cache_* : as heatkv_qkv_prepare_append's slab (cache_offset -1 = head not written); rows of
- *             the heads given an offset are written from the same registers
+ *   cache_* : as heatkv_qkv_prepare_append's slab (cache_offset -1 = head not written; cache_k
+ *             rows in qk_dtype, cache_v rows in dtype); rows of the heads given an offset are
+ *             written from the same registers
  * heads must be even, embed_dim a multiple of 64; x, w, bias, q, k, v, the rope rows and the
  * caches 16-byte aligned. Results equal heatkv_qkv_prepare_append applied to the rounded projection up
  * to the summation order of the projection and of the row norms.
  */
 int heatkv_qkv_project(const void* x, const void* w, const float* bias, void* q, void* k, void* v,
-                       int dtype,
+                       int dtype, int qk_dtype,
                        int64_t batch, int64_t seq_len, int64_t heads, int64_t embed_dim,
                        const float* scale_mul, float eps, const float* rope_cos,
                        const float* rope_sin, int64_t rope_group_stride, void* cache_k,

@@ -174,9 +174,11 @@ def test_installed_model_matches_keep_mask_attention(dtype, cos_attn, autocast, 
 
 
 def test_fused_qkv_prep_matches_the_torch_chain():
-    """fused_qkv_prep=True (one-pass unbind / permute / cos-attention normalisation / RoPE) against
-    the PyTorch chain, on cos-attention models with a 2-D rope cache under bf16 autocast (fp32 q, k
-    and bf16 v: the real model's dtypes), every layer at every one of the 13 scales."""
+    """fused_qkv_prep=True against the PyTorch chain, on cos-attention models with a 2-D rope cache
+    under bf16 autocast (fp32 q, k and bf16 v: the real model's dtypes) and non-zero q/v biases,
+    every layer at every one of the 13 scales. Under autocast the fused path is the QKV projection
+    with the preparation in its epilogue (heatkv_qkv_project); the chain is F.linear, then
+    unbind / permute / normalisation / RoPE in PyTorch."""
     dev = torch.device("cuda", 0)
     L, H, C = 2, 16, 2048
     schedule = synthetic.SCALE_SCHEDULE_1M
@@ -190,6 +192,10 @@ def test_fused_qkv_prep_matches_the_torch_chain():
     for fused in (False, True):
         torch.manual_seed(0)
         model = nn.ModuleList([SelfAttention(C, H, True) for _ in range(L)]).to(dev)
+        with torch.no_grad():
+            for m in model:
+                m.q_bias.normal_(0.0, 0.1)
+                m.v_bias.normal_(0.0, 0.1)
         enable_real_pruning_scale_specific_fused_segmented(
             model, 0.10, orders, protected_prefix_scales=3, source_scale_start=3,
             fused_qkv_prep=fused)
