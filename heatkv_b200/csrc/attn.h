@@ -59,7 +59,7 @@ cudaError_t launch_attention_simt(const AttnArgs& a, int q_dtype, int k_dtype, i
 // arguments. _cs: q, k, v all bf16 or all f16 (scatter epilogue supported); _tf32: fp32 q and k
 // with 16-bit v, kind::tf32 QK with Q in TMEM (no scatter).
 cudaError_t launch_attention_sm100_cs(const AttnArgs& a, bool bf16, cudaStream_t st);
-// 64-key tiles, two CTAs per SM (16-bit, no scatter); cudaErrorNotSupported otherwise
+// 64-key tiles, two CTAs per SM (16-bit, scatter epilogue supported); cudaErrorNotSupported otherwise
 cudaError_t launch_attention_sm100_cs64(const AttnArgs& a, bool bf16, cudaStream_t st);
 // kv_splits = 0 for the 64-key kernel: enough splits of every 128-row block for two waves
 int attention_cs64_auto_splits(int64_t batch, int64_t heads, int64_t q_len);

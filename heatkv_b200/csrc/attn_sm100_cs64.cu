@@ -30,8 +30,9 @@
 // attn_sm100_cs.cu: the blocks after the first `unsplit` are cut into `splits` ranges of their key
 // tiles; a split writes (m, l) and its unnormalised O rows to the workspace, and the CTA that
 // completes a block's last split (an atomic counter per block) merges them; a split without key
-// tiles only publishes (-inf, 0). No scatter epilogue (such callers take attn_sm100_cs.cu). Every
-// wait is bounded; on expiry the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains its copies and
+// tiles only publishes (-inf, 0). The scatter epilogue (its own instantiation, unsplit calls
+// only) stores every output row into n_out full outputs - every rank's copy, through peer
+// pointers - at the mapped row and head, as attn_sm100_cs.cu's does. Every wait is bounded; on expiry the CTA raises HEATKV_DEVICE_WAIT_TIMEOUT, drains its copies and
 // MMAs, frees TMEM and returns.
 #include "attn.h"
 #include "common.cuh"
@@ -110,6 +111,14 @@ struct Params {
   int static_meta;
   int current_in_segments;
   int out_align32;      // out is 32-byte aligned: 32-byte stores in the epilogue
+  // scatter epilogue (kScatter, unsplit): every output row goes to n_out full [out_batch, Lq,
+  // out_heads_total * D] tensors at row out_rows[b] and head out_heads[h]
+  void* const* out_ptrs;
+  const int32_t* out_rows;
+  const int32_t* out_heads;
+  int n_out;
+  int out_batch;
+  int out_heads_total;
 };
 
 struct Item {
@@ -165,7 +174,7 @@ __device__ __forceinline__ int slot_item(const Smem& sm, const Params& p, int sl
   return (item >= p.n_items || item < -1) ? -1 : item;
 }
 
-template <bool kBF16>
+template <bool kBF16, bool kScatter>
 __global__ void __launch_bounds__(kThreads, 2)
     attn_sm100_cs64_kernel(const __grid_constant__ CUtensorMap tm_q,
                            const __grid_constant__ CUtensorMap tm_ck,
@@ -585,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         cur.next();
       }
-      const bool split = it.nsplit > 1;
+      const bool split = !kScatter && it.nsplit > 1;  // a scattering launch runs unsplit
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.o_final, ocnt & 1, abort_flag, p.status));
       if (split && it.q0 + row < Lq)
         __stcg(p.ws_ml + split_slot(it, it.split),
@@ -594,8 +603,18 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc_fence_after();
         const int qrow = it.q0 + row;
         const float inv = 1.f / l_run;
-        OutT* orow = static_cast<OutT*>(p.out) + ((int64_t(it.b) * Lq + qrow) * H + it.h) * kD;
+        OutT* orow = kScatter ? nullptr
+                              : static_cast<OutT*>(p.out) + ((int64_t(it.b) * Lq + qrow) * H + it.h) * kD;
         float* prow = split ? p.ws_o + split_slot(it, it.split) * kD : nullptr;
+        // scatter: the row's place in every full output (the same offset in each)
+        int64_t soff = 0;
+        bool in_range = true;
+        if constexpr (kScatter) {
+          const int grow = __ldg(p.out_rows + it.b), ghead = __ldg(p.out_heads + it.h);
+          in_range = grow >= 0 && grow < p.out_batch && ghead >= 0 && ghead < p.out_heads_total;
+          if (!in_range && row == 0) raise_status(p.status, HEATKV_DEVICE_GATHER_OUT_OF_RANGE);
+          soff = ((int64_t(grow) * Lq + qrow) * p.out_heads_total + ghead) * kD;
+        }
 #pragma unroll 1
         for (int half = 0; half < 4; ++half) {
           float o[32];
@@ -615,7 +634,21 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
               for (int i = 0; i < 8; ++i)
                 wv[i] = pack2<kBF16>(o[cc * 16 + 2 * i] * inv, o[cc * 16 + 2 * i + 1] * inv);
-              if (p.out_align32) {
+              if constexpr (kScatter) {
+                if (in_range) {
+#pragma unroll 1
+                  for (int r = 0; r < p.n_out; ++r) {
+                    OutT* dst = static_cast<OutT*>(p.out_ptrs[r]) + soff + 32 * half + 16 * cc;
+                    if ((reinterpret_cast<uintptr_t>(dst) & 31u) == 0) {
+                      st_global_v8(dst, wv);
+                    } else {
+                      uint4* d4 = reinterpret_cast<uint4*>(dst);
+                      d4[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                      d4[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+                    }
+                  }
+                }
+              } else if (p.out_align32) {
                 // one full 32-byte sector per store: half the store instructions of 16-byte
                 // vectors, and no partial-sector writes (each thread writes its own row)
                 st_global_v8(orow + 32 * half + 16 * cc, wv);
@@ -648,11 +681,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-template <bool kBF16>
+template <bool kBF16, bool kScatter>
 static cudaError_t launch_t(const CUtensorMap& tq, const CUtensorMap& tck, const CUtensorMap& tcv,
                             const CUtensorMap& tsk, const CUtensorMap& tsv, const Params& p,
                             int grid, cudaStream_t st) {
-  auto kern = attn_sm100_cs64_kernel<kBF16>;
+  auto kern = attn_sm100_cs64_kernel<kBF16, kScatter>;
   const int smem = static_cast<int>(sizeof(Smem)) + 1024;
   static_assert(2 * (sizeof(Smem) + 1024 + 1024) <= 228 * 1024, "two CTAs per SM");
   static std::atomic<uint64_t> configured{0};
@@ -688,8 +721,12 @@ cudaError_t launch_attention_sm100_cs64(const AttnArgs& a, bool bf16, cudaStream
   const int64_t slab_rows = a.batch * a.capacity;
   if (cur_rows >= (int64_t(1) << 31) || slab_rows >= (int64_t(1) << 31) ||
       a.heads > kMaxHeads || a.heads * std::max<int64_t>(a.max_segments, 1) > kMaxSegTable ||
-      !(a.scale > 0.f) || a.q_len <= 0 || a.n_out > 0)
+      !(a.scale > 0.f) || a.q_len <= 0 || a.n_out < 0 || a.n_out > 64)
     return cudaErrorNotSupported;
+  const bool scatter = a.n_out > 0;
+  if (scatter && (!a.out_ptrs || !a.out_rows || !a.out_heads || a.out_batch > 0x7fffffff ||
+                  a.out_heads_total > 0x7fffffff))
+    return cudaErrorInvalidValue;
   const uintptr_t align = reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.cur_k) |
                           reinterpret_cast<uintptr_t>(a.cur_v) |
                           reinterpret_cast<uintptr_t>(a.slab_k) |
@@ -701,6 +738,7 @@ cudaError_t launch_attention_sm100_cs64(const AttnArgs& a, bool bf16, cudaStream
   int splits = a.kv_splits <= 0 ? attention_cs64_auto_splits(a.batch, a.heads, a.q_len)
                                 : a.kv_splits;
   splits = std::min(splits, kMaxKvSplits);
+  if (scatter) splits = 1;  // the scatter epilogue stores finished rows only
   int64_t unsplit = splits > 1 ? std::min<int64_t>(std::max<int64_t>(a.unsplit_blocks, 0), blocks)
                                : blocks;
   if (unsplit == blocks) splits = 1;
@@ -754,10 +792,19 @@ cudaError_t launch_attention_sm100_cs64(const AttnArgs& a, bool bf16, cudaStream
   p.static_meta = a.static_meta ? 1 : 0;
   p.current_in_segments = a.current_in_segments ? 1 : 0;
   p.out_align32 = (reinterpret_cast<uintptr_t>(a.out) & 31u) == 0 ? 1 : 0;
+  p.out_ptrs = a.out_ptrs;
+  p.out_rows = a.out_rows;
+  p.out_heads = a.out_heads;
+  p.n_out = a.n_out;
+  p.out_batch = static_cast<int>(a.out_batch);
+  p.out_heads_total = static_cast<int>(a.out_heads_total);
   const int grid = use_map ? a.map_grid
                            : static_cast<int>(std::min<int64_t>(n_items, 2 * sm100::sm_count()));
-  return bf16 ? launch_t<true>(tq, tck, tcv, tsk, tsv, p, grid, st)
-              : launch_t<false>(tq, tck, tcv, tsk, tsv, p, grid, st);
+  if (scatter)
+    return bf16 ? launch_t<true, true>(tq, tck, tcv, tsk, tsv, p, grid, st)
+                : launch_t<false, true>(tq, tck, tcv, tsk, tsv, p, grid, st);
+  return bf16 ? launch_t<true, false>(tq, tck, tcv, tsk, tsv, p, grid, st)
+              : launch_t<false, false>(tq, tck, tcv, tsk, tsv, p, grid, st);
 }
 
 }  // namespace heatkv

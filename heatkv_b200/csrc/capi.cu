@@ -24,7 +24,7 @@ bool pdl_enabled() {
 }
 
 // HEATKV_TCGEN05_VARIANT: "cs" (column-split kernel) or "cs64" (64-key kernel) for 16-bit calls
-// that name neither; unset: the 64-key kernel, scattering calls the column-split kernel.
+// that name neither (scattering calls included); unset: the 64-key kernel.
 static int tcgen05_variant() {
   static const int v = [] {
     const char* e = getenv("HEATKV_TCGEN05_VARIANT");
@@ -186,15 +186,15 @@ static int plan_attention(int q_dtype, int k_dtype, int v_dtype, int64_t batch, 
     out->run = HEATKV_RUN_TCGEN05_TF32;
   } else if (kernel != HEATKV_ATTN_EXACT && same16) {
     // Default: the 64-key kernel (two CTAs per SM), faster at every launch size measured, with
-    // or without key-range splits (unsplit_blocks counts 128-row blocks for both kernels). It
-    // has no scatter epilogue: scattering calls take the column-split kernel.
+    // or without key-range splits (unsplit_blocks counts 128-row blocks for both kernels) and
+    // for scattering calls (unsplit) too.
     (void)kv_splits;
     (void)has_workspace;
     (void)unsplit_blocks;
     (void)batch;
     (void)heads;
     (void)q_len;
-    out->run = (!scatter && variant != 2) ? HEATKV_RUN_TCGEN05_CS64 : HEATKV_RUN_TCGEN05_CS;
+    out->run = variant != 2 ? HEATKV_RUN_TCGEN05_CS64 : HEATKV_RUN_TCGEN05_CS;
   } else {
     if (scatter)
       return fail(HEATKV_ERR_UNSUPPORTED,

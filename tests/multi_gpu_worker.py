@@ -42,14 +42,13 @@ def main() -> int:
         ctrl, L, H = bench.build_controller("2b", 0.10)
         layers, batch = [0, 21], 2
         # no key-range splits on either side: a split block sums in a different order
-        # the peer-to-peer exchange scatters from the column-split kernel, over prefix-only
+        # the peer-to-peer exchange scatters from the 64-key kernel unsplit, over prefix-only
         # dense segments followed by the current tiles: compare bits with exactly that
         p2p = exchange == "p2p"
         full = HotPath(ctrl, L, H, batch, dev, layers=layers, plan_splits=1,
                        dense_append_first=not p2p)
         inputs, ref_out, _, _ = allocate_io(full, seed=11)       # identical on every rank
-        ref_kernel = _native.ATTN_TCGEN05_CS if p2p else _native.ATTN_AUTO
-        HotPath.run(full.launches(inputs, ref_out, kernel=ref_kernel))
+        HotPath.run(full.launches(inputs, ref_out, kernel=_native.ATTN_AUTO))
         plan = sharding.plan_shards(sharding.head_costs(ctrl, L, H), batch, world, split=split)
         sh = sharding.ShardedHotPath(ctrl, L, H, plan, rank, dev, gather=True, layers=layers,
                                      exchange=exchange, plan_splits=1)

@@ -122,7 +122,7 @@ def _random_layout(rng, heads, max_segments, capacity, lengths=(1, 4, 16, 36, 64
 ])
 def test_tcgen05_random_layouts(which, dtype, B, H, L, cap, S, cuda_device, kernel):
     """Both 16-bit tcgen05 kernels: the 64-key one (two CTAs per SM, the default) and the
-    column-split one (the scatter kernel)."""
+    column-split one."""
     kernel(which)
     rng = np.random.default_rng(B * 1000 + H * 100 + L)
     gen = torch.Generator().manual_seed(L)

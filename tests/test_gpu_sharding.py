@@ -119,8 +119,9 @@ def test_sharded_ranks_reassemble_the_single_gpu_outputs(world, split):
 
 def test_scatter_attention_places_rows_in_every_destination():
     """heatkv_segmented_attention_scatter: the heads of one call split over two emulated ranks,
-    each storing its rows into two full outputs (both on this GPU), equals the unsharded call of
-    the kernel the scatter runs (the column-split one), bit for bit."""
+    each storing its rows into two full outputs (both on this GPU; one 32-byte aligned, one only
+    16-byte aligned), equals the unsharded call of the kernel the scatter runs (the 64-key one,
+    unsplit), bit for bit."""
     dev = torch.device("cuda", 0)
     lib = _native.load()
     B, H, L, cap, S = 2, 16, 600, 5000, 8
@@ -142,9 +143,12 @@ def test_scatter_attention_places_rows_in_every_destination():
     _native.check(lib.heatkv_segmented_attention(
         _native.ptr(q), _native.ptr(pk), _native.ptr(pv), *[_native.ptr(m) for m in meta],
         _native.ptr(k), _native.ptr(v), _native.ptr(ref), DT[q.dtype], DT[k.dtype], DT[v.dtype],
-        B, H, L, cap, 128, S, scale, 0, _native.ATTN_TCGEN05_CS,
+        B, H, L, cap, 128, S, scale, 0, _native.ATTN_TCGEN05_CS64,
         _native.stream_handle(dev)), "reference call")
-    dests = [torch.full_like(ref, float("nan")) for _ in range(2)]
+    # the second destination starts 16 bytes into its buffer: the epilogue's 16-byte stores
+    spare = torch.full((ref.numel() + 8,), float("nan"), dtype=ref.dtype, device=dev)
+    dests = [torch.full_like(ref, float("nan")), spare[8:].view(ref.shape)]
+    assert dests[1].data_ptr() % 32 == 16
     ptrs = torch.tensor([d.data_ptr() for d in dests], dtype=torch.int64, device=dev)
     rows = torch.arange(B, dtype=torch.int32, device=dev)
     groups = [sorted(rng.permutation(H)[:H // 2].tolist())]
@@ -171,9 +175,9 @@ def test_scatter_of_dense_launches_uses_prefix_only_segments():
     exchange takes no kernel selector, so the exchange re-issues those launches with their
     prefix-only segments (Launch.unflagged_meta). Re-issued that way into one full output on this
     GPU, every dense target of a layer matches the hot path's own output (bf16 tolerance: the
-    scatter runs the column-split kernel, the hot path the 64-key one) and, bit for bit, the hot
-    path built without dense appends first and run on the column-split kernel (the reference the
-    2-GPU peer-to-peer test compares with)."""
+    re-issued launch splits its keys into tiles at other places) and, bit for bit, the hot path
+    built without dense appends first (the reference the 2-GPU peer-to-peer test compares
+    with)."""
     dev = torch.device("cuda", 0)
     lib = _native.load()
     ctrl, L, H = bench.build_controller("2b", 0.10)
@@ -183,7 +187,7 @@ def test_scatter_of_dense_launches_uses_prefix_only_segments():
     HotPath.run(launches)
     plain = HotPath(ctrl, L, H, 2, dev, layers=[21], plan_splits=1, dense_append_first=False)
     _, plain_out, _, _ = allocate_io(plain, seed=4, fill=False)
-    HotPath.run(plain.launches(inputs, plain_out, kernel=_native.ATTN_TCGEN05_CS))
+    HotPath.run(plain.launches(inputs, plain_out))
     torch.cuda.synchronize()
     rows = torch.arange(2, dtype=torch.int32, device=dev)
     heads = torch.arange(H, dtype=torch.int32, device=dev)

@@ -28,9 +28,8 @@ def test_sixteen_bit_calls_take_the_64_key_kernel():
 
 def test_split_calls_take_the_64_key_kernel():
     """The 64-key kernel takes key-range splits too (unsplit_blocks counts its 128-row blocks),
-    so splits, the workspace and unsplit_blocks leave 16-bit calls on it at every size. (Only
-    scattering calls, which it cannot serve, go to the column-split kernel; the GPU scatter tests
-    cover those.)"""
+    so splits, the workspace and unsplit_blocks leave 16-bit calls on it at every size.
+    (Scattering calls run it unsplit; the GPU scatter tests cover those.)"""
     for splits, unsplit in ((2, 0), (4, 100), (3, 2 * 16 * 32)):
         assert run(splits=splits, ws=1, unsplit=unsplit) == _native.RUN_TCGEN05_CS64
         assert run(batch=16, splits=splits, ws=1, unsplit=unsplit) == _native.RUN_TCGEN05_CS64
