@@ -660,6 +660,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
           }
         }
+        // stores to other GPUs are visible system-wide before this kernel's completion is
+        if constexpr (kScatter) __threadfence_system();
         tc_fence_before();
         __syncwarp();
         // O has been read into registers (tcgen05.wait::ld): the hand-off to the next item's PV

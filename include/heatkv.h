@@ -67,14 +67,13 @@ typedef enum {
                              are f32 with bf16/f16 v (tf32 QK, P in v's dtype), else exact */
   HEATKV_ATTN_EXACT = 1,  /* CUDA-core kernel: fp32 products and accumulation for every dtype */
   HEATKV_ATTN_TCGEN05 = 2, /* tcgen05/TMEM kernel; requires q/k/v all bf16 or all f16, or q and
-                              k f32 with bf16/f16 v. 16-bit calls take the 64-key kernel,
-                              scattering calls the column-split kernel; f32 q/k the column-split
-                              kernel's tf32 mode */
+                              k f32 with bf16/f16 v. 16-bit calls take the 64-key kernel
+                              (scattering calls included); f32 q/k the column-split kernel's
+                              tf32 mode */
   /* 3 is retired (a two-tile kernel of 256 query rows per CTA) and rejected */
   HEATKV_ATTN_TCGEN05_CS = 4,   /* the column-split tcgen05 kernel (128 query rows per CTA) */
   HEATKV_ATTN_TCGEN05_CS64 = 5  /* 64-key tiles, two CTAs per SM (128 query rows each); q/k/v all
-                                   bf16 or all f16; no scatter epilogue (such calls take the
-                                   column-split kernel) */
+                                   bf16 or all f16 */
 } heatkv_attn_kernel;
 
 /* The kernel an attention call runs (heatkv_attention_kernel_for). */
@@ -216,8 +215,9 @@ int heatkv_segmented_attention_ws(const void* q, const void* slab_k, const void*
  *                     out_heads_total * head_dim] tensors in q's dtype (local or peer memory)
  *   out_rows        : int32 [batch] device array, the full-output row of each local batch row
  *   out_heads       : int32 [heads] device array, the full-output head of each local head
- * Other arguments as heatkv_segmented_attention_ws, always on the tcgen05 kernel unsplit (q, k, v
- * all bf16 or all f16). A mapped row or head outside the full output is skipped and raises
+ * Other arguments as heatkv_segmented_attention_ws, always on a 16-bit tcgen05 kernel unsplit (q,
+ * k, v all bf16 or all f16; the 64-key kernel unless HEATKV_TCGEN05_VARIANT=cs). Each destination
+ * must be 16-byte aligned. A mapped row or head outside the full output is skipped and raises
  * HEATKV_DEVICE_GATHER_OUT_OF_RANGE. The stores are complete and visible system-wide when the
  * kernel completes; readers on other GPUs must still synchronise with it (heatkv_peer_barrier).
  */
