@@ -61,6 +61,10 @@ SIGNATURES = {
     "heatkv_segmented_attention_scatter": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _p, _p,
                                                 _i64, _i64, _i, _i, _i, _i64, _i64, _i64, _i64,
                                                 _i64, _i64, ctypes.c_float, _p, _p]),
+    "heatkv_segmented_attention_scatter_mapped": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _p,
+                                                       _p, _i64, _i64, _i, _i, _i, _i64, _i64,
+                                                       _i64, _i64, _i64, _i64, ctypes.c_float,
+                                                       _p, _p, _i64, _i, _p]),
     "heatkv_peer_barrier": (_i, [_p, _p, _i, _i, _p]),
     "heatkv_peer_alloc": (_i, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _p]),
     "heatkv_peer_open": (_i, [_p, ctypes.POINTER(ctypes.c_void_p)]),

@@ -346,6 +346,30 @@ int heatkv_segmented_attention_ws(const void* q, const void* slab_k, const void*
                         workspace_bytes, stream);
 }
 
+static int scatter_impl(const char* name, const void* q, const void* slab_k, const void* slab_v,
+                        const int32_t* seg_starts, const int32_t* seg_ends,
+                        const int32_t* seg_counts, const void* cur_k, const void* cur_v,
+                        void* const* out_ptrs, int n_out, const int32_t* out_rows,
+                        const int32_t* out_heads, int64_t out_batch, int64_t out_heads_total,
+                        int q_dtype, int k_dtype, int v_dtype, int64_t batch, int64_t heads,
+                        int64_t q_len, int64_t capacity, int64_t head_dim, int64_t max_segments,
+                        float softmax_scale, const int32_t* head_order, const int32_t* item_map,
+                        int64_t map_len, int map_grid, void* stream) {
+  g_last_error.clear();
+  if (n_out <= 0 || n_out > 64 || !out_ptrs || !out_rows || !out_heads)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: 1..64 destinations and both maps are required",
+                name);
+  if (out_batch < batch || out_heads_total < heads || out_batch > 0x7fffffff ||
+      out_heads_total > 0x7fffffff)
+    return fail(HEATKV_ERR_INVALID_ARGUMENT, "%s: the full output is smaller than this shard",
+                name);
+  const Scatter sc{out_ptrs, out_rows, out_heads, n_out, out_batch, out_heads_total};
+  return attention_impl(q, slab_k, slab_v, seg_starts, seg_ends, seg_counts, cur_k, cur_v, nullptr,
+                        q_dtype, k_dtype, v_dtype, batch, heads, q_len, capacity, head_dim,
+                        max_segments, softmax_scale, HEATKV_ATTN_TCGEN05, head_order, 1, nullptr, 0,
+                        stream, &sc, 0, item_map, map_len, map_grid);
+}
+
 int heatkv_segmented_attention_scatter(
     const void* q, const void* slab_k, const void* slab_v, const int32_t* seg_starts,
     const int32_t* seg_ends, const int32_t* seg_counts, const void* cur_k, const void* cur_v,
@@ -353,19 +377,33 @@ int heatkv_segmented_attention_scatter(
     int64_t out_batch, int64_t out_heads_total, int q_dtype, int k_dtype, int v_dtype,
     int64_t batch, int64_t heads, int64_t q_len, int64_t capacity, int64_t head_dim,
     int64_t max_segments, float softmax_scale, const int32_t* head_order, void* stream) {
-  g_last_error.clear();
-  if (n_out <= 0 || n_out > 64 || !out_ptrs || !out_rows || !out_heads)
+  return scatter_impl("heatkv_segmented_attention_scatter", q, slab_k, slab_v, seg_starts,
+                      seg_ends, seg_counts, cur_k, cur_v, out_ptrs, n_out, out_rows, out_heads,
+                      out_batch, out_heads_total, q_dtype, k_dtype, v_dtype, batch, heads, q_len,
+                      capacity, head_dim, max_segments, softmax_scale, head_order, nullptr, 0, 0,
+                      stream);
+}
+
+int heatkv_segmented_attention_scatter_mapped(
+    const void* q, const void* slab_k, const void* slab_v, const int32_t* seg_starts,
+    const int32_t* seg_ends, const int32_t* seg_counts, const void* cur_k, const void* cur_v,
+    void* const* out_ptrs, int n_out, const int32_t* out_rows, const int32_t* out_heads,
+    int64_t out_batch, int64_t out_heads_total, int q_dtype, int k_dtype, int v_dtype,
+    int64_t batch, int64_t heads, int64_t q_len, int64_t capacity, int64_t head_dim,
+    int64_t max_segments, float softmax_scale, const int32_t* head_order, const int32_t* item_map,
+    int64_t map_len, int map_grid, void* stream) {
+  if (!item_map || map_len <= 0 || map_len >= (int64_t(1) << 31) || map_grid <= 0 ||
+      map_grid > 65535 || map_len % map_grid != 0) {
+    g_last_error.clear();
     return fail(HEATKV_ERR_INVALID_ARGUMENT,
-                "heatkv_segmented_attention_scatter: 1..64 destinations and both maps are required");
-  if (out_batch < batch || out_heads_total < heads || out_batch > 0x7fffffff ||
-      out_heads_total > 0x7fffffff)
-    return fail(HEATKV_ERR_INVALID_ARGUMENT,
-                "heatkv_segmented_attention_scatter: the full output is smaller than this shard");
-  const Scatter sc{out_ptrs, out_rows, out_heads, n_out, out_batch, out_heads_total};
-  return attention_impl(q, slab_k, slab_v, seg_starts, seg_ends, seg_counts, cur_k, cur_v, nullptr,
-                        q_dtype, k_dtype, v_dtype, batch, heads, q_len, capacity, head_dim,
-                        max_segments, softmax_scale, HEATKV_ATTN_TCGEN05, head_order, 1, nullptr, 0,
-                        stream, &sc);
+                "heatkv_segmented_attention_scatter_mapped: item_map of rounds x map_grid slots "
+                "required");
+  }
+  return scatter_impl("heatkv_segmented_attention_scatter_mapped", q, slab_k, slab_v, seg_starts,
+                      seg_ends, seg_counts, cur_k, cur_v, out_ptrs, n_out, out_rows, out_heads,
+                      out_batch, out_heads_total, q_dtype, k_dtype, v_dtype, batch, heads, q_len,
+                      capacity, head_dim, max_segments, softmax_scale, head_order, item_map,
+                      map_len, map_grid, stream);
 }
 
 int heatkv_peer_barrier(uint32_t* const* flag_ptrs, uint32_t* counter, int world, int rank,

@@ -479,15 +479,19 @@ class ShardedHotPath:
             a = launch.args
             # a: q, sk, sv, st, en, ct, k, v, out, dtq, dtk, dtv, B, H, n, cap, D, S, scale,
             #    kernel, order, splits, unsplit, [item map, slots, grid,] ws, ws_bytes
-            #    (HotPath.launches); the scatter runs unsplit, in its own CTA order, and takes no
-            #    kernel selector: a launch whose segments already end with the current scale
+            #    (HotPath.launches); the scatter runs unsplit, in the launch's item map when
+            #    it has one (planned unsplit), and takes no kernel selector: a launch whose segments already end with the current scale
             #    (HEATKV_ATTN_CURRENT_IN_SEGMENTS) is re-issued with its prefix-only segments
             meta = launch.unflagged_meta or (a[3], a[4], a[5])
             args = (a[0], a[1], a[2], meta[0], meta[1], meta[2], a[6], a[7], _native.ptr(ptrs),
                     p.world, _native.ptr(rows), _native.ptr(heads[layer]), p.batch, p.num_heads,
                     a[9], a[10], a[11], a[12], a[13], a[14], a[15], a[16], a[17], a[18], a[20])
-            scatter = Launch("attention", layer, t, lib.heatkv_segmented_attention_scatter, args,
-                             launch.work)
+            fn = lib.heatkv_segmented_attention_scatter
+            if launch.fn is lib.heatkv_segmented_attention_mapped and int(a[21]) == 1:
+                # the planner's longest-first map of this launch numbers the same unsplit items
+                fn = lib.heatkv_segmented_attention_scatter_mapped
+                args = args + (a[23], a[24], a[25])
+            scatter = Launch("attention", layer, t, fn, args, launch.work)
             scatter.keep = (ptrs, rows, heads[layer])
             out.append(scatter)
             out.append(Launch("barrier", layer, t, lib.heatkv_peer_barrier,

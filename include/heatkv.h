@@ -230,6 +230,21 @@ int heatkv_segmented_attention_scatter(
     int64_t max_segments, float softmax_scale, const int32_t* head_order, void* stream);
 
 /*
+ * heatkv_segmented_attention_scatter_mapped - heatkv_segmented_attention_scatter with an explicit
+ * assignment of its items (128-row query blocks, schedule order) to map_grid CTAs, as
+ * heatkv_segmented_attention_mapped with kv_splits = 1: the peer-to-peer exchange passes the
+ * longest-first map its planner made for the same launch. No reference counterpart.
+ */
+int heatkv_segmented_attention_scatter_mapped(
+    const void* q, const void* slab_k, const void* slab_v, const int32_t* seg_starts,
+    const int32_t* seg_ends, const int32_t* seg_counts, const void* cur_k, const void* cur_v,
+    void* const* out_ptrs, int n_out, const int32_t* out_rows, const int32_t* out_heads,
+    int64_t out_batch, int64_t out_heads_total, int q_dtype, int k_dtype, int v_dtype,
+    int64_t batch, int64_t heads, int64_t q_len, int64_t capacity, int64_t head_dim,
+    int64_t max_segments, float softmax_scale, const int32_t* head_order, const int32_t* item_map,
+    int64_t map_len, int map_grid, void* stream);
+
+/*
  * heatkv_peer_barrier - one step of a barrier across the `world` GPUs of a sharded call, run by
  * every rank on its own GPU after its scatter. flag_ptrs: device array of `world` pointers, entry i
  * being rank i's array of `world` uint32 flags (peer-accessible memory, zero before the first step);
@@ -263,9 +278,7 @@ int heatkv_enable_peer_access(int peer_device);
 /*
  * heatkv_segmented_attention_sched - heatkv_segmented_attention_ws with the split applied to the
  * tail of the schedule only: the first `unsplit_blocks` query blocks of the schedule order (head
- * rank major, then batch row, then query block of the kernel that runs: 256 rows for the
- * two-tile kernel, 128 for the column-split kernel; heatkv_attention_kernel_for names it) run
- * whole, every later block is divided into kv_splits (>= 1) key ranges that different CTAs
+ * rank major, then batch row, then 128-row query block) run whole, every later block is divided into kv_splits (>= 1) key ranges that different CTAs
  * process and the last one merges. A planner that knows the key tiles of every head chooses
  * unsplit_blocks so that the last wave of blocks over the SMs is filled with half-size work
  * instead of leaving SMs idle. The workspace needs at most
@@ -284,16 +297,15 @@ int heatkv_segmented_attention_sched(const void* q, const void* slab_k, const vo
 
 /*
  * heatkv_segmented_attention_mapped - heatkv_segmented_attention_sched with an explicit
- * assignment of the column-split kernel's items to its CTAs: the launch has map_grid CTAs and CTA
+ * assignment of the tcgen05 kernels' items to their CTAs: the launch has map_grid CTAs and CTA
  * c runs, in order, the items item_map[c], item_map[c + map_grid], ... (-1 = empty slot); map_len
  * (a multiple of map_grid) is the number of slots. Items are numbered as the kernel numbers them:
  * the first unsplit_blocks blocks of 128 query rows (schedule order), then kv_splits items per
  * later block. Every item must appear exactly once; an entry outside the item space is skipped
  * and raises HEATKV_DEVICE_BAD_ITEM_MAP. A planner that knows every block's key tiles fills the
  * map (e.g. longest first to the least-loaded CTA) so that no CTA runs long while others idle.
- * The map is a schedule only: the output is the same with or without it, and launches that do
- * not run the column-split kernel with this split layout (another kernel, tf32 operands, a
- * workspace too small for the splits) ignore it. No reference counterpart.
+ * The map is a schedule only: the output is the same with or without it, and launches that run
+ * the exact kernel or another split layout (a workspace too small for the splits) ignore it. No reference counterpart.
  */
 int heatkv_segmented_attention_mapped(
     const void* q, const void* slab_k, const void* slab_v, const int32_t* seg_starts,

@@ -87,3 +87,34 @@ def test_pack_argument_errors(lib):
     assert call(n=0) == _native.HEATKV_OK
     assert call(ml=0) == _native.HEATKV_OK
     assert call(n=70000) == _native.HEATKV_ERR_UNSUPPORTED
+
+
+def test_scatter_argument_errors(lib):
+    """Both scatter entry points check their destinations, full-output sizes and (mapped) item
+    map before any device work."""
+    p = ctypes.c_void_p
+
+    def scatter(mapped=False, **o):
+        args = (p(16), p(16), p(16), p(16), p(16), p(16), p(16), p(16),
+                None if o.get("no_ptrs") else p(16), o.get("n_out", 2), p(16), p(16),
+                o.get("out_batch", 4), o.get("out_heads", 16), 2, 2, 2, 2, 8, 64, 100, 128, 4,
+                ctypes.c_float(0.088), None)
+        if mapped:
+            return lib.heatkv_segmented_attention_scatter_mapped(
+                *args, None if o.get("no_map") else p(16), o.get("map_len", 296),
+                o.get("grid", 148), None)
+        return lib.heatkv_segmented_attention_scatter(*args, None)
+
+    for mapped in (False, True):
+        name = b"heatkv_segmented_attention_scatter" + (b"_mapped" if mapped else b"")
+        assert scatter(mapped, n_out=0) == _native.HEATKV_ERR_INVALID_ARGUMENT
+        assert name + b": 1..64 destinations" in lib.heatkv_last_error_string()
+        assert scatter(mapped, n_out=65) == _native.HEATKV_ERR_INVALID_ARGUMENT
+        assert scatter(mapped, no_ptrs=True) == _native.HEATKV_ERR_INVALID_ARGUMENT
+        assert scatter(mapped, out_batch=1) == _native.HEATKV_ERR_INVALID_ARGUMENT
+        assert b"smaller than this shard" in lib.heatkv_last_error_string()
+        assert scatter(mapped, out_heads=4) == _native.HEATKV_ERR_INVALID_ARGUMENT
+    assert scatter(True, no_map=True) == _native.HEATKV_ERR_INVALID_ARGUMENT
+    assert b"item_map of rounds x map_grid" in lib.heatkv_last_error_string()
+    assert scatter(True, map_len=300) == _native.HEATKV_ERR_INVALID_ARGUMENT   # not rounds x grid
+    assert scatter(True, grid=0) == _native.HEATKV_ERR_INVALID_ARGUMENT

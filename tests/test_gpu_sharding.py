@@ -117,11 +117,13 @@ def test_sharded_ranks_reassemble_the_single_gpu_outputs(world, split):
     assert _native.device_status(dev) == 0
 
 
-def test_scatter_attention_places_rows_in_every_destination():
+@pytest.mark.parametrize("mapped", [False, True])
+def test_scatter_attention_places_rows_in_every_destination(mapped):
     """heatkv_segmented_attention_scatter: the heads of one call split over two emulated ranks,
     each storing its rows into two full outputs (both on this GPU; one 32-byte aligned, one only
     16-byte aligned), equals the unsharded call of the kernel the scatter runs (the 64-key one,
-    unsplit), bit for bit."""
+    unsplit), bit for bit. ``mapped``: heatkv_segmented_attention_scatter_mapped with a random
+    assignment of the items to 37 CTAs (empty slots included) - a schedule only, same bits."""
     dev = torch.device("cuda", 0)
     lib = _native.load()
     B, H, L, cap, S = 2, 16, 600, 5000, 8
@@ -158,11 +160,23 @@ def test_scatter_attention_places_rows_in_every_destination():
         qs, ks, vs = (x.index_select(1, idx).contiguous() for x in (q, k, v))
         ms = [m.index_select(0, idx).contiguous() for m in meta]
         heads = torch.tensor(hs, dtype=torch.int32, device=dev)
-        _native.check(lib.heatkv_segmented_attention_scatter(
-            _native.ptr(qs), _native.ptr(pk), _native.ptr(pv), *[_native.ptr(m) for m in ms],
-            _native.ptr(ks), _native.ptr(vs), _native.ptr(ptrs), 2, _native.ptr(rows),
-            _native.ptr(heads), B, H, DT[q.dtype], DT[k.dtype], DT[v.dtype], B, len(hs), L, cap,
-            128, S, scale, None, _native.stream_handle(dev)), "scatter call")
+        args = (_native.ptr(qs), _native.ptr(pk), _native.ptr(pv), *[_native.ptr(m) for m in ms],
+                _native.ptr(ks), _native.ptr(vs), _native.ptr(ptrs), 2, _native.ptr(rows),
+                _native.ptr(heads), B, H, DT[q.dtype], DT[k.dtype], DT[v.dtype], B, len(hs), L,
+                cap, 128, S, scale, None)
+        if mapped:
+            items = B * len(hs) * ((L + 127) // 128)
+            grid = 37
+            slots = np.full(((items + 9 + grid - 1) // grid) * grid, -1, np.int32)
+            slots[rng.permutation(slots.size)[:items]] = rng.permutation(items)
+            imap = torch.from_numpy(slots).to(dev)
+            _native.check(lib.heatkv_segmented_attention_scatter_mapped(
+                *args, _native.ptr(imap), imap.numel(), grid, _native.stream_handle(dev)),
+                "mapped scatter call")
+            torch.cuda.synchronize()
+        else:
+            _native.check(lib.heatkv_segmented_attention_scatter(
+                *args, _native.stream_handle(dev)), "scatter call")
     torch.cuda.synchronize()
     for d in dests:
         assert torch.equal(d, ref)
