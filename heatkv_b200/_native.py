@@ -131,12 +131,23 @@ def check(status: int, what: str) -> None:
     raise RuntimeError(msg)
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device: torch.device):
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    """The current CUDA stream of ``device`` as the ``cudaStream_t`` the C ABI takes (the raw
+    handle is read without building a ``torch.cuda.Stream``: this runs on every launch)."""
+    if not isinstance(device, torch.device):
+        device = torch.device(device)
+    if _RAW_STREAM is not None:
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        return _RAW_STREAM(index)
+    return torch.cuda.current_stream(device).cuda_stream
 
 
 def ptr(t):
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    """Device address of a tensor (or None) for a ``void*`` argument."""
+    return None if t is None else t.data_ptr()
 
 
 def device_status(device=None, clear: bool = True) -> int:

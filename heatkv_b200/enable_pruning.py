@@ -197,6 +197,10 @@ class ScaleSpecificPruningController:
         return out
 
     def any_removed(self, layer_idx: int, target_scale_idx: int) -> bool:
-        """True when the removed-head map of (layer, target) holds at least one head."""
-        t = min(int(target_scale_idx), self._mask.shape[0] - 1)
-        return bool(self._mask[t, :, int(layer_idx), :].any())
+        """True when the removed-head map of (layer, target) holds at least one head (a table
+        built once: the mask is fixed at construction and this runs every layer and scale)."""
+        table = self.__dict__.get("_any_removed")
+        if table is None:
+            table = self._any_removed = self._mask.any(axis=(1, 3)).tolist()
+        t = min(int(target_scale_idx), len(table) - 1)
+        return table[t][int(layer_idx)]

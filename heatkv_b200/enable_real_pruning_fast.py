@@ -68,6 +68,7 @@ from . import _native
 from .hotpath import NUM_SMS, plan_column_split
 from .real_pruning_fused_attention import (
     _kernel_selector,
+    _scheduled_attention,
     fused_real_pruning_flat_segmented_attention,
     pack_flat_segments_kv,
 )
@@ -491,6 +492,22 @@ def _dense_append_desc(layer, old_len: int, n: int, device):
     return _items_desc([(h * ld + old_len, h, 0, n) for h in range(layer.num_heads)], n, device)
 
 
+def _segmented_attention(module, q, slab_k, slab_v, meta, k, v, plan):
+    """The fused segmented attention of the installer's forward: straight to the planned launch
+    when the layer has a plan and q/k/v are contiguous (the slabs and segment tables are the
+    installer's own, checked here against q/k/v for what the library cannot see: the batch and
+    the slab dtypes), else through the validating public wrapper."""
+    if (plan is not None and q.is_contiguous() and k.is_contiguous() and v.is_contiguous()
+            and slab_k.dtype == k.dtype and slab_v.dtype == v.dtype
+            and slab_k.shape == slab_v.shape and slab_k.shape[0] == q.shape[0]):
+        return _scheduled_attention(q, slab_k, slab_v, *meta, k, v, module.scale, plan)
+    starts, ends, counts = meta
+    return fused_real_pruning_flat_segmented_attention(
+        q=q, persisted_k=slab_k, persisted_v=slab_v, segment_starts=starts, segment_ends=ends,
+        segment_counts=counts, current_k=k, current_v=v, softmax_scale=module.scale,
+        softmax_mode=_fused_softmax_mode(), _schedule=plan)
+
+
 def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=None, attn_fn=None,
                                                scale_schedule=None, rope2d_freqs_grid=None,
                                                scale_ind=0):
@@ -550,7 +567,7 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
         if rope2d_freqs_grid is not None:
             if pdt is not None:
                 cg, sg = _qkv_prep.rope_groups(rope2d_freqs_grid, scale_schedule, x.device)
-                rope = (cg, sg, int(sum(a * b * c for a, b, c in scale_schedule[:scale_ind])))
+                rope = (cg, sg, _qkv_prep.schedule_info(scale_schedule)[1][scale_ind])
             else:
                 rope = _qkv_prep.rope_rows(rope2d_freqs_grid, scale_schedule, scale_ind,
                                            seq_len, qkv.device)
@@ -610,11 +627,8 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
             dk, dv = _ensure_dense(self, batch_size, self.head_dim, k.device, k.dtype, v.dtype)
             starts, ends, counts = state.dense_segments(old_len, k.device)
         with _Phase("attention"):
-            output = fused_real_pruning_flat_segmented_attention(
-                q=q, persisted_k=dk, persisted_v=dv, segment_starts=starts, segment_ends=ends,
-                segment_counts=counts, current_k=k, current_v=v, softmax_scale=self.scale,
-                softmax_mode=_fused_softmax_mode(),
-                _schedule=state.dense_plan(old_len, q, k, v))
+            output = _segmented_attention(self, q, dk, dv, (starts, ends, counts), k, v,
+                                          state.dense_plan(old_len, q, k, v))
     elif old_len == 0:
         with _Phase("attention"):
             output = slow_attn(query=q, key=k, value=v, scale=self.scale, dropout_p=0.0).transpose(
@@ -645,11 +659,9 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
             self._heatkv_layer.to(k.device)
             starts, ends, counts = self._heatkv_layer.meta[scale_ind]
         with _Phase("attention"):
-            output = fused_real_pruning_flat_segmented_attention(
-                q=q, persisted_k=self._heatkv_slab_k, persisted_v=self._heatkv_slab_v,
-                segment_starts=starts, segment_ends=ends, segment_counts=counts, current_k=k,
-                current_v=v, softmax_scale=self.scale, softmax_mode=_fused_softmax_mode(),
-                _schedule=self._heatkv_layer.attention_plan(scale_ind, q, k, v))
+            output = _segmented_attention(self, q, self._heatkv_slab_k, self._heatkv_slab_v,
+                                          (starts, ends, counts), k, v,
+                                          self._heatkv_layer.attention_plan(scale_ind, q, k, v))
     del q
     output = self.proj_drop(self.proj(output))
 
@@ -662,7 +674,9 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
             if dense_append and not early_dense:
                 _pack(_dense_append_desc(state, old_len, seq_len, k.device), dk, dv, k, v,
                       "dense_append_copy")
-            self._heatkv_dense_live = True
+            # plain attributes written straight into the instance dict, as nn.Module's
+            # __setattr__ ends up doing for them, without its checks: this runs every call
+            self.__dict__["_heatkv_dense_live"] = True
             if ctrl.any_removed(layer, scale_ind + 1):
                 # activation: the dense cache holds exactly the tokens before the next scale
                 ld = max(state.dense_len, 1)
@@ -670,8 +684,8 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
                 _activate_from_dense(self, dk.view(B_, self.num_heads, ld, D_)[:, :, :logical_len],
                                      dv.view(B_, self.num_heads, ld, D_)[:, :, :logical_len],
                                      scale_ind + 1)
-                self._heatkv_dense_live = False
-            self._real_pruning_logical_len = logical_len
+                self.__dict__["_heatkv_dense_live"] = False
+            self.__dict__["_real_pruning_logical_len"] = logical_len
         else:
             removed_next = ctrl.any_removed(layer, scale_ind + 1)
             if not active and not removed_next:
@@ -691,7 +705,7 @@ def _real_pruning_scale_specific_fast_forward(self, x, attn_bias_or_two_vector=N
                 _activate_from_dense_and_current(self, self.cached_k, self.cached_v, k, v,
                                                  scale_ind, old_len, scale_ind + 1)
                 self.cached_k = self.cached_v = None
-            self._real_pruning_logical_len = logical_len
+            self.__dict__["_real_pruning_logical_len"] = logical_len
     return output
 
 

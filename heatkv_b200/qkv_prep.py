@@ -20,7 +20,6 @@ from __future__ import annotations
 import ctypes
 from typing import Optional, Tuple
 
-import numpy as np
 import torch
 
 from . import _native
@@ -40,13 +39,11 @@ def rope_rows(rope2d_freqs_grid, scale_schedule, scale_ind: int, seq_len: int,
     """The (cos, sin) rows ``[seq_len, D/2]`` that ``apply_rotary_emb`` slices for a scale
     (infinity/models/basic.py:104-109): the rope cache of the schedule, rows ``start ..
     start + seq_len`` with ``start`` the tokens of the earlier scales."""
-    key = str(tuple(scale_schedule))
+    key, starts = schedule_info(scale_schedule)
     grid = rope2d_freqs_grid[key]
     if grid.device != torch.device(device):
         grid = rope2d_freqs_grid[key] = grid.to(device)
-    start = 0
-    if scale_ind >= 1:
-        start = int(np.sum([it[0] * it[1] * it[2] for it in scale_schedule[:scale_ind]]))
+    start = starts[scale_ind] if scale_ind >= 1 else 0
     if start + seq_len > grid.shape[4]:
         raise ValueError("rope cache shorter than the scale's tokens")
     rows = grid[:, 0, 0, 0, start:start + seq_len]  # [2, seq_len, half_dim]
@@ -136,13 +133,35 @@ def prepare_qkv(qkv: torch.Tensor, *, scale_mul: Optional[torch.Tensor] = None,
 
 
 _ROPE_GROUPS = {}
+_SCHEDULES = {}
+
+
+def schedule_info(scale_schedule):
+    """``(str(tuple(scale_schedule)), first token of every scale)`` - the rope cache's key and the
+    scales' offsets - memoised on the schedule's contents (every layer and scale asks)."""
+    try:
+        snap = tuple(scale_schedule)
+        hit = _SCHEDULES.get(snap)
+    except TypeError:  # unhashable entries (lists): no memo
+        snap, hit = None, None
+    if hit is None:
+        starts, total = [], 0
+        for a, b, c in scale_schedule:
+            starts.append(total)
+            total += int(a) * int(b) * int(c)
+        hit = (str(tuple(scale_schedule)), starts)
+        if snap is not None:
+            if len(_SCHEDULES) > 16:
+                _SCHEDULES.clear()
+            _SCHEDULES[snap] = hit
+    return hit
 
 
 def rope_groups(rope2d_freqs_grid, scale_schedule, device):
     """The schedule's whole rope cache (cos, sin) in pair-group-major order ``[16, T, 4]``
     (``rope_pair_groups``), built once per cache tensor and device; a scale starting at token
     ``s`` is read from token offset ``s``."""
-    key = str(tuple(scale_schedule))
+    key = schedule_info(scale_schedule)[0]
     grid = rope2d_freqs_grid[key]
     ck = (key, grid.data_ptr(), grid._version, str(device))
     hit = _ROPE_GROUPS.get(ck)

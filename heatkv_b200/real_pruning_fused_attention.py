@@ -258,21 +258,11 @@ def fused_real_pruning_flat_segmented_attention(
     current_k = current_k.contiguous()
     current_v = current_v.contiguous()
     capacity = int(persisted_k.shape[1])
-    output = q.new_empty((batch_size, current_len, num_heads * head_dim))
     if _schedule is not None:
-        order, item_map, grid = _schedule
-        status = lib.heatkv_segmented_attention_mapped(
-            _native.ptr(q), _native.ptr(persisted_k) if capacity else None,
-            _native.ptr(persisted_v) if capacity else None, _native.ptr(segment_starts),
-            _native.ptr(segment_ends), _native.ptr(segment_counts), _native.ptr(current_k),
-            _native.ptr(current_v), _native.ptr(output), _native.DTYPE_CODES[q.dtype],
-            _native.DTYPE_CODES[current_k.dtype], _native.DTYPE_CODES[current_v.dtype],
-            int(batch_size), int(num_heads), int(current_len), capacity, int(head_dim),
-            int(segment_starts.shape[1]), float(softmax_scale), kernel, _native.ptr(order), 1, 0,
-            _native.ptr(item_map), item_map.numel(), int(grid), None, 0,
-            _native.stream_handle(q.device))
-        _native.check(status, "fused_real_pruning_flat_segmented_attention")
-        return output
+        return _scheduled_attention(q, persisted_k, persisted_v, segment_starts, segment_ends,
+                                    segment_counts, current_k, current_v, softmax_scale,
+                                    _schedule, kernel)
+    output = q.new_empty((batch_size, current_len, num_heads * head_dim))
     splits = int(os.environ.get("HEATKV_KV_SPLITS", "1"))
     need = int(lib.heatkv_attention_workspace_bytes(batch_size, num_heads, current_len, splits))
     ws = _workspace(q.device, need) if need > 0 else None
@@ -286,5 +276,32 @@ def fused_real_pruning_flat_segmented_attention(
         int(segment_starts.shape[1]), float(softmax_scale), int(softmax_mode == "exp2"), kernel,
         None, splits, _native.ptr(ws), 0 if ws is None else ws.numel(),
         _native.stream_handle(q.device))
+    _native.check(status, "fused_real_pruning_flat_segmented_attention")
+    return output
+
+
+def _scheduled_attention(q, persisted_k, persisted_v, segment_starts, segment_ends, segment_counts,
+                         current_k, current_v, softmax_scale, schedule, kernel=None):
+    """The launch of ``fused_real_pruning_flat_segmented_attention(..., _schedule=schedule)``
+    without the Python-side validation: for the installer's forward, whose tensors are its own
+    (contiguous CUDA tensors, int32 segment tables, ``[B, capacity, 128]`` slabs). The library
+    still checks sizes, dtypes and head_dim with the reference's messages. ``kernel``: the
+    selector, read from the environment knobs when None."""
+    if kernel is None:
+        kernel = _kernel_selector()
+    lib = _native.load()
+    batch_size, num_heads, current_len, head_dim = q.shape
+    capacity = int(persisted_k.shape[1])
+    order, item_map, grid = schedule
+    output = q.new_empty((batch_size, current_len, num_heads * head_dim))
+    status = lib.heatkv_segmented_attention_mapped(
+        q.data_ptr(), persisted_k.data_ptr() if capacity else None,
+        persisted_v.data_ptr() if capacity else None, segment_starts.data_ptr(),
+        segment_ends.data_ptr(), segment_counts.data_ptr(), current_k.data_ptr(),
+        current_v.data_ptr(), output.data_ptr(), _native.DTYPE_CODES[q.dtype],
+        _native.DTYPE_CODES[current_k.dtype], _native.DTYPE_CODES[current_v.dtype],
+        batch_size, num_heads, current_len, capacity, head_dim, int(segment_starts.shape[1]),
+        float(softmax_scale), kernel, order.data_ptr(), 1, 0, item_map.data_ptr(),
+        item_map.numel(), int(grid), None, 0, _native.stream_handle(q.device))
     _native.check(status, "fused_real_pruning_flat_segmented_attention")
     return output
