@@ -117,8 +117,9 @@ def test_sharded_ranks_reassemble_the_single_gpu_outputs(world, split):
     assert _native.device_status(dev) == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("mapped", [False, True])
-def test_scatter_attention_places_rows_in_every_destination(mapped):
+def test_scatter_attention_places_rows_in_every_destination(mapped, dtype):
     """heatkv_segmented_attention_scatter: the heads of one call split over two emulated ranks,
     each storing its rows into two full outputs (both on this GPU; one 32-byte aligned, one only
     16-byte aligned), equals the unsharded call of the kernel the scatter runs (the 64-key one,
@@ -129,8 +130,8 @@ def test_scatter_attention_places_rows_in_every_destination(mapped):
     B, H, L, cap, S = 2, 16, 600, 5000, 8
     rng = np.random.default_rng(17)
     gen = torch.Generator().manual_seed(17)
-    q, k, v = (torch.randn(B, H, L, 128, generator=gen).bfloat16().to(dev) for _ in range(3))
-    pk, pv = (torch.randn(B, cap, 128, generator=gen).bfloat16().to(dev) for _ in range(2))
+    q, k, v = (torch.randn(B, H, L, 128, generator=gen).to(dtype).to(dev) for _ in range(3))
+    pk, pv = (torch.randn(B, cap, 128, generator=gen).to(dtype).to(dev) for _ in range(2))
     st = np.zeros((H, S), np.int32)
     en = np.zeros((H, S), np.int32)
     ct = rng.integers(0, S + 1, size=H).astype(np.int32)
@@ -140,7 +141,7 @@ def test_scatter_attention_places_rows_in_every_destination(mapped):
             s0 = int(rng.integers(0, cap - n + 1))
             st[h, i], en[h, i] = s0, s0 + n
     scale = ctypes.c_float(128 ** -0.5)
-    ref = torch.empty(B, L, H * 128, dtype=torch.bfloat16, device=dev)
+    ref = torch.empty(B, L, H * 128, dtype=dtype, device=dev)
     meta = [torch.from_numpy(x).to(dev) for x in (st, en, ct)]
     _native.check(lib.heatkv_segmented_attention(
         _native.ptr(q), _native.ptr(pk), _native.ptr(pv), *[_native.ptr(m) for m in meta],
@@ -181,6 +182,43 @@ def test_scatter_attention_places_rows_in_every_destination(mapped):
     for d in dests:
         assert torch.equal(d, ref)
     assert _native.device_status(dev) == 0
+
+
+def test_scatter_skips_and_flags_rows_mapped_outside_the_full_output():
+    """A local row or head whose mapped place lies outside the full output is not stored (the
+    epilogue checks the maps before every store) and raises HEATKV_DEVICE_GATHER_OUT_OF_RANGE;
+    the other rows land where their maps say."""
+    dev = torch.device("cuda", 0)
+    lib = _native.load()
+    B, H, L = 2, 4, 130
+    gen = torch.Generator().manual_seed(5)
+    q, k, v = (torch.randn(B, H, L, 128, generator=gen).bfloat16().to(dev) for _ in range(3))
+    st = torch.zeros(H, 1, dtype=torch.int32, device=dev)
+    ct = torch.zeros(H, dtype=torch.int32, device=dev)     # current keys only
+    scale = ctypes.c_float(128 ** -0.5)
+    ref = torch.empty(B, L, H * 128, dtype=torch.bfloat16, device=dev)
+    _native.check(lib.heatkv_segmented_attention(
+        _native.ptr(q), None, None, _native.ptr(st), _native.ptr(st), _native.ptr(ct),
+        _native.ptr(k), _native.ptr(v), _native.ptr(ref), DT[q.dtype], DT[k.dtype], DT[v.dtype],
+        B, H, L, 0, 128, 1, scale, 0, _native.ATTN_TCGEN05_CS64,
+        _native.stream_handle(dev)), "reference call")
+    out = torch.full_like(ref, float("nan"))
+    ptrs = torch.tensor([out.data_ptr()], dtype=torch.int64, device=dev)
+    rows = torch.tensor([1, 7], dtype=torch.int32, device=dev)       # row 1 -> 7: outside
+    heads = torch.tensor([3, 2, -1, 0], dtype=torch.int32, device=dev)  # head 2 -> -1: outside
+    _native.check(lib.heatkv_segmented_attention_scatter(
+        _native.ptr(q), None, None, _native.ptr(st), _native.ptr(st), _native.ptr(ct),
+        _native.ptr(k), _native.ptr(v), _native.ptr(ptrs), 1, _native.ptr(rows), _native.ptr(heads),
+        B, H, DT[q.dtype], DT[k.dtype], DT[v.dtype], B, H, L, 0, 128, 1, scale, None,
+        _native.stream_handle(dev)), "scatter call")
+    torch.cuda.synchronize()
+    ref4 = ref.view(B, L, H, 128)
+    out4 = out.view(B, L, H, 128)
+    for h, g in ((0, 3), (1, 2), (3, 0)):
+        assert torch.equal(out4[1, :, g], ref4[0, :, h])
+    assert torch.isnan(out4[0]).all()        # nothing maps to row 0
+    assert torch.isnan(out4[1, :, 1]).all()  # the head mapped outside
+    assert _native.device_status(dev) == _native.DEVICE_GATHER_OUT_OF_RANGE
 
 
 def test_scatter_of_dense_launches_uses_prefix_only_segments():
