@@ -311,7 +311,7 @@ def _items_desc(items, seq_len: int, device):
     return dst, src, ln, max(it[3] for it in items), sum(it[3] for it in items)
 
 
-def _derived(module, name: str, params, make):
+def _derived(module, name, params, make):
     """``make()`` computed once per module and reused while ``params`` (tensors it is derived
     from) keep their data pointer and version: inference calls need not rebuild the QKV bias
     (torch.cat of three parameters) or the cos-attention head scale (clamp_max + exp) every
@@ -368,9 +368,9 @@ def _project_weights(module, dt):
     """The QKV weight and bias as F.linear uses them in ``dt``: the weight cast to ``dt``, the
     bias ``cat(q_bias, zero_k_bias, v_bias)`` cast to ``dt`` and held in fp32."""
     w = module.mat_qkv.weight
-    wd = _derived(module, f"qkv_weight_{dt}", (w,), lambda: w.detach().to(dt).contiguous())
+    wd = _derived(module, ("qkv_weight", dt), (w,), lambda: w.detach().to(dt).contiguous())
     ps = (module.q_bias, module.zero_k_bias, module.v_bias)
-    bd = _derived(module, f"qkv_bias32_{dt}", ps,
+    bd = _derived(module, ("qkv_bias32", dt), ps,
                   lambda: torch.cat(ps).detach().to(dt).float().contiguous())
     return wd, bd
 

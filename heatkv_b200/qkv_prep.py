@@ -215,7 +215,11 @@ def project_qkv(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tens
     if scale_mul is not None:
         if scale_mul.numel() != H:
             raise ValueError("scale_mul must have one value per head")
-        sm = scale_mul.detach().reshape(H).to(device=dev, dtype=torch.float32).contiguous()
+        if (scale_mul.dtype == torch.float32 and scale_mul.device == dev
+                and scale_mul.is_contiguous()):
+            sm = scale_mul  # read as H contiguous fp32 values, whatever its shape
+        else:
+            sm = scale_mul.detach().reshape(H).to(device=dev, dtype=torch.float32).contiguous()
     cos = sin = None
     gstride = 0
     if rope is not None:
